@@ -1,0 +1,401 @@
+"""Benchmark of the K-quant decode GEMV (the hot path) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload q6k-gemv|q4k-gemv] [--m M]
+
+Workload (default): the Q6_K dequant-GEMV of a 14336 -> 4096 down-projection
+(N = 4096 output rows, K = 14336, GGUF Q6_K, 48,168,960 weight bytes) at batch
+M = 1, f32 activations.  One step = that GEMV over each of 8 distinct seeded
+weights (385 MB in total, more than the 126 MB L2, so every step streams its
+weights from HBM).  Data is synthetic: seeded random Q6_K superblocks with the
+distribution the reference's benchmark names (int8 scales in [-32, 31], d =
+f16(|N(0, 0.005)|)), x ~ N(0, 1).
+
+Metric: GB/s of algorithmic bytes (weight bytes + M*K*4 + M*N*4 per GEMV).
+* value    -- device-resident inputs, a step captured once into a CUDA graph and
+              replayed; CUDA events on the launch stream; max over ranks.
+* e2e      -- the same GEMVs through the C ABI with host buffers (pinned),
+              host->device copy of x and device->host copy of y per call.
+* roofline -- the GEMV kernel alone, bracketed by CUDA events inside the last
+              replay of the timed region, against MEASURED_PEAKS.json's HBM
+              copy bandwidth.
+* cpu_baseline -- the reference's CPU algorithm (QuantizedLinear::forward over
+              tile_dequant blocks, restated in oracle/kq_oracle.c) on the same
+              shape, timed on this host.
+
+Multi-GPU (torchrun): every rank runs its own 8 weights (the decode GEMVs of
+independent layers shard with no exchange), "scaling": "weak"; the only
+collectives are the barrier and the max-over-ranks of the timing.
+
+--impl reference runs the reference's CPU path alone (rank 0; other ranks
+exit 0) with the same metric, on a bounded sample of rows per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+METRIC = "Q4_K/Q6_K dequant-GEMV GB/s (% HBM peak); decode tok/s at 1/2/4/8 B200"
+WORKLOADS = {
+    # name: (gguf type, legacy type, N rows, K, description)
+    "q6k-gemv": (14, 114, 4096, 14336, "Q6_K dequant+GEMV 4096x14336 (down-proj shape)"),
+    "q4k-gemv": (12, 112, 4096, 4096, "Q4_K dequant+GEMV 4096x4096"),
+}
+NUM_WEIGHTS = 8
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=50)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=sorted(WORKLOADS), default="q6k-gemv")
+    p.add_argument("--m", type=int, default=1)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def algorithmic_bytes(qtype, n, k, m):
+    wbytes = n * (k // 256) * (144 if qtype == 12 else 210)
+    return wbytes, wbytes + m * k * 4 + m * n * 4
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(workload, m):
+    """dram bytes per launch of the GEMV kernel from a committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", f"gemv_{workload}_m{m}.txt")
+    try:
+        with open(path) as fh:
+            for line in fh:
+                if line.startswith("dram_bytes_per_launch:"):
+                    return int(float(line.split(":", 1)[1].split()[0]))
+    except OSError:
+        pass
+    return None
+
+
+# ---- clocks during the timed region ------------------------------------------
+
+class ClockSampler:
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks",
+               0x1: "gpu_idle", 0x10: "sync_boost"}
+
+    def __init__(self, device_index, period_s=0.01):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            uuid = None
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            except Exception:
+                pass
+            h = None
+            if uuid:
+                for i in range(pynvml.nvmlDeviceGetCount()):
+                    hi = pynvml.nvmlDeviceGetHandleByIndex(i)
+                    u = pynvml.nvmlDeviceGetUUID(hi)
+                    u = u.decode() if isinstance(u, bytes) else u
+                    if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                        h = hi
+            self.h = h or pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.period = period_s
+            self.ok = True
+        except Exception as e:  # no NVML: report that, do not guess
+            self.err = str(e)
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                self.samples.append(n.nvmlDeviceGetClockInfo(self.h, n.NVML_CLOCK_SM))
+                r = n.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "err", "")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": sorted(self.reasons - {"gpu_idle"})}
+
+
+# ---- CPU legs ------------------------------------------------------------------
+
+class CpuReference:
+    """The reference's algorithm -- QuantizedLinear::forward: full f32
+    dequantization, then a sequential f32 dot per output, threads over batch
+    rows only -- over the workload shape in the reference's own block layout
+    (restated in oracle/kq_oracle.c)."""
+
+    def __init__(self, workload, m, seed=0):
+        import oracle
+        from pesti_b200 import synthetic
+        self.oracle = oracle
+        self.qtype, self.legacy, self.n, self.k, _ = WORKLOADS[workload]
+        self.m = m
+        self.data = synthetic.legacy_weight(self.legacy, self.n, self.k, seed=seed)
+        self.x = synthetic.activations(m, self.k, seed=seed + 1)
+
+    def run(self, row0, rows):
+        """Forward over rows [row0, row0+rows); returns (seconds, algorithmic bytes)."""
+        sub = self.data[row0:row0 + rows]
+        t0 = time.perf_counter()
+        self.oracle.legacy_forward(self.legacy, sub, self.k, rows, self.x, self.m,
+                                   nthreads=os.cpu_count() or 1, threads_over_batch=True)
+        dt = time.perf_counter() - t0
+        return dt, algorithmic_bytes(self.qtype, rows, self.k, self.m)[1]
+
+
+def cpu_baseline(workload, m, budget_s=12.0):
+    ref = CpuReference(workload, m)
+    n, k = ref.n, ref.k
+    total_t, total_b, passes = 0.0, 0, 0
+    while total_t < budget_s and passes < 64:
+        dt, alg = ref.run(0, n)
+        total_t += dt
+        total_b += alg
+        passes += 1
+    cores = min(m, os.cpu_count() or 1)
+    return {"value": round(total_b / total_t / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+            "sample": f"{passes} full passes of QuantizedLinear::forward (full f32 dequant + sequential "
+                      f"dot, threads over batch rows) over a {n}x{k} pesti-legacy weight at M={m}; "
+                      f"bytes counted as the GGUF workload's",
+            "host_cpus": os.cpu_count()}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    qtype, _, n, k, desc = WORKLOADS[args.workload]
+    m = args.m
+    steps, warm = max(args.steps, 1), max(args.warmup, 0)
+    ref = CpuReference(args.workload, m)
+    # each step is a bounded sample of rows so the whole run stays ~2 minutes
+    dt1, _ = ref.run(0, 256)
+    per_row = dt1 / 256
+    rows = int(max(16, min(n, 90.0 / ((steps + warm) * per_row))))
+    starts = list(range(0, n - rows + 1, rows)) or [0]
+    for i in range(warm):
+        ref.run(starts[i % len(starts)], rows)
+    tt, tb = 0.0, 0
+    for i in range(steps):
+        dt, alg = ref.run(starts[i % len(starts)], rows)
+        tt += dt
+        tb += alg
+    value = tb / tt / 1e9
+    cores = min(m, os.cpu_count() or 1)
+    line = {"metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": round(tt / steps * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": f"{args.workload}: {desc}, M={m}, {rows} of {n} rows per step",
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"{rows} of {n} rows per step of QuantizedLinear::forward restated "
+                                       f"(oracle/kq_oracle.c) in the reference's block layout"},
+            "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- our arm -------------------------------------------------------------------
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from pesti_b200 import kq, synthetic
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    qtype, _, n, k, desc = WORKLOADS[args.workload]
+    m = args.m
+    wbytes, alg = algorithmic_bytes(qtype, n, k, m)
+
+    ctx = kq.Context(local_rank)
+    weights = [kq.Weight(ctx, qtype, synthetic.gguf_weight(qtype, n, k, seed=1000 * rank + i), n, k)
+               for i in range(NUM_WEIGHTS)]
+    x = torch.from_numpy(synthetic.activations(m, k, seed=7 + rank)).to(dev)
+    ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _ in range(NUM_WEIGHTS)]
+    ctx.reserve(m, k)
+
+    stream = torch.cuda.Stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+
+    def step():
+        for w, y in zip(weights, ys):
+            w.linear(x, m, y, device_ptrs=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):  # eager warm-up (module load, first launches)
+            step()
+    stream.synchronize()
+
+    # one step captured into a CUDA graph; the GEMV launches carry timing events
+    graph = torch.cuda.CUDAGraph()
+    ctx.profile_begin(NUM_WEIGHTS)
+    launches0 = ctx.launch_count
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    launches_per_step = ctx.launch_count - launches0
+
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record(stream)
+    stop.synchronize()
+    clocks.stop()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms_total = start.elapsed_time(stop)
+    kernel_ms, kernel_n = ctx.profile_end()
+
+    t = torch.tensor([ms_total, kernel_ms / max(kernel_n, 1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total, kernel_ms_avg = float(t[0]), float(t[1])
+    ms_per_step = ms_total / args.steps
+    value = world * NUM_WEIGHTS * alg / (ms_per_step * 1e-3) / 1e9
+
+    # e2e through the C ABI with pinned host buffers (copies inside the timed region)
+    ctx.set_stream(None)
+    xh = torch.empty((m, k), dtype=torch.float32).pin_memory()
+    xh.copy_(x.cpu())
+    yh = [torch.empty((m, n), dtype=torch.float32).pin_memory() for _ in range(NUM_WEIGHTS)]
+    xn, yn = xh.numpy(), [y.numpy() for y in yh]
+
+    def step_host():
+        for w, y in zip(weights, yn):
+            w.linear(xn, m, y)  # synchronous: H2D x, kernels, D2H y
+
+    for _ in range(3):
+        step_host()
+    e2e_steps = max(1, min(args.steps, 400))
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        step_host()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * NUM_WEIGHTS * alg * e2e_steps / float(te[0]) / 1e9
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        achieved = alg / (kernel_ms_avg * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded random GGUF superblocks, x ~ N(0,1))",
+            "config": {"workload": f"{args.workload}: {desc}, M={m}, {NUM_WEIGHTS} distinct weights per step",
+                       "rows": n, "k": k, "m": m, "weights_per_step": NUM_WEIGHTS,
+                       "weight_bytes_per_gemv": wbytes, "algorithmic_bytes_per_gemv": alg,
+                       "l2": f"inputs larger than L2 ({NUM_WEIGHTS * wbytes / 1e6:.0f} MB of weights per step)",
+                       "parallelism": f"replicas x{world} (independent weights per rank, no data-path collective)"},
+            "gpu_launches": launches_per_step * args.steps,
+            "pct_hbm_peak": round(100.0 * value / world / peak, 2),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (hbm copy)",
+                         "kernel": "gemv_kernel (CUDA events around each launch, last replay)",
+                         "kernel_us": round(kernel_ms_avg * 1e3, 3),
+                         "traffic": profiled_traffic(args.workload, m)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": NUM_WEIGHTS * m * k * 4,
+                    "d2h_bytes_per_step": NUM_WEIGHTS * m * n * 4,
+                    "api": "kq_linear_f32 with host pointers (pinned), synchronous per call"},
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.workload, m)
+        print(json.dumps(line), flush=True)
+    del graph
+    for w in weights:
+        w.free()
+    ctx.close()
+    return 0
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

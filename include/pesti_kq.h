@@ -1,0 +1,116 @@
+/*
+ * pesti_kq.h -- C ABI of libpesti_kq.so, the B200 (sm_100a) K-quant linear
+ * library.  This is the layer the reference's `cuda-oxide` crate stands for
+ * (cuda-oxide/src/kernels.rs:4-36 and pesti-runner/src/dequantize_cuda.rs:12-55
+ * are stubs that return "not yet implemented"); the Rust QuantizedLinear
+ * (pesti-runner/src/quantized_linear.rs:12-183) binds to it as a drop-in.
+ *
+ * Conventions
+ *  - Every entry returns an int status: KQ_OK (0) or a KQ_ERR_* code.  No entry
+ *    aborts, traps or falls back to the CPU; kq_last_error() describes the
+ *    most recent failure on a context.
+ *  - A context owns one CUDA device and one stream (its own, or one the caller
+ *    installs with kq_ctx_set_stream).  A context is not thread-safe: callers
+ *    serialise use of one context (the Rust side wraps it in a Mutex).
+ *  - Weights are immutable once uploaded and may be used from any context on
+ *    the same device.
+ *  - Pointer arguments of the compute entries are host pointers unless
+ *    KQ_DEVICE_PTRS is set, in which case they are device pointers on the
+ *    context's device and the call is stream-ordered (asynchronous unless
+ *    KQ_SYNC is also set).  Host-pointer calls are synchronous.
+ */
+#ifndef PESTI_KQ_H
+#define PESTI_KQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KQ_ABI_VERSION 1
+
+/* status codes */
+#define KQ_OK 0
+#define KQ_ERR_INVALID_ARG 1  /* null pointer, bad size, bad flag        */
+#define KQ_ERR_UNSUPPORTED 2  /* unknown kq_type / shape not supported  */
+#define KQ_ERR_CUDA 3         /* a CUDA runtime call failed             */
+#define KQ_ERR_SHORT_BUFFER 4 /* weight bytes too short for the shape   */
+#define KQ_ERR_NCCL 5         /* a collective failed                    */
+#define KQ_ERR_STATE 6        /* call out of order (e.g. no TP group)   */
+#define KQ_ERR_NOMEM 7        /* device allocation failed               */
+
+/* weight encodings (values follow GGML's type ids for the GGUF layouts) */
+enum kq_type {
+  KQ_GGUF_Q4_K = 12,          /* 144 B per 256 weights                    */
+  KQ_GGUF_Q6_K = 14,          /* 210 B per 256 weights                    */
+  KQ_PESTI_Q4_K_LEGACY = 112, /* tile_dequant.rs 28 B per 16 weights      */
+  KQ_PESTI_Q6_K_LEGACY = 114, /* tile_dequant.rs 42 B per 16 weights      */
+};
+
+/* flags of the compute entries */
+#define KQ_HOST_PTRS 0   /* x / bias / y are host pointers (synchronous)  */
+#define KQ_DEVICE_PTRS 1 /* x / bias / y are device pointers (async)      */
+#define KQ_SYNC 2        /* synchronise the context stream before return  */
+
+typedef struct kq_ctx kq_ctx;
+typedef struct kq_weight kq_weight;
+
+/* ---- context ------------------------------------------------------------ */
+/* New context on `device` with its own non-blocking stream.
+ * Replaces cuda-oxide's device/stream placeholders (cuda-oxide/src/stream.rs:6-15). */
+int kq_ctx_create(int device, kq_ctx **out);
+int kq_ctx_destroy(kq_ctx *ctx);
+/* Install an external cudaStream_t (NULL restores the context's own). */
+int kq_ctx_set_stream(kq_ctx *ctx, void *cuda_stream);
+int kq_ctx_synchronize(kq_ctx *ctx);
+/* Reserve scratch for calls with up to `m` rows of `k` activations, so that
+ * later calls allocate nothing (e.g. before CUDA-graph capture). */
+int kq_ctx_reserve(kq_ctx *ctx, int64_t m, int64_t k);
+/* Number of kernels this context has launched so far. */
+int64_t kq_ctx_launch_count(const kq_ctx *ctx);
+/* Bracket the main kernel of each of the next `max_calls` compute calls with a
+ * pair of CUDA events on the context stream (event nodes when the stream is
+ * being captured into a CUDA graph).  kq_ctx_profile_end synchronises the
+ * stream and returns the summed elapsed time of the recorded pairs (for a
+ * replayed graph: of its most recent replay) and their count.  This is the
+ * benchmark's timing hook; the reference has none (it times with Instant,
+ * pesti-runner/examples/quant_bench.rs:89-101). */
+int kq_ctx_profile_begin(kq_ctx *ctx, int max_calls);
+int kq_ctx_profile_end(kq_ctx *ctx, double *total_ms, int64_t *count);
+const char *kq_last_error(const kq_ctx *ctx);
+const char *kq_status_string(int status);
+int kq_abi_version(void);
+
+/* ---- weights ------------------------------------------------------------ */
+/* Bytes of one row of `in_features` weights in the given encoding (GGUF types:
+ * in_features must be a multiple of 256).  Replaces QuantizedLinear::row_bytes
+ * (quantized_linear.rs:86-95) for the legacy types, which it reproduces. */
+int kq_row_bytes(int kq_type, int64_t in_features, int64_t *out);
+/* Upload a row-major [out_features][row bytes] weight and keep it resident on
+ * the context's device (QuantizedLinear::new / from_quantized,
+ * quantized_linear.rs:27-67, with the bytes moved to HBM once).  `nbytes` must
+ * cover every row (legacy: the last row only needs the bytes its tile reads). */
+int kq_weight_upload(kq_ctx *ctx, int kq_type, const void *bytes, size_t nbytes,
+                     int64_t out_features, int64_t in_features, kq_weight **out);
+int kq_weight_free(kq_weight *w);
+int kq_weight_info(const kq_weight *w, int *kq_type, int64_t *out_features,
+                   int64_t *in_features, int64_t *device_bytes);
+
+/* ---- compute ------------------------------------------------------------ */
+/* y[m][out] = x[m][in] . W[out][in] (+ bias[out]), f32 in and out.
+ * QuantizedLinear::forward (quantized_linear.rs:101-143) / Linear::forward
+ * (transformer/linear.rs:108-150).  bias may be NULL. */
+int kq_linear_f32(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t m,
+                  const float *bias, float *y, int flags);
+/* Dequantize rows [row0, row0+nrows) to f32 [nrows][in_features], bit-exact
+ * with the CPU decode of the same encoding (QuantizedLinear::
+ * dequantize_full_row_range, quantized_linear.rs:146-183, for legacy types). */
+int kq_dequant_f32(kq_ctx *ctx, const kq_weight *w, int64_t row0, int64_t nrows,
+                   float *out, int flags);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PESTI_KQ_H */

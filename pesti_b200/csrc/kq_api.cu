@@ -1,0 +1,461 @@
+// kq_api.cu -- the C ABI (include/pesti_kq.h): contexts, device-resident
+// weights, argument validation, host<->device staging and kernel dispatch.
+// Every failure is reported as a status code plus a message on the context;
+// nothing here aborts, traps, or computes on the CPU.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/pesti_kq.h"
+#include "kq_kernels.h"
+
+struct kq_ctx {
+  int device = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  void* ws = nullptr;  // kernel scratch (permuted activations, partial sums)
+  size_t ws_bytes = 0;
+  void* xbuf = nullptr;  // device staging of host inputs
+  size_t xbuf_bytes = 0;
+  void* ybuf = nullptr;  // device staging of host outputs
+  size_t ybuf_bytes = 0;
+  void* bbuf = nullptr;  // device staging of a host bias
+  size_t bbuf_bytes = 0;
+  int64_t launches = 0;
+  std::string err;
+  // timing brackets of the main kernel (kq_ctx_profile_begin/end)
+  std::vector<cudaEvent_t> prof_ev;  // 2 per slot
+  int prof_cap = 0, prof_next = 0;
+  bool prof_on = false;
+
+  kq::Bracket next_bracket() {
+    kq::Bracket b;
+    if (prof_on && prof_next < prof_cap) {
+      b.start = prof_ev[2 * prof_next];
+      b.stop = prof_ev[2 * prof_next + 1];
+      ++prof_next;
+    }
+    return b;
+  }
+};
+
+struct kq_weight {
+  int device = 0;
+  kq::DevWeight dw{};
+  void* q_alloc = nullptr;
+  void* d_alloc = nullptr;
+  int64_t device_bytes = 0;
+};
+
+namespace {
+
+const char* kNoCtx = "no context";
+
+int fail(kq_ctx* ctx, int status, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->err = buf;
+  }
+  return status;
+}
+
+int cuda_fail(kq_ctx* ctx, cudaError_t e, const char* what) {
+  cudaGetLastError();  // clear a non-sticky error so the context stays usable
+  return fail(ctx, KQ_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+// Makes `dev` current for the scope and restores the caller's device.
+struct DeviceGuard {
+  int prev = -1;
+  cudaError_t status = cudaSuccess;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) status = cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+// Grow-only device buffer.
+int ensure(kq_ctx* ctx, void** buf, size_t* have, size_t need, const char* what) {
+  if (need <= *have) return KQ_OK;
+  if (*buf) {
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "synchronize before growing scratch");
+    cudaFree(*buf);
+    *buf = nullptr;
+    *have = 0;
+  }
+  size_t sz = (need + 255) & ~size_t(255);
+  cudaError_t e = cudaMalloc(buf, sz);
+  if (e != cudaSuccess) {
+    *buf = nullptr;
+    cudaGetLastError();
+    return fail(ctx, KQ_ERR_NOMEM, "cudaMalloc(%zu) for %s failed: %s", sz, what,
+                cudaGetErrorString(e));
+  }
+  *have = sz;
+  return KQ_OK;
+}
+
+bool is_gguf(int t) { return t == kq::GGUF_Q4_K || t == kq::GGUF_Q6_K; }
+bool is_legacy(int t) { return t == kq::LEGACY_Q4_K || t == kq::LEGACY_Q6_K; }
+
+int64_t legacy_row_bytes(int t, int64_t k) {
+  return t == kq::LEGACY_Q4_K ? ((k + 15) / 16) * 28 : ((k + 15) / 16) * 42;
+}
+
+// Bytes the legacy tile decoder reads from the last row (tile_dequant.rs:224-227, 334-335).
+int64_t legacy_tile_bytes(int t, int64_t k) {
+  if (t == kq::LEGACY_Q4_K) return (k / 16) * 28 + ((k % 16) ? 4 : 0);
+  return ((k + 15) / 16) * 42;
+}
+
+int check_ctx(kq_ctx* ctx) { return ctx ? KQ_OK : KQ_ERR_INVALID_ARG; }
+
+}  // namespace
+
+extern "C" {
+
+int kq_abi_version(void) { return KQ_ABI_VERSION; }
+
+const char* kq_status_string(int status) {
+  switch (status) {
+    case KQ_OK: return "ok";
+    case KQ_ERR_INVALID_ARG: return "invalid argument";
+    case KQ_ERR_UNSUPPORTED: return "unsupported";
+    case KQ_ERR_CUDA: return "CUDA error";
+    case KQ_ERR_SHORT_BUFFER: return "buffer too short";
+    case KQ_ERR_NCCL: return "collective error";
+    case KQ_ERR_STATE: return "invalid state";
+    case KQ_ERR_NOMEM: return "out of device memory";
+    default: return "unknown status";
+  }
+}
+
+const char* kq_last_error(const kq_ctx* ctx) { return ctx ? ctx->err.c_str() : kNoCtx; }
+
+int kq_ctx_create(int device, kq_ctx** out) {
+  if (!out) return KQ_ERR_INVALID_ARG;
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return KQ_ERR_CUDA;
+  }
+  if (device < 0 || device >= n) return KQ_ERR_INVALID_ARG;
+  DeviceGuard g(device);
+  if (g.status != cudaSuccess) return KQ_ERR_CUDA;
+  kq_ctx* ctx = new kq_ctx();
+  ctx->device = device;
+  e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) {
+    delete ctx;
+    cudaGetLastError();
+    return KQ_ERR_CUDA;
+  }
+  ctx->stream = ctx->own_stream;
+  *out = ctx;
+  return KQ_OK;
+}
+
+int kq_ctx_destroy(kq_ctx* ctx) {
+  if (!ctx) return KQ_ERR_INVALID_ARG;
+  {
+    DeviceGuard g(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->xbuf) cudaFree(ctx->xbuf);
+    if (ctx->ybuf) cudaFree(ctx->ybuf);
+    if (ctx->bbuf) cudaFree(ctx->bbuf);
+    for (cudaEvent_t ev : ctx->prof_ev) cudaEventDestroy(ev);
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    cudaGetLastError();
+  }
+  delete ctx;
+  return KQ_OK;
+}
+
+int kq_ctx_set_stream(kq_ctx* ctx, void* stream) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  return KQ_OK;
+}
+
+int kq_ctx_synchronize(kq_ctx* ctx) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  return e == cudaSuccess ? KQ_OK : cuda_fail(ctx, e, "cudaStreamSynchronize");
+}
+
+int kq_ctx_reserve(kq_ctx* ctx, int64_t m, int64_t k) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (m < 0 || k < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative size");
+  DeviceGuard g(ctx->device);
+  const int64_t kr = ((k + kq::QK - 1) / kq::QK) * kq::QK;
+  return ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::gemv_gguf_workspace_bytes(m, kr), "workspace");
+}
+
+int64_t kq_ctx_launch_count(const kq_ctx* ctx) { return ctx ? ctx->launches : -1; }
+
+int kq_ctx_profile_begin(kq_ctx* ctx, int max_calls) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (max_calls < 0 || max_calls > (1 << 20)) return fail(ctx, KQ_ERR_INVALID_ARG, "max_calls %d", max_calls);
+  DeviceGuard g(ctx->device);
+  while ((int)ctx->prof_ev.size() < 2 * max_calls) {
+    cudaEvent_t ev;
+    cudaError_t e = cudaEventCreate(&ev);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventCreate");
+    ctx->prof_ev.push_back(ev);
+  }
+  ctx->prof_cap = max_calls;
+  ctx->prof_next = 0;
+  ctx->prof_on = true;
+  return KQ_OK;
+}
+
+int kq_ctx_profile_end(kq_ctx* ctx, double* total_ms, int64_t* count) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!ctx->prof_on) return fail(ctx, KQ_ERR_STATE, "profiling was not started");
+  DeviceGuard g(ctx->device);
+  ctx->prof_on = false;
+  cudaError_t e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+  double sum = 0.0;
+  for (int i = 0; i < ctx->prof_next; ++i) {
+    float ms = 0.f;
+    e = cudaEventElapsedTime(&ms, ctx->prof_ev[2 * i], ctx->prof_ev[2 * i + 1]);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventElapsedTime");
+    sum += ms;
+  }
+  if (total_ms) *total_ms = sum;
+  if (count) *count = ctx->prof_next;
+  return KQ_OK;
+}
+
+int kq_row_bytes(int type, int64_t in_features, int64_t* out) {
+  if (!out || in_features < 0) return KQ_ERR_INVALID_ARG;
+  if (is_gguf(type)) {
+    if (in_features % kq::QK) return KQ_ERR_UNSUPPORTED;
+    *out = (in_features / kq::QK) * (type == kq::GGUF_Q4_K ? kq::Q4K_BYTES : kq::Q6K_BYTES);
+    return KQ_OK;
+  }
+  if (is_legacy(type)) {
+    *out = legacy_row_bytes(type, in_features);
+    return KQ_OK;
+  }
+  return KQ_ERR_UNSUPPORTED;
+}
+
+int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, int64_t n,
+                     int64_t k, kq_weight** out) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!out) return fail(ctx, KQ_ERR_INVALID_ARG, "out is null");
+  *out = nullptr;
+  if (n < 0 || k < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative shape %lld x %lld",
+                                  (long long)n, (long long)k);
+  if (!is_gguf(type) && !is_legacy(type))
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "unsupported kq_type %d", type);
+  if (is_gguf(type) && k % kq::QK)
+    return fail(ctx, KQ_ERR_UNSUPPORTED,
+                "GGUF K-quant rows hold whole 256-weight superblocks; in_features=%lld",
+                (long long)k);
+  int64_t need;
+  if (is_gguf(type)) {
+    need = n * (k / kq::QK) * (type == kq::GGUF_Q4_K ? kq::Q4K_BYTES : kq::Q6K_BYTES);
+  } else {
+    need = (n == 0 || k == 0) ? 0 : (n - 1) * legacy_row_bytes(type, k) + legacy_tile_bytes(type, k);
+  }
+  if ((int64_t)nbytes < need)
+    return fail(ctx, KQ_ERR_SHORT_BUFFER, "weight has %zu bytes, shape %lld x %lld needs %lld",
+                nbytes, (long long)n, (long long)k, (long long)need);
+  if (need > 0 && !bytes) return fail(ctx, KQ_ERR_INVALID_ARG, "bytes is null");
+
+  DeviceGuard g(ctx->device);
+  if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
+  kq_weight* w = new kq_weight();
+  w->device = ctx->device;
+  w->dw.type = type;
+  w->dw.n = n;
+  w->dw.k = k;
+  w->dw.sb = is_gguf(type) ? k / kq::QK : 0;
+  w->dw.row_bytes = is_legacy(type) ? legacy_row_bytes(type, k) : 0;
+  cudaError_t e = cudaSuccess;
+  const size_t pad = 64;  // vector loads never read past the allocation
+  if (type == kq::GGUF_Q6_K) {
+    const int64_t nsb = n * w->dw.sb;
+    void* raw = nullptr;
+    e = cudaMalloc(&raw, (size_t)nsb * kq::Q6K_BYTES + pad);
+    if (e == cudaSuccess) e = cudaMalloc(&w->q_alloc, (size_t)nsb * kq::Q6K_BODY + pad);
+    if (e == cudaSuccess) e = cudaMalloc(&w->d_alloc, (size_t)nsb * 2 + pad);
+    if (e == cudaSuccess && nsb)
+      e = cudaMemcpyAsync(raw, bytes, (size_t)nsb * kq::Q6K_BYTES, cudaMemcpyHostToDevice,
+                          ctx->stream);
+    if (e == cudaSuccess)
+      e = kq::launch_q6k_relayout(static_cast<const uint8_t*>(raw), nsb,
+                                  static_cast<uint8_t*>(w->q_alloc),
+                                  static_cast<uint16_t*>(w->d_alloc), ctx->stream);
+    if (e == cudaSuccess) {
+      ++ctx->launches;
+      e = cudaStreamSynchronize(ctx->stream);
+    }
+    if (raw) cudaFree(raw);
+    w->device_bytes = nsb * (kq::Q6K_BODY + 2);
+    w->dw.len = w->device_bytes;
+  } else {
+    e = cudaMalloc(&w->q_alloc, (size_t)need + pad);
+    if (e == cudaSuccess) e = cudaMemsetAsync(w->q_alloc, 0, (size_t)need + pad, ctx->stream);
+    if (e == cudaSuccess && need)
+      e = cudaMemcpyAsync(w->q_alloc, bytes, (size_t)need, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    w->device_bytes = need;
+    w->dw.len = need;
+  }
+  if (e != cudaSuccess) {
+    int rc = cuda_fail(ctx, e, "weight upload");
+    if (w->q_alloc) cudaFree(w->q_alloc);
+    if (w->d_alloc) cudaFree(w->d_alloc);
+    delete w;
+    return rc;
+  }
+  w->dw.q = static_cast<const uint8_t*>(w->q_alloc);
+  w->dw.d = static_cast<const uint16_t*>(w->d_alloc);
+  *out = w;
+  return KQ_OK;
+}
+
+int kq_weight_free(kq_weight* w) {
+  if (!w) return KQ_ERR_INVALID_ARG;
+  DeviceGuard g(w->device);
+  if (w->q_alloc) cudaFree(w->q_alloc);
+  if (w->d_alloc) cudaFree(w->d_alloc);
+  cudaGetLastError();
+  delete w;
+  return KQ_OK;
+}
+
+int kq_weight_info(const kq_weight* w, int* type, int64_t* n, int64_t* k, int64_t* bytes) {
+  if (!w) return KQ_ERR_INVALID_ARG;
+  if (type) *type = w->dw.type;
+  if (n) *n = w->dw.n;
+  if (k) *k = w->dw.k;
+  if (bytes) *bytes = w->device_bytes;
+  return KQ_OK;
+}
+
+int kq_linear_f32(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, const float* bias,
+                  float* y, int flags) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!w) return fail(ctx, KQ_ERR_INVALID_ARG, "weight is null");
+  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
+  if (w->device != ctx->device)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device,
+                ctx->device);
+  if (m < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative m");
+  const int64_t n = w->dw.n, k = w->dw.k;
+  if (m == 0 || n == 0) return KQ_OK;
+  if (!y || (k > 0 && !x)) return fail(ctx, KQ_ERR_INVALID_ARG, "x or y is null");
+  const bool dev = flags & KQ_DEVICE_PTRS;
+  DeviceGuard g(ctx->device);
+  if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
+  cudaStream_t s = ctx->stream;
+  cudaError_t e = cudaSuccess;
+  int rc;
+
+  const float* xd = x;
+  const float* bd = bias;
+  float* yd = y;
+  if (!dev) {
+    if ((rc = ensure(ctx, &ctx->xbuf, &ctx->xbuf_bytes, (size_t)(m * k * 4), "input staging"))) return rc;
+    if ((rc = ensure(ctx, &ctx->ybuf, &ctx->ybuf_bytes, (size_t)(m * n * 4), "output staging"))) return rc;
+    if (k > 0) {
+      e = cudaMemcpyAsync(ctx->xbuf, x, (size_t)(m * k * 4), cudaMemcpyHostToDevice, s);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "copy x to device");
+    }
+    if (bias) {
+      if ((rc = ensure(ctx, &ctx->bbuf, &ctx->bbuf_bytes, (size_t)(n * 4), "bias staging"))) return rc;
+      e = cudaMemcpyAsync(ctx->bbuf, bias, (size_t)(n * 4), cudaMemcpyHostToDevice, s);
+      if (e != cudaSuccess) return cuda_fail(ctx, e, "copy bias to device");
+      bd = static_cast<const float*>(ctx->bbuf);
+    }
+    xd = static_cast<const float*>(ctx->xbuf);
+    yd = static_cast<float*>(ctx->ybuf);
+  }
+
+  int launches = 0;
+  if (k == 0) {
+    // no inputs: the product is empty, y = bias (quantized_linear.rs:147-150)
+    if (bd) {
+      for (int64_t i = 0; i < m && e == cudaSuccess; ++i)
+        e = cudaMemcpyAsync(yd + i * n, bd, (size_t)n * 4, cudaMemcpyDeviceToDevice, s);
+    } else {
+      e = cudaMemsetAsync(yd, 0, (size_t)(m * n * 4), s);
+    }
+  } else if (is_gguf(w->dw.type)) {
+    if ((rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::gemv_gguf_workspace_bytes(m, k), "workspace")))
+      return rc;
+    e = kq::launch_gemv_gguf(w->dw, xd, m, bd, yd, ctx->ws, s, &launches, ctx->next_bracket());
+  } else {
+    e = kq::launch_gemv_legacy(w->dw, xd, m, bd, yd, s, &launches, ctx->next_bracket());
+  }
+  ctx->launches += launches;
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
+  if (!dev) {
+    e = cudaMemcpyAsync(y, ctx->ybuf, (size_t)(m * n * 4), cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "copy y to host");
+  }
+  if (!dev || (flags & KQ_SYNC)) {
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "kq_linear_f32");
+  }
+  return KQ_OK;
+}
+
+int kq_dequant_f32(kq_ctx* ctx, const kq_weight* w, int64_t row0, int64_t nrows, float* out,
+                   int flags) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!w) return fail(ctx, KQ_ERR_INVALID_ARG, "weight is null");
+  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
+  if (w->device != ctx->device) return fail(ctx, KQ_ERR_INVALID_ARG, "weight on another device");
+  if (row0 < 0 || nrows < 0 || row0 + nrows > w->dw.n)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "rows [%lld, %lld) outside [0, %lld)", (long long)row0,
+                (long long)(row0 + nrows), (long long)w->dw.n);
+  const int64_t count = nrows * w->dw.k;
+  if (count == 0) return KQ_OK;
+  if (!out) return fail(ctx, KQ_ERR_INVALID_ARG, "out is null");
+  const bool dev = flags & KQ_DEVICE_PTRS;
+  DeviceGuard g(ctx->device);
+  if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
+  int rc;
+  float* od = out;
+  if (!dev) {
+    if ((rc = ensure(ctx, &ctx->ybuf, &ctx->ybuf_bytes, (size_t)count * 4, "output staging"))) return rc;
+    od = static_cast<float*>(ctx->ybuf);
+  }
+  cudaError_t e = kq::launch_dequant_f32(w->dw, row0, nrows, od, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "dequant launch");
+  ++ctx->launches;
+  if (!dev) {
+    e = cudaMemcpyAsync(out, od, (size_t)count * 4, cudaMemcpyDeviceToHost, ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "copy to host");
+  }
+  if (!dev || (flags & KQ_SYNC)) {
+    e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "kq_dequant_f32");
+  }
+  return KQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,206 @@
+// kq_dequant.cu -- bit-exact dequantization, the Q6_K upload re-layout, and
+// the pesti-legacy block kernels.
+//
+// Dequantized values are computed with explicitly rounded f32 operations
+// (__fmul_rn / __fadd_rn / __fsub_rn) in the same association as the
+// CPU definitions they must match bit for bit:
+//   GGUF Q4_K  (d*sc)*q - (dmin*m)                         (gguf-py / ggml)
+//   GGUF Q6_K  (d*sc)*(q-32)                                (gguf-py / ggml)
+//   legacy Q4_K ((delta*h)*(q-4)) + d     pesti-runner/src/tile_dequant.rs:261
+//   legacy Q6_K (d*(q-32))*scale          pesti-runner/src/tile_dequant.rs:373
+#include "kq_common.cuh"
+#include "kq_kernels.h"
+
+namespace kq {
+
+namespace {
+
+__device__ __forceinline__ float gguf_q4k_value(const uint8_t* blk, int e) {
+  const float d = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+  const float dmin = f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+  const int c = e >> 6, p = e & 63;
+  const int j = 2 * c + (p >> 5);
+  int sc, m;
+  q4k_scale_min(blk + 4, j, sc, m);
+  const uint8_t byte = blk[16 + 32 * c + (p & 31)];
+  const int q = (p < 32) ? (byte & 0x0f) : (byte >> 4);
+  const float d1 = __fmul_rn(d, (float)sc);
+  const float m1 = __fmul_rn(dmin, (float)m);
+  return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+}
+
+__device__ __forceinline__ float gguf_q6k_value(const uint8_t* body, uint16_t dbits, int e) {
+  const int h = e >> 7, g = (e >> 5) & 3, l = e & 31;
+  const uint8_t qlb = body[64 * h + l + 32 * (g & 1)];
+  const int lo = (g < 2) ? (qlb & 0x0f) : (qlb >> 4);
+  const int hi = (body[128 + 32 * h + l] >> (2 * g)) & 3;
+  const int q = (lo | (hi << 4)) - 32;
+  const int sc = (int)(int8_t)body[192 + (e >> 4)];
+  const float d = f16_bits_to_f32(dbits);
+  return __fmul_rn(__fmul_rn(d, (float)sc), (float)q);
+}
+
+__device__ __forceinline__ uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+// Legacy Q4_K: tile_dequant.rs:238-290.  Element i of a row.
+__device__ __forceinline__ float legacy_q4k_value(const uint8_t* row, int64_t k, int64_t i) {
+  const int64_t nfull = k / 16;
+  const int64_t b = i / 16;
+  if (b >= nfull) {  // trailing 4-byte partial block: value = d
+    return f16_bits_to_f32(rd16(row + nfull * 28));
+  }
+  const uint8_t* p = row + b * 28;
+  const int e = (int)(i & 15);
+  const float d = f16_bits_to_f32(rd16(p));
+  const float delta = f16_bits_to_f32(rd16(p + 2));
+  const uint8_t* qsrc = p + 4 + (e >> 3) * 4;  // qs_low for e<8, qs_high for e>=8
+  const int ei = e & 7;
+  const int q = (qsrc[ei >> 1] >> (4 * (ei & 1))) & 0x0f;
+  const float h = f16_bits_to_f32(rd16(p + 12 + 2 * (e >> 3)));
+  float t = __fmul_rn(delta, h);
+  t = __fmul_rn(t, __fsub_rn((float)q, 4.0f));
+  return __fadd_rn(t, d);
+}
+
+// Legacy Q6_K: tile_dequant.rs:347-374.
+__device__ __forceinline__ float legacy_q6k_value(const uint8_t* row, int64_t i) {
+  const uint8_t* p = row + (i / 16) * 42;
+  const int e = (int)(i & 15);
+  const float d = f16_bits_to_f32(rd16(p));
+  const float sc = f16_bits_to_f32(rd16(p + 2 + 2 * (e >> 2)));
+  const int qlow = (p[10 + (e >> 2)] >> ((e & 3) * 2)) & 3;
+  const int flag = (p[18 + (e >> 2)] >> ((e & 3) * 2)) & 3;
+  const int qhigh = flag == 0 ? 0 : flag - 1;
+  const int q = qlow + 4 * qhigh;
+  const float t = __fmul_rn(d, __fsub_rn((float)q, 32.0f));
+  return __fmul_rn(t, sc);
+}
+
+__global__ void dequant_kernel(DevWeight w, int64_t row0, int64_t nrows, float* __restrict__ out) {
+  const int64_t total = nrows * w.k;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = row0 + idx / w.k;
+    const int64_t i = idx - (idx / w.k) * w.k;
+    float v;
+    switch (w.type) {
+      case GGUF_Q4_K:
+        v = gguf_q4k_value(w.q + ((size_t)r * w.sb + i / QK) * Q4K_BYTES, (int)(i % QK));
+        break;
+      case GGUF_Q6_K: {
+        const size_t g = (size_t)r * w.sb + i / QK;
+        v = gguf_q6k_value(w.q + g * Q6K_BODY, w.d[g], (int)(i % QK));
+        break;
+      }
+      case LEGACY_Q4_K:
+        v = legacy_q4k_value(w.q + r * w.row_bytes, w.k, i);
+        break;
+      default:
+        v = legacy_q6k_value(w.q + r * w.row_bytes, i);
+        break;
+    }
+    out[idx] = v;
+  }
+}
+
+__global__ void q6k_relayout_kernel(const uint16_t* __restrict__ raw, int64_t nsb,
+                                    uint16_t* __restrict__ body, uint16_t* __restrict__ d) {
+  const int64_t total = nsb * 105;  // 210 bytes = 105 halfwords
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t g = idx / 105;
+    const int wd = (int)(idx - g * 105);
+    const uint16_t v = raw[idx];
+    if (wd < 104)
+      body[g * 104 + wd] = v;
+    else
+      d[g] = v;
+  }
+}
+
+// Legacy linear: one warp per output row, lanes stride over 16-weight blocks.
+// Not a tuned path: it exists so the reference's own block layout can be run
+// on the device and compared with its CPU forward.
+template <int M>
+__global__ void __launch_bounds__(256) legacy_gemv_kernel(DevWeight w, const float* __restrict__ x,
+                                                          const float* __restrict__ bias,
+                                                          float* __restrict__ y, int64_t ldy) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= w.n) return;
+  const uint8_t* rp = w.q + row * w.row_bytes;
+  float acc[M];
+#pragma unroll
+  for (int mi = 0; mi < M; ++mi) acc[mi] = 0.f;
+  const int64_t nblk = (w.k + 15) / 16;
+  for (int64_t b = lane; b < nblk; b += 32) {
+    float v[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int64_t i = b * 16 + e;
+      v[e] = (i < w.k) ? (w.type == LEGACY_Q4_K ? legacy_q4k_value(rp, w.k, i) : legacy_q6k_value(rp, i))
+                       : 0.f;
+    }
+#pragma unroll
+    for (int mi = 0; mi < M; ++mi) {
+      const float* xr = x + mi * w.k + b * 16;
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (b * 16 + e < w.k) acc[mi] = fmaf(v[e], __ldg(xr + e), acc[mi]);
+    }
+  }
+#pragma unroll
+  for (int mi = 0; mi < M; ++mi)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc[mi] += __shfl_xor_sync(0xffffffffu, acc[mi], off);
+  if (lane == 0) {
+    const float bv = bias ? bias[row] : 0.f;
+#pragma unroll
+    for (int mi = 0; mi < M; ++mi) y[mi * ldy + row] = acc[mi] + bv;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_dequant_f32(const DevWeight& w, int64_t row0, int64_t nrows, float* out,
+                               cudaStream_t s) {
+  const int64_t total = nrows * w.k;
+  if (total <= 0) return cudaSuccess;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  dequant_kernel<<<(unsigned)blocks, 256, 0, s>>>(w, row0, nrows, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t nsb, uint8_t* body, uint16_t* d,
+                                cudaStream_t s) {
+  const int64_t total = nsb * 105;
+  if (total <= 0) return cudaSuccess;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 64) blocks = 148 * 64;
+  q6k_relayout_kernel<<<(unsigned)blocks, 256, 0, s>>>(reinterpret_cast<const uint16_t*>(raw), nsb,
+                                                       reinterpret_cast<uint16_t*>(body), d);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemv_legacy(const DevWeight& w, const float* x, int64_t m, const float* bias,
+                               float* y, cudaStream_t s, int* launches, Bracket br) {
+  const unsigned grid = (unsigned)((w.n + 7) / 8);
+  bracket_record(br.start, s);
+  for (int64_t m0 = 0; m0 < m; m0 += 4) {
+    const int mc = (int)((m - m0) < 4 ? (m - m0) : 4);
+    const float* xc = x + m0 * w.k;
+    float* yc = y + m0 * w.n;
+    switch (mc) {
+      case 1: legacy_gemv_kernel<1><<<grid, 256, 0, s>>>(w, xc, bias, yc, w.n); break;
+      case 2: legacy_gemv_kernel<2><<<grid, 256, 0, s>>>(w, xc, bias, yc, w.n); break;
+      case 3: legacy_gemv_kernel<3><<<grid, 256, 0, s>>>(w, xc, bias, yc, w.n); break;
+      default: legacy_gemv_kernel<4><<<grid, 256, 0, s>>>(w, xc, bias, yc, w.n); break;
+    }
+    if (launches) ++*launches;
+  }
+  bracket_record(br.stop, s);
+  return cudaGetLastError();
+}
+
+}  // namespace kq

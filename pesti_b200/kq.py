@@ -1,0 +1,347 @@
+"""Python binding of libpesti_kq.so and the QuantizedLinear drop-in.
+
+``QuantizedLinear`` mirrors pesti-runner's quantized-matmul entry point
+(pesti-runner/src/quantized_linear.rs:12-183): the same constructor names and
+argument meaning (``new``, ``from_quantized``), ``forward(x, batch_size)``
+returning a fresh f32 vector of ``batch_size * out_features`` values, and the
+memory accounting helpers.  The weight bytes are uploaded once and stay
+resident in HBM; ``forward`` runs the sm_100a kernels through the C ABI
+(include/pesti_kq.h).  There is no CPU path: if the library cannot be loaded or
+no GPU is present, construction raises.
+
+Error behaviour follows the reference:
+* ``from_quantized`` with an unknown dtype name raises (reference: Err).
+* a weight whose bytes are too short for its shape does not fail at
+  construction; ``forward`` prints the decode error to stderr and returns
+  zeros, as ``QuantizedLinear::forward`` does (quantized_linear.rs:108-114).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import sys
+import threading
+from typing import Optional
+
+import numpy as np
+
+from . import build as _build
+
+KQ_OK = 0
+KQ_ERR_INVALID_ARG = 1
+KQ_ERR_UNSUPPORTED = 2
+KQ_ERR_CUDA = 3
+KQ_ERR_SHORT_BUFFER = 4
+KQ_ERR_NCCL = 5
+KQ_ERR_STATE = 6
+KQ_ERR_NOMEM = 7
+
+KQ_GGUF_Q4_K = 12
+KQ_GGUF_Q6_K = 14
+KQ_PESTI_Q4_K_LEGACY = 112
+KQ_PESTI_Q6_K_LEGACY = 114
+
+KQ_HOST_PTRS = 0
+KQ_DEVICE_PTRS = 1
+KQ_SYNC = 2
+
+#: every symbol include/pesti_kq.h declares
+EXPORTED_SYMBOLS = (
+    "kq_abi_version", "kq_status_string", "kq_last_error",
+    "kq_ctx_create", "kq_ctx_destroy", "kq_ctx_set_stream", "kq_ctx_synchronize",
+    "kq_ctx_reserve", "kq_ctx_launch_count", "kq_ctx_profile_begin", "kq_ctx_profile_end",
+    "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
+    "kq_linear_f32", "kq_dequant_f32",
+)
+
+
+class KqError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{message} (status {status})")
+        self.status = status
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def library_path() -> str:
+    return _build.LIB
+
+
+def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
+    """Load libpesti_kq.so (building it in-tree first if it is absent)."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB
+        if not os.path.exists(path):
+            if not build_if_missing:
+                raise KqError(KQ_ERR_STATE, f"{path} is missing; build it with python -m pesti_b200.build")
+            _build.build()
+        lib = ctypes.CDLL(path)
+        P, I, I64, Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
+        PP = ctypes.POINTER(ctypes.c_void_p)
+        sig = {
+            "kq_abi_version": ([], I),
+            "kq_status_string": ([I], ctypes.c_char_p),
+            "kq_last_error": ([P], ctypes.c_char_p),
+            "kq_ctx_create": ([I, PP], I),
+            "kq_ctx_destroy": ([P], I),
+            "kq_ctx_set_stream": ([P, P], I),
+            "kq_ctx_synchronize": ([P], I),
+            "kq_ctx_reserve": ([P, I64, I64], I),
+            "kq_ctx_launch_count": ([P], I64),
+            "kq_ctx_profile_begin": ([P, I], I),
+            "kq_ctx_profile_end": ([P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(I64)], I),
+            "kq_row_bytes": ([I, I64, ctypes.POINTER(I64)], I),
+            "kq_weight_upload": ([P, I, P, Z, I64, I64, PP], I),
+            "kq_weight_free": ([P], I),
+            "kq_weight_info": ([P, ctypes.POINTER(I), ctypes.POINTER(I64), ctypes.POINTER(I64),
+                                ctypes.POINTER(I64)], I),
+            "kq_linear_f32": ([P, P, P, I64, P, P, I], I),
+            "kq_dequant_f32": ([P, P, I64, I64, P, I], I),
+        }
+        for name, (args, res) in sig.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = lib
+        return lib
+
+
+def status_string(status: int) -> str:
+    return load_library().kq_status_string(status).decode()
+
+
+def row_bytes(kq_type: int, in_features: int) -> int:
+    out = ctypes.c_int64()
+    rc = load_library().kq_row_bytes(kq_type, in_features, ctypes.byref(out))
+    if rc:
+        raise KqError(rc, f"kq_row_bytes({kq_type}, {in_features}): {status_string(rc)}")
+    return out.value
+
+
+def _ptr(a) -> Optional[int]:
+    if a is None:
+        return None
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return int(a.data_ptr())  # torch tensor
+
+
+class Context:
+    """One device and one stream (include/pesti_kq.h kq_ctx)."""
+
+    def __init__(self, device: int = 0):
+        self.lib = load_library()
+        h = ctypes.c_void_p()
+        rc = self.lib.kq_ctx_create(device, ctypes.byref(h))
+        if rc:
+            raise KqError(rc, f"kq_ctx_create(device={device}) failed: {status_string(rc)}")
+        self.handle = h
+        self.device = device
+
+    def check(self, rc: int, what: str) -> None:
+        if rc:
+            msg = self.lib.kq_last_error(self.handle).decode()
+            raise KqError(rc, f"{what}: {msg or status_string(rc)}")
+
+    def set_stream(self, stream) -> None:
+        """Install a cudaStream_t (int handle, torch.cuda.Stream, or None)."""
+        if stream is not None and hasattr(stream, "cuda_stream"):
+            stream = stream.cuda_stream
+        handle = ctypes.c_void_p(int(stream)) if stream else None
+        self.check(self.lib.kq_ctx_set_stream(self.handle, handle), "kq_ctx_set_stream")
+
+    def synchronize(self) -> None:
+        self.check(self.lib.kq_ctx_synchronize(self.handle), "kq_ctx_synchronize")
+
+    def reserve(self, m: int, k: int) -> None:
+        self.check(self.lib.kq_ctx_reserve(self.handle, m, k), "kq_ctx_reserve")
+
+    @property
+    def launch_count(self) -> int:
+        return int(self.lib.kq_ctx_launch_count(self.handle))
+
+    def profile_begin(self, max_calls: int) -> None:
+        """Bracket the main kernel of the next max_calls compute calls with CUDA events."""
+        self.check(self.lib.kq_ctx_profile_begin(self.handle, max_calls), "kq_ctx_profile_begin")
+
+    def profile_end(self):
+        """-> (summed main-kernel milliseconds, number of bracketed calls)."""
+        ms, n = ctypes.c_double(), ctypes.c_int64()
+        self.check(self.lib.kq_ctx_profile_end(self.handle, ctypes.byref(ms), ctypes.byref(n)),
+                   "kq_ctx_profile_end")
+        return ms.value, n.value
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.lib.kq_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+_default_ctx = {}
+
+
+def default_context(device: int = 0) -> Context:
+    ctx = _default_ctx.get(device)
+    if ctx is None:
+        ctx = _default_ctx[device] = Context(device)
+    return ctx
+
+
+class Weight:
+    """A device-resident K-quant weight (kq_weight)."""
+
+    def __init__(self, ctx: Context, kq_type: int, data, out_features: int, in_features: int):
+        self.ctx = ctx
+        raw = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray))
+                                   else np.asarray(data, dtype=np.uint8)).reshape(-1)
+        h = ctypes.c_void_p()
+        rc = ctx.lib.kq_weight_upload(ctx.handle, kq_type, raw.ctypes.data if raw.size else None,
+                                      raw.size, out_features, in_features, ctypes.byref(h))
+        ctx.check(rc, "kq_weight_upload")
+        self.handle = h
+        self.kq_type = kq_type
+        self.out_features = out_features
+        self.in_features = in_features
+        dev_bytes = ctypes.c_int64()
+        ctx.lib.kq_weight_info(h, None, None, None, ctypes.byref(dev_bytes))
+        self.device_bytes = dev_bytes.value
+
+    def linear(self, x, m: int, y, bias=None, device_ptrs: bool = False, sync: bool = False) -> None:
+        flags = (KQ_DEVICE_PTRS if device_ptrs else KQ_HOST_PTRS) | (KQ_SYNC if sync else 0)
+        rc = self.ctx.lib.kq_linear_f32(self.ctx.handle, self.handle, _ptr(x), m, _ptr(bias), _ptr(y), flags)
+        self.ctx.check(rc, "kq_linear_f32")
+
+    def dequant(self, row0: int = 0, nrows: Optional[int] = None, out=None, device_ptrs: bool = False):
+        nrows = self.out_features - row0 if nrows is None else nrows
+        if out is None:
+            out = np.empty((nrows, self.in_features), np.float32)
+        flags = KQ_DEVICE_PTRS | KQ_SYNC if device_ptrs else KQ_HOST_PTRS
+        rc = self.ctx.lib.kq_dequant_f32(self.ctx.handle, self.handle, row0, nrows, _ptr(out), flags)
+        self.ctx.check(rc, "kq_dequant_f32")
+        return out
+
+    def free(self) -> None:
+        if getattr(self, "handle", None):
+            self.ctx.lib.kq_weight_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class QuantDtype:
+    """pesti-runner/src/tile_dequant.rs:394-402 (the K-quant members)."""
+    Q4_K = "Q4_K"
+    Q6_K = "Q6_K"
+
+
+_DTYPE_NAMES = {
+    "Q4_K": QuantDtype.Q4_K, "Q4_K_M": QuantDtype.Q4_K, "Q4_K_S": QuantDtype.Q4_K,
+    "Q6_K": QuantDtype.Q6_K, "Q6_K_S": QuantDtype.Q6_K,
+}
+
+_LAYOUTS = {
+    ("gguf", QuantDtype.Q4_K): KQ_GGUF_Q4_K,
+    ("gguf", QuantDtype.Q6_K): KQ_GGUF_Q6_K,
+    ("pesti-legacy", QuantDtype.Q4_K): KQ_PESTI_Q4_K_LEGACY,
+    ("pesti-legacy", QuantDtype.Q6_K): KQ_PESTI_Q6_K_LEGACY,
+}
+
+
+class QuantizedLinear:
+    """Drop-in for pesti-runner's ``QuantizedLinear`` on a B200.
+
+    ``layout="gguf"`` (default) reads GGUF superblocks (Q4_K 144 B / Q6_K
+    210 B per 256 weights).  ``layout="pesti-legacy"`` reads the reference's
+    own 28 B / 42 B per 16-weight blocks (tile_dequant.rs) so its CPU forward
+    can be reproduced byte for byte.
+    """
+
+    def __init__(self, data, dtype: str, in_features: int, out_features: int,
+                 bias=None, layout: str = "gguf", device: int = 0, ctx: Optional[Context] = None):
+        if (layout, dtype) not in _LAYOUTS:
+            raise KqError(KQ_ERR_UNSUPPORTED, f"unsupported layout/dtype {layout}/{dtype}")
+        self.dtype = dtype
+        self.layout = layout
+        self.in_features = int(in_features)
+        self.out_features = int(out_features)
+        self.kq_type = _LAYOUTS[(layout, dtype)]
+        self.data = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray))
+                                         else np.asarray(data, dtype=np.uint8)).reshape(-1)
+        self.bias = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32).reshape(-1)
+        self.ctx = ctx or default_context(device)
+        self._decode_error = None
+        self.weight = None
+        try:
+            self.weight = Weight(self.ctx, self.kq_type, self.data, self.out_features, self.in_features)
+        except KqError as e:
+            if e.status != KQ_ERR_SHORT_BUFFER:
+                raise
+            self._decode_error = str(e)
+
+    # quantized_linear.rs:27-41
+    @classmethod
+    def new(cls, data, dtype: str, in_features: int, out_features: int, bias=None, **kw):
+        return cls(data, dtype, in_features, out_features, bias, **kw)
+
+    # quantized_linear.rs:44-67
+    @classmethod
+    def from_quantized(cls, data, gguf_dtype: str, in_features: int, out_features: int, bias=None, **kw):
+        dtype = _DTYPE_NAMES.get(gguf_dtype)
+        if dtype is None:
+            raise KqError(KQ_ERR_UNSUPPORTED, f"Unsupported quantization type for QuantizedLinear: {gguf_dtype}")
+        return cls(data, dtype, in_features, out_features, bias, **kw)
+
+    # quantized_linear.rs:70-83
+    def memory_bytes(self) -> int:
+        return int(self.data.size + (0 if self.bias is None else self.bias.size * 4))
+
+    def f32_memory_bytes(self) -> int:
+        return self.in_features * self.out_features * 4 + (0 if self.bias is None else self.bias.size * 4)
+
+    def memory_savings(self) -> float:
+        return self.f32_memory_bytes() / self.memory_bytes()
+
+    def forward(self, x, batch_size: int) -> np.ndarray:
+        """y = x @ W^T + bias for x of batch_size * in_features f32 values
+        (quantized_linear.rs:101-143); returns batch_size * out_features f32."""
+        m, k, n = int(batch_size), self.in_features, self.out_features
+        y = np.zeros(m * n, np.float32)
+        if self._decode_error is not None:
+            print(f"dequantize_full_row_range error: {self._decode_error}", file=sys.stderr)
+            return y
+        xa = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+        if xa.size < m * k:
+            raise KqError(KQ_ERR_INVALID_ARG, f"x has {xa.size} values, batch {m} x {k} needs {m * k}")
+        self.weight.linear(xa, m, y, self.bias)
+        return y
+
+    def forward_device(self, x, bias=None, out=None):
+        """Device path: x is a CUDA torch tensor [m, in_features] f32 on this
+        context's device; runs on torch's current stream and returns y
+        [m, out_features] (no host round trip)."""
+        import torch
+        if self._decode_error is not None:
+            raise KqError(KQ_ERR_SHORT_BUFFER, self._decode_error)
+        if not (x.is_cuda and x.dtype == torch.float32 and x.is_contiguous()):
+            raise KqError(KQ_ERR_INVALID_ARG, "x must be a contiguous CUDA float32 tensor")
+        m = x.numel() // self.in_features
+        if out is None:
+            out = torch.empty((m, self.out_features), dtype=torch.float32, device=x.device)
+        self.ctx.set_stream(torch.cuda.current_stream(x.device).cuda_stream)
+        self.weight.linear(x, m, out, bias, device_ptrs=True)
+        return out

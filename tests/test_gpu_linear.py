@@ -1,0 +1,203 @@
+"""GPU parity: the sm_100a kernels, called through the C ABI, against the oracle.
+
+Bars (stated here, applied below):
+* dequantized values: bit-exact (NaN compared as NaN);
+* f32 linear: max|y - y_ref| / max|y_ref| <= 1e-3, y_ref = the oracle's
+  sequential f32 sum (the f64 error is also checked, to the same bar).
+"""
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+from pesti_b200 import kq, synthetic
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3
+
+
+def rel_err(y, ref):
+    y = np.asarray(y, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def same_bits(a, b):
+    a = np.asarray(a, np.float32).reshape(-1)
+    b = np.asarray(b, np.float32).reshape(-1)
+    return bool(np.all((a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))))
+
+
+GGUF = {"Q4_K": (kq.KQ_GGUF_Q4_K, oracle.GGUF_Q4_K), "Q6_K": (kq.KQ_GGUF_Q6_K, oracle.GGUF_Q6_K)}
+LEGACY = {"Q4_K": (kq.KQ_PESTI_Q4_K_LEGACY, oracle.PESTI_Q4_K_LEGACY),
+          "Q6_K": (kq.KQ_PESTI_Q6_K_LEGACY, oracle.PESTI_Q6_K_LEGACY)}
+
+
+# ---- dequantization: bit-exact -------------------------------------------
+
+@pytest.mark.parametrize("tag,dt", [("q4k", "Q4_K"), ("q6k", "Q6_K")])
+def test_dequant_golden_blocks_bit_exact(gpu_ctx, tag, dt):
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "gguf_kquant_golden.npz"))
+    raw = g[f"{tag}_raw"]
+    w = kq.Weight(gpu_ctx, GGUF[dt][0], raw, raw.shape[0], 256)
+    got = w.dequant()
+    assert same_bits(got, g[f"{tag}_bits"].view(np.float32))
+
+
+@pytest.mark.parametrize("dt,n,k", [("Q4_K", 4096, 4096), ("Q6_K", 4096, 14336), ("Q6_K", 7, 4864)])
+def test_dequant_random_bit_exact(gpu_ctx, dt, n, k):
+    kt, ot = GGUF[dt]
+    raw = synthetic.gguf_weight(kt, n, k, seed=11)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    for r0, nr in ((0, min(n, 48)), (max(0, n - 5), min(n, 5))):
+        assert same_bits(w.dequant(r0, nr), oracle.gguf_dequant_rows(ot, raw, n, k, r0, nr))
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("k", [16, 20, 50, 300, 4096])
+def test_dequant_legacy_bit_exact(gpu_ctx, dt, k):
+    kt, ot = LEGACY[dt]
+    n = 9
+    raw = synthetic.legacy_weight(kt, n, k, seed=k)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    assert same_bits(w.dequant(), oracle.legacy_dequant_rows(ot, raw, k, 0, n))
+
+
+# ---- linear: tolerance against the oracle ---------------------------------
+
+CASES = [
+    ("Q4_K", 4096, 4096, 1),   # decode GEMV, the Q4_K benchmark shape
+    ("Q4_K", 13, 256, 1),      # one superblock per row, odd row count
+    ("Q4_K", 257, 512, 3),
+    ("Q4_K", 64, 1024, 31),    # m not a multiple of the m-tile
+    ("Q6_K", 4096, 14336, 1),  # decode GEMV, the Q6_K benchmark shape
+    ("Q6_K", 4096, 14336, 8),
+    ("Q6_K", 4096, 14336, 32),
+    ("Q6_K", 33, 4864, 2),     # 19 superblocks per row
+    ("Q6_K", 1, 256, 5),
+]
+
+
+@pytest.mark.parametrize("dt,n,k,m", CASES)
+def test_linear_matches_oracle(gpu_ctx, dt, n, k, m):
+    kt, ot = GGUF[dt]
+    raw = synthetic.gguf_weight(kt, n, k, seed=n + k)
+    x = synthetic.activations(m, k, seed=m)
+    bias = np.random.default_rng(3).standard_normal(n).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    y = np.empty((m, n), np.float32)
+    w.linear(x, m, y, bias)
+    ref = oracle.gguf_linear(ot, raw, n, k, x, bias)
+    assert rel_err(y, ref) <= TOL
+    wf = oracle.gguf_dequant_rows(ot, raw, n, k).astype(np.float64)
+    ref64 = x.astype(np.float64) @ wf.T + bias
+    assert rel_err(y, ref64) <= TOL
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("n,k,m", [(37, 300, 1), (37, 300, 5), (16, 16, 2), (5, 20, 1)])
+def test_legacy_linear_matches_reference_forward(gpu_ctx, dt, n, k, m):
+    kt, ot = LEGACY[dt]
+    raw = synthetic.legacy_weight(kt, n, k, seed=7)
+    x = synthetic.activations(m, k, seed=8)
+    bias = np.linspace(-1, 1, n).astype(np.float32)
+    ql = kq.QuantizedLinear(raw, dt, k, n, bias, layout="pesti-legacy", ctx=gpu_ctx)
+    y = ql.forward(x.reshape(-1), m)
+    ref = oracle.legacy_forward(ot, raw, k, n, x, m, bias=bias)
+    assert y.shape == (m * n,)
+    assert rel_err(y, ref) <= TOL
+
+
+def test_device_pointer_path_on_a_torch_stream(gpu_ctx):
+    import torch
+    n, k, m = 4096, 4096, 4
+    raw = synthetic.q4_k_weight(n, k, seed=21)
+    x = synthetic.activations(m, k, seed=22)
+    ql = kq.QuantizedLinear.from_quantized(raw, "Q4_K_M", k, n, ctx=gpu_ctx)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        xd = torch.from_numpy(x).cuda()
+        before = gpu_ctx.launch_count
+        yd = ql.forward_device(xd)
+        assert gpu_ctx.launch_count > before
+    s.synchronize()
+    ref = oracle.gguf_linear(oracle.GGUF_Q4_K, raw, n, k, x)
+    assert rel_err(yd.cpu().numpy(), ref) <= TOL
+
+
+# ---- size-independent properties at full size ----------------------------
+
+@pytest.mark.parametrize("dt,n,k", [("Q4_K", 4096, 4096), ("Q6_K", 4096, 14336)])
+def test_linearity_and_zero_input(gpu_ctx, dt, n, k):
+    kt, _ = GGUF[dt]
+    raw = synthetic.gguf_weight(kt, n, k, seed=5)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    x1 = synthetic.activations(2, k, seed=1)
+    x2 = synthetic.activations(2, k, seed=2)
+    y1, y2, y3 = (np.empty((2, n), np.float32) for _ in range(3))
+    w.linear(x1, 2, y1)
+    w.linear(x2, 2, y2)
+    w.linear(2.0 * x1 + x2, 2, y3)
+    assert rel_err(y3, 2.0 * y1.astype(np.float64) + y2) <= TOL
+    bias = np.arange(n, dtype=np.float32)
+    y0 = np.empty((1, n), np.float32)
+    w.linear(np.zeros((1, k), np.float32), 1, y0, bias)
+    assert np.array_equal(y0.reshape(-1), bias)
+
+
+def test_repeat_calls_are_deterministic(gpu_ctx):
+    raw = synthetic.q6_k_weight(512, 4096, seed=9)
+    w = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q6_K, raw, 512, 4096)
+    x = synthetic.activations(3, 4096, seed=10)
+    a, b = np.empty((3, 512), np.float32), np.empty((3, 512), np.float32)
+    w.linear(x, 3, a)
+    w.linear(x, 3, b)
+    assert np.array_equal(a, b)
+
+
+# ---- drop-in behaviour and edge cases ------------------------------------
+
+def test_quantized_linear_memory_accounting(gpu_ctx):
+    raw = synthetic.q4_k_weight(8, 512, seed=1)
+    ql = kq.QuantizedLinear.new(raw, kq.QuantDtype.Q4_K, 512, 8, np.zeros(8, np.float32), ctx=gpu_ctx)
+    assert ql.memory_bytes() == raw.size + 32
+    assert ql.f32_memory_bytes() == 8 * 512 * 4 + 32
+    assert abs(ql.memory_savings() - (8 * 512 * 4 + 32) / (raw.size + 32)) < 1e-12
+
+
+def test_short_weight_returns_zeros_like_the_reference(gpu_ctx, capsys):
+    # quantized_linear.rs:108-114: decode error -> eprintln + zeros
+    raw = synthetic.q4_k_weight(4, 256, seed=1).reshape(-1)[:-1]
+    ql = kq.QuantizedLinear.from_quantized(raw, "Q4_K", 256, 4, ctx=gpu_ctx)
+    y = ql.forward(np.ones(256, np.float32), 1)
+    assert y.shape == (4,) and np.all(y == 0)
+    assert "dequantize_full_row_range error" in capsys.readouterr().err
+
+
+def test_empty_shapes(gpu_ctx):
+    w = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q4_K, np.zeros(0, np.uint8), 5, 0)
+    bias = np.arange(5, dtype=np.float32)
+    y = np.full((2, 5), -1.0, np.float32)
+    w.linear(np.zeros((2, 0), np.float32), 2, y, bias)
+    assert np.array_equal(y, np.stack([bias, bias]))
+    w2 = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q6_K, synthetic.q6_k_weight(3, 256), 3, 256)
+    w2.linear(np.zeros((0, 256), np.float32), 0, np.zeros((0, 3), np.float32))  # m = 0: no-op
+
+
+def test_invalid_arguments_report_status(gpu_ctx):
+    with pytest.raises(kq.KqError) as e:
+        kq.Weight(gpu_ctx, kq.KQ_GGUF_Q4_K, np.zeros(144, np.uint8), 1, 300)
+    assert e.value.status == kq.KQ_ERR_UNSUPPORTED
+    with pytest.raises(kq.KqError) as e:
+        kq.Weight(gpu_ctx, kq.KQ_GGUF_Q6_K, np.zeros(209, np.uint8), 1, 256)
+    assert e.value.status == kq.KQ_ERR_SHORT_BUFFER
+    w = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q6_K, synthetic.q6_k_weight(3, 256), 3, 256)
+    with pytest.raises(kq.KqError) as e:
+        w.dequant(2, 5)
+    assert e.value.status == kq.KQ_ERR_INVALID_ARG
+    rc = gpu_ctx.lib.kq_linear_f32(gpu_ctx.handle, w.handle, None, 1, None, None, 0)
+    assert rc == kq.KQ_ERR_INVALID_ARG
+    rc = gpu_ctx.lib.kq_linear_f32(gpu_ctx.handle, w.handle, None, 1, None, None, 0x40)
+    assert rc == kq.KQ_ERR_INVALID_ARG
