@@ -157,6 +157,11 @@ int kq_ctx_create(int device, kq_ctx** out) {
   if (device < 0 || device >= n) return KQ_ERR_INVALID_ARG;
   DeviceGuard g(device);
   if (g.status != cudaSuccess) return KQ_ERR_CUDA;
+  e = kq::gemv_init_device();
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return KQ_ERR_CUDA;
+  }
   kq_ctx* ctx = new kq_ctx();
   ctx->device = device;
   e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);

@@ -17,6 +17,24 @@
 
 namespace kq {
 
+// Device Q6_K body: where GGUF byte b (0..207: ql[128] | qh[64] | scales[16])
+// of a superblock is stored.  The 32 columns l of each 32-weight group are
+// split into four slots c = l/8; slot c's 48 bytes are contiguous at 48c:
+// pieces 0..3 = ql[64h + 32gg + 8c .. +8] (piece 2h+gg), pieces 4..5 =
+// qh[32h + 8c .. +8].  Scales stay at 192.  Slot c is what one lane of the
+// decode kernel reads with three 16-byte loads.
+__host__ __device__ __forceinline__ int q6k_body_offset(int b) {
+  if (b < 128) {
+    const int h = b >> 6, gg = (b >> 5) & 1, l = b & 31;
+    return 48 * (l >> 3) + 8 * (2 * h + gg) + (l & 7);
+  }
+  if (b < 192) {
+    const int i = b - 128, h = i >> 5, l = i & 31;
+    return 48 * (l >> 3) + 8 * (4 + h) + (l & 7);
+  }
+  return b;
+}
+
 // Exact f16 bits -> f32 (the hardware conversion is exact for every input).
 __device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
   return __half2float(__ushort_as_half(h));

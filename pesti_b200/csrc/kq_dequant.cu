@@ -29,11 +29,12 @@ __device__ __forceinline__ float gguf_q4k_value(const uint8_t* blk, int e) {
   return __fsub_rn(__fmul_rn(d1, (float)q), m1);
 }
 
+// Device Q6_K body (see q6k_body_offset): element e = 128h + 32g + l.
 __device__ __forceinline__ float gguf_q6k_value(const uint8_t* body, uint16_t dbits, int e) {
   const int h = e >> 7, g = (e >> 5) & 3, l = e & 31;
-  const uint8_t qlb = body[64 * h + l + 32 * (g & 1)];
+  const uint8_t qlb = body[q6k_body_offset(64 * h + l + 32 * (g & 1))];
   const int lo = (g < 2) ? (qlb & 0x0f) : (qlb >> 4);
-  const int hi = (body[128 + 32 * h + l] >> (2 * g)) & 3;
+  const int hi = (body[q6k_body_offset(128 + 32 * h + l)] >> (2 * g)) & 3;
   const int q = (lo | (hi << 4)) - 32;
   const int sc = (int)(int8_t)body[192 + (e >> 4)];
   const float d = f16_bits_to_f32(dbits);
@@ -103,18 +104,17 @@ __global__ void dequant_kernel(DevWeight w, int64_t row0, int64_t nrows, float* 
   }
 }
 
-__global__ void q6k_relayout_kernel(const uint16_t* __restrict__ raw, int64_t nsb,
-                                    uint16_t* __restrict__ body, uint16_t* __restrict__ d) {
-  const int64_t total = nsb * 105;  // 210 bytes = 105 halfwords
+__global__ void q6k_relayout_kernel(const uint8_t* __restrict__ raw, int64_t nsb,
+                                    uint8_t* __restrict__ body, uint16_t* __restrict__ d) {
+  const int64_t total = nsb * Q6K_BYTES;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t g = idx / 105;
-    const int wd = (int)(idx - g * 105);
-    const uint16_t v = raw[idx];
-    if (wd < 104)
-      body[g * 104 + wd] = v;
-    else
-      d[g] = v;
+    const int64_t g = idx / Q6K_BYTES;
+    const int b = (int)(idx - g * Q6K_BYTES);
+    if (b < Q6K_BODY)
+      body[g * Q6K_BODY + q6k_body_offset(b)] = raw[idx];
+    else if (b == Q6K_BODY)
+      d[g] = (uint16_t)(raw[idx] | (raw[idx + 1] << 8));
   }
 }
 
@@ -174,12 +174,11 @@ cudaError_t launch_dequant_f32(const DevWeight& w, int64_t row0, int64_t nrows, 
 
 cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t nsb, uint8_t* body, uint16_t* d,
                                 cudaStream_t s) {
-  const int64_t total = nsb * 105;
+  const int64_t total = nsb * Q6K_BYTES;
   if (total <= 0) return cudaSuccess;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 64) blocks = 148 * 64;
-  q6k_relayout_kernel<<<(unsigned)blocks, 256, 0, s>>>(reinterpret_cast<const uint16_t*>(raw), nsb,
-                                                       reinterpret_cast<uint16_t*>(body), d);
+  q6k_relayout_kernel<<<(unsigned)blocks, 256, 0, s>>>(raw, nsb, body, d);
   return cudaGetLastError();
 }
 

@@ -33,6 +33,10 @@ struct DevWeight {
   int64_t row_bytes;  // legacy row stride
 };
 
+// One-time per-device kernel set-up (shared-memory carve-outs); call with the
+// device current, outside any stream capture.
+cudaError_t gemv_init_device();
+
 // Scratch needed by launch_gemv_gguf for an m x k activation (bytes): the
 // permuted activations and per-run activation sums.
 size_t gemv_gguf_workspace_bytes(int64_t m, int64_t k);

@@ -77,6 +77,9 @@ CASES = [
     ("Q6_K", 4096, 14336, 32),
     ("Q6_K", 33, 4864, 2),     # 19 superblocks per row
     ("Q6_K", 1, 256, 5),
+    ("Q4_K", 100, 2048, 12),   # m > 8: hi-only fragments, 2 n-tiles
+    ("Q6_K", 48, 1536, 20),    # 3 n-tiles
+    ("Q4_K", 40, 768, 40),     # m > 32: two chunks
 ]
 
 
