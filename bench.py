@@ -63,6 +63,8 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="q6k-gemv")
     p.add_argument("--m", type=int, default=1)
+    p.add_argument("--path", choices=["auto", "tcgen05", "mma"], default="auto",
+                   help="kernel family for the GEMV (auto = tcgen05)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 
@@ -261,7 +263,8 @@ def run_ours(args, rank, world, local_rank):
                for i in range(NUM_WEIGHTS)]
     x = torch.from_numpy(synthetic.activations(m, k, seed=7 + rank)).to(dev)
     ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _ in range(NUM_WEIGHTS)]
-    ctx.reserve(m, k)
+    ctx.set_path({"auto": kq.KQ_PATH_AUTO, "tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA}[args.path])
+    ctx.reserve(weights[0], m)
 
     stream = torch.cuda.Stream(dev)
     ctx.set_stream(stream.cuda_stream)

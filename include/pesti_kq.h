@@ -54,6 +54,11 @@ enum kq_type {
 #define KQ_DEVICE_PTRS 1 /* x / bias / y are device pointers (async)      */
 #define KQ_SYNC 2        /* synchronise the context stream before return  */
 
+/* kernel families for GGUF weights with f32 activations (kq_ctx_set_path) */
+#define KQ_PATH_AUTO 0    /* default: the tcgen05 tensor-memory kernels       */
+#define KQ_PATH_TCGEN05 1 /* tcgen05.mma, dequantized A written to TMEM      */
+#define KQ_PATH_MMA 2     /* warp-level mma.sync tiles (cp.async staging)     */
+
 typedef struct kq_ctx kq_ctx;
 typedef struct kq_weight kq_weight;
 
@@ -64,10 +69,14 @@ int kq_ctx_create(int device, kq_ctx **out);
 int kq_ctx_destroy(kq_ctx *ctx);
 /* Install an external cudaStream_t (NULL restores the context's own). */
 int kq_ctx_set_stream(kq_ctx *ctx, void *cuda_stream);
+/* Wait for the context stream; also reports a device-side pipeline error of
+ * an earlier asynchronous call (KQ_ERR_CUDA with a message). */
 int kq_ctx_synchronize(kq_ctx *ctx);
-/* Reserve scratch for calls with up to `m` rows of `k` activations, so that
- * later calls allocate nothing (e.g. before CUDA-graph capture). */
-int kq_ctx_reserve(kq_ctx *ctx, int64_t m, int64_t k);
+/* Select the kernel family for GGUF weights (KQ_PATH_*). */
+int kq_ctx_set_path(kq_ctx *ctx, int path);
+/* Reserve scratch for calls on weight `w` with up to `m` activation rows, so
+ * that later calls allocate nothing (e.g. before CUDA-graph capture). */
+int kq_ctx_reserve(kq_ctx *ctx, const kq_weight *w, int64_t m);
 /* Number of kernels this context has launched so far. */
 int64_t kq_ctx_launch_count(const kq_ctx *ctx);
 /* Bracket the main kernel of each of the next `max_calls` compute calls with a
@@ -104,6 +113,12 @@ int kq_weight_info(const kq_weight *w, int *kq_type, int64_t *out_features,
  * (transformer/linear.rs:108-150).  bias may be NULL. */
 int kq_linear_f32(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t m,
                   const float *bias, float *y, int flags);
+/* Prefill form: x is bf16 [m][in] (raw 16-bit values), y f32 [m][out].  The
+ * weights are dequantized to bf16 tiles on the tensor cores (tcgen05); GGUF
+ * weights only.  No reference counterpart: the reference has no prefill
+ * kernel (the north-star prefill dequant-GEMM). */
+int kq_linear_bf16(kq_ctx *ctx, const kq_weight *w, const void *x_bf16, int64_t m,
+                   const float *bias, float *y, int flags);
 /* Dequantize rows [row0, row0+nrows) to f32 [nrows][in_features], bit-exact
  * with the CPU decode of the same encoding (QuantizedLinear::
  * dequantize_full_row_range, quantized_linear.rs:146-183, for legacy types). */

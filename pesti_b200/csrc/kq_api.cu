@@ -4,6 +4,7 @@
 // nothing here aborts, traps, or computes on the CPU.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -15,11 +16,17 @@
 
 struct kq_ctx {
   int device = 0;
+  int num_sms = 148;
+  int path = KQ_PATH_AUTO;
   cudaStream_t own_stream = nullptr;
   cudaStream_t stream = nullptr;
-  void* ws = nullptr;  // kernel scratch (permuted activations, partial sums)
+  void* ws = nullptr;  // kernel scratch (prepared activations, partial sums)
   size_t ws_bytes = 0;
-  void* xbuf = nullptr;  // device staging of host inputs
+  void* ctr = nullptr;  // split-K arrival counters: zero between calls
+  size_t ctr_bytes = 0;
+  int* dev_err = nullptr;   // set by a tensor-core kernel whose pipeline wait gave up
+  int* host_err = nullptr;  // pinned mirror of dev_err, read after synchronising
+  void* xbuf = nullptr;     // device staging of host inputs
   size_t xbuf_bytes = 0;
   void* ybuf = nullptr;  // device staging of host outputs
   size_t ybuf_bytes = 0;
@@ -86,8 +93,8 @@ struct DeviceGuard {
   }
 };
 
-// Grow-only device buffer.
-int ensure(kq_ctx* ctx, void** buf, size_t* have, size_t need, const char* what) {
+// Grow-only device buffer; `zero` clears a newly allocated buffer.
+int ensure(kq_ctx* ctx, void** buf, size_t* have, size_t need, const char* what, bool zero = false) {
   if (need <= *have) return KQ_OK;
   if (*buf) {
     cudaError_t e = cudaStreamSynchronize(ctx->stream);
@@ -103,6 +110,10 @@ int ensure(kq_ctx* ctx, void** buf, size_t* have, size_t need, const char* what)
     cudaGetLastError();
     return fail(ctx, KQ_ERR_NOMEM, "cudaMalloc(%zu) for %s failed: %s", sz, what,
                 cudaGetErrorString(e));
+  }
+  if (zero) {
+    e = cudaMemset(*buf, 0, sz);
+    if (e != cudaSuccess) return cuda_fail(ctx, e, "clear scratch");
   }
   *have = sz;
   return KQ_OK;
@@ -122,6 +133,49 @@ int64_t legacy_tile_bytes(int t, int64_t k) {
 }
 
 int check_ctx(kq_ctx* ctx) { return ctx ? KQ_OK : KQ_ERR_INVALID_ARG; }
+
+// After the stream is synchronised: report (and clear) a tensor-core pipeline
+// timeout.  The split-K counters may then be stale, so they are cleared too.
+int check_device_error(kq_ctx* ctx) {
+  const int code = *reinterpret_cast<volatile int*>(ctx->host_err);
+  if (code == 0) return KQ_OK;
+  *ctx->host_err = 0;
+  cudaMemset(ctx->dev_err, 0, sizeof(int));
+  if (ctx->ctr) cudaMemset(ctx->ctr, 0, ctx->ctr_bytes);
+  cudaDeviceSynchronize();
+  cudaGetLastError();
+  return fail(ctx, KQ_ERR_CUDA, "tensor-core pipeline wait gave up (code %d); the call's output is invalid",
+              code);
+}
+
+// Stream-ordered copy of the device error word into the pinned mirror.
+cudaError_t stage_error_word(kq_ctx* ctx) {
+  return cudaMemcpyAsync(ctx->host_err, ctx->dev_err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream);
+}
+
+int finish_sync(kq_ctx* ctx, const char* what) {
+  cudaError_t e = stage_error_word(ctx);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  return check_device_error(ctx);
+}
+
+bool use_tc(const kq_ctx* ctx, int type) {
+  return is_gguf(type) && ctx->path != KQ_PATH_MMA;
+}
+
+// Scratch and counters for a GGUF f32 call of m tokens on weight w.
+int prepare_f32(kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
+  if (use_tc(ctx, w.type)) {
+    int rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes(m, w.n, w.k, ctx->num_sms),
+                    "workspace");
+    if (rc) return rc;
+    size_t off = 0, cnt = 0;
+    kq::tc_counter_span(m, w.n, w.k, ctx->num_sms, &off, &cnt);
+    return ensure(ctx, &ctx->ctr, &ctx->ctr_bytes, cnt, "counters", true);
+  }
+  return ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::gemv_gguf_workspace_bytes(m, w.k), "workspace");
+}
 
 }  // namespace
 
@@ -158,18 +212,26 @@ int kq_ctx_create(int device, kq_ctx** out) {
   DeviceGuard g(device);
   if (g.status != cudaSuccess) return KQ_ERR_CUDA;
   e = kq::gemv_init_device();
+  if (e == cudaSuccess) e = kq::tc_init_device();
   if (e != cudaSuccess) {
     cudaGetLastError();
     return KQ_ERR_CUDA;
   }
   kq_ctx* ctx = new kq_ctx();
   ctx->device = device;
+  cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
   e = cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->dev_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(ctx->dev_err, 0, sizeof(int));
+  if (e == cudaSuccess) e = cudaHostAlloc(&ctx->host_err, sizeof(int), cudaHostAllocDefault);
   if (e != cudaSuccess) {
+    if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
     delete ctx;
     cudaGetLastError();
     return KQ_ERR_CUDA;
   }
+  *ctx->host_err = 0;
   ctx->stream = ctx->own_stream;
   *out = ctx;
   return KQ_OK;
@@ -181,6 +243,9 @@ int kq_ctx_destroy(kq_ctx* ctx) {
     DeviceGuard g(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->ctr) cudaFree(ctx->ctr);
+    if (ctx->dev_err) cudaFree(ctx->dev_err);
+    if (ctx->host_err) cudaFreeHost(ctx->host_err);
     if (ctx->xbuf) cudaFree(ctx->xbuf);
     if (ctx->ybuf) cudaFree(ctx->ybuf);
     if (ctx->bbuf) cudaFree(ctx->bbuf);
@@ -198,19 +263,28 @@ int kq_ctx_set_stream(kq_ctx* ctx, void* stream) {
   return KQ_OK;
 }
 
+int kq_ctx_set_path(kq_ctx* ctx, int path) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (path != KQ_PATH_AUTO && path != KQ_PATH_TCGEN05 && path != KQ_PATH_MMA)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "unknown path %d", path);
+  ctx->path = path;
+  return KQ_OK;
+}
+
 int kq_ctx_synchronize(kq_ctx* ctx) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   DeviceGuard g(ctx->device);
-  cudaError_t e = cudaStreamSynchronize(ctx->stream);
-  return e == cudaSuccess ? KQ_OK : cuda_fail(ctx, e, "cudaStreamSynchronize");
+  return finish_sync(ctx, "cudaStreamSynchronize");
 }
 
-int kq_ctx_reserve(kq_ctx* ctx, int64_t m, int64_t k) {
+int kq_ctx_reserve(kq_ctx* ctx, const kq_weight* w, int64_t m) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
-  if (m < 0 || k < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative size");
+  if (!w || m < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "bad reserve arguments");
+  if (!is_gguf(w->dw.type) || m == 0 || w->dw.k == 0) return KQ_OK;
   DeviceGuard g(ctx->device);
-  const int64_t kr = ((k + kq::QK - 1) / kq::QK) * kq::QK;
-  return ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::gemv_gguf_workspace_bytes(m, kr), "workspace");
+  int rc = prepare_f32(ctx, w->dw, m);
+  if (rc) return rc;
+  return ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes_bf16(m, w->dw.k), "workspace");
 }
 
 int64_t kq_ctx_launch_count(const kq_ctx* ctx) { return ctx ? ctx->launches : -1; }
@@ -236,12 +310,12 @@ int kq_ctx_profile_end(kq_ctx* ctx, double* total_ms, int64_t* count) {
   if (!ctx->prof_on) return fail(ctx, KQ_ERR_STATE, "profiling was not started");
   DeviceGuard g(ctx->device);
   ctx->prof_on = false;
-  cudaError_t e = cudaStreamSynchronize(ctx->stream);
-  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaStreamSynchronize");
+  int rc = finish_sync(ctx, "cudaStreamSynchronize");
+  if (rc) return rc;
   double sum = 0.0;
   for (int i = 0; i < ctx->prof_next; ++i) {
     float ms = 0.f;
-    e = cudaEventElapsedTime(&ms, ctx->prof_ev[2 * i], ctx->prof_ev[2 * i + 1]);
+    cudaError_t e = cudaEventElapsedTime(&ms, ctx->prof_ev[2 * i], ctx->prof_ev[2 * i + 1]);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaEventElapsedTime");
     sum += ms;
   }
@@ -264,19 +338,18 @@ int kq_row_bytes(int type, int64_t in_features, int64_t* out) {
   return KQ_ERR_UNSUPPORTED;
 }
 
-int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, int64_t n,
-                     int64_t k, kq_weight** out) {
+int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, int64_t n, int64_t k,
+                     kq_weight** out) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!out) return fail(ctx, KQ_ERR_INVALID_ARG, "out is null");
   *out = nullptr;
-  if (n < 0 || k < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative shape %lld x %lld",
-                                  (long long)n, (long long)k);
-  if (!is_gguf(type) && !is_legacy(type))
-    return fail(ctx, KQ_ERR_UNSUPPORTED, "unsupported kq_type %d", type);
+  if (n < 0 || k < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative shape %lld x %lld", (long long)n, (long long)k);
+  if (!is_gguf(type) && !is_legacy(type)) return fail(ctx, KQ_ERR_UNSUPPORTED, "unsupported kq_type %d", type);
   if (is_gguf(type) && k % kq::QK)
-    return fail(ctx, KQ_ERR_UNSUPPORTED,
-                "GGUF K-quant rows hold whole 256-weight superblocks; in_features=%lld",
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "GGUF K-quant rows hold whole 256-weight superblocks; in_features=%lld",
                 (long long)k);
+  if (n > (int64_t)1 << 31 || k > (int64_t)1 << 28)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "shape %lld x %lld too large", (long long)n, (long long)k);
   int64_t need;
   if (is_gguf(type)) {
     need = n * (k / kq::QK) * (type == kq::GGUF_Q4_K ? kq::Q4K_BYTES : kq::Q6K_BYTES);
@@ -284,8 +357,8 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
     need = (n == 0 || k == 0) ? 0 : (n - 1) * legacy_row_bytes(type, k) + legacy_tile_bytes(type, k);
   }
   if ((int64_t)nbytes < need)
-    return fail(ctx, KQ_ERR_SHORT_BUFFER, "weight has %zu bytes, shape %lld x %lld needs %lld",
-                nbytes, (long long)n, (long long)k, (long long)need);
+    return fail(ctx, KQ_ERR_SHORT_BUFFER, "weight has %zu bytes, shape %lld x %lld needs %lld", nbytes, (long long)n,
+                (long long)k, (long long)need);
   if (need > 0 && !bytes) return fail(ctx, KQ_ERR_INVALID_ARG, "bytes is null");
 
   DeviceGuard g(ctx->device);
@@ -301,16 +374,17 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
   const size_t pad = 64;  // vector loads never read past the allocation
   if (type == kq::GGUF_Q6_K) {
     const int64_t nsb = n * w->dw.sb;
+    const int64_t dld = kq::q6k_d_ld(n);
+    w->dw.d_ld = dld;
     void* raw = nullptr;
     e = cudaMalloc(&raw, (size_t)nsb * kq::Q6K_BYTES + pad);
     if (e == cudaSuccess) e = cudaMalloc(&w->q_alloc, (size_t)nsb * kq::Q6K_BODY + pad);
-    if (e == cudaSuccess) e = cudaMalloc(&w->d_alloc, (size_t)nsb * 2 + pad);
+    if (e == cudaSuccess) e = cudaMalloc(&w->d_alloc, (size_t)w->dw.sb * dld * 2 + pad);
+    if (e == cudaSuccess) e = cudaMemsetAsync(w->d_alloc, 0, (size_t)w->dw.sb * dld * 2 + pad, ctx->stream);
     if (e == cudaSuccess && nsb)
-      e = cudaMemcpyAsync(raw, bytes, (size_t)nsb * kq::Q6K_BYTES, cudaMemcpyHostToDevice,
-                          ctx->stream);
+      e = cudaMemcpyAsync(raw, bytes, (size_t)nsb * kq::Q6K_BYTES, cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess)
-      e = kq::launch_q6k_relayout(static_cast<const uint8_t*>(raw), nsb,
-                                  static_cast<uint8_t*>(w->q_alloc),
+      e = kq::launch_q6k_relayout(static_cast<const uint8_t*>(raw), n, w->dw.sb, static_cast<uint8_t*>(w->q_alloc),
                                   static_cast<uint16_t*>(w->d_alloc), ctx->stream);
     if (e == cudaSuccess) {
       ++ctx->launches;
@@ -337,6 +411,12 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
   }
   w->dw.q = static_cast<const uint8_t*>(w->q_alloc);
   w->dw.d = static_cast<const uint16_t*>(w->d_alloc);
+  if (is_gguf(type) && n > 0 && k > 0 && !kq::tc_make_weight_maps(w->dw)) {
+    cudaFree(w->q_alloc);
+    if (w->d_alloc) cudaFree(w->d_alloc);
+    delete w;
+    return fail(ctx, KQ_ERR_CUDA, "could not build the weight's TMA descriptors");
+  }
   *out = w;
   return KQ_OK;
 }
@@ -360,15 +440,18 @@ int kq_weight_info(const kq_weight* w, int* type, int64_t* n, int64_t* k, int64_
   return KQ_OK;
 }
 
-int kq_linear_f32(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, const float* bias,
-                  float* y, int flags) {
+// Shared body of kq_linear_f32 / kq_linear_bf16.
+static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xelem, int64_t m, const float* bias,
+                       float* y, int flags, bool bf16) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!w) return fail(ctx, KQ_ERR_INVALID_ARG, "weight is null");
   if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
   if (w->device != ctx->device)
-    return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device,
-                ctx->device);
+    return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device, ctx->device);
   if (m < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative m");
+  if (m > (int64_t)1 << 24) return fail(ctx, KQ_ERR_UNSUPPORTED, "m = %lld is too large", (long long)m);
+  if (bf16 && !is_gguf(w->dw.type))
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "bf16 activations need a GGUF Q4_K / Q6_K weight");
   const int64_t n = w->dw.n, k = w->dw.k;
   if (m == 0 || n == 0) return KQ_OK;
   if (!y || (k > 0 && !x)) return fail(ctx, KQ_ERR_INVALID_ARG, "x or y is null");
@@ -379,14 +462,14 @@ int kq_linear_f32(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, co
   cudaError_t e = cudaSuccess;
   int rc;
 
-  const float* xd = x;
+  const void* xd = x;
   const float* bd = bias;
   float* yd = y;
   if (!dev) {
-    if ((rc = ensure(ctx, &ctx->xbuf, &ctx->xbuf_bytes, (size_t)(m * k * 4), "input staging"))) return rc;
+    if ((rc = ensure(ctx, &ctx->xbuf, &ctx->xbuf_bytes, (size_t)(m * k) * xelem, "input staging"))) return rc;
     if ((rc = ensure(ctx, &ctx->ybuf, &ctx->ybuf_bytes, (size_t)(m * n * 4), "output staging"))) return rc;
     if (k > 0) {
-      e = cudaMemcpyAsync(ctx->xbuf, x, (size_t)(m * k * 4), cudaMemcpyHostToDevice, s);
+      e = cudaMemcpyAsync(ctx->xbuf, x, (size_t)(m * k) * xelem, cudaMemcpyHostToDevice, s);
       if (e != cudaSuccess) return cuda_fail(ctx, e, "copy x to device");
     }
     if (bias) {
@@ -395,7 +478,7 @@ int kq_linear_f32(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, co
       if (e != cudaSuccess) return cuda_fail(ctx, e, "copy bias to device");
       bd = static_cast<const float*>(ctx->bbuf);
     }
-    xd = static_cast<const float*>(ctx->xbuf);
+    xd = ctx->xbuf;
     yd = static_cast<float*>(ctx->ybuf);
   }
 
@@ -408,12 +491,21 @@ int kq_linear_f32(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, co
     } else {
       e = cudaMemsetAsync(yd, 0, (size_t)(m * n * 4), s);
     }
+  } else if (bf16) {
+    if ((rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes_bf16(m, k), "workspace"))) return rc;
+    e = kq::launch_tc_bf16(w->dw, xd, m, bd, yd, ctx->ws, ctx->dev_err, s, &launches, ctx->next_bracket());
   } else if (is_gguf(w->dw.type)) {
-    if ((rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::gemv_gguf_workspace_bytes(m, k), "workspace")))
-      return rc;
-    e = kq::launch_gemv_gguf(w->dw, xd, m, bd, yd, ctx->ws, s, &launches, ctx->next_bracket());
+    if ((rc = prepare_f32(ctx, w->dw, m))) return rc;
+    if (use_tc(ctx, w->dw.type)) {
+      // counters live in their own zeroed buffer; the scratch layout's counter span is unused
+      e = kq::launch_tc_f32(w->dw, static_cast<const float*>(xd), m, bd, yd, ctx->ws, ctx->num_sms, ctx->dev_err,
+                            s, &launches, ctx->next_bracket(), static_cast<unsigned*>(ctx->ctr));
+    } else {
+      e = kq::launch_gemv_gguf(w->dw, static_cast<const float*>(xd), m, bd, yd, ctx->ws, s, &launches,
+                               ctx->next_bracket());
+    }
   } else {
-    e = kq::launch_gemv_legacy(w->dw, xd, m, bd, yd, s, &launches, ctx->next_bracket());
+    e = kq::launch_gemv_legacy(w->dw, static_cast<const float*>(xd), m, bd, yd, s, &launches, ctx->next_bracket());
   }
   ctx->launches += launches;
   if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
@@ -421,15 +513,21 @@ int kq_linear_f32(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, co
     e = cudaMemcpyAsync(y, ctx->ybuf, (size_t)(m * n * 4), cudaMemcpyDeviceToHost, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "copy y to host");
   }
-  if (!dev || (flags & KQ_SYNC)) {
-    e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "kq_linear_f32");
-  }
+  if (!dev || (flags & KQ_SYNC)) return finish_sync(ctx, "linear");
   return KQ_OK;
 }
 
-int kq_dequant_f32(kq_ctx* ctx, const kq_weight* w, int64_t row0, int64_t nrows, float* out,
+int kq_linear_f32(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, const float* bias, float* y,
+                  int flags) {
+  return linear_impl(ctx, w, x, 4, m, bias, y, flags, false);
+}
+
+int kq_linear_bf16(kq_ctx* ctx, const kq_weight* w, const void* x_bf16, int64_t m, const float* bias, float* y,
                    int flags) {
+  return linear_impl(ctx, w, x_bf16, 2, m, bias, y, flags, true);
+}
+
+int kq_dequant_f32(kq_ctx* ctx, const kq_weight* w, int64_t row0, int64_t nrows, float* out, int flags) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!w) return fail(ctx, KQ_ERR_INVALID_ARG, "weight is null");
   if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
@@ -456,10 +554,7 @@ int kq_dequant_f32(kq_ctx* ctx, const kq_weight* w, int64_t row0, int64_t nrows,
     e = cudaMemcpyAsync(out, od, (size_t)count * 4, cudaMemcpyDeviceToHost, ctx->stream);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "copy to host");
   }
-  if (!dev || (flags & KQ_SYNC)) {
-    e = cudaStreamSynchronize(ctx->stream);
-    if (e != cudaSuccess) return cuda_fail(ctx, e, "kq_dequant_f32");
-  }
+  if (!dev || (flags & KQ_SYNC)) return finish_sync(ctx, "kq_dequant_f32");
   return KQ_OK;
 }
 

@@ -89,8 +89,9 @@ __global__ void dequant_kernel(DevWeight w, int64_t row0, int64_t nrows, float* 
         v = gguf_q4k_value(w.q + ((size_t)r * w.sb + i / QK) * Q4K_BYTES, (int)(i % QK));
         break;
       case GGUF_Q6_K: {
-        const size_t g = (size_t)r * w.sb + i / QK;
-        v = gguf_q6k_value(w.q + g * Q6K_BODY, w.d[g], (int)(i % QK));
+        const int64_t kb = i / QK;
+        const size_t g = (size_t)r * w.sb + kb;
+        v = gguf_q6k_value(w.q + g * Q6K_BODY, w.d[kb * w.d_ld + r], (int)(i % QK));
         break;
       }
       case LEGACY_Q4_K:
@@ -104,17 +105,20 @@ __global__ void dequant_kernel(DevWeight w, int64_t row0, int64_t nrows, float* 
   }
 }
 
-__global__ void q6k_relayout_kernel(const uint8_t* __restrict__ raw, int64_t nsb,
+__global__ void q6k_relayout_kernel(const uint8_t* __restrict__ raw, int64_t n, int64_t sb,
                                     uint8_t* __restrict__ body, uint16_t* __restrict__ d) {
-  const int64_t total = nsb * Q6K_BYTES;
+  const int64_t total = n * sb * Q6K_BYTES;
+  const int64_t ld = q6k_d_ld(n);
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t g = idx / Q6K_BYTES;
+    const int64_t g = idx / Q6K_BYTES;  // row * sb + kb
     const int b = (int)(idx - g * Q6K_BYTES);
-    if (b < Q6K_BODY)
+    if (b < Q6K_BODY) {
       body[g * Q6K_BODY + q6k_body_offset(b)] = raw[idx];
-    else if (b == Q6K_BODY)
-      d[g] = (uint16_t)(raw[idx] | (raw[idx + 1] << 8));
+    } else if (b == Q6K_BODY) {
+      const int64_t row = g / sb, kb = g - row * sb;
+      d[kb * ld + row] = (uint16_t)(raw[idx] | (raw[idx + 1] << 8));
+    }
   }
 }
 
@@ -172,13 +176,13 @@ cudaError_t launch_dequant_f32(const DevWeight& w, int64_t row0, int64_t nrows, 
   return cudaGetLastError();
 }
 
-cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t nsb, uint8_t* body, uint16_t* d,
+cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t n, int64_t sb, uint8_t* body, uint16_t* d,
                                 cudaStream_t s) {
-  const int64_t total = nsb * Q6K_BYTES;
+  const int64_t total = n * sb * Q6K_BYTES;
   if (total <= 0) return cudaSuccess;
   int64_t blocks = (total + 255) / 256;
   if (blocks > 148 * 64) blocks = 148 * 64;
-  q6k_relayout_kernel<<<(unsigned)blocks, 256, 0, s>>>(raw, nsb, body, d);
+  q6k_relayout_kernel<<<(unsigned)blocks, 256, 0, s>>>(raw, n, sb, body, d);
   return cudaGetLastError();
 }
 

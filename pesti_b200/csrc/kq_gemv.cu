@@ -180,7 +180,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // Copy superblock kb of rows ra (= tile row g) and rb (= g + 8) into `slot`.
 template <int QT>
 __device__ __forceinline__ void stage_issue(uint8_t* slot, const uint8_t* __restrict__ wq,
-                                            const uint16_t* __restrict__ wd, int64_t ra,
+                                            const uint16_t* __restrict__ wd, int64_t n, int64_t ra,
                                             int64_t rb, int sb, int kb, int g, int c, int lane) {
   using S = Stage<QT>;
   const size_t ga = (size_t)ra * sb + kb, gb = (size_t)rb * sb + kb;
@@ -203,15 +203,17 @@ __device__ __forceinline__ void stage_issue(uint8_t* slot, const uint8_t* __rest
     cp_async16(la + 48, B + 48 * c);
     cp_async16(la + 64, B + 48 * c + 16);
     cp_async16(la + 80, B + 48 * c + 32);
-    cp_async4(la + 96, wd + (ga & ~size_t(1)));
-    cp_async4(la + 100, wd + (gb & ~size_t(1)));
+    // d is superblock-major [sb][d_ld]: copy the aligned pair holding d(row, kb)
+    const size_t dld = (size_t)q6k_d_ld(n);
+    cp_async4(la + 96, wd + (size_t)kb * dld + (size_t)(ra & ~int64_t(1)));
+    cp_async4(la + 100, wd + (size_t)kb * dld + (size_t)(rb & ~int64_t(1)));
     if (c == 0) cp_async16(slot + S::HDR + 16 * g, A + 192);
     if (c == 1) cp_async16(slot + S::HDR + 16 * (g + 8), B + 192);
   }
 }
 
 template <int QT>
-__device__ __forceinline__ void stage_read(const uint8_t* slot, int64_t ga_idx, int64_t gb_idx,
+__device__ __forceinline__ void stage_read(const uint8_t* slot, int64_t ra, int64_t rb,
                                            int g, int lane, typename RawT<QT>::type& a,
                                            typename RawT<QT>::type& b) {
   using S = Stage<QT>;
@@ -232,8 +234,8 @@ __device__ __forceinline__ void stage_read(const uint8_t* slot, int64_t ga_idx, 
     b.p23 = l4[4];
     b.p45 = l4[5];
     const uint2 dd = *reinterpret_cast<const uint2*>(la + 96);
-    a.d = (ga_idx & 1) ? (dd.x >> 16) : (dd.x & 0xffff);
-    b.d = (gb_idx & 1) ? (dd.y >> 16) : (dd.y & 0xffff);
+    a.d = (ra & 1) ? (dd.x >> 16) : (dd.x & 0xffff);
+    b.d = (rb & 1) ? (dd.y >> 16) : (dd.y & 0xffff);
     a.sc = *reinterpret_cast<const uint4*>(slot + S::HDR + 16 * g);
     b.sc = *reinterpret_cast<const uint4*>(slot + S::HDR + 16 * (g + 8));
   }
@@ -401,7 +403,7 @@ __global__ void __launch_bounds__(32 * KSPLIT_WARPS)
 #pragma unroll
   for (int j = 0; j < ST - 1; ++j) {
     const int kj = warp + j * KSPLIT_WARPS;
-    if (kj < sb) stage_issue<QT>(wring + j * slot, wq, wd, ra, rb, sb, kj, g, c, lane);
+    if (kj < sb) stage_issue<QT>(wring + j * slot, wq, wd, n, ra, rb, sb, kj, g, c, lane);
     if (!STAGEB) cp_async_commit();
   }
   pdl_wait();  // activation fragments are written by the preceding prep kernel
@@ -426,7 +428,7 @@ __global__ void __launch_bounds__(32 * KSPLIT_WARPS)
       const int kn = kb + (ST - 1) * KSPLIT_WARPS;
       if (kn < sb) {
         uint8_t* sl = wring + ((it + ST - 1) % ST) * slot;
-        stage_issue<QT>(sl, wq, wd, ra, rb, sb, kn, g, c, lane);
+        stage_issue<QT>(sl, wq, wd, n, ra, rb, sb, kn, g, c, lane);
         if (STAGEB) stage_issue_b(sl + Stage<QT>::BYTES, bf, scl, kn, m, g, c, lane);
       }
       cp_async_commit();
@@ -435,7 +437,7 @@ __global__ void __launch_bounds__(32 * KSPLIT_WARPS)
     __syncwarp();
     const uint8_t* cur = wring + (it % ST) * slot;
     Raw ca, cb;
-    stage_read<QT>(cur, ra * sb + kb, rb * sb + kb, g, lane, ca, cb);
+    stage_read<QT>(cur, ra, rb, g, lane, ca, cb);
     // B fragments of this superblock, from the slot or (m > 4) from L2
     const uint4* bs = bcol[0] ? reinterpret_cast<const uint4*>(cur + Stage<QT>::BYTES + 16 +
                                                                compact * 128)

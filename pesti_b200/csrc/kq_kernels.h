@@ -2,6 +2,7 @@
 // (kq_api.cu) and the kernels.  Not part of the public ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -22,16 +23,23 @@ enum QType : int {
 // Device-resident weight.  For GGUF types the row count is n, the row length k
 // (a multiple of 256) and sb = k/256 superblocks per row.
 //  GGUF_Q4_K: q = raw GGUF superblocks [n][sb][144]; d unused.
-//  GGUF_Q6_K: q = bodies [n][sb][208] (ql|qh|scales), d = f16 [n][sb].
+//  GGUF_Q6_K: q = bodies [n][sb][208] (ql|qh|scales), d = f16 [sb][d_ld]
+//             (superblock-major, rows padded to d_ld = n rounded up to 8, so
+//             the d values of 128 consecutive rows are one 256-byte run).
 //  LEGACY_*:  q = raw bytes as uploaded (row stride = legacy row bytes), len.
+// wmap / dmap: TMA descriptors of q (128 rows x one superblock per box) and d.
 struct DevWeight {
   int type;
   int64_t n, k, sb;
   const uint8_t* q;
   const uint16_t* d;
+  int64_t d_ld;
   int64_t len;        // uploaded byte count (legacy) / device bytes
   int64_t row_bytes;  // legacy row stride
+  CUtensorMap wmap, dmap;
 };
+
+__host__ __device__ inline int64_t q6k_d_ld(int64_t n) { return (n + 7) & ~int64_t(7); }
 
 // One-time per-device kernel set-up (shared-memory carve-outs); call with the
 // device current, outside any stream capture.
@@ -68,8 +76,30 @@ cudaError_t launch_gemv_legacy(const DevWeight& w, const float* x, int64_t m, co
 cudaError_t launch_dequant_f32(const DevWeight& w, int64_t row0, int64_t nrows, float* out,
                                cudaStream_t s);
 
-// Re-lay GGUF Q6_K superblocks [nsb][210] into bodies [nsb][208] + d [nsb].
-cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t nsb, uint8_t* body, uint16_t* d,
+// Re-lay GGUF Q6_K superblocks [n][sb][210] into bodies [n][sb][208] and
+// d [sb][d_ld] (padding entries are left as they are).
+cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t n, int64_t sb, uint8_t* body, uint16_t* d,
                                 cudaStream_t s);
+
+// ---- tensor-core (tcgen05) path: kq_mma.cu ----
+// Build the TMA descriptors of a GGUF weight (after its device arrays exist).
+bool tc_make_weight_maps(DevWeight& w);
+// Per-device set-up of the tcgen05 kernels (shared-memory carve-outs).
+cudaError_t tc_init_device();
+// Scratch for launch_tc_f32 / launch_tc_bf16.
+size_t tc_workspace_bytes(int64_t m, int64_t n, int64_t k, int num_sms);
+size_t tc_workspace_bytes_bf16(int64_t m, int64_t k);
+// Bytes of split-K arrival counters launch_tc_f32 needs (reported as a span;
+// `offset` is kept for callers that place them after the scratch).  They must
+// be zero before the first call; the kernel leaves them zero.
+void tc_counter_span(int64_t m, int64_t n, int64_t k, int num_sms, size_t* offset, size_t* count);
+// y = x . W^T (+bias) with f32 x (split into f16 hi/lo) on tcgen05 tensor cores.
+// *err (device int) receives a nonzero code if a pipeline wait gave up.
+cudaError_t launch_tc_f32(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y,
+                          void* ws, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br,
+                          unsigned* counters);
+// Same with bf16 x (prefill); A is dequantized to bf16.
+cudaError_t launch_tc_bf16(const DevWeight& w, const void* x, int64_t m, const float* bias, float* y,
+                           void* ws, int* err, cudaStream_t s, int* launches, Bracket br = Bracket());
 
 }  // namespace kq

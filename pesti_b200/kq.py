@@ -45,13 +45,17 @@ KQ_HOST_PTRS = 0
 KQ_DEVICE_PTRS = 1
 KQ_SYNC = 2
 
+KQ_PATH_AUTO = 0
+KQ_PATH_TCGEN05 = 1
+KQ_PATH_MMA = 2
+
 #: every symbol include/pesti_kq.h declares
 EXPORTED_SYMBOLS = (
     "kq_abi_version", "kq_status_string", "kq_last_error",
     "kq_ctx_create", "kq_ctx_destroy", "kq_ctx_set_stream", "kq_ctx_synchronize",
-    "kq_ctx_reserve", "kq_ctx_launch_count", "kq_ctx_profile_begin", "kq_ctx_profile_end",
-    "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
-    "kq_linear_f32", "kq_dequant_f32",
+    "kq_ctx_set_path", "kq_ctx_reserve", "kq_ctx_launch_count", "kq_ctx_profile_begin",
+    "kq_ctx_profile_end", "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
+    "kq_linear_f32", "kq_linear_bf16", "kq_dequant_f32",
 )
 
 
@@ -91,7 +95,8 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
             "kq_ctx_destroy": ([P], I),
             "kq_ctx_set_stream": ([P, P], I),
             "kq_ctx_synchronize": ([P], I),
-            "kq_ctx_reserve": ([P, I64, I64], I),
+            "kq_ctx_set_path": ([P, I], I),
+            "kq_ctx_reserve": ([P, P, I64], I),
             "kq_ctx_launch_count": ([P], I64),
             "kq_ctx_profile_begin": ([P, I], I),
             "kq_ctx_profile_end": ([P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(I64)], I),
@@ -101,6 +106,7 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
             "kq_weight_info": ([P, ctypes.POINTER(I), ctypes.POINTER(I64), ctypes.POINTER(I64),
                                 ctypes.POINTER(I64)], I),
             "kq_linear_f32": ([P, P, P, I64, P, P, I], I),
+            "kq_linear_bf16": ([P, P, P, I64, P, P, I], I),
             "kq_dequant_f32": ([P, P, I64, I64, P, I], I),
         }
         for name, (args, res) in sig.items():
@@ -158,8 +164,13 @@ class Context:
     def synchronize(self) -> None:
         self.check(self.lib.kq_ctx_synchronize(self.handle), "kq_ctx_synchronize")
 
-    def reserve(self, m: int, k: int) -> None:
-        self.check(self.lib.kq_ctx_reserve(self.handle, m, k), "kq_ctx_reserve")
+    def set_path(self, path: int) -> None:
+        """KQ_PATH_AUTO / KQ_PATH_TCGEN05 / KQ_PATH_MMA for GGUF weights."""
+        self.check(self.lib.kq_ctx_set_path(self.handle, path), "kq_ctx_set_path")
+
+    def reserve(self, weight: "Weight", m: int) -> None:
+        """Allocate the scratch calls on `weight` with up to m rows need."""
+        self.check(self.lib.kq_ctx_reserve(self.handle, weight.handle, m), "kq_ctx_reserve")
 
     @property
     def launch_count(self) -> int:
@@ -221,6 +232,12 @@ class Weight:
         flags = (KQ_DEVICE_PTRS if device_ptrs else KQ_HOST_PTRS) | (KQ_SYNC if sync else 0)
         rc = self.ctx.lib.kq_linear_f32(self.ctx.handle, self.handle, _ptr(x), m, _ptr(bias), _ptr(y), flags)
         self.ctx.check(rc, "kq_linear_f32")
+
+    def linear_bf16(self, x, m: int, y, bias=None, device_ptrs: bool = False, sync: bool = False) -> None:
+        """x holds bf16 bit patterns (uint16 numpy array or bf16 torch tensor)."""
+        flags = (KQ_DEVICE_PTRS if device_ptrs else KQ_HOST_PTRS) | (KQ_SYNC if sync else 0)
+        rc = self.ctx.lib.kq_linear_bf16(self.ctx.handle, self.handle, _ptr(x), m, _ptr(bias), _ptr(y), flags)
+        self.ctx.check(rc, "kq_linear_bf16")
 
     def dequant(self, row0: int = 0, nrows: Optional[int] = None, out=None, device_ptrs: bool = False):
         nrows = self.out_features - row0 if nrows is None else nrows

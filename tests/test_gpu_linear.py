@@ -83,13 +83,38 @@ CASES = [
 ]
 
 
+PATHS = {"tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA}
+
+
+@pytest.fixture(params=sorted(PATHS))
+def path_ctx(gpu_ctx, request):
+    gpu_ctx.set_path(PATHS[request.param])
+    yield gpu_ctx
+    gpu_ctx.set_path(kq.KQ_PATH_AUTO)
+
+
+def test_tcgen05_single_tile_first(gpu_ctx):
+    # the smallest tensor-core case (one CTA, one superblock) before anything larger
+    gpu_ctx.set_path(kq.KQ_PATH_TCGEN05)
+    try:
+        for kt, ot in GGUF.values():
+            raw = synthetic.gguf_weight(kt, 128, 256, seed=1)
+            x = synthetic.activations(1, 256, seed=2)
+            w = kq.Weight(gpu_ctx, kt, raw, 128, 256)
+            y = np.empty((1, 128), np.float32)
+            w.linear(x, 1, y)
+            assert rel_err(y, oracle.gguf_linear(ot, raw, 128, 256, x)) <= TOL
+    finally:
+        gpu_ctx.set_path(kq.KQ_PATH_AUTO)
+
+
 @pytest.mark.parametrize("dt,n,k,m", CASES)
-def test_linear_matches_oracle(gpu_ctx, dt, n, k, m):
+def test_linear_matches_oracle(path_ctx, dt, n, k, m):
     kt, ot = GGUF[dt]
     raw = synthetic.gguf_weight(kt, n, k, seed=n + k)
     x = synthetic.activations(m, k, seed=m)
     bias = np.random.default_rng(3).standard_normal(n).astype(np.float32)
-    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    w = kq.Weight(path_ctx, kt, raw, n, k)
     y = np.empty((m, n), np.float32)
     w.linear(x, m, y, bias)
     ref = oracle.gguf_linear(ot, raw, n, k, x, bias)
@@ -97,6 +122,37 @@ def test_linear_matches_oracle(gpu_ctx, dt, n, k, m):
     wf = oracle.gguf_dequant_rows(ot, raw, n, k).astype(np.float64)
     ref64 = x.astype(np.float64) @ wf.T + bias
     assert rel_err(y, ref64) <= TOL
+
+
+# ---- prefill: bf16 activations on tcgen05, <= 2e-2 against the f32 product ----
+
+PREFILL_TOL = 2e-2
+PREFILL_CASES = [
+    ("Q4_K", 4096, 4096, 512),
+    ("Q6_K", 1024, 4096, 300),   # m not a multiple of the 256-token tile
+    ("Q4_K", 100, 1024, 37),     # partial row tile, few tokens
+    ("Q6_K", 256, 4864, 257),
+]
+
+
+def to_bf16_bits(x):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(x, np.float32)).to(torch.bfloat16)
+    return t.view(torch.int16).numpy().view(np.uint16), t.float().numpy()
+
+
+@pytest.mark.parametrize("dt,n,k,m", PREFILL_CASES)
+def test_prefill_bf16_matches_f32_product(gpu_ctx, dt, n, k, m):
+    kt, ot = GGUF[dt]
+    raw = synthetic.gguf_weight(kt, n, k, seed=n + 3 * k)
+    bits, xr = to_bf16_bits(synthetic.activations(m, k, seed=m + 1))
+    bias = np.random.default_rng(4).standard_normal(n).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    y = np.empty((m, n), np.float32)
+    w.linear_bf16(bits, m, y, bias)
+    wf = oracle.gguf_dequant_rows(ot, raw, n, k).astype(np.float64)
+    ref = xr.astype(np.float64) @ wf.T + bias
+    assert rel_err(y, ref) <= PREFILL_TOL
 
 
 @pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
