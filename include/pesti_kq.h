@@ -55,9 +55,11 @@ enum kq_type {
 #define KQ_SYNC 2        /* synchronise the context stream before return  */
 
 /* kernel families for GGUF weights with f32 activations (kq_ctx_set_path) */
-#define KQ_PATH_AUTO 0    /* default: the tcgen05 tensor-memory kernels       */
+#define KQ_PATH_AUTO 0    /* default: DP4A for m <= 4, else TCGEN05           */
 #define KQ_PATH_TCGEN05 1 /* tcgen05.mma, dequantized A written to TMEM      */
 #define KQ_PATH_MMA 2     /* warp-level mma.sync tiles (cp.async staging)     */
+#define KQ_PATH_DP4A 3    /* CUDA-core integer dot products, m <= 4 only;    */
+                          /* larger m falls back to the AUTO choice          */
 
 typedef struct kq_ctx kq_ctx;
 typedef struct kq_weight kq_weight;
@@ -88,6 +90,9 @@ int64_t kq_ctx_launch_count(const kq_ctx *ctx);
  * pesti-runner/examples/quant_bench.rs:89-101). */
 int kq_ctx_profile_begin(kq_ctx *ctx, int max_calls);
 int kq_ctx_profile_end(kq_ctx *ctx, double *total_ms, int64_t *count);
+/* Same sums without ending the session: after each replay of a graph that
+ * holds the brackets, this reads that replay's kernel times. */
+int kq_ctx_profile_read(kq_ctx *ctx, double *total_ms, int64_t *count);
 const char *kq_last_error(const kq_ctx *ctx);
 const char *kq_status_string(int status);
 int kq_abi_version(void);

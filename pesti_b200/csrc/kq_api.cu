@@ -160,21 +160,34 @@ int finish_sync(kq_ctx* ctx, const char* what) {
   return check_device_error(ctx);
 }
 
-bool use_tc(const kq_ctx* ctx, int type) {
-  return is_gguf(type) && ctx->path != KQ_PATH_MMA;
+// Kernel family for a GGUF f32 call of m tokens.
+int f32_family(const kq_ctx* ctx, int64_t m) {
+  if (ctx->path == KQ_PATH_MMA || ctx->path == KQ_PATH_TCGEN05) return ctx->path;
+  return m <= kq::DP4A_MAX_M ? KQ_PATH_DP4A : KQ_PATH_TCGEN05;
 }
 
-// Scratch and counters for a GGUF f32 call of m tokens on weight w.
-int prepare_f32(kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
-  if (use_tc(ctx, w.type)) {
-    int rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes(m, w.n, w.k, ctx->num_sms),
-                    "workspace");
-    if (rc) return rc;
-    size_t off = 0, cnt = 0;
-    kq::tc_counter_span(m, w.n, w.k, ctx->num_sms, &off, &cnt);
-    return ensure(ctx, &ctx->ctr, &ctx->ctr_bytes, cnt, "counters", true);
+// Scratch bytes and zeroed counter bytes a GGUF f32 call of m tokens needs.
+void f32_needs(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m, size_t* ws, size_t* ctr) {
+  *ws = 0;
+  *ctr = 0;
+  const int fam = f32_family(ctx, m);
+  if (fam == KQ_PATH_DP4A) {
+    *ws = kq::dp4a_workspace_bytes(w.type, m, w.sb);
+  } else if (fam == KQ_PATH_TCGEN05) {
+    *ws = kq::tc_workspace_bytes(m, w.n, w.k, ctx->num_sms);
+    size_t off = 0;
+    kq::tc_counter_span(m, w.n, w.k, ctx->num_sms, &off, ctr);
+  } else {
+    *ws = kq::gemv_gguf_workspace_bytes(m, w.k);
   }
-  return ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::gemv_gguf_workspace_bytes(m, w.k), "workspace");
+}
+
+int prepare_f32(kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
+  size_t ws = 0, ctr = 0;
+  f32_needs(ctx, w, m, &ws, &ctr);
+  int rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, ws, "workspace");
+  if (rc == KQ_OK && ctr) rc = ensure(ctx, &ctx->ctr, &ctx->ctr_bytes, ctr, "counters", true);
+  return rc;
 }
 
 }  // namespace
@@ -213,6 +226,7 @@ int kq_ctx_create(int device, kq_ctx** out) {
   if (g.status != cudaSuccess) return KQ_ERR_CUDA;
   e = kq::gemv_init_device();
   if (e == cudaSuccess) e = kq::tc_init_device();
+  if (e == cudaSuccess) e = kq::dp4a_init_device();
   if (e != cudaSuccess) {
     cudaGetLastError();
     return KQ_ERR_CUDA;
@@ -265,7 +279,7 @@ int kq_ctx_set_stream(kq_ctx* ctx, void* stream) {
 
 int kq_ctx_set_path(kq_ctx* ctx, int path) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
-  if (path != KQ_PATH_AUTO && path != KQ_PATH_TCGEN05 && path != KQ_PATH_MMA)
+  if (path != KQ_PATH_AUTO && path != KQ_PATH_TCGEN05 && path != KQ_PATH_MMA && path != KQ_PATH_DP4A)
     return fail(ctx, KQ_ERR_INVALID_ARG, "unknown path %d", path);
   ctx->path = path;
   return KQ_OK;
@@ -282,9 +296,17 @@ int kq_ctx_reserve(kq_ctx* ctx, const kq_weight* w, int64_t m) {
   if (!w || m < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "bad reserve arguments");
   if (!is_gguf(w->dw.type) || m == 0 || w->dw.k == 0) return KQ_OK;
   DeviceGuard g(ctx->device);
-  int rc = prepare_f32(ctx, w->dw, m);
-  if (rc) return rc;
-  return ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes_bf16(m, w->dw.k), "workspace");
+  // every call with 1..m rows may pick a different kernel family: cover them all
+  size_t ws = kq::tc_workspace_bytes_bf16(m, w->dw.k), ctr = 0;
+  for (int64_t i = 1; i <= m; ++i) {
+    size_t a = 0, b = 0;
+    f32_needs(ctx, w->dw, i, &a, &b);
+    ws = a > ws ? a : ws;
+    ctr = b > ctr ? b : ctr;
+  }
+  int rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, ws, "workspace");
+  if (rc == KQ_OK && ctr) rc = ensure(ctx, &ctx->ctr, &ctx->ctr_bytes, ctr, "counters", true);
+  return rc;
 }
 
 int64_t kq_ctx_launch_count(const kq_ctx* ctx) { return ctx ? ctx->launches : -1; }
@@ -305,11 +327,23 @@ int kq_ctx_profile_begin(kq_ctx* ctx, int max_calls) {
   return KQ_OK;
 }
 
+static int profile_sums(kq_ctx* ctx, double* total_ms, int64_t* count);
+
 int kq_ctx_profile_end(kq_ctx* ctx, double* total_ms, int64_t* count) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!ctx->prof_on) return fail(ctx, KQ_ERR_STATE, "profiling was not started");
-  DeviceGuard g(ctx->device);
   ctx->prof_on = false;
+  return profile_sums(ctx, total_ms, count);
+}
+
+int kq_ctx_profile_read(kq_ctx* ctx, double* total_ms, int64_t* count) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!ctx->prof_on) return fail(ctx, KQ_ERR_STATE, "profiling was not started");
+  return profile_sums(ctx, total_ms, count);
+}
+
+static int profile_sums(kq_ctx* ctx, double* total_ms, int64_t* count) {
+  DeviceGuard g(ctx->device);
   int rc = finish_sync(ctx, "cudaStreamSynchronize");
   if (rc) return rc;
   double sum = 0.0;
@@ -374,13 +408,13 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
   const size_t pad = 64;  // vector loads never read past the allocation
   if (type == kq::GGUF_Q6_K) {
     const int64_t nsb = n * w->dw.sb;
-    const int64_t dld = kq::q6k_d_ld(n);
+    const int64_t dld = kq::q6k_d_ld(w->dw.sb);
     w->dw.d_ld = dld;
     void* raw = nullptr;
     e = cudaMalloc(&raw, (size_t)nsb * kq::Q6K_BYTES + pad);
     if (e == cudaSuccess) e = cudaMalloc(&w->q_alloc, (size_t)nsb * kq::Q6K_BODY + pad);
-    if (e == cudaSuccess) e = cudaMalloc(&w->d_alloc, (size_t)w->dw.sb * dld * 2 + pad);
-    if (e == cudaSuccess) e = cudaMemsetAsync(w->d_alloc, 0, (size_t)w->dw.sb * dld * 2 + pad, ctx->stream);
+    if (e == cudaSuccess) e = cudaMalloc(&w->d_alloc, (size_t)n * dld * 2 + pad);
+    if (e == cudaSuccess) e = cudaMemsetAsync(w->d_alloc, 0, (size_t)n * dld * 2 + pad, ctx->stream);
     if (e == cudaSuccess && nsb)
       e = cudaMemcpyAsync(raw, bytes, (size_t)nsb * kq::Q6K_BYTES, cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess)
@@ -456,6 +490,11 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
   if (m == 0 || n == 0) return KQ_OK;
   if (!y || (k > 0 && !x)) return fail(ctx, KQ_ERR_INVALID_ARG, "x or y is null");
   const bool dev = flags & KQ_DEVICE_PTRS;
+  // the kernels read activations in 16-byte vectors and write y in 4-byte words
+  if (dev && k > 0 && (reinterpret_cast<uintptr_t>(x) & 15))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "device x must be 16-byte aligned");
+  if (dev && ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(bias)) & 3))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "device y and bias must be 4-byte aligned");
   DeviceGuard g(ctx->device);
   if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
   cudaStream_t s = ctx->stream;
@@ -496,7 +535,11 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
     e = kq::launch_tc_bf16(w->dw, xd, m, bd, yd, ctx->ws, ctx->dev_err, s, &launches, ctx->next_bracket());
   } else if (is_gguf(w->dw.type)) {
     if ((rc = prepare_f32(ctx, w->dw, m))) return rc;
-    if (use_tc(ctx, w->dw.type)) {
+    const int fam = f32_family(ctx, m);
+    if (fam == KQ_PATH_DP4A) {
+      e = kq::launch_gemv_dp4a(w->dw, static_cast<const float*>(xd), m, bd, yd, ctx->ws, ctx->num_sms,
+                               ctx->dev_err, s, &launches, ctx->next_bracket());
+    } else if (fam == KQ_PATH_TCGEN05) {
       // counters live in their own zeroed buffer; the scratch layout's counter span is unused
       e = kq::launch_tc_f32(w->dw, static_cast<const float*>(xd), m, bd, yd, ctx->ws, ctx->num_sms, ctx->dev_err,
                             s, &launches, ctx->next_bracket(), static_cast<unsigned*>(ctx->ctr));

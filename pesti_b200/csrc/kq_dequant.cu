@@ -91,7 +91,7 @@ __global__ void dequant_kernel(DevWeight w, int64_t row0, int64_t nrows, float* 
       case GGUF_Q6_K: {
         const int64_t kb = i / QK;
         const size_t g = (size_t)r * w.sb + kb;
-        v = gguf_q6k_value(w.q + g * Q6K_BODY, w.d[kb * w.d_ld + r], (int)(i % QK));
+        v = gguf_q6k_value(w.q + g * Q6K_BODY, w.d[r * w.d_ld + kb], (int)(i % QK));
         break;
       }
       case LEGACY_Q4_K:
@@ -108,7 +108,7 @@ __global__ void dequant_kernel(DevWeight w, int64_t row0, int64_t nrows, float* 
 __global__ void q6k_relayout_kernel(const uint8_t* __restrict__ raw, int64_t n, int64_t sb,
                                     uint8_t* __restrict__ body, uint16_t* __restrict__ d) {
   const int64_t total = n * sb * Q6K_BYTES;
-  const int64_t ld = q6k_d_ld(n);
+  const int64_t ld = q6k_d_ld(sb);
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t g = idx / Q6K_BYTES;  // row * sb + kb
@@ -117,7 +117,7 @@ __global__ void q6k_relayout_kernel(const uint8_t* __restrict__ raw, int64_t n, 
       body[g * Q6K_BODY + q6k_body_offset(b)] = raw[idx];
     } else if (b == Q6K_BODY) {
       const int64_t row = g / sb, kb = g - row * sb;
-      d[kb * ld + row] = (uint16_t)(raw[idx] | (raw[idx + 1] << 8));
+      d[row * ld + kb] = (uint16_t)(raw[idx] | (raw[idx + 1] << 8));
     }
   }
 }

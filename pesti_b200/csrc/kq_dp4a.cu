@@ -1,0 +1,1029 @@
+// kq_dp4a.cu -- decode dequant-GEMV for small batches (M <= 4 tokens) on the
+// CUDA cores, built to keep HBM busy.
+//
+// Work split: one warp streams one weight row at a time (rows are dealt out
+// grid-stride, so every SM gets the same number of rows within one), in
+// "iterations" of 32 lane units:
+//   GGUF Q4_K: 4 superblocks per iteration; lane i takes superblock 4it+i/8,
+//              16-byte quant chunk c = i%8 (32 weights: 16 of sub-block 2(c/2)
+//              in the low nibbles, 16 of sub-block 2(c/2)+1 in the high ones)
+//              plus the superblock's 16-byte header (d, dmin, 6-bit scales).
+//   GGUF Q6_K: 8 superblocks per iteration; lane i takes superblock 8it+i/4,
+//              slot c = i%4 of the device body (48 bytes = 64 weights, see
+//              q6k_body_offset), the 16 scale bytes and d.
+// Every lane keeps D iterations of raw weights in flight in registers
+// (coalesced 128-bit loads that bypass L1), so an SM has ~16-24 warps x D
+// iterations of loads outstanding -- the memory-level parallelism HBM needs.
+//
+// Products: the activations are prepared once per call (prep kernel) as
+// 16-bit integers x_int = rint(x * 2^-e), one power-of-two scale 2^e per
+// (token, superblock) chosen so that max|x| * 2^-e is in [2^14, 2^15), split
+// into a signed high byte and an unsigned low byte (x_int = 256 hi + lo).
+// The quants are non-negative bytes, so two dp4a per 4 weights give exact
+// integer partial sums; sub-block scales are applied in integer (Q4_K) or in
+// f32 per 8-weight group (Q6_K), the superblock factor d * 2^e in f32.  The
+// only approximation is the 16-bit activation rounding (relative 2^-15 of
+// each superblock's largest activation); the Q4_K min term uses exact f32
+// activation sums.  Partial sums are added with warp shuffles.
+//
+// The prepared activations are laid out in the order lanes read them
+// (x[token][iteration][j][lane] in 16-byte units), so each activation load of
+// a warp is one contiguous 512-byte run (L1-resident: every warp of an SM
+// reads the same activations).
+#include "kq_common.cuh"
+#include "kq_kernels.h"
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <utility>
+
+namespace kq {
+namespace {
+
+constexpr int WARPS = 8;  // per CTA
+
+template <int QT>
+struct Dp4aFmt;
+template <>
+struct Dp4aFmt<GGUF_Q4_K> {
+  static constexpr int SPI = 4;   // superblocks per iteration
+  static constexpr int XJ = 4;    // 16-byte activation units per lane per iteration
+  static constexpr int SUMJ = 1;  // 8-byte f32 sums (2 floats) per lane per iteration
+  static constexpr int D = 4;     // iterations in flight
+  static constexpr int CPS = 3;   // CTAs per SM
+};
+template <>
+struct Dp4aFmt<GGUF_Q6_K> {
+  static constexpr int SPI = 8;
+  static constexpr int XJ = 8;
+  static constexpr int SUMJ = 2;  // 16-byte int sums (4 ints) per lane per iteration
+  static constexpr int D = 3;
+  static constexpr int CPS = 2;
+};
+
+// Scratch layout for m tokens (offsets in bytes, each 256-aligned).
+struct Dp4aLayout {
+  int64_t iters;
+  size_t xq, sums, xs, end;
+};
+template <int QT>
+Dp4aLayout dp4a_layout(int64_t m, int64_t sb) {
+  using F = Dp4aFmt<QT>;
+  Dp4aLayout L;
+  L.iters = (sb + F::SPI - 1) / F::SPI;
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  const size_t per_it = 32 * 16;  // one 16-byte unit per lane
+  L.xq = 0;
+  L.sums = up(L.xq + (size_t)m * L.iters * F::XJ * per_it);
+  const size_t sum_bytes = QT == GGUF_Q4_K ? 8 : 16;
+  L.xs = up(L.sums + (size_t)m * L.iters * F::SUMJ * 32 * sum_bytes);
+  L.end = up(L.xs + (size_t)m * L.iters * F::SPI * sizeof(float));
+  return L;
+}
+
+struct Dp4aParams {
+  const uint8_t* q;
+  const uint16_t* d;
+  int64_t d_ld;
+  int n, sb, iters, m;
+  const uint4* xq;     // [m][iters][XJ][32] 16-byte units
+  const void* sums;    // Q4_K: float2 [m][iters][32]; Q6_K: int4 [m][iters][2][32]
+  const float* xs;     // [m][iters * SPI] superblock factors 2^e (NaN: non-finite block)
+  const float* bias;
+  float* y;
+};
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t ldg_nc_u16(const uint16_t* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+  return v;
+}
+
+// ---- activation prep ------------------------------------------------------------
+// Quantize one superblock's activations: the block maximum over the `group`
+// lanes that share superblock kb (consecutive lanes), then 2^-e scaling.
+struct BlockScale {
+  float inv;     // 2^-e
+  float factor;  // 2^e, or NaN when the block holds a non-finite value
+};
+__device__ __forceinline__ BlockScale block_scale(float amax_lane, int group) {
+  float amax = amax_lane;
+  for (int o = 1; o < group; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  BlockScale s;
+  if (!(amax <= 3.4e38f)) {  // inf or NaN somewhere in the block
+    s.inv = 0.f;
+    s.factor = __int_as_float(0x7fc00000);
+    return s;
+  }
+  int e = 0;
+  if (amax > 0.f) e = (int)((__float_as_uint(amax) >> 23) & 0xff) - 127 - 14;
+  e = max(-126, min(126, e));
+  s.inv = __uint_as_float((uint32_t)(127 - e) << 23);
+  s.factor = __uint_as_float((uint32_t)(127 + e) << 23);
+  return s;
+}
+__device__ __forceinline__ int quant16(float v, float inv) {
+  const float r = rintf(v * inv);
+  return (int)fminf(fmaxf(r, -32768.f), 32767.f);
+}
+// Four 16-bit activations -> (hi bytes, lo bytes) words, byte i = activation i.
+__device__ __forceinline__ void split4(const int (&v)[4], uint32_t& hi, uint32_t& lo) {
+  hi = 0;
+  lo = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    hi |= (uint32_t)((v[i] >> 8) & 0xff) << (8 * i);
+    lo |= (uint32_t)(v[i] & 0xff) << (8 * i);
+  }
+}
+
+// One thread per (token, iteration, lane unit); blockDim = 128 (4 iterations).
+template <int QT>
+__global__ void __launch_bounds__(128) dp4a_prep_kernel(const float* __restrict__ x, int m, int k, int sb,
+                                                        int iters, uint4* __restrict__ xq,
+                                                        void* __restrict__ sums, float* __restrict__ xs) {
+  using F = Dp4aFmt<QT>;
+  pdl_trigger();  // let the GEMV kernel start streaming weights now
+  const int lane = threadIdx.x & 31;
+  const int it = blockIdx.x * 4 + (threadIdx.x >> 5);
+  const int t = blockIdx.y;
+  if (it >= iters) return;  // whole warp
+  const float* xr = x + (int64_t)t * k;
+  uint4* xo = xq + ((int64_t)t * iters + it) * F::XJ * 32 + lane;
+  if constexpr (QT == GGUF_Q4_K) {
+    const int kb = 4 * it + (lane >> 3), c = lane & 7;
+    const bool live = kb < sb;
+    const int base = kb * 256 + 64 * (c >> 1) + 16 * (c & 1);  // sub-block A run; B run = base + 32
+    float a[16], b[16];
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      float4 va = make_float4(0.f, 0.f, 0.f, 0.f), vb = va;
+      if (live) {
+        va = ldg_f4(xr + base + i);
+        vb = ldg_f4(xr + base + 32 + i);
+      }
+      a[i] = va.x; a[i + 1] = va.y; a[i + 2] = va.z; a[i + 3] = va.w;
+      b[i] = vb.x; b[i + 1] = vb.y; b[i + 2] = vb.z; b[i + 3] = vb.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fmaxf(fabsf(a[i]), fabsf(b[i])));
+    const BlockScale s = block_scale(amax, 8);
+    float sa = 0.f, sbm = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      int qa[4], qb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        qa[i] = quant16(a[4 * w + i], s.inv);
+        qb[i] = quant16(b[4 * w + i], s.inv);
+        sa += a[4 * w + i];
+        sbm += b[4 * w + i];
+      }
+      uint4 u;
+      split4(qa, u.x, u.y);
+      split4(qb, u.z, u.w);
+      xo[w * 32] = u;
+    }
+    reinterpret_cast<float2*>(sums)[((int64_t)t * iters + it) * 32 + lane] = make_float2(sa, sbm);
+    if (c == 0) xs[(int64_t)t * iters * F::SPI + kb] = live ? s.factor : 0.f;
+  } else {
+    const int kb = 8 * it + (lane >> 2), c = lane & 3;
+    const bool live = kb < sb;
+    // group (h, g, w): weights 128h + 32g + 8c + 4w + [0, 4)
+    float v[2][4][2][4];
+    float amax = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (live) f = ldg_f4(xr + kb * 256 + 128 * h + 32 * g + 8 * c + 4 * w);
+          v[h][g][w][0] = f.x; v[h][g][w][1] = f.y; v[h][g][w][2] = f.z; v[h][g][w][3] = f.w;
+          amax = fmaxf(amax, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+        }
+    const BlockScale s = block_scale(amax, 4);
+    int4* so = reinterpret_cast<int4*>(sums) + ((int64_t)t * iters + it) * 2 * 32 + lane;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      int gs[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        gs[g] = 0;
+        uint32_t hw[2], lw[2];
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          int qv[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            qv[i] = quant16(v[h][g][w][i], s.inv);
+            gs[g] += qv[i];
+          }
+          split4(qv, hw[w], lw[w]);
+        }
+        // unit j = 4h + 2w + g/2 holds {hi, lo} of g even then g odd
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          uint32_t* u = reinterpret_cast<uint32_t*>(xo + (4 * h + 2 * w + (g >> 1)) * 32);
+          u[2 * (g & 1)] = hw[w];
+          u[2 * (g & 1) + 1] = lw[w];
+        }
+      }
+      so[h * 32] = make_int4(-32 * gs[0], -32 * gs[1], -32 * gs[2], -32 * gs[3]);
+    }
+    if (c == 0) xs[(int64_t)t * iters * F::SPI + kb] = live ? s.factor : 0.f;
+  }
+}
+
+// ---- GEMV -----------------------------------------------------------------------
+template <int QT>
+struct Raw;
+template <>
+struct Raw<GGUF_Q4_K> {
+  uint4 qs, hdr;
+};
+template <>
+struct Raw<GGUF_Q6_K> {
+  uint4 p0, p1, p2, sc;
+  uint32_t d;
+};
+
+template <int QT>
+__device__ __forceinline__ void load_raw(Raw<QT>& r, const Dp4aParams& P, int row, int it, int lane, bool valid) {
+  if constexpr (QT == GGUF_Q4_K) {
+    const int kb = 4 * it + (lane >> 3), c = lane & 7;
+    if (valid && kb < P.sb) {
+      const uint8_t* blk = P.q + ((int64_t)row * P.sb + kb) * Q4K_BYTES;
+      r.qs = ldg_nc_v4(blk + 16 + 16 * c);
+      r.hdr = ldg_nc_v4(blk);
+    } else {
+      r.qs = make_uint4(0, 0, 0, 0);
+      r.hdr = r.qs;
+    }
+  } else {
+    const int kb = 8 * it + (lane >> 2), c = lane & 3;
+    if (valid && kb < P.sb) {
+      const uint8_t* blk = P.q + ((int64_t)row * P.sb + kb) * Q6K_BODY;
+      r.p0 = ldg_nc_v4(blk + 48 * c);
+      r.p1 = ldg_nc_v4(blk + 48 * c + 16);
+      r.p2 = ldg_nc_v4(blk + 48 * c + 32);
+      r.sc = ldg_nc_v4(blk + 192);
+      r.d = ldg_nc_u16(P.d + (int64_t)row * P.d_ld + kb);
+    } else {
+      r.p0 = make_uint4(0, 0, 0, 0);
+      r.p1 = r.p0;
+      r.p2 = r.p0;
+      r.sc = r.p0;
+      r.d = 0;
+    }
+  }
+}
+
+__device__ __forceinline__ int dp4a_s(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+__device__ __forceinline__ int dp4a_u(uint32_t a, uint32_t b, int c) {
+  return (int)__dp4a(a, b, (unsigned)c);
+}
+
+// acc[t] += this lane's share of row . x_t for iteration `it`.
+template <int MT>
+__device__ __forceinline__ void compute_q4(const Raw<GGUF_Q4_K>& r, const Dp4aParams& P, int it, int lane,
+                                           float (&acc)[MT]) {
+  const int c = lane & 7, j2 = 2 * (c >> 1);
+  const float d = f16_bits_to_f32((uint16_t)(r.hdr.x & 0xffff));
+  const float dmin = f16_bits_to_f32((uint16_t)(r.hdr.x >> 16));
+  int sca, ma, scb, mb;
+  q4k_scale_min_w(r.hdr.y, r.hdr.z, r.hdr.w, j2, sca, ma);
+  q4k_scale_min_w(r.hdr.y, r.hdr.z, r.hdr.w, j2 + 1, scb, mb);
+  uint32_t qa[4], qb[4];
+  const uint32_t W[4] = {r.qs.x, r.qs.y, r.qs.z, r.qs.w};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    qa[w] = W[w] & 0x0F0F0F0Fu;
+    qb[w] = (W[w] >> 4) & 0x0F0F0F0Fu;
+  }
+  const int kb = 4 * it + (lane >> 3);
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    const int64_t ti = (int64_t)t * P.iters + it;
+    const uint4* xv = P.xq + ti * 4 * 32 + lane;
+    int ahi = 0, alo = 0, bhi = 0, blo = 0;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint4 u = __ldg(xv + w * 32);
+      ahi = dp4a_s(qa[w], u.x, ahi);
+      alo = dp4a_u(qa[w], u.y, alo);
+      bhi = dp4a_s(qb[w], u.z, bhi);
+      blo = dp4a_u(qb[w], u.w, blo);
+    }
+    const float2 s = __ldg(reinterpret_cast<const float2*>(P.sums) + ti * 32 + lane);
+    const float f = __ldg(P.xs + (int64_t)t * P.iters * 4 + kb);
+    const int da = ahi * 256 + alo, db = bhi * 256 + blo;
+    const int iv = sca * da + scb * db;  // |iv| < 2^30
+    acc[t] = fmaf(d * f, (float)iv, acc[t]);
+    acc[t] = fmaf(-dmin, fmaf((float)ma, s.x, (float)mb * s.y), acc[t]);
+  }
+}
+
+__device__ __forceinline__ float sbyte(uint32_t w, int b) { return (float)(int)(int8_t)((w >> (8 * b)) & 0xff); }
+
+template <int MT>
+__device__ __forceinline__ void compute_q6(const Raw<GGUF_Q6_K>& r, const Dp4aParams& P, int it, int lane,
+                                           float (&acc)[MT]) {
+  const int c = lane & 3;
+  const int kb = 8 * it + (lane >> 2);
+  // q[h][g][w]: the 4 six-bit quants of group (h, g, w) as bytes
+  uint32_t q[2][4][2];
+  const uint32_t ql[2][2][2] = {{{r.p0.x, r.p0.y}, {r.p0.z, r.p0.w}}, {{r.p1.x, r.p1.y}, {r.p1.z, r.p1.w}}};
+  const uint32_t qh[2][2] = {{r.p2.x, r.p2.y}, {r.p2.z, r.p2.w}};
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      const uint32_t H = qh[h][w];
+      q[h][0][w] = (ql[h][0][w] & 0x0F0F0F0Fu) | ((H << 4) & 0x30303030u);
+      q[h][1][w] = (ql[h][1][w] & 0x0F0F0F0Fu) | ((H << 2) & 0x30303030u);
+      q[h][2][w] = ((ql[h][0][w] >> 4) & 0x0F0F0F0Fu) | (H & 0x30303030u);
+      q[h][3][w] = ((ql[h][1][w] >> 4) & 0x0F0F0F0Fu) | ((H >> 2) & 0x30303030u);
+    }
+  // scale of group (h, g): byte 8h + 2g + c/2 of the 16 scale bytes
+  float scf[2][4];
+  const uint32_t S[4] = {r.sc.x, r.sc.y, r.sc.z, r.sc.w};
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int si = 8 * h + 2 * g;  // + c/2
+      const uint32_t word = S[si >> 2];
+      scf[h][g] = sbyte(word, (si & 3) + (c >> 1));
+    }
+  const float d = f16_bits_to_f32((uint16_t)r.d);
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    const int64_t ti = (int64_t)t * P.iters + it;
+    const uint4* xv = P.xq + ti * 8 * 32 + lane;
+    const int4* sv = reinterpret_cast<const int4*>(P.sums) + ti * 2 * 32 + lane;
+    float part = 0.f;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int4 sg = __ldg(sv + h * 32);
+      const int sgv[4] = {sg.x, sg.y, sg.z, sg.w};
+      uint4 u[2][2];
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int gp = 0; gp < 2; ++gp) u[w][gp] = __ldg(xv + (4 * h + 2 * w + gp) * 32);
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        const int gp = g >> 1, od = g & 1;
+        int hi = 0, lo = 0;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          const uint32_t xh = od ? u[w][gp].z : u[w][gp].x;
+          const uint32_t xl = od ? u[w][gp].w : u[w][gp].y;
+          hi = dp4a_s(q[h][g][w], xh, hi);
+          lo = dp4a_u(q[h][g][w], xl, lo);
+        }
+        const int v = hi * 256 + lo + sgv[g];  // sum of (q - 32) * x_int, |v| < 2^24
+        part = fmaf((float)v, scf[h][g], part);
+      }
+    }
+    const float f = __ldg(P.xs + (int64_t)t * P.iters * 8 + kb);
+    acc[t] = fmaf(part, d * f, acc[t]);
+  }
+}
+
+template <int QT, int MT>
+__global__ void __launch_bounds__(32 * WARPS, Dp4aFmt<QT>::CPS) dp4a_gemv_kernel(const Dp4aParams P) {
+  using F = Dp4aFmt<QT>;
+  constexpr int D = F::D;
+  const int lane = threadIdx.x & 31;
+  const int slot = (threadIdx.x >> 5) * gridDim.x + blockIdx.x;  // warp slot: rows slot, slot + stride, ...
+  const int stride = WARPS * gridDim.x;
+  if (slot >= P.n) {
+    pdl_wait();
+    return;
+  }
+  // load cursor (row, iteration) runs D iterations ahead of the compute cursor
+  int lrow = slot, lit = 0;
+  Raw<QT> buf[D];
+#pragma unroll
+  for (int j = 0; j < D; ++j) {
+    load_raw<QT>(buf[j], P, lrow, lit, lane, lrow < P.n);
+    if (++lit == P.iters) { lit = 0; lrow += stride; }
+  }
+  pdl_wait();  // activations are ready from here on
+  int crow = slot, cit = 0;
+  float acc[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) acc[t] = 0.f;
+  bool more = true;
+  while (more) {
+#pragma unroll
+    for (int j = 0; j < D; ++j) {
+      if (more) {
+        if constexpr (QT == GGUF_Q4_K) compute_q4<MT>(buf[j], P, cit, lane, acc);
+        else compute_q6<MT>(buf[j], P, cit, lane, acc);
+        load_raw<QT>(buf[j], P, lrow, lit, lane, lrow < P.n);
+        if (++lit == P.iters) { lit = 0; lrow += stride; }
+        if (++cit == P.iters) {
+#pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            float v = acc[t];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && t < P.m) P.y[(int64_t)t * P.n + crow] = v + (P.bias ? P.bias[crow] : 0.f);
+            acc[t] = 0.f;
+          }
+          cit = 0;
+          crow += stride;
+          more = crow < P.n;
+        }
+      }
+    }
+  }
+}
+
+template <int QT, int MT>
+cudaError_t launch_main(const Dp4aParams& P, int num_sms, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(num_sms * Dp4aFmt<QT>::CPS));
+  cfg.blockDim = dim3(32 * WARPS);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, dp4a_gemv_kernel<QT, MT>, P);
+}
+
+template <int QT>
+cudaError_t launch_typed(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y, void* ws,
+                         int num_sms, cudaStream_t s, int* launches, Bracket br) {
+  using F = Dp4aFmt<QT>;
+  const Dp4aLayout L = dp4a_layout<QT>(m, w.sb);
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  Dp4aParams P;
+  P.q = w.q;
+  P.d = w.d;
+  P.d_ld = w.d_ld;
+  P.n = (int)w.n;
+  P.sb = (int)w.sb;
+  P.iters = (int)L.iters;
+  P.m = (int)m;
+  P.xq = reinterpret_cast<const uint4*>(base + L.xq);
+  P.sums = base + L.sums;
+  P.xs = reinterpret_cast<const float*>(base + L.xs);
+  P.bias = bias;
+  P.y = y;
+  dim3 pg((unsigned)((L.iters + 3) / 4), (unsigned)m);
+  dp4a_prep_kernel<QT><<<pg, 128, 0, s>>>(x, (int)m, (int)w.k, (int)w.sb, (int)L.iters,
+                                         reinterpret_cast<uint4*>(base + L.xq), base + L.sums,
+                                         reinterpret_cast<float*>(base + L.xs));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  if (launches) ++*launches;
+  bracket_record(br.start, s);
+  switch (m) {
+    case 1: e = launch_main<QT, 1>(P, num_sms, s); break;
+    case 2: e = launch_main<QT, 2>(P, num_sms, s); break;
+    case 3: e = launch_main<QT, 3>(P, num_sms, s); break;
+    case 4: e = launch_main<QT, 4>(P, num_sms, s); break;
+    default: return cudaErrorInvalidValue;
+  }
+  if (e != cudaSuccess) return e;
+  if (launches) ++*launches;
+  bracket_record(br.stop, s);
+  (void)F::SPI;
+  return cudaSuccess;
+}
+
+// ---- one token: TMA-streamed rows, activation-stationary warps -------------------
+// For a single token the activations of an 8-superblock K-slice fit in a
+// warp's registers (64 weights per lane -> 32 registers of hi/lo bytes), so
+// each compute warp owns one K-slice and applies it to every row of its CTA.
+// The weights reach shared memory by bulk TMA copies (cp.async.bulk) issued
+// by one producer warp: each CTA owns a contiguous block of rows and streams
+// it through a ring of S stages of G rows each (rows are contiguous in
+// memory, Q6_K d rows too), so up to ~100 KB per CTA are in flight without
+// tying up registers or L1 miss slots.  Compute warps: nk K-slices x G row
+// groups; warp (s, g) takes row g of every stage and reduces its partial with
+// shuffles into shared memory; the CTA adds the nk partials in slice order at
+// the end (deterministic).
+//
+// One CTA per SM (up to 15 compute warps + the producer).  The ring holds
+// about XS_INFLIGHT bytes: streaming-read measurements on B200 peak near
+// 64-128 KB in flight per SM with 16-32 KB bulk copies; much deeper rings
+// lose bandwidth.  The kernel triggers its dependents at once, so the next
+// GEMV's CTAs can start streaming on an SM as soon as ours retires there.
+//
+// Lane i of slice s works on superblock kb = 8s + i/4, unit u = i%4:
+//   Q4_K: qs bytes 32u .. 32u+31 (sub-blocks 2u and 2u+1 complete) + header
+//   Q6_K: body slot u (48 bytes, 64 weights) + the scale bytes + d
+// Each lane quantizes its own 64 activations once (per superblock 2^e with
+// max|x| * 2^-e in [2^13, 2^14), rounding by the 1.5 * 2^23 float addition,
+// so the low 16 bits of the float are the two's-complement integer).
+// Q6_K sub-block scales are applied in exact int32: the hi- and lo-limb
+// products are accumulated separately (each sum of 8 (q-32) x products is
+// < 2^17 in size), the -32 x corrections are the accumulators' start values.
+// Every mbarrier wait is bounded: a stalled pipeline ends the kernel with an
+// error code in *err instead of hanging, and the producer always waits for
+// its issued copies to land before the CTA may exit.
+constexpr int XS_SPW = 8;          // superblocks per warp slice
+constexpr int XS_MAX_COMPUTE = 15;  // compute warps (+ 1 producer = 512 threads)
+constexpr int XS_MAX_SMEM = 227 * 1024;
+constexpr int64_t XS_INFLIGHT = 96 * 1024;  // ring bytes in flight per CTA
+
+enum : int { XS_ERR_FULL = 21, XS_ERR_EMPTY = 22, XS_ERR_DRAIN = 23 };
+
+struct XsParams {
+  const uint8_t* q;     // [n][row_bytes]
+  const uint16_t* d;    // Q6_K: [n][d_row_bytes / 2]
+  int64_t row_bytes;    // weight bytes per row
+  int d_row_bytes;      // Q6_K: d bytes per row (a multiple of 16); Q4_K: 0
+  int n, sb, nk, G, S;  // rows, superblocks per row, K-slices, rows per stage, ring stages
+  int rows_max;         // most rows any CTA owns (shared-memory sizing)
+  int64_t stage_bytes;  // G * (row_bytes + d_row_bytes)
+  const float* x;
+  const float* bias;
+  float* y;
+  int* err;
+};
+
+// Dynamic shared memory: ring | staged x: words uint4 [sb8 * 4 units][8]
+// (swizzled), sums (Q4_K float2 / Q6_K int4[4] per unit), 2^e per superblock
+// | row partials [rows_max][nk] | full[S], empty[S].
+struct XsSmem {
+  size_t ring, xw, sums, xsf, part, bar, end;
+  __host__ __device__ XsSmem(int qt, int nk, int64_t stage_bytes, int S, int rows_max) {
+    const size_t units = (size_t)XS_SPW * nk * 4;
+    ring = 0;
+    xw = ring + (size_t)S * (size_t)stage_bytes;
+    sums = xw + units * 128;
+    xsf = sums + units * (qt == GGUF_Q4_K ? 8 : 64);
+    part = xsf + units;  // one float per superblock = units / 4 floats
+    bar = (part + (size_t)rows_max * nk * 4 + 7) & ~size_t(7);
+    end = bar + (size_t)2 * S * 8;
+  }
+};
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void xs_bar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void xs_bar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(b)) : "memory");
+}
+__device__ __forceinline__ void xs_bar_expect(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(b)), "r"(bytes) : "memory");
+}
+// Bounded wait for the phase of parity `par`; on giving up sets *err (first
+// code wins) and returns false.
+__device__ __forceinline__ bool xs_bar_wait(uint64_t* b, uint32_t par, int* err, int code) {
+  const uint32_t a = smem_addr(b);
+  for (uint32_t i = 0; i < (1u << 22); ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a), "r"(par)
+        : "memory");
+    if (done) return true;
+    if ((i & 1023u) == 1023u && *(volatile int*)err) return false;
+  }
+  atomicCAS(err, 0, code);
+  return false;
+}
+// Global -> shared bulk copy completing on mbarrier b (no multicast).
+__device__ __forceinline__ void xs_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(b))
+               : "memory");
+}
+__device__ __forceinline__ void xs_named_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// Per-superblock activation scale shared by the 8 lanes staging a
+// superblock: max|x| * inv in [2^13, 2^14) so that rint(x * inv) fits 15 bits.
+struct XScale {
+  float inv, factor;  // 2^-e, 2^e (NaN: the block holds a non-finite value)
+};
+__device__ __forceinline__ XScale xs_scale(float amax) {
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+  XScale s;
+  if (!(amax <= 3.4e38f)) {
+    s.inv = 0.f;
+    s.factor = __int_as_float(0x7fc00000);
+    return s;
+  }
+  int e = 0;
+  if (amax > 0.f) e = (int)((__float_as_uint(amax) >> 23) & 0xff) - 127 - 13;
+  e = max(-126, min(126, e));
+  s.inv = __uint_as_float((uint32_t)(127 - e) << 23);
+  s.factor = __uint_as_float((uint32_t)(127 + e) << 23);
+  return s;
+}
+// Four activations -> {hi bytes, lo bytes} of rint(v * inv) (|.| <= 2^14).
+__device__ __forceinline__ void xs_pack4(float v0, float v1, float v2, float v3, float inv, uint32_t& hi,
+                                         uint32_t& lo) {
+  constexpr float M = 12582912.0f;  // 1.5 * 2^23: the sum's low 16 bits are rint(v * inv)
+  const uint32_t f0 = __float_as_uint(fmaf(v0, inv, M)), f1 = __float_as_uint(fmaf(v1, inv, M));
+  const uint32_t f2 = __float_as_uint(fmaf(v2, inv, M)), f3 = __float_as_uint(fmaf(v3, inv, M));
+  const uint32_t p01 = prmt(f0, f1, 0x5140u), p23 = prmt(f2, f3, 0x5140u);  // {lo0, lo1, hi0, hi1}
+  lo = prmt(p01, p23, 0x5410u);
+  hi = prmt(p01, p23, 0x7632u);
+}
+
+__device__ __forceinline__ int xs_swz(int kb, int u) { return (u + 4 * (kb & 1)) & 7; }
+
+// Quantize x into shared memory: half-unit hu = 8 kb + 2 u + hf (32 weights)
+// per thread of the `nthreads` compute threads, the 8 half-units of a
+// superblock on consecutive lanes, written in the order lanes read them.
+template <int QT>
+__device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, uint8_t* smem, int nthreads) {
+  uint4* xw = reinterpret_cast<uint4*>(smem + L.xw);
+  float* xsf = reinterpret_cast<float*>(smem + L.xsf);
+  const int lane = threadIdx.x & 31;
+  const int total = XS_SPW * P.nk * 8;  // multiple of 64
+  for (int base = (threadIdx.x & ~31); base < total; base += nthreads) {
+    const int hu = base + lane;
+    const int kb = hu >> 3, u = (hu >> 1) & 3, hf = hu & 1;
+    const bool live = kb < P.sb;
+    const float* xr = P.x + (int64_t)kb * 256;
+    float v[32];  // Q4: [0,16) sub-block 2u run, [16,32) sub-block 2u+1 run; Q6: group (g, w) at 8g + 4w
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      int off;
+      if constexpr (QT == GGUF_Q4_K) off = 64 * u + 16 * hf + (i < 4 ? 4 * i : 32 + 4 * (i - 4));
+      else off = 128 * hf + 32 * (i >> 1) + 8 * u + 4 * (i & 1);
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (live) f = ldg_f4(xr + off);
+      v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const XScale sc = xs_scale(amax);
+    uint4* unit = xw + (size_t)(kb * 4 + u) * 8;
+    const int sw = xs_swz(kb, u);
+    if constexpr (QT == GGUF_Q4_K) {
+      // word 4 hf + j: {hi, lo} of A elements 4j.., then of B elements 4j..
+      float sa = 0.f, sbb = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        sa += v[i];
+        sbb += v[16 + i];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 o;
+        xs_pack4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3], sc.inv, o.x, o.y);
+        xs_pack4(v[16 + 4 * j], v[17 + 4 * j], v[18 + 4 * j], v[19 + 4 * j], sc.inv, o.z, o.w);
+        unit[(4 * hf + j) ^ sw] = o;
+      }
+      sa += __shfl_xor_sync(0xffffffffu, sa, 1);  // the unit's other half
+      sbb += __shfl_xor_sync(0xffffffffu, sbb, 1);
+      if (hf == 0) reinterpret_cast<float2*>(smem + L.sums)[kb * 4 + u] = make_float2(sa, sbb);
+    } else {
+      // h = hf; word 4h + 2w + gp holds {hi, lo} of group (h, 2gp, w), then of (h, 2gp + 1, w)
+      int shs[4], sls[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        shs[g] = 0;
+        sls[g] = 0;
+      }
+#pragma unroll
+      for (int w = 0; w < 2; ++w)
+#pragma unroll
+        for (int gp = 0; gp < 2; ++gp) {
+          uint4 o;
+          const int g0 = 2 * gp, g1 = 2 * gp + 1;
+          xs_pack4(v[8 * g0 + 4 * w], v[8 * g0 + 4 * w + 1], v[8 * g0 + 4 * w + 2], v[8 * g0 + 4 * w + 3], sc.inv,
+                   o.x, o.y);
+          xs_pack4(v[8 * g1 + 4 * w], v[8 * g1 + 4 * w + 1], v[8 * g1 + 4 * w + 2], v[8 * g1 + 4 * w + 3], sc.inv,
+                   o.z, o.w);
+          shs[g0] = __dp4a((int)o.x, 0x01010101, shs[g0]);
+          sls[g0] = (int)__dp4a(o.y, 0x01010101u, (unsigned)sls[g0]);
+          shs[g1] = __dp4a((int)o.z, 0x01010101, shs[g1]);
+          sls[g1] = (int)__dp4a(o.w, 0x01010101u, (unsigned)sls[g1]);
+          unit[(4 * hf + 2 * w + gp) ^ sw] = o;
+        }
+      int4* so = reinterpret_cast<int4*>(smem + L.sums) + (size_t)(kb * 4 + u) * 4 + 2 * hf;
+      so[0] = make_int4(-32 * shs[0], -32 * shs[1], -32 * shs[2], -32 * shs[3]);
+      so[1] = make_int4(-32 * sls[0], -32 * sls[1], -32 * sls[2], -32 * sls[3]);
+    }
+    if ((hu & 7) == 0) xsf[kb] = live ? sc.factor : 0.f;
+  }
+}
+
+template <int QT>
+__global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(const XsParams P) {
+  extern __shared__ __align__(128) uint8_t xs_smem[];
+  pdl_trigger();  // the next kernel may move in beside us and start streaming
+  const int C = gridDim.x, b = blockIdx.x;
+  const int64_t r0 = (int64_t)P.n * b / C, r1 = (int64_t)P.n * (b + 1) / C;
+  const int rows = (int)(r1 - r0);  // this CTA's rows r0 .. r1-1
+  const int T = (rows + P.G - 1) / P.G;
+  const int NC = P.nk * P.G;
+  const XsSmem L(QT, P.nk, P.stage_bytes, P.S, P.rows_max);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xs_smem + L.bar);
+  uint64_t* empty = full + P.S;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < P.S; ++i) {
+      xs_bar_init(&full[i], 1);
+      xs_bar_init(&empty[i], NC);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == NC) {
+    // ---------------- producer: the weights do not depend on the previous kernel ----------------
+    if (lane == 0) {
+      int t = 0;
+      for (; t < T; ++t) {
+        const int st = t % P.S;
+        if (t >= P.S && !xs_bar_wait(&empty[st], ((t / P.S) - 1) & 1, P.err, XS_ERR_EMPTY)) break;
+        const int nr = min(P.G, rows - t * P.G);
+        const int64_t row = r0 + (int64_t)t * P.G;
+        uint8_t* dst = xs_smem + L.ring + (size_t)st * (size_t)P.stage_bytes;
+        const uint32_t wb = (uint32_t)(nr * P.row_bytes), db = (uint32_t)(nr * P.d_row_bytes);
+        xs_bar_expect(&full[st], wb + db);
+        xs_bulk_g2s(dst, P.q + row * P.row_bytes, wb, &full[st]);
+        if constexpr (QT == GGUF_Q6_K)
+          xs_bulk_g2s(dst + (size_t)P.G * P.row_bytes, reinterpret_cast<const uint8_t*>(P.d) + row * P.d_row_bytes,
+                      db, &full[st]);
+      }
+      // the CTA must not retire while a copy into its shared memory is in flight
+      for (int v = max(0, t - P.S); v < t; ++v) xs_bar_wait(&full[v % P.S], (v / P.S) & 1, P.err, XS_ERR_DRAIN);
+    }
+    return;
+  }
+
+  // ---------------- compute warps ----------------
+  const int s = warp % P.nk, g = warp / P.nk;
+  const int kb = XS_SPW * s + (lane >> 2), u = lane & 3;
+  const bool live = kb < P.sb;
+  pdl_wait();  // x may be the previous kernel's output
+
+  xs_stage_x<QT>(P, L, xs_smem, NC * 32);
+  xs_named_sync(1, NC * 32);
+
+  // this lane's 64 activations, from the staged copy
+  uint4 X[8];
+  {
+    const uint4* unit = reinterpret_cast<const uint4*>(xs_smem + L.xw) + (size_t)(kb * 4 + u) * 8;
+    const int sw = xs_swz(kb, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) X[j] = unit[j ^ sw];
+  }
+  const float xf = reinterpret_cast<const float*>(xs_smem + L.xsf)[kb];
+  float sa = 0.f, sbb = 0.f;   // Q4_K: exact sums of the sub-block 2u / 2u+1 activations
+  int Sh[2][4], Sl[2][4];      // Q6_K: -32 * (sum of hi / lo bytes) of group (h, g)
+  uint32_t sel_lo = 0, sel_hi = 0;  // Q6_K: PRMT selectors of this lane's scale bytes
+  if constexpr (QT == GGUF_Q4_K) {
+    const float2 t = reinterpret_cast<const float2*>(xs_smem + L.sums)[kb * 4 + u];
+    sa = t.x;
+    sbb = t.y;
+  } else {
+    const int4* si = reinterpret_cast<const int4*>(xs_smem + L.sums) + (size_t)(kb * 4 + u) * 4;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int4 a = si[2 * h], c = si[2 * h + 1];
+      Sh[h][0] = a.x; Sh[h][1] = a.y; Sh[h][2] = a.z; Sh[h][3] = a.w;
+      Sl[h][0] = c.x; Sl[h][1] = c.y; Sl[h][2] = c.z; Sl[h][3] = c.w;
+    }
+    // scale byte of group (h, g) = byte 8h + 2g + u/2: byte (u/2) of word 2h + g/2 for even g,
+    // byte 2 + u/2 for odd g; sign-extended by PRMT (selector nibble | 8 replicates the sign)
+    const uint32_t b0 = (uint32_t)(u >> 1), b2 = b0 + 2;
+    sel_lo = b0 | ((b0 | 8) << 4) | ((b0 | 8) << 8) | ((b0 | 8) << 12);
+    sel_hi = b2 | ((b2 | 8) << 4) | ((b2 | 8) << 8) | ((b2 | 8) << 12);
+  }
+  float* part = reinterpret_cast<float*>(xs_smem + L.part);
+  const bool hi4 = u >= 2;  // Q4_K: sub-blocks 2u, 2u+1 take the packed high scale/min bits
+  const int sh = 16 * (u & 1);
+
+  for (int t = 0; t < T; ++t) {
+    const int st = t % P.S;
+    if (!__all_sync(0xffffffffu, xs_bar_wait(&full[st], (t / P.S) & 1, P.err, XS_ERR_FULL))) break;
+    const int q = t * P.G + g;  // this warp's row of the stage (local index)
+    if (q < rows) {
+      const uint8_t* stage = xs_smem + L.ring + (size_t)st * (size_t)P.stage_bytes;
+      const uint8_t* rowp = stage + (size_t)g * P.row_bytes;
+      float v = 0.f;
+      if (live) {
+        if constexpr (QT == GGUF_Q4_K) {
+          const uint8_t* blk = rowp + kb * Q4K_BYTES;
+          const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * u);
+          const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * u);
+          const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+          const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+          int ahi = 0, alo = 0, bhi = 0, blo = 0;
+#pragma unroll
+          for (int w = 0; w < 8; ++w) {
+            const uint32_t qa4 = W[w] & 0x0F0F0F0Fu, qb4 = (W[w] >> 4) & 0x0F0F0F0Fu;
+            ahi = dp4a_s(qa4, X[w].x, ahi);
+            alo = dp4a_u(qa4, X[w].y, alo);
+            bhi = dp4a_s(qb4, X[w].z, bhi);
+            blo = dp4a_u(qb4, X[w].w, blo);
+          }
+          const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
+          uint32_t scp, mp;
+          if (!hi4) {
+            scp = (s0 >> sh) & 0x3F3Fu;
+            mp = (s1 >> sh) & 0x3F3Fu;
+          } else {
+            scp = ((s2 >> sh) & 0x0F0Fu) | ((s0 >> (sh + 2)) & 0x3030u);
+            mp = ((s2 >> (sh + 4)) & 0x0F0Fu) | ((s1 >> (sh + 2)) & 0x3030u);
+          }
+          const int da = ahi * 256 + alo, db = bhi * 256 + blo;  // |.| < 2^23
+          const int iv = (int)(scp & 0xffu) * da + (int)(scp >> 8) * db;  // |iv| < 2^30
+          const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xffff));
+          const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
+          const float msum = fmaf((float)(mp & 0xffu), sa, (float)(mp >> 8) * sbb);
+          v = fmaf(d * xf, (float)iv, -dmin * msum);
+        } else {
+          const uint8_t* blk = rowp + kb * Q6K_BODY;
+          const uint4 p0 = *reinterpret_cast<const uint4*>(blk + 48 * u);
+          const uint4 p1 = *reinterpret_cast<const uint4*>(blk + 48 * u + 16);
+          const uint4 p2 = *reinterpret_cast<const uint4*>(blk + 48 * u + 32);
+          const uint4 scw = *reinterpret_cast<const uint4*>(blk + 192);
+          const uint16_t dbits =
+              reinterpret_cast<const uint16_t*>(stage + (size_t)P.G * P.row_bytes + (size_t)g * P.d_row_bytes)[kb];
+          const uint32_t ql[2][2][2] = {{{p0.x, p0.y}, {p0.z, p0.w}}, {{p1.x, p1.y}, {p1.z, p1.w}}};
+          const uint32_t qh[2][2] = {{p2.x, p2.y}, {p2.z, p2.w}};
+          const uint32_t SCW[4] = {scw.x, scw.y, scw.z, scw.w};
+          int ih = 0, il = 0;  // sum over groups of scale * (hi-limb / lo-limb products)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            int hi[4], lo[4];
+#pragma unroll
+            for (int gg = 0; gg < 4; ++gg) {
+              hi[gg] = Sh[h][gg];
+              lo[gg] = Sl[h][gg];
+            }
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+              // six-bit quants: low nibble | two high bits << 4 (Hm: fields g0, g2; Hn: g1, g3)
+              const uint32_t H = qh[h][w];
+              const uint32_t Hm = H & 0x33333333u, Hn = (H >> 2) & 0x33333333u;
+              const uint32_t A0 = ql[h][0][w], A1 = ql[h][1][w];
+              const uint32_t q0 = (A0 & 0x0F0F0F0Fu) | ((Hm << 4) & 0xF0F0F0F0u);
+              const uint32_t q1 = (A1 & 0x0F0F0F0Fu) | ((Hn << 4) & 0xF0F0F0F0u);
+              const uint32_t q2 = ((A0 >> 4) & 0x0F0F0F0Fu) | (Hm & 0xF0F0F0F0u);
+              const uint32_t q3 = ((A1 >> 4) & 0x0F0F0F0Fu) | (Hn & 0xF0F0F0F0u);
+              const uint4 x01 = X[4 * h + 2 * w], x23 = X[4 * h + 2 * w + 1];
+              hi[0] = dp4a_s(q0, x01.x, hi[0]);
+              lo[0] = dp4a_u(q0, x01.y, lo[0]);
+              hi[1] = dp4a_s(q1, x01.z, hi[1]);
+              lo[1] = dp4a_u(q1, x01.w, lo[1]);
+              hi[2] = dp4a_s(q2, x23.x, hi[2]);
+              lo[2] = dp4a_u(q2, x23.y, lo[2]);
+              hi[3] = dp4a_s(q3, x23.z, hi[3]);
+              lo[3] = dp4a_u(q3, x23.w, lo[3]);
+            }
+#pragma unroll
+            for (int gg = 0; gg < 4; ++gg) {
+              // scale byte 8h + 2gg + u/2: word 2h + gg/2, byte 2(gg%2) + u/2
+              const int scv = (int)prmt(SCW[2 * h + (gg >> 1)], 0u, (gg & 1) ? sel_hi : sel_lo);
+              ih += scv * hi[gg];  // |.| < 2^24 in total
+              il += scv * lo[gg];  // |.| < 2^26 in total
+            }
+          }
+          v = fmaf(256.f, (float)ih, (float)il) * (f16_bits_to_f32(dbits) * xf);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) part[q * P.nk + s] = v;
+    }
+    __syncwarp();
+    if (lane == 0) xs_bar_arrive(&empty[st]);
+  }
+  xs_named_sync(1, NC * 32);
+  for (int q = threadIdx.x; q < rows; q += NC * 32) {
+    float acc = 0.f;
+    for (int t = 0; t < P.nk; ++t) acc += part[q * P.nk + t];
+    const int64_t row = r0 + q;
+    P.y[row] = acc + (P.bias ? P.bias[row] : 0.f);
+  }
+}
+
+struct XsLaunch {
+  bool ok = false;
+  int threads = 0, grid = 0, G = 0, S = 0, rows_max = 0;
+  int64_t stage_bytes = 0;
+  size_t smem = 0;
+};
+
+// Launch shape of the single-token kernel, or ok = false when it does not
+// apply (more than XS_MAX_COMPUTE slices, or a ring of fewer than 2 stages).
+XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms) {
+  XsLaunch r;
+  const int nk = (int)((sb + XS_SPW - 1) / XS_SPW);
+  if (n < 1 || nk < 1 || nk > XS_MAX_COMPUTE) return r;
+  r.G = XS_MAX_COMPUTE / nk;
+  r.threads = 32 * (nk * r.G + 1);
+  r.grid = (int)std::min<int64_t>(n, num_sms);
+  r.rows_max = (int)((n + r.grid - 1) / r.grid);
+  const int64_t row_bytes = sb * (qt == GGUF_Q4_K ? Q4K_BYTES : Q6K_BODY);
+  const int64_t d_row_bytes = qt == GGUF_Q6_K ? q6k_d_ld(sb) * 2 : 0;
+  r.stage_bytes = r.G * (row_bytes + d_row_bytes);
+  const int T = (r.rows_max + r.G - 1) / r.G;
+  const size_t fixed = XsSmem(qt, nk, r.stage_bytes, 0, r.rows_max).end + 64;
+  if (fixed >= (size_t)XS_MAX_SMEM) return r;
+  const int64_t fit = (int64_t)((XS_MAX_SMEM - fixed) / (size_t)(r.stage_bytes + 16));
+  const int64_t want = std::max<int64_t>(2, (XS_INFLIGHT + r.stage_bytes / 2) / r.stage_bytes);
+  const int S = (int)std::min<int64_t>(std::min<int64_t>(T, fit), want);
+  if (S < std::min(T, 2)) return r;
+  r.S = S;
+  r.smem = XsSmem(qt, nk, r.stage_bytes, S, r.rows_max).end;
+  r.ok = r.smem <= (size_t)XS_MAX_SMEM;
+  return r;
+}
+
+template <int QT>
+cudaError_t launch_xs(const DevWeight& w, const float* x, const float* bias, float* y, int* err, cudaStream_t s,
+                      const XsLaunch& sh) {
+  XsParams P;
+  P.q = w.q;
+  P.d = w.d;
+  P.row_bytes = w.sb * (QT == GGUF_Q4_K ? Q4K_BYTES : Q6K_BODY);
+  P.d_row_bytes = QT == GGUF_Q6_K ? (int)(w.d_ld * 2) : 0;
+  P.n = (int)w.n;
+  P.sb = (int)w.sb;
+  P.nk = (int)((w.sb + XS_SPW - 1) / XS_SPW);
+  P.G = sh.G;
+  P.S = sh.S;
+  P.rows_max = sh.rows_max;
+  P.stage_bytes = sh.stage_bytes;
+  P.x = x;
+  P.bias = bias;
+  P.y = y;
+  P.err = err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)sh.grid);
+  cfg.blockDim = dim3((unsigned)sh.threads);
+  cfg.dynamicSmemBytes = sh.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT>, P);
+}
+
+}  // namespace
+
+cudaError_t dp4a_init_device() {
+  cudaError_t e = cudaFuncSetAttribute(xs_gemv_kernel<GGUF_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       XS_MAX_SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(xs_gemv_kernel<GGUF_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, XS_MAX_SMEM);
+  return e;
+}
+
+size_t dp4a_workspace_bytes(int type, int64_t m, int64_t sb) {
+  if (type == GGUF_Q4_K) return dp4a_layout<GGUF_Q4_K>(m, sb).end;
+  if (type == GGUF_Q6_K) return dp4a_layout<GGUF_Q6_K>(m, sb).end;
+  return 0;
+}
+
+cudaError_t launch_gemv_dp4a(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y, void* ws,
+                             int num_sms, int* err, cudaStream_t s, int* launches, Bracket br) {
+  if (m < 1 || m > DP4A_MAX_M) return cudaErrorInvalidValue;
+  if (m == 1 && (w.type == GGUF_Q4_K || w.type == GGUF_Q6_K)) {
+    const XsLaunch sh = xs_shape(w.type, w.n, w.sb, num_sms);
+    if (sh.ok) {
+      bracket_record(br.start, s);
+      cudaError_t e = w.type == GGUF_Q4_K ? launch_xs<GGUF_Q4_K>(w, x, bias, y, err, s, sh)
+                                          : launch_xs<GGUF_Q6_K>(w, x, bias, y, err, s, sh);
+      if (e != cudaSuccess) return e;
+      if (launches) ++*launches;
+      bracket_record(br.stop, s);
+      return cudaSuccess;
+    }
+  }
+  if (w.type == GGUF_Q4_K) return launch_typed<GGUF_Q4_K>(w, x, m, bias, y, ws, num_sms, s, launches, br);
+  if (w.type == GGUF_Q6_K) return launch_typed<GGUF_Q6_K>(w, x, m, bias, y, ws, num_sms, s, launches, br);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace kq

@@ -203,17 +203,17 @@ __device__ __forceinline__ void stage_issue(uint8_t* slot, const uint8_t* __rest
     cp_async16(la + 48, B + 48 * c);
     cp_async16(la + 64, B + 48 * c + 16);
     cp_async16(la + 80, B + 48 * c + 32);
-    // d is superblock-major [sb][d_ld]: copy the aligned pair holding d(row, kb)
-    const size_t dld = (size_t)q6k_d_ld(n);
-    cp_async4(la + 96, wd + (size_t)kb * dld + (size_t)(ra & ~int64_t(1)));
-    cp_async4(la + 100, wd + (size_t)kb * dld + (size_t)(rb & ~int64_t(1)));
+    // d is row-major [n][d_ld]: copy the aligned pair holding d(row, kb)
+    const size_t dld = (size_t)q6k_d_ld(sb);
+    cp_async4(la + 96, wd + (size_t)ra * dld + (size_t)(kb & ~1));
+    cp_async4(la + 100, wd + (size_t)rb * dld + (size_t)(kb & ~1));
     if (c == 0) cp_async16(slot + S::HDR + 16 * g, A + 192);
     if (c == 1) cp_async16(slot + S::HDR + 16 * (g + 8), B + 192);
   }
 }
 
 template <int QT>
-__device__ __forceinline__ void stage_read(const uint8_t* slot, int64_t ra, int64_t rb,
+__device__ __forceinline__ void stage_read(const uint8_t* slot, int kb,
                                            int g, int lane, typename RawT<QT>::type& a,
                                            typename RawT<QT>::type& b) {
   using S = Stage<QT>;
@@ -234,8 +234,8 @@ __device__ __forceinline__ void stage_read(const uint8_t* slot, int64_t ra, int6
     b.p23 = l4[4];
     b.p45 = l4[5];
     const uint2 dd = *reinterpret_cast<const uint2*>(la + 96);
-    a.d = (ra & 1) ? (dd.x >> 16) : (dd.x & 0xffff);
-    b.d = (rb & 1) ? (dd.y >> 16) : (dd.y & 0xffff);
+    a.d = (kb & 1) ? (dd.x >> 16) : (dd.x & 0xffff);
+    b.d = (kb & 1) ? (dd.y >> 16) : (dd.y & 0xffff);
     a.sc = *reinterpret_cast<const uint4*>(slot + S::HDR + 16 * g);
     b.sc = *reinterpret_cast<const uint4*>(slot + S::HDR + 16 * (g + 8));
   }
@@ -437,7 +437,7 @@ __global__ void __launch_bounds__(32 * KSPLIT_WARPS)
     __syncwarp();
     const uint8_t* cur = wring + (it % ST) * slot;
     Raw ca, cb;
-    stage_read<QT>(cur, ra, rb, g, lane, ca, cb);
+    stage_read<QT>(cur, kb, g, lane, ca, cb);
     // B fragments of this superblock, from the slot or (m > 4) from L2
     const uint4* bs = bcol[0] ? reinterpret_cast<const uint4*>(cur + Stage<QT>::BYTES + 16 +
                                                                compact * 128)

@@ -23,9 +23,9 @@ enum QType : int {
 // Device-resident weight.  For GGUF types the row count is n, the row length k
 // (a multiple of 256) and sb = k/256 superblocks per row.
 //  GGUF_Q4_K: q = raw GGUF superblocks [n][sb][144]; d unused.
-//  GGUF_Q6_K: q = bodies [n][sb][208] (ql|qh|scales), d = f16 [sb][d_ld]
-//             (superblock-major, rows padded to d_ld = n rounded up to 8, so
-//             the d values of 128 consecutive rows are one 256-byte run).
+//  GGUF_Q6_K: q = bodies [n][sb][208] (ql|qh|scales), d = f16 [n][d_ld]
+//             (row-major, d_ld = sb rounded up to 8 so every row's d is a
+//             whole number of 16-byte units and a block of rows is one run).
 //  LEGACY_*:  q = raw bytes as uploaded (row stride = legacy row bytes), len.
 // wmap / dmap: TMA descriptors of q (128 rows x one superblock per box) and d.
 struct DevWeight {
@@ -39,7 +39,7 @@ struct DevWeight {
   CUtensorMap wmap, dmap;
 };
 
-__host__ __device__ inline int64_t q6k_d_ld(int64_t n) { return (n + 7) & ~int64_t(7); }
+__host__ __device__ inline int64_t q6k_d_ld(int64_t sb) { return (sb + 7) & ~int64_t(7); }
 
 // One-time per-device kernel set-up (shared-memory carve-outs); call with the
 // device current, outside any stream capture.
@@ -77,9 +77,21 @@ cudaError_t launch_dequant_f32(const DevWeight& w, int64_t row0, int64_t nrows, 
                                cudaStream_t s);
 
 // Re-lay GGUF Q6_K superblocks [n][sb][210] into bodies [n][sb][208] and
-// d [sb][d_ld] (padding entries are left as they are).
+// d [n][d_ld] (padding entries are left as they are).
 cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t n, int64_t sb, uint8_t* body, uint16_t* d,
                                 cudaStream_t s);
+
+// ---- CUDA-core integer decode path: kq_dp4a.cu ----
+constexpr int DP4A_MAX_M = 4;
+// Per-device set-up of the dp4a kernels (shared-memory carve-outs).
+cudaError_t dp4a_init_device();
+// Scratch for launch_gemv_dp4a (prepared activations for m tokens).
+size_t dp4a_workspace_bytes(int type, int64_t m, int64_t sb);
+// y = x . W^T (+bias) for GGUF Q4_K / Q6_K, 1 <= m <= DP4A_MAX_M, f32 x.
+// *err (device int) receives a nonzero code if a pipeline wait gave up.
+cudaError_t launch_gemv_dp4a(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y,
+                             void* ws, int num_sms, int* err, cudaStream_t s, int* launches,
+                             Bracket br = Bracket());
 
 // ---- tensor-core (tcgen05) path: kq_mma.cu ----
 // Build the TMA descriptors of a GGUF weight (after its device arrays exist).

@@ -61,7 +61,7 @@ template <>
 struct RawTile<GGUF_Q6_K> {
   static constexpr int ROW = Q6K_BODY;
   static constexpr int BODY = TM * Q6K_BODY;     // 26624
-  static constexpr int BYTES = BODY + TM * 2;    // + d of the 128 rows
+  static constexpr int BYTES = BODY + TM * 16;   // + d of the 128 rows for 8 superblocks
 };
 
 template <int QT, int BN>
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
         mbar_expect_tx(&raw_full[rs], R::BYTES);
         const int kb = sb_lo + i;
         tma_load_2d(dst, &wmap, kb * R::ROW, row0, &raw_full[rs]);
-        if constexpr (QT == GGUF_Q6_K) tma_load_2d(dst + R::BODY, &dmap, row0, kb, &raw_full[rs]);
+        if constexpr (QT == GGUF_Q6_K) tma_load_2d(dst + R::BODY, &dmap, kb & ~7, row0, &raw_full[rs]);
         for (; bq < nq && bq < 4 * (i + 1); ++bq) {
           const int bs = bq % C::BS;
           if (bq >= C::BS && !mbar_wait(&b_empty[bs], ((bq / C::BS) - 1) & 1, P.err, ERR_WAIT_B)) {
@@ -343,7 +343,7 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
         const uint4 p0 = rp[3 * c0], p1 = rp[3 * c0 + 1], p2 = rp[3 * c0 + 2];
         const uint4 p3 = rp[3 * c0 + 3], p4 = rp[3 * c0 + 4], p5 = rp[3 * c0 + 5];
         const uint4 sc = rp[12];
-        const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(raw + R::BODY)[r]);
+        const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(raw + R::BODY)[r * 8 + ((sb_lo + i) & 7)]);
         mbar_arrive(&raw_empty[rs]);
         unpack_q6<BF16>(p0, p1, p2, sc, d, c0, a0);
         const int q0 = 4 * i + c0, s0 = q0 % C::AS;
@@ -648,8 +648,9 @@ bool tc_make_weight_maps(DevWeight& w) {
   if (!make_map_2d(&w.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q, rb, (uint64_t)w.n, rb, Q6K_BODY, TM,
                    CU_TENSOR_MAP_SWIZZLE_NONE))
     return false;
-  return make_map_2d(&w.dmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.d, (uint64_t)w.d_ld, (uint64_t)w.sb,
-                     (uint64_t)w.d_ld * 2, TM, 1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  // d [n][d_ld]: one box = the d of 8 superblocks (16 bytes) for 128 rows
+  return make_map_2d(&w.dmap, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.d, (uint64_t)w.d_ld, (uint64_t)w.n,
+                     (uint64_t)w.d_ld * 2, 8, TM, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 size_t tc_workspace_bytes(int64_t m, int64_t n, int64_t k, int num_sms) {

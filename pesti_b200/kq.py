@@ -48,13 +48,14 @@ KQ_SYNC = 2
 KQ_PATH_AUTO = 0
 KQ_PATH_TCGEN05 = 1
 KQ_PATH_MMA = 2
+KQ_PATH_DP4A = 3
 
 #: every symbol include/pesti_kq.h declares
 EXPORTED_SYMBOLS = (
     "kq_abi_version", "kq_status_string", "kq_last_error",
     "kq_ctx_create", "kq_ctx_destroy", "kq_ctx_set_stream", "kq_ctx_synchronize",
     "kq_ctx_set_path", "kq_ctx_reserve", "kq_ctx_launch_count", "kq_ctx_profile_begin",
-    "kq_ctx_profile_end", "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
+    "kq_ctx_profile_end", "kq_ctx_profile_read", "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
     "kq_linear_f32", "kq_linear_bf16", "kq_dequant_f32",
 )
 
@@ -100,6 +101,7 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
             "kq_ctx_launch_count": ([P], I64),
             "kq_ctx_profile_begin": ([P, I], I),
             "kq_ctx_profile_end": ([P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(I64)], I),
+            "kq_ctx_profile_read": ([P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(I64)], I),
             "kq_row_bytes": ([I, I64, ctypes.POINTER(I64)], I),
             "kq_weight_upload": ([P, I, P, Z, I64, I64, PP], I),
             "kq_weight_free": ([P], I),
@@ -165,7 +167,7 @@ class Context:
         self.check(self.lib.kq_ctx_synchronize(self.handle), "kq_ctx_synchronize")
 
     def set_path(self, path: int) -> None:
-        """KQ_PATH_AUTO / KQ_PATH_TCGEN05 / KQ_PATH_MMA for GGUF weights."""
+        """KQ_PATH_AUTO / KQ_PATH_TCGEN05 / KQ_PATH_MMA / KQ_PATH_DP4A for GGUF weights."""
         self.check(self.lib.kq_ctx_set_path(self.handle, path), "kq_ctx_set_path")
 
     def reserve(self, weight: "Weight", m: int) -> None:
@@ -185,6 +187,13 @@ class Context:
         ms, n = ctypes.c_double(), ctypes.c_int64()
         self.check(self.lib.kq_ctx_profile_end(self.handle, ctypes.byref(ms), ctypes.byref(n)),
                    "kq_ctx_profile_end")
+        return ms.value, n.value
+
+    def profile_read(self):
+        """-> (summed main-kernel milliseconds, count) as last recorded, session kept open."""
+        ms, n = ctypes.c_double(), ctypes.c_int64()
+        self.check(self.lib.kq_ctx_profile_read(self.handle, ctypes.byref(ms), ctypes.byref(n)),
+                   "kq_ctx_profile_read")
         return ms.value, n.value
 
     def close(self) -> None:

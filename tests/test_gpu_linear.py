@@ -83,12 +83,14 @@ CASES = [
 ]
 
 
-PATHS = {"tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA}
+PATHS = {"tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA, "dp4a": kq.KQ_PATH_DP4A}
+DP4A_MAX_M = 4  # the integer dot-product family serves 1..4 tokens
 
 
 @pytest.fixture(params=sorted(PATHS))
 def path_ctx(gpu_ctx, request):
     gpu_ctx.set_path(PATHS[request.param])
+    gpu_ctx.path_name = request.param
     yield gpu_ctx
     gpu_ctx.set_path(kq.KQ_PATH_AUTO)
 
@@ -110,6 +112,8 @@ def test_tcgen05_single_tile_first(gpu_ctx):
 
 @pytest.mark.parametrize("dt,n,k,m", CASES)
 def test_linear_matches_oracle(path_ctx, dt, n, k, m):
+    if path_ctx.path_name == "dp4a" and m > DP4A_MAX_M:
+        pytest.skip("larger batches leave the dp4a family")
     kt, ot = GGUF[dt]
     raw = synthetic.gguf_weight(kt, n, k, seed=n + k)
     x = synthetic.activations(m, k, seed=m)
@@ -122,6 +126,41 @@ def test_linear_matches_oracle(path_ctx, dt, n, k, m):
     wf = oracle.gguf_dequant_rows(ot, raw, n, k).astype(np.float64)
     ref64 = x.astype(np.float64) @ wf.T + bias
     assert rel_err(y, ref64) <= TOL
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
+def test_activation_outliers(path_ctx, dt):
+    # one large activation per token and a superblock of tiny ones: the decode
+    # kernels scale activations per token or per superblock, both must hold
+    kt, ot = GGUF[dt]
+    n, k, m = 96, 2048, 3
+    raw = synthetic.gguf_weight(kt, n, k, seed=11)
+    x = synthetic.activations(m, k, seed=12)
+    x[0, 7] = 3.0e4
+    x[1, 300:556] *= 1e-30
+    x[2, 1000] = -5.0e3
+    w = kq.Weight(path_ctx, kt, raw, n, k)
+    y = np.empty((m, n), np.float32)
+    w.linear(x, m, y)
+    wf = oracle.gguf_dequant_rows(ot, raw, n, k).astype(np.float64)
+    ref = x.astype(np.float64) @ wf.T
+    for t in range(m):
+        assert rel_err(y[t], ref[t]) <= TOL
+
+
+def test_nonfinite_activation_gives_nonfinite_rows(gpu_ctx):
+    kt, ot = GGUF["Q4_K"]
+    n, k = 64, 1024
+    raw = synthetic.gguf_weight(kt, n, k, seed=13)
+    x = synthetic.activations(2, k, seed=14)
+    x[1, 5] = np.inf
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    y = np.empty((2, n), np.float32)
+    w.linear(x, 2, y)
+    ref = oracle.gguf_linear(ot, raw, n, k, x)
+    assert np.isfinite(y[0]).all()
+    assert rel_err(y[0], ref[0]) <= TOL
+    assert not np.isfinite(ref[1]).any() and not np.isfinite(y[1]).any()
 
 
 # ---- prefill: bf16 activations on tcgen05, <= 2e-2 against the f32 product ----
