@@ -124,6 +124,16 @@ int kq_linear_f32(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t m,
  * kernel (the north-star prefill dequant-GEMM). */
 int kq_linear_bf16(kq_ctx *ctx, const kq_weight *w, const void *x_bf16, int64_t m,
                    const float *bias, float *y, int flags);
+/* Same product for callers that must not allocate device memory during the
+ * call.  No counterpart in the reference (its CPU path has no device memory).
+ * GGUF weights, 1 <= m <= 4, device pointers only (flags must hold
+ * KQ_DEVICE_PTRS).  Scratch comes from one fixed 256 KiB device array per
+ * device (enough for in_features <= 16384); larger shapes are rejected with
+ * KQ_ERR_UNSUPPORTED.  The array's address is looked up on the first call on
+ * each device, so make that first call before any stream capture.  Calls on
+ * one device that are not ordered with each other race on the shared scratch. */
+int kq_linear_f32_static(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t m,
+                         const float *bias, float *y, int flags);
 /* Dequantize rows [row0, row0+nrows) to f32 [nrows][in_features], bit-exact
  * with the CPU decode of the same encoding (QuantizedLinear::
  * dequantize_full_row_range, quantized_linear.rs:146-183, for legacy types). */

@@ -570,6 +570,43 @@ int kq_linear_bf16(kq_ctx* ctx, const kq_weight* w, const void* x_bf16, int64_t 
   return linear_impl(ctx, w, x_bf16, 2, m, bias, y, flags, true);
 }
 
+int kq_linear_f32_static(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, const float* bias, float* y,
+                         int flags) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!w) return fail(ctx, KQ_ERR_INVALID_ARG, "weight is null");
+  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
+  if (!(flags & KQ_DEVICE_PTRS))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_linear_f32_static takes device pointers only (KQ_DEVICE_PTRS)");
+  if (w->device != ctx->device)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device, ctx->device);
+  if (!is_gguf(w->dw.type)) return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_linear_f32_static needs a GGUF Q4_K / Q6_K weight");
+  if (m < 1 || m > kq::DP4A_MAX_M)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_linear_f32_static serves 1..%d rows, got m = %lld", kq::DP4A_MAX_M,
+                (long long)m);
+  const size_t need = kq::dp4a_workspace_bytes(w->dw.type, m, w->dw.sb);
+  if (need > kq::DP4A_STATIC_SCRATCH)
+    return fail(ctx, KQ_ERR_UNSUPPORTED,
+                "m = %lld x in_features = %lld needs %zu bytes of scratch; the fixed scratch holds %zu "
+                "(enough for m <= 4 with in_features <= 16384)",
+                (long long)m, (long long)w->dw.k, need, kq::DP4A_STATIC_SCRATCH);
+  if (w->dw.n == 0) return KQ_OK;
+  if (!y || !x) return fail(ctx, KQ_ERR_INVALID_ARG, "x or y is null");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) ||
+      ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(bias)) & 3))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "x must be 16-byte aligned, y and bias 4-byte aligned");
+  DeviceGuard g(ctx->device);
+  if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
+  void* scratch = nullptr;
+  cudaError_t e = kq::dp4a_static_scratch(&scratch);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "cudaGetSymbolAddress of the fixed scratch");
+  int launches = 0;
+  e = kq::launch_gemv_dp4a_batched(w->dw, x, m, bias, y, scratch, ctx->num_sms, ctx->stream, &launches);
+  ctx->launches += launches;
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
+  if (flags & KQ_SYNC) return finish_sync(ctx, "linear");
+  return KQ_OK;
+}
+
 int kq_dequant_f32(kq_ctx* ctx, const kq_weight* w, int64_t row0, int64_t nrows, float* out, int flags) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!w) return fail(ctx, KQ_ERR_INVALID_ARG, "weight is null");

@@ -992,6 +992,48 @@ cudaError_t launch_xs(const DevWeight& w, const float* x, const float* bias, flo
 
 }  // namespace
 
+// ---- fixed scratch for the no-allocation entry ----------------------------------
+// Some callers cannot allocate device memory on the call path: a serving
+// engine that has handed all of HBM to weights and KV cache up front, or a
+// loop whose latency budget cannot absorb cudaMalloc (which may synchronise
+// the device and stall every stream).  For them the batched dp4a kernels can
+// take their scratch (the prepared activations) from this file-scope array
+// instead of the context's grow-on-demand buffer.  Nothing in it needs to
+// start at zero: the prep kernel writes every byte the GEMV kernel reads.
+// There is one array per device, shared by every context: calls that use it
+// concurrently (different streams or contexts on one device without
+// ordering between them) race on its contents.
+static __device__ __align__(256) uint8_t g_dp4a_static_scratch[DP4A_STATIC_SCRATCH];
+
+cudaError_t dp4a_static_scratch(void** ptr) {
+  constexpr int MAX_DEVICES = 64;
+  static std::mutex mu;
+  static void* cached[MAX_DEVICES] = {};
+  *ptr = nullptr;
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= MAX_DEVICES) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (!cached[dev]) {
+    // once per device, with that device current
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_dp4a_static_scratch);
+    if (e != cudaSuccess) return e;
+    cached[dev] = p;
+  }
+  *ptr = cached[dev];
+  return cudaSuccess;
+}
+
+cudaError_t launch_gemv_dp4a_batched(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y,
+                                     void* ws, int num_sms, cudaStream_t s, int* launches) {
+  if (m < 1 || m > DP4A_MAX_M) return cudaErrorInvalidValue;
+  if (w.type == GGUF_Q4_K) return launch_typed<GGUF_Q4_K>(w, x, m, bias, y, ws, num_sms, s, launches, Bracket());
+  if (w.type == GGUF_Q6_K) return launch_typed<GGUF_Q6_K>(w, x, m, bias, y, ws, num_sms, s, launches, Bracket());
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t dp4a_init_device() {
   cudaError_t e = cudaFuncSetAttribute(xs_gemv_kernel<GGUF_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        XS_MAX_SMEM);

@@ -88,6 +88,15 @@ cudaError_t dp4a_init_device();
 // Scratch for launch_gemv_dp4a (prepared activations for m tokens).
 size_t dp4a_workspace_bytes(int type, int64_t m, int64_t sb);
 // y = x . W^T (+bias) for GGUF Q4_K / Q6_K, 1 <= m <= DP4A_MAX_M, f32 x.
+// The batched dp4a kernels (prepare + GEMV) with caller-provided scratch of
+// dp4a_workspace_bytes(type, m, sb) bytes; 1 <= m <= DP4A_MAX_M.
+cudaError_t launch_gemv_dp4a_batched(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y,
+                                     void* ws, int num_sms, cudaStream_t s, int* launches);
+// Fixed scratch of DP4A_STATIC_SCRATCH bytes in device memory (a file-scope
+// __device__ array): its address on the current device, looked up once per
+// device.  Used by the no-allocation entry point.
+constexpr size_t DP4A_STATIC_SCRATCH = 256 * 1024;
+cudaError_t dp4a_static_scratch(void** ptr);
 // *err (device int) receives a nonzero code if a pipeline wait gave up.
 cudaError_t launch_gemv_dp4a(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y,
                              void* ws, int num_sms, int* err, cudaStream_t s, int* launches,

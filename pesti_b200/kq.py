@@ -56,7 +56,7 @@ EXPORTED_SYMBOLS = (
     "kq_ctx_create", "kq_ctx_destroy", "kq_ctx_set_stream", "kq_ctx_synchronize",
     "kq_ctx_set_path", "kq_ctx_reserve", "kq_ctx_launch_count", "kq_ctx_profile_begin",
     "kq_ctx_profile_end", "kq_ctx_profile_read", "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
-    "kq_linear_f32", "kq_linear_bf16", "kq_dequant_f32",
+    "kq_linear_f32", "kq_linear_bf16", "kq_linear_f32_static", "kq_dequant_f32",
 )
 
 
@@ -109,6 +109,7 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
                                 ctypes.POINTER(I64)], I),
             "kq_linear_f32": ([P, P, P, I64, P, P, I], I),
             "kq_linear_bf16": ([P, P, P, I64, P, P, I], I),
+            "kq_linear_f32_static": ([P, P, P, I64, P, P, I], I),
             "kq_dequant_f32": ([P, P, I64, I64, P, I], I),
         }
         for name, (args, res) in sig.items():
@@ -247,6 +248,12 @@ class Weight:
         flags = (KQ_DEVICE_PTRS if device_ptrs else KQ_HOST_PTRS) | (KQ_SYNC if sync else 0)
         rc = self.ctx.lib.kq_linear_bf16(self.ctx.handle, self.handle, _ptr(x), m, _ptr(bias), _ptr(y), flags)
         self.ctx.check(rc, "kq_linear_bf16")
+
+    def linear_static(self, x, m: int, y, bias=None, sync: bool = False) -> None:
+        """kq_linear_f32_static: device tensors only, scratch from the fixed device array."""
+        flags = KQ_DEVICE_PTRS | (KQ_SYNC if sync else 0)
+        rc = self.ctx.lib.kq_linear_f32_static(self.ctx.handle, self.handle, _ptr(x), m, _ptr(bias), _ptr(y), flags)
+        self.ctx.check(rc, "kq_linear_f32_static")
 
     def dequant(self, row0: int = 0, nrows: Optional[int] = None, out=None, device_ptrs: bool = False):
         nrows = self.out_features - row0 if nrows is None else nrows
