@@ -510,12 +510,13 @@ cudaError_t launch_typed(const DevWeight& w, const float* x, int64_t m, const fl
 // each compute warp owns one K-slice and applies it to every row of its CTA.
 // The weights reach shared memory by bulk TMA copies (cp.async.bulk) issued
 // by one producer warp: each CTA owns a contiguous block of rows and streams
-// it through a ring of S stages of G rows each (rows are contiguous in
+// it through a ring of S stages of 2G rows each (rows are contiguous in
 // memory, Q6_K d rows too), so up to ~100 KB per CTA are in flight without
 // tying up registers or L1 miss slots.  Compute warps: nk K-slices x G row
-// groups; warp (s, g) takes row g of every stage and reduces its partial with
-// shuffles into shared memory; the CTA adds the nk partials in slice order at
-// the end (deterministic).
+// groups; warp (s, g) takes rows g and g + G of every stage and reduces the
+// two partials together with shuffles into shared memory; the CTA adds the
+// nk partials in slice order at the end (deterministic).  Bulk copies carry a
+// fixed cost each, so stages are large (tens of KB).
 //
 // One CTA per SM (up to 15 compute warps + the producer).  The ring holds
 // about XS_INFLIGHT bytes: streaming-read measurements on B200 peak near
@@ -538,7 +539,7 @@ cudaError_t launch_typed(const DevWeight& w, const float* x, int64_t m, const fl
 constexpr int XS_SPW = 8;          // superblocks per warp slice
 constexpr int XS_MAX_COMPUTE = 15;  // compute warps (+ 1 producer = 512 threads)
 constexpr int XS_MAX_SMEM = 227 * 1024;
-constexpr int64_t XS_INFLIGHT = 96 * 1024;  // ring bytes in flight per CTA
+constexpr int64_t XS_INFLIGHT = 144 * 1024;  // ring bytes in flight per CTA
 
 enum : int { XS_ERR_FULL = 21, XS_ERR_EMPTY = 22, XS_ERR_DRAIN = 23 };
 
@@ -549,7 +550,7 @@ struct XsParams {
   int d_row_bytes;      // Q6_K: d bytes per row (a multiple of 16); Q4_K: 0
   int n, sb, nk, G, S;  // rows, superblocks per row, K-slices, rows per stage, ring stages
   int rows_max;         // most rows any CTA owns (shared-memory sizing)
-  int64_t stage_bytes;  // G * (row_bytes + d_row_bytes)
+  int64_t stage_bytes;  // 2G * (row_bytes + d_row_bytes)
   const float* x;
   const float* bias;
   float* y;
@@ -734,11 +735,12 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
 template <int QT>
 __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(const XsParams P) {
   extern __shared__ __align__(128) uint8_t xs_smem[];
-  pdl_trigger();  // the next kernel may move in beside us and start streaming
+  pdl_trigger();  // the next kernel's CTAs may start on each SM as ours retire there
   const int C = gridDim.x, b = blockIdx.x;
   const int64_t r0 = (int64_t)P.n * b / C, r1 = (int64_t)P.n * (b + 1) / C;
   const int rows = (int)(r1 - r0);  // this CTA's rows r0 .. r1-1
-  const int T = (rows + P.G - 1) / P.G;
+  const int R = 2 * P.G;  // rows per stage: each compute warp takes two of them
+  const int T = (rows + R - 1) / R;
   const int NC = P.nk * P.G;
   const XsSmem L(QT, P.nk, P.stage_bytes, P.S, P.rows_max);
   uint64_t* full = reinterpret_cast<uint64_t*>(xs_smem + L.bar);
@@ -760,14 +762,14 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
       for (; t < T; ++t) {
         const int st = t % P.S;
         if (t >= P.S && !xs_bar_wait(&empty[st], ((t / P.S) - 1) & 1, P.err, XS_ERR_EMPTY)) break;
-        const int nr = min(P.G, rows - t * P.G);
-        const int64_t row = r0 + (int64_t)t * P.G;
+        const int nr = min(R, rows - t * R);
+        const int64_t row = r0 + (int64_t)t * R;
         uint8_t* dst = xs_smem + L.ring + (size_t)st * (size_t)P.stage_bytes;
         const uint32_t wb = (uint32_t)(nr * P.row_bytes), db = (uint32_t)(nr * P.d_row_bytes);
         xs_bar_expect(&full[st], wb + db);
         xs_bulk_g2s(dst, P.q + row * P.row_bytes, wb, &full[st]);
         if constexpr (QT == GGUF_Q6_K)
-          xs_bulk_g2s(dst + (size_t)P.G * P.row_bytes, reinterpret_cast<const uint8_t*>(P.d) + row * P.d_row_bytes,
+          xs_bulk_g2s(dst + (size_t)R * P.row_bytes, reinterpret_cast<const uint8_t*>(P.d) + row * P.d_row_bytes,
                       db, &full[st]);
       }
       // the CTA must not retire while a copy into its shared memory is in flight
@@ -781,7 +783,6 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   const int kb = XS_SPW * s + (lane >> 2), u = lane & 3;
   const bool live = kb < P.sb;
   pdl_wait();  // x may be the previous kernel's output
-
   xs_stage_x<QT>(P, L, xs_smem, NC * 32);
   xs_named_sync(1, NC * 32);
 
@@ -819,100 +820,112 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   const bool hi4 = u >= 2;  // Q4_K: sub-blocks 2u, 2u+1 take the packed high scale/min bits
   const int sh = 16 * (u & 1);
 
+  // one row of this warp's slice: returns the lane's partial (0 for lanes past the row's end)
+  auto row_partial = [&](const uint8_t* rowp, const uint8_t* drow) -> float {
+    float v = 0.f;
+    if (live) {
+      if constexpr (QT == GGUF_Q4_K) {
+        const uint8_t* blk = rowp + kb * Q4K_BYTES;
+        const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * u);
+        const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * u);
+        const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+        const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        int ahi = 0, alo = 0, bhi = 0, blo = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const uint32_t qa4 = W[w] & 0x0F0F0F0Fu, qb4 = (W[w] >> 4) & 0x0F0F0F0Fu;
+          ahi = dp4a_s(qa4, X[w].x, ahi);
+          alo = dp4a_u(qa4, X[w].y, alo);
+          bhi = dp4a_s(qb4, X[w].z, bhi);
+          blo = dp4a_u(qb4, X[w].w, blo);
+        }
+        const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
+        uint32_t scp, mp;
+        if (!hi4) {
+          scp = (s0 >> sh) & 0x3F3Fu;
+          mp = (s1 >> sh) & 0x3F3Fu;
+        } else {
+          scp = ((s2 >> sh) & 0x0F0Fu) | ((s0 >> (sh + 2)) & 0x3030u);
+          mp = ((s2 >> (sh + 4)) & 0x0F0Fu) | ((s1 >> (sh + 2)) & 0x3030u);
+        }
+        const int da = ahi * 256 + alo, db = bhi * 256 + blo;  // |.| < 2^23
+        const int iv = (int)(scp & 0xffu) * da + (int)(scp >> 8) * db;  // |iv| < 2^30
+        const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xffff));
+        const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
+        const float msum = fmaf((float)(mp & 0xffu), sa, (float)(mp >> 8) * sbb);
+        v = fmaf(d * xf, (float)iv, -dmin * msum);
+      } else {
+        const uint8_t* blk = rowp + kb * Q6K_BODY;
+        const uint4 p0 = *reinterpret_cast<const uint4*>(blk + 48 * u);
+        const uint4 p1 = *reinterpret_cast<const uint4*>(blk + 48 * u + 16);
+        const uint4 p2 = *reinterpret_cast<const uint4*>(blk + 48 * u + 32);
+        const uint4 scw = *reinterpret_cast<const uint4*>(blk + 192);
+        const uint16_t dbits = reinterpret_cast<const uint16_t*>(drow)[kb];
+        const uint32_t ql[2][2][2] = {{{p0.x, p0.y}, {p0.z, p0.w}}, {{p1.x, p1.y}, {p1.z, p1.w}}};
+        const uint32_t qh[2][2] = {{p2.x, p2.y}, {p2.z, p2.w}};
+        const uint32_t SCW[4] = {scw.x, scw.y, scw.z, scw.w};
+        int ih = 0, il = 0;  // sum over groups of scale * (hi-limb / lo-limb products)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          int hi[4], lo[4];
+#pragma unroll
+          for (int gg = 0; gg < 4; ++gg) {
+            hi[gg] = Sh[h][gg];
+            lo[gg] = Sl[h][gg];
+          }
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            // six-bit quants: low nibble | two high bits << 4 (Hm: fields g0, g2; Hn: g1, g3)
+            const uint32_t H = qh[h][w];
+            const uint32_t Hm = H & 0x33333333u, Hn = (H >> 2) & 0x33333333u;
+            const uint32_t A0 = ql[h][0][w], A1 = ql[h][1][w];
+            const uint32_t q0 = (A0 & 0x0F0F0F0Fu) | ((Hm << 4) & 0xF0F0F0F0u);
+            const uint32_t q1 = (A1 & 0x0F0F0F0Fu) | ((Hn << 4) & 0xF0F0F0F0u);
+            const uint32_t q2 = ((A0 >> 4) & 0x0F0F0F0Fu) | (Hm & 0xF0F0F0F0u);
+            const uint32_t q3 = ((A1 >> 4) & 0x0F0F0F0Fu) | (Hn & 0xF0F0F0F0u);
+            const uint4 x01 = X[4 * h + 2 * w], x23 = X[4 * h + 2 * w + 1];
+            hi[0] = dp4a_s(q0, x01.x, hi[0]);
+            lo[0] = dp4a_u(q0, x01.y, lo[0]);
+            hi[1] = dp4a_s(q1, x01.z, hi[1]);
+            lo[1] = dp4a_u(q1, x01.w, lo[1]);
+            hi[2] = dp4a_s(q2, x23.x, hi[2]);
+            lo[2] = dp4a_u(q2, x23.y, lo[2]);
+            hi[3] = dp4a_s(q3, x23.z, hi[3]);
+            lo[3] = dp4a_u(q3, x23.w, lo[3]);
+          }
+#pragma unroll
+          for (int gg = 0; gg < 4; ++gg) {
+            // scale byte 8h + 2gg + u/2: word 2h + gg/2, byte 2(gg%2) + u/2
+            const int scv = (int)prmt(SCW[2 * h + (gg >> 1)], 0u, (gg & 1) ? sel_hi : sel_lo);
+            ih += scv * hi[gg];  // |.| < 2^24 in total
+            il += scv * lo[gg];  // |.| < 2^26 in total
+          }
+        }
+        v = fmaf(256.f, (float)ih, (float)il) * (f16_bits_to_f32(dbits) * xf);
+      }
+    }
+    return v;
+  };
+
+  // each warp takes rows g and g + G of every stage
   for (int t = 0; t < T; ++t) {
     const int st = t % P.S;
     if (!__all_sync(0xffffffffu, xs_bar_wait(&full[st], (t / P.S) & 1, P.err, XS_ERR_FULL))) break;
-    const int q = t * P.G + g;  // this warp's row of the stage (local index)
-    if (q < rows) {
-      const uint8_t* stage = xs_smem + L.ring + (size_t)st * (size_t)P.stage_bytes;
-      const uint8_t* rowp = stage + (size_t)g * P.row_bytes;
-      float v = 0.f;
-      if (live) {
-        if constexpr (QT == GGUF_Q4_K) {
-          const uint8_t* blk = rowp + kb * Q4K_BYTES;
-          const uint4 qa = *reinterpret_cast<const uint4*>(blk + 16 + 32 * u);
-          const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * u);
-          const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-          const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-          int ahi = 0, alo = 0, bhi = 0, blo = 0;
+    const uint8_t* stage = xs_smem + L.ring + (size_t)st * (size_t)P.stage_bytes;
+    const uint8_t* dstage = stage + (size_t)R * P.row_bytes;
+    const int q0 = t * R + g, q1 = q0 + P.G;  // local rows of this warp
+    const float v0 = q0 < rows ? row_partial(stage + (size_t)g * P.row_bytes, dstage + (size_t)g * P.d_row_bytes) : 0.f;
+    const float v1 = q1 < rows ? row_partial(stage + (size_t)(g + P.G) * P.row_bytes,
+                                             dstage + (size_t)(g + P.G) * P.d_row_bytes)
+                               : 0.f;
+    // reduce both rows at once: lanes 0-15 end with row q0's sum, lanes 16-31 with q1's
+    const bool upper = lane & 16;
+    float keep = upper ? v1 : v0;
+    keep += __shfl_xor_sync(0xffffffffu, upper ? v0 : v1, 16);
 #pragma unroll
-          for (int w = 0; w < 8; ++w) {
-            const uint32_t qa4 = W[w] & 0x0F0F0F0Fu, qb4 = (W[w] >> 4) & 0x0F0F0F0Fu;
-            ahi = dp4a_s(qa4, X[w].x, ahi);
-            alo = dp4a_u(qa4, X[w].y, alo);
-            bhi = dp4a_s(qb4, X[w].z, bhi);
-            blo = dp4a_u(qb4, X[w].w, blo);
-          }
-          const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
-          uint32_t scp, mp;
-          if (!hi4) {
-            scp = (s0 >> sh) & 0x3F3Fu;
-            mp = (s1 >> sh) & 0x3F3Fu;
-          } else {
-            scp = ((s2 >> sh) & 0x0F0Fu) | ((s0 >> (sh + 2)) & 0x3030u);
-            mp = ((s2 >> (sh + 4)) & 0x0F0Fu) | ((s1 >> (sh + 2)) & 0x3030u);
-          }
-          const int da = ahi * 256 + alo, db = bhi * 256 + blo;  // |.| < 2^23
-          const int iv = (int)(scp & 0xffu) * da + (int)(scp >> 8) * db;  // |iv| < 2^30
-          const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xffff));
-          const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
-          const float msum = fmaf((float)(mp & 0xffu), sa, (float)(mp >> 8) * sbb);
-          v = fmaf(d * xf, (float)iv, -dmin * msum);
-        } else {
-          const uint8_t* blk = rowp + kb * Q6K_BODY;
-          const uint4 p0 = *reinterpret_cast<const uint4*>(blk + 48 * u);
-          const uint4 p1 = *reinterpret_cast<const uint4*>(blk + 48 * u + 16);
-          const uint4 p2 = *reinterpret_cast<const uint4*>(blk + 48 * u + 32);
-          const uint4 scw = *reinterpret_cast<const uint4*>(blk + 192);
-          const uint16_t dbits =
-              reinterpret_cast<const uint16_t*>(stage + (size_t)P.G * P.row_bytes + (size_t)g * P.d_row_bytes)[kb];
-          const uint32_t ql[2][2][2] = {{{p0.x, p0.y}, {p0.z, p0.w}}, {{p1.x, p1.y}, {p1.z, p1.w}}};
-          const uint32_t qh[2][2] = {{p2.x, p2.y}, {p2.z, p2.w}};
-          const uint32_t SCW[4] = {scw.x, scw.y, scw.z, scw.w};
-          int ih = 0, il = 0;  // sum over groups of scale * (hi-limb / lo-limb products)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            int hi[4], lo[4];
-#pragma unroll
-            for (int gg = 0; gg < 4; ++gg) {
-              hi[gg] = Sh[h][gg];
-              lo[gg] = Sl[h][gg];
-            }
-#pragma unroll
-            for (int w = 0; w < 2; ++w) {
-              // six-bit quants: low nibble | two high bits << 4 (Hm: fields g0, g2; Hn: g1, g3)
-              const uint32_t H = qh[h][w];
-              const uint32_t Hm = H & 0x33333333u, Hn = (H >> 2) & 0x33333333u;
-              const uint32_t A0 = ql[h][0][w], A1 = ql[h][1][w];
-              const uint32_t q0 = (A0 & 0x0F0F0F0Fu) | ((Hm << 4) & 0xF0F0F0F0u);
-              const uint32_t q1 = (A1 & 0x0F0F0F0Fu) | ((Hn << 4) & 0xF0F0F0F0u);
-              const uint32_t q2 = ((A0 >> 4) & 0x0F0F0F0Fu) | (Hm & 0xF0F0F0F0u);
-              const uint32_t q3 = ((A1 >> 4) & 0x0F0F0F0Fu) | (Hn & 0xF0F0F0F0u);
-              const uint4 x01 = X[4 * h + 2 * w], x23 = X[4 * h + 2 * w + 1];
-              hi[0] = dp4a_s(q0, x01.x, hi[0]);
-              lo[0] = dp4a_u(q0, x01.y, lo[0]);
-              hi[1] = dp4a_s(q1, x01.z, hi[1]);
-              lo[1] = dp4a_u(q1, x01.w, lo[1]);
-              hi[2] = dp4a_s(q2, x23.x, hi[2]);
-              lo[2] = dp4a_u(q2, x23.y, lo[2]);
-              hi[3] = dp4a_s(q3, x23.z, hi[3]);
-              lo[3] = dp4a_u(q3, x23.w, lo[3]);
-            }
-#pragma unroll
-            for (int gg = 0; gg < 4; ++gg) {
-              // scale byte 8h + 2gg + u/2: word 2h + gg/2, byte 2(gg%2) + u/2
-              const int scv = (int)prmt(SCW[2 * h + (gg >> 1)], 0u, (gg & 1) ? sel_hi : sel_lo);
-              ih += scv * hi[gg];  // |.| < 2^24 in total
-              il += scv * lo[gg];  // |.| < 2^26 in total
-            }
-          }
-          v = fmaf(256.f, (float)ih, (float)il) * (f16_bits_to_f32(dbits) * xf);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) part[q * P.nk + s] = v;
-    }
+    for (int o = 8; o > 0; o >>= 1) keep += __shfl_xor_sync(0xffffffffu, keep, o);
+    if (lane == 0 && q0 < rows) part[q0 * P.nk + s] = keep;
+    if (lane == 16 && q1 < rows) part[q1 * P.nk + s] = keep;
     __syncwarp();
     if (lane == 0) xs_bar_arrive(&empty[st]);
   }
@@ -944,8 +957,8 @@ XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms) {
   r.rows_max = (int)((n + r.grid - 1) / r.grid);
   const int64_t row_bytes = sb * (qt == GGUF_Q4_K ? Q4K_BYTES : Q6K_BODY);
   const int64_t d_row_bytes = qt == GGUF_Q6_K ? q6k_d_ld(sb) * 2 : 0;
-  r.stage_bytes = r.G * (row_bytes + d_row_bytes);
-  const int T = (r.rows_max + r.G - 1) / r.G;
+  r.stage_bytes = 2 * r.G * (row_bytes + d_row_bytes);  // 2G rows per stage
+  const int T = (r.rows_max + 2 * r.G - 1) / (2 * r.G);
   const size_t fixed = XsSmem(qt, nk, r.stage_bytes, 0, r.rows_max).end + 64;
   if (fixed >= (size_t)XS_MAX_SMEM) return r;
   const int64_t fit = (int64_t)((XS_MAX_SMEM - fixed) / (size_t)(r.stage_bytes + 16));
