@@ -70,7 +70,7 @@ def parse():
     p.add_argument("--workload", choices=sorted(WORKLOADS), default="q6k-gemv")
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a"], default="auto",
-                   help="kernel family for the GEMV (auto = tcgen05)")
+                   help="kernel family for the GEMV (auto: dp4a m<=4, mma m<=64, tcgen05 above)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     return p.parse_args()
 

@@ -55,7 +55,7 @@ enum kq_type {
 #define KQ_SYNC 2        /* synchronise the context stream before return  */
 
 /* kernel families for GGUF weights with f32 activations (kq_ctx_set_path) */
-#define KQ_PATH_AUTO 0    /* default: DP4A for m <= 4, else TCGEN05           */
+#define KQ_PATH_AUTO 0    /* default: DP4A m <= 4, MMA m <= 64, else TCGEN05 */
 #define KQ_PATH_TCGEN05 1 /* tcgen05.mma, dequantized A written to TMEM      */
 #define KQ_PATH_MMA 2     /* warp-level mma.sync tiles (cp.async staging)     */
 #define KQ_PATH_DP4A 3    /* CUDA-core integer dot products, m <= 4 only;    */

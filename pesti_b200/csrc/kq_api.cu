@@ -160,10 +160,13 @@ int finish_sync(kq_ctx* ctx, const char* what) {
   return check_device_error(ctx);
 }
 
-// Kernel family for a GGUF f32 call of m tokens.
+// Kernel family for a GGUF f32 call of m tokens.  AUTO: integer dot products
+// up to DP4A_MAX_M tokens, warp-level mma.sync tiles up to 64, tcgen05 above
+// (the choice follows the measured decode throughput of each family).
 int f32_family(const kq_ctx* ctx, int64_t m) {
   if (ctx->path == KQ_PATH_MMA || ctx->path == KQ_PATH_TCGEN05) return ctx->path;
-  return m <= kq::DP4A_MAX_M ? KQ_PATH_DP4A : KQ_PATH_TCGEN05;
+  if (m <= kq::DP4A_MAX_M) return KQ_PATH_DP4A;
+  return m <= 64 ? KQ_PATH_MMA : KQ_PATH_TCGEN05;
 }
 
 // Scratch bytes and zeroed counter bytes a GGUF f32 call of m tokens needs.
