@@ -51,6 +51,12 @@ WORKLOADS = {
     "q6k-gemv": (14, 114, 4096, 14336, "Q6_K dequant+GEMV 4096x14336 (down-proj shape)"),
     "q4k-gemv": (12, 112, 4096, 4096, "Q4_K dequant+GEMV 4096x4096"),
 }
+PREFILL_METRIC = "Q4_K prefill dequant-GEMM TFLOP/s (% dense bf16 peak)"
+PREFILL = {
+    # name: (gguf type, legacy type, N rows, K, description); bf16 activations, M tokens
+    "prefill-4096": (12, 112, 4096, 4096, "Q4_K dequant-GEMM 4096x4096, bf16 x"),
+    "prefill-14336": (12, 112, 14336, 4096, "Q4_K dequant-GEMM 14336x4096, bf16 x"),
+}
 L2_BYTES = 126 * 1024 * 1024  # B200 L2
 
 
@@ -67,7 +73,7 @@ def parse():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=50)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS), default="q6k-gemv")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(PREFILL), default="q6k-gemv")
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a"], default="auto",
                    help="kernel family for the GEMV (auto: dp4a m<=4, mma m<=64, tcgen05 above)")
@@ -80,14 +86,14 @@ def algorithmic_bytes(qtype, n, k, m):
     return wbytes, wbytes + m * k * 4 + m * n * 4
 
 
-def peaks():
+def peaks(key="hbm_gbs", fallback=None):
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as fh:
             d = json.load(fh)
-        return float(d["hbm_gbs"]), "measured"
+        return float(d[key]), "measured"
     except Exception:
-        return FALLBACK_HBM_GBS, "fallback"
+        return (FALLBACK_HBM_GBS if fallback is None else fallback), "fallback"
 
 
 def profiled_traffic(workload, m):
@@ -184,7 +190,7 @@ class CpuReference:
         import oracle
         from pesti_b200 import synthetic
         self.oracle = oracle
-        self.qtype, self.legacy, self.n, self.k, _ = WORKLOADS[workload]
+        self.qtype, self.legacy, self.n, self.k, _ = {**WORKLOADS, **PREFILL}[workload]
         self.m = m
         self.data = synthetic.legacy_weight(self.legacy, self.n, self.k, seed=seed)
         self.x = synthetic.activations(m, self.k, seed=seed + 1)
@@ -219,8 +225,9 @@ def cpu_baseline(workload, m, budget_s=12.0):
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    qtype, _, n, k, desc = WORKLOADS[args.workload]
-    m = args.m
+    prefill = args.workload in PREFILL
+    qtype, _, n, k, desc = {**WORKLOADS, **PREFILL}[args.workload]
+    m = args.m if not prefill or args.m > 1 else 2048
     steps, warm = max(args.steps, 1), max(args.warmup, 0)
     ref = CpuReference(args.workload, m)
     # each step is a bounded sample of rows so the whole run stays ~2 minutes
@@ -236,17 +243,21 @@ def run_reference(args, rank, world):
         tt += dt
         tb += alg
     value = tb / tt / 1e9
+    unit, metric = "GB/s", METRIC
+    if prefill:  # the same sampled work counted in FLOPs
+        value = steps * 2.0 * m * rows * k / tt / 1e12
+        unit, metric = "TFLOP/s", PREFILL_METRIC
     cores = min(m, os.cpu_count() or 1)
-    line = {"metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world, "steps": steps,
+    line = {"metric": metric, "value": round(value, 6), "unit": unit, "n_gpus": world, "steps": steps,
             "warmup": warm, "ms_per_step": round(tt / steps * 1e3, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": f"{args.workload}: {desc}, M={m}, {rows} of {n} rows per step",
                        "parallelism": "cpu"},
-            "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": round(value, 6), "unit": unit, "cores": cores, "kind": "port",
                              "sample": f"{rows} of {n} rows per step of QuantizedLinear::forward restated "
                                        f"(oracle/kq_oracle.c) in the reference's block layout"},
-            "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": round(value, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -410,6 +421,129 @@ def run_ours(args, rank, world, local_rank):
     return 0
 
 
+def run_prefill(args, rank, world, local_rank):
+    """Prefill dequant-GEMM: y[M][N] = x_bf16[M][K] . W_q4k[N][K] on tcgen05."""
+    import torch
+    import torch.distributed as dist
+    from pesti_b200 import kq, synthetic
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    qtype, _, n, k, desc = PREFILL[args.workload]
+    m = args.m if args.m > 1 else 2048
+    flops = 2.0 * m * n * k
+    wbytes = n * (k // 256) * 144
+    xbytes = m * k * 2
+    nw = max(4, -(-3 * L2_BYTES // (wbytes + xbytes)))
+    ctx = kq.Context(local_rank)
+    weights = [kq.Weight(ctx, qtype, synthetic.gguf_weight(qtype, n, k, seed=1000 * rank + i), n, k)
+               for i in range(nw)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7 + rank)
+    xs = [torch.randn((m, k), generator=gen, device=dev).to(torch.bfloat16) for _ in range(nw)]
+    ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _ in range(nw)]
+    ctx.reserve(weights[0], m)
+    stream = torch.cuda.Stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+
+    def step():
+        for w, x, y in zip(weights, xs, ys):
+            w.linear_bf16(x, m, y, device_ptrs=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            step()
+    stream.synchronize()
+    ctx.profile_begin(nw)
+    bracketed = torch.cuda.CUDAGraph()
+    launches0 = ctx.launch_count
+    with torch.cuda.graph(bracketed, stream=stream):
+        step()
+    launches_per_step = ctx.launch_count - launches0
+    plain = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(plain, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            plain.replay()
+            bracketed.replay()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local_rank)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            plain.replay()
+        stop.record(stream)
+    stop.synchronize()
+    clocks.stop()
+    ms_total = start.elapsed_time(stop)
+    kernel_ms, kernel_n = 0.0, 0
+    for _ in range(max(1, min(args.steps, 20))):
+        with torch.cuda.stream(stream):
+            bracketed.replay()
+        ms, cnt = ctx.profile_read()
+        kernel_ms += ms
+        kernel_n += cnt
+    ctx.profile_end()
+    t = torch.tensor([ms_total, kernel_ms / max(kernel_n, 1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t[0]) / args.steps
+    kernel_us = float(t[1]) * 1e3
+    value = world * nw * flops / (ms_per_step * 1e-3) / 1e12
+
+    # e2e: host bf16 x and host y through the C ABI (copies inside the timed region)
+    ctx.set_stream(None)
+    xh = xs[0].cpu().view(torch.int16).numpy().view(np.uint16)
+    yh = np.empty((m, n), np.float32)
+    e2e_steps = max(1, min(args.steps, 10))
+    weights[0].linear_bf16(xh, m, yh)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        weights[0].linear_bf16(xh, m, yh)
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * flops * e2e_steps / float(te[0]) / 1e12
+
+    if rank == 0:
+        peak, peak_kind = peaks("bf16_tflops", 1590.0)
+        achieved = flops / (kernel_us * 1e-6) / 1e12
+        line = {
+            "metric": PREFILL_METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random GGUF Q4_K superblocks, x ~ N(0,1) in bf16)",
+            "config": {"workload": f"{args.workload}: {desc}, M={m}, {nw} distinct weights and inputs per step",
+                       "rows": n, "k": k, "m": m, "flops_per_gemm": flops,
+                       "l2": f"inputs larger than L2 ({nw * (wbytes + xbytes) / 1e6:.0f} MB per step)",
+                       "parallelism": f"replicas x{world}"},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} (cuBLAS bf16 burst)",
+                         "kernel": "tcgen05 dequant-GEMM kernel: CUDA events around each launch",
+                         "kernel_us": round(kernel_us, 3), "traffic": None},
+            "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": m * k * 2,
+                    "d2h_bytes_per_step": m * n * 4,
+                    "api": "kq_linear_bf16 with host pointers, synchronous per call"},
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del plain, bracketed
+    for w in weights:
+        w.free()
+    ctx.close()
+    return 0
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -426,6 +560,8 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.workload in PREFILL:
+            return run_prefill(args, rank, world, local_rank)
         return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
