@@ -63,6 +63,7 @@ enum kq_type {
 
 typedef struct kq_ctx kq_ctx;
 typedef struct kq_weight kq_weight;
+typedef struct kq_tp kq_tp;
 
 /* ---- context ------------------------------------------------------------ */
 /* New context on `device` with its own non-blocking stream.
@@ -139,6 +140,30 @@ int kq_linear_f32_static(kq_ctx *ctx, const kq_weight *w, const float *x, int64_
  * dequantize_full_row_range, quantized_linear.rs:146-183, for legacy types). */
 int kq_dequant_f32(kq_ctx *ctx, const kq_weight *w, int64_t row0, int64_t nrows,
                    float *out, int flags);
+
+/* ---- tensor parallel (one process per GPU of one node) ------------------- */
+/* Row-sharded linears whose output slices are all-gathered over NVLink: each
+ * rank stores its rows straight into every rank's exchange buffer (CUDA IPC
+ * peer memory) and publishes a per-call epoch; each rank waits for all of them
+ * and copies the full output out.  Replaces the survey's NCCL all-gather
+ * policy (kq_tp_init with an NCCL id); no counterpart in the reference, which
+ * is single-process CPU code.  Setup: kq_tp_create on every rank, exchange
+ * the kq_tp_handle blobs (any host channel), kq_tp_open with all of them in
+ * rank order.  max_out_elems bounds m * out_features of any call. */
+int kq_tp_create(kq_ctx *ctx, int world, int rank, int64_t max_out_elems, kq_tp **out);
+/* This rank's handle blob; with out == NULL only writes its size. */
+int kq_tp_handle(const kq_tp *tp, void *out, size_t *size);
+int kq_tp_open(kq_tp *tp, const void *handles, size_t nbytes);
+/* y[m][n_total] = x[m][in] . W^T for a weight whose rows [row0, row0 +
+ * out_features(shard)) this rank holds as `shard`; every rank of the group
+ * must make the same sequence of calls.  Device pointers only (flags must hold
+ * KQ_DEVICE_PTRS); bias is the shard's slice. */
+int kq_tp_linear_f32(kq_tp *tp, const kq_weight *shard, int64_t row0, int64_t n_total,
+                     const float *x, int64_t m, const float *bias, float *y, int flags);
+/* The all-gather alone: y_local holds rows [row0, row0 + rows) of y[m][n_total]. */
+int kq_tp_allgather_f32(kq_tp *tp, const float *y_local, int64_t m, int64_t row0, int64_t rows,
+                        int64_t n_total, float *y, int flags);
+int kq_tp_destroy(kq_tp *tp);
 
 #ifdef __cplusplus
 }

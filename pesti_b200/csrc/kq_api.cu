@@ -50,6 +50,21 @@ struct kq_ctx {
   }
 };
 
+// A tensor-parallel group member: this rank's exchange buffer (two image
+// slots of max_elems floats, then one 32-bit flag per source rank), its
+// block buffer, and the peers' exchange buffers mapped over CUDA IPC.
+struct kq_tp {
+  kq_ctx* ctx = nullptr;
+  int world = 0, rank = 0;
+  int64_t max_elems = 0;
+  void* exch = nullptr;
+  float* ylocal = nullptr;
+  unsigned* ctr = nullptr;
+  void* peer_base[kq::TP_MAX_WORLD] = {};
+  bool opened = false;
+  unsigned epoch = 0;
+};
+
 struct kq_weight {
   int device = 0;
   kq::DevWeight dw{};
@@ -134,8 +149,8 @@ int64_t legacy_tile_bytes(int t, int64_t k) {
 
 int check_ctx(kq_ctx* ctx) { return ctx ? KQ_OK : KQ_ERR_INVALID_ARG; }
 
-// After the stream is synchronised: report (and clear) a tensor-core pipeline
-// timeout.  The split-K counters may then be stale, so they are cleared too.
+// After the stream is synchronised: report (and clear) a device-side wait
+// that gave up.  The split-K counters may then be stale, so they are cleared too.
 int check_device_error(kq_ctx* ctx) {
   const int code = *reinterpret_cast<volatile int*>(ctx->host_err);
   if (code == 0) return KQ_OK;
@@ -144,7 +159,9 @@ int check_device_error(kq_ctx* ctx) {
   if (ctx->ctr) cudaMemset(ctx->ctr, 0, ctx->ctr_bytes);
   cudaDeviceSynchronize();
   cudaGetLastError();
-  return fail(ctx, KQ_ERR_CUDA, "tensor-core pipeline wait gave up (code %d); the call's output is invalid",
+  return fail(ctx, KQ_ERR_CUDA,
+              "a device-side wait gave up (code %d: 1-5 tcgen05 pipeline, 21-23 decode weight ring, 31 "
+              "tensor-parallel peer flag); the call's output is invalid",
               code);
 }
 
@@ -607,6 +624,149 @@ int kq_linear_f32_static(kq_ctx* ctx, const kq_weight* w, const float* x, int64_
   ctx->launches += launches;
   if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");
   if (flags & KQ_SYNC) return finish_sync(ctx, "linear");
+  return KQ_OK;
+}
+
+// ---- tensor parallel --------------------------------------------------------------
+
+static size_t tp_flags_offset(int64_t max_elems) { return ((size_t)2 * (size_t)max_elems * 4 + 255) & ~size_t(255); }
+
+int kq_tp_create(kq_ctx* ctx, int world, int rank, int64_t max_out_elems, kq_tp** out) {
+  if (check_ctx(ctx) || !out) return KQ_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (world < 1 || world > kq::TP_MAX_WORLD || rank < 0 || rank >= world)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "world %d / rank %d (world must be 1..%d)", world, rank, kq::TP_MAX_WORLD);
+  if (max_out_elems < 1 || max_out_elems > ((int64_t)1 << 31))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "max_out_elems %lld", (long long)max_out_elems);
+  DeviceGuard g(ctx->device);
+  if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
+  kq_tp* tp = new kq_tp;
+  tp->ctx = ctx;
+  tp->world = world;
+  tp->rank = rank;
+  tp->max_elems = max_out_elems;
+  const size_t xbytes = tp_flags_offset(max_out_elems) + 256;
+  cudaError_t e = cudaMalloc(&tp->exch, xbytes);
+  if (e == cudaSuccess) e = cudaMemset(tp->exch, 0, xbytes);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&tp->ylocal), (size_t)max_out_elems * 4);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&tp->ctr), 256);
+  if (e == cudaSuccess) e = cudaMemset(tp->ctr, 0, 256);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    kq_tp_destroy(tp);
+    return cuda_fail(ctx, e, "allocate the tensor-parallel exchange buffer");
+  }
+  tp->peer_base[rank] = tp->exch;
+  *out = tp;
+  return KQ_OK;
+}
+
+int kq_tp_handle(const kq_tp* tp, void* out, size_t* size) {
+  if (!tp || !size) return KQ_ERR_INVALID_ARG;
+  const size_t need = sizeof(cudaIpcMemHandle_t);
+  if (!out) {
+    *size = need;
+    return KQ_OK;
+  }
+  if (*size < need) return fail(tp->ctx, KQ_ERR_SHORT_BUFFER, "handle needs %zu bytes", need);
+  DeviceGuard g(tp->ctx->device);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, tp->exch);
+  if (e != cudaSuccess) return cuda_fail(tp->ctx, e, "cudaIpcGetMemHandle");
+  std::memcpy(out, &h, need);
+  *size = need;
+  return KQ_OK;
+}
+
+int kq_tp_open(kq_tp* tp, const void* handles, size_t nbytes) {
+  if (!tp || !handles) return KQ_ERR_INVALID_ARG;
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  if (nbytes < hb * (size_t)tp->world)
+    return fail(tp->ctx, KQ_ERR_SHORT_BUFFER, "need %d handles of %zu bytes", tp->world, hb);
+  if (tp->opened) return fail(tp->ctx, KQ_ERR_STATE, "peers are already open");
+  DeviceGuard g(tp->ctx->device);
+  for (int r = 0; r < tp->world; ++r) {
+    if (r == tp->rank) continue;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(handles) + hb * r, hb);
+    void* p = nullptr;
+    cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(tp->ctx, e, "cudaIpcOpenMemHandle (is the peer on another GPU of this node?)");
+    tp->peer_base[r] = p;
+  }
+  tp->opened = true;
+  return KQ_OK;
+}
+
+int kq_tp_allgather_f32(kq_tp* tp, const float* y_local, int64_t m, int64_t row0, int64_t rows, int64_t n_total,
+                        float* y, int flags) {
+  if (!tp) return KQ_ERR_INVALID_ARG;
+  kq_ctx* ctx = tp->ctx;
+  if (!tp->opened) return fail(ctx, KQ_ERR_STATE, "kq_tp_open has not been called");
+  if (!(flags & KQ_DEVICE_PTRS)) return fail(ctx, KQ_ERR_INVALID_ARG, "tensor-parallel calls take device pointers");
+  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
+  if (m < 1 || rows < 0 || row0 < 0 || row0 + rows > n_total || n_total < 1 || !y || (rows > 0 && !y_local))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "bad all-gather shape");
+  if (m * n_total > tp->max_elems)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "m x n = %lld exceeds the exchange buffer (%lld floats)",
+                (long long)(m * n_total), (long long)tp->max_elems);
+  DeviceGuard g(ctx->device);
+  kq::TpArgs a{};
+  a.y_local = y_local;
+  a.y_out = y;
+  a.m = m;
+  a.n = n_total;
+  a.r0 = row0;
+  a.r1 = row0 + rows;
+  a.world = tp->world;
+  a.rank = tp->rank;
+  a.epoch = ++tp->epoch;
+  const size_t slot = (size_t)(a.epoch & 1u) * (size_t)tp->max_elems;
+  const size_t foff = tp_flags_offset(tp->max_elems);
+  for (int p = 0; p < tp->world; ++p) {
+    a.peer_slot[p] = static_cast<float*>(tp->peer_base[p]) + slot;
+    a.peer_flags[p] = reinterpret_cast<unsigned*>(static_cast<char*>(tp->peer_base[p]) + foff);
+  }
+  a.local_slot = static_cast<const float*>(tp->exch) + slot;
+  a.local_flags = reinterpret_cast<const unsigned*>(static_cast<char*>(tp->exch) + foff);
+  a.ctr = tp->ctr;
+  a.err = ctx->dev_err;
+  const int64_t work = m * n_total;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ctx->num_sms, (work + 4095) / 4096));
+  cudaError_t e = kq::launch_tp_allgather(a, blocks, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "all-gather launch");
+  ctx->launches += 1;
+  if (flags & KQ_SYNC) return finish_sync(ctx, "all-gather");
+  return KQ_OK;
+}
+
+int kq_tp_linear_f32(kq_tp* tp, const kq_weight* shard, int64_t row0, int64_t n_total, const float* x, int64_t m,
+                     const float* bias, float* y, int flags) {
+  if (!tp || !shard) return KQ_ERR_INVALID_ARG;
+  kq_ctx* ctx = tp->ctx;
+  if (!(flags & KQ_DEVICE_PTRS)) return fail(ctx, KQ_ERR_INVALID_ARG, "tensor-parallel calls take device pointers");
+  if (row0 < 0 || row0 + shard->dw.n > n_total)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "shard rows [%lld, %lld) outside the %lld-row weight", (long long)row0,
+                (long long)(row0 + shard->dw.n), (long long)n_total);
+  if (m < 1 || m * n_total > tp->max_elems)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "m x n = %lld exceeds the exchange buffer (%lld floats)",
+                (long long)(m * n_total), (long long)tp->max_elems);
+  int rc = kq_linear_f32(ctx, shard, x, m, bias, tp->ylocal, KQ_DEVICE_PTRS);
+  if (rc) return rc;
+  return kq_tp_allgather_f32(tp, tp->ylocal, m, row0, shard->dw.n, n_total, y, flags);
+}
+
+int kq_tp_destroy(kq_tp* tp) {
+  if (!tp) return KQ_ERR_INVALID_ARG;
+  DeviceGuard g(tp->ctx->device);
+  cudaDeviceSynchronize();
+  for (int r = 0; r < tp->world; ++r)
+    if (r != tp->rank && tp->peer_base[r]) cudaIpcCloseMemHandle(tp->peer_base[r]);
+  if (tp->exch) cudaFree(tp->exch);
+  if (tp->ylocal) cudaFree(tp->ylocal);
+  if (tp->ctr) cudaFree(tp->ctr);
+  cudaGetLastError();
+  delete tp;
   return KQ_OK;
 }
 

@@ -102,6 +102,24 @@ cudaError_t launch_gemv_dp4a(const DevWeight& w, const float* x, int64_t m, cons
                              void* ws, int num_sms, int* err, cudaStream_t s, int* launches,
                              Bracket br = Bracket());
 
+// ---- tensor parallel: all-gather of row-sharded outputs over peer memory (kq_tp.cu) ----
+constexpr int TP_MAX_WORLD = 8;
+struct TpArgs {
+  const float* y_local;                  // [m][r1 - r0] this rank's block
+  float* y_out;                          // [m][n] the gathered result
+  int64_t m, n, r0, r1;                  // tokens, total rows, this rank's rows
+  float* peer_slot[TP_MAX_WORLD];        // every rank's image slot of this epoch ([m][n])
+  unsigned* peer_flags[TP_MAX_WORLD];    // every rank's flag array (one per source rank)
+  const float* local_slot;               // this rank's image slot of this epoch
+  const unsigned* local_flags;           // this rank's flag array
+  int world, rank;
+  unsigned epoch;                        // 1, 2, 3, ... per call
+  unsigned* ctr;                         // zero between calls (last-CTA detection)
+  int* err;                              // set to a nonzero code if a wait gave up
+};
+// One launch per call; `blocks` must fit the GPU at once (<= SM count).
+cudaError_t launch_tp_allgather(const TpArgs& a, int blocks, cudaStream_t s);
+
 // ---- tensor-core (tcgen05) path: kq_mma.cu ----
 // Build the TMA descriptors of a GGUF weight (after its device arrays exist).
 bool tc_make_weight_maps(DevWeight& w);

@@ -57,6 +57,8 @@ EXPORTED_SYMBOLS = (
     "kq_ctx_set_path", "kq_ctx_reserve", "kq_ctx_launch_count", "kq_ctx_profile_begin",
     "kq_ctx_profile_end", "kq_ctx_profile_read", "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
     "kq_linear_f32", "kq_linear_bf16", "kq_linear_f32_static", "kq_dequant_f32",
+    "kq_tp_create", "kq_tp_handle", "kq_tp_open", "kq_tp_linear_f32", "kq_tp_allgather_f32",
+    "kq_tp_destroy",
 )
 
 
@@ -111,6 +113,12 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
             "kq_linear_bf16": ([P, P, P, I64, P, P, I], I),
             "kq_linear_f32_static": ([P, P, P, I64, P, P, I], I),
             "kq_dequant_f32": ([P, P, I64, I64, P, I], I),
+            "kq_tp_create": ([P, I, I, I64, PP], I),
+            "kq_tp_handle": ([P, P, ctypes.POINTER(Z)], I),
+            "kq_tp_open": ([P, P, Z], I),
+            "kq_tp_linear_f32": ([P, P, I64, I64, P, I64, P, P, I], I),
+            "kq_tp_allgather_f32": ([P, P, I64, I64, I64, I64, P, I], I),
+            "kq_tp_destroy": ([P], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(lib, name)
@@ -272,6 +280,65 @@ class Weight:
     def __del__(self):
         try:
             self.free()
+        except Exception:
+            pass
+
+
+def shard_rows(n: int, world: int, rank: int):
+    """Contiguous, balanced row block [r0, r1) of an n-row weight for `rank`."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError(f"rank {rank} of world {world}")
+    return n * rank // world, n * (rank + 1) // world
+
+
+def torch_exchange(blob: bytes, group=None):
+    """All ranks' blobs in rank order, over torch.distributed (any backend)."""
+    import torch.distributed as dist
+    out = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, blob, group=group)
+    return out
+
+
+class TensorParallel:
+    """One rank of a row-sharded linear group (kq_tp_*): each rank holds rows
+    [r0, r1) of a weight; ``linear`` returns the full output on every rank,
+    all-gathered over NVLink peer memory.  ``exchange(blob) -> [blob per rank]``
+    moves the IPC handles between ranks (torch.distributed by default)."""
+
+    def __init__(self, ctx: "Context", world: int, rank: int, max_out_elems: int, exchange=None):
+        self.ctx, self.world, self.rank = ctx, world, rank
+        h = ctypes.c_void_p()
+        ctx.check(ctx.lib.kq_tp_create(ctx.handle, world, rank, max_out_elems, ctypes.byref(h)), "kq_tp_create")
+        self.handle = h
+        size = ctypes.c_size_t(0)
+        ctx.check(ctx.lib.kq_tp_handle(self.handle, None, ctypes.byref(size)), "kq_tp_handle")
+        buf = ctypes.create_string_buffer(size.value)
+        ctx.check(ctx.lib.kq_tp_handle(self.handle, buf, ctypes.byref(size)), "kq_tp_handle")
+        blobs = (exchange or torch_exchange)(buf.raw[:size.value])
+        if len(blobs) != world or any(len(b) != size.value for b in blobs):
+            raise KqError(KQ_ERR_INVALID_ARG, "handle exchange returned the wrong blobs")
+        joined = b"".join(blobs)
+        ctx.check(ctx.lib.kq_tp_open(self.handle, joined, len(joined)), "kq_tp_open")
+
+    def linear(self, shard: "Weight", row0: int, n_total: int, x, m: int, y, bias=None, sync: bool = False):
+        flags = KQ_DEVICE_PTRS | (KQ_SYNC if sync else 0)
+        rc = self.ctx.lib.kq_tp_linear_f32(self.handle, shard.handle, row0, n_total, _ptr(x), m, _ptr(bias),
+                                           _ptr(y), flags)
+        self.ctx.check(rc, "kq_tp_linear_f32")
+
+    def allgather(self, y_local, m: int, row0: int, rows: int, n_total: int, y, sync: bool = False):
+        flags = KQ_DEVICE_PTRS | (KQ_SYNC if sync else 0)
+        rc = self.ctx.lib.kq_tp_allgather_f32(self.handle, _ptr(y_local), m, row0, rows, n_total, _ptr(y), flags)
+        self.ctx.check(rc, "kq_tp_allgather_f32")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            self.ctx.lib.kq_tp_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
         except Exception:
             pass
 
