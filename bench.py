@@ -57,6 +57,12 @@ PREFILL = {
     "prefill-4096": (12, 112, 4096, 4096, "Q4_K dequant-GEMM 4096x4096, bf16 x"),
     "prefill-14336": (12, 112, 14336, 4096, "Q4_K dequant-GEMM 14336x4096, bf16 x"),
 }
+DECODE_METRIC = METRIC
+DECODERS = {
+    # name: (config name in pesti_b200.decoder, context length)
+    "decode-llama8b": ("LLAMA3_8B", 2048),
+    "decode-qwen05b": ("QWEN25_05B", 512),
+}
 L2_BYTES = 126 * 1024 * 1024  # B200 L2
 
 
@@ -73,7 +79,8 @@ def parse():
     p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=50)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(PREFILL), default="q6k-gemv")
+    p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(PREFILL) + sorted(DECODERS),
+                   default="q6k-gemv")
     p.add_argument("--m", type=int, default=1)
     p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a"], default="auto",
                    help="kernel family for the GEMV (auto: dp4a m<=4, mma m<=64, tcgen05 above)")
@@ -224,6 +231,21 @@ def cpu_baseline(workload, m, budget_s=12.0):
 
 def run_reference(args, rank, world):
     if rank != 0:
+        return 0
+    if args.workload in DECODERS:
+        from pesti_b200 import decoder as dec
+        cfg_name, ctx_len = DECODERS[args.workload]
+        cfg = getattr(dec, cfg_name)
+        base = cpu_decode_sample(cfg)
+        print(json.dumps({"metric": DECODE_METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": world,
+                          "steps": 1, "warmup": 0, "ms_per_step": round(1e3 / base["value"], 3),
+                          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+                          "data": "synthetic", "impl": "reference",
+                          "config": {"workload": f"{args.workload}: {cfg.name} decode, batch 1, context {ctx_len}",
+                                     "parallelism": "cpu"},
+                          "cpu_baseline": base,
+                          "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
         return 0
     prefill = args.workload in PREFILL
     qtype, _, n, k, desc = {**WORKLOADS, **PREFILL}[args.workload]
@@ -544,6 +566,157 @@ def run_prefill(args, rank, world, local_rank):
     return 0
 
 
+def cpu_decode_sample(cfg, budget_s=12.0):
+    """The reference's CPU decode of this model shape, timed on a sample: the
+    seven QuantizedLinear::forward calls of one layer (full f32 dequant +
+    sequential dot, restated in oracle/kq_oracle.c, legacy block layout) on
+    bounded row counts, scaled to a whole token (layers x per-layer time +
+    head).  Attention and norms are omitted (under 1% of the CPU time)."""
+    import oracle
+    from pesti_b200 import synthetic
+    D, F, hd = cfg.dim, cfg.ffn, cfg.head_dim
+    Dp = -(-D // 256) * 256
+    shapes = [(cfg.heads * hd, Dp), (cfg.kv_heads * hd, Dp), (cfg.kv_heads * hd, Dp), (D, Dp), (F, Dp), (F, Dp), (D, F)]
+    per_layer = 0.0
+    used = 0.0
+    for n, k in shapes:
+        rows = max(16, min(n, 64))
+        data = synthetic.legacy_weight(112, rows, k, seed=1)
+        x = synthetic.activations(1, k, seed=2)
+        t0 = time.perf_counter()
+        oracle.legacy_forward(112, data, k, rows, x, 1, nthreads=1, threads_over_batch=True)
+        dt = time.perf_counter() - t0
+        used += dt
+        per_layer += dt * n / rows
+    rows = 64
+    data = synthetic.legacy_weight(112, rows, Dp, seed=3)
+    x = synthetic.activations(1, Dp, seed=4)
+    t0 = time.perf_counter()
+    oracle.legacy_forward(112, data, Dp, rows, x, 1, nthreads=1, threads_over_batch=True)
+    head = (time.perf_counter() - t0) * cfg.vocab / rows
+    sec_per_token = cfg.layers * per_layer + head
+    return {"value": round(1.0 / sec_per_token, 6), "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": f"QuantizedLinear::forward (oracle/kq_oracle.c, legacy blocks) on <=64 rows of each of the "
+                      f"7 per-layer projections and the head of {cfg.name}, scaled to {cfg.layers} layers; "
+                      f"batch 1, one core (the reference threads over batch rows only)",
+            "host_cpus": os.cpu_count()}
+
+
+def run_decoder(args, rank, world, local_rank):
+    """Decode throughput of a synthetic decoder (one step = one token for each
+    of `--m` sequences at the context length), tensor-parallel over the ranks."""
+    import torch
+    import torch.distributed as dist
+    from pesti_b200 import decoder as dec, kq
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg_name, ctx_len = DECODERS[args.workload]
+    cfg = getattr(dec, cfg_name)
+    B = args.m
+    ctx = kq.Context(local_rank)
+    tp = None
+    if world > 1:
+        tp = kq.TensorParallel(ctx, world, rank, max_out_elems=B * max(cfg.vocab, cfg.ffn, cfg.dim))
+    model = dec.Decoder(cfg, ctx, B, ctx_len, max_new=2, world=world, rank=rank, tp=tp, seed=11)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    model.tokens.copy_(torch.randint(0, cfg.vocab, (B,), generator=gen, device=dev, dtype=torch.int32))
+    stream = torch.cuda.Stream(dev)
+    ctx.set_stream(stream.cuda_stream)
+    pos = ctx_len
+    with torch.cuda.stream(stream):
+        model.step(pos)
+    stream.synchronize()
+    launches0 = ctx.launch_count
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        model.step(pos)
+    launches_per_step = ctx.launch_count - launches0
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+    stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local_rank)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.start()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record(stream)
+    stop.synchronize()
+    clocks.stop()
+    t = torch.tensor([start.elapsed_time(stop)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t[0]) / args.steps
+    value = B / (ms_per_step * 1e-3)  # tokens per second for the whole group
+
+    # e2e: token ids in from pinned host memory, logits out, per step
+    tok_h = torch.empty(B, dtype=torch.int32).pin_memory()
+    tok_h.copy_(model.tokens.cpu())
+    logits_h = torch.empty((B, cfg.vocab), dtype=torch.float32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 50))
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(stream):
+            model.tokens.copy_(tok_h, non_blocking=True)
+            graph.replay()
+            logits_h.copy_(model.logits, non_blocking=True)
+        stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = B * e2e_steps / float(te[0])
+
+    wb = torch.tensor([float(model.weight_bytes()), float(model.kv_bytes(pos))], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(wb)
+    step_bytes = float(wb[0] + wb[1])
+    if rank == 0:
+        peak, peak_kind = peaks()
+        achieved = step_bytes / (ms_per_step * 1e-3) / 1e9
+        line = {
+            "metric": DECODE_METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (random GGUF K-quant weights, random f16 KV cache, random token ids)",
+            "config": {"workload": f"{args.workload}: {cfg.name} decode, batch {B}, context {ctx_len}",
+                       "layers": cfg.layers, "dim": cfg.dim, "heads": cfg.heads, "kv_heads": cfg.kv_heads,
+                       "head_dim": cfg.head_dim, "ffn": cfg.ffn, "vocab": cfg.vocab, "batch": B,
+                       "context": ctx_len, "weight_bytes": int(wb[0]), "kv_bytes_per_step": int(wb[1]),
+                       "l2": "inputs larger than L2 (every step streams all weights and the KV cache)",
+                       "parallelism": (f"tensor parallel x{world}: heads, KV cache and row blocks sharded, "
+                                       f"4 all-gathers per layer over NVLink peer memory") if world > 1
+                       else "single GPU"},
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak * world, "unit": "GB/s",
+                         "frac": round(achieved / (peak * world), 4),
+                         "peak_source": f"{peak_kind} (hbm copy) x {world} GPUs",
+                         "kernel": "whole decode step (graph replay): weight + KV bytes / step time",
+                         "kernel_us": round(ms_per_step * 1e3, 3), "traffic": None},
+            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": B * 4,
+                    "d2h_bytes_per_step": B * cfg.vocab * 4,
+                    "api": "graph replay with token ids copied in and logits copied out per step"},
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_decode_sample(cfg)
+        print(json.dumps(line), flush=True)
+    del graph
+    model.close()
+    if tp is not None:
+        tp.close()
+    ctx.close()
+    return 0
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -562,6 +735,8 @@ def main():
     try:
         if args.workload in PREFILL:
             return run_prefill(args, rank, world, local_rank)
+        if args.workload in DECODERS:
+            return run_decoder(args, rank, world, local_rank)
         return run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -53,6 +53,7 @@ enum kq_type {
 #define KQ_HOST_PTRS 0   /* x / bias / y are host pointers (synchronous)  */
 #define KQ_DEVICE_PTRS 1 /* x / bias / y are device pointers (async)      */
 #define KQ_SYNC 2        /* synchronise the context stream before return  */
+#define KQ_ACCUMULATE 4  /* kq_tp_allgather_f32: add into y instead of overwrite */
 
 /* kernel families for GGUF weights with f32 activations (kq_ctx_set_path) */
 #define KQ_PATH_AUTO 0    /* default: DP4A m <= 4, MMA m <= 64, else TCGEN05 */
@@ -106,7 +107,8 @@ int kq_row_bytes(int kq_type, int64_t in_features, int64_t *out);
 /* Upload a row-major [out_features][row bytes] weight and keep it resident on
  * the context's device (QuantizedLinear::new / from_quantized,
  * quantized_linear.rs:27-67, with the bytes moved to HBM once).  `nbytes` must
- * cover every row (legacy: the last row only needs the bytes its tile reads). */
+ * cover every row (legacy: the last row only needs the bytes its tile reads).
+ * `bytes` may be host memory or device memory of any GPU CUDA can address. */
 int kq_weight_upload(kq_ctx *ctx, int kq_type, const void *bytes, size_t nbytes,
                      int64_t out_features, int64_t in_features, kq_weight **out);
 int kq_weight_free(kq_weight *w);
@@ -160,9 +162,11 @@ int kq_tp_open(kq_tp *tp, const void *handles, size_t nbytes);
  * KQ_DEVICE_PTRS); bias is the shard's slice. */
 int kq_tp_linear_f32(kq_tp *tp, const kq_weight *shard, int64_t row0, int64_t n_total,
                      const float *x, int64_t m, const float *bias, float *y, int flags);
-/* The all-gather alone: y_local holds rows [row0, row0 + rows) of y[m][n_total]. */
+/* The all-gather alone: y_local holds columns [row0, row0 + rows) of
+ * y[m][n_total]; y's rows are y_ld floats apart (>= n_total).  With
+ * KQ_ACCUMULATE in flags the gathered values are added to y (a residual). */
 int kq_tp_allgather_f32(kq_tp *tp, const float *y_local, int64_t m, int64_t row0, int64_t rows,
-                        int64_t n_total, float *y, int flags);
+                        int64_t n_total, float *y, int64_t y_ld, int flags);
 int kq_tp_destroy(kq_tp *tp);
 
 #ifdef __cplusplus

@@ -11,6 +11,7 @@
 #include <string>
 #include <vector>
 
+#include "../../include/pesti_decoder.h"
 #include "../../include/pesti_kq.h"
 #include "kq_kernels.h"
 
@@ -62,7 +63,6 @@ struct kq_tp {
   unsigned* ctr = nullptr;
   void* peer_base[kq::TP_MAX_WORLD] = {};
   bool opened = false;
-  unsigned epoch = 0;
 };
 
 struct kq_weight {
@@ -436,7 +436,7 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
     if (e == cudaSuccess) e = cudaMalloc(&w->d_alloc, (size_t)n * dld * 2 + pad);
     if (e == cudaSuccess) e = cudaMemsetAsync(w->d_alloc, 0, (size_t)n * dld * 2 + pad, ctx->stream);
     if (e == cudaSuccess && nsb)
-      e = cudaMemcpyAsync(raw, bytes, (size_t)nsb * kq::Q6K_BYTES, cudaMemcpyHostToDevice, ctx->stream);
+      e = cudaMemcpyAsync(raw, bytes, (size_t)nsb * kq::Q6K_BYTES, cudaMemcpyDefault, ctx->stream);
     if (e == cudaSuccess)
       e = kq::launch_q6k_relayout(static_cast<const uint8_t*>(raw), n, w->dw.sb, static_cast<uint8_t*>(w->q_alloc),
                                   static_cast<uint16_t*>(w->d_alloc), ctx->stream);
@@ -451,7 +451,7 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
     e = cudaMalloc(&w->q_alloc, (size_t)need + pad);
     if (e == cudaSuccess) e = cudaMemsetAsync(w->q_alloc, 0, (size_t)need + pad, ctx->stream);
     if (e == cudaSuccess && need)
-      e = cudaMemcpyAsync(w->q_alloc, bytes, (size_t)need, cudaMemcpyHostToDevice, ctx->stream);
+      e = cudaMemcpyAsync(w->q_alloc, bytes, (size_t)need, cudaMemcpyDefault, ctx->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     w->device_bytes = need;
     w->dw.len = need;
@@ -649,7 +649,7 @@ int kq_tp_create(kq_ctx* ctx, int world, int rank, int64_t max_out_elems, kq_tp*
   cudaError_t e = cudaMalloc(&tp->exch, xbytes);
   if (e == cudaSuccess) e = cudaMemset(tp->exch, 0, xbytes);
   if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&tp->ylocal), (size_t)max_out_elems * 4);
-  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&tp->ctr), 256);
+  if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&tp->ctr), 256);  // [0] CTA counter, [1] epoch
   if (e == cudaSuccess) e = cudaMemset(tp->ctr, 0, 256);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
@@ -699,13 +699,15 @@ int kq_tp_open(kq_tp* tp, const void* handles, size_t nbytes) {
 }
 
 int kq_tp_allgather_f32(kq_tp* tp, const float* y_local, int64_t m, int64_t row0, int64_t rows, int64_t n_total,
-                        float* y, int flags) {
+                        float* y, int64_t y_ld, int flags) {
   if (!tp) return KQ_ERR_INVALID_ARG;
   kq_ctx* ctx = tp->ctx;
   if (!tp->opened) return fail(ctx, KQ_ERR_STATE, "kq_tp_open has not been called");
   if (!(flags & KQ_DEVICE_PTRS)) return fail(ctx, KQ_ERR_INVALID_ARG, "tensor-parallel calls take device pointers");
-  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
-  if (m < 1 || rows < 0 || row0 < 0 || row0 + rows > n_total || n_total < 1 || !y || (rows > 0 && !y_local))
+  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC | KQ_ACCUMULATE))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
+  if (m < 1 || rows < 0 || row0 < 0 || row0 + rows > n_total || n_total < 1 || !y || (rows > 0 && !y_local) ||
+      y_ld < n_total)
     return fail(ctx, KQ_ERR_INVALID_ARG, "bad all-gather shape");
   if (m * n_total > tp->max_elems)
     return fail(ctx, KQ_ERR_UNSUPPORTED, "m x n = %lld exceeds the exchange buffer (%lld floats)",
@@ -714,22 +716,19 @@ int kq_tp_allgather_f32(kq_tp* tp, const float* y_local, int64_t m, int64_t row0
   kq::TpArgs a{};
   a.y_local = y_local;
   a.y_out = y;
+  a.y_ld = y_ld;
+  a.accumulate = (flags & KQ_ACCUMULATE) ? 1 : 0;
   a.m = m;
   a.n = n_total;
   a.r0 = row0;
   a.r1 = row0 + rows;
   a.world = tp->world;
   a.rank = tp->rank;
-  a.epoch = ++tp->epoch;
-  const size_t slot = (size_t)(a.epoch & 1u) * (size_t)tp->max_elems;
-  const size_t foff = tp_flags_offset(tp->max_elems);
-  for (int p = 0; p < tp->world; ++p) {
-    a.peer_slot[p] = static_cast<float*>(tp->peer_base[p]) + slot;
-    a.peer_flags[p] = reinterpret_cast<unsigned*>(static_cast<char*>(tp->peer_base[p]) + foff);
-  }
-  a.local_slot = static_cast<const float*>(tp->exch) + slot;
-  a.local_flags = reinterpret_cast<const unsigned*>(static_cast<char*>(tp->exch) + foff);
+  for (int p = 0; p < tp->world; ++p) a.exch[p] = static_cast<float*>(tp->peer_base[p]);
+  a.max_elems = tp->max_elems;
+  a.flags_off = tp_flags_offset(tp->max_elems);
   a.ctr = tp->ctr;
+  a.epoch = tp->ctr + 1;
   a.err = ctx->dev_err;
   const int64_t work = m * n_total;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ctx->num_sms, (work + 4095) / 4096));
@@ -745,6 +744,7 @@ int kq_tp_linear_f32(kq_tp* tp, const kq_weight* shard, int64_t row0, int64_t n_
   if (!tp || !shard) return KQ_ERR_INVALID_ARG;
   kq_ctx* ctx = tp->ctx;
   if (!(flags & KQ_DEVICE_PTRS)) return fail(ctx, KQ_ERR_INVALID_ARG, "tensor-parallel calls take device pointers");
+  if (flags & KQ_ACCUMULATE) return fail(ctx, KQ_ERR_INVALID_ARG, "KQ_ACCUMULATE applies to kq_tp_allgather_f32");
   if (row0 < 0 || row0 + shard->dw.n > n_total)
     return fail(ctx, KQ_ERR_INVALID_ARG, "shard rows [%lld, %lld) outside the %lld-row weight", (long long)row0,
                 (long long)(row0 + shard->dw.n), (long long)n_total);
@@ -753,7 +753,7 @@ int kq_tp_linear_f32(kq_tp* tp, const kq_weight* shard, int64_t row0, int64_t n_
                 (long long)(m * n_total), (long long)tp->max_elems);
   int rc = kq_linear_f32(ctx, shard, x, m, bias, tp->ylocal, KQ_DEVICE_PTRS);
   if (rc) return rc;
-  return kq_tp_allgather_f32(tp, tp->ylocal, m, row0, shard->dw.n, n_total, y, flags);
+  return kq_tp_allgather_f32(tp, tp->ylocal, m, row0, shard->dw.n, n_total, y, n_total, flags);
 }
 
 int kq_tp_destroy(kq_tp* tp) {
@@ -768,6 +768,86 @@ int kq_tp_destroy(kq_tp* tp) {
   cudaGetLastError();
   delete tp;
   return KQ_OK;
+}
+
+// ---- decoder step kernels ----------------------------------------------------------
+
+static int dec_status(kq_ctx* ctx, cudaError_t e, const char* what) {
+  return e == cudaSuccess ? KQ_OK : cuda_fail(ctx, e, what);
+}
+
+int kq_dec_rmsnorm(kq_ctx* ctx, const float* x, int64_t x_ld, const float* w, float* out, int64_t out_ld,
+                   int64_t rows, int64_t dim, float eps) {
+  if (check_ctx(ctx) || !x || !w || !out || rows < 0 || dim < 0 || x_ld < dim || out_ld < dim)
+    return KQ_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  ctx->launches += rows > 0 && dim > 0;
+  return dec_status(ctx, kq::dec_rmsnorm(x, x_ld, w, out, out_ld, rows, dim, eps, ctx->stream), "rmsnorm");
+}
+
+int kq_dec_rope_append(kq_ctx* ctx, float* qkv, int64_t ld, void* k_cache, void* v_cache, int64_t batch, int heads,
+                       int kv_heads, int head_dim, int64_t pos, int64_t max_seq, float theta) {
+  if (check_ctx(ctx) || !qkv || !k_cache || !v_cache) return KQ_ERR_INVALID_ARG;
+  if (batch < 1 || heads < 1 || kv_heads < 1 || head_dim < 2 || head_dim % 2 || pos < 0 || pos >= max_seq ||
+      ld < (int64_t)(heads + 2 * kv_heads) * head_dim)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "rope: bad shape or position %lld of %lld", (long long)pos,
+                (long long)max_seq);
+  DeviceGuard g(ctx->device);
+  ctx->launches += 1;
+  return dec_status(
+      ctx, kq::dec_rope_append(qkv, ld, k_cache, v_cache, batch, heads, kv_heads, head_dim, pos, max_seq, theta,
+                               ctx->stream),
+      "rope");
+}
+
+size_t kq_dec_attention_scratch(kq_ctx* ctx, int64_t batch, int heads, int kv_heads, int head_dim, int64_t len) {
+  if (!ctx || batch < 1 || heads < 1 || kv_heads < 1 || len < 1 || head_dim < 1) return 0;
+  const int sp = kq::dec_attention_splits(batch, kv_heads, len, ctx->num_sms);
+  return kq::dec_attention_scratch_bytes(batch, heads, head_dim, sp);
+}
+
+int kq_dec_attention(kq_ctx* ctx, const float* q, int64_t q_ld, const void* k_cache, const void* v_cache, float* out,
+                     int64_t out_ld, int64_t batch, int heads, int kv_heads, int head_dim, int64_t len,
+                     int64_t max_seq, void* scratch, size_t scratch_bytes) {
+  if (check_ctx(ctx) || !q || !k_cache || !v_cache || !out || !scratch) return KQ_ERR_INVALID_ARG;
+  if (len < 1 || len > max_seq || batch < 1)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "attention over %lld of %lld positions", (long long)len, (long long)max_seq);
+  const int sp = kq::dec_attention_splits(batch, kv_heads, len, ctx->num_sms);
+  if (scratch_bytes < kq::dec_attention_scratch_bytes(batch, heads, head_dim, sp))
+    return fail(ctx, KQ_ERR_SHORT_BUFFER, "attention scratch too small");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = kq::dec_attention(q, q_ld, k_cache, v_cache, out, out_ld, batch, heads, kv_heads, head_dim, len,
+                                    max_seq, static_cast<float*>(scratch), sp, ctx->stream);
+  if (e == cudaErrorInvalidValue) {
+    cudaGetLastError();
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "attention: head_dim %d / group %d unsupported", head_dim,
+                kv_heads ? heads / kv_heads : 0);
+  }
+  ctx->launches += 2;
+  return dec_status(ctx, e, "attention");
+}
+
+int kq_dec_swiglu(kq_ctx* ctx, const float* gate_up, float* out, int64_t batch, int64_t ffn, int mode) {
+  if (check_ctx(ctx) || !gate_up || !out || batch < 0 || ffn < 0 || (mode != 0 && mode != 1))
+    return KQ_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  ctx->launches += batch * ffn > 0;
+  return dec_status(ctx, kq::dec_swiglu(gate_up, out, batch, ffn, mode, ctx->stream), "swiglu");
+}
+
+int kq_dec_add(kq_ctx* ctx, float* h, int64_t h_ld, const float* y, int64_t y_ld, int64_t rows, int64_t cols) {
+  if (check_ctx(ctx) || !h || !y || rows < 0 || cols < 0 || h_ld < cols || y_ld < cols) return KQ_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  ctx->launches += rows * cols > 0;
+  return dec_status(ctx, kq::dec_add(h, h_ld, y, y_ld, rows, cols, ctx->stream), "add");
+}
+
+int kq_dec_embed(kq_ctx* ctx, const float* table, const int32_t* tokens, float* out, int64_t out_ld, int64_t batch,
+                 int64_t dim) {
+  if (check_ctx(ctx) || !table || !tokens || !out || batch < 1 || dim < 1 || out_ld < dim) return KQ_ERR_INVALID_ARG;
+  DeviceGuard g(ctx->device);
+  ctx->launches += 1;
+  return dec_status(ctx, kq::dec_embed(table, tokens, out, out_ld, batch, dim, ctx->stream), "embed");
 }
 
 int kq_dequant_f32(kq_ctx* ctx, const kq_weight* w, int64_t row0, int64_t nrows, float* out, int flags) {

@@ -106,19 +106,36 @@ cudaError_t launch_gemv_dp4a(const DevWeight& w, const float* x, int64_t m, cons
 constexpr int TP_MAX_WORLD = 8;
 struct TpArgs {
   const float* y_local;                  // [m][r1 - r0] this rank's block
-  float* y_out;                          // [m][n] the gathered result
-  int64_t m, n, r0, r1;                  // tokens, total rows, this rank's rows
-  float* peer_slot[TP_MAX_WORLD];        // every rank's image slot of this epoch ([m][n])
-  unsigned* peer_flags[TP_MAX_WORLD];    // every rank's flag array (one per source rank)
-  const float* local_slot;               // this rank's image slot of this epoch
-  const unsigned* local_flags;           // this rank's flag array
+  float* y_out;                          // [m][y_ld] the gathered result (first n columns)
+  int64_t y_ld;
+  int accumulate;                        // nonzero: y_out += gathered
+  int64_t m, n, r0, r1;                  // tokens, total columns, this rank's columns
+  float* exch[TP_MAX_WORLD];             // every rank's exchange buffer: 2 slots of max_elems floats, then flags
+  int64_t max_elems;
+  size_t flags_off;                      // byte offset of the flag array in an exchange buffer
   int world, rank;
-  unsigned epoch;                        // 1, 2, 3, ... per call
+  unsigned* epoch;                       // local device counter: the last completed call's epoch
   unsigned* ctr;                         // zero between calls (last-CTA detection)
   int* err;                              // set to a nonzero code if a wait gave up
 };
 // One launch per call; `blocks` must fit the GPU at once (<= SM count).
 cudaError_t launch_tp_allgather(const TpArgs& a, int blocks, cudaStream_t s);
+
+// ---- decoder step kernels: kq_decoder.cu ----
+cudaError_t dec_rmsnorm(const float* x, int64_t x_ld, const float* w, float* out, int64_t out_ld, int64_t rows,
+                        int64_t dim, float eps, cudaStream_t s);
+cudaError_t dec_rope_append(float* qkv, int64_t ld, void* kc, void* vc, int64_t batch, int hq, int hkv, int hd,
+                            int64_t pos, int64_t max_seq, float theta, cudaStream_t s);
+int dec_attention_splits(int64_t batch, int hkv, int64_t len, int num_sms);
+size_t dec_attention_scratch_bytes(int64_t batch, int hq, int hd, int splits);
+cudaError_t dec_attention(const float* q, int64_t q_ld, const void* kc, const void* vc, float* out, int64_t out_ld,
+                          int64_t batch, int hq, int hkv, int hd, int64_t len, int64_t max_seq, float* scratch,
+                          int splits, cudaStream_t s);
+cudaError_t dec_swiglu(const float* gu, float* out, int64_t batch, int64_t ffn, int mode, cudaStream_t s);
+cudaError_t dec_add(float* h, int64_t h_ld, const float* y, int64_t y_ld, int64_t rows, int64_t cols,
+                    cudaStream_t s);
+cudaError_t dec_embed(const float* table, const int* tokens, float* out, int64_t out_ld, int64_t batch, int64_t dim,
+                      cudaStream_t s);
 
 // ---- tensor-core (tcgen05) path: kq_mma.cu ----
 // Build the TMA descriptors of a GGUF weight (after its device arrays exist).

@@ -1,0 +1,313 @@
+"""Decode step of a Llama-style decoder on the quantized linears.
+
+The device form of pesti-runner's CPU decode step (transformer/model.rs:961-1075,
+layer.rs:169-244,266-274,344-372): embedding lookup, per layer RMSNorm ->
+Q/K/V projections -> rotary embedding + KV-cache append -> attention over the
+cache -> output projection + residual -> RMSNorm -> gate/up projections ->
+SwiGLU -> down projection + residual, then the optional final norm and the
+output head.  Every projection is a GGUF K-quant weight resident in HBM and
+runs through ``kq_linear_f32``; the small ops are the kernels of
+``include/pesti_decoder.h``.  Activations are f32, the KV cache f16.
+
+Tensor parallelism (``world > 1``, one process per GPU): heads are split across
+ranks -- rank r owns query heads and KV heads [r*h/world, (r+1)*h/world), its
+slice of the fused Q|K|V rows, its KV cache, a contiguous block of the output,
+down-projection and head rows and of the gate|up rows.  Four all-gathers per
+layer move activations over NVLink peer memory (``kq_tp_allgather_f32``): the
+attention output, the output projection (added into the residual), the SwiGLU
+output and the down projection (added into the residual); one more gathers the
+logits.
+
+Weights are synthetic (no checkpoints): random GGUF superblocks generated on
+the GPU from a seed per tensor, the same bytes on every rank, so a model
+sharded over any number of GPUs computes the same function.
+"""
+from __future__ import annotations
+
+import ctypes
+import zlib
+from dataclasses import dataclass
+from typing import Optional
+
+from . import kq
+
+SWIGLU_REFERENCE = 0  # pesti's swiglu (layer.rs:16-29): negative gates use g / (1 + e^g)
+SWIGLU_SILU = 1
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    name: str
+    layers: int
+    dim: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    eps: float
+    theta: float
+    final_norm: bool
+    linear_type: int = kq.KQ_GGUF_Q4_K
+    down_type: int = kq.KQ_GGUF_Q6_K
+    head_type: int = kq.KQ_GGUF_Q6_K
+
+
+# Qwen2.5-0.5B-shaped: 896-wide activations are fed to K-quant rows as 1024
+# (zero activations in the padded superblock).  Qwen models carry a final norm
+# (model.rs:290-293).
+QWEN25_05B = DecoderConfig("qwen2.5-0.5b-shaped", 24, 896, 14, 2, 64, 4864, 151936, 1e-6, 1e6, True)
+# Llama-3-8B-shaped.  pesti's Llama path applies no final norm (model.rs:290-293).
+LLAMA3_8B = DecoderConfig("llama-3-8b-shaped", 32, 4096, 32, 8, 128, 14336, 128256, 1e-5, 500000.0, False)
+
+
+def round_up(v: int, a: int) -> int:
+    return (v + a - 1) // a * a
+
+
+def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
+    P, I, I64, F, Z = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+    sig = {
+        "kq_dec_rmsnorm": [P, P, I64, P, P, I64, I64, I64, F],
+        "kq_dec_rope_append": [P, P, I64, P, P, I64, I, I, I, I64, I64, F],
+        "kq_dec_attention": [P, P, I64, P, P, P, I64, I64, I, I, I, I64, I64, P, Z],
+        "kq_dec_swiglu": [P, P, P, I64, I64, I],
+        "kq_dec_add": [P, P, I64, P, I64, I64, I64],
+        "kq_dec_embed": [P, P, P, P, I64, I64, I64],
+    }
+    for name, args in sig.items():
+        getattr(lib, name).argtypes = args
+        getattr(lib, name).restype = I
+    lib.kq_dec_attention_scratch.argtypes = [P, I64, I, I, I, I64]
+    lib.kq_dec_attention_scratch.restype = Z
+    return lib
+
+
+def gguf_weight_device(qtype: int, n: int, k: int, seed: int, device):
+    """Seeded random GGUF superblocks [n][k/256][bytes] as a uint8 CUDA tensor,
+    with the distributions of pesti_b200.synthetic: Q4_K d, dmin = f16(|N(0,
+    0.02)|); Q6_K int8 scales in [-32, 31], d = f16(|N(0, 0.005)|)."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    sb = k // 256
+    if qtype == kq.KQ_GGUF_Q4_K:
+        raw = torch.randint(0, 256, (n, sb, 144), dtype=torch.uint8, device=device, generator=gen)
+        dd = (torch.randn((n, sb, 2), generator=gen, device=device) * 0.02).abs().to(torch.float16)
+        raw[:, :, 0:4] = dd.view(torch.uint8).view(n, sb, 4)
+    elif qtype == kq.KQ_GGUF_Q6_K:
+        raw = torch.randint(0, 256, (n, sb, 210), dtype=torch.uint8, device=device, generator=gen)
+        sc = torch.randint(-32, 32, (n, sb, 16), dtype=torch.int8, device=device, generator=gen)
+        raw[:, :, 192:208] = sc.view(torch.uint8)
+        d = (torch.randn((n, sb, 1), generator=gen, device=device) * 0.005).abs().to(torch.float16)
+        raw[:, :, 208:210] = d.view(torch.uint8).view(n, sb, 2)
+    else:
+        raise ValueError(f"type {qtype}")
+    return raw.view(n, -1)
+
+
+class Decoder:
+    """One model replica (or one rank of a tensor-parallel group) with its KV
+    cache, able to run decode steps for `batch` sequences.  ``step`` queues one
+    step on the context stream (capturable into a CUDA graph)."""
+
+    def __init__(self, cfg: DecoderConfig, ctx: "kq.Context", batch: int, context_len: int, max_new: int = 8,
+                 world: int = 1, rank: int = 0, tp: Optional["kq.TensorParallel"] = None, seed: int = 0,
+                 swiglu_mode: int = SWIGLU_REFERENCE, kv_scale: float = 1.0, keep_raw: bool = False):
+        import torch
+        if cfg.heads % world or cfg.kv_heads % world:
+            raise ValueError(f"{cfg.name}: {cfg.heads} query / {cfg.kv_heads} KV heads do not split over {world}")
+        if world > 1 and tp is None:
+            raise ValueError("world > 1 needs a TensorParallel group")
+        self.cfg, self.ctx, self.batch, self.world, self.rank, self.tp = cfg, ctx, batch, world, rank, tp
+        self.swiglu_mode = swiglu_mode
+        self.lib = _bind(ctx.lib)
+        dev = torch.device("cuda", ctx.device)
+        self.device = dev
+        D, hd, F = cfg.dim, cfg.head_dim, cfg.ffn
+        self.Dp = round_up(D, 256)                 # K of projections fed by the residual stream
+        self.Ap = round_up(cfg.heads * hd, 256)    # K of the output projection
+        self.hq, self.hkv = cfg.heads // world, cfg.kv_heads // world
+        self.max_seq = context_len + max_new
+        self.context_len = context_len
+        B = batch
+
+        def slot(i, name):  # one seed per tensor, the same in every process
+            return (seed * 1000003 + i * 1009 + zlib.crc32(name.encode())) % (1 << 62)
+
+        # keep_raw: host copies of the full tensors (small test models only)
+        self.raw = {} if keep_raw else None
+
+        def keep(key, t):
+            if self.raw is not None:
+                self.raw[key] = t.cpu().numpy()
+
+        def upload(raw, qtype, n, k):
+            return kq.Weight(ctx, qtype, raw, n, k)
+
+        hq0, hkv0 = self.hq * rank, self.hkv * rank
+        self.o_rows = kq.shard_rows(D, world, rank)
+        self.f_rows = kq.shard_rows(F, world, rank)
+        self.v_rows = kq.shard_rows(cfg.vocab, world, rank)
+        self.layers = []
+        for li in range(cfg.layers):
+            L = {}
+            wq = gguf_weight_device(cfg.linear_type, cfg.heads * hd, self.Dp, slot(li, "q"), dev)
+            wk = gguf_weight_device(cfg.linear_type, cfg.kv_heads * hd, self.Dp, slot(li, "k"), dev)
+            wv = gguf_weight_device(cfg.linear_type, cfg.kv_heads * hd, self.Dp, slot(li, "v"), dev)
+            keep((li, "q"), wq)
+            keep((li, "k"), wk)
+            keep((li, "v"), wv)
+            qkv = torch.cat([wq[hq0 * hd:(hq0 + self.hq) * hd], wk[hkv0 * hd:(hkv0 + self.hkv) * hd],
+                             wv[hkv0 * hd:(hkv0 + self.hkv) * hd]]).contiguous()
+            L["qkv"] = upload(qkv, cfg.linear_type, qkv.shape[0], self.Dp)
+            del wq, wk, wv, qkv
+            wo = gguf_weight_device(cfg.linear_type, D, self.Ap, slot(li, "o"), dev)
+            keep((li, "o"), wo)
+            r0, r1 = self.o_rows
+            L["o"] = upload(wo[r0:r1].contiguous(), cfg.linear_type, r1 - r0, self.Ap)
+            wg = gguf_weight_device(cfg.linear_type, F, self.Dp, slot(li, "gate"), dev)
+            wu = gguf_weight_device(cfg.linear_type, F, self.Dp, slot(li, "up"), dev)
+            keep((li, "gate"), wg)
+            keep((li, "up"), wu)
+            f0, f1 = self.f_rows
+            gu = torch.cat([wg[f0:f1], wu[f0:f1]]).contiguous()
+            L["gu"] = upload(gu, cfg.linear_type, 2 * (f1 - f0), self.Dp)
+            del wg, wu, gu
+            wd = gguf_weight_device(cfg.down_type, D, F, slot(li, "down"), dev)
+            keep((li, "down"), wd)
+            L["down"] = upload(wd[r0:r1].contiguous(), cfg.down_type, r1 - r0, F)
+            del wd
+            g = torch.Generator(device=dev)
+            g.manual_seed(slot(li, "norms"))
+            L["attn_norm"] = 1.0 + 0.1 * torch.randn(D, generator=g, device=dev)
+            L["ffn_norm"] = 1.0 + 0.1 * torch.randn(D, generator=g, device=dev)
+            keep((li, "attn_norm"), L["attn_norm"])
+            keep((li, "ffn_norm"), L["ffn_norm"])
+            # KV cache: this rank's heads, a random N(0, kv_scale) prefix of context_len positions
+            kvshape = (B, cfg.kv_heads, self.max_seq, hd)
+            g.manual_seed(slot(li, "kv"))
+            kc = (kv_scale * torch.randn(kvshape, generator=g, device=dev)).to(torch.float16)
+            vc = (kv_scale * torch.randn(kvshape, generator=g, device=dev)).to(torch.float16)
+            L["k"] = kc[:, hkv0:hkv0 + self.hkv].contiguous()
+            L["v"] = vc[:, hkv0:hkv0 + self.hkv].contiguous()
+            keep((li, "kcache"), kc)
+            keep((li, "vcache"), vc)
+            del kc, vc
+            self.layers.append(L)
+        wh = gguf_weight_device(cfg.head_type, cfg.vocab, self.Dp, slot(cfg.layers, "head"), dev)
+        keep("head", wh)
+        v0, v1 = self.v_rows
+        self.head = upload(wh[v0:v1].contiguous(), cfg.head_type, v1 - v0, self.Dp)
+        del wh
+        g = torch.Generator(device=dev)
+        g.manual_seed(slot(cfg.layers, "embed"))
+        self.embed = 0.5 * torch.randn((cfg.vocab, D), generator=g, device=dev)
+        self.final_norm = 1.0 + 0.1 * torch.randn(D, generator=g, device=dev) if cfg.final_norm else None
+        keep("embed", self.embed)
+        if self.final_norm is not None:
+            keep("final_norm", self.final_norm)
+
+        # activations (padded columns stay zero)
+        z = lambda *s: torch.zeros(s, device=dev)  # noqa: E731
+        self.h, self.a = z(B, self.Dp), z(B, self.Dp)
+        self.qkv_ld = (self.hq + 2 * self.hkv) * hd
+        self.qkv = z(B, self.qkv_ld)
+        self.attn = z(B, self.Ap)
+        self.attn_r = z(B, self.hq * hd)
+        self.o = z(B, r1 - r0)
+        self.gu = z(B, 2 * (f1 - f0))
+        self.s_r = z(B, f1 - f0)
+        self.s = z(B, F)
+        self.dn = z(B, r1 - r0)
+        self.logits_r = z(B, v1 - v0)
+        self.logits = z(B, cfg.vocab)
+        self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
+        sbytes = self.lib.kq_dec_attention_scratch(ctx.handle, B, self.hq, self.hkv, hd, self.max_seq)
+        self.att_scratch = torch.empty(max(sbytes // 4, 1), device=dev)
+        self.att_scratch_bytes = sbytes
+        for L in self.layers:
+            for key in ("qkv", "o", "gu", "down"):
+                ctx.reserve(L[key], B)
+        ctx.reserve(self.head, B)
+        torch.cuda.synchronize(dev)
+
+    # ---- one decode step ------------------------------------------------------------
+    def _check(self, rc, what):
+        self.ctx.check(rc, what)
+
+    def _gather(self, src, cols, row0, rows, dst, ld, accumulate):
+        self.tp.allgather(src, self.batch, row0, rows, cols, dst, y_ld=ld, accumulate=accumulate)
+
+    def step(self, pos: int) -> None:
+        """Queue one decode step for the tokens in ``self.tokens`` at position
+        ``pos`` (the cache holds positions [0, pos)); logits land in
+        ``self.logits``."""
+        cfg, lib, c, B = self.cfg, self.lib, self.ctx.handle, self.batch
+        D, hd, F = cfg.dim, cfg.head_dim, cfg.ffn
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        if not 0 <= pos < self.max_seq:
+            raise ValueError(f"position {pos} outside the cache ({self.max_seq})")
+        r0, r1 = self.o_rows
+        f0, f1 = self.f_rows
+        tp = self.world > 1
+        self._check(lib.kq_dec_embed(c, ptr(self.embed), ptr(self.tokens), ptr(self.h), self.Dp, B, D), "embed")
+        for L in self.layers:
+            self._check(lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(L["attn_norm"]), ptr(self.a), self.Dp, B, D,
+                                           cfg.eps), "rmsnorm")
+            L["qkv"].linear(self.a, B, self.qkv, device_ptrs=True)
+            self._check(lib.kq_dec_rope_append(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]), B, self.hq,
+                                               self.hkv, hd, pos, self.max_seq, cfg.theta), "rope")
+            out, out_ld = (self.attn_r, self.hq * hd) if tp else (self.attn, self.Ap)
+            self._check(lib.kq_dec_attention(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]), ptr(out), out_ld,
+                                             B, self.hq, self.hkv, hd, pos + 1, self.max_seq, ptr(self.att_scratch),
+                                             self.att_scratch_bytes), "attention")
+            if tp:
+                self._gather(self.attn_r, cfg.heads * hd, self.rank * self.hq * hd, self.hq * hd, self.attn, self.Ap,
+                             False)
+            L["o"].linear(self.attn, B, self.o, device_ptrs=True)
+            if tp:
+                self._gather(self.o, D, r0, r1 - r0, self.h, self.Dp, True)
+            else:
+                self._check(lib.kq_dec_add(c, ptr(self.h), self.Dp, ptr(self.o), D, B, D), "add")
+            self._check(lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(L["ffn_norm"]), ptr(self.a), self.Dp, B, D,
+                                           cfg.eps), "rmsnorm")
+            L["gu"].linear(self.a, B, self.gu, device_ptrs=True)
+            self._check(lib.kq_dec_swiglu(c, ptr(self.gu), ptr(self.s_r if tp else self.s), B, f1 - f0,
+                                          self.swiglu_mode), "swiglu")
+            if tp:
+                self._gather(self.s_r, F, f0, f1 - f0, self.s, F, False)
+            L["down"].linear(self.s, B, self.dn, device_ptrs=True)
+            if tp:
+                self._gather(self.dn, D, r0, r1 - r0, self.h, self.Dp, True)
+            else:
+                self._check(lib.kq_dec_add(c, ptr(self.h), self.Dp, ptr(self.dn), D, B, D), "add")
+        x = self.h
+        if self.final_norm is not None:
+            self._check(lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(self.final_norm), ptr(self.a), self.Dp, B, D,
+                                           cfg.eps), "rmsnorm")
+            x = self.a
+        v0, v1 = self.v_rows
+        if tp:
+            self.head.linear(x, B, self.logits_r, device_ptrs=True)
+            self._gather(self.logits_r, cfg.vocab, v0, v1 - v0, self.logits, cfg.vocab, False)
+        else:
+            self.head.linear(x, B, self.logits, device_ptrs=True)
+
+    def weight_bytes(self) -> int:
+        """HBM bytes of this rank's quantized weights."""
+        total = self.head.device_bytes
+        for L in self.layers:
+            total += sum(L[key].device_bytes for key in ("qkv", "o", "gu", "down"))
+        return total
+
+    def kv_bytes(self, pos: int) -> int:
+        """KV-cache bytes one step at `pos` reads on this rank."""
+        return self.cfg.layers * 2 * self.batch * self.hkv * (pos + 1) * self.cfg.head_dim * 2
+
+    def close(self) -> None:
+        for L in self.layers:
+            for key in ("qkv", "o", "gu", "down"):
+                L[key].free()
+        self.head.free()
+        self.layers = []

@@ -44,6 +44,7 @@ KQ_PESTI_Q6_K_LEGACY = 114
 KQ_HOST_PTRS = 0
 KQ_DEVICE_PTRS = 1
 KQ_SYNC = 2
+KQ_ACCUMULATE = 4
 
 KQ_PATH_AUTO = 0
 KQ_PATH_TCGEN05 = 1
@@ -58,7 +59,8 @@ EXPORTED_SYMBOLS = (
     "kq_ctx_profile_end", "kq_ctx_profile_read", "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
     "kq_linear_f32", "kq_linear_bf16", "kq_linear_f32_static", "kq_dequant_f32",
     "kq_tp_create", "kq_tp_handle", "kq_tp_open", "kq_tp_linear_f32", "kq_tp_allgather_f32",
-    "kq_tp_destroy",
+    "kq_tp_destroy", "kq_dec_rmsnorm", "kq_dec_rope_append", "kq_dec_attention_scratch", "kq_dec_attention",
+    "kq_dec_swiglu", "kq_dec_add", "kq_dec_embed",
 )
 
 
@@ -117,7 +119,7 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
             "kq_tp_handle": ([P, P, ctypes.POINTER(Z)], I),
             "kq_tp_open": ([P, P, Z], I),
             "kq_tp_linear_f32": ([P, P, I64, I64, P, I64, P, P, I], I),
-            "kq_tp_allgather_f32": ([P, P, I64, I64, I64, I64, P, I], I),
+            "kq_tp_allgather_f32": ([P, P, I64, I64, I64, I64, P, I64, I], I),
             "kq_tp_destroy": ([P], I),
         }
         for name, (args, res) in sig.items():
@@ -232,11 +234,15 @@ class Weight:
 
     def __init__(self, ctx: Context, kq_type: int, data, out_features: int, in_features: int):
         self.ctx = ctx
-        raw = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray))
-                                   else np.asarray(data, dtype=np.uint8)).reshape(-1)
+        if getattr(data, "is_cuda", False):  # a CUDA tensor: uploaded device to device
+            t = data.contiguous()
+            ptr, size = (t.data_ptr() if t.numel() else None), t.numel() * t.element_size()
+        else:
+            raw = np.ascontiguousarray(np.frombuffer(data, np.uint8) if isinstance(data, (bytes, bytearray))
+                                       else np.asarray(data, dtype=np.uint8)).reshape(-1)
+            ptr, size = (raw.ctypes.data if raw.size else None), raw.size
         h = ctypes.c_void_p()
-        rc = ctx.lib.kq_weight_upload(ctx.handle, kq_type, raw.ctypes.data if raw.size else None,
-                                      raw.size, out_features, in_features, ctypes.byref(h))
+        rc = ctx.lib.kq_weight_upload(ctx.handle, kq_type, ptr, size, out_features, in_features, ctypes.byref(h))
         ctx.check(rc, "kq_weight_upload")
         self.handle = h
         self.kq_type = kq_type
@@ -326,9 +332,11 @@ class TensorParallel:
                                            _ptr(y), flags)
         self.ctx.check(rc, "kq_tp_linear_f32")
 
-    def allgather(self, y_local, m: int, row0: int, rows: int, n_total: int, y, sync: bool = False):
-        flags = KQ_DEVICE_PTRS | (KQ_SYNC if sync else 0)
-        rc = self.ctx.lib.kq_tp_allgather_f32(self.handle, _ptr(y_local), m, row0, rows, n_total, _ptr(y), flags)
+    def allgather(self, y_local, m: int, row0: int, rows: int, n_total: int, y, y_ld: Optional[int] = None,
+                  accumulate: bool = False, sync: bool = False):
+        flags = KQ_DEVICE_PTRS | (KQ_SYNC if sync else 0) | (KQ_ACCUMULATE if accumulate else 0)
+        rc = self.ctx.lib.kq_tp_allgather_f32(self.handle, _ptr(y_local), m, row0, rows, n_total, _ptr(y),
+                                              n_total if y_ld is None else y_ld, flags)
         self.ctx.check(rc, "kq_tp_allgather_f32")
 
     def close(self) -> None:

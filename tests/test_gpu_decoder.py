@@ -1,0 +1,139 @@
+"""Decoder step on the GPU against the CPU restatement of pesti's decode step
+(oracle/decoder_oracle.py) on small models: same weights, same KV-cache
+prefix, logits within tolerance; CUDA-graph replay; tensor parallelism on 2
+GPUs giving the same logits as one GPU."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3  # max|logit - ref| / max|ref| after two layers and the head
+
+from pesti_b200 import decoder as dec  # noqa: E402
+from pesti_b200 import kq  # noqa: E402
+
+QWEN_TINY = dec.DecoderConfig("qwen-like-tiny", 2, 448, 7, 1, 64, 512, 300, 1e-6, 1e6, True)
+LLAMA_TINY = dec.DecoderConfig("llama-like-tiny", 2, 512, 4, 2, 128, 768, 300, 1e-5, 5e5, False)
+
+
+def rel_err(y, ref):
+    y = np.asarray(y, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def _oracle_caches(model, cfg):
+    ks = [model.raw[(li, "kcache")].astype(np.float32) for li in range(cfg.layers)]
+    vs = [model.raw[(li, "vcache")].astype(np.float32) for li in range(cfg.layers)]
+    return ks, vs
+
+
+@pytest.mark.parametrize("cfg", [QWEN_TINY, LLAMA_TINY], ids=lambda c: c.name)
+@pytest.mark.parametrize("mode", [dec.SWIGLU_REFERENCE, dec.SWIGLU_SILU])
+def test_decode_steps_match_the_restated_reference(gpu_ctx, cfg, mode):
+    import torch
+    from oracle import decoder_oracle
+    batch, ctx_len = 2, 20
+    model = dec.Decoder(cfg, gpu_ctx, batch, ctx_len, max_new=4, seed=5, swiglu_mode=mode, keep_raw=True)
+    ks, vs = _oracle_caches(model, cfg)
+    for step, toks in enumerate(([3, 250], [17, 9])):
+        pos = ctx_len + step
+        model.tokens.copy_(torch.tensor(toks, dtype=torch.int32))
+        model.step(pos)
+        gpu_ctx.synchronize()
+        got = model.logits.cpu().numpy()
+        ref = decoder_oracle.decode_step(cfg, model.raw, toks, pos, ks, vs, swiglu_mode=mode)
+        assert np.isfinite(got).all()
+        assert rel_err(got, ref) <= TOL, f"step {step}"
+    model.close()
+
+
+def test_decode_step_replays_from_a_cuda_graph(gpu_ctx):
+    import torch
+    cfg = LLAMA_TINY
+    model = dec.Decoder(cfg, gpu_ctx, 2, 20, max_new=2, seed=6)
+    model.tokens.copy_(torch.tensor([1, 2], dtype=torch.int32))
+    s = torch.cuda.Stream()
+    gpu_ctx.set_stream(s.cuda_stream)
+    try:
+        with torch.cuda.stream(s):
+            model.step(20)
+        s.synchronize()
+        eager = model.logits.clone()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            model.step(20)
+        for _ in range(2):
+            model.logits.zero_()
+            with torch.cuda.stream(s):
+                g.replay()
+            s.synchronize()
+            assert torch.equal(model.logits, eager)
+        del g
+    finally:
+        gpu_ctx.set_stream(None)
+    model.close()
+
+
+def test_decoder_rejects_heads_that_do_not_split(gpu_ctx):
+    with pytest.raises(ValueError):
+        dec.Decoder(QWEN_TINY, gpu_ctx, 1, 8, world=2, rank=0)
+
+
+def _gpus():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _tp_worker(rank, world, port, out_dir):
+    import datetime
+    import torch
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    status = "ok"
+    try:
+        cfg = LLAMA_TINY
+        ctx = kq.Context(rank)
+        tp = kq.TensorParallel(ctx, world, rank, max_out_elems=4 * cfg.vocab)
+        model = dec.Decoder(cfg, ctx, 2, 20, max_new=2, world=world, rank=rank, tp=tp, seed=7)
+        single = dec.Decoder(cfg, ctx, 2, 20, max_new=2, seed=7)
+        for m in (model, single):
+            m.tokens.copy_(torch.tensor([4, 5], dtype=torch.int32))
+            m.step(20)
+        ctx.synchronize()
+        a, b = model.logits.cpu().numpy(), single.logits.cpu().numpy()
+        if not np.isfinite(a).all() or rel_err(a, b) > 1e-5:
+            status = f"tensor-parallel logits differ: {rel_err(a, b):.2e}"
+        model.close()
+        single.close()
+        tp.close()
+        ctx.close()
+    except Exception as e:
+        status = f"exception: {e!r}"
+    finally:
+        with open(os.path.join(out_dir, f"r{rank}"), "w") as fh:
+            fh.write(status)
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_decode_matches_one_gpu(tmp_path):
+    import torch.multiprocessing as mp
+    mp.start_processes(_tp_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
+    for r in range(2):
+        assert (tmp_path / f"r{r}").read_text() == "ok", f"rank {r}"
