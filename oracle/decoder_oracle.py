@@ -54,6 +54,24 @@ def swiglu(g, u, mode):
     return (sig * g * u).astype(np.float32)
 
 
+def attention(q, kc, vc, length, heads, kv_heads, hd):
+    """softmax(q . k^T / sqrt(hd)) . v over positions [0, length) with grouped
+    query heads (Attention::forward_with_cache, layer.rs:197-239).
+    q [B][heads*hd]; kc, vc [B][kv_heads][max_seq][hd] -> [B][heads*hd]."""
+    B = q.shape[0]
+    group = heads // kv_heads
+    out = np.zeros((B, heads * hd), np.float32)
+    scale = 1.0 / np.sqrt(hd)
+    for b in range(B):
+        for hh in range(heads):
+            g = hh // group
+            qh = q[b, hh * hd:(hh + 1) * hd].astype(np.float64)
+            scores = (kc[b, g, :length].astype(np.float64) @ qh) * scale
+            e = np.exp(scores - scores.max())
+            out[b, hh * hd:(hh + 1) * hd] = (e / e.sum()) @ vc[b, g, :length].astype(np.float64)
+    return out
+
+
 def decode_step(cfg, raw, tokens, pos, kcache, vcache, swiglu_mode=0):
     """One step for tokens [B] at position pos.  raw: the decoder's host
     copies of the full tensors; kcache / vcache: per layer f32 arrays
@@ -63,7 +81,6 @@ def decode_step(cfg, raw, tokens, pos, kcache, vcache, swiglu_mode=0):
     Dp = -(-D // 256) * 256
     Ap = -(-(cfg.heads * hd) // 256) * 256
     B = len(tokens)
-    group = cfg.heads // cfg.kv_heads
     h = raw["embed"][np.asarray(tokens)].astype(np.float32)
     for li in range(cfg.layers):
         def W(name, qt, n, k, cols):
@@ -77,16 +94,7 @@ def decode_step(cfg, raw, tokens, pos, kcache, vcache, swiglu_mode=0):
         kc, vc = kcache[li], vcache[li]
         kc[:, :, pos, :] = k.reshape(B, cfg.kv_heads, hd).astype(np.float16).astype(np.float32)
         vc[:, :, pos, :] = v.reshape(B, cfg.kv_heads, hd).astype(np.float16).astype(np.float32)
-        attn = np.zeros((B, cfg.heads * hd), np.float32)
-        scale = np.float32(1.0 / np.sqrt(np.float32(hd)))
-        for b in range(B):
-            for hh in range(cfg.heads):
-                g = hh // group
-                qh = q[b, hh * hd:(hh + 1) * hd].astype(np.float64)
-                scores = (kc[b, g, :pos + 1].astype(np.float64) @ qh) * scale
-                e = np.exp(scores - scores.max())
-                wts = e / e.sum()
-                attn[b, hh * hd:(hh + 1) * hd] = wts @ vc[b, g, :pos + 1].astype(np.float64)
+        attn = attention(q, kc, vc, pos + 1, cfg.heads, cfg.kv_heads, hd)
         o = (attn.astype(np.float64) @ W("o", cfg.linear_type, D, Ap, cfg.heads * hd).T).astype(np.float32)
         h = (h + o).astype(np.float32)
         a2 = rmsnorm(h, raw[(li, "ffn_norm")], cfg.eps)
