@@ -81,7 +81,8 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--workload", choices=sorted(WORKLOADS) + sorted(PREFILL) + sorted(DECODERS),
                    default="q6k-gemv")
-    p.add_argument("--m", type=int, default=1)
+    p.add_argument("--m", "--batch", dest="m", type=int, default=1,
+                   help="tokens per call (decode batch); --batch is the form to use under torchrun")
     p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a"], default="auto",
                    help="kernel family for the GEMV (auto: dp4a m<=4, mma m<=64, tcgen05 above)")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -617,7 +618,7 @@ def run_decoder(args, rank, world, local_rank):
     ctx = kq.Context(local_rank)
     tp = None
     if world > 1:
-        tp = kq.TensorParallel(ctx, world, rank, max_out_elems=B * max(cfg.vocab, cfg.ffn, cfg.dim))
+        tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, B))
     model = dec.Decoder(cfg, ctx, B, ctx_len, max_new=2, world=world, rank=rank, tp=tp, seed=11)
     gen = torch.Generator(device=dev)
     gen.manual_seed(3)

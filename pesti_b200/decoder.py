@@ -106,6 +106,12 @@ def gguf_weight_device(qtype: int, n: int, k: int, seed: int, device):
     return raw.view(n, -1)
 
 
+def exchange_elems(cfg: DecoderConfig, batch: int) -> int:
+    """Floats the tensor-parallel exchange buffer needs for this model: the
+    widest all-gathered activation (logits, SwiGLU output, residual stream)."""
+    return batch * max(cfg.vocab, cfg.ffn, cfg.dim, cfg.heads * cfg.head_dim)
+
+
 class Decoder:
     """One model replica (or one rank of a tensor-parallel group) with its KV
     cache, able to run decode steps for `batch` sequences.  ``step`` queues one

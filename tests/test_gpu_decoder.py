@@ -109,7 +109,7 @@ def _tp_worker(rank, world, port, out_dir):
     try:
         cfg = LLAMA_TINY
         ctx = kq.Context(rank)
-        tp = kq.TensorParallel(ctx, world, rank, max_out_elems=4 * cfg.vocab)
+        tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, 2))
         model = dec.Decoder(cfg, ctx, 2, 20, max_new=2, world=world, rank=rank, tp=tp, seed=7)
         single = dec.Decoder(cfg, ctx, 2, 20, max_new=2, seed=7)
         for m in (model, single):
