@@ -86,6 +86,10 @@ def parse():
     p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a"], default="auto",
                    help="kernel family for the GEMV (auto: dp4a m<=4, mma m<=64, tcgen05 above)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-prefetch", action="store_true",
+                   help="GEMV stream without the next-weight L2 prefetch hint")
+    p.add_argument("--no-fuse", action="store_true",
+                   help="decoders: separate RMSNorm / SwiGLU / add kernels at batch 1")
     return p.parse_args()
 
 
@@ -311,8 +315,11 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.Stream(dev)
     ctx.set_stream(stream.cuda_stream)
 
-    def step():
-        for w, y in zip(weights, ys):
+    def step(prefetch=not args.no_prefetch):
+        # a stream of GEMVs as in a decode step: each call is told the weight
+        # the next one reads (kq_ctx_prefetch_next), the last one the first
+        for i, (w, y) in enumerate(zip(weights, ys)):
+            ctx.prefetch_next(weights[(i + 1) % NUM_WEIGHTS] if prefetch else None)
             w.linear(x, m, y, device_ptrs=True)
 
     with torch.cuda.stream(stream):
@@ -333,9 +340,13 @@ def run_ours(args, rank, world, local_rank):
     plain = torch.cuda.CUDAGraph()  # the bracket budget is used up: no events
     with torch.cuda.graph(plain, stream=stream):
         step()
+    plain_np = torch.cuda.CUDAGraph()  # the same stream without prefetch hints
+    with torch.cuda.graph(plain_np, stream=stream):
+        step(prefetch=False)
 
     for _ in range(max(args.warmup, 3)):
         plain.replay()
+        plain_np.replay()
         bracketed.replay()
     stream.synchronize()
     if world > 1:
@@ -356,6 +367,13 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     ms_total = start.elapsed_time(stop)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            plain_np.replay()
+        stop.record(stream)
+    stop.synchronize()
+    ms_total_np = start.elapsed_time(stop)
 
     # per-kernel average over replays of the bracketed graph
     kernel_ms, kernel_n = 0.0, 0
@@ -367,10 +385,10 @@ def run_ours(args, rank, world, local_rank):
         kernel_n += cnt
     ctx.profile_end()
 
-    t = torch.tensor([ms_total, kernel_ms / max(kernel_n, 1)], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms_total, kernel_ms / max(kernel_n, 1), ms_total_np], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_total, kernel_ms_avg = float(t[0]), float(t[1])
+    ms_total, kernel_ms_avg, ms_total_np = float(t[0]), float(t[1]), float(t[2])
     ms_per_step = ms_total / args.steps
     value = world * NUM_WEIGHTS * alg / (ms_per_step * 1e-3) / 1e9
 
@@ -417,7 +435,12 @@ def run_ours(args, rank, world, local_rank):
                        "rows": n, "k": k, "m": m, "weights_per_step": NUM_WEIGHTS,
                        "weight_bytes_per_gemv": wbytes, "algorithmic_bytes_per_gemv": alg,
                        "l2": f"inputs larger than L2 ({NUM_WEIGHTS * wbytes / 1e6:.0f} MB of weights per step)",
-                       "parallelism": f"replicas x{world} (independent weights per rank, no data-path collective)"},
+                       "parallelism": f"replicas x{world} (independent weights per rank, no data-path collective)",
+                       "prefetch": ("off" if args.no_prefetch else
+                                    "each GEMV prefetches the next one's weight into L2 (kq_ctx_prefetch_next)")},
+            "without_prefetch": {"value": round(world * NUM_WEIGHTS * alg / (ms_total_np / args.steps * 1e-3) / 1e9,
+                                                2),
+                                 "ms_per_step": round(ms_total_np / args.steps, 5)},
             "gpu_launches": launches_per_step * args.steps,
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
@@ -437,7 +460,7 @@ def run_ours(args, rank, world, local_rank):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.workload, m)
         print(json.dumps(line), flush=True)
-    del plain, bracketed
+    del plain, plain_np, bracketed
     for w in weights:
         w.free()
     ctx.close()
@@ -619,7 +642,8 @@ def run_decoder(args, rank, world, local_rank):
     tp = None
     if world > 1:
         tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, B))
-    model = dec.Decoder(cfg, ctx, B, ctx_len, max_new=2, world=world, rank=rank, tp=tp, seed=11)
+    model = dec.Decoder(cfg, ctx, B, ctx_len, max_new=2, world=world, rank=rank, tp=tp, seed=11,
+                        fused=not args.no_fuse, prefetch=not args.no_prefetch)
     gen = torch.Generator(device=dev)
     gen.manual_seed(3)
     model.tokens.copy_(torch.randint(0, cfg.vocab, (B,), generator=gen, device=dev, dtype=torch.int32))
@@ -695,7 +719,12 @@ def run_decoder(args, rank, world, local_rank):
                        "l2": "inputs larger than L2 (every step streams all weights and the KV cache)",
                        "parallelism": (f"tensor parallel x{world}: heads, KV cache and row blocks sharded, "
                                        f"4 all-gathers per layer over NVLink peer memory") if world > 1
-                       else "single GPU"},
+                       else "single GPU",
+                       "fused": ("RoPE + KV append + attention in one kernel; "
+                                 + ("RMSNorm, SwiGLU and residual adds inside the single-token GEMVs"
+                                    if model.fused else "separate RMSNorm / SwiGLU / add kernels")
+                                 if model.fused_attention else "separate kernels"),
+                       "prefetch": "next weight into L2 during each linear" if model.prefetch else "off"},
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak * world, "unit": "GB/s",
                          "frac": round(achieved / (peak * world), 4),

@@ -28,7 +28,10 @@ int kq_dec_rmsnorm(kq_ctx *ctx, const float *x, int64_t x_ld, const float *w, fl
  * to f16. */
 int kq_dec_rope_append(kq_ctx *ctx, float *qkv, int64_t ld, void *k_cache, void *v_cache, int64_t batch, int heads,
                        int kv_heads, int head_dim, int64_t pos, int64_t max_seq, float theta);
-/* Scratch bytes kq_dec_attention needs for these sizes (0 if unsupported). */
+/* Scratch bytes kq_dec_attention / kq_dec_rope_attention need for these sizes
+ * (len: the longest sequence the scratch will serve).  The scratch must be
+ * zero-filled before its first use (it holds arrival counters that every
+ * call leaves at zero). */
 size_t kq_dec_attention_scratch(kq_ctx *ctx, int64_t batch, int heads, int kv_heads, int head_dim, int64_t len);
 /* Softmax(q . k^T / sqrt(head_dim)) . v over cache positions [0, len) with
  * grouped query heads (Attention::forward_with_cache, layer.rs:169-244); q
@@ -37,12 +40,37 @@ size_t kq_dec_attention_scratch(kq_ctx *ctx, int64_t batch, int heads, int kv_he
 int kq_dec_attention(kq_ctx *ctx, const float *q, int64_t q_ld, const void *k_cache, const void *v_cache,
                      float *out, int64_t out_ld, int64_t batch, int heads, int kv_heads, int head_dim, int64_t len,
                      int64_t max_seq, void *scratch, size_t scratch_bytes);
+/* kq_dec_rope_append followed by kq_dec_attention over [0, pos], in one
+ * kernel: qkv rows as in kq_dec_rope_append; the query heads are rotated in
+ * registers (qkv is not modified), the rotated k and v of position pos are
+ * appended to the caches, and the attention output goes to out. */
+int kq_dec_rope_attention(kq_ctx *ctx, const float *qkv, int64_t ld, void *k_cache, void *v_cache, float *out,
+                          int64_t out_ld, int64_t batch, int heads, int kv_heads, int head_dim, int64_t pos,
+                          int64_t max_seq, float theta, void *scratch, size_t scratch_bytes);
 /* out[b][i] from gate_up[b] = [gate(ffn) | up(ffn)].  mode 0: pesti's
  * swiglu (layer.rs:16-29), whose negative-gate branch uses g / (1 + e^g) as
  * the sigmoid; mode 1: SiLU(gate) * up. */
 int kq_dec_swiglu(kq_ctx *ctx, const float *gate_up, float *out, int64_t batch, int64_t ffn, int mode);
 /* h[r][c] += y[r][c] for c < cols (the residual connections, layer.rs:346-368). */
 int kq_dec_add(kq_ctx *ctx, float *h, int64_t h_ld, const float *y, int64_t y_ld, int64_t rows, int64_t cols);
+/* Fused single-token linears (batch 1, GGUF Q4_K / Q6_K, in_features <= 30720):
+ * the activation transform runs inside the GEMV's activation staging.
+ * bias may alias y, which makes the call the residual update y += W . act(x).
+ * KQ_ERR_UNSUPPORTED when the single-token kernel does not apply (the caller
+ * then queues kq_dec_rmsnorm / kq_dec_swiglu and kq_linear_f32).
+ *   norm_linear:   y = rmsnorm(x[0:dim]; norm_w, eps) . W^T + bias, the
+ *                  normalised vector zero past dim (dim <= in_features, a
+ *                  multiple of 4);
+ *   swiglu_linear: y = swiglu(gate_up; mode) . W^T + bias with gate_up =
+ *                  [gate (in_features) | up (in_features)], mode as in kq_dec_swiglu;
+ *   residual_linear: h += x . W^T.
+ * flags: KQ_SYNC or 0 (pointers are device pointers). */
+int kq_dec_norm_linear(kq_ctx *ctx, const kq_weight *w, const float *x, const float *norm_w, int64_t dim, float eps,
+                       const float *bias, float *y, int flags);
+int kq_dec_swiglu_linear(kq_ctx *ctx, const kq_weight *w, const float *gate_up, int mode, const float *bias, float *y,
+                         int flags);
+/* h[0:out_features] += x . W^T (the residual connection fused into the linear). */
+int kq_dec_residual_linear(kq_ctx *ctx, const kq_weight *w, const float *x, float *h, int flags);
 /* out[b] = table[tokens[b]] (Model::embed, model.rs:966-984); table f32 [vocab][dim]. */
 int kq_dec_embed(kq_ctx *ctx, const float *table, const int32_t *tokens, float *out, int64_t out_ld,
                  int64_t batch, int64_t dim);

@@ -81,6 +81,13 @@ int kq_ctx_set_path(kq_ctx *ctx, int path);
 /* Reserve scratch for calls on weight `w` with up to `m` activation rows, so
  * that later calls allocate nothing (e.g. before CUDA-graph capture). */
 int kq_ctx_reserve(kq_ctx *ctx, const kq_weight *w, int64_t m);
+/* Hint: the compute call queued after the next one will read weight `next`.
+ * The next linear call on this context (kq_linear_f32 and the fused decoder
+ * linears, single-token GGUF kernel) prefetches `next` into L2 while it
+ * streams its own weight, so the following call starts on cached data; the
+ * hint is consumed by that call whatever path it takes.  NULL clears it.
+ * No reference counterpart (pesti-runner's forward is synchronous). */
+int kq_ctx_prefetch_next(kq_ctx *ctx, const kq_weight *next);
 /* Number of kernels this context has launched so far. */
 int64_t kq_ctx_launch_count(const kq_ctx *ctx);
 /* Bracket the main kernel of each of the next `max_calls` compute calls with a

@@ -35,6 +35,14 @@ struct kq_ctx {
   size_t bbuf_bytes = 0;
   int64_t launches = 0;
   std::string err;
+  // one-shot L2 prefetch hint for the next linear call (kq_ctx_prefetch_next)
+  kq::Prefetch pf;
+  bool pf_set = false;
+  const kq::Prefetch* take_prefetch() {
+    if (!pf_set) return nullptr;
+    pf_set = false;
+    return &pf;
+  }
   // timing brackets of the main kernel (kq_ctx_profile_begin/end)
   std::vector<cudaEvent_t> prof_ev;  // 2 per slot
   int prof_cap = 0, prof_next = 0;
@@ -160,8 +168,8 @@ int check_device_error(kq_ctx* ctx) {
   cudaDeviceSynchronize();
   cudaGetLastError();
   return fail(ctx, KQ_ERR_CUDA,
-              "a device-side wait gave up (code %d: 1-5 tcgen05 pipeline, 21-23 decode weight ring, 31 "
-              "tensor-parallel peer flag); the call's output is invalid",
+              "a device-side wait gave up (code %d: 1-5 tcgen05 pipeline, 21-23 decode weight ring, 24 "
+              "attention KV ring, 31 tensor-parallel peer flag); the call's output is invalid",
               code);
 }
 
@@ -247,6 +255,7 @@ int kq_ctx_create(int device, kq_ctx** out) {
   e = kq::gemv_init_device();
   if (e == cudaSuccess) e = kq::tc_init_device();
   if (e == cudaSuccess) e = kq::dp4a_init_device();
+  if (e == cudaSuccess) e = kq::dec_init_device();
   if (e != cudaSuccess) {
     cudaGetLastError();
     return KQ_ERR_CUDA;
@@ -302,6 +311,31 @@ int kq_ctx_set_path(kq_ctx* ctx, int path) {
   if (path != KQ_PATH_AUTO && path != KQ_PATH_TCGEN05 && path != KQ_PATH_MMA && path != KQ_PATH_DP4A)
     return fail(ctx, KQ_ERR_INVALID_ARG, "unknown path %d", path);
   ctx->path = path;
+  return KQ_OK;
+}
+
+int kq_ctx_prefetch_next(kq_ctx* ctx, const kq_weight* next) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  ctx->pf = kq::Prefetch();
+  ctx->pf_set = false;
+  if (!next) return KQ_OK;
+  if (next->device != ctx->device)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", next->device, ctx->device);
+  const kq::DevWeight& w = next->dw;
+  if (w.type == kq::GGUF_Q4_K) {
+    ctx->pf.p[0] = w.q;
+    ctx->pf.bytes[0] = w.n * w.sb * kq::Q4K_BYTES;
+  } else if (w.type == kq::GGUF_Q6_K) {
+    ctx->pf.p[0] = w.q;
+    ctx->pf.bytes[0] = w.n * w.sb * kq::Q6K_BODY;
+    ctx->pf.p[1] = w.d;
+    ctx->pf.bytes[1] = w.n * w.d_ld * 2;
+  } else {
+    return KQ_OK;  // legacy blocks: no hint
+  }
+  for (int r = 0; r < 2; ++r)  // bulk prefetches start on 16-byte boundaries
+    if (reinterpret_cast<uintptr_t>(ctx->pf.p[r]) & 15) ctx->pf.p[r] = nullptr;
+  ctx->pf_set = true;
   return KQ_OK;
 }
 
@@ -520,6 +554,7 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
   cudaStream_t s = ctx->stream;
   cudaError_t e = cudaSuccess;
   int rc;
+  const kq::Prefetch* pf = ctx->take_prefetch();
 
   const void* xd = x;
   const float* bd = bias;
@@ -558,7 +593,7 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
     const int fam = f32_family(ctx, m);
     if (fam == KQ_PATH_DP4A) {
       e = kq::launch_gemv_dp4a(w->dw, static_cast<const float*>(xd), m, bd, yd, ctx->ws, ctx->num_sms,
-                               ctx->dev_err, s, &launches, ctx->next_bracket());
+                               ctx->dev_err, s, &launches, ctx->next_bracket(), pf);
     } else if (fam == KQ_PATH_TCGEN05) {
       // counters live in their own zeroed buffer; the scratch layout's counter span is unused
       e = kq::launch_tc_f32(w->dw, static_cast<const float*>(xd), m, bd, yd, ctx->ws, ctx->num_sms, ctx->dev_err,
@@ -803,28 +838,48 @@ int kq_dec_rope_append(kq_ctx* ctx, float* qkv, int64_t ld, void* k_cache, void*
 size_t kq_dec_attention_scratch(kq_ctx* ctx, int64_t batch, int heads, int kv_heads, int head_dim, int64_t len) {
   if (!ctx || batch < 1 || heads < 1 || kv_heads < 1 || len < 1 || head_dim < 1) return 0;
   const int sp = kq::dec_attention_splits(batch, kv_heads, len, ctx->num_sms);
-  return kq::dec_attention_scratch_bytes(batch, heads, head_dim, sp);
+  return kq::dec_attention_scratch_bytes(batch, heads, kv_heads, head_dim, sp);
+}
+
+static int attention_impl(kq_ctx* ctx, const float* q, int64_t q_ld, void* k_cache, void* v_cache, float* out,
+                          int64_t out_ld, int64_t batch, int heads, int kv_heads, int head_dim, int64_t len,
+                          int64_t max_seq, void* scratch, size_t scratch_bytes, bool rope, float theta) {
+  if (check_ctx(ctx) || !q || !k_cache || !v_cache || !out || !scratch) return KQ_ERR_INVALID_ARG;
+  if (len < 1 || len > max_seq || batch < 1)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "attention over %lld of %lld positions", (long long)len, (long long)max_seq);
+  if (kv_heads < 1 || heads < 1)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "attention: %d heads / %d kv heads", heads, kv_heads);
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "attention: the caches must be 16-byte aligned");
+  const int sp = kq::dec_attention_splits(batch, kv_heads, len, ctx->num_sms);
+  if (scratch_bytes < kq::dec_attention_scratch_bytes(batch, heads, kv_heads, head_dim, sp))
+    return fail(ctx, KQ_ERR_SHORT_BUFFER, "attention scratch too small");
+  DeviceGuard g(ctx->device);
+  cudaError_t e = kq::dec_attention(q, q_ld, k_cache, v_cache, out, out_ld, batch, heads, kv_heads, head_dim, len,
+                                    max_seq, scratch, sp, rope, theta, ctx->dev_err, ctx->stream);
+  if (e == cudaErrorInvalidValue) {
+    cudaGetLastError();
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "attention: head_dim %d / group %d unsupported", head_dim,
+                heads / kv_heads);
+  }
+  ctx->launches += 1;
+  return dec_status(ctx, e, "attention");
 }
 
 int kq_dec_attention(kq_ctx* ctx, const float* q, int64_t q_ld, const void* k_cache, const void* v_cache, float* out,
                      int64_t out_ld, int64_t batch, int heads, int kv_heads, int head_dim, int64_t len,
                      int64_t max_seq, void* scratch, size_t scratch_bytes) {
-  if (check_ctx(ctx) || !q || !k_cache || !v_cache || !out || !scratch) return KQ_ERR_INVALID_ARG;
-  if (len < 1 || len > max_seq || batch < 1)
-    return fail(ctx, KQ_ERR_INVALID_ARG, "attention over %lld of %lld positions", (long long)len, (long long)max_seq);
-  const int sp = kq::dec_attention_splits(batch, kv_heads, len, ctx->num_sms);
-  if (scratch_bytes < kq::dec_attention_scratch_bytes(batch, heads, head_dim, sp))
-    return fail(ctx, KQ_ERR_SHORT_BUFFER, "attention scratch too small");
-  DeviceGuard g(ctx->device);
-  cudaError_t e = kq::dec_attention(q, q_ld, k_cache, v_cache, out, out_ld, batch, heads, kv_heads, head_dim, len,
-                                    max_seq, static_cast<float*>(scratch), sp, ctx->stream);
-  if (e == cudaErrorInvalidValue) {
-    cudaGetLastError();
-    return fail(ctx, KQ_ERR_UNSUPPORTED, "attention: head_dim %d / group %d unsupported", head_dim,
-                kv_heads ? heads / kv_heads : 0);
-  }
-  ctx->launches += 2;
-  return dec_status(ctx, e, "attention");
+  // the caches are only read without rope
+  return attention_impl(ctx, q, q_ld, const_cast<void*>(k_cache), const_cast<void*>(v_cache), out, out_ld, batch,
+                        heads, kv_heads, head_dim, len, max_seq, scratch, scratch_bytes, false, 0.f);
+}
+
+int kq_dec_rope_attention(kq_ctx* ctx, const float* qkv, int64_t ld, void* k_cache, void* v_cache, float* out,
+                          int64_t out_ld, int64_t batch, int heads, int kv_heads, int head_dim, int64_t pos,
+                          int64_t max_seq, float theta, void* scratch, size_t scratch_bytes) {
+  if (pos < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "rope_attention: negative position");
+  return attention_impl(ctx, qkv, ld, k_cache, v_cache, out, out_ld, batch, heads, kv_heads, head_dim, pos + 1,
+                        max_seq, scratch, scratch_bytes, true, theta);
 }
 
 int kq_dec_swiglu(kq_ctx* ctx, const float* gate_up, float* out, int64_t batch, int64_t ffn, int mode) {
@@ -840,6 +895,69 @@ int kq_dec_add(kq_ctx* ctx, float* h, int64_t h_ld, const float* y, int64_t y_ld
   DeviceGuard g(ctx->device);
   ctx->launches += rows * cols > 0;
   return dec_status(ctx, kq::dec_add(h, h_ld, y, y_ld, rows, cols, ctx->stream), "add");
+}
+
+// Shared checks of the fused single-token linears.
+static int fused_linear(kq_ctx* ctx, const kq_weight* w, const kq::XsInput& in, const float* bias, float* y,
+                        int flags, const char* what) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!w || !in.x || !y) return fail(ctx, KQ_ERR_INVALID_ARG, "%s: null weight, input or output", what);
+  if (flags & ~(KQ_SYNC | KQ_DEVICE_PTRS)) return fail(ctx, KQ_ERR_INVALID_ARG, "%s: bad flags 0x%x", what, flags);
+  if (w->device != ctx->device)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device, ctx->device);
+  if (!is_gguf(w->dw.type)) return fail(ctx, KQ_ERR_UNSUPPORTED, "%s needs a GGUF Q4_K / Q6_K weight", what);
+  const uintptr_t x16 = reinterpret_cast<uintptr_t>(in.x) | reinterpret_cast<uintptr_t>(in.x2) |
+                        reinterpret_cast<uintptr_t>(in.nw);
+  if ((x16 & 15) || ((reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(bias)) & 3))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "%s: inputs must be 16-byte aligned, y and bias 4-byte aligned", what);
+  DeviceGuard g(ctx->device);
+  if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
+  const kq::Prefetch* pf = ctx->take_prefetch();
+  int launches = 0;
+  const cudaError_t e = kq::launch_gemv_xs(w->dw, in, bias, y, ctx->num_sms, ctx->dev_err, pf, ctx->stream,
+                                           &launches, ctx->next_bracket());
+  ctx->launches += launches;
+  if (e == cudaErrorNotSupported)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "%s: in_features %lld is beyond the single-token kernel", what,
+                (long long)w->dw.k);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  if (flags & KQ_SYNC) return finish_sync(ctx, what);
+  return KQ_OK;
+}
+
+int kq_dec_norm_linear(kq_ctx* ctx, const kq_weight* w, const float* x, const float* norm_w, int64_t dim, float eps,
+                       const float* bias, float* y, int flags) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!norm_w) return fail(ctx, KQ_ERR_INVALID_ARG, "norm_linear: null norm weights");
+  if (!w || dim < 4 || (dim & 3) || dim > w->dw.k)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "norm_linear: dim %lld must be a positive multiple of 4 <= in_features",
+                (long long)dim);
+  kq::XsInput in;
+  in.mode = kq::XS_X_NORM;
+  in.x = x;
+  in.nw = norm_w;
+  in.dim = (int)dim;
+  in.eps = eps;
+  return fused_linear(ctx, w, in, bias, y, flags, "norm_linear");
+}
+
+int kq_dec_swiglu_linear(kq_ctx* ctx, const kq_weight* w, const float* gate_up, int mode, const float* bias,
+                         float* y, int flags) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (mode != 0 && mode != 1) return fail(ctx, KQ_ERR_INVALID_ARG, "swiglu_linear: mode %d", mode);
+  if (!w || !gate_up) return fail(ctx, KQ_ERR_INVALID_ARG, "swiglu_linear: null weight or input");
+  kq::XsInput in;
+  in.mode = kq::XS_X_SWIGLU;
+  in.x = gate_up;
+  in.x2 = gate_up + w->dw.k;
+  in.act = mode;
+  return fused_linear(ctx, w, in, bias, y, flags, "swiglu_linear");
+}
+
+int kq_dec_residual_linear(kq_ctx* ctx, const kq_weight* w, const float* x, float* h, int flags) {
+  kq::XsInput in;
+  in.x = x;
+  return fused_linear(ctx, w, in, h, h, flags, "residual_linear");
 }
 
 int kq_dec_embed(kq_ctx* ctx, const float* table, const int32_t* tokens, float* out, int64_t out_ld, int64_t batch,

@@ -91,4 +91,14 @@ __device__ __forceinline__ float4 ldg_f4(const float* p) {
   return __ldg(reinterpret_cast<const float4*>(p));
 }
 
+// Gate activation of the SwiGLU FFN: act(g) * u with act(g) = s(g) * g.
+// mode 1: s is the logistic sigmoid (SiLU).  mode 0 follows pesti-runner's
+// layer.rs:16-29 as written: for g < 0 it uses g / (1 + e^g) in place of the
+// sigmoid.  Both kernels that apply it (the SwiGLU kernel and the fused
+// single-token GEMV) call this one function.
+__device__ __forceinline__ float swiglu_gate(float g, int mode) {
+  const float sg = (g >= 0.f || mode == 1) ? 1.f / (1.f + expf(-g)) : g / (1.f + expf(g));
+  return sg * g;
+}
+
 }  // namespace kq

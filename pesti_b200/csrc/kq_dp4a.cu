@@ -542,6 +542,7 @@ constexpr int XS_MAX_SMEM = 227 * 1024;
 constexpr int64_t XS_INFLIGHT = 144 * 1024;  // ring bytes in flight per CTA
 
 enum : int { XS_ERR_FULL = 21, XS_ERR_EMPTY = 22, XS_ERR_DRAIN = 23 };
+constexpr int64_t XS_PF_CHUNK = 64 * 1024;  // bytes per L2 prefetch instruction
 
 struct XsParams {
   const uint8_t* q;     // [n][row_bytes]
@@ -552,16 +553,26 @@ struct XsParams {
   int rows_max;         // most rows any CTA owns (shared-memory sizing)
   int64_t stage_bytes;  // 2G * (row_bytes + d_row_bytes)
   const float* x;
-  const float* bias;
+  const float* bias;  // may alias y (residual update)
   float* y;
   int* err;
+  // activation source: XS_X_NORM x / sqrt(mean(x[0:dim]^2) + eps) * nw (zero past dim);
+  // XS_X_SWIGLU act(x) * x2 with the decoder's gate activation `act`
+  const float* x2;
+  const float* nw;
+  int dim;
+  float eps;
+  int act;
+  // L2 prefetch of the weight the next kernel reads: two byte ranges, split over the CTAs
+  const uint8_t* pf[2];
+  int64_t pf_bytes[2];
 };
 
 // Dynamic shared memory: ring | staged x: words uint4 [sb8 * 4 units][8]
 // (swizzled), sums (Q4_K float2 / Q6_K int4[4] per unit), 2^e per superblock
-// | row partials [rows_max][nk] | full[S], empty[S].
+// | row partials [rows_max][nk] | 32 reduction floats | full[S], empty[S].
 struct XsSmem {
-  size_t ring, xw, sums, xsf, part, bar, end;
+  size_t ring, xw, sums, xsf, part, red, bar, end;
   __host__ __device__ XsSmem(int qt, int nk, int64_t stage_bytes, int S, int rows_max) {
     const size_t units = (size_t)XS_SPW * nk * 4;
     ring = 0;
@@ -569,7 +580,8 @@ struct XsSmem {
     sums = xw + units * 128;
     xsf = sums + units * (qt == GGUF_Q4_K ? 8 : 64);
     part = xsf + units;  // one float per superblock = units / 4 floats
-    bar = (part + (size_t)rows_max * nk * 4 + 7) & ~size_t(7);
+    red = (part + (size_t)rows_max * nk * 4 + 15) & ~size_t(15);
+    bar = red + 32 * 4;
     end = bar + (size_t)2 * S * 8;
   }
 };
@@ -601,12 +613,28 @@ __device__ __forceinline__ bool xs_bar_wait(uint64_t* b, uint32_t par, int* err,
   atomicCAS(err, 0, code);
   return false;
 }
-// Global -> shared bulk copy completing on mbarrier b (no multicast).
-__device__ __forceinline__ void xs_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_addr(dst)),
-               "l"(src), "r"(bytes), "r"(smem_addr(b))
-               : "memory");
+// Global -> shared bulk copy completing on mbarrier b (no multicast), with an
+// L2 eviction policy (the weights are read once per call: evict first).
+__device__ __forceinline__ void xs_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(b)), "l"(pol)
+      : "memory");
+}
+// This CTA's share of the next weight's bytes into L2 (16-byte units only:
+// nothing past the end of a range is touched).
+__device__ __forceinline__ void xs_prefetch(const XsParams& P, int b, int C) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    if (!P.pf[r] || P.pf_bytes[r] < 16) continue;
+    const int64_t units = P.pf_bytes[r] / 16;
+    const int64_t u0 = units * b / C, u1 = units * (b + 1) / C;
+    for (int64_t u = u0; u < u1; u += XS_PF_CHUNK / 16) {
+      const uint32_t bytes = (uint32_t)((XS_PF_CHUNK / 16 < u1 - u ? XS_PF_CHUNK / 16 : u1 - u) * 16);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(P.pf[r] + u * 16), "r"(bytes) : "memory");
+    }
+  }
 }
 __device__ __forceinline__ void xs_named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -655,11 +683,32 @@ __device__ __forceinline__ int xs_swz(int kb, int u) { return (u + 4 * (kb & 1))
 // Quantize x into shared memory: half-unit hu = 8 kb + 2 u + hf (32 weights)
 // per thread of the `nthreads` compute threads, the 8 half-units of a
 // superblock on consecutive lanes, written in the order lanes read them.
-template <int QT>
+// XS_X_NORM first reduces sum(x^2) over the CTA (every CTA does it: the
+// vector is small and L2-resident); XS_X_SWIGLU applies the gate per element.
+template <int QT, int XM>
 __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, uint8_t* smem, int nthreads) {
   uint4* xw = reinterpret_cast<uint4*>(smem + L.xw);
   float* xsf = reinterpret_cast<float*>(smem + L.xsf);
   const int lane = threadIdx.x & 31;
+  float rms = 1.f;
+  if constexpr (XM == XS_X_NORM) {
+    float ss = 0.f;
+    for (int i = 4 * threadIdx.x; i < P.dim; i += 4 * nthreads) {
+      const float4 f = ldg_f4(P.x + i);
+      ss = fmaf(f.x, f.x, ss);
+      ss = fmaf(f.y, f.y, ss);
+      ss = fmaf(f.z, f.z, ss);
+      ss = fmaf(f.w, f.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    float* red = reinterpret_cast<float*>(smem + L.red);
+    if (lane == 0) red[threadIdx.x >> 5] = ss;
+    xs_named_sync(1, nthreads);
+    float t = 0.f;
+    for (int w = 0; w < (nthreads >> 5); ++w) t += red[w];
+    rms = sqrtf(t / (float)P.dim + P.eps);
+  }
   const int total = XS_SPW * P.nk * 8;  // multiple of 64
   for (int base = (threadIdx.x & ~31); base < total; base += nthreads) {
     const int hu = base + lane;
@@ -673,7 +722,27 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
       if constexpr (QT == GGUF_Q4_K) off = 64 * u + 16 * hf + (i < 4 ? 4 * i : 32 + 4 * (i - 4));
       else off = 128 * hf + 32 * (i >> 1) + 8 * u + 4 * (i & 1);
       float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (live) f = ldg_f4(xr + off);
+      if constexpr (XM == XS_X_PLAIN) {
+        if (live) f = ldg_f4(xr + off);
+      } else if constexpr (XM == XS_X_NORM) {
+        const int64_t gi = (int64_t)kb * 256 + off;
+        if (live && gi < P.dim) {
+          f = ldg_f4(xr + off);
+          const float4 wv = ldg_f4(P.nw + gi);
+          f.x = f.x / rms * wv.x;
+          f.y = f.y / rms * wv.y;
+          f.z = f.z / rms * wv.z;
+          f.w = f.w / rms * wv.w;
+        }
+      } else {
+        if (live) {
+          const float4 g = ldg_f4(xr + off), uu = ldg_f4(P.x2 + (int64_t)kb * 256 + off);
+          f.x = swiglu_gate(g.x, P.act) * uu.x;
+          f.y = swiglu_gate(g.y, P.act) * uu.y;
+          f.z = swiglu_gate(g.z, P.act) * uu.z;
+          f.w = swiglu_gate(g.w, P.act) * uu.w;
+        }
+      }
       v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
     }
     float amax = 0.f;
@@ -732,7 +801,7 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
   }
 }
 
-template <int QT>
+template <int QT, int XM>
 __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(const XsParams P) {
   extern __shared__ __align__(128) uint8_t xs_smem[];
   pdl_trigger();  // the next kernel's CTAs may start on each SM as ours retire there
@@ -758,8 +827,13 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   if (warp == NC) {
     // ---------------- producer: the weights do not depend on the previous kernel ----------------
     if (lane == 0) {
+      uint64_t pol;
+      asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+      // the next weight is prefetched once the ring's first fill is issued
+      const int fill = min(T, P.S);
       int t = 0;
       for (; t < T; ++t) {
+        if (t == fill) xs_prefetch(P, b, C);
         const int st = t % P.S;
         if (t >= P.S && !xs_bar_wait(&empty[st], ((t / P.S) - 1) & 1, P.err, XS_ERR_EMPTY)) break;
         const int nr = min(R, rows - t * R);
@@ -767,11 +841,12 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
         uint8_t* dst = xs_smem + L.ring + (size_t)st * (size_t)P.stage_bytes;
         const uint32_t wb = (uint32_t)(nr * P.row_bytes), db = (uint32_t)(nr * P.d_row_bytes);
         xs_bar_expect(&full[st], wb + db);
-        xs_bulk_g2s(dst, P.q + row * P.row_bytes, wb, &full[st]);
+        xs_bulk_g2s(dst, P.q + row * P.row_bytes, wb, &full[st], pol);
         if constexpr (QT == GGUF_Q6_K)
           xs_bulk_g2s(dst + (size_t)R * P.row_bytes, reinterpret_cast<const uint8_t*>(P.d) + row * P.d_row_bytes,
-                      db, &full[st]);
+                      db, &full[st], pol);
       }
+      if (t == fill && t == T) xs_prefetch(P, b, C);
       // the CTA must not retire while a copy into its shared memory is in flight
       for (int v = max(0, t - P.S); v < t; ++v) xs_bar_wait(&full[v % P.S], (v / P.S) & 1, P.err, XS_ERR_DRAIN);
     }
@@ -783,7 +858,7 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   const int kb = XS_SPW * s + (lane >> 2), u = lane & 3;
   const bool live = kb < P.sb;
   pdl_wait();  // x may be the previous kernel's output
-  xs_stage_x<QT>(P, L, xs_smem, NC * 32);
+  xs_stage_x<QT, XM>(P, L, xs_smem, NC * 32);
   xs_named_sync(1, NC * 32);
 
   // this lane's 64 activations, from the staged copy
@@ -972,8 +1047,8 @@ XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms) {
 }
 
 template <int QT>
-cudaError_t launch_xs(const DevWeight& w, const float* x, const float* bias, float* y, int* err, cudaStream_t s,
-                      const XsLaunch& sh) {
+cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, float* y, int* err,
+                      const Prefetch* pf, cudaStream_t s, const XsLaunch& sh) {
   XsParams P;
   P.q = w.q;
   P.d = w.d;
@@ -986,10 +1061,19 @@ cudaError_t launch_xs(const DevWeight& w, const float* x, const float* bias, flo
   P.S = sh.S;
   P.rows_max = sh.rows_max;
   P.stage_bytes = sh.stage_bytes;
-  P.x = x;
+  P.x = in.x;
   P.bias = bias;
   P.y = y;
   P.err = err;
+  P.x2 = in.x2;
+  P.nw = in.nw;
+  P.dim = in.dim;
+  P.eps = in.eps;
+  P.act = in.act;
+  for (int r = 0; r < 2; ++r) {
+    P.pf[r] = pf ? static_cast<const uint8_t*>(pf->p[r]) : nullptr;
+    P.pf_bytes[r] = pf && pf->p[r] ? pf->bytes[r] : 0;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sh.grid);
   cfg.blockDim = dim3((unsigned)sh.threads);
@@ -1000,7 +1084,12 @@ cudaError_t launch_xs(const DevWeight& w, const float* x, const float* bias, flo
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT>, P);
+  switch (in.mode) {
+    case XS_X_PLAIN: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN>, P);
+    case XS_X_NORM: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_NORM>, P);
+    case XS_X_SWIGLU: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_SWIGLU>, P);
+  }
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace
@@ -1047,12 +1136,37 @@ cudaError_t launch_gemv_dp4a_batched(const DevWeight& w, const float* x, int64_t
   return cudaErrorInvalidValue;
 }
 
-cudaError_t dp4a_init_device() {
-  cudaError_t e = cudaFuncSetAttribute(xs_gemv_kernel<GGUF_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <int QT>
+static cudaError_t xs_attrs() {
+  cudaError_t e = cudaFuncSetAttribute(xs_gemv_kernel<QT, XS_X_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        XS_MAX_SMEM);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(xs_gemv_kernel<GGUF_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, XS_MAX_SMEM);
+    e = cudaFuncSetAttribute(xs_gemv_kernel<QT, XS_X_NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, XS_MAX_SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(xs_gemv_kernel<QT, XS_X_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             XS_MAX_SMEM);
   return e;
+}
+
+cudaError_t dp4a_init_device() {
+  cudaError_t e = xs_attrs<GGUF_Q4_K>();
+  if (e == cudaSuccess) e = xs_attrs<GGUF_Q6_K>();
+  return e;
+}
+
+cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* bias, float* y, int num_sms, int* err,
+                           const Prefetch* pf, cudaStream_t s, int* launches, Bracket br) {
+  if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
+  if (in.mode < XS_X_PLAIN || in.mode > XS_X_SWIGLU) return cudaErrorInvalidValue;
+  const XsLaunch sh = xs_shape(w.type, w.n, w.sb, num_sms);
+  if (!sh.ok) return cudaErrorNotSupported;
+  bracket_record(br.start, s);
+  cudaError_t e = w.type == GGUF_Q4_K ? launch_xs<GGUF_Q4_K>(w, in, bias, y, err, pf, s, sh)
+                                      : launch_xs<GGUF_Q6_K>(w, in, bias, y, err, pf, s, sh);
+  if (e != cudaSuccess) return e;
+  if (launches) ++*launches;
+  bracket_record(br.stop, s);
+  return cudaSuccess;
 }
 
 size_t dp4a_workspace_bytes(int type, int64_t m, int64_t sb) {
@@ -1062,19 +1176,13 @@ size_t dp4a_workspace_bytes(int type, int64_t m, int64_t sb) {
 }
 
 cudaError_t launch_gemv_dp4a(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y, void* ws,
-                             int num_sms, int* err, cudaStream_t s, int* launches, Bracket br) {
+                             int num_sms, int* err, cudaStream_t s, int* launches, Bracket br, const Prefetch* pf) {
   if (m < 1 || m > DP4A_MAX_M) return cudaErrorInvalidValue;
-  if (m == 1 && (w.type == GGUF_Q4_K || w.type == GGUF_Q6_K)) {
-    const XsLaunch sh = xs_shape(w.type, w.n, w.sb, num_sms);
-    if (sh.ok) {
-      bracket_record(br.start, s);
-      cudaError_t e = w.type == GGUF_Q4_K ? launch_xs<GGUF_Q4_K>(w, x, bias, y, err, s, sh)
-                                          : launch_xs<GGUF_Q6_K>(w, x, bias, y, err, s, sh);
-      if (e != cudaSuccess) return e;
-      if (launches) ++*launches;
-      bracket_record(br.stop, s);
-      return cudaSuccess;
-    }
+  if (m == 1) {
+    XsInput in;
+    in.x = x;
+    const cudaError_t e = launch_gemv_xs(w, in, bias, y, num_sms, err, pf, s, launches, br);
+    if (e != cudaErrorNotSupported) return e;
   }
   if (w.type == GGUF_Q4_K) return launch_typed<GGUF_Q4_K>(w, x, m, bias, y, ws, num_sms, s, launches, br);
   if (w.type == GGUF_Q6_K) return launch_typed<GGUF_Q6_K>(w, x, m, bias, y, ws, num_sms, s, launches, br);

@@ -55,6 +55,25 @@ struct Bracket {
   cudaEvent_t start = nullptr, stop = nullptr;
 };
 
+// Launch with programmatic dependent launch allowed: the kernel may start
+// while its predecessor on the stream finishes; it must execute
+// griddepcontrol.wait before reading anything the predecessor writes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
+
 // Record a timing event; under stream capture it becomes an event-record node
 // of the graph (cudaEventRecordExternal), so graph replays keep timing it.
 inline void bracket_record(cudaEvent_t e, cudaStream_t s) {
@@ -97,10 +116,33 @@ cudaError_t launch_gemv_dp4a_batched(const DevWeight& w, const float* x, int64_t
 // device.  Used by the no-allocation entry point.
 constexpr size_t DP4A_STATIC_SCRATCH = 256 * 1024;
 cudaError_t dp4a_static_scratch(void** ptr);
+// Up to two byte ranges (a weight's quants and, for Q6_K, its d array) the
+// single-token kernel prefetches into L2 while it runs: the weight the next
+// kernel on the stream will read.
+struct Prefetch {
+  const void* p[2] = {nullptr, nullptr};
+  int64_t bytes[2] = {0, 0};
+};
 // *err (device int) receives a nonzero code if a pipeline wait gave up.
 cudaError_t launch_gemv_dp4a(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y,
                              void* ws, int num_sms, int* err, cudaStream_t s, int* launches,
-                             Bracket br = Bracket());
+                             Bracket br = Bracket(), const Prefetch* pf = nullptr);
+// Activation source of the single-token kernel.
+enum : int { XS_X_PLAIN = 0, XS_X_NORM = 1, XS_X_SWIGLU = 2 };
+struct XsInput {
+  int mode = XS_X_PLAIN;
+  const float* x = nullptr;   // [k] (XS_X_SWIGLU: the gate)
+  const float* x2 = nullptr;  // XS_X_SWIGLU: the up projection [k]
+  const float* nw = nullptr;  // XS_X_NORM: norm weights [dim]
+  int dim = 0;                // XS_X_NORM: elements normalised (x and the result are zero past dim)
+  float eps = 0.f;
+  int act = 0;                // XS_X_SWIGLU: gate activation (swiglu_gate)
+};
+// Single-token GEMV y = act(x) . W^T (+bias; bias may alias y) for GGUF
+// Q4_K / Q6_K; cudaErrorNotSupported when the kernel does not apply to the
+// shape (more than 120 superblocks per row).
+cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* bias, float* y, int num_sms, int* err,
+                           const Prefetch* pf, cudaStream_t s, int* launches, Bracket br = Bracket());
 
 // ---- tensor parallel: all-gather of row-sharded outputs over peer memory (kq_tp.cu) ----
 constexpr int TP_MAX_WORLD = 8;
@@ -126,11 +168,19 @@ cudaError_t dec_rmsnorm(const float* x, int64_t x_ld, const float* w, float* out
                         int64_t dim, float eps, cudaStream_t s);
 cudaError_t dec_rope_append(float* qkv, int64_t ld, void* kc, void* vc, int64_t batch, int hq, int hkv, int hd,
                             int64_t pos, int64_t max_seq, float theta, cudaStream_t s);
+// Per-device set-up of the decoder kernels (shared-memory sizes).
+cudaError_t dec_init_device();
 int dec_attention_splits(int64_t batch, int hkv, int64_t len, int num_sms);
-size_t dec_attention_scratch_bytes(int64_t batch, int hq, int hd, int splits);
-cudaError_t dec_attention(const float* q, int64_t q_ld, const void* kc, const void* vc, float* out, int64_t out_ld,
-                          int64_t batch, int hq, int hkv, int hd, int64_t len, int64_t max_seq, float* scratch,
-                          int splits, cudaStream_t s);
+size_t dec_attention_scratch_bytes(int64_t batch, int hq, int hkv, int hd, int splits);
+// Attention of token b's query heads (q + b * q_ld) over cache positions
+// [0, len), one kernel.  rope: q is the fused qkv row; the query heads are
+// rotated in registers and the rotated k and v of position len - 1 are
+// appended to the caches first.  scratch: dec_attention_scratch_bytes,
+// zero-filled before its first use.  *err receives 24 if a tile copy wait
+// gave up (the output is then invalid and the scratch must be re-zeroed).
+cudaError_t dec_attention(const float* q, int64_t q_ld, void* kc, void* vc, float* out, int64_t out_ld,
+                          int64_t batch, int hq, int hkv, int hd, int64_t len, int64_t max_seq, void* scratch,
+                          int splits, bool rope, float theta, int* err, cudaStream_t s);
 cudaError_t dec_swiglu(const float* gu, float* out, int64_t batch, int64_t ffn, int mode, cudaStream_t s);
 cudaError_t dec_add(float* h, int64_t h_ld, const float* y, int64_t y_ld, int64_t rows, int64_t cols,
                     cudaStream_t s);

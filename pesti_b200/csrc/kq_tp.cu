@@ -39,6 +39,10 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 constexpr int ERR_TP_WAIT = 31;
 
 __global__ void __launch_bounds__(512) tp_allgather_kernel(const __grid_constant__ TpArgs A) {
+  // let the next kernel launch (it waits for our completion before reading
+  // the gathered output); wait for the kernel that produced y_local
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // This call's epoch: one more than the last completed call's (a device
   // counter, so CUDA-graph replays advance it); its parity picks the slot.
   __shared__ unsigned epoch_sh;
@@ -107,8 +111,7 @@ __global__ void __launch_bounds__(512) tp_allgather_kernel(const __grid_constant
 
 cudaError_t launch_tp_allgather(const TpArgs& a, int blocks, cudaStream_t s) {
   if (a.world < 1 || a.world > TP_MAX_WORLD || blocks < 1) return cudaErrorInvalidValue;
-  tp_allgather_kernel<<<blocks, 512, 0, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(tp_allgather_kernel, dim3(blocks), dim3(512), 0, s, a);
 }
 
 }  // namespace kq

@@ -74,6 +74,10 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "kq_dec_swiglu": [P, P, P, I64, I64, I],
         "kq_dec_add": [P, P, I64, P, I64, I64, I64],
         "kq_dec_embed": [P, P, P, P, I64, I64, I64],
+        "kq_dec_norm_linear": [P, P, P, P, I64, F, P, P, I],
+        "kq_dec_swiglu_linear": [P, P, P, I, P, P, I],
+        "kq_dec_residual_linear": [P, P, P, P, I],
+        "kq_dec_rope_attention": [P, P, I64, P, P, P, I64, I64, I, I, I, I64, I64, F, P, Z],
     }
     for name, args in sig.items():
         getattr(lib, name).argtypes = args
@@ -119,7 +123,8 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, ctx: "kq.Context", batch: int, context_len: int, max_new: int = 8,
                  world: int = 1, rank: int = 0, tp: Optional["kq.TensorParallel"] = None, seed: int = 0,
-                 swiglu_mode: int = SWIGLU_REFERENCE, kv_scale: float = 1.0, keep_raw: bool = False):
+                 swiglu_mode: int = SWIGLU_REFERENCE, kv_scale: float = 1.0, keep_raw: bool = False,
+                 fused: bool = True, prefetch: bool = True):
         import torch
         if cfg.heads % world or cfg.kv_heads % world:
             raise ValueError(f"{cfg.name}: {cfg.heads} query / {cfg.kv_heads} KV heads do not split over {world}")
@@ -127,6 +132,10 @@ class Decoder:
             raise ValueError("world > 1 needs a TensorParallel group")
         self.cfg, self.ctx, self.batch, self.world, self.rank, self.tp = cfg, ctx, batch, world, rank, tp
         self.swiglu_mode = swiglu_mode
+        # fused: RoPE + KV append + attention in one kernel, and at batch 1
+        # RMSNorm, SwiGLU and the residual adds inside the single-token GEMVs;
+        # prefetch: each linear pulls the next one's weight into L2
+        self.fused_attention, self.fused, self.prefetch = fused, fused and batch == 1, prefetch
         self.lib = _bind(ctx.lib)
         dev = torch.device("cuda", ctx.device)
         self.device = dev
@@ -230,12 +239,15 @@ class Decoder:
         self.logits = z(B, cfg.vocab)
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         sbytes = self.lib.kq_dec_attention_scratch(ctx.handle, B, self.hq, self.hkv, hd, self.max_seq)
-        self.att_scratch = torch.empty(max(sbytes // 4, 1), device=dev)
+        self.att_scratch = torch.zeros(max(sbytes // 4, 1), device=dev)  # counters start at zero
         self.att_scratch_bytes = sbytes
         for L in self.layers:
             for key in ("qkv", "o", "gu", "down"):
                 ctx.reserve(L[key], B)
         ctx.reserve(self.head, B)
+        # the weights in the order a step reads them; _next[id] is the one after
+        order = [L[key] for L in self.layers for key in ("qkv", "o", "gu", "down")] + [self.head]
+        self._next = {id(a): b for a, b in zip(order, order[1:] + [None])}
         torch.cuda.synchronize(dev)
 
     # ---- one decode step ------------------------------------------------------------
@@ -244,6 +256,24 @@ class Decoder:
 
     def _gather(self, src, cols, row0, rows, dst, ld, accumulate):
         self.tp.allgather(src, self.batch, row0, rows, cols, dst, y_ld=ld, accumulate=accumulate)
+
+    def _hint(self, w) -> None:
+        """Tell the next linear call on the context which weight follows `w`."""
+        if self.prefetch:
+            self.ctx.prefetch_next(self._next[id(w)])
+
+    def _norm_linear(self, w, norm, y) -> None:
+        """y = rmsnorm(h; norm) . W^T (token 0 only when fused)."""
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        c, cfg = self.ctx.handle, self.cfg
+        self._hint(w)
+        if self.fused:
+            self._check(self.lib.kq_dec_norm_linear(c, w.handle, ptr(self.h), ptr(norm), cfg.dim, cfg.eps, None,
+                                                    ptr(y), 0), "norm_linear")
+            return
+        self._check(self.lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(norm), ptr(self.a), self.Dp, self.batch,
+                                            cfg.dim, cfg.eps), "rmsnorm")
+        w.linear(self.a, self.batch, y, device_ptrs=True)
 
     def step(self, pos: int) -> None:
         """Queue one decode step for the tokens in ``self.tokens`` at position
@@ -259,26 +289,37 @@ class Decoder:
         tp = self.world > 1
         self._check(lib.kq_dec_embed(c, ptr(self.embed), ptr(self.tokens), ptr(self.h), self.Dp, B, D), "embed")
         for L in self.layers:
-            self._check(lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(L["attn_norm"]), ptr(self.a), self.Dp, B, D,
-                                           cfg.eps), "rmsnorm")
-            L["qkv"].linear(self.a, B, self.qkv, device_ptrs=True)
-            self._check(lib.kq_dec_rope_append(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]), B, self.hq,
-                                               self.hkv, hd, pos, self.max_seq, cfg.theta), "rope")
+            self._norm_linear(L["qkv"], L["attn_norm"], self.qkv)
             out, out_ld = (self.attn_r, self.hq * hd) if tp else (self.attn, self.Ap)
-            self._check(lib.kq_dec_attention(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]), ptr(out), out_ld,
-                                             B, self.hq, self.hkv, hd, pos + 1, self.max_seq, ptr(self.att_scratch),
-                                             self.att_scratch_bytes), "attention")
+            if self.fused_attention:
+                self._check(lib.kq_dec_rope_attention(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]),
+                                                      ptr(out), out_ld, B, self.hq, self.hkv, hd, pos, self.max_seq,
+                                                      cfg.theta, ptr(self.att_scratch), self.att_scratch_bytes),
+                            "rope_attention")
+            else:
+                self._check(lib.kq_dec_rope_append(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]), B,
+                                                   self.hq, self.hkv, hd, pos, self.max_seq, cfg.theta), "rope")
+                self._check(lib.kq_dec_attention(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]), ptr(out),
+                                                 out_ld, B, self.hq, self.hkv, hd, pos + 1, self.max_seq,
+                                                 ptr(self.att_scratch), self.att_scratch_bytes), "attention")
             if tp:
                 self._gather(self.attn_r, cfg.heads * hd, self.rank * self.hq * hd, self.hq * hd, self.attn, self.Ap,
                              False)
-            L["o"].linear(self.attn, B, self.o, device_ptrs=True)
+            self._hint(L["o"])
             if tp:
+                L["o"].linear(self.attn, B, self.o, device_ptrs=True)
                 self._gather(self.o, D, r0, r1 - r0, self.h, self.Dp, True)
+            elif self.fused:
+                self._check(lib.kq_dec_residual_linear(c, L["o"].handle, ptr(self.attn), ptr(self.h), 0), "o")
             else:
+                L["o"].linear(self.attn, B, self.o, device_ptrs=True)
                 self._check(lib.kq_dec_add(c, ptr(self.h), self.Dp, ptr(self.o), D, B, D), "add")
-            self._check(lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(L["ffn_norm"]), ptr(self.a), self.Dp, B, D,
-                                           cfg.eps), "rmsnorm")
-            L["gu"].linear(self.a, B, self.gu, device_ptrs=True)
+            self._norm_linear(L["gu"], L["ffn_norm"], self.gu)
+            self._hint(L["down"])
+            if self.fused and not tp:
+                self._check(lib.kq_dec_swiglu_linear(c, L["down"].handle, ptr(self.gu), self.swiglu_mode,
+                                                     ptr(self.h), ptr(self.h), 0), "swiglu_linear")
+                continue
             self._check(lib.kq_dec_swiglu(c, ptr(self.gu), ptr(self.s_r if tp else self.s), B, f1 - f0,
                                           self.swiglu_mode), "swiglu")
             if tp:
@@ -288,17 +329,15 @@ class Decoder:
                 self._gather(self.dn, D, r0, r1 - r0, self.h, self.Dp, True)
             else:
                 self._check(lib.kq_dec_add(c, ptr(self.h), self.Dp, ptr(self.dn), D, B, D), "add")
-        x = self.h
-        if self.final_norm is not None:
-            self._check(lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(self.final_norm), ptr(self.a), self.Dp, B, D,
-                                           cfg.eps), "rmsnorm")
-            x = self.a
         v0, v1 = self.v_rows
-        if tp:
-            self.head.linear(x, B, self.logits_r, device_ptrs=True)
-            self._gather(self.logits_r, cfg.vocab, v0, v1 - v0, self.logits, cfg.vocab, False)
+        logits = self.logits_r if tp else self.logits
+        if self.final_norm is not None:
+            self._norm_linear(self.head, self.final_norm, logits)
         else:
-            self.head.linear(x, B, self.logits, device_ptrs=True)
+            self._hint(self.head)
+            self.head.linear(self.h, B, logits, device_ptrs=True)
+        if tp:
+            self._gather(self.logits_r, cfg.vocab, v0, v1 - v0, self.logits, cfg.vocab, False)
 
     def weight_bytes(self) -> int:
         """HBM bytes of this rank's quantized weights."""

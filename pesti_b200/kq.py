@@ -55,12 +55,13 @@ KQ_PATH_DP4A = 3
 EXPORTED_SYMBOLS = (
     "kq_abi_version", "kq_status_string", "kq_last_error",
     "kq_ctx_create", "kq_ctx_destroy", "kq_ctx_set_stream", "kq_ctx_synchronize",
-    "kq_ctx_set_path", "kq_ctx_reserve", "kq_ctx_launch_count", "kq_ctx_profile_begin",
+    "kq_ctx_set_path", "kq_ctx_reserve", "kq_ctx_prefetch_next", "kq_ctx_launch_count", "kq_ctx_profile_begin",
     "kq_ctx_profile_end", "kq_ctx_profile_read", "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
     "kq_linear_f32", "kq_linear_bf16", "kq_linear_f32_static", "kq_dequant_f32",
     "kq_tp_create", "kq_tp_handle", "kq_tp_open", "kq_tp_linear_f32", "kq_tp_allgather_f32",
     "kq_tp_destroy", "kq_dec_rmsnorm", "kq_dec_rope_append", "kq_dec_attention_scratch", "kq_dec_attention",
-    "kq_dec_swiglu", "kq_dec_add", "kq_dec_embed",
+    "kq_dec_swiglu", "kq_dec_add", "kq_dec_embed", "kq_dec_norm_linear", "kq_dec_swiglu_linear",
+    "kq_dec_residual_linear", "kq_dec_rope_attention",
 )
 
 
@@ -102,6 +103,7 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
             "kq_ctx_synchronize": ([P], I),
             "kq_ctx_set_path": ([P, I], I),
             "kq_ctx_reserve": ([P, P, I64], I),
+            "kq_ctx_prefetch_next": ([P, P], I),
             "kq_ctx_launch_count": ([P], I64),
             "kq_ctx_profile_begin": ([P, I], I),
             "kq_ctx_profile_end": ([P, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(I64)], I),
@@ -184,6 +186,11 @@ class Context:
     def reserve(self, weight: "Weight", m: int) -> None:
         """Allocate the scratch calls on `weight` with up to m rows need."""
         self.check(self.lib.kq_ctx_reserve(self.handle, weight.handle, m), "kq_ctx_reserve")
+
+    def prefetch_next(self, weight: Optional["Weight"]) -> None:
+        """The next linear call prefetches `weight` into L2 (one-shot hint; None clears)."""
+        self.check(self.lib.kq_ctx_prefetch_next(self.handle, weight.handle if weight is not None else None),
+                   "kq_ctx_prefetch_next")
 
     @property
     def launch_count(self) -> int:

@@ -31,15 +31,19 @@ def _oracle_caches(model, cfg):
     return ks, vs
 
 
+# batch 1 runs the fused single-token linears (RMSNorm / SwiGLU / residual
+# inside the GEMV), batch 2 the separate kernels; "unfused" forces the latter at batch 1
 @pytest.mark.parametrize("cfg", [QWEN_TINY, LLAMA_TINY], ids=lambda c: c.name)
 @pytest.mark.parametrize("mode", [dec.SWIGLU_REFERENCE, dec.SWIGLU_SILU])
-def test_decode_steps_match_the_restated_reference(gpu_ctx, cfg, mode):
+@pytest.mark.parametrize("batch,fused", [(1, True), (1, False), (2, True)], ids=["b1", "b1-unfused", "b2"])
+def test_decode_steps_match_the_restated_reference(gpu_ctx, cfg, mode, batch, fused):
     import torch
     from oracle import decoder_oracle
-    batch, ctx_len = 2, 20
-    model = dec.Decoder(cfg, gpu_ctx, batch, ctx_len, max_new=4, seed=5, swiglu_mode=mode, keep_raw=True)
+    ctx_len = 20
+    model = dec.Decoder(cfg, gpu_ctx, batch, ctx_len, max_new=4, seed=5, swiglu_mode=mode, keep_raw=True,
+                        fused=fused)
     ks, vs = _oracle_caches(model, cfg)
-    for step, toks in enumerate(([3, 250], [17, 9])):
+    for step, toks in enumerate(([3, 250][:batch], [17, 9][:batch])):
         pos = ctx_len + step
         model.tokens.copy_(torch.tensor(toks, dtype=torch.int32))
         model.step(pos)
@@ -51,11 +55,12 @@ def test_decode_steps_match_the_restated_reference(gpu_ctx, cfg, mode):
     model.close()
 
 
-def test_decode_step_replays_from_a_cuda_graph(gpu_ctx):
+@pytest.mark.parametrize("batch", [1, 2])
+def test_decode_step_replays_from_a_cuda_graph(gpu_ctx, batch):
     import torch
     cfg = LLAMA_TINY
-    model = dec.Decoder(cfg, gpu_ctx, 2, 20, max_new=2, seed=6)
-    model.tokens.copy_(torch.tensor([1, 2], dtype=torch.int32))
+    model = dec.Decoder(cfg, gpu_ctx, batch, 20, max_new=2, seed=6)
+    model.tokens.copy_(torch.tensor([1, 2][:batch], dtype=torch.int32))
     s = torch.cuda.Stream()
     gpu_ctx.set_stream(s.cuda_stream)
     try:
@@ -110,17 +115,18 @@ def _tp_worker(rank, world, port, out_dir):
         cfg = LLAMA_TINY
         ctx = kq.Context(rank)
         tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, 2))
-        model = dec.Decoder(cfg, ctx, 2, 20, max_new=2, world=world, rank=rank, tp=tp, seed=7)
-        single = dec.Decoder(cfg, ctx, 2, 20, max_new=2, seed=7)
-        for m in (model, single):
-            m.tokens.copy_(torch.tensor([4, 5], dtype=torch.int32))
-            m.step(20)
-        ctx.synchronize()
-        a, b = model.logits.cpu().numpy(), single.logits.cpu().numpy()
-        if not np.isfinite(a).all() or rel_err(a, b) > 1e-5:
-            status = f"tensor-parallel logits differ: {rel_err(a, b):.2e}"
-        model.close()
-        single.close()
+        for batch in (1, 2):
+            model = dec.Decoder(cfg, ctx, batch, 20, max_new=2, world=world, rank=rank, tp=tp, seed=7)
+            single = dec.Decoder(cfg, ctx, batch, 20, max_new=2, seed=7)
+            for m in (model, single):
+                m.tokens.copy_(torch.tensor([4, 5][:batch], dtype=torch.int32))
+                m.step(20)
+            ctx.synchronize()
+            a, b = model.logits.cpu().numpy(), single.logits.cpu().numpy()
+            if not np.isfinite(a).all() or rel_err(a, b) > 1e-5:
+                status = f"batch {batch}: tensor-parallel logits differ: {rel_err(a, b):.2e}"
+            model.close()
+            single.close()
         tp.close()
         ctx.close()
     except Exception as e:

@@ -1,0 +1,137 @@
+"""Single-token linears with the decoder's activation transform fused into
+the GEMV's activation staging (kq_dec_norm_linear, kq_dec_swiglu_linear,
+kq_dec_residual_linear) and the L2 prefetch hint (kq_ctx_prefetch_next),
+against the oracle: RMSNorm / SwiGLU restated from pesti's transformer
+(oracle/decoder_oracle.py) followed by the GGUF dequantization and an f64
+product."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from oracle import decoder_oracle
+from pesti_b200 import decoder as dec
+from pesti_b200 import kq, synthetic
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-3  # max|y - yref| / max|yref|, as for the plain GEMV
+GGUF = {"Q4_K": (kq.KQ_GGUF_Q4_K, oracle.GGUF_Q4_K), "Q6_K": (kq.KQ_GGUF_Q6_K, oracle.GGUF_Q6_K)}
+
+
+def rel_err(y, ref):
+    y = np.asarray(y, np.float64).reshape(-1)
+    ref = np.asarray(ref, np.float64).reshape(-1)
+    return float(np.max(np.abs(y - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def _lib(ctx):
+    return dec._bind(ctx.lib)
+
+
+def _dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _w64(ot, raw, n, k):
+    return oracle.gguf_dequant_rows(ot, raw, n, k).astype(np.float64)
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("n,k,dim", [(256, 1024, 896), (300, 4096, 4096), (64, 14336, 14336)])
+def test_norm_linear_matches_rmsnorm_then_linear(gpu_ctx, dt, n, k, dim):
+    kt, ot = GGUF[dt]
+    rng = np.random.default_rng(n + k)
+    raw = synthetic.gguf_weight(kt, n, k, seed=k)
+    h = np.zeros((1, k), np.float32)
+    h[0, :dim] = 3.0 * rng.standard_normal(dim)
+    nw = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    hd, nwd, yd = _dev(h), _dev(nw), _dev(np.full((1, n), np.nan, np.float32))
+    rc = _lib(gpu_ctx).kq_dec_norm_linear(gpu_ctx.handle, w.handle, _p(hd), _p(nwd), dim, 1e-5, None, _p(yd), kq.KQ_SYNC)
+    gpu_ctx.check(rc, "norm_linear")
+    a = np.zeros((1, k), np.float32)
+    a[0, :dim] = decoder_oracle.rmsnorm(h[:, :dim], nw, 1e-5)
+    ref = a.astype(np.float64) @ _w64(ot, raw, n, k).T
+    assert rel_err(yd.cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("mode", [dec.SWIGLU_REFERENCE, dec.SWIGLU_SILU])
+def test_swiglu_linear_with_residual(gpu_ctx, dt, mode):
+    kt, ot = GGUF[dt]
+    n, k = 512, 4864
+    rng = np.random.default_rng(mode + 7)
+    raw = synthetic.gguf_weight(kt, n, k, seed=11)
+    gu = (2.0 * rng.standard_normal((1, 2 * k))).astype(np.float32)
+    h = rng.standard_normal((1, n)).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    gud, hd = _dev(gu), _dev(h)
+    rc = _lib(gpu_ctx).kq_dec_swiglu_linear(gpu_ctx.handle, w.handle, _p(gud), mode, _p(hd), _p(hd), kq.KQ_SYNC)
+    gpu_ctx.check(rc, "swiglu_linear")
+    s = decoder_oracle.swiglu(gu[:, :k], gu[:, k:], mode)
+    ref = h.astype(np.float64) + s.astype(np.float64) @ _w64(ot, raw, n, k).T
+    assert rel_err(hd.cpu().numpy() - h, ref - h) <= TOL
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
+def test_residual_linear_adds_in_place(gpu_ctx, dt):
+    kt, ot = GGUF[dt]
+    n, k = 1000, 2048
+    raw = synthetic.gguf_weight(kt, n, k, seed=3)
+    x = synthetic.activations(1, k, seed=4)
+    h = np.random.default_rng(5).standard_normal((1, n)).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    xd, hd = _dev(x), _dev(h)
+    gpu_ctx.check(_lib(gpu_ctx).kq_dec_residual_linear(gpu_ctx.handle, w.handle, _p(xd), _p(hd), kq.KQ_SYNC),
+                 "residual")
+    prod = x.astype(np.float64) @ _w64(ot, raw, n, k).T
+    assert rel_err(hd.cpu().numpy() - h, prod) <= TOL
+
+
+def test_fused_linears_reject_what_they_cannot_run(gpu_ctx):
+    lib = _lib(gpu_ctx)
+    raw = synthetic.gguf_weight(kq.KQ_GGUF_Q4_K, 8, 256, seed=1)
+    w = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q4_K, raw, 8, 256)
+    x, y = _dev(np.zeros((1, 256), np.float32)), _dev(np.zeros((1, 8), np.float32))
+    h = gpu_ctx.handle
+    assert lib.kq_dec_norm_linear(h, w.handle, _p(x), _p(x), 6, 1e-5, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
+    assert lib.kq_dec_norm_linear(h, w.handle, _p(x), _p(x), 512, 1e-5, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
+    assert lib.kq_dec_swiglu_linear(h, w.handle, _p(x), 2, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
+    assert lib.kq_dec_residual_linear(h, w.handle, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
+    # a row too long for the single-token kernel (121 superblocks)
+    kb = 121 * 256
+    big = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q4_K, synthetic.gguf_weight(kq.KQ_GGUF_Q4_K, 4, kb, seed=2), 4, kb)
+    xb = _dev(np.zeros((1, kb), np.float32))
+    assert lib.kq_dec_residual_linear(h, big.handle, _p(xb), _p(y), 0) == kq.KQ_ERR_UNSUPPORTED
+    gpu_ctx.synchronize()
+
+
+def test_prefetch_hint_leaves_results_unchanged(gpu_ctx):
+    """A linear that prefetches the next weight into L2 computes the same bits,
+    and the hint is consumed by exactly one call."""
+    import torch
+    ws, xs = [], []
+    shapes = [(kq.KQ_GGUF_Q4_K, 700, 4096), (kq.KQ_GGUF_Q6_K, 900, 4096), (kq.KQ_GGUF_Q4_K, 64, 512)]
+    for i, (kt, n, k) in enumerate(shapes):
+        ws.append(kq.Weight(gpu_ctx, kt, synthetic.gguf_weight(kt, n, k, seed=20 + i), n, k))
+        xs.append(_dev(synthetic.activations(1, k, seed=30 + i)))
+    plain = []
+    for w, x in zip(ws, xs):
+        y = torch.empty((1, w.out_features), device="cuda")
+        w.linear(x, 1, y, device_ptrs=True)
+        plain.append(y)
+    for j in range(3):
+        for i, (w, x) in enumerate(zip(ws, xs)):
+            gpu_ctx.prefetch_next(ws[(i + 1 + j) % len(ws)])
+            y = torch.empty_like(plain[i])
+            w.linear(x, 1, y, device_ptrs=True)
+            gpu_ctx.synchronize()
+            assert torch.equal(y, plain[i])
+    gpu_ctx.prefetch_next(None)
