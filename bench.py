@@ -717,8 +717,12 @@ def run_decoder(args, rank, world, local_rank):
                        "head_dim": cfg.head_dim, "ffn": cfg.ffn, "vocab": cfg.vocab, "batch": B,
                        "context": ctx_len, "weight_bytes": int(wb[0]), "kv_bytes_per_step": int(wb[1]),
                        "l2": "inputs larger than L2 (every step streams all weights and the KV cache)",
-                       "parallelism": (f"tensor parallel x{world}: heads, KV cache and row blocks sharded, "
-                                       f"4 all-gathers per layer over NVLink peer memory") if world > 1
+                       "parallelism": ((f"tensor parallel x{world}: heads, KV cache and FFN blocks split; output and "
+                                        f"down projections column-split, their partial residual vectors exchanged "
+                                        f"over NVLink peer memory from inside the GEMVs (2 exchanges per layer)")
+                                       if model.col_split else
+                                       (f"tensor parallel x{world}: heads, KV cache and row blocks sharded, "
+                                        f"4 all-gathers per layer over NVLink peer memory")) if world > 1
                        else "single GPU",
                        "fused": ("RoPE + KV append + attention in one kernel; "
                                  + ("RMSNorm, SwiGLU and residual adds inside the single-token GEMVs"

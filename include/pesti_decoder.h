@@ -71,6 +71,24 @@ int kq_dec_swiglu_linear(kq_ctx *ctx, const kq_weight *w, const float *gate_up, 
                          int flags);
 /* h[0:out_features] += x . W^T (the residual connection fused into the linear). */
 int kq_dec_residual_linear(kq_ctx *ctx, const kq_weight *w, const float *x, float *h, int flags);
+/* Tensor-parallel single-token linears (batch 1) for the column-split
+ * layout: a projection whose input is split across the ranks (the output
+ * projection over this rank's heads, the down projection over its FFN block)
+ * holds W[:, this rank's columns] and produces a partial of the full output;
+ * kq_dec_tp_partial_linear sends that partial to every rank (stores into
+ * their exchange buffers over NVLink, inside the GEMV) and publishes the
+ * exchange.  The next kq_dec_tp_reduce_linear on every rank waits for all
+ * partials, forms h_out = h_in + sum over ranks (rank order: identical on
+ * every rank), then y = [rmsnorm](h_out[0:dim]) . W^T with its own
+ * (row-split or replicated) weight.  Two exchanges per transformer layer.
+ *   partial: act -1 = x as is (in_features floats), 0 / 1 = SwiGLU mode of
+ *            x = [gate | up] (as kq_dec_swiglu_linear); out_features =
+ *            the partial's length.
+ *   reduce:  norm_w NULL = no norm; dim = the partials' length; h_in and
+ *            h_out distinct.  Status codes as kq_dec_norm_linear. */
+int kq_dec_tp_partial_linear(kq_tp *tp, const kq_weight *w, const float *x, int act, int flags);
+int kq_dec_tp_reduce_linear(kq_tp *tp, const kq_weight *w, const float *h_in, float *h_out, const float *norm_w,
+                            int64_t dim, float eps, float *y, int flags);
 /* out[b] = table[tokens[b]] (Model::embed, model.rs:966-984); table f32 [vocab][dim]. */
 int kq_dec_embed(kq_ctx *ctx, const float *table, const int32_t *tokens, float *out, int64_t out_ld,
                  int64_t batch, int64_t dim);

@@ -153,8 +153,9 @@ int kq_dequant_f32(kq_ctx *ctx, const kq_weight *w, int64_t row0, int64_t nrows,
 /* ---- tensor parallel (one process per GPU of one node) ------------------- */
 /* Row-sharded linears whose output slices are all-gathered over NVLink: each
  * rank stores its rows straight into every rank's exchange buffer (CUDA IPC
- * peer memory) and publishes a per-call epoch; each rank waits for all of them
- * and copies the full output out.  Replaces the survey's NCCL all-gather
+ * peer memory) as 8-byte words {value, epoch of the call}; each rank reads
+ * its full image once every word carries the call's epoch (no fences or
+ * flags), and copies it out.  Replaces the survey's NCCL all-gather
  * policy (kq_tp_init with an NCCL id); no counterpart in the reference, which
  * is single-process CPU code.  Setup: kq_tp_create on every rank, exchange
  * the kq_tp_handle blobs (any host channel), kq_tp_open with all of them in

@@ -59,9 +59,9 @@ struct kq_ctx {
   }
 };
 
-// A tensor-parallel group member: this rank's exchange buffer (two image
-// slots of max_elems floats, then one 32-bit flag per source rank), its
-// block buffer, and the peers' exchange buffers mapped over CUDA IPC.
+// A tensor-parallel group member: this rank's exchange buffer (two slots of
+// max_elems 8-byte words {f32 bits, epoch}), its block buffer, and the
+// peers' exchange buffers mapped over CUDA IPC.
 struct kq_tp {
   kq_ctx* ctx = nullptr;
   int world = 0, rank = 0;
@@ -169,7 +169,7 @@ int check_device_error(kq_ctx* ctx) {
   cudaGetLastError();
   return fail(ctx, KQ_ERR_CUDA,
               "a device-side wait gave up (code %d: 1-5 tcgen05 pipeline, 21-23 decode weight ring, 24 "
-              "attention KV ring, 31 tensor-parallel peer flag); the call's output is invalid",
+              "attention KV ring, 31-32 tensor-parallel peer flag); the call's output is invalid",
               code);
 }
 
@@ -664,7 +664,8 @@ int kq_linear_f32_static(kq_ctx* ctx, const kq_weight* w, const float* x, int64_
 
 // ---- tensor parallel --------------------------------------------------------------
 
-static size_t tp_flags_offset(int64_t max_elems) { return ((size_t)2 * (size_t)max_elems * 4 + 255) & ~size_t(255); }
+// Exchange buffer: two slots of max_elems 8-byte words {f32 bits, epoch}.
+static size_t tp_exchange_bytes(int64_t max_elems) { return (size_t)2 * (size_t)max_elems * 8; }
 
 int kq_tp_create(kq_ctx* ctx, int world, int rank, int64_t max_out_elems, kq_tp** out) {
   if (check_ctx(ctx) || !out) return KQ_ERR_INVALID_ARG;
@@ -680,7 +681,7 @@ int kq_tp_create(kq_ctx* ctx, int world, int rank, int64_t max_out_elems, kq_tp*
   tp->world = world;
   tp->rank = rank;
   tp->max_elems = max_out_elems;
-  const size_t xbytes = tp_flags_offset(max_out_elems) + 256;
+  const size_t xbytes = tp_exchange_bytes(max_out_elems);
   cudaError_t e = cudaMalloc(&tp->exch, xbytes);
   if (e == cudaSuccess) e = cudaMemset(tp->exch, 0, xbytes);
   if (e == cudaSuccess) e = cudaMalloc(reinterpret_cast<void**>(&tp->ylocal), (size_t)max_out_elems * 4);
@@ -759,9 +760,8 @@ int kq_tp_allgather_f32(kq_tp* tp, const float* y_local, int64_t m, int64_t row0
   a.r1 = row0 + rows;
   a.world = tp->world;
   a.rank = tp->rank;
-  for (int p = 0; p < tp->world; ++p) a.exch[p] = static_cast<float*>(tp->peer_base[p]);
+  for (int p = 0; p < tp->world; ++p) a.exch[p] = static_cast<unsigned long long*>(tp->peer_base[p]);
   a.max_elems = tp->max_elems;
-  a.flags_off = tp_flags_offset(tp->max_elems);
   a.ctr = tp->ctr;
   a.epoch = tp->ctr + 1;
   a.err = ctx->dev_err;
@@ -901,7 +901,8 @@ int kq_dec_add(kq_ctx* ctx, float* h, int64_t h_ld, const float* y, int64_t y_ld
 static int fused_linear(kq_ctx* ctx, const kq_weight* w, const kq::XsInput& in, const float* bias, float* y,
                         int flags, const char* what) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
-  if (!w || !in.x || !y) return fail(ctx, KQ_ERR_INVALID_ARG, "%s: null weight, input or output", what);
+  if (!w || !in.x || (!y && in.ymode == kq::XS_Y_LOCAL))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "%s: null weight, input or output", what);
   if (flags & ~(KQ_SYNC | KQ_DEVICE_PTRS)) return fail(ctx, KQ_ERR_INVALID_ARG, "%s: bad flags 0x%x", what, flags);
   if (w->device != ctx->device)
     return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device, ctx->device);
@@ -958,6 +959,64 @@ int kq_dec_residual_linear(kq_ctx* ctx, const kq_weight* w, const float* x, floa
   kq::XsInput in;
   in.x = x;
   return fused_linear(ctx, w, in, h, h, flags, "residual_linear");
+}
+
+// Exchange-buffer view of a tensor-parallel group for the fused linears.
+static kq::XsTp xs_tp(const kq_tp* tp) {
+  kq::XsTp t;
+  for (int p = 0; p < tp->world; ++p) t.exch[p] = static_cast<unsigned long long*>(tp->peer_base[p]);
+  t.slot_elems = tp->max_elems;
+  t.world = tp->world;
+  t.rank = tp->rank;
+  t.ctr = tp->ctr;
+  t.epoch = tp->ctr + 1;
+  return t;
+}
+
+int kq_dec_tp_reduce_linear(kq_tp* tp, const kq_weight* w, const float* h_in, float* h_out, const float* norm_w,
+                            int64_t dim, float eps, float* y, int flags) {
+  if (!tp) return KQ_ERR_INVALID_ARG;
+  kq_ctx* ctx = tp->ctx;
+  if (!tp->opened) return fail(ctx, KQ_ERR_STATE, "kq_tp_open has not been called");
+  if (!w || !h_in || !h_out || h_in == h_out)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "tp_reduce_linear: h_in and h_out must be distinct device buffers");
+  if (dim < 4 || (dim & 3) || dim > w->dw.k)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "tp_reduce_linear: dim %lld must be a positive multiple of 4 <= in_features",
+                (long long)dim);
+  if (dim * tp->world > tp->max_elems)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "tp_reduce_linear: %d partials of %lld exceed the exchange slot",
+                tp->world, (long long)dim);
+  if ((reinterpret_cast<uintptr_t>(h_in) | reinterpret_cast<uintptr_t>(h_out)) & 15)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "tp_reduce_linear: h_in and h_out must be 16-byte aligned");
+  kq::XsInput in;
+  in.mode = norm_w ? kq::XS_X_REDUCE_NORM : kq::XS_X_REDUCE;
+  in.x = h_in;
+  in.nw = norm_w;
+  in.dim = (int)dim;
+  in.eps = eps;
+  in.tp = xs_tp(tp);
+  in.tp.h_in = h_in;
+  in.tp.h_out = h_out;
+  return fused_linear(ctx, w, in, nullptr, y, flags, "tp_reduce_linear");
+}
+
+int kq_dec_tp_partial_linear(kq_tp* tp, const kq_weight* w, const float* x, int act, int flags) {
+  if (!tp) return KQ_ERR_INVALID_ARG;
+  kq_ctx* ctx = tp->ctx;
+  if (!tp->opened) return fail(ctx, KQ_ERR_STATE, "kq_tp_open has not been called");
+  if (!w || !x) return fail(ctx, KQ_ERR_INVALID_ARG, "tp_partial_linear: null weight or input");
+  if (act < -1 || act > 1) return fail(ctx, KQ_ERR_INVALID_ARG, "tp_partial_linear: activation %d", act);
+  if (w->dw.n * tp->world > tp->max_elems)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "tp_partial_linear: %d partials of %lld exceed the exchange slot",
+                tp->world, (long long)w->dw.n);
+  kq::XsInput in;
+  in.mode = act < 0 ? kq::XS_X_PLAIN : kq::XS_X_SWIGLU;
+  in.x = x;
+  in.x2 = act < 0 ? nullptr : x + w->dw.k;
+  in.act = act < 0 ? 0 : act;
+  in.ymode = kq::XS_Y_PEERS;
+  in.tp = xs_tp(tp);
+  return fused_linear(ctx, w, in, nullptr, nullptr, flags, "tp_partial_linear");
 }
 
 int kq_dec_embed(kq_ctx* ctx, const float* table, const int32_t* tokens, float* out, int64_t out_ld, int64_t batch,

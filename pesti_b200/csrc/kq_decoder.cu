@@ -124,7 +124,7 @@ struct AttnArgs {
   int64_t q_ld;
   __half* kc;         // [batch][hkv][max_seq][HD]
   __half* vc;
-  float* part;        // [batch][hq][splits][HD + 2]
+  float* part;        // [batch][hq][splits][HD + 4]: max, sum, 2 pad, acc[HD]
   unsigned* ctr;      // [batch][hkv] arrival counters, zero between calls
   float* out;         // token b's heads at out + b * out_ld
   int64_t out_ld;
@@ -150,8 +150,8 @@ struct AttnSmem {
   static constexpr int CF = 0;                              // weights [G][ATT_MAX_SPLITS]
   static constexpr int CL = CF + G * ATT_MAX_SPLITS * 4;    // sums [G][ATT_MAX_SPLITS]
   static constexpr int CI = CL + G * ATT_MAX_SPLITS * 4;    // 1 / total sum [G]
-  static constexpr int CR = CI + ((G * 4 + 15) / 16) * 16;  // float4 [2][G * HD / 4]
-  static_assert(CR + 2 * G * HD * 4 <= 2 * STAGE, "merge scratch exceeds the ring");
+  static constexpr int CR = CI + ((G * 4 + 15) / 16) * 16;  // per-warp sums [AT_THREADS / 32][G * HD]
+  static_assert(CR + (AT_THREADS / 32) * G * HD * 4 <= 2 * STAGE, "merge scratch exceeds the ring");
 };
 
 template <int HD, int G, bool ROPE>
@@ -336,16 +336,17 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
   }
 
   // this split's partial per query head
-  float* pb = A.part + ((int64_t)b * A.hq + hk * G) * A.splits * (HD + 2);
+  constexpr int PS = HD + 4;  // partial row: max, sum, 2 pad, acc[HD] (16-byte aligned)
+  float* pb = A.part + ((int64_t)b * A.hq + hk * G) * A.splits * PS;
 #pragma unroll
   for (int k = 0; k < NPAIR; ++k) {
     const int e = tid + k * AT_THREADS;
     if (e < G * HALF) {
       const int g = e / HALF, d2 = e - g * HALF;
-      *reinterpret_cast<float2*>(pb + ((int64_t)g * A.splits + sp) * (HD + 2) + 2 + 2 * d2) = acc[k];
+      *reinterpret_cast<float2*>(pb + ((int64_t)g * A.splits + sp) * PS + 4 + 2 * d2) = acc[k];
     }
   }
-  if (tid < G) *reinterpret_cast<float2*>(pb + ((int64_t)tid * A.splits + sp) * (HD + 2)) = make_float2(m_s[tid], l_s[tid]);
+  if (tid < G) *reinterpret_cast<float2*>(pb + ((int64_t)tid * A.splits + sp) * PS) = make_float2(m_s[tid], l_s[tid]);
   // the last CTA of (token, kv head) merges the splits
   __shared__ int last;
   __threadfence();
@@ -358,67 +359,66 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
   float* f_s = reinterpret_cast<float*>(sm + L::CF);
   float* l2 = reinterpret_cast<float*>(sm + L::CL);
   float* inv_l = reinterpret_cast<float*>(sm + L::CI);
-  float4* red = reinterpret_cast<float4*>(sm + L::CR);
+  float* red = reinterpret_cast<float*>(sm + L::CR);
+  // (1) every split's max and sum
   for (int e = tid; e < G * A.splits; e += AT_THREADS) {
     const int g = e / A.splits, s2 = e - g * A.splits;
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(pb + ((int64_t)g * A.splits + s2) * (HD + 2)));
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(pb + ((int64_t)g * A.splits + s2) * PS));
     f_s[g * ATT_MAX_SPLITS + s2] = ml.x;
     l2[g * ATT_MAX_SPLITS + s2] = ml.y;
   }
   __syncthreads();
-  if (tid < G) {
-    const int g = tid;
+  // (2) warp g: the splits' weights e^(m_s - M) and 1 / sum_s l_s e^(m_s - M)
+  for (int g = warp; g < G; g += AT_THREADS / 32) {
     float* fg = f_s + g * ATT_MAX_SPLITS;
-    float mx = -INFINITY;
-    for (int s2 = 0; s2 < A.splits; ++s2) mx = fmaxf(mx, fg[s2]);
-    float ls = 0.f;
-    for (int s2 = 0; s2 < A.splits; ++s2) {
-      const float f = fg[s2] == -INFINITY ? 0.f : __expf(fg[s2] - mx);
-      fg[s2] = f;
-      ls += l2[g * ATT_MAX_SPLITS + s2] * f;
-    }
-    inv_l[g] = 1.f / ls;
+    const float* lg = l2 + g * ATT_MAX_SPLITS;
+    const bool v0 = lane < A.splits, v1 = lane + 32 < A.splits;
+    const float a0 = v0 ? fg[lane] : -INFINITY, a1 = v1 ? fg[lane + 32] : -INFINITY;
+    float mx = fmaxf(a0, a1);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float f0 = a0 == -INFINITY ? 0.f : __expf(a0 - mx), f1 = a1 == -INFINITY ? 0.f : __expf(a1 - mx);
+    if (v0) fg[lane] = f0;
+    if (v1) fg[lane + 32] = f1;
+    float ls = (v0 ? f0 * lg[lane] : 0.f) + (v1 ? f1 * lg[lane + 32] : 0.f);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+    if (lane == 0) inv_l[g] = 1.f / ls;
   }
   __syncthreads();
-  // slot = (g, 4 dims); group r of R takes splits r, r + R, ...
-  constexpr int SLOTS = G * HD / 4;
-  constexpr int R = AT_THREADS / SLOTS >= 2 ? 2 : 1;
-  for (int e = tid; e < R * SLOTS; e += AT_THREADS) {
-    const int r = e / SLOTS, sl = e - r * SLOTS;
-    const int g = sl / (HD / 4), d4 = sl - g * (HD / 4);
-    const float* pg = pb + (int64_t)g * A.splits * (HD + 2) + 2 + 4 * d4;
-    const float* fg = f_s + g * ATT_MAX_SPLITS;
-    float4 as = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int s2 = r; s2 < A.splits; s2 += R) {
-      // rows are HD + 2 floats apart: 8-byte aligned, so two float2 loads
-      const float2 lo = __ldcg(reinterpret_cast<const float2*>(pg + (int64_t)s2 * (HD + 2)));
-      const float2 hi = __ldcg(reinterpret_cast<const float2*>(pg + (int64_t)s2 * (HD + 2) + 2));
-      const float f = fg[s2];
-      as.x = fmaf(lo.x, f, as.x);
-      as.y = fmaf(lo.y, f, as.y);
-      as.z = fmaf(hi.x, f, as.z);
-      as.w = fmaf(hi.y, f, as.w);
+  // (3) warp w sums splits w, w + 8, ...; lane c takes float4 columns c, c + 32, ... of [G][HD]
+  constexpr int C4 = G * HD / 4, PER = (C4 + 31) / 32;
+  float4 a[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) a[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
+  for (int s2 = warp; s2 < A.splits; s2 += AT_THREADS / 32) {
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int c = lane + 32 * k;
+      if (c < C4) {
+        const int g = c / (HD / 4), d4 = c - g * (HD / 4);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(pb + ((int64_t)g * A.splits + s2) * PS + 4) + d4);
+        const float f = f_s[g * ATT_MAX_SPLITS + s2];
+        a[k].x = fmaf(v.x, f, a[k].x);
+        a[k].y = fmaf(v.y, f, a[k].y);
+        a[k].z = fmaf(v.z, f, a[k].z);
+        a[k].w = fmaf(v.w, f, a[k].w);
+      }
     }
-    red[e] = as;
+  }
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int c = lane + 32 * k;
+    if (c < C4) reinterpret_cast<float4*>(red + warp * G * HD)[c] = a[k];
   }
   __syncthreads();
-  for (int sl = tid; sl < SLOTS; sl += AT_THREADS) {
-    const int g = sl / (HD / 4), d4 = sl - g * (HD / 4);
-    float4 a = red[sl];
-    if (R == 2) {
-      const float4 c = red[SLOTS + sl];
-      a.x += c.x;
-      a.y += c.y;
-      a.z += c.z;
-      a.w += c.w;
-    }
-    float* o = A.out + (int64_t)b * A.out_ld + (int64_t)(hk * G + g) * HD + 4 * d4;
-    const float il = inv_l[g];
-    o[0] = a.x * il;
-    o[1] = a.y * il;
-    o[2] = a.z * il;
-    o[3] = a.w * il;
+  for (int e = tid; e < G * HD; e += AT_THREADS) {
+    const int g = e / HD, d = e - g * HD;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < AT_THREADS / 32; ++w) v += red[w * G * HD + e];
+    A.out[(int64_t)b * A.out_ld + (int64_t)(hk * G + g) * HD + d] = v * inv_l[g];
   }
   if (tid == 0) *ctr = 0u;  // ready for the next call (stream-ordered)
 }
@@ -528,14 +528,14 @@ int dec_attention_splits(int64_t batch, int hkv, int64_t len, int num_sms) {
 
 // Scratch: the arrival counters [batch][hkv] u32 (zero before the first
 // call; every call leaves them zero), then from a 256-byte boundary the
-// partials [batch][hq][splits][hd + 2] f32.  The counters' place does not
+// partials [batch][hq][splits][hd + 4] f32.  The counters' place does not
 // depend on the split count, which grows with the sequence length.
 static size_t attn_part_offset(int64_t batch, int hkv) {
   return ((size_t)batch * hkv * sizeof(unsigned) + 255) & ~size_t(255);
 }
 
 size_t dec_attention_scratch_bytes(int64_t batch, int hq, int hkv, int hd, int splits) {
-  return attn_part_offset(batch, hkv) + (size_t)batch * hq * splits * (hd + 2) * sizeof(float);
+  return attn_part_offset(batch, hkv) + (size_t)batch * hq * splits * (hd + 4) * sizeof(float);
 }
 
 cudaError_t dec_attention(const float* q, int64_t q_ld, void* kc, void* vc, float* out, int64_t out_ld,

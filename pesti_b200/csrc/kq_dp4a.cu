@@ -541,11 +541,12 @@ constexpr int XS_MAX_COMPUTE = 15;  // compute warps (+ 1 producer = 512 threads
 constexpr int XS_MAX_SMEM = 227 * 1024;
 constexpr int64_t XS_INFLIGHT = 144 * 1024;  // ring bytes in flight per CTA
 
-enum : int { XS_ERR_FULL = 21, XS_ERR_EMPTY = 22, XS_ERR_DRAIN = 23 };
+enum : int { XS_ERR_FULL = 21, XS_ERR_EMPTY = 22, XS_ERR_DRAIN = 23, XS_ERR_TP = 32 };
 constexpr int64_t XS_PF_CHUNK = 64 * 1024;  // bytes per L2 prefetch instruction
 
 struct XsParams {
   const uint8_t* q;     // [n][row_bytes]
+  // (tensor-parallel fields last)
   const uint16_t* d;    // Q6_K: [n][d_row_bytes / 2]
   int64_t row_bytes;    // weight bytes per row
   int d_row_bytes;      // Q6_K: d bytes per row (a multiple of 16); Q4_K: 0
@@ -566,14 +567,19 @@ struct XsParams {
   // L2 prefetch of the weight the next kernel reads: two byte ranges, split over the CTAs
   const uint8_t* pf[2];
   int64_t pf_bytes[2];
+  // tensor parallel (XsTp): XS_Y_PEERS sends y to every rank's exchange image;
+  // XS_X_REDUCE* stage x = h_in + the ranks' partials (and write it to h_out)
+  XsTp tp;
+  int64_t xr_floats;  // XS_X_REDUCE*: floats of the reduced vector kept in shared memory
 };
 
 // Dynamic shared memory: ring | staged x: words uint4 [sb8 * 4 units][8]
 // (swizzled), sums (Q4_K float2 / Q6_K int4[4] per unit), 2^e per superblock
-// | row partials [rows_max][nk] | 32 reduction floats | full[S], empty[S].
+// | row partials [rows_max][nk] | 32 reduction floats | reduced x (tensor
+// parallel consumers) | full[S], empty[S].
 struct XsSmem {
-  size_t ring, xw, sums, xsf, part, red, bar, end;
-  __host__ __device__ XsSmem(int qt, int nk, int64_t stage_bytes, int S, int rows_max) {
+  size_t ring, xw, sums, xsf, part, red, xr, bar, end;
+  __host__ __device__ XsSmem(int qt, int nk, int64_t stage_bytes, int S, int rows_max, int64_t xr_floats) {
     const size_t units = (size_t)XS_SPW * nk * 4;
     ring = 0;
     xw = ring + (size_t)S * (size_t)stage_bytes;
@@ -581,7 +587,8 @@ struct XsSmem {
     xsf = sums + units * (qt == GGUF_Q4_K ? 8 : 64);
     part = xsf + units;  // one float per superblock = units / 4 floats
     red = (part + (size_t)rows_max * nk * 4 + 15) & ~size_t(15);
-    bar = red + 32 * 4;
+    xr = red + 32 * 4;
+    bar = xr + (size_t)xr_floats * 4;
     end = bar + (size_t)2 * S * 8;
   }
 };
@@ -635,6 +642,13 @@ __device__ __forceinline__ void xs_prefetch(const XsParams& P, int b, int C) {
       asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(P.pf[r] + u * 16), "r"(bytes) : "memory");
     }
   }
+}
+// 8-byte exchange words {f32 bits, epoch}: single 64-bit accesses
+__device__ __forceinline__ void st_word(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void ld_words2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 __device__ __forceinline__ void xs_named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
@@ -691,10 +705,51 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
   float* xsf = reinterpret_cast<float*>(smem + L.xsf);
   const int lane = threadIdx.x & 31;
   float rms = 1.f;
-  if constexpr (XM == XS_X_NORM) {
+  constexpr bool REDUCE = XM == XS_X_REDUCE || XM == XS_X_REDUCE_NORM;
+  float* xr = reinterpret_cast<float*>(smem + L.xr);
+  if constexpr (REDUCE) {
+    // every rank's partial of the last exchange (sent by the previous kernel
+    // on every rank): x = h_in + sum_r p_r in rank order into shared memory,
+    // each value taken once its word carries that exchange's epoch; this
+    // CTA's slice also goes to h_out
+    const XsTp& T = P.tp;
+    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(T.epoch);
+    const unsigned long long* img = T.exch[T.rank] + (size_t)(epoch & 1u) * (size_t)T.slot_elems;
+    const int q4 = P.dim / 4, C = gridDim.x, b = blockIdx.x;
+    const int lo = (int)((int64_t)q4 * b / C) * 4, hi = (int)((int64_t)q4 * (b + 1) / C) * 4;
+    bool ok = true;
+    for (int i = 4 * threadIdx.x; i < P.dim; i += 4 * nthreads) {
+      float4 v = __ldcg(reinterpret_cast<const float4*>(T.h_in + i));
+      for (int r = 0; r < T.world; ++r) {
+        const unsigned long long* wp = img + (size_t)r * P.dim + i;
+        unsigned long long w0, w1, w2, w3;
+        for (uint32_t it = 0;; ++it) {
+          ld_words2(wp, w0, w1);
+          ld_words2(wp + 2, w2, w3);
+          if (!ok || ((unsigned)(w0 >> 32) == epoch && (unsigned)(w1 >> 32) == epoch &&
+                      (unsigned)(w2 >> 32) == epoch && (unsigned)(w3 >> 32) == epoch))
+            break;
+          if (it >= (1u << 22) || ((it & 255u) == 255u && *(volatile int*)P.err)) {
+            atomicCAS(P.err, 0, XS_ERR_TP);  // the output is invalid; the kernel still runs to its end
+            ok = false;
+            break;
+          }
+          __nanosleep(32);
+        }
+        v.x += __uint_as_float((unsigned)w0);
+        v.y += __uint_as_float((unsigned)w1);
+        v.z += __uint_as_float((unsigned)w2);
+        v.w += __uint_as_float((unsigned)w3);
+      }
+      *reinterpret_cast<float4*>(xr + i) = v;
+      if (i >= lo && i < hi) *reinterpret_cast<float4*>(T.h_out + i) = v;
+    }
+    xs_named_sync(1, nthreads);
+  }
+  if constexpr (XM == XS_X_NORM || XM == XS_X_REDUCE_NORM) {
     float ss = 0.f;
     for (int i = 4 * threadIdx.x; i < P.dim; i += 4 * nthreads) {
-      const float4 f = ldg_f4(P.x + i);
+      const float4 f = REDUCE ? *reinterpret_cast<const float4*>(xr + i) : ldg_f4(P.x + i);
       ss = fmaf(f.x, f.x, ss);
       ss = fmaf(f.y, f.y, ss);
       ss = fmaf(f.z, f.z, ss);
@@ -714,7 +769,7 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
     const int hu = base + lane;
     const int kb = hu >> 3, u = (hu >> 1) & 3, hf = hu & 1;
     const bool live = kb < P.sb;
-    const float* xr = P.x + (int64_t)kb * 256;
+    const float* xrow = P.x + (int64_t)kb * 256;
     float v[32];  // Q4: [0,16) sub-block 2u run, [16,32) sub-block 2u+1 run; Q6: group (g, w) at 8g + 4w
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -723,11 +778,23 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
       else off = 128 * hf + 32 * (i >> 1) + 8 * u + 4 * (i & 1);
       float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
       if constexpr (XM == XS_X_PLAIN) {
-        if (live) f = ldg_f4(xr + off);
+        if (live) f = ldg_f4(xrow + off);
+      } else if constexpr (REDUCE) {
+        const int64_t gi = (int64_t)kb * 256 + off;
+        if (live && gi < P.dim) {
+          f = *reinterpret_cast<const float4*>(xr + gi);
+          if constexpr (XM == XS_X_REDUCE_NORM) {
+            const float4 wv = ldg_f4(P.nw + gi);
+            f.x = f.x / rms * wv.x;
+            f.y = f.y / rms * wv.y;
+            f.z = f.z / rms * wv.z;
+            f.w = f.w / rms * wv.w;
+          }
+        }
       } else if constexpr (XM == XS_X_NORM) {
         const int64_t gi = (int64_t)kb * 256 + off;
         if (live && gi < P.dim) {
-          f = ldg_f4(xr + off);
+          f = ldg_f4(xrow + off);
           const float4 wv = ldg_f4(P.nw + gi);
           f.x = f.x / rms * wv.x;
           f.y = f.y / rms * wv.y;
@@ -736,7 +803,7 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
         }
       } else {
         if (live) {
-          const float4 g = ldg_f4(xr + off), uu = ldg_f4(P.x2 + (int64_t)kb * 256 + off);
+          const float4 g = ldg_f4(xrow + off), uu = ldg_f4(P.x2 + (int64_t)kb * 256 + off);
           f.x = swiglu_gate(g.x, P.act) * uu.x;
           f.y = swiglu_gate(g.y, P.act) * uu.y;
           f.z = swiglu_gate(g.z, P.act) * uu.z;
@@ -801,7 +868,7 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
   }
 }
 
-template <int QT, int XM>
+template <int QT, int XM, int YM>
 __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(const XsParams P) {
   extern __shared__ __align__(128) uint8_t xs_smem[];
   pdl_trigger();  // the next kernel's CTAs may start on each SM as ours retire there
@@ -811,7 +878,7 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   const int R = 2 * P.G;  // rows per stage: each compute warp takes two of them
   const int T = (rows + R - 1) / R;
   const int NC = P.nk * P.G;
-  const XsSmem L(QT, P.nk, P.stage_bytes, P.S, P.rows_max);
+  const XsSmem L(QT, P.nk, P.stage_bytes, P.S, P.rows_max, P.xr_floats);
   uint64_t* full = reinterpret_cast<uint64_t*>(xs_smem + L.bar);
   uint64_t* empty = full + P.S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1005,16 +1072,37 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
     if (lane == 0) xs_bar_arrive(&empty[st]);
   }
   xs_named_sync(1, NC * 32);
-  for (int q = threadIdx.x; q < rows; q += NC * 32) {
-    float acc = 0.f;
-    for (int t = 0; t < P.nk; ++t) acc += part[q * P.nk + t];
-    const int64_t row = r0 + q;
-    P.y[row] = acc + (P.bias ? P.bias[row] : 0.f);
+  if constexpr (YM == XS_Y_LOCAL) {
+    for (int q = threadIdx.x; q < rows; q += NC * 32) {
+      float acc = 0.f;
+      for (int t = 0; t < P.nk; ++t) acc += part[q * P.nk + t];
+      const int64_t row = r0 + q;
+      P.y[row] = acc + (P.bias ? P.bias[row] : 0.f);
+    }
+  } else {
+    // this exchange's epoch: one past the last; the last CTA to arrive
+    // advances the counter, after every CTA has read it here
+    const XsTp& T = P.tp;
+    const unsigned epoch = *reinterpret_cast<volatile unsigned*>(T.epoch) + 1u;
+    const unsigned long long tag = (unsigned long long)epoch << 32;
+    const size_t at = (size_t)(epoch & 1u) * (size_t)T.slot_elems + (size_t)T.rank * P.n + r0;
+    for (int q = threadIdx.x; q < rows; q += NC * 32) {
+      float acc = 0.f;
+      for (int t = 0; t < P.nk; ++t) acc += part[q * P.nk + t];
+      const float v = acc + (P.bias ? P.bias[r0 + q] : 0.f);
+      for (int p = 0; p < T.world; ++p) st_word(T.exch[p] + at + q, tag | __float_as_uint(v));  // over NVLink
+    }
+    xs_named_sync(1, NC * 32);
+    if (threadIdx.x == 0 && atomicAdd(T.ctr, 1u) == gridDim.x - 1) {
+      *T.ctr = 0u;
+      *T.epoch = epoch;
+    }
   }
 }
 
 struct XsLaunch {
   bool ok = false;
+  int64_t xr_floats = 0;
   int threads = 0, grid = 0, G = 0, S = 0, rows_max = 0;
   int64_t stage_bytes = 0;
   size_t smem = 0;
@@ -1022,8 +1110,9 @@ struct XsLaunch {
 
 // Launch shape of the single-token kernel, or ok = false when it does not
 // apply (more than XS_MAX_COMPUTE slices, or a ring of fewer than 2 stages).
-XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms) {
+XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms, int64_t xr_floats = 0) {
   XsLaunch r;
+  r.xr_floats = xr_floats;
   const int nk = (int)((sb + XS_SPW - 1) / XS_SPW);
   if (n < 1 || nk < 1 || nk > XS_MAX_COMPUTE) return r;
   r.G = XS_MAX_COMPUTE / nk;
@@ -1034,14 +1123,14 @@ XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms) {
   const int64_t d_row_bytes = qt == GGUF_Q6_K ? q6k_d_ld(sb) * 2 : 0;
   r.stage_bytes = 2 * r.G * (row_bytes + d_row_bytes);  // 2G rows per stage
   const int T = (r.rows_max + 2 * r.G - 1) / (2 * r.G);
-  const size_t fixed = XsSmem(qt, nk, r.stage_bytes, 0, r.rows_max).end + 64;
+  const size_t fixed = XsSmem(qt, nk, r.stage_bytes, 0, r.rows_max, xr_floats).end + 64;
   if (fixed >= (size_t)XS_MAX_SMEM) return r;
   const int64_t fit = (int64_t)((XS_MAX_SMEM - fixed) / (size_t)(r.stage_bytes + 16));
   const int64_t want = std::max<int64_t>(2, (XS_INFLIGHT + r.stage_bytes / 2) / r.stage_bytes);
   const int S = (int)std::min<int64_t>(std::min<int64_t>(T, fit), want);
   if (S < std::min(T, 2)) return r;
   r.S = S;
-  r.smem = XsSmem(qt, nk, r.stage_bytes, S, r.rows_max).end;
+  r.smem = XsSmem(qt, nk, r.stage_bytes, S, r.rows_max, xr_floats).end;
   r.ok = r.smem <= (size_t)XS_MAX_SMEM;
   return r;
 }
@@ -1074,6 +1163,8 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
     P.pf[r] = pf ? static_cast<const uint8_t*>(pf->p[r]) : nullptr;
     P.pf_bytes[r] = pf && pf->p[r] ? pf->bytes[r] : 0;
   }
+  P.tp = in.tp;
+  P.xr_floats = sh.xr_floats;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sh.grid);
   cfg.blockDim = dim3((unsigned)sh.threads);
@@ -1084,10 +1175,19 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (in.ymode == XS_Y_PEERS) {
+    switch (in.mode) {
+      case XS_X_PLAIN: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_PEERS>, P);
+      case XS_X_SWIGLU: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_SWIGLU, XS_Y_PEERS>, P);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (in.mode) {
-    case XS_X_PLAIN: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN>, P);
-    case XS_X_NORM: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_NORM>, P);
-    case XS_X_SWIGLU: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_SWIGLU>, P);
+    case XS_X_PLAIN: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_LOCAL>, P);
+    case XS_X_NORM: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_NORM, XS_Y_LOCAL>, P);
+    case XS_X_SWIGLU: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_SWIGLU, XS_Y_LOCAL>, P);
+    case XS_X_REDUCE: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_REDUCE, XS_Y_LOCAL>, P);
+    case XS_X_REDUCE_NORM: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_REDUCE_NORM, XS_Y_LOCAL>, P);
   }
   return cudaErrorInvalidValue;
 }
@@ -1136,15 +1236,20 @@ cudaError_t launch_gemv_dp4a_batched(const DevWeight& w, const float* x, int64_t
   return cudaErrorInvalidValue;
 }
 
+template <typename K>
+static cudaError_t xs_attr(K kernel) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, XS_MAX_SMEM);
+}
+
 template <int QT>
 static cudaError_t xs_attrs() {
-  cudaError_t e = cudaFuncSetAttribute(xs_gemv_kernel<QT, XS_X_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       XS_MAX_SMEM);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(xs_gemv_kernel<QT, XS_X_NORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, XS_MAX_SMEM);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(xs_gemv_kernel<QT, XS_X_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             XS_MAX_SMEM);
+  cudaError_t e = xs_attr(xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_NORM, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_SWIGLU, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_REDUCE, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_REDUCE_NORM, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_PEERS>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_SWIGLU, XS_Y_PEERS>);
   return e;
 }
 
@@ -1157,8 +1262,9 @@ cudaError_t dp4a_init_device() {
 cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* bias, float* y, int num_sms, int* err,
                            const Prefetch* pf, cudaStream_t s, int* launches, Bracket br) {
   if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
-  if (in.mode < XS_X_PLAIN || in.mode > XS_X_SWIGLU) return cudaErrorInvalidValue;
-  const XsLaunch sh = xs_shape(w.type, w.n, w.sb, num_sms);
+  if (in.mode < XS_X_PLAIN || in.mode > XS_X_REDUCE_NORM) return cudaErrorInvalidValue;
+  const bool reduce = in.mode == XS_X_REDUCE || in.mode == XS_X_REDUCE_NORM;
+  const XsLaunch sh = xs_shape(w.type, w.n, w.sb, num_sms, reduce ? (int64_t)((in.dim + 3) & ~3) : 0);
   if (!sh.ok) return cudaErrorNotSupported;
   bracket_record(br.start, s);
   cudaError_t e = w.type == GGUF_Q4_K ? launch_xs<GGUF_Q4_K>(w, in, bias, y, err, pf, s, sh)

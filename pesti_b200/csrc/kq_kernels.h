@@ -127,10 +127,34 @@ struct Prefetch {
 cudaError_t launch_gemv_dp4a(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y,
                              void* ws, int num_sms, int* err, cudaStream_t s, int* launches,
                              Bracket br = Bracket(), const Prefetch* pf = nullptr);
-// Activation source of the single-token kernel.
-enum : int { XS_X_PLAIN = 0, XS_X_NORM = 1, XS_X_SWIGLU = 2 };
+// Activation source of the single-token kernel.  The REDUCE forms are the
+// tensor-parallel consumers: x = h_in + the partial vectors every rank sent
+// in the last exchange (summed in rank order, so every rank gets the same
+// bits), written to h_out, then (REDUCE_NORM) RMS-normalised.
+enum : int { XS_X_PLAIN = 0, XS_X_NORM = 1, XS_X_SWIGLU = 2, XS_X_REDUCE = 3, XS_X_REDUCE_NORM = 4 };
+// Destination of y: this rank's buffer, or (XS_Y_PEERS) slot rows
+// [rank * n, rank * n + n) of every rank's exchange image, then the
+// exchange's epoch is published in every rank's flags.
+enum : int { XS_Y_LOCAL = 0, XS_Y_PEERS = 1 };
+constexpr int TP_MAX_WORLD = 8;
+// Exchange buffers (as in TpArgs): two slots of slot_elems 8-byte words.
+// A word is {f32 value bits, epoch}: a reader takes a value once its word
+// carries the epoch of the exchange it waits for, so no fences or flags are
+// needed (each 64-bit word is stored and loaded as one single-copy-atomic
+// access).  Slot = epoch % 2.
+struct XsTp {
+  unsigned long long* exch[TP_MAX_WORLD] = {};  // every rank's buffer, mapped here
+  int64_t slot_elems = 0;
+  int world = 1, rank = 0;
+  unsigned* ctr = nullptr;          // CTA arrival counter (zero between calls)
+  unsigned* epoch = nullptr;        // last published exchange epoch
+  const float* h_in = nullptr;      // REDUCE: residual stream in / out
+  float* h_out = nullptr;
+};
 struct XsInput {
   int mode = XS_X_PLAIN;
+  int ymode = XS_Y_LOCAL;
+  XsTp tp;                    // REDUCE modes and XS_Y_PEERS
   const float* x = nullptr;   // [k] (XS_X_SWIGLU: the gate)
   const float* x2 = nullptr;  // XS_X_SWIGLU: the up projection [k]
   const float* nw = nullptr;  // XS_X_NORM: norm weights [dim]
@@ -145,16 +169,14 @@ cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* b
                            const Prefetch* pf, cudaStream_t s, int* launches, Bracket br = Bracket());
 
 // ---- tensor parallel: all-gather of row-sharded outputs over peer memory (kq_tp.cu) ----
-constexpr int TP_MAX_WORLD = 8;
 struct TpArgs {
   const float* y_local;                  // [m][r1 - r0] this rank's block
   float* y_out;                          // [m][y_ld] the gathered result (first n columns)
   int64_t y_ld;
   int accumulate;                        // nonzero: y_out += gathered
   int64_t m, n, r0, r1;                  // tokens, total columns, this rank's columns
-  float* exch[TP_MAX_WORLD];             // every rank's exchange buffer: 2 slots of max_elems floats, then flags
+  unsigned long long* exch[TP_MAX_WORLD];  // every rank's exchange buffer: 2 slots of max_elems words
   int64_t max_elems;
-  size_t flags_off;                      // byte offset of the flag array in an exchange buffer
   int world, rank;
   unsigned* epoch;                       // local device counter: the last completed call's epoch
   unsigned* ctr;                         // zero between calls (last-CTA detection)

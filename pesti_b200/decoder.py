@@ -78,6 +78,8 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "kq_dec_swiglu_linear": [P, P, P, I, P, P, I],
         "kq_dec_residual_linear": [P, P, P, P, I],
         "kq_dec_rope_attention": [P, P, I64, P, P, P, I64, I64, I, I, I, I64, I64, F, P, Z],
+        "kq_dec_tp_partial_linear": [P, P, P, I, I],
+        "kq_dec_tp_reduce_linear": [P, P, P, P, P, I64, F, P, I],
     }
     for name, args in sig.items():
         getattr(lib, name).argtypes = args
@@ -110,10 +112,19 @@ def gguf_weight_device(qtype: int, n: int, k: int, seed: int, device):
     return raw.view(n, -1)
 
 
-def exchange_elems(cfg: DecoderConfig, batch: int) -> int:
-    """Floats the tensor-parallel exchange buffer needs for this model: the
-    widest all-gathered activation (logits, SwiGLU output, residual stream)."""
-    return batch * max(cfg.vocab, cfg.ffn, cfg.dim, cfg.heads * cfg.head_dim)
+def exchange_elems(cfg: DecoderConfig, batch: int, world: int = 8) -> int:
+    """Floats one slot of the tensor-parallel exchange buffer needs for this
+    model: the widest all-gathered activation (logits, SwiGLU output, residual
+    stream) or, at batch 1, one partial residual vector per rank."""
+    return max(batch * max(cfg.vocab, cfg.ffn, cfg.dim, cfg.heads * cfg.head_dim), world * cfg.dim)
+
+
+def column_block(raw, k: int, c0: int, c1: int):
+    """Columns [c0, c1) (multiples of 256) of a GGUF weight held as [n][k/256 *
+    bytes]: the superblocks of that range in every row."""
+    n = raw.shape[0]
+    sb = k // 256
+    return raw.view(n, sb, -1)[:, c0 // 256:c1 // 256].contiguous().view(n, -1)
 
 
 class Decoder:
@@ -136,6 +147,12 @@ class Decoder:
         # RMSNorm, SwiGLU and the residual adds inside the single-token GEMVs;
         # prefetch: each linear pulls the next one's weight into L2
         self.fused_attention, self.fused, self.prefetch = fused, fused and batch == 1, prefetch
+        # column split (batch 1, tensor parallel): the output and down
+        # projections hold W[:, this rank's heads / FFN block] and exchange
+        # partial residual vectors (2 exchanges per layer) instead of
+        # all-gathering row blocks (4); needs both blocks on superblock edges
+        self.col_split = (world > 1 and self.fused and (cfg.heads // world * cfg.head_dim) % 256 == 0
+                          and cfg.ffn % (256 * world) == 0)
         self.lib = _bind(ctx.lib)
         dev = torch.device("cuda", ctx.device)
         self.device = dev
@@ -180,7 +197,11 @@ class Decoder:
             wo = gguf_weight_device(cfg.linear_type, D, self.Ap, slot(li, "o"), dev)
             keep((li, "o"), wo)
             r0, r1 = self.o_rows
-            L["o"] = upload(wo[r0:r1].contiguous(), cfg.linear_type, r1 - r0, self.Ap)
+            if self.col_split:
+                a0, a1 = hq0 * hd, (hq0 + self.hq) * hd
+                L["o"] = upload(column_block(wo, self.Ap, a0, a1), cfg.linear_type, D, a1 - a0)
+            else:
+                L["o"] = upload(wo[r0:r1].contiguous(), cfg.linear_type, r1 - r0, self.Ap)
             wg = gguf_weight_device(cfg.linear_type, F, self.Dp, slot(li, "gate"), dev)
             wu = gguf_weight_device(cfg.linear_type, F, self.Dp, slot(li, "up"), dev)
             keep((li, "gate"), wg)
@@ -191,7 +212,10 @@ class Decoder:
             del wg, wu, gu
             wd = gguf_weight_device(cfg.down_type, D, F, slot(li, "down"), dev)
             keep((li, "down"), wd)
-            L["down"] = upload(wd[r0:r1].contiguous(), cfg.down_type, r1 - r0, F)
+            if self.col_split:
+                L["down"] = upload(column_block(wd, F, f0, f1), cfg.down_type, D, f1 - f0)
+            else:
+                L["down"] = upload(wd[r0:r1].contiguous(), cfg.down_type, r1 - r0, F)
             del wd
             g = torch.Generator(device=dev)
             g.manual_seed(slot(li, "norms"))
@@ -226,6 +250,7 @@ class Decoder:
         # activations (padded columns stay zero)
         z = lambda *s: torch.zeros(s, device=dev)  # noqa: E731
         self.h, self.a = z(B, self.Dp), z(B, self.Dp)
+        self.h2 = z(B, self.Dp) if self.col_split else None  # the other residual buffer
         self.qkv_ld = (self.hq + 2 * self.hkv) * hd
         self.qkv = z(B, self.qkv_ld)
         self.attn = z(B, self.Ap)
@@ -284,6 +309,9 @@ class Decoder:
         ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
         if not 0 <= pos < self.max_seq:
             raise ValueError(f"position {pos} outside the cache ({self.max_seq})")
+        if self.col_split:
+            self._step_col_split(pos)
+            return
         r0, r1 = self.o_rows
         f0, f1 = self.f_rows
         tp = self.world > 1
@@ -338,6 +366,53 @@ class Decoder:
             self.head.linear(self.h, B, logits, device_ptrs=True)
         if tp:
             self._gather(self.logits_r, cfg.vocab, v0, v1 - v0, self.logits, cfg.vocab, False)
+
+    def _step_col_split(self, pos: int) -> None:
+        """Batch-1 tensor-parallel step with column-split output / down
+        projections: per layer two exchanges of partial residual vectors, each
+        sent from inside the producing GEMV and summed (with the residual and
+        the next RMSNorm) inside the consuming GEMV's activation staging."""
+        cfg, lib, c = self.cfg, self.lib, self.ctx.handle
+        D, hd = cfg.dim, cfg.head_dim
+        tph = self.tp.handle
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        cur, nxt = self.h, self.h2
+        self._check(lib.kq_dec_embed(c, ptr(self.embed), ptr(self.tokens), ptr(cur), self.Dp, 1, D), "embed")
+        pending = False  # an exchange of partials waits to be added to `cur`
+
+        def reduce_linear(w, norm, y):
+            nonlocal cur, nxt
+            self._hint(w)
+            if not pending:
+                self._check(lib.kq_dec_norm_linear(c, w.handle, ptr(cur), ptr(norm), D, cfg.eps, None, ptr(y), 0),
+                            "norm_linear")
+                return
+            self._check(lib.kq_dec_tp_reduce_linear(tph, w.handle, ptr(cur), ptr(nxt),
+                                                    ptr(norm) if norm is not None else None, D, cfg.eps, ptr(y), 0),
+                        "tp_reduce_linear")
+            cur, nxt = nxt, cur
+
+        for L in self.layers:
+            reduce_linear(L["qkv"], L["attn_norm"], self.qkv)
+            self._check(lib.kq_dec_rope_attention(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]),
+                                                  ptr(self.attn_r), self.hq * hd, 1, self.hq, self.hkv, hd, pos,
+                                                  self.max_seq, cfg.theta, ptr(self.att_scratch),
+                                                  self.att_scratch_bytes), "rope_attention")
+            self._hint(L["o"])
+            self._check(lib.kq_dec_tp_partial_linear(tph, L["o"].handle, ptr(self.attn_r), -1, 0), "o partial")
+            pending = True
+            reduce_linear(L["gu"], L["ffn_norm"], self.gu)
+            self._hint(L["down"])
+            self._check(lib.kq_dec_tp_partial_linear(tph, L["down"].handle, ptr(self.gu), self.swiglu_mode, 0),
+                        "down partial")
+            pending = True
+        v0, v1 = self.v_rows
+        self._hint(self.head)
+        if self.final_norm is not None or pending:
+            reduce_linear(self.head, self.final_norm, self.logits_r)
+        else:
+            self.head.linear(cur, 1, self.logits_r, device_ptrs=True)
+        self._gather(self.logits_r, cfg.vocab, v0, v1 - v0, self.logits, cfg.vocab, False)
 
     def weight_bytes(self) -> int:
         """HBM bytes of this rank's quantized weights."""

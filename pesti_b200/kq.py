@@ -61,7 +61,7 @@ EXPORTED_SYMBOLS = (
     "kq_tp_create", "kq_tp_handle", "kq_tp_open", "kq_tp_linear_f32", "kq_tp_allgather_f32",
     "kq_tp_destroy", "kq_dec_rmsnorm", "kq_dec_rope_append", "kq_dec_attention_scratch", "kq_dec_attention",
     "kq_dec_swiglu", "kq_dec_add", "kq_dec_embed", "kq_dec_norm_linear", "kq_dec_swiglu_linear",
-    "kq_dec_residual_linear", "kq_dec_rope_attention",
+    "kq_dec_residual_linear", "kq_dec_rope_attention", "kq_dec_tp_partial_linear", "kq_dec_tp_reduce_linear",
 )
 
 
