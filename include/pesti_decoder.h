@@ -60,13 +60,17 @@ int kq_dec_add(kq_ctx *ctx, float *h, int64_t h_ld, const float *y, int64_t y_ld
  * then queues kq_dec_rmsnorm / kq_dec_swiglu and kq_linear_f32).
  *   norm_linear:   y = rmsnorm(x[0:dim]; norm_w, eps) . W^T + bias, the
  *                  normalised vector zero past dim (dim <= in_features, a
- *                  multiple of 4);
+ *                  multiple of 4).  act -1: y has out_features values;
+ *                  act 0 / 1 (SwiGLU mode as in kq_dec_swiglu): W's rows are
+ *                  (gate, up) pairs and y[j] = swiglu(row 2j, row 2j+1), so
+ *                  the FFN's gate and up projections and the SwiGLU are one
+ *                  call (out_features / 2 values);
  *   swiglu_linear: y = swiglu(gate_up; mode) . W^T + bias with gate_up =
  *                  [gate (in_features) | up (in_features)], mode as in kq_dec_swiglu;
  *   residual_linear: h += x . W^T.
  * flags: KQ_SYNC or 0 (pointers are device pointers). */
 int kq_dec_norm_linear(kq_ctx *ctx, const kq_weight *w, const float *x, const float *norm_w, int64_t dim, float eps,
-                       const float *bias, float *y, int flags);
+                       int act, const float *bias, float *y, int flags);
 int kq_dec_swiglu_linear(kq_ctx *ctx, const kq_weight *w, const float *gate_up, int mode, const float *bias, float *y,
                          int flags);
 /* h[0:out_features] += x . W^T (the residual connection fused into the linear). */
@@ -85,10 +89,11 @@ int kq_dec_residual_linear(kq_ctx *ctx, const kq_weight *w, const float *x, floa
  *            x = [gate | up] (as kq_dec_swiglu_linear); out_features =
  *            the partial's length.
  *   reduce:  norm_w NULL = no norm; dim = the partials' length; h_in and
- *            h_out distinct.  Status codes as kq_dec_norm_linear. */
+ *            h_out distinct; act as in kq_dec_norm_linear (with a norm).
+ *            Status codes as kq_dec_norm_linear. */
 int kq_dec_tp_partial_linear(kq_tp *tp, const kq_weight *w, const float *x, int act, int flags);
 int kq_dec_tp_reduce_linear(kq_tp *tp, const kq_weight *w, const float *h_in, float *h_out, const float *norm_w,
-                            int64_t dim, float eps, float *y, int flags);
+                            int64_t dim, float eps, int act, float *y, int flags);
 /* out[b] = table[tokens[b]] (Model::embed, model.rs:966-984); table f32 [vocab][dim]. */
 int kq_dec_embed(kq_ctx *ctx, const float *table, const int32_t *tokens, float *out, int64_t out_ld,
                  int64_t batch, int64_t dim);

@@ -926,8 +926,20 @@ static int fused_linear(kq_ctx* ctx, const kq_weight* w, const kq::XsInput& in, 
   return KQ_OK;
 }
 
+// act -1: plain rows; 0 / 1: (gate, up) row pairs through the SwiGLU gate.
+static int set_pairs(kq_ctx* ctx, const kq_weight* w, int act, kq::XsInput& in, const char* what) {
+  if (act < -1 || act > 1) return fail(ctx, KQ_ERR_INVALID_ARG, "%s: activation %d", what, act);
+  if (act >= 0) {
+    if (!w || (w->dw.n & 1))
+      return fail(ctx, KQ_ERR_INVALID_ARG, "%s: a SwiGLU output needs (gate, up) row pairs", what);
+    in.ymode = kq::XS_Y_SWIGLU;
+    in.act = act;
+  }
+  return KQ_OK;
+}
+
 int kq_dec_norm_linear(kq_ctx* ctx, const kq_weight* w, const float* x, const float* norm_w, int64_t dim, float eps,
-                       const float* bias, float* y, int flags) {
+                       int act, const float* bias, float* y, int flags) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!norm_w) return fail(ctx, KQ_ERR_INVALID_ARG, "norm_linear: null norm weights");
   if (!w || dim < 4 || (dim & 3) || dim > w->dw.k)
@@ -939,6 +951,7 @@ int kq_dec_norm_linear(kq_ctx* ctx, const kq_weight* w, const float* x, const fl
   in.nw = norm_w;
   in.dim = (int)dim;
   in.eps = eps;
+  if (int rc = set_pairs(ctx, w, act, in, "norm_linear")) return rc;
   return fused_linear(ctx, w, in, bias, y, flags, "norm_linear");
 }
 
@@ -974,7 +987,7 @@ static kq::XsTp xs_tp(const kq_tp* tp) {
 }
 
 int kq_dec_tp_reduce_linear(kq_tp* tp, const kq_weight* w, const float* h_in, float* h_out, const float* norm_w,
-                            int64_t dim, float eps, float* y, int flags) {
+                            int64_t dim, float eps, int act, float* y, int flags) {
   if (!tp) return KQ_ERR_INVALID_ARG;
   kq_ctx* ctx = tp->ctx;
   if (!tp->opened) return fail(ctx, KQ_ERR_STATE, "kq_tp_open has not been called");
@@ -997,6 +1010,8 @@ int kq_dec_tp_reduce_linear(kq_tp* tp, const kq_weight* w, const float* h_in, fl
   in.tp = xs_tp(tp);
   in.tp.h_in = h_in;
   in.tp.h_out = h_out;
+  if (act >= 0 && !norm_w) return fail(ctx, KQ_ERR_UNSUPPORTED, "tp_reduce_linear: a SwiGLU output needs the norm");
+  if (int rc = set_pairs(ctx, w, act, in, "tp_reduce_linear")) return rc;
   return fused_linear(ctx, w, in, nullptr, y, flags, "tp_reduce_linear");
 }
 

@@ -571,15 +571,17 @@ struct XsParams {
   // XS_X_REDUCE* stage x = h_in + the ranks' partials (and write it to h_out)
   XsTp tp;
   int64_t xr_floats;  // XS_X_REDUCE*: floats of the reduced vector kept in shared memory
+  int64_t nw_floats;  // NORM modes: norm weights copied to shared memory at kernel start
 };
 
 // Dynamic shared memory: ring | staged x: words uint4 [sb8 * 4 units][8]
 // (swizzled), sums (Q4_K float2 / Q6_K int4[4] per unit), 2^e per superblock
 // | row partials [rows_max][nk] | 32 reduction floats | reduced x (tensor
-// parallel consumers) | full[S], empty[S].
+// parallel consumers) | norm weights | full[S], empty[S], aux.
 struct XsSmem {
-  size_t ring, xw, sums, xsf, part, red, xr, bar, end;
-  __host__ __device__ XsSmem(int qt, int nk, int64_t stage_bytes, int S, int rows_max, int64_t xr_floats) {
+  size_t ring, xw, sums, xsf, part, red, xr, nw, bar, end;
+  __host__ __device__ XsSmem(int qt, int nk, int64_t stage_bytes, int S, int rows_max, int64_t xr_floats,
+                             int64_t nw_floats) {
     const size_t units = (size_t)XS_SPW * nk * 4;
     ring = 0;
     xw = ring + (size_t)S * (size_t)stage_bytes;
@@ -588,8 +590,9 @@ struct XsSmem {
     part = xsf + units;  // one float per superblock = units / 4 floats
     red = (part + (size_t)rows_max * nk * 4 + 15) & ~size_t(15);
     xr = red + 32 * 4;
-    bar = xr + (size_t)xr_floats * 4;
-    end = bar + (size_t)2 * S * 8;
+    nw = xr + (size_t)xr_floats * 4;
+    bar = (nw + (size_t)nw_floats * 4 + 7) & ~size_t(7);
+    end = bar + (size_t)(2 * S + 1) * 8;
   }
 };
 
@@ -628,6 +631,12 @@ __device__ __forceinline__ void xs_bulk_g2s(void* dst, const void* src, uint32_t
           smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(b)), "l"(pol)
       : "memory");
+}
+__device__ __forceinline__ void xs_bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(b))
+               : "memory");
 }
 // This CTA's share of the next weight's bytes into L2 (16-byte units only:
 // nothing past the end of a range is touched).
@@ -704,7 +713,6 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
   uint4* xw = reinterpret_cast<uint4*>(smem + L.xw);
   float* xsf = reinterpret_cast<float*>(smem + L.xsf);
   const int lane = threadIdx.x & 31;
-  float rms = 1.f;
   constexpr bool REDUCE = XM == XS_X_REDUCE || XM == XS_X_REDUCE_NORM;
   float* xr = reinterpret_cast<float*>(smem + L.xr);
   if constexpr (REDUCE) {
@@ -746,23 +754,17 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
     }
     xs_named_sync(1, nthreads);
   }
-  if constexpr (XM == XS_X_NORM || XM == XS_X_REDUCE_NORM) {
-    float ss = 0.f;
-    for (int i = 4 * threadIdx.x; i < P.dim; i += 4 * nthreads) {
-      const float4 f = REDUCE ? *reinterpret_cast<const float4*>(xr + i) : ldg_f4(P.x + i);
-      ss = fmaf(f.x, f.x, ss);
-      ss = fmaf(f.y, f.y, ss);
-      ss = fmaf(f.z, f.z, ss);
-      ss = fmaf(f.w, f.w, ss);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    float* red = reinterpret_cast<float*>(smem + L.red);
-    if (lane == 0) red[threadIdx.x >> 5] = ss;
-    xs_named_sync(1, nthreads);
-    float t = 0.f;
-    for (int w = 0; w < (nthreads >> 5); ++w) t += red[w];
-    rms = sqrtf(t / (float)P.dim + P.eps);
+  // RMSNorm: the staged values are x * w and the kernel scales each output
+  // row by 1 / rms at the end (the product is linear in x; each superblock's
+  // power-of-two quantization scale absorbs the constant), so sum(x^2) is
+  // gathered here, in the same pass, and reduced after the staging barrier
+  constexpr bool NORM = XM == XS_X_NORM || XM == XS_X_REDUCE_NORM;
+  float ss = 0.f;
+  const float* nws = reinterpret_cast<const float*>(smem + L.nw);
+  if constexpr (NORM) {
+    // the norm weights were bulk-copied at kernel start (they do not depend on the previous kernel)
+    uint64_t* aux = reinterpret_cast<uint64_t*>(smem + L.bar) + 2 * P.S;
+    xs_bar_wait(aux, 0, P.err, XS_ERR_FULL);
   }
   const int total = XS_SPW * P.nk * 8;  // multiple of 64
   for (int base = (threadIdx.x & ~31); base < total; base += nthreads) {
@@ -784,22 +786,24 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
         if (live && gi < P.dim) {
           f = *reinterpret_cast<const float4*>(xr + gi);
           if constexpr (XM == XS_X_REDUCE_NORM) {
-            const float4 wv = ldg_f4(P.nw + gi);
-            f.x = f.x / rms * wv.x;
-            f.y = f.y / rms * wv.y;
-            f.z = f.z / rms * wv.z;
-            f.w = f.w / rms * wv.w;
+            const float4 wv = *reinterpret_cast<const float4*>(nws + gi);
+            ss = fmaf(f.x, f.x, fmaf(f.y, f.y, fmaf(f.z, f.z, fmaf(f.w, f.w, ss))));
+            f.x *= wv.x;
+            f.y *= wv.y;
+            f.z *= wv.z;
+            f.w *= wv.w;
           }
         }
       } else if constexpr (XM == XS_X_NORM) {
         const int64_t gi = (int64_t)kb * 256 + off;
         if (live && gi < P.dim) {
           f = ldg_f4(xrow + off);
-          const float4 wv = ldg_f4(P.nw + gi);
-          f.x = f.x / rms * wv.x;
-          f.y = f.y / rms * wv.y;
-          f.z = f.z / rms * wv.z;
-          f.w = f.w / rms * wv.w;
+          const float4 wv = *reinterpret_cast<const float4*>(nws + gi);
+          ss = fmaf(f.x, f.x, fmaf(f.y, f.y, fmaf(f.z, f.z, fmaf(f.w, f.w, ss))));
+          f.x *= wv.x;
+          f.y *= wv.y;
+          f.z *= wv.z;
+          f.w *= wv.w;
         }
       } else {
         if (live) {
@@ -807,7 +811,7 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
           f.x = swiglu_gate(g.x, P.act) * uu.x;
           f.y = swiglu_gate(g.y, P.act) * uu.y;
           f.z = swiglu_gate(g.z, P.act) * uu.z;
-          f.w = swiglu_gate(g.w, P.act) * uu.w;
+          f.w = swiglu_gate(g.w, P.act) * uu.w;  // fast exp: see swiglu_gate
         }
       }
       v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
@@ -866,6 +870,11 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
     }
     if ((hu & 7) == 0) xsf[kb] = live ? sc.factor : 0.f;
   }
+  if constexpr (NORM) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) reinterpret_cast<float*>(smem + L.red)[threadIdx.x >> 5] = ss;  // read after the staging barrier
+  }
 }
 
 template <int QT, int XM, int YM>
@@ -873,12 +882,14 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   extern __shared__ __align__(128) uint8_t xs_smem[];
   pdl_trigger();  // the next kernel's CTAs may start on each SM as ours retire there
   const int C = gridDim.x, b = blockIdx.x;
-  const int64_t r0 = (int64_t)P.n * b / C, r1 = (int64_t)P.n * (b + 1) / C;
+  // XS_Y_SWIGLU: rows come in (gate, up) pairs that must stay in one CTA
+  const int64_t r0 = YM == XS_Y_SWIGLU ? 2 * ((int64_t)(P.n / 2) * b / C) : (int64_t)P.n * b / C;
+  const int64_t r1 = YM == XS_Y_SWIGLU ? 2 * ((int64_t)(P.n / 2) * (b + 1) / C) : (int64_t)P.n * (b + 1) / C;
   const int rows = (int)(r1 - r0);  // this CTA's rows r0 .. r1-1
   const int R = 2 * P.G;  // rows per stage: each compute warp takes two of them
   const int T = (rows + R - 1) / R;
   const int NC = P.nk * P.G;
-  const XsSmem L(QT, P.nk, P.stage_bytes, P.S, P.rows_max, P.xr_floats);
+  const XsSmem L(QT, P.nk, P.stage_bytes, P.S, P.rows_max, P.xr_floats, P.nw_floats);
   uint64_t* full = reinterpret_cast<uint64_t*>(xs_smem + L.bar);
   uint64_t* empty = full + P.S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -887,6 +898,7 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
       xs_bar_init(&full[i], 1);
       xs_bar_init(&empty[i], NC);
     }
+    xs_bar_init(empty + P.S, 1);  // aux: the norm weights
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -894,6 +906,11 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   if (warp == NC) {
     // ---------------- producer: the weights do not depend on the previous kernel ----------------
     if (lane == 0) {
+      if constexpr (XM == XS_X_NORM || XM == XS_X_REDUCE_NORM) {
+        const uint32_t nb = (uint32_t)(P.dim * 4);  // a multiple of 16 (dim % 4 == 0)
+        xs_bar_expect(empty + P.S, nb);
+        xs_bulk_g2s_plain(xs_smem + L.nw, P.nw, nb, empty + P.S);
+      }
       uint64_t pol;
       asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
       // the next weight is prefetched once the ring's first fill is issued
@@ -916,6 +933,7 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
       if (t == fill && t == T) xs_prefetch(P, b, C);
       // the CTA must not retire while a copy into its shared memory is in flight
       for (int v = max(0, t - P.S); v < t; ++v) xs_bar_wait(&full[v % P.S], (v / P.S) & 1, P.err, XS_ERR_DRAIN);
+      if constexpr (XM == XS_X_NORM || XM == XS_X_REDUCE_NORM) xs_bar_wait(empty + P.S, 0, P.err, XS_ERR_DRAIN);
     }
     return;
   }
@@ -927,6 +945,13 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   pdl_wait();  // x may be the previous kernel's output
   xs_stage_x<QT, XM>(P, L, xs_smem, NC * 32);
   xs_named_sync(1, NC * 32);
+  float yscale = 1.f;  // RMSNorm: 1 / sqrt(mean(x^2) + eps), applied to every output row
+  if constexpr (XM == XS_X_NORM || XM == XS_X_REDUCE_NORM) {
+    const float* red = reinterpret_cast<const float*>(xs_smem + L.red);
+    float t = 0.f;
+    for (int w = 0; w < NC; ++w) t += red[w];
+    yscale = 1.f / sqrtf(t / (float)P.dim + P.eps);
+  }
 
   // this lane's 64 activations, from the staged copy
   uint4 X[8];
@@ -1072,12 +1097,25 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
     if (lane == 0) xs_bar_arrive(&empty[st]);
   }
   xs_named_sync(1, NC * 32);
-  if constexpr (YM == XS_Y_LOCAL) {
+  if constexpr (YM == XS_Y_SWIGLU) {
+    // rows (2j, 2j + 1) = (gate, up) of output j = r0 / 2 + j
+    for (int j = threadIdx.x; 2 * j < rows; j += NC * 32) {
+      float g = 0.f, u = 0.f;
+      for (int t = 0; t < P.nk; ++t) {
+        g += part[(2 * j) * P.nk + t];
+        u += part[(2 * j + 1) * P.nk + t];
+      }
+      const int64_t row = r0 + 2 * j;
+      g = fmaf(g, yscale, P.bias ? P.bias[row] : 0.f);
+      u = fmaf(u, yscale, P.bias ? P.bias[row + 1] : 0.f);
+      P.y[r0 / 2 + j] = swiglu_gate(g, P.act) * u;
+    }
+  } else if constexpr (YM == XS_Y_LOCAL) {
     for (int q = threadIdx.x; q < rows; q += NC * 32) {
       float acc = 0.f;
       for (int t = 0; t < P.nk; ++t) acc += part[q * P.nk + t];
       const int64_t row = r0 + q;
-      P.y[row] = acc + (P.bias ? P.bias[row] : 0.f);
+      P.y[row] = fmaf(acc, yscale, P.bias ? P.bias[row] : 0.f);
     }
   } else {
     // this exchange's epoch: one past the last; the last CTA to arrive
@@ -1102,7 +1140,7 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
 
 struct XsLaunch {
   bool ok = false;
-  int64_t xr_floats = 0;
+  int64_t xr_floats = 0, nw_floats = 0;
   int threads = 0, grid = 0, G = 0, S = 0, rows_max = 0;
   int64_t stage_bytes = 0;
   size_t smem = 0;
@@ -1110,9 +1148,10 @@ struct XsLaunch {
 
 // Launch shape of the single-token kernel, or ok = false when it does not
 // apply (more than XS_MAX_COMPUTE slices, or a ring of fewer than 2 stages).
-XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms, int64_t xr_floats = 0) {
+XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms, int64_t xr_floats = 0, int64_t nw_floats = 0) {
   XsLaunch r;
   r.xr_floats = xr_floats;
+  r.nw_floats = nw_floats;
   const int nk = (int)((sb + XS_SPW - 1) / XS_SPW);
   if (n < 1 || nk < 1 || nk > XS_MAX_COMPUTE) return r;
   r.G = XS_MAX_COMPUTE / nk;
@@ -1123,14 +1162,14 @@ XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms, int64_t xr_floats 
   const int64_t d_row_bytes = qt == GGUF_Q6_K ? q6k_d_ld(sb) * 2 : 0;
   r.stage_bytes = 2 * r.G * (row_bytes + d_row_bytes);  // 2G rows per stage
   const int T = (r.rows_max + 2 * r.G - 1) / (2 * r.G);
-  const size_t fixed = XsSmem(qt, nk, r.stage_bytes, 0, r.rows_max, xr_floats).end + 64;
+  const size_t fixed = XsSmem(qt, nk, r.stage_bytes, 0, r.rows_max, xr_floats, nw_floats).end + 64;
   if (fixed >= (size_t)XS_MAX_SMEM) return r;
   const int64_t fit = (int64_t)((XS_MAX_SMEM - fixed) / (size_t)(r.stage_bytes + 16));
   const int64_t want = std::max<int64_t>(2, (XS_INFLIGHT + r.stage_bytes / 2) / r.stage_bytes);
   const int S = (int)std::min<int64_t>(std::min<int64_t>(T, fit), want);
   if (S < std::min(T, 2)) return r;
   r.S = S;
-  r.smem = XsSmem(qt, nk, r.stage_bytes, S, r.rows_max, xr_floats).end;
+  r.smem = XsSmem(qt, nk, r.stage_bytes, S, r.rows_max, xr_floats, nw_floats).end;
   r.ok = r.smem <= (size_t)XS_MAX_SMEM;
   return r;
 }
@@ -1165,6 +1204,7 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
   }
   P.tp = in.tp;
   P.xr_floats = sh.xr_floats;
+  P.nw_floats = sh.nw_floats;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)sh.grid);
   cfg.blockDim = dim3((unsigned)sh.threads);
@@ -1175,6 +1215,14 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (in.ymode == XS_Y_SWIGLU) {
+    switch (in.mode) {
+      case XS_X_PLAIN: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_SWIGLU>, P);
+      case XS_X_NORM: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_NORM, XS_Y_SWIGLU>, P);
+      case XS_X_REDUCE_NORM: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_REDUCE_NORM, XS_Y_SWIGLU>, P);
+    }
+    return cudaErrorInvalidValue;
+  }
   if (in.ymode == XS_Y_PEERS) {
     switch (in.mode) {
       case XS_X_PLAIN: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_PEERS>, P);
@@ -1250,6 +1298,9 @@ static cudaError_t xs_attrs() {
   if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_REDUCE_NORM, XS_Y_LOCAL>);
   if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_PEERS>);
   if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_SWIGLU, XS_Y_PEERS>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_SWIGLU>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_NORM, XS_Y_SWIGLU>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<QT, XS_X_REDUCE_NORM, XS_Y_SWIGLU>);
   return e;
 }
 
@@ -1264,7 +1315,10 @@ cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* b
   if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
   if (in.mode < XS_X_PLAIN || in.mode > XS_X_REDUCE_NORM) return cudaErrorInvalidValue;
   const bool reduce = in.mode == XS_X_REDUCE || in.mode == XS_X_REDUCE_NORM;
-  const XsLaunch sh = xs_shape(w.type, w.n, w.sb, num_sms, reduce ? (int64_t)((in.dim + 3) & ~3) : 0);
+  const bool norm = in.mode == XS_X_NORM || in.mode == XS_X_REDUCE_NORM;
+  if (in.ymode == XS_Y_SWIGLU && (w.n & 1)) return cudaErrorInvalidValue;
+  const int64_t vec = (int64_t)((in.dim + 3) & ~3);
+  const XsLaunch sh = xs_shape(w.type, w.n, w.sb, num_sms, reduce ? vec : 0, norm ? vec : 0);
   if (!sh.ok) return cudaErrorNotSupported;
   bracket_record(br.start, s);
   cudaError_t e = w.type == GGUF_Q4_K ? launch_xs<GGUF_Q4_K>(w, in, bias, y, err, pf, s, sh)

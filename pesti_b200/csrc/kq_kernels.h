@@ -135,7 +135,9 @@ enum : int { XS_X_PLAIN = 0, XS_X_NORM = 1, XS_X_SWIGLU = 2, XS_X_REDUCE = 3, XS
 // Destination of y: this rank's buffer, or (XS_Y_PEERS) slot rows
 // [rank * n, rank * n + n) of every rank's exchange image, then the
 // exchange's epoch is published in every rank's flags.
-enum : int { XS_Y_LOCAL = 0, XS_Y_PEERS = 1 };
+// XS_Y_SWIGLU: the weight's rows are (gate, up) pairs and y[j] =
+// swiglu_gate(row 2j, act) * row 2j+1 (n / 2 outputs).
+enum : int { XS_Y_LOCAL = 0, XS_Y_PEERS = 1, XS_Y_SWIGLU = 2 };
 constexpr int TP_MAX_WORLD = 8;
 // Exchange buffers (as in TpArgs): two slots of slot_elems 8-byte words.
 // A word is {f32 value bits, epoch}: a reader takes a value once its word
@@ -160,7 +162,7 @@ struct XsInput {
   const float* nw = nullptr;  // XS_X_NORM: norm weights [dim]
   int dim = 0;                // XS_X_NORM: elements normalised (x and the result are zero past dim)
   float eps = 0.f;
-  int act = 0;                // XS_X_SWIGLU: gate activation (swiglu_gate)
+  int act = 0;                // XS_X_SWIGLU / XS_Y_SWIGLU: gate activation (swiglu_gate)
 };
 // Single-token GEMV y = act(x) . W^T (+bias; bias may alias y) for GGUF
 // Q4_K / Q6_K; cudaErrorNotSupported when the kernel does not apply to the

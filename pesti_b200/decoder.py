@@ -74,12 +74,12 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "kq_dec_swiglu": [P, P, P, I64, I64, I],
         "kq_dec_add": [P, P, I64, P, I64, I64, I64],
         "kq_dec_embed": [P, P, P, P, I64, I64, I64],
-        "kq_dec_norm_linear": [P, P, P, P, I64, F, P, P, I],
+        "kq_dec_norm_linear": [P, P, P, P, I64, F, I, P, P, I],
         "kq_dec_swiglu_linear": [P, P, P, I, P, P, I],
         "kq_dec_residual_linear": [P, P, P, P, I],
         "kq_dec_rope_attention": [P, P, I64, P, P, P, I64, I64, I, I, I, I64, I64, F, P, Z],
         "kq_dec_tp_partial_linear": [P, P, P, I, I],
-        "kq_dec_tp_reduce_linear": [P, P, P, P, P, I64, F, P, I],
+        "kq_dec_tp_reduce_linear": [P, P, P, P, P, I64, F, I, P, I],
     }
     for name, args in sig.items():
         getattr(lib, name).argtypes = args
@@ -207,7 +207,10 @@ class Decoder:
             keep((li, "gate"), wg)
             keep((li, "up"), wu)
             f0, f1 = self.f_rows
-            gu = torch.cat([wg[f0:f1], wu[f0:f1]]).contiguous()
+            if self.fused:  # (gate, up) row pairs: the GEMV applies the SwiGLU itself
+                gu = torch.stack([wg[f0:f1], wu[f0:f1]], dim=1).reshape(2 * (f1 - f0), -1).contiguous()
+            else:
+                gu = torch.cat([wg[f0:f1], wu[f0:f1]]).contiguous()
             L["gu"] = upload(gu, cfg.linear_type, 2 * (f1 - f0), self.Dp)
             del wg, wu, gu
             wd = gguf_weight_device(cfg.down_type, D, F, slot(li, "down"), dev)
@@ -287,13 +290,14 @@ class Decoder:
         if self.prefetch:
             self.ctx.prefetch_next(self._next[id(w)])
 
-    def _norm_linear(self, w, norm, y) -> None:
-        """y = rmsnorm(h; norm) . W^T (token 0 only when fused)."""
+    def _norm_linear(self, w, norm, y, act: int = -1) -> None:
+        """y = rmsnorm(h; norm) . W^T (token 0 only when fused; act >= 0: SwiGLU
+        of (gate, up) row pairs)."""
         ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
         c, cfg = self.ctx.handle, self.cfg
         self._hint(w)
         if self.fused:
-            self._check(self.lib.kq_dec_norm_linear(c, w.handle, ptr(self.h), ptr(norm), cfg.dim, cfg.eps, None,
+            self._check(self.lib.kq_dec_norm_linear(c, w.handle, ptr(self.h), ptr(norm), cfg.dim, cfg.eps, act, None,
                                                     ptr(y), 0), "norm_linear")
             return
         self._check(self.lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(norm), ptr(self.a), self.Dp, self.batch,
@@ -342,12 +346,14 @@ class Decoder:
             else:
                 L["o"].linear(self.attn, B, self.o, device_ptrs=True)
                 self._check(lib.kq_dec_add(c, ptr(self.h), self.Dp, ptr(self.o), D, B, D), "add")
+            if self.fused and not tp:
+                # gate/up pairs + SwiGLU in one GEMV, then the down projection's residual update
+                self._norm_linear(L["gu"], L["ffn_norm"], self.s, act=self.swiglu_mode)
+                self._hint(L["down"])
+                self._check(lib.kq_dec_residual_linear(c, L["down"].handle, ptr(self.s), ptr(self.h), 0), "down")
+                continue
             self._norm_linear(L["gu"], L["ffn_norm"], self.gu)
             self._hint(L["down"])
-            if self.fused and not tp:
-                self._check(lib.kq_dec_swiglu_linear(c, L["down"].handle, ptr(self.gu), self.swiglu_mode,
-                                                     ptr(self.h), ptr(self.h), 0), "swiglu_linear")
-                continue
             self._check(lib.kq_dec_swiglu(c, ptr(self.gu), ptr(self.s_r if tp else self.s), B, f1 - f0,
                                           self.swiglu_mode), "swiglu")
             if tp:
@@ -380,16 +386,16 @@ class Decoder:
         self._check(lib.kq_dec_embed(c, ptr(self.embed), ptr(self.tokens), ptr(cur), self.Dp, 1, D), "embed")
         pending = False  # an exchange of partials waits to be added to `cur`
 
-        def reduce_linear(w, norm, y):
+        def reduce_linear(w, norm, y, act=-1):
             nonlocal cur, nxt
             self._hint(w)
             if not pending:
-                self._check(lib.kq_dec_norm_linear(c, w.handle, ptr(cur), ptr(norm), D, cfg.eps, None, ptr(y), 0),
-                            "norm_linear")
+                self._check(lib.kq_dec_norm_linear(c, w.handle, ptr(cur), ptr(norm), D, cfg.eps, act, None, ptr(y),
+                                                   0), "norm_linear")
                 return
             self._check(lib.kq_dec_tp_reduce_linear(tph, w.handle, ptr(cur), ptr(nxt),
-                                                    ptr(norm) if norm is not None else None, D, cfg.eps, ptr(y), 0),
-                        "tp_reduce_linear")
+                                                    ptr(norm) if norm is not None else None, D, cfg.eps, act, ptr(y),
+                                                    0), "tp_reduce_linear")
             cur, nxt = nxt, cur
 
         for L in self.layers:
@@ -401,10 +407,9 @@ class Decoder:
             self._hint(L["o"])
             self._check(lib.kq_dec_tp_partial_linear(tph, L["o"].handle, ptr(self.attn_r), -1, 0), "o partial")
             pending = True
-            reduce_linear(L["gu"], L["ffn_norm"], self.gu)
+            reduce_linear(L["gu"], L["ffn_norm"], self.s_r, act=self.swiglu_mode)
             self._hint(L["down"])
-            self._check(lib.kq_dec_tp_partial_linear(tph, L["down"].handle, ptr(self.gu), self.swiglu_mode, 0),
-                        "down partial")
+            self._check(lib.kq_dec_tp_partial_linear(tph, L["down"].handle, ptr(self.s_r), -1, 0), "down partial")
             pending = True
         v0, v1 = self.v_rows
         self._hint(self.head)

@@ -54,11 +54,41 @@ def test_norm_linear_matches_rmsnorm_then_linear(gpu_ctx, dt, n, k, dim):
     nw = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
     w = kq.Weight(gpu_ctx, kt, raw, n, k)
     hd, nwd, yd = _dev(h), _dev(nw), _dev(np.full((1, n), np.nan, np.float32))
-    rc = _lib(gpu_ctx).kq_dec_norm_linear(gpu_ctx.handle, w.handle, _p(hd), _p(nwd), dim, 1e-5, None, _p(yd), kq.KQ_SYNC)
+    rc = _lib(gpu_ctx).kq_dec_norm_linear(gpu_ctx.handle, w.handle, _p(hd), _p(nwd), dim, 1e-5, -1, None, _p(yd),
+                                          kq.KQ_SYNC)
     gpu_ctx.check(rc, "norm_linear")
     a = np.zeros((1, k), np.float32)
     a[0, :dim] = decoder_oracle.rmsnorm(h[:, :dim], nw, 1e-5)
     ref = a.astype(np.float64) @ _w64(ot, raw, n, k).T
+    assert rel_err(yd.cpu().numpy(), ref) <= TOL
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("mode", [dec.SWIGLU_REFERENCE, dec.SWIGLU_SILU])
+def test_norm_linear_with_swiglu_pairs(gpu_ctx, dt, mode):
+    """Gate and up projections as interleaved row pairs of one weight, the
+    SwiGLU applied in the GEMV's epilogue: y[j] = swiglu(gate_j . a, up_j . a)
+    with a = rmsnorm(h)."""
+    kt, ot = GGUF[dt]
+    f, k, dim = 1000, 4096, 4000
+    rng = np.random.default_rng(mode + 31)
+    raw_g = synthetic.gguf_weight(kt, f, k, seed=41)
+    raw_u = synthetic.gguf_weight(kt, f, k, seed=42)
+    rb = raw_g.size // f
+    pairs = np.stack([raw_g.reshape(f, rb), raw_u.reshape(f, rb)], axis=1).reshape(-1)
+    h = np.zeros((1, k), np.float32)
+    h[0, :dim] = 2.0 * rng.standard_normal(dim)
+    nw = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, pairs, 2 * f, k)
+    hd, nwd, yd = _dev(h), _dev(nw), _dev(np.full((1, f), np.nan, np.float32))
+    rc = _lib(gpu_ctx).kq_dec_norm_linear(gpu_ctx.handle, w.handle, _p(hd), _p(nwd), dim, 1e-6, mode, None, _p(yd),
+                                          kq.KQ_SYNC)
+    gpu_ctx.check(rc, "norm_linear pairs")
+    a = np.zeros((1, k), np.float32)
+    a[0, :dim] = decoder_oracle.rmsnorm(h[:, :dim], nw, 1e-6)
+    g = a.astype(np.float64) @ _w64(ot, raw_g, f, k).T
+    u = a.astype(np.float64) @ _w64(ot, raw_u, f, k).T
+    ref = decoder_oracle.swiglu(g.astype(np.float32), u.astype(np.float32), mode)
     assert rel_err(yd.cpu().numpy(), ref) <= TOL
 
 
@@ -101,8 +131,11 @@ def test_fused_linears_reject_what_they_cannot_run(gpu_ctx):
     w = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q4_K, raw, 8, 256)
     x, y = _dev(np.zeros((1, 256), np.float32)), _dev(np.zeros((1, 8), np.float32))
     h = gpu_ctx.handle
-    assert lib.kq_dec_norm_linear(h, w.handle, _p(x), _p(x), 6, 1e-5, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
-    assert lib.kq_dec_norm_linear(h, w.handle, _p(x), _p(x), 512, 1e-5, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
+    assert lib.kq_dec_norm_linear(h, w.handle, _p(x), _p(x), 6, 1e-5, -1, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
+    assert lib.kq_dec_norm_linear(h, w.handle, _p(x), _p(x), 512, 1e-5, -1, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
+    assert lib.kq_dec_norm_linear(h, w.handle, _p(x), _p(x), 256, 1e-5, 2, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
+    odd = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q4_K, synthetic.gguf_weight(kq.KQ_GGUF_Q4_K, 7, 256, seed=1), 7, 256)
+    assert lib.kq_dec_norm_linear(h, odd.handle, _p(x), _p(x), 256, 1e-5, 0, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
     assert lib.kq_dec_swiglu_linear(h, w.handle, _p(x), 2, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
     assert lib.kq_dec_residual_linear(h, w.handle, None, _p(y), 0) == kq.KQ_ERR_INVALID_ARG
     # a row too long for the single-token kernel (121 superblocks)
