@@ -86,8 +86,8 @@ def parse():
     p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a"], default="auto",
                    help="kernel family for the GEMV (auto: dp4a m<=4, mma m<=64, tcgen05 above)")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--no-prefetch", action="store_true",
-                   help="GEMV stream without the next-weight L2 prefetch hint")
+    p.add_argument("--prefetch", action="store_true",
+                   help="each GEMV prefetches the next one's weight into L2 (kq_ctx_prefetch_next)")
     p.add_argument("--no-fuse", action="store_true",
                    help="decoders: separate RMSNorm / SwiGLU / add kernels at batch 1")
     return p.parse_args()
@@ -315,7 +315,7 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.Stream(dev)
     ctx.set_stream(stream.cuda_stream)
 
-    def step(prefetch=not args.no_prefetch):
+    def step(prefetch=args.prefetch):
         # a stream of GEMVs as in a decode step: each call is told the weight
         # the next one reads (kq_ctx_prefetch_next), the last one the first
         for i, (w, y) in enumerate(zip(weights, ys)):
@@ -340,9 +340,9 @@ def run_ours(args, rank, world, local_rank):
     plain = torch.cuda.CUDAGraph()  # the bracket budget is used up: no events
     with torch.cuda.graph(plain, stream=stream):
         step()
-    plain_np = torch.cuda.CUDAGraph()  # the same stream without prefetch hints
+    plain_np = torch.cuda.CUDAGraph()  # the same stream with the other prefetch setting
     with torch.cuda.graph(plain_np, stream=stream):
-        step(prefetch=False)
+        step(prefetch=not args.prefetch)
 
     for _ in range(max(args.warmup, 3)):
         plain.replay()
@@ -436,11 +436,11 @@ def run_ours(args, rank, world, local_rank):
                        "weight_bytes_per_gemv": wbytes, "algorithmic_bytes_per_gemv": alg,
                        "l2": f"inputs larger than L2 ({NUM_WEIGHTS * wbytes / 1e6:.0f} MB of weights per step)",
                        "parallelism": f"replicas x{world} (independent weights per rank, no data-path collective)",
-                       "prefetch": ("off" if args.no_prefetch else
-                                    "each GEMV prefetches the next one's weight into L2 (kq_ctx_prefetch_next)")},
-            "without_prefetch": {"value": round(world * NUM_WEIGHTS * alg / (ms_total_np / args.steps * 1e-3) / 1e9,
-                                                2),
-                                 "ms_per_step": round(ms_total_np / args.steps, 5)},
+                       "prefetch": ("each GEMV prefetches the next one's weight into L2 (kq_ctx_prefetch_next)"
+                                    if args.prefetch else "off")},
+            ("without_prefetch" if args.prefetch else "with_prefetch"): {
+                "value": round(world * NUM_WEIGHTS * alg / (ms_total_np / args.steps * 1e-3) / 1e9, 2),
+                "ms_per_step": round(ms_total_np / args.steps, 5)},
             "gpu_launches": launches_per_step * args.steps,
             "pct_hbm_peak": round(100.0 * value / world / peak, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
@@ -643,7 +643,7 @@ def run_decoder(args, rank, world, local_rank):
     if world > 1:
         tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, B))
     model = dec.Decoder(cfg, ctx, B, ctx_len, max_new=2, world=world, rank=rank, tp=tp, seed=11,
-                        fused=not args.no_fuse, prefetch=not args.no_prefetch)
+                        fused=not args.no_fuse, prefetch=args.prefetch)
     gen = torch.Generator(device=dev)
     gen.manual_seed(3)
     model.tokens.copy_(torch.randint(0, cfg.vocab, (B,), generator=gen, device=dev, dtype=torch.int32))

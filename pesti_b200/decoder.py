@@ -135,7 +135,7 @@ class Decoder:
     def __init__(self, cfg: DecoderConfig, ctx: "kq.Context", batch: int, context_len: int, max_new: int = 8,
                  world: int = 1, rank: int = 0, tp: Optional["kq.TensorParallel"] = None, seed: int = 0,
                  swiglu_mode: int = SWIGLU_REFERENCE, kv_scale: float = 1.0, keep_raw: bool = False,
-                 fused: bool = True, prefetch: bool = True):
+                 fused: bool = True, prefetch: bool = False):
         import torch
         if cfg.heads % world or cfg.kv_heads % world:
             raise ValueError(f"{cfg.name}: {cfg.heads} query / {cfg.kv_heads} KV heads do not split over {world}")
