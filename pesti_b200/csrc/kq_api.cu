@@ -765,6 +765,7 @@ int kq_tp_allgather_f32(kq_tp* tp, const float* y_local, int64_t m, int64_t row0
   a.ctr = tp->ctr;
   a.epoch = tp->ctr + 1;
   a.err = ctx->dev_err;
+  // about 8 gathered elements per thread (one batch of reads), at most one CTA per SM
   const int64_t work = m * n_total;
   const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ctx->num_sms, (work + 4095) / 4096));
   cudaError_t e = kq::launch_tp_allgather(a, blocks, ctx->stream);

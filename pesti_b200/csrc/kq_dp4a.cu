@@ -728,27 +728,39 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
     bool ok = true;
     for (int i = 4 * threadIdx.x; i < P.dim; i += 4 * nthreads) {
       float4 v = __ldcg(reinterpret_cast<const float4*>(T.h_in + i));
-      for (int r = 0; r < T.world; ++r) {
-        const unsigned long long* wp = img + (size_t)r * P.dim + i;
-        unsigned long long w0, w1, w2, w3;
-        for (uint32_t it = 0;; ++it) {
-          ld_words2(wp, w0, w1);
-          ld_words2(wp + 2, w2, w3);
-          if (!ok || ((unsigned)(w0 >> 32) == epoch && (unsigned)(w1 >> 32) == epoch &&
-                      (unsigned)(w2 >> 32) == epoch && (unsigned)(w3 >> 32) == epoch))
-            break;
-          if (it >= (1u << 22) || ((it & 255u) == 255u && *(volatile int*)P.err)) {
-            atomicCAS(P.err, 0, XS_ERR_TP);  // the output is invalid; the kernel still runs to its end
-            ok = false;
-            break;
+      // all ranks' words of these 4 elements in flight at once; re-read only
+      // while some word still carries an older epoch
+      unsigned long long w[TP_MAX_WORLD][4];
+      for (uint32_t it = 0;; ++it) {
+#pragma unroll
+        for (int r = 0; r < TP_MAX_WORLD; ++r)
+          if (r < T.world) {
+            const unsigned long long* wp = img + (size_t)r * P.dim + i;
+            ld_words2(wp, w[r][0], w[r][1]);
+            ld_words2(wp + 2, w[r][2], w[r][3]);
           }
-          __nanosleep(32);
+        bool ready = true;
+#pragma unroll
+        for (int r = 0; r < TP_MAX_WORLD; ++r)
+          if (r < T.world)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) ready = ready && (unsigned)(w[r][c] >> 32) == epoch;
+        if (ready || !ok) break;
+        if (it >= (1u << 22) || ((it & 255u) == 255u && *(volatile int*)P.err)) {
+          atomicCAS(P.err, 0, XS_ERR_TP);  // the output is invalid; the kernel still runs to its end
+          ok = false;
+          break;
         }
-        v.x += __uint_as_float((unsigned)w0);
-        v.y += __uint_as_float((unsigned)w1);
-        v.z += __uint_as_float((unsigned)w2);
-        v.w += __uint_as_float((unsigned)w3);
+        __nanosleep(32);
       }
+#pragma unroll
+      for (int r = 0; r < TP_MAX_WORLD; ++r)
+        if (r < T.world) {  // rank order: every rank sums the same way
+          v.x += __uint_as_float((unsigned)w[r][0]);
+          v.y += __uint_as_float((unsigned)w[r][1]);
+          v.z += __uint_as_float((unsigned)w[r][2]);
+          v.w += __uint_as_float((unsigned)w[r][3]);
+        }
       *reinterpret_cast<float4*>(xr + i) = v;
       if (i >= lo && i < hi) *reinterpret_cast<float4*>(T.h_out + i) = v;
     }

@@ -64,26 +64,42 @@ __global__ void __launch_bounds__(512) tp_allgather_kernel(const __grid_constant
     *A.ctr = 0u;
     *A.epoch = epoch;
   }
-  // phase 2: each element of my image once its word carries this epoch
+  // phase 2: each element of my image once its word carries this epoch;
+  // a thread reads up to 8 words at once and re-reads only while one is old
+  constexpr int U = 8;
   const unsigned long long* image = A.exch[A.rank] + slot;
   const int64_t all = A.m * A.n;
   bool ok = true;
-  for (int64_t e = tid; e < all && ok; e += stride) {
-    unsigned long long w = ld_word(image + e);
-    for (uint32_t i = 0; (unsigned)(w >> 32) != epoch; ++i) {
-      if (i >= (1u << 22) || ((i & 255u) == 255u && *(volatile int*)A.err)) {
+  for (int64_t e0 = tid; e0 < all && ok; e0 += stride * U) {
+    unsigned long long w[U];
+    for (uint32_t it = 0;; ++it) {
+      bool ready = true;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t e = e0 + (int64_t)u * stride;
+        w[u] = e < all ? ld_word(image + e) : tag;
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) ready = ready && (unsigned)(w[u] >> 32) == epoch;
+      if (ready) break;
+      if (it >= (1u << 22) || ((it & 255u) == 255u && *(volatile int*)A.err)) {
         atomicCAS(A.err, 0, ERR_TP_WAIT);
         ok = false;
         break;
       }
       __nanosleep(32);
-      w = ld_word(image + e);
     }
     if (!ok) break;
-    const int64_t t = e / A.n, j = e - t * A.n;
-    float* dst = A.y_out + t * A.y_ld + j;
-    const float v = __uint_as_float((unsigned)w);
-    *dst = A.accumulate ? *dst + v : v;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t e = e0 + (int64_t)u * stride;
+      if (e < all) {
+        const int64_t t = e / A.n, j = e - t * A.n;
+        float* dst = A.y_out + t * A.y_ld + j;
+        const float v = __uint_as_float((unsigned)w[u]);
+        *dst = A.accumulate ? *dst + v : v;
+      }
+    }
   }
 }
 

@@ -153,6 +153,10 @@ class Decoder:
         # all-gathering row blocks (4); needs both blocks on superblock edges
         self.col_split = (world > 1 and self.fused and (cfg.heads // world * cfg.head_dim) % 256 == 0
                           and cfg.ffn % (256 * world) == 0)
+        # gate/up as (gate, up) row pairs with the SwiGLU in the GEMV epilogue: the
+        # paths that run it (one GPU or the column split at batch 1); otherwise
+        # [gate block | up block] for the separate SwiGLU kernel
+        self.pairs = self.fused and (world == 1 or self.col_split)
         self.lib = _bind(ctx.lib)
         dev = torch.device("cuda", ctx.device)
         self.device = dev
@@ -207,7 +211,7 @@ class Decoder:
             keep((li, "gate"), wg)
             keep((li, "up"), wu)
             f0, f1 = self.f_rows
-            if self.fused:  # (gate, up) row pairs: the GEMV applies the SwiGLU itself
+            if self.pairs:  # (gate, up) row pairs: the GEMV applies the SwiGLU itself
                 gu = torch.stack([wg[f0:f1], wu[f0:f1]], dim=1).reshape(2 * (f1 - f0), -1).contiguous()
             else:
                 gu = torch.cat([wg[f0:f1], wu[f0:f1]]).contiguous()

@@ -20,6 +20,9 @@ LLAMA_TINY = dec.DecoderConfig("llama-like-tiny", 2, 512, 4, 2, 128, 768, 300, 1
 # FFN 1024: both column blocks fall on superblock edges at 2 ranks, so batch 1
 # takes the column-split exchange of partials (batch 2 the row all-gathers)
 LLAMA_TINY_TP = dec.DecoderConfig("llama-like-tiny-tp", 2, 512, 4, 2, 128, 1024, 300, 1e-5, 5e5, False)
+# 16 query / 8 KV heads of 128 and FFN 4096: the column blocks stay on superblock
+# edges up to 8 ranks (2 heads = 256 columns, FFN block 512)
+LLAMA_TINY_TP8 = dec.DecoderConfig("llama-like-tiny-tp8", 2, 1024, 16, 8, 128, 4096, 300, 1e-5, 5e5, False)
 
 
 def rel_err(y, ref):
@@ -105,7 +108,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _tp_worker(rank, world, port, out_dir):
+def _tp_worker(rank, world, port, out_dir, cfg_names=("LLAMA_TINY", "LLAMA_TINY_TP")):
     import datetime
     import torch
     import torch.distributed as dist
@@ -117,14 +120,14 @@ def _tp_worker(rank, world, port, out_dir):
     status = "ok"
     try:
         ctx = kq.Context(rank)
-        for cfg in (LLAMA_TINY, LLAMA_TINY_TP):
+        for cfg in (globals()[c] for c in cfg_names):
             tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, 2))
             for batch in (1, 2):
                 model = dec.Decoder(cfg, ctx, batch, 20, max_new=3, world=world, rank=rank, tp=tp, seed=7,
                                     keep_raw=True)
                 single = dec.Decoder(cfg, ctx, batch, 20, max_new=3, seed=7)
-                expect_split = cfg is LLAMA_TINY_TP and batch == 1
-                if model.col_split != expect_split:
+                expect_split = cfg is not LLAMA_TINY and batch == 1
+                if status == "ok" and model.col_split != expect_split:
                     status = f"{cfg.name} batch {batch}: column split {model.col_split}"
                 ks, vs = _oracle_caches(model, cfg)
                 for pos in (20, 21):  # two steps: the exchange slots alternate
@@ -140,7 +143,7 @@ def _tp_worker(rank, world, port, out_dir):
                     # 15-bit quantization can round a value one step apart, so it is held to the
                     # oracle's tolerance and half of it against one GPU.
                     tol = TOL / 2 if model.col_split else 1e-5
-                    if not np.isfinite(a).all() or rel_err(a, b) > tol or rel_err(a, ref) > TOL:
+                    if status == "ok" and (not np.isfinite(a).all() or rel_err(a, b) > tol or rel_err(a, ref) > TOL):
                         status = (f"{cfg.name} batch {batch} pos {pos}: logits differ: {rel_err(a, b):.2e} "
                                   f"from one GPU, {rel_err(a, ref):.2e} from the oracle")
                 model.close()
@@ -160,4 +163,16 @@ def test_tensor_parallel_decode_matches_one_gpu(tmp_path):
     import torch.multiprocessing as mp
     mp.start_processes(_tp_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn", join=True)
     for r in range(2):
+        assert (tmp_path / f"r{r}").read_text() == "ok", f"rank {r}"
+
+
+@pytest.mark.skipif(_gpus() < 4, reason="needs 4 GPUs")
+def test_tensor_parallel_decode_on_every_gpu(tmp_path):
+    """4 or 8 ranks (all GPUs of the box, up to 8): column-split exchange at
+    batch 1, row all-gathers at batch 2, against one GPU and the oracle."""
+    import torch.multiprocessing as mp
+    world = 8 if _gpus() >= 8 else 4
+    mp.start_processes(_tp_worker, args=(world, _free_port(), str(tmp_path), ("LLAMA_TINY_TP8",)), nprocs=world,
+                       start_method="spawn", join=True)
+    for r in range(world):
         assert (tmp_path / f"r{r}").read_text() == "ok", f"rank {r}"
