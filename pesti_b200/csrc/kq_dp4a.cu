@@ -289,6 +289,12 @@ __device__ __forceinline__ int dp4a_s(uint32_t a, uint32_t b, int c) { return __
 __device__ __forceinline__ int dp4a_u(uint32_t a, uint32_t b, int c) {
   return (int)__dp4a(a, b, (unsigned)c);
 }
+// unsigned bytes of a times signed bytes of b
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
 
 // acc[t] += this lane's share of row . x_t for iteration `it`.
 template <int MT>
@@ -1009,14 +1015,16 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
         const uint4 qb = *reinterpret_cast<const uint4*>(blk + 32 + 32 * u);
         const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
         const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        // high nibbles are used in place (16 x the value, no shift per word);
+        // the B sums are divided by 16 once, exactly
         int ahi = 0, alo = 0, bhi = 0, blo = 0;
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
-          const uint32_t qa4 = W[w] & 0x0F0F0F0Fu, qb4 = (W[w] >> 4) & 0x0F0F0F0Fu;
+          const uint32_t qa4 = W[w] & 0x0F0F0F0Fu, qb16 = W[w] & 0xF0F0F0F0u;
           ahi = dp4a_s(qa4, X[w].x, ahi);
           alo = dp4a_u(qa4, X[w].y, alo);
-          bhi = dp4a_s(qb4, X[w].z, bhi);
-          blo = dp4a_u(qb4, X[w].w, blo);
+          bhi = dp4a_us(qb16, X[w].z, bhi);
+          blo = dp4a_u(qb16, X[w].w, blo);
         }
         const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
         uint32_t scp, mp;
@@ -1027,7 +1035,7 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
           scp = ((s2 >> sh) & 0x0F0Fu) | ((s0 >> (sh + 2)) & 0x3030u);
           mp = ((s2 >> (sh + 4)) & 0x0F0Fu) | ((s1 >> (sh + 2)) & 0x3030u);
         }
-        const int da = ahi * 256 + alo, db = bhi * 256 + blo;  // |.| < 2^23
+        const int da = ahi * 256 + alo, db = (bhi * 256 + blo) >> 4;  // |.| < 2^23 (16 | bhi, blo)
         const int iv = (int)(scp & 0xffu) * da + (int)(scp >> 8) * db;  // |iv| < 2^30
         const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xffff));
         const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
