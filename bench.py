@@ -83,7 +83,7 @@ def parse():
                    default="q6k-gemv")
     p.add_argument("--m", "--batch", dest="m", type=int, default=1,
                    help="tokens per call (decode batch); --batch is the form to use under torchrun")
-    p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a"], default="auto",
+    p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a", "imma"], default="auto",
                    help="kernel family for the GEMV (auto: dp4a m<=4, mma m<=64, tcgen05 above)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--prefetch", action="store_true",
@@ -309,7 +309,7 @@ def run_ours(args, rank, world, local_rank):
     x = torch.from_numpy(synthetic.activations(m, k, seed=7 + rank)).to(dev)
     ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _ in range(NUM_WEIGHTS)]
     ctx.set_path({"auto": kq.KQ_PATH_AUTO, "tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA,
-                  "dp4a": kq.KQ_PATH_DP4A}[args.path])
+                  "dp4a": kq.KQ_PATH_DP4A, "imma": kq.KQ_PATH_IMMA}[args.path])
     ctx.reserve(weights[0], m)
 
     stream = torch.cuda.Stream(dev)

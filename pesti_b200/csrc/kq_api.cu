@@ -169,7 +169,8 @@ int check_device_error(kq_ctx* ctx) {
   cudaGetLastError();
   return fail(ctx, KQ_ERR_CUDA,
               "a device-side wait gave up (code %d: 1-5 tcgen05 pipeline, 21-23 decode weight ring, 24 "
-              "attention KV ring, 31-32 tensor-parallel peer flag); the call's output is invalid",
+              "attention KV ring, 27-28 batched Q4_K ring, 31-32 tensor-parallel peer flag); the call's output "
+              "is invalid",
               code);
 }
 
@@ -188,9 +189,12 @@ int finish_sync(kq_ctx* ctx, const char* what) {
 // Kernel family for a GGUF f32 call of m tokens.  AUTO: integer dot products
 // up to DP4A_MAX_M tokens, warp-level mma.sync tiles up to 64, tcgen05 above
 // (the choice follows the measured decode throughput of each family).
-int f32_family(const kq_ctx* ctx, int64_t m) {
+int f32_family(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
+  const bool q4 = w.type == kq::GGUF_Q4_K;
+  if (ctx->path == KQ_PATH_IMMA) return q4 ? KQ_PATH_IMMA : KQ_PATH_MMA;
   if (ctx->path == KQ_PATH_MMA || ctx->path == KQ_PATH_TCGEN05) return ctx->path;
-  if (m <= kq::DP4A_MAX_M) return KQ_PATH_DP4A;
+  if (m == 1 || (m <= kq::DP4A_MAX_M && (!q4 || ctx->path == KQ_PATH_DP4A))) return KQ_PATH_DP4A;
+  if (q4 && m <= 64) return KQ_PATH_IMMA;
   return m <= 64 ? KQ_PATH_MMA : KQ_PATH_TCGEN05;
 }
 
@@ -198,9 +202,12 @@ int f32_family(const kq_ctx* ctx, int64_t m) {
 void f32_needs(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m, size_t* ws, size_t* ctr) {
   *ws = 0;
   *ctr = 0;
-  const int fam = f32_family(ctx, m);
+  const int fam = f32_family(ctx, w, m);
   if (fam == KQ_PATH_DP4A) {
     *ws = kq::dp4a_workspace_bytes(w.type, m, w.sb);
+  } else if (fam == KQ_PATH_IMMA) {
+    *ws = kq::imma_workspace_bytes(m, w.n, w.k, ctx->num_sms);
+    *ctr = kq::imma_counter_bytes(w.n);
   } else if (fam == KQ_PATH_TCGEN05) {
     *ws = kq::tc_workspace_bytes(m, w.n, w.k, ctx->num_sms);
     size_t off = 0;
@@ -255,6 +262,7 @@ int kq_ctx_create(int device, kq_ctx** out) {
   e = kq::gemv_init_device();
   if (e == cudaSuccess) e = kq::tc_init_device();
   if (e == cudaSuccess) e = kq::dp4a_init_device();
+  if (e == cudaSuccess) e = kq::imma_init_device();
   if (e == cudaSuccess) e = kq::dec_init_device();
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -308,7 +316,8 @@ int kq_ctx_set_stream(kq_ctx* ctx, void* stream) {
 
 int kq_ctx_set_path(kq_ctx* ctx, int path) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
-  if (path != KQ_PATH_AUTO && path != KQ_PATH_TCGEN05 && path != KQ_PATH_MMA && path != KQ_PATH_DP4A)
+  if (path != KQ_PATH_AUTO && path != KQ_PATH_TCGEN05 && path != KQ_PATH_MMA && path != KQ_PATH_DP4A &&
+      path != KQ_PATH_IMMA)
     return fail(ctx, KQ_ERR_INVALID_ARG, "unknown path %d", path);
   ctx->path = path;
   return KQ_OK;
@@ -590,8 +599,12 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
     e = kq::launch_tc_bf16(w->dw, xd, m, bd, yd, ctx->ws, ctx->dev_err, s, &launches, ctx->next_bracket());
   } else if (is_gguf(w->dw.type)) {
     if ((rc = prepare_f32(ctx, w->dw, m))) return rc;
-    const int fam = f32_family(ctx, m);
-    if (fam == KQ_PATH_DP4A) {
+    const int fam = f32_family(ctx, w->dw, m);
+    if (fam == KQ_PATH_IMMA) {
+      e = kq::launch_gemv_imma(w->dw, static_cast<const float*>(xd), m, bd, yd, ctx->ws,
+                               static_cast<unsigned*>(ctx->ctr), ctx->num_sms, ctx->dev_err, s, &launches,
+                               ctx->next_bracket());
+    } else if (fam == KQ_PATH_DP4A) {
       e = kq::launch_gemv_dp4a(w->dw, static_cast<const float*>(xd), m, bd, yd, ctx->ws, ctx->num_sms,
                                ctx->dev_err, s, &launches, ctx->next_bracket(), pf);
     } else if (fam == KQ_PATH_TCGEN05) {

@@ -1,0 +1,434 @@
+// kq_imma.cu -- batched decode linear (2..32 tokens) for GGUF Q4_K on the
+// integer tensor-core path: y[m][n] = x[m][k] . W[n][k] (+ bias).
+//
+// A Q4_K sub-block is 32 weights with one 6-bit scale and one 6-bit min, so it
+// is exactly one k32 step of mma.sync.m16n8k32 with 8-bit operands:
+//  * A = the raw codes: the qs bytes of a row hold sub-blocks 2p (low
+//    nibbles) and 2p+1 (high nibbles) of pair p, so one 32-bit load and one
+//    mask give a lane its four codes of an A fragment;
+//  * B = the activations as in the single-token kernel: per (token,
+//    superblock) a power of two 2^e with max|x| 2^-e in [2^13, 2^14), the
+//    15-bit integer split into a signed high byte and an unsigned low byte,
+//    so two MMAs (u8 x s8, u8 x u8) give exact int32 sums of q x;
+//  * per sub-block the int32 result is scaled by sc (f32 accumulate) and the
+//    min term dmin m_j sum(x) uses exact int32 sums of the quantized
+//    activations; d, dmin and 2^e are applied once per superblock.
+// Only the 15-bit activation rounding approximates, as in the single-token
+// kernel.
+//
+// Data movement: one CTA = 128 weight rows x a contiguous range of
+// superblocks (split-K across CTAs when there are few row tiles).  A producer
+// warp streams one superblock of all 128 rows per stage with one 2D TMA copy
+// (the weight's tensor map: box = one superblock x 128 rows), plus the
+// superblock's activation fragments and sums (bulk copies), through a ring of
+// shared-memory stages; eight MMA warps each own a 16-row tile of every
+// stage.  Partials of the K-splits are added in split order by the last CTA of
+// each row tile (deterministic).  Every wait is bounded.
+//
+// Reference semantics: QuantizedLinear::forward (pesti-runner/src/
+// quantized_linear.rs:101-143).
+#include "kq_common.cuh"
+#include "kq_kernels.h"
+#include "kq_sm100.cuh"
+
+#include <algorithm>
+
+namespace kq {
+namespace {
+
+constexpr int IM_WARPS = 8;
+constexpr int IM_ROWS = 16 * IM_WARPS;    // the weight maps' box height
+constexpr int IM_MAX_SMEM = 226 * 1024;   // dynamic; room for the static bytes
+constexpr int IM_ERR_FULL = 27, IM_ERR_EMPTY = 28;
+
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Four 15-bit integers -> their signed high bytes and unsigned low bytes.
+__device__ __forceinline__ void split4(int v0, int v1, int v2, int v3, uint32_t& hi, uint32_t& lo) {
+  hi = ((uint32_t)(v0 >> 8) & 0xffu) | (((uint32_t)(v1 >> 8) & 0xffu) << 8) | (((uint32_t)(v2 >> 8) & 0xffu) << 16) |
+       (((uint32_t)(v3 >> 8) & 0xffu) << 24);
+  lo = ((uint32_t)v0 & 0xffu) | (((uint32_t)v1 & 0xffu) << 8) | (((uint32_t)v2 & 0xffu) << 16) |
+       (((uint32_t)v3 & 0xffu) << 24);
+}
+
+// One warp per (token slot t, superblock kb); lane = (sub-block j = lane/4, c = lane%4).
+// Token slots t >= m (the rest of the last 8-token tile) get zero fragments.
+//   bq[((tile * sb + kb) * 8 + j) * 32 + 4 * (t % 8) + c] = {hi(k 4c..4c+3), hi(k 16+4c..), lo(..), lo(..)}
+//   ssum[(kb * 32 + t) * 8 + j] = sum of the 32 quantized values of sub-block j
+//   scl[kb * 32 + t] = 2^e (NaN when the superblock holds a non-finite value)
+__global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict__ x, int m, int slots, int64_t k,
+                                                        int sb, uint4* __restrict__ bq, int* __restrict__ ssum,
+                                                        float* __restrict__ scl) {
+  pdl_trigger();
+  pdl_wait();  // x may be the previous kernel's output
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (wid >= (int64_t)slots * sb) return;
+  const int t = (int)(wid / sb), kb = (int)(wid - (int64_t)t * sb);
+  const int j = lane >> 2, c = lane & 3;
+  uint4* dst = bq + ((int64_t)((t >> 3) * sb + kb) * 8 + j) * 32 + 4 * (t & 7) + c;
+  if (t >= m) {
+    *dst = make_uint4(0u, 0u, 0u, 0u);
+    return;
+  }
+  const float* xs = x + (int64_t)t * k + (int64_t)kb * 256 + 32 * j;
+  const float4 a = ldg_f4(xs + 4 * c), b = ldg_f4(xs + 16 + 4 * c);
+  float amax = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
+  amax = fmaxf(amax, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  float inv = 0.f, factor = __int_as_float(0x7fc00000);
+  if (amax <= 3.4e38f) {  // finite (NaN compares false)
+    int e = 0;
+    if (amax > 0.f) e = (int)((__float_as_uint(amax) >> 23) & 0xff) - 127 - 13;
+    e = max(-126, min(126, e));
+    inv = __uint_as_float((uint32_t)(127 - e) << 23);
+    factor = __uint_as_float((uint32_t)(127 + e) << 23);
+  }
+  const int v0 = __float2int_rn(a.x * inv), v1 = __float2int_rn(a.y * inv), v2 = __float2int_rn(a.z * inv),
+            v3 = __float2int_rn(a.w * inv);
+  const int v4 = __float2int_rn(b.x * inv), v5 = __float2int_rn(b.y * inv), v6 = __float2int_rn(b.z * inv),
+            v7 = __float2int_rn(b.w * inv);
+  uint4 o;
+  split4(v0, v1, v2, v3, o.x, o.z);
+  split4(v4, v5, v6, v7, o.y, o.w);
+  *dst = o;
+  int s = v0 + v1 + v2 + v3 + v4 + v5 + v6 + v7;
+  s += __shfl_xor_sync(0xffffffffu, s, 1);
+  s += __shfl_xor_sync(0xffffffffu, s, 2);
+  if (c == 0) ssum[((int64_t)kb * 32 + t) * 8 + j] = s;
+  if (lane == 0) scl[(int64_t)kb * 32 + t] = factor;
+}
+
+template <int NT>
+struct ImStage {
+  static constexpr int W = IM_ROWS * Q4K_BYTES;  // 18432
+  static constexpr int B = NT * 4096;            // activation fragments of 8 tokens per tile
+  static constexpr int S = 32 * 8 * 4;           // activation sums of the 32 token slots
+  static constexpr int BYTES = W + B + S;        // a multiple of 128
+};
+
+struct ImParams {
+  const uint4* bq;
+  const int* ssum;
+  const float* scl;
+  const float* bias;
+  float* y;     // [m][n]
+  float* part;  // [splits][m][n] (splits > 1)
+  unsigned* ctr;
+  int64_t n;
+  int sb, m, splits, kb_per, S;
+  int* err;
+};
+
+__device__ __forceinline__ void mbar_expect_only(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_u8u8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <int NT>
+__global__ void __launch_bounds__(32 * (IM_WARPS + 1), 1)
+    imma_q4_kernel(const __grid_constant__ CUtensorMap wmap, const ImParams P) {
+  using St = ImStage<NT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  pdl_trigger();
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)P.S * St::BYTES);
+  uint64_t* empty = full + P.S;
+  __shared__ int last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row0 = (int64_t)blockIdx.x * IM_ROWS;
+  const int sp = blockIdx.y;
+  const int kb0 = sp * P.kb_per;
+  const int T = max(0, min(P.sb, kb0 + P.kb_per) - kb0);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < P.S; ++i) {
+      sm100::mbar_init(&full[i], 1);
+      sm100::mbar_init(&empty[i], IM_WARPS);
+    }
+    sm100::mbar_fence_init();
+  }
+  __syncthreads();
+
+  if (warp == IM_WARPS) {
+    // ---- producer: the weights first (they do not depend on the previous kernel)
+    if (lane == 0) {
+      sm100::tma_prefetch(&wmap);
+      auto weights = [&](int t) {
+        const int st = t % P.S;
+        mbar_expect_only(&full[st], St::W);
+        sm100::tma_load_2d(smem + (size_t)st * St::BYTES, &wmap, (kb0 + t) * Q4K_BYTES, (int)row0, &full[st]);
+      };
+      const int pre = min(T, P.S);
+      for (int t = 0; t < pre; ++t) weights(t);
+      pdl_wait();  // activation fragments and sums come from the prep kernel
+      int t = 0;
+      for (; t < T; ++t) {
+        const int st = t % P.S, kb = kb0 + t;
+        if (t >= pre) {
+          if (!sm100::mbar_wait(&empty[st], ((t / P.S) - 1) & 1, P.err, IM_ERR_EMPTY)) break;
+          weights(t);
+        }
+        uint8_t* dst = smem + (size_t)st * St::BYTES + St::W;
+        sm100::mbar_expect_tx(&full[st], St::B + St::S);  // the stage's arrival
+#pragma unroll
+        for (int i = 0; i < NT; ++i)
+          sm100::bulk_load(dst + i * 4096, P.bq + ((size_t)i * P.sb + kb) * 8 * 32, 4096, &full[st]);
+        sm100::bulk_load(dst + St::B, P.ssum + (size_t)kb * 32 * 8, St::S, &full[st]);
+      }
+      // no copy may still be in flight into the ring when the CTA retires
+      for (int v = max(0, t - P.S); v < t; ++v) sm100::mbar_wait(&full[v % P.S], (v / P.S) & 1, P.err, IM_ERR_FULL);
+    }
+    return;
+  }
+
+  // ---- MMA warps: warp w owns tile rows 16w + g (C rows 0-7) and 16w + g + 8
+  pdl_wait();  // the per-(superblock, token) scales come from the prep kernel
+  const int g = lane >> 2, c = lane & 3;
+  const int ra = 16 * warp + g, rb = ra + 8;
+  float tot[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) tot[i][0] = tot[i][1] = tot[i][2] = tot[i][3] = 0.f;
+
+  for (int t = 0; t < T; ++t) {
+    const int st = t % P.S, kb = kb0 + t;
+    if (!sm100::mbar_wait_warp(&full[st], (t / P.S) & 1, P.err, IM_ERR_FULL)) break;
+    const uint8_t* stage = smem + (size_t)st * St::BYTES;
+    const uint8_t* pa = stage + ra * Q4K_BYTES;
+    const uint8_t* pb = stage + rb * Q4K_BYTES;
+    const uint4 ha = *reinterpret_cast<const uint4*>(pa), hb = *reinterpret_cast<const uint4*>(pb);
+    // the eight 6-bit scales / mins of each row as bytes: [0..3] and [4..7]
+    const uint32_t sca_lo = ha.y & 0x3F3F3F3Fu, ma_lo = ha.z & 0x3F3F3F3Fu;
+    const uint32_t sca_hi = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
+    const uint32_t ma_hi = ((ha.w >> 4) & 0x0F0F0F0Fu) | ((ha.z >> 2) & 0x30303030u);
+    const uint32_t scb_lo = hb.y & 0x3F3F3F3Fu, mb_lo = hb.z & 0x3F3F3F3Fu;
+    const uint32_t scb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
+    const uint32_t mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
+    const uint4* bs = reinterpret_cast<const uint4*>(stage + St::W);
+    const int* ss = reinterpret_cast<const int*>(stage + St::W + St::B);
+    float fa[NT][4];
+    int ma[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; ++i)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        fa[i][e] = 0.f;
+        ma[i][e] = 0;
+      }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      // qs of pair p: bytes 16 + 32p ..; this lane's k = 4c..4c+3 and 16+4c..
+      const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(pa + 16 + 32 * p + 4 * c);
+      const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(pa + 32 + 32 * p + 4 * c);
+      const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(pb + 16 + 32 * p + 4 * c);
+      const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(pb + 32 + 32 * p + 4 * c);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = 2 * p + h;
+        const uint32_t a0 = (h ? wa0 >> 4 : wa0) & 0x0F0F0F0Fu, a1 = (h ? wb0 >> 4 : wb0) & 0x0F0F0F0Fu;
+        const uint32_t a2 = (h ? wa1 >> 4 : wa1) & 0x0F0F0F0Fu, a3 = (h ? wb1 >> 4 : wb1) & 0x0F0F0F0Fu;
+        const int sh = 8 * (j & 3);
+        const float sca = (float)(((j < 4 ? sca_lo : sca_hi) >> sh) & 0xffu);
+        const float scb = (float)(((j < 4 ? scb_lo : scb_hi) >> sh) & 0xffu);
+        const int mina = (int)(((j < 4 ? ma_lo : ma_hi) >> sh) & 0xffu);
+        const int minb = (int)(((j < 4 ? mb_lo : mb_hi) >> sh) & 0xffu);
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+          const uint4 bv = bs[(i * 8 + j) * 32 + lane];
+          int ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
+          mma_u8s8(ch, a0, a1, a2, a3, bv.x, bv.y);
+          mma_u8u8(cl, a0, a1, a2, a3, bv.z, bv.w);
+          // C: [0], [1] row g, tokens 8i + 2c, +1; [2], [3] row g + 8
+          fa[i][0] = fmaf((float)(ch[0] * 256 + cl[0]), sca, fa[i][0]);
+          fa[i][1] = fmaf((float)(ch[1] * 256 + cl[1]), sca, fa[i][1]);
+          fa[i][2] = fmaf((float)(ch[2] * 256 + cl[2]), scb, fa[i][2]);
+          fa[i][3] = fmaf((float)(ch[3] * 256 + cl[3]), scb, fa[i][3]);
+          const int s0 = ss[(8 * i + 2 * c) * 8 + j], s1 = ss[(8 * i + 2 * c + 1) * 8 + j];
+          ma[i][0] += mina * s0;
+          ma[i][1] += mina * s1;
+          ma[i][2] += minb * s0;
+          ma[i][3] += minb * s1;
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) sm100::mbar_arrive(&empty[st]);  // the stage may be refilled
+    const float da = f16_bits_to_f32((uint16_t)(ha.x & 0xffff)), dma = f16_bits_to_f32((uint16_t)(ha.x >> 16));
+    const float db = f16_bits_to_f32((uint16_t)(hb.x & 0xffff)), dmb = f16_bits_to_f32((uint16_t)(hb.x >> 16));
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int tk = 8 * i + 2 * c + e;
+        const float f = tk < P.m ? __ldg(P.scl + (size_t)kb * 32 + tk) : 0.f;
+        tot[i][e] = fmaf(f, fmaf(da, fa[i][e], -dma * (float)ma[i][e]), tot[i][e]);
+        tot[i][2 + e] = fmaf(f, fmaf(db, fa[i][2 + e], -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
+      }
+    }
+  }
+
+  // ---- this CTA's result for its 128 rows and K range
+  const int64_t rowa = row0 + ra, rowb = row0 + rb;
+  float* dst = P.splits == 1 ? P.y : P.part + (size_t)sp * P.m * P.n;
+  const bool add_bias = P.splits == 1 && P.bias;
+#pragma unroll
+  for (int i = 0; i < NT; ++i)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int tk = 8 * i + 2 * c + e;
+      if (tk < P.m) {
+        if (rowa < P.n) dst[(int64_t)tk * P.n + rowa] = tot[i][e] + (add_bias ? P.bias[rowa] : 0.f);
+        if (rowb < P.n) dst[(int64_t)tk * P.n + rowb] = tot[i][2 + e] + (add_bias ? P.bias[rowb] : 0.f);
+      }
+    }
+  if (P.splits == 1) return;
+  // split-K: the last CTA of this row tile adds the splits in order
+  __threadfence();
+  asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
+  if (threadIdx.x == 0) last = atomicAdd(P.ctr + blockIdx.x, 1u) == (unsigned)P.splits - 1;
+  asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
+  if (!last) return;
+  __threadfence();
+  const int rows = (int)(P.n - row0 < IM_ROWS ? P.n - row0 : IM_ROWS);
+  for (int e = threadIdx.x; e < P.m * rows; e += 32 * IM_WARPS) {
+    const int tk = e / rows, r = e - tk * rows;
+    const int64_t idx = (int64_t)tk * P.n + row0 + r;
+    float v = P.bias ? P.bias[row0 + r] : 0.f;
+    for (int q = 0; q < P.splits; ++q) v += __ldcg(P.part + (size_t)q * P.m * P.n + idx);
+    P.y[idx] = v;
+  }
+  if (threadIdx.x == 0) P.ctr[blockIdx.x] = 0u;  // ready for the next call (stream-ordered)
+}
+
+// Ring stages and K-splits: about one CTA per SM, at least 2 superblocks per CTA.
+struct ImShape {
+  int S, splits, kb_per;
+  size_t smem;
+};
+ImShape im_shape(int nt, int64_t n, int sb, int num_sms) {
+  ImShape r;
+  const int64_t tiles = (n + IM_ROWS - 1) / IM_ROWS;
+  const int splits = (int)std::max<int64_t>(1, std::min<int64_t>((num_sms + tiles / 2) / tiles, sb / 2));
+  r.kb_per = (sb + splits - 1) / splits;
+  r.splits = (sb + r.kb_per - 1) / r.kb_per;
+  const int stage = IM_ROWS * Q4K_BYTES + nt * 4096 + 32 * 8 * 4;
+  const int fit = (IM_MAX_SMEM - 2 * 8 * 8) / (stage + 16);
+  r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
+  r.smem = (size_t)r.S * stage + (size_t)2 * r.S * 8;
+  return r;
+}
+
+struct ImWs {
+  size_t bq, ssum, scl, part, end;
+};
+ImWs im_ws(int64_t m, int64_t n, int64_t k, int num_sms) {
+  const int64_t mc = m < 32 ? m : 32;
+  const int nt = (int)((mc + 7) / 8);
+  const int64_t sb = k / QK;
+  ImWs L;
+  L.bq = 0;
+  L.ssum = (size_t)nt * sb * 4096;
+  L.scl = L.ssum + (size_t)sb * 32 * 8 * 4;
+  L.part = (L.scl + (size_t)sb * 32 * 4 + 255) & ~size_t(255);
+  const ImShape sh = im_shape(nt, n, (int)sb, num_sms);
+  L.end = L.part + (sh.splits > 1 ? (size_t)sh.splits * mc * n * 4 : 0) + 256;
+  return L;
+}
+
+template <int NT>
+cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const float* bias, float* y, unsigned* ctr,
+                      int num_sms, int* err, cudaStream_t s) {
+  const ImShape sh = im_shape(NT, w.n, (int)w.sb, num_sms);
+  char* base = static_cast<char*>(ws);
+  ImParams P;
+  P.bq = reinterpret_cast<const uint4*>(base + L.bq);
+  P.ssum = reinterpret_cast<const int*>(base + L.ssum);
+  P.scl = reinterpret_cast<const float*>(base + L.scl);
+  P.bias = bias;
+  P.y = y;
+  P.part = reinterpret_cast<float*>(base + L.part);
+  P.ctr = ctr;
+  P.n = w.n;
+  P.sb = (int)w.sb;
+  P.m = m;
+  P.splits = sh.splits;
+  P.kb_per = sh.kb_per;
+  P.S = sh.S;
+  P.err = err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((w.n + IM_ROWS - 1) / IM_ROWS), (unsigned)sh.splits);
+  cfg.blockDim = dim3(32 * (IM_WARPS + 1));
+  cfg.dynamicSmemBytes = sh.smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, imma_q4_kernel<NT>, w.wmap, P);
+}
+
+}  // namespace
+
+cudaError_t imma_init_device() {
+  cudaError_t e = cudaSuccess, r;
+  if ((r = cudaFuncSetAttribute(imma_q4_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
+    e = r;
+  if ((r = cudaFuncSetAttribute(imma_q4_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
+    e = r;
+  if ((r = cudaFuncSetAttribute(imma_q4_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
+    e = r;
+  if ((r = cudaFuncSetAttribute(imma_q4_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
+    e = r;
+  return e;
+}
+
+size_t imma_workspace_bytes(int64_t m, int64_t n, int64_t k, int num_sms) { return im_ws(m, n, k, num_sms).end; }
+size_t imma_counter_bytes(int64_t n) { return (size_t)((n + IM_ROWS - 1) / IM_ROWS) * 4 + 256; }
+
+cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, const float* bias, float* y, void* ws,
+                             unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br) {
+  if (w.type != GGUF_Q4_K) return cudaErrorNotSupported;
+  const ImWs L = im_ws(m64, w.n, w.k, num_sms);
+  const int sb = (int)w.sb;
+  for (int64_t m0 = 0; m0 < m64; m0 += 32) {
+    const int m = (int)((m64 - m0) < 32 ? (m64 - m0) : 32);
+    const int nt = (m + 7) / 8;
+    char* base = static_cast<char*>(ws);
+    const int64_t warps = (int64_t)nt * 8 * sb;
+    cudaError_t e = launch_pdl(imma_prep_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, x + m0 * w.k, m,
+                               nt * 8, w.k, sb, reinterpret_cast<uint4*>(base + L.bq),
+                               reinterpret_cast<int*>(base + L.ssum), reinterpret_cast<float*>(base + L.scl));
+    if (e != cudaSuccess) return e;
+    if (launches) ++*launches;
+    bracket_record(br.start, s);
+    float* yc = y + m0 * w.n;
+    switch (nt) {
+      case 1: e = launch_im<1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+      case 2: e = launch_im<2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+      case 3: e = launch_im<3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+      default: e = launch_im<4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+    }
+    bracket_record(br.stop, s);
+    br = Bracket();  // only the first chunk is bracketed
+    if (e != cudaSuccess) return e;
+    if (launches) ++*launches;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace kq

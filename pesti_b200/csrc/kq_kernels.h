@@ -100,6 +100,17 @@ cudaError_t launch_dequant_f32(const DevWeight& w, int64_t row0, int64_t nrows, 
 cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t n, int64_t sb, uint8_t* body, uint16_t* d,
                                 cudaStream_t s);
 
+// ---- integer tensor-core batched decode, GGUF Q4_K: kq_imma.cu ----
+cudaError_t imma_init_device();
+// Scratch (bytes) for m tokens of an n x k weight, and the zeroed counters.
+size_t imma_workspace_bytes(int64_t m, int64_t n, int64_t k, int num_sms);
+size_t imma_counter_bytes(int64_t n);
+// y = x . W^T (+bias) for GGUF Q4_K (cudaErrorNotSupported otherwise); any m,
+// in chunks of 32 tokens; *err receives 27 / 28 if a pipeline wait gave up.
+cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y, void* ws,
+                             unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches,
+                             Bracket br = Bracket());
+
 // ---- CUDA-core integer decode path: kq_dp4a.cu ----
 constexpr int DP4A_MAX_M = 4;
 // Per-device set-up of the dp4a kernels (shared-memory carve-outs).

@@ -50,6 +50,7 @@ KQ_PATH_AUTO = 0
 KQ_PATH_TCGEN05 = 1
 KQ_PATH_MMA = 2
 KQ_PATH_DP4A = 3
+KQ_PATH_IMMA = 4
 
 #: every symbol include/pesti_kq.h declares
 EXPORTED_SYMBOLS = (

@@ -80,10 +80,13 @@ CASES = [
     ("Q4_K", 100, 2048, 12),   # m > 8: hi-only fragments, 2 n-tiles
     ("Q6_K", 48, 1536, 20),    # 3 n-tiles
     ("Q4_K", 40, 768, 40),     # m > 32: two chunks
+    ("Q4_K", 4096, 4096, 8),   # batched decode shapes (integer MMA: split-K over 32 row tiles)
+    ("Q4_K", 4096, 4096, 32),
+    ("Q4_K", 300, 14336, 5),   # rows not a multiple of the 128-row tile, 56 superblocks
 ]
 
 
-PATHS = {"tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA, "dp4a": kq.KQ_PATH_DP4A}
+PATHS = {"tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA, "dp4a": kq.KQ_PATH_DP4A, "imma": kq.KQ_PATH_IMMA}
 DP4A_MAX_M = 4  # the integer dot-product family serves 1..4 tokens
 
 
