@@ -93,6 +93,12 @@ def parse():
     return p.parse_args()
 
 
+def kernel_path(name):
+    from pesti_b200 import kq
+    return {"auto": kq.KQ_PATH_AUTO, "tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA,
+            "dp4a": kq.KQ_PATH_DP4A, "imma": kq.KQ_PATH_IMMA}[name]
+
+
 def algorithmic_bytes(qtype, n, k, m):
     wbytes = n * (k // 256) * (144 if qtype == 12 else 210)
     return wbytes, wbytes + m * k * 4 + m * n * 4
@@ -308,8 +314,7 @@ def run_ours(args, rank, world, local_rank):
                for i in range(NUM_WEIGHTS)]
     x = torch.from_numpy(synthetic.activations(m, k, seed=7 + rank)).to(dev)
     ys = [torch.empty((m, n), dtype=torch.float32, device=dev) for _ in range(NUM_WEIGHTS)]
-    ctx.set_path({"auto": kq.KQ_PATH_AUTO, "tcgen05": kq.KQ_PATH_TCGEN05, "mma": kq.KQ_PATH_MMA,
-                  "dp4a": kq.KQ_PATH_DP4A, "imma": kq.KQ_PATH_IMMA}[args.path])
+    ctx.set_path(kernel_path(args.path))
     ctx.reserve(weights[0], m)
 
     stream = torch.cuda.Stream(dev)
@@ -639,6 +644,7 @@ def run_decoder(args, rank, world, local_rank):
     cfg = getattr(dec, cfg_name)
     B = args.m
     ctx = kq.Context(local_rank)
+    ctx.set_path(kernel_path(args.path))
     tp = None
     if world > 1:
         tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, B))

@@ -57,13 +57,13 @@ enum kq_type {
 
 /* kernel families for GGUF weights with f32 activations (kq_ctx_set_path) */
 #define KQ_PATH_AUTO 0    /* default: DP4A m = 1; Q4_K IMMA m <= 64; Q6_K    */
-                          /* DP4A m <= 4, MMA m <= 64; else TCGEN05          */
+                          /* DP4A m = 2, IMMA m <= 8, MMA m <= 64; TCGEN05   */
 #define KQ_PATH_TCGEN05 1 /* tcgen05.mma, dequantized A written to TMEM      */
 #define KQ_PATH_MMA 2     /* warp-level mma.sync tiles (cp.async staging)     */
 #define KQ_PATH_DP4A 3    /* CUDA-core integer dot products, m <= 4 only;    */
                           /* larger m falls back to the AUTO choice          */
-#define KQ_PATH_IMMA 4    /* Q4_K: integer mma.sync on the raw codes (TMA-fed */
-                          /* 128-row tiles); Q6_K takes MMA                  */
+#define KQ_PATH_IMMA 4    /* integer mma.sync on the raw 4/6-bit codes        */
+                          /* (TMA-fed 128-row tiles, split-K)                */
 
 typedef struct kq_ctx kq_ctx;
 typedef struct kq_weight kq_weight;

@@ -186,15 +186,17 @@ int finish_sync(kq_ctx* ctx, const char* what) {
   return check_device_error(ctx);
 }
 
-// Kernel family for a GGUF f32 call of m tokens.  AUTO: integer dot products
-// up to DP4A_MAX_M tokens, warp-level mma.sync tiles up to 64, tcgen05 above
-// (the choice follows the measured decode throughput of each family).
+// Kernel family for a GGUF f32 call of m tokens.  AUTO follows the measured
+// decode throughput of each family: integer dot products for one token (and
+// two Q6_K tokens), integer tensor-core tiles for Q4_K up to 64 tokens and
+// Q6_K up to 8, mma.sync bf16 tiles for Q6_K up to 64, tcgen05 above.
 int f32_family(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
   const bool q4 = w.type == kq::GGUF_Q4_K;
-  if (ctx->path == KQ_PATH_IMMA) return q4 ? KQ_PATH_IMMA : KQ_PATH_MMA;
-  if (ctx->path == KQ_PATH_MMA || ctx->path == KQ_PATH_TCGEN05) return ctx->path;
-  if (m == 1 || (m <= kq::DP4A_MAX_M && (!q4 || ctx->path == KQ_PATH_DP4A))) return KQ_PATH_DP4A;
-  if (q4 && m <= 64) return KQ_PATH_IMMA;
+  if (ctx->path == KQ_PATH_IMMA || ctx->path == KQ_PATH_MMA || ctx->path == KQ_PATH_TCGEN05) return ctx->path;
+  if (m == 1 || (ctx->path == KQ_PATH_DP4A && m <= kq::DP4A_MAX_M)) return KQ_PATH_DP4A;
+  if (q4) return m <= 64 ? KQ_PATH_IMMA : KQ_PATH_TCGEN05;
+  if (m == 2) return KQ_PATH_DP4A;
+  if (m <= 8) return KQ_PATH_IMMA;
   return m <= 64 ? KQ_PATH_MMA : KQ_PATH_TCGEN05;
 }
 

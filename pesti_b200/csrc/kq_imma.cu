@@ -1,5 +1,5 @@
-// kq_imma.cu -- batched decode linear (2..32 tokens) for GGUF Q4_K on the
-// integer tensor-core path: y[m][n] = x[m][k] . W[n][k] (+ bias).
+// kq_imma.cu -- batched decode linear (2..32 tokens per chunk) for GGUF Q4_K
+// and Q6_K on the integer tensor-core path: y[m][n] = x[m][k] . W[n][k] (+ bias).
 //
 // A Q4_K sub-block is 32 weights with one 6-bit scale and one 6-bit min, so it
 // is exactly one k32 step of mma.sync.m16n8k32 with 8-bit operands:
@@ -13,6 +13,13 @@
 //  * per sub-block the int32 result is scaled by sc (f32 accumulate) and the
 //    min term dmin m_j sum(x) uses exact int32 sums of the quantized
 //    activations; d, dmin and 2^e are applied once per superblock.
+// Q6_K's scale groups are 16 weights (elements 16s .. 16s+15 of a
+// superblock), so a group is one k16 step of mma.sync.m16n8k16 with 8-bit
+// operands: in the device body layout a lane's four codes of a group are one
+// 32-bit ql word and one 32-bit qh word per row (nibble | 2 high bits << 4 by
+// four bit operations), the -32 offset is applied with exact int32 group sums
+// of the quantized activations, the int8 group scale per group, d per
+// superblock.
 // Only the 15-bit activation rounding approximates, as in the single-token
 // kernel.
 //
@@ -39,6 +46,9 @@ namespace {
 constexpr int IM_WARPS = 8;
 constexpr int IM_ROWS = 16 * IM_WARPS;    // the weight maps' box height
 constexpr int IM_MAX_SMEM = 226 * 1024;   // dynamic; room for the static bytes
+constexpr int IM_HALF_SMEM = 112 * 1024;  // two CTAs per SM
+// CTAs per SM: one or two token tiles leave registers and shared memory for two
+constexpr int im_ctas_per_sm(int nt) { return nt <= 2 ? 2 : 1; }
 constexpr int IM_ERR_FULL = 27, IM_ERR_EMPTY = 28;
 
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -57,6 +67,10 @@ __device__ __forceinline__ void split4(int v0, int v1, int v2, int v3, uint32_t&
 //   bq[((tile * sb + kb) * 8 + j) * 32 + 4 * (t % 8) + c] = {hi(k 4c..4c+3), hi(k 16+4c..), lo(..), lo(..)}
 //   ssum[(kb * 32 + t) * 8 + j] = sum of the 32 quantized values of sub-block j
 //   scl[kb * 32 + t] = 2^e (NaN when the superblock holds a non-finite value)
+// Q6_K: lane = (group s0 = lane/4, c = lane%4) handles groups s0 and s0 + 8:
+//   bq[((tile * sb + kb) * 16 + s) * 32 + 4 * (t % 8) + c] = uint2 {hi(k 4c..4c+3), lo(..)} of group s
+//   ssum[(kb * 32 + t) * 16 + s] = 32 x the sum of the 16 quantized values of group s
+template <int QT>
 __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict__ x, int m, int slots, int64_t k,
                                                         int sb, uint4* __restrict__ bq, int* __restrict__ ssum,
                                                         float* __restrict__ scl) {
@@ -67,13 +81,25 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
   if (wid >= (int64_t)slots * sb) return;
   const int t = (int)(wid / sb), kb = (int)(wid - (int64_t)t * sb);
   const int j = lane >> 2, c = lane & 3;
-  uint4* dst = bq + ((int64_t)((t >> 3) * sb + kb) * 8 + j) * 32 + 4 * (t & 7) + c;
+  constexpr bool Q4 = QT == GGUF_Q4_K;
+  // Q4_K: sub-block j, elements 32j + 4c.. and 32j + 16 + 4c..; Q6_K: groups j and j + 8,
+  // elements 16j + 4c.. and 16(j + 8) + 4c..
+  const int64_t ea = Q4 ? 32 * j + 4 * c : 16 * j + 4 * c;
+  const int64_t eb = Q4 ? ea + 16 : ea + 128;
+  uint4* dst4 = bq + ((int64_t)((t >> 3) * sb + kb) * 8 + j) * 32 + 4 * (t & 7) + c;
+  uint2* dst2a = reinterpret_cast<uint2*>(bq) + ((int64_t)((t >> 3) * sb + kb) * 16 + j) * 32 + 4 * (t & 7) + c;
+  uint2* dst2b = dst2a + 8 * 32;
   if (t >= m) {
-    *dst = make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (Q4) {
+      *dst4 = make_uint4(0u, 0u, 0u, 0u);
+    } else {
+      *dst2a = make_uint2(0u, 0u);
+      *dst2b = make_uint2(0u, 0u);
+    }
     return;
   }
-  const float* xs = x + (int64_t)t * k + (int64_t)kb * 256 + 32 * j;
-  const float4 a = ldg_f4(xs + 4 * c), b = ldg_f4(xs + 16 + 4 * c);
+  const float* xs = x + (int64_t)t * k + (int64_t)kb * 256;
+  const float4 a = ldg_f4(xs + ea), b = ldg_f4(xs + eb);
   float amax = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
   amax = fmaxf(amax, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
 #pragma unroll
@@ -93,20 +119,36 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
   uint4 o;
   split4(v0, v1, v2, v3, o.x, o.z);
   split4(v4, v5, v6, v7, o.y, o.w);
-  *dst = o;
-  int s = v0 + v1 + v2 + v3 + v4 + v5 + v6 + v7;
-  s += __shfl_xor_sync(0xffffffffu, s, 1);
-  s += __shfl_xor_sync(0xffffffffu, s, 2);
-  if (c == 0) ssum[((int64_t)kb * 32 + t) * 8 + j] = s;
+  if constexpr (Q4) {
+    *dst4 = o;
+    int s = v0 + v1 + v2 + v3 + v4 + v5 + v6 + v7;
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if (c == 0) ssum[((int64_t)kb * 32 + t) * 8 + j] = s;
+  } else {
+    *dst2a = make_uint2(o.x, o.z);
+    *dst2b = make_uint2(o.y, o.w);
+    int sa = v0 + v1 + v2 + v3, sbv = v4 + v5 + v6 + v7;
+    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
+    sa += __shfl_xor_sync(0xffffffffu, sa, 2);
+    sbv += __shfl_xor_sync(0xffffffffu, sbv, 1);
+    sbv += __shfl_xor_sync(0xffffffffu, sbv, 2);
+    if (c == 0) {  // times the code offset 32
+      ssum[((int64_t)kb * 32 + t) * 16 + j] = 32 * sa;
+      ssum[((int64_t)kb * 32 + t) * 16 + j + 8] = 32 * sbv;
+    }
+  }
   if (lane == 0) scl[(int64_t)kb * 32 + t] = factor;
 }
 
-template <int NT>
+template <int QT, int NT>
 struct ImStage {
-  static constexpr int W = IM_ROWS * Q4K_BYTES;  // 18432
-  static constexpr int B = NT * 4096;            // activation fragments of 8 tokens per tile
-  static constexpr int S = 32 * 8 * 4;           // activation sums of the 32 token slots
-  static constexpr int BYTES = W + B + S;        // a multiple of 128
+  static constexpr bool Q4 = QT == GGUF_Q4_K;
+  static constexpr int W = IM_ROWS * (Q4 ? Q4K_BYTES : Q6K_BODY);  // 18432 / 26624
+  static constexpr int D = Q4 ? 0 : IM_ROWS * 16;                  // Q6_K: d of 8 superblocks per row
+  static constexpr int B = NT * 4096;                              // activation fragments, 8 tokens per tile
+  static constexpr int S = 32 * (Q4 ? 8 : 16) * 4;                 // activation sums of the 32 token slots
+  static constexpr int BYTES = W + D + B + S;                      // a multiple of 128
 };
 
 struct ImParams {
@@ -122,6 +164,15 @@ struct ImParams {
   int* err;
 };
 
+// Hand a ring stage back to the producer.  The warp's shared-memory reads of
+// the stage (generic proxy) are fenced against the TMA / bulk copies that
+// refill it (async proxy) before the release: without the fence a refill was
+// seen to overtake reads still queued behind the arrive.
+__device__ __forceinline__ void stage_release(uint64_t* empty, int lane) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  __syncwarp();
+  if (lane == 0) sm100::mbar_arrive(empty);
+}
 __device__ __forceinline__ void mbar_expect_only(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(sm100::smem_u32(bar)), "r"(bytes)
                : "memory");
@@ -140,11 +191,24 @@ __device__ __forceinline__ void mma_u8u8(int (&c)[4], uint32_t a0, uint32_t a1, 
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// k16 forms (Q6_K groups): A = a0 (row g, k 4c..4c+3), a1 (row g + 8); B = b0 (k 4c..4c+3, column g)
+__device__ __forceinline__ void mma16_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+               : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+               : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ void mma16_u8u8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+               : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+               : "r"(a0), "r"(a1), "r"(b0));
+}
 
-template <int NT>
-__global__ void __launch_bounds__(32 * (IM_WARPS + 1), 1)
-    imma_q4_kernel(const __grid_constant__ CUtensorMap wmap, const ImParams P) {
-  using St = ImStage<NT>;
+template <int QT, int NT>
+__global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
+    imma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap dmap, const ImParams P) {
+  using St = ImStage<QT, NT>;
+  constexpr bool Q4 = QT == GGUF_Q4_K;
+  constexpr int BPS = Q4 ? Q4K_BYTES : Q6K_BODY;
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_trigger();
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)P.S * St::BYTES);
@@ -168,10 +232,13 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), 1)
     // ---- producer: the weights first (they do not depend on the previous kernel)
     if (lane == 0) {
       sm100::tma_prefetch(&wmap);
+      if constexpr (!Q4) sm100::tma_prefetch(&dmap);
       auto weights = [&](int t) {
-        const int st = t % P.S;
-        mbar_expect_only(&full[st], St::W);
-        sm100::tma_load_2d(smem + (size_t)st * St::BYTES, &wmap, (kb0 + t) * Q4K_BYTES, (int)row0, &full[st]);
+        const int st = t % P.S, kb = kb0 + t;
+        uint8_t* dst = smem + (size_t)st * St::BYTES;
+        mbar_expect_only(&full[st], St::W + St::D);
+        sm100::tma_load_2d(dst, &wmap, kb * BPS, (int)row0, &full[st]);
+        if constexpr (!Q4) sm100::tma_load_2d(dst + St::W, &dmap, kb & ~7, (int)row0, &full[st]);
       };
       const int pre = min(T, P.S);
       for (int t = 0; t < pre; ++t) weights(t);
@@ -183,12 +250,12 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), 1)
           if (!sm100::mbar_wait(&empty[st], ((t / P.S) - 1) & 1, P.err, IM_ERR_EMPTY)) break;
           weights(t);
         }
-        uint8_t* dst = smem + (size_t)st * St::BYTES + St::W;
+        uint8_t* dst = smem + (size_t)st * St::BYTES + St::W + St::D;
         sm100::mbar_expect_tx(&full[st], St::B + St::S);  // the stage's arrival
 #pragma unroll
         for (int i = 0; i < NT; ++i)
           sm100::bulk_load(dst + i * 4096, P.bq + ((size_t)i * P.sb + kb) * 8 * 32, 4096, &full[st]);
-        sm100::bulk_load(dst + St::B, P.ssum + (size_t)kb * 32 * 8, St::S, &full[st]);
+        sm100::bulk_load(dst + St::B, P.ssum + (size_t)kb * St::S / 4, St::S, &full[st]);
       }
       // no copy may still be in flight into the ring when the CTA retires
       for (int v = max(0, t - P.S); v < t; ++v) sm100::mbar_wait(&full[v % P.S], (v / P.S) & 1, P.err, IM_ERR_FULL);
@@ -208,75 +275,138 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), 1)
     const int st = t % P.S, kb = kb0 + t;
     if (!sm100::mbar_wait_warp(&full[st], (t / P.S) & 1, P.err, IM_ERR_FULL)) break;
     const uint8_t* stage = smem + (size_t)st * St::BYTES;
-    const uint8_t* pa = stage + ra * Q4K_BYTES;
-    const uint8_t* pb = stage + rb * Q4K_BYTES;
-    const uint4 ha = *reinterpret_cast<const uint4*>(pa), hb = *reinterpret_cast<const uint4*>(pb);
-    // the eight 6-bit scales / mins of each row as bytes: [0..3] and [4..7]
-    const uint32_t sca_lo = ha.y & 0x3F3F3F3Fu, ma_lo = ha.z & 0x3F3F3F3Fu;
-    const uint32_t sca_hi = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
-    const uint32_t ma_hi = ((ha.w >> 4) & 0x0F0F0F0Fu) | ((ha.z >> 2) & 0x30303030u);
-    const uint32_t scb_lo = hb.y & 0x3F3F3F3Fu, mb_lo = hb.z & 0x3F3F3F3Fu;
-    const uint32_t scb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
-    const uint32_t mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
-    const uint4* bs = reinterpret_cast<const uint4*>(stage + St::W);
-    const int* ss = reinterpret_cast<const int*>(stage + St::W + St::B);
-    float fa[NT][4];
-    int ma[NT][4];
+    if constexpr (Q4) {
+      const uint8_t* pa = stage + ra * Q4K_BYTES;
+      const uint8_t* pb = stage + rb * Q4K_BYTES;
+      const uint4 ha = *reinterpret_cast<const uint4*>(pa), hb = *reinterpret_cast<const uint4*>(pb);
+      // the eight 6-bit scales / mins of each row as bytes: [0..3] and [4..7]
+      const uint32_t sca_lo = ha.y & 0x3F3F3F3Fu, ma_lo = ha.z & 0x3F3F3F3Fu;
+      const uint32_t sca_hi = (ha.w & 0x0F0F0F0Fu) | ((ha.y >> 2) & 0x30303030u);
+      const uint32_t ma_hi = ((ha.w >> 4) & 0x0F0F0F0Fu) | ((ha.z >> 2) & 0x30303030u);
+      const uint32_t scb_lo = hb.y & 0x3F3F3F3Fu, mb_lo = hb.z & 0x3F3F3F3Fu;
+      const uint32_t scb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
+      const uint32_t mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
+      const uint4* bs = reinterpret_cast<const uint4*>(stage + St::W);
+      const int* ss = reinterpret_cast<const int*>(stage + St::W + St::B);
+      float fa[NT][4];
+      int ma[NT][4];
 #pragma unroll
-    for (int i = 0; i < NT; ++i)
+      for (int i = 0; i < NT; ++i)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        fa[i][e] = 0.f;
-        ma[i][e] = 0;
-      }
+        for (int e = 0; e < 4; ++e) {
+          fa[i][e] = 0.f;
+          ma[i][e] = 0;
+        }
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-      // qs of pair p: bytes 16 + 32p ..; this lane's k = 4c..4c+3 and 16+4c..
-      const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(pa + 16 + 32 * p + 4 * c);
-      const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(pa + 32 + 32 * p + 4 * c);
-      const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(pb + 16 + 32 * p + 4 * c);
-      const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(pb + 32 + 32 * p + 4 * c);
+      for (int p = 0; p < 4; ++p) {
+        // qs of pair p: bytes 16 + 32p ..; this lane's k = 4c..4c+3 and 16+4c..
+        const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(pa + 16 + 32 * p + 4 * c);
+        const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(pa + 32 + 32 * p + 4 * c);
+        const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(pb + 16 + 32 * p + 4 * c);
+        const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(pb + 32 + 32 * p + 4 * c);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int j = 2 * p + h;
-        const uint32_t a0 = (h ? wa0 >> 4 : wa0) & 0x0F0F0F0Fu, a1 = (h ? wb0 >> 4 : wb0) & 0x0F0F0F0Fu;
-        const uint32_t a2 = (h ? wa1 >> 4 : wa1) & 0x0F0F0F0Fu, a3 = (h ? wb1 >> 4 : wb1) & 0x0F0F0F0Fu;
-        const int sh = 8 * (j & 3);
-        const float sca = (float)(((j < 4 ? sca_lo : sca_hi) >> sh) & 0xffu);
-        const float scb = (float)(((j < 4 ? scb_lo : scb_hi) >> sh) & 0xffu);
-        const int mina = (int)(((j < 4 ? ma_lo : ma_hi) >> sh) & 0xffu);
-        const int minb = (int)(((j < 4 ? mb_lo : mb_hi) >> sh) & 0xffu);
+        for (int h = 0; h < 2; ++h) {
+          const int j = 2 * p + h;
+          const uint32_t a0 = (h ? wa0 >> 4 : wa0) & 0x0F0F0F0Fu, a1 = (h ? wb0 >> 4 : wb0) & 0x0F0F0F0Fu;
+          const uint32_t a2 = (h ? wa1 >> 4 : wa1) & 0x0F0F0F0Fu, a3 = (h ? wb1 >> 4 : wb1) & 0x0F0F0F0Fu;
+          const int sh = 8 * (j & 3);
+          const float sca = (float)(((j < 4 ? sca_lo : sca_hi) >> sh) & 0xffu);
+          const float scb = (float)(((j < 4 ? scb_lo : scb_hi) >> sh) & 0xffu);
+          const int mina = (int)(((j < 4 ? ma_lo : ma_hi) >> sh) & 0xffu);
+          const int minb = (int)(((j < 4 ? mb_lo : mb_hi) >> sh) & 0xffu);
 #pragma unroll
-        for (int i = 0; i < NT; ++i) {
-          const uint4 bv = bs[(i * 8 + j) * 32 + lane];
-          int ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
-          mma_u8s8(ch, a0, a1, a2, a3, bv.x, bv.y);
-          mma_u8u8(cl, a0, a1, a2, a3, bv.z, bv.w);
-          // C: [0], [1] row g, tokens 8i + 2c, +1; [2], [3] row g + 8
-          fa[i][0] = fmaf((float)(ch[0] * 256 + cl[0]), sca, fa[i][0]);
-          fa[i][1] = fmaf((float)(ch[1] * 256 + cl[1]), sca, fa[i][1]);
-          fa[i][2] = fmaf((float)(ch[2] * 256 + cl[2]), scb, fa[i][2]);
-          fa[i][3] = fmaf((float)(ch[3] * 256 + cl[3]), scb, fa[i][3]);
-          const int s0 = ss[(8 * i + 2 * c) * 8 + j], s1 = ss[(8 * i + 2 * c + 1) * 8 + j];
-          ma[i][0] += mina * s0;
-          ma[i][1] += mina * s1;
-          ma[i][2] += minb * s0;
-          ma[i][3] += minb * s1;
+          for (int i = 0; i < NT; ++i) {
+            const uint4 bv = bs[(i * 8 + j) * 32 + lane];
+            int ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
+            mma_u8s8(ch, a0, a1, a2, a3, bv.x, bv.y);
+            mma_u8u8(cl, a0, a1, a2, a3, bv.z, bv.w);
+            // C: [0], [1] row g, tokens 8i + 2c, +1; [2], [3] row g + 8
+            fa[i][0] = fmaf((float)(ch[0] * 256 + cl[0]), sca, fa[i][0]);
+            fa[i][1] = fmaf((float)(ch[1] * 256 + cl[1]), sca, fa[i][1]);
+            fa[i][2] = fmaf((float)(ch[2] * 256 + cl[2]), scb, fa[i][2]);
+            fa[i][3] = fmaf((float)(ch[3] * 256 + cl[3]), scb, fa[i][3]);
+            const int s0 = ss[(8 * i + 2 * c) * 8 + j], s1 = ss[(8 * i + 2 * c + 1) * 8 + j];
+            ma[i][0] += mina * s0;
+            ma[i][1] += mina * s1;
+            ma[i][2] += minb * s0;
+            ma[i][3] += minb * s1;
+          }
         }
       }
-    }
-    __syncwarp();
-    if (lane == 0) sm100::mbar_arrive(&empty[st]);  // the stage may be refilled
-    const float da = f16_bits_to_f32((uint16_t)(ha.x & 0xffff)), dma = f16_bits_to_f32((uint16_t)(ha.x >> 16));
-    const float db = f16_bits_to_f32((uint16_t)(hb.x & 0xffff)), dmb = f16_bits_to_f32((uint16_t)(hb.x >> 16));
+      stage_release(&empty[st], lane);
+      const float da = f16_bits_to_f32((uint16_t)(ha.x & 0xffff)), dma = f16_bits_to_f32((uint16_t)(ha.x >> 16));
+      const float db = f16_bits_to_f32((uint16_t)(hb.x & 0xffff)), dmb = f16_bits_to_f32((uint16_t)(hb.x >> 16));
 #pragma unroll
-    for (int i = 0; i < NT; ++i) {
+      for (int i = 0; i < NT; ++i) {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int tk = 8 * i + 2 * c + e;
-        const float f = tk < P.m ? __ldg(P.scl + (size_t)kb * 32 + tk) : 0.f;
-        tot[i][e] = fmaf(f, fmaf(da, fa[i][e], -dma * (float)ma[i][e]), tot[i][e]);
-        tot[i][2 + e] = fmaf(f, fmaf(db, fa[i][2 + e], -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
+        for (int e = 0; e < 2; ++e) {
+          const int tk = 8 * i + 2 * c + e;
+          const float f = tk < P.m ? __ldg(P.scl + (size_t)kb * 32 + tk) : 0.f;
+          tot[i][e] = fmaf(f, fmaf(da, fa[i][e], -dma * (float)ma[i][e]), tot[i][e]);
+          tot[i][2 + e] = fmaf(f, fmaf(db, fa[i][2 + e], -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
+        }
+      }
+    } else {
+      const uint8_t* pa = stage + ra * Q6K_BODY;
+      const uint8_t* pb = stage + rb * Q6K_BODY;
+      const uint16_t* dtile = reinterpret_cast<const uint16_t*>(stage + St::W);
+      const uint4 sca4 = *reinterpret_cast<const uint4*>(pa + 192), scb4 = *reinterpret_cast<const uint4*>(pb + 192);
+      const uint2* bs = reinterpret_cast<const uint2*>(stage + St::W + St::D);
+      const int* ss = reinterpret_cast<const int*>(stage + St::W + St::D + St::B);
+      float fa[NT][4];
+#pragma unroll
+      for (int i = 0; i < NT; ++i) fa[i][0] = fa[i][1] = fa[i][2] = fa[i][3] = 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int l16 = 0; l16 < 2; ++l16) {
+          // this lane's 4 columns of the groups: slot 2 l16 + c/2, bytes 4 (c % 2) ..
+          const int off = 48 * (2 * l16 + (c >> 1)) + 4 * (c & 1);
+          const uint32_t qha = *reinterpret_cast<const uint32_t*>(pa + off + 8 * (4 + h));
+          const uint32_t qhb = *reinterpret_cast<const uint32_t*>(pb + off + 8 * (4 + h));
+#pragma unroll
+          for (int gg = 0; gg < 2; ++gg) {
+            const uint32_t qla = *reinterpret_cast<const uint32_t*>(pa + off + 8 * (2 * h + gg));
+            const uint32_t qlb = *reinterpret_cast<const uint32_t*>(pb + off + 8 * (2 * h + gg));
+#pragma unroll
+            for (int nib = 0; nib < 2; ++nib) {
+              const int G = gg + 2 * nib, sg = 8 * h + 2 * G + l16;
+              // six-bit codes: nibble | two high bits << 4
+              const uint32_t a0 = ((nib ? qla >> 4 : qla) & 0x0F0F0F0Fu) | (((qha >> (2 * G)) & 0x03030303u) << 4);
+              const uint32_t a1 = ((nib ? qlb >> 4 : qlb) & 0x0F0F0F0Fu) | (((qhb >> (2 * G)) & 0x03030303u) << 4);
+              const uint32_t wsa = sg < 4 ? sca4.x : sg < 8 ? sca4.y : sg < 12 ? sca4.z : sca4.w;
+              const uint32_t wsb = sg < 4 ? scb4.x : sg < 8 ? scb4.y : sg < 12 ? scb4.z : scb4.w;
+              const float sca = (float)(int)(int8_t)(wsa >> (8 * (sg & 3)));
+              const float scb = (float)(int)(int8_t)(wsb >> (8 * (sg & 3)));
+#pragma unroll
+              for (int i = 0; i < NT; ++i) {
+                const uint2 bv = bs[(i * 16 + sg) * 32 + lane];
+                // sum (q - 32) x = sum q x - 32 sum x: the low-byte product starts
+                // from -32 sum x; |.| < 2^24, exact in int32 and as a float
+                const int s0 = ss[(8 * i + 2 * c) * 16 + sg], s1 = ss[(8 * i + 2 * c + 1) * 16 + sg];
+                int ch[4] = {0, 0, 0, 0}, cl[4] = {-s0, -s1, -s0, -s1};
+                mma16_u8s8(ch, a0, a1, bv.x);
+                mma16_u8u8(cl, a0, a1, bv.y);
+                fa[i][0] = fmaf((float)(ch[0] * 256 + cl[0]), sca, fa[i][0]);
+                fa[i][1] = fmaf((float)(ch[1] * 256 + cl[1]), sca, fa[i][1]);
+                fa[i][2] = fmaf((float)(ch[2] * 256 + cl[2]), scb, fa[i][2]);
+                fa[i][3] = fmaf((float)(ch[3] * 256 + cl[3]), scb, fa[i][3]);
+              }
+            }
+          }
+        }
+      // the superblock scales leave the stage before it is released
+      const float da = f16_bits_to_f32(dtile[ra * 8 + (kb & 7)]), db = f16_bits_to_f32(dtile[rb * 8 + (kb & 7)]);
+      stage_release(&empty[st], lane);
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tk = 8 * i + 2 * c + e;
+          const float f = tk < P.m ? __ldg(P.scl + (size_t)kb * 32 + tk) : 0.f;
+          tot[i][e] = fmaf(f * da, fa[i][e], tot[i][e]);
+          tot[i][2 + e] = fmaf(f * db, fa[i][2 + e], tot[i][2 + e]);
+        }
       }
     }
   }
@@ -319,14 +449,30 @@ struct ImShape {
   int S, splits, kb_per;
   size_t smem;
 };
-ImShape im_shape(int nt, int64_t n, int sb, int num_sms) {
+ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms) {
   ImShape r;
   const int64_t tiles = (n + IM_ROWS - 1) / IM_ROWS;
-  const int splits = (int)std::max<int64_t>(1, std::min<int64_t>((num_sms + tiles / 2) / tiles, sb / 2));
-  r.kb_per = (sb + splits - 1) / splits;
-  r.splits = (sb + r.kb_per - 1) / r.kb_per;
-  const int stage = IM_ROWS * Q4K_BYTES + nt * 4096 + 32 * 8 * 4;
-  const int fit = (IM_MAX_SMEM - 2 * 8 * 8) / (stage + 16);
+  const int per_sm = im_ctas_per_sm(nt);
+  const int64_t slots = (int64_t)per_sm * num_sms;
+  // split-K count: the fewest waves of CTAs x (superblocks per CTA + one for
+  // a CTA's fixed start-up and merge), fewer splits on a tie
+  r.splits = 1;
+  r.kb_per = sb;
+  int64_t best = INT64_MAX;
+  for (int s = 1; s <= sb; ++s) {
+    const int per = (sb + s - 1) / s, sp = (sb + per - 1) / per;
+    if (sp != s) continue;  // the same split as a smaller count
+    const int64_t cost = (tiles * sp + slots - 1) / slots * (per + 1);
+    if (cost < best) {
+      best = cost;
+      r.splits = sp;
+      r.kb_per = per;
+    }
+    if (tiles * sp >= 2 * slots) break;
+  }
+  const int stage = qt == GGUF_Q4_K ? IM_ROWS * Q4K_BYTES + nt * 4096 + 32 * 8 * 4
+                                    : IM_ROWS * Q6K_BODY + IM_ROWS * 16 + nt * 4096 + 32 * 16 * 4;
+  const int fit = ((per_sm == 2 ? IM_HALF_SMEM : IM_MAX_SMEM) - 2 * 8 * 8) / (stage + 16);
   r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
   r.smem = (size_t)r.S * stage + (size_t)2 * r.S * 8;
   return r;
@@ -342,17 +488,17 @@ ImWs im_ws(int64_t m, int64_t n, int64_t k, int num_sms) {
   ImWs L;
   L.bq = 0;
   L.ssum = (size_t)nt * sb * 4096;
-  L.scl = L.ssum + (size_t)sb * 32 * 8 * 4;
+  L.scl = L.ssum + (size_t)sb * 32 * 16 * 4;  // room for Q6_K's 16 group sums
   L.part = (L.scl + (size_t)sb * 32 * 4 + 255) & ~size_t(255);
-  const ImShape sh = im_shape(nt, n, (int)sb, num_sms);
+  const ImShape sh = im_shape(GGUF_Q4_K, nt, n, (int)sb, num_sms);  // the split count does not depend on the type
   L.end = L.part + (sh.splits > 1 ? (size_t)sh.splits * mc * n * 4 : 0) + 256;
   return L;
 }
 
-template <int NT>
+template <int QT, int NT>
 cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const float* bias, float* y, unsigned* ctr,
                       int num_sms, int* err, cudaStream_t s) {
-  const ImShape sh = im_shape(NT, w.n, (int)w.sb, num_sms);
+  const ImShape sh = im_shape(QT, NT, w.n, (int)w.sb, num_sms);
   char* base = static_cast<char*>(ws);
   ImParams P;
   P.bq = reinterpret_cast<const uint4*>(base + L.bq);
@@ -379,21 +525,28 @@ cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, imma_q4_kernel<NT>, w.wmap, P);
+  return cudaLaunchKernelEx(&cfg, imma_kernel<QT, NT>, w.wmap, w.dmap, P);
 }
 
 }  // namespace
 
-cudaError_t imma_init_device() {
+template <int QT>
+static cudaError_t im_attrs() {
   cudaError_t e = cudaSuccess, r;
-  if ((r = cudaFuncSetAttribute(imma_q4_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
+  if ((r = cudaFuncSetAttribute(imma_kernel<QT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
     e = r;
-  if ((r = cudaFuncSetAttribute(imma_q4_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
+  if ((r = cudaFuncSetAttribute(imma_kernel<QT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
     e = r;
-  if ((r = cudaFuncSetAttribute(imma_q4_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
+  if ((r = cudaFuncSetAttribute(imma_kernel<QT, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
     e = r;
-  if ((r = cudaFuncSetAttribute(imma_q4_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
+  if ((r = cudaFuncSetAttribute(imma_kernel<QT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
     e = r;
+  return e;
+}
+
+cudaError_t imma_init_device() {
+  cudaError_t e = im_attrs<GGUF_Q4_K>();
+  if (e == cudaSuccess) e = im_attrs<GGUF_Q6_K>();
   return e;
 }
 
@@ -402,7 +555,8 @@ size_t imma_counter_bytes(int64_t n) { return (size_t)((n + IM_ROWS - 1) / IM_RO
 
 cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, const float* bias, float* y, void* ws,
                              unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br) {
-  if (w.type != GGUF_Q4_K) return cudaErrorNotSupported;
+  if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
+  const bool q4 = w.type == GGUF_Q4_K;
   const ImWs L = im_ws(m64, w.n, w.k, num_sms);
   const int sb = (int)w.sb;
   for (int64_t m0 = 0; m0 < m64; m0 += 32) {
@@ -410,18 +564,32 @@ cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, co
     const int nt = (m + 7) / 8;
     char* base = static_cast<char*>(ws);
     const int64_t warps = (int64_t)nt * 8 * sb;
-    cudaError_t e = launch_pdl(imma_prep_kernel, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, x + m0 * w.k, m,
-                               nt * 8, w.k, sb, reinterpret_cast<uint4*>(base + L.bq),
-                               reinterpret_cast<int*>(base + L.ssum), reinterpret_cast<float*>(base + L.scl));
+    const dim3 pg((unsigned)((warps + 7) / 8));
+    uint4* bq = reinterpret_cast<uint4*>(base + L.bq);
+    int* ssum = reinterpret_cast<int*>(base + L.ssum);
+    float* scl = reinterpret_cast<float*>(base + L.scl);
+    cudaError_t e = q4 ? launch_pdl(imma_prep_kernel<GGUF_Q4_K>, pg, dim3(256), 0, s, x + m0 * w.k, m, nt * 8, w.k,
+                                    sb, bq, ssum, scl)
+                       : launch_pdl(imma_prep_kernel<GGUF_Q6_K>, pg, dim3(256), 0, s, x + m0 * w.k, m, nt * 8, w.k,
+                                    sb, bq, ssum, scl);
     if (e != cudaSuccess) return e;
     if (launches) ++*launches;
     bracket_record(br.start, s);
     float* yc = y + m0 * w.n;
-    switch (nt) {
-      case 1: e = launch_im<1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-      case 2: e = launch_im<2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-      case 3: e = launch_im<3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-      default: e = launch_im<4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+    if (q4) {
+      switch (nt) {
+        case 1: e = launch_im<GGUF_Q4_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 2: e = launch_im<GGUF_Q4_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 3: e = launch_im<GGUF_Q4_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        default: e = launch_im<GGUF_Q4_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+      }
+    } else {
+      switch (nt) {
+        case 1: e = launch_im<GGUF_Q6_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 2: e = launch_im<GGUF_Q6_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 3: e = launch_im<GGUF_Q6_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        default: e = launch_im<GGUF_Q6_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+      }
     }
     bracket_record(br.stop, s);
     br = Bracket();  // only the first chunk is bracketed

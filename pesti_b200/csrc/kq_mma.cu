@@ -205,6 +205,13 @@ struct Params {
   int* err;
 };
 
+// Hand a raw-ring slot back to the TMA producer: this thread's shared-memory
+// reads of it (generic proxy) are fenced against the TMA refill (async proxy).
+__device__ __forceinline__ void raw_release(uint64_t* empty) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  mbar_arrive(empty);
+}
+
 template <int QT, int BN, bool BF16>
 __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
     kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap dmap,
@@ -333,7 +340,7 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
         uint4 qs[8];
 #pragma unroll
         for (int j = 0; j < 4; ++j) qs[2 * c0 + j] = rp[1 + 2 * c0 + j];
-        mbar_arrive(&raw_empty[rs]);
+        raw_release(&raw_empty[rs]);
         unpack_q4<BF16>(qs, hdr, c0, a0);
         const int q0 = 4 * i + c0, s0 = q0 % C::AS;
         if (q0 >= C::AS && !mbar_wait_warp(&a_empty[s0], ((q0 / C::AS) - 1) & 1, P.err, ERR_WAIT_MMA)) break;
@@ -344,7 +351,7 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
         const uint4 p3 = rp[3 * c0 + 3], p4 = rp[3 * c0 + 4], p5 = rp[3 * c0 + 5];
         const uint4 sc = rp[12];
         const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(raw + R::BODY)[r * 8 + ((sb_lo + i) & 7)]);
-        mbar_arrive(&raw_empty[rs]);
+        raw_release(&raw_empty[rs]);
         unpack_q6<BF16>(p0, p1, p2, sc, d, c0, a0);
         const int q0 = 4 * i + c0, s0 = q0 % C::AS;
         if (q0 >= C::AS && !mbar_wait_warp(&a_empty[s0], ((q0 / C::AS) - 1) & 1, P.err, ERR_WAIT_MMA)) break;

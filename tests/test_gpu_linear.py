@@ -83,6 +83,9 @@ CASES = [
     ("Q4_K", 4096, 4096, 8),   # batched decode shapes (integer MMA: split-K over 32 row tiles)
     ("Q4_K", 4096, 4096, 32),
     ("Q4_K", 300, 14336, 5),   # rows not a multiple of the 128-row tile, 56 superblocks
+    ("Q6_K", 4096, 4096, 8),
+    ("Q6_K", 1024, 14336, 32),
+    ("Q6_K", 300, 14336, 5),
 ]
 
 
