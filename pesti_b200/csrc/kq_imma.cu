@@ -27,7 +27,7 @@
 // superblocks (split-K across CTAs when there are few row tiles).  A producer
 // warp streams one superblock of all 128 rows per stage with one 2D TMA copy
 // (the weight's tensor map: box = one superblock x 128 rows), plus the
-// superblock's activation fragments and sums (bulk copies), through a ring of
+// superblock's activation fragments, sums and scales (bulk copies), through a ring of
 // shared-memory stages; eight MMA warps each own a 16-row tile of every
 // stage.  Partials of the K-splits are added in split order by the last CTA of
 // each row tile (deterministic).  Every wait is bounded.
@@ -148,7 +148,8 @@ struct ImStage {
   static constexpr int D = Q4 ? 0 : IM_ROWS * 16;                  // Q6_K: d of 8 superblocks per row
   static constexpr int B = NT * 4096;                              // activation fragments, 8 tokens per tile
   static constexpr int S = 32 * (Q4 ? 8 : 16) * 4;                 // activation sums of the 32 token slots
-  static constexpr int BYTES = W + D + B + S;                      // a multiple of 128
+  static constexpr int F = 32 * 4;                                 // 2^e of the 32 token slots
+  static constexpr int BYTES = W + D + B + S + F;                  // a multiple of 128
 };
 
 struct ImParams {
@@ -251,11 +252,12 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
           weights(t);
         }
         uint8_t* dst = smem + (size_t)st * St::BYTES + St::W + St::D;
-        sm100::mbar_expect_tx(&full[st], St::B + St::S);  // the stage's arrival
+        sm100::mbar_expect_tx(&full[st], St::B + St::S + St::F);  // the stage's arrival
 #pragma unroll
         for (int i = 0; i < NT; ++i)
           sm100::bulk_load(dst + i * 4096, P.bq + ((size_t)i * P.sb + kb) * 8 * 32, 4096, &full[st]);
         sm100::bulk_load(dst + St::B, P.ssum + (size_t)kb * St::S / 4, St::S, &full[st]);
+        sm100::bulk_load(dst + St::B + St::S, P.scl + (size_t)kb * 32, St::F, &full[st]);
       }
       // no copy may still be in flight into the ring when the CTA retires
       for (int v = max(0, t - P.S); v < t; ++v) sm100::mbar_wait(&full[v % P.S], (v / P.S) & 1, P.err, IM_ERR_FULL);
@@ -333,6 +335,12 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
           }
         }
       }
+      const float* fsc = reinterpret_cast<const float*>(stage + St::W + St::B + St::S);
+      float f[NT][2];
+#pragma unroll
+      for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) f[i][e] = 8 * i + 2 * c + e < P.m ? fsc[8 * i + 2 * c + e] : 0.f;
       stage_release(&empty[st], lane);
       const float da = f16_bits_to_f32((uint16_t)(ha.x & 0xffff)), dma = f16_bits_to_f32((uint16_t)(ha.x >> 16));
       const float db = f16_bits_to_f32((uint16_t)(hb.x & 0xffff)), dmb = f16_bits_to_f32((uint16_t)(hb.x >> 16));
@@ -340,10 +348,8 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       for (int i = 0; i < NT; ++i) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int tk = 8 * i + 2 * c + e;
-          const float f = tk < P.m ? __ldg(P.scl + (size_t)kb * 32 + tk) : 0.f;
-          tot[i][e] = fmaf(f, fmaf(da, fa[i][e], -dma * (float)ma[i][e]), tot[i][e]);
-          tot[i][2 + e] = fmaf(f, fmaf(db, fa[i][2 + e], -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
+          tot[i][e] = fmaf(f[i][e], fmaf(da, fa[i][e], -dma * (float)ma[i][e]), tot[i][e]);
+          tot[i][2 + e] = fmaf(f[i][e], fmaf(db, fa[i][2 + e], -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
         }
       }
     } else {
@@ -397,15 +403,19 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
         }
       // the superblock scales leave the stage before it is released
       const float da = f16_bits_to_f32(dtile[ra * 8 + (kb & 7)]), db = f16_bits_to_f32(dtile[rb * 8 + (kb & 7)]);
+      const float* fsc = reinterpret_cast<const float*>(stage + St::W + St::D + St::B + St::S);
+      float f[NT][2];
+#pragma unroll
+      for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) f[i][e] = 8 * i + 2 * c + e < P.m ? fsc[8 * i + 2 * c + e] : 0.f;
       stage_release(&empty[st], lane);
 #pragma unroll
       for (int i = 0; i < NT; ++i) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const int tk = 8 * i + 2 * c + e;
-          const float f = tk < P.m ? __ldg(P.scl + (size_t)kb * 32 + tk) : 0.f;
-          tot[i][e] = fmaf(f * da, fa[i][e], tot[i][e]);
-          tot[i][2 + e] = fmaf(f * db, fa[i][2 + e], tot[i][2 + e]);
+          tot[i][e] = fmaf(f[i][e] * da, fa[i][e], tot[i][e]);
+          tot[i][2 + e] = fmaf(f[i][e] * db, fa[i][2 + e], tot[i][2 + e]);
         }
       }
     }
@@ -433,13 +443,57 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
   if (!last) return;
   __threadfence();
+  // a full tile (128 rows, n a multiple of 4): each thread owns up to four
+  // 4-row groups of the <= 32 x 128 outputs and reads a split's partials for
+  // all of them at once (one memory round trip per split); summation order as
+  // in the scalar form (bias, then the splits in order)
   const int rows = (int)(P.n - row0 < IM_ROWS ? P.n - row0 : IM_ROWS);
-  for (int e = threadIdx.x; e < P.m * rows; e += 32 * IM_WARPS) {
-    const int tk = e / rows, r = e - tk * rows;
-    const int64_t idx = (int64_t)tk * P.n + row0 + r;
-    float v = P.bias ? P.bias[row0 + r] : 0.f;
-    for (int q = 0; q < P.splits; ++q) v += __ldcg(P.part + (size_t)q * P.m * P.n + idx);
-    P.y[idx] = v;
+  if (rows == IM_ROWS && (P.n & 3) == 0) {
+    constexpr int U = 32 * (IM_ROWS / 4) / (32 * IM_WARPS);
+    const int total4 = P.m * (IM_ROWS / 4);
+    float4 v[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = threadIdx.x + u * 32 * IM_WARPS, r = 4 * (e & (IM_ROWS / 4 - 1));
+      v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < total4 && P.bias)
+        v[u] = make_float4(P.bias[row0 + r], P.bias[row0 + r + 1], P.bias[row0 + r + 2], P.bias[row0 + r + 3]);
+    }
+#pragma unroll 2
+    for (int q = 0; q < P.splits; ++q) {
+      const float* pq = P.part + (size_t)q * P.m * P.n + row0;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int e = threadIdx.x + u * 32 * IM_WARPS;
+        if (e < total4) {
+          const float4 t = __ldcg(reinterpret_cast<const float4*>(pq + (int64_t)(e / (IM_ROWS / 4)) * P.n +
+                                                                  4 * (e & (IM_ROWS / 4 - 1))));
+          v[u].x += t.x;
+          v[u].y += t.y;
+          v[u].z += t.z;
+          v[u].w += t.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = threadIdx.x + u * 32 * IM_WARPS;
+      if (e < total4) {
+        float* yo = P.y + (int64_t)(e / (IM_ROWS / 4)) * P.n + row0 + 4 * (e & (IM_ROWS / 4 - 1));
+        yo[0] = v[u].x;
+        yo[1] = v[u].y;
+        yo[2] = v[u].z;
+        yo[3] = v[u].w;
+      }
+    }
+  } else {
+    for (int e = threadIdx.x; e < P.m * rows; e += 32 * IM_WARPS) {
+      const int tk = e / rows, r = e - tk * rows;
+      const int64_t idx = (int64_t)tk * P.n + row0 + r;
+      float v = P.bias ? P.bias[row0 + r] : 0.f;
+      for (int q = 0; q < P.splits; ++q) v += __ldcg(P.part + (size_t)q * P.m * P.n + idx);
+      P.y[idx] = v;
+    }
   }
   if (threadIdx.x == 0) P.ctr[blockIdx.x] = 0u;  // ready for the next call (stream-ordered)
 }
@@ -470,8 +524,8 @@ ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms) {
     }
     if (tiles * sp >= 2 * slots) break;
   }
-  const int stage = qt == GGUF_Q4_K ? IM_ROWS * Q4K_BYTES + nt * 4096 + 32 * 8 * 4
-                                    : IM_ROWS * Q6K_BODY + IM_ROWS * 16 + nt * 4096 + 32 * 16 * 4;
+  const int stage = qt == GGUF_Q4_K ? IM_ROWS * Q4K_BYTES + nt * 4096 + 32 * 8 * 4 + 128
+                                    : IM_ROWS * Q6K_BODY + IM_ROWS * 16 + nt * 4096 + 32 * 16 * 4 + 128;
   const int fit = ((per_sm == 2 ? IM_HALF_SMEM : IM_MAX_SMEM) - 2 * 8 * 8) / (stage + 16);
   r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
   r.smem = (size_t)r.S * stage + (size_t)2 * r.S * 8;
