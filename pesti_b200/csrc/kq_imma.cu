@@ -544,8 +544,16 @@ ImWs im_ws(int64_t m, int64_t n, int64_t k, int num_sms) {
   L.ssum = (size_t)nt * sb * 4096;
   L.scl = L.ssum + (size_t)sb * 32 * 16 * 4;  // room for Q6_K's 16 group sums
   L.part = (L.scl + (size_t)sb * 32 * 4 + 255) & ~size_t(255);
-  const ImShape sh = im_shape(GGUF_Q4_K, nt, n, (int)sb, num_sms);  // the split count does not depend on the type
-  L.end = L.part + (sh.splits > 1 ? (size_t)sh.splits * mc * n * 4 : 0) + 256;
+  // partials of the largest chunk: a full 32-token chunk and the tail chunk
+  // can split K differently (one or two CTAs per SM); the split count does
+  // not depend on the weight type
+  size_t part = 0;
+  for (const int64_t c : {mc, m > 32 ? m % 32 : (int64_t)0}) {
+    if (c <= 0) continue;
+    const ImShape sh = im_shape(GGUF_Q4_K, (int)((c + 7) / 8), n, (int)sb, num_sms);
+    if (sh.splits > 1) part = std::max(part, (size_t)sh.splits * c * n * 4);
+  }
+  L.end = L.part + part + 256;
   return L;
 }
 

@@ -86,6 +86,7 @@ CASES = [
     ("Q6_K", 4096, 4096, 8),
     ("Q6_K", 1024, 14336, 32),
     ("Q6_K", 300, 14336, 5),
+    ("Q4_K", 9600, 512, 40),   # 75 row tiles: the 32-token chunk runs unsplit, the 8-token tail split in two
 ]
 
 
