@@ -98,26 +98,34 @@ __global__ void __launch_bounds__(256) rope_append_kernel(float* __restrict__ qk
 
 // Decode attention, split over the sequence (flash-decoding), in one kernel.
 // CTA = (kv head, split, token), 256 threads, about two CTAs per SM.  The
-// split's K and V rows are contiguous in the cache, so they arrive by bulk
-// copies (cp.async.bulk) in tiles of AT_TILE positions through a two-stage
-// shared-memory ring: tile j + 1 lands while tile j is computed.  Per tile:
-// one thread per (query head, position) score -- a 16-byte-chunk walk along
-// the K row, rotated by the position so 8 neighbouring threads read 8
-// different chunks (no bank conflicts) -- then one warp per query head for
-// the online-softmax update, then one thread per (query head, 2 dims) for
-// P.V.  With ROPE the kernel also rotates the group's query heads (in shared
+// split's K and V rows arrive in tiles of AT_TILE positions through a
+// two-stage shared-memory ring filled with 16-byte cp.async copies (all
+// threads; tile j + 2 is issued once tile j is consumed), into rows padded to
+// HD * 2 + 16 bytes so that the eight rows a warp's fragment loads touch sit
+// on different banks.  Both products run on the tensor cores
+// (mma.sync.m16n8k16, f16 inputs, f32 accumulate) with the group's query
+// heads as the M rows (G <= 8 of 16; the other rows are zero):
+//  * scores: warp w takes positions 8w .. 8w+7 of the tile; A = q, B = K^T
+//    read straight from the K rows.  q enters as two f16 parts (hi, and the
+//    f16 rounding of q - hi) after scaling each head by a power of two that
+//    puts its largest |q| in [2^14, 2^15), so the f16 products carry q to
+//    about 2^-22 of that head's largest element;
+//  * online softmax: one warp per query head over the tile, as before;
+//  * P.V: warp w takes head dims 16w .. 16w+15; A = the probabilities (hi and
+//    lo f16 parts again), B = V through ldmatrix.trans.
+// With ROPE the kernel also rotates the group's query heads (in shared
 // memory: qkv is not written back) and the split holding `pos` appends the
 // rotated k and v of the new token to the f16 caches; that row is patched
-// into its tile in shared memory (the bulk copies stop before it), so it is
-// read as the same f16 values every later step reads.  Each CTA writes one
-// partial (max, sum, acc[HD]) per query head; the last CTA of a (token, kv
-// head) to finish -- an arrival counter in the scratch, reset by that CTA --
-// merges the splits' partials into `out`.
+// into its tile in shared memory (the copies skip it), so it is read as the
+// same f16 values every later step reads.  Each CTA writes one partial (max,
+// sum, acc[HD]) per query head; the last CTA of a (token, kv head) to finish
+// -- an arrival counter in the scratch, reset by that CTA -- merges the
+// splits' partials into `out`.  No wait in the kernel spins: the ring is
+// ordered by cp.async groups and block barriers.
 constexpr int AT_THREADS = 256;
 constexpr int AT_TILE = 64;  // positions per ring stage
 constexpr int ATT_MAX_GROUP = 8;  // query heads per kv head
 constexpr int ATT_MAX_SPLITS = 64;
-constexpr int ERR_ATT_WAIT = 24;
 
 struct AttnArgs {
   const float* q;     // token b's query heads at q + b * q_ld (ROPE: the fused qkv row)
@@ -138,77 +146,111 @@ struct AttnArgs {
 // Dynamic shared memory of the decode-attention kernel (bytes).
 template <int HD, int G>
 struct AttnSmem {
-  static constexpr int TILE_B = AT_TILE * HD * 2;  // one K or V tile (f16)
+  static constexpr int PITCH = HD * 2 + 16;        // bytes per K / V row in shared memory
+  static constexpr int TILE_B = AT_TILE * PITCH;   // one K or V tile
   static constexpr int STAGE = 2 * TILE_B;
   static constexpr int Q = 2 * STAGE;                       // q [G][HD] f32
   static constexpr int S = Q + G * HD * 4;                  // scores / probabilities [G][AT_TILE]
-  static constexpr int ML = S + G * AT_TILE * 4;            // running max, sum, tile correction [3][G]
-  static constexpr int NEW = ML + ((3 * G * 4 + 15) / 16) * 16;  // appended k | v row, f16
-  static constexpr int BAR = NEW + 2 * HD * 2;
-  static constexpr int END = BAR + 16;
+  static constexpr int ML = S + G * AT_TILE * 4;            // running max, sum, tile correction, q scale [4][G]
+  static constexpr int NEW = ML + ((4 * G * 4 + 15) / 16) * 16;  // appended k | v row, f16
+  static constexpr int END = NEW + 2 * HD * 2;
   // after the last tile the ring is reused by the split merge
   static constexpr int CF = 0;                              // weights [G][ATT_MAX_SPLITS]
   static constexpr int CL = CF + G * ATT_MAX_SPLITS * 4;    // sums [G][ATT_MAX_SPLITS]
   static constexpr int CI = CL + G * ATT_MAX_SPLITS * 4;    // 1 / total sum [G]
   static constexpr int CR = CI + ((G * 4 + 15) / 16) * 16;  // per-warp sums [AT_THREADS / 32][G * HD]
   static_assert(CR + (AT_THREADS / 32) * G * HD * 4 <= 2 * STAGE, "merge scratch exceeds the ring");
+  static_assert(HD / 16 <= AT_THREADS / 32 && AT_TILE == 8 * (AT_THREADS / 32), "warp roles");
 };
+
+__device__ __forceinline__ void at_cp16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sm100::smem_u32(dst)), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void at_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void at_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// f16 pair {hi(a), hi(b)} and the pair of remainders {a - hi(a), b - hi(b)}, low half = a
+__device__ __forceinline__ void at_split(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const __half2 l = __floats2half2_rn(a - __low2float(h), b - __high2float(h));
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// D = A . B + D, m16n8k16, f16 inputs, f32 accumulate; A rows 8..15 are zero here
+__device__ __forceinline__ void at_mma(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void at_ldm_x4_trans(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(sm100::smem_u32(p))
+               : "memory");
+}
 
 template <int HD, int G, bool ROPE>
 __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnArgs A) {
   using L = AttnSmem<HD, G>;
-  constexpr int HALF = HD / 2, C8 = HD / 8;  // C8: 16-byte chunks per f16 row
-  constexpr int NPAIR = (G * HALF + AT_THREADS - 1) / AT_THREADS;
+  constexpr int HALF = HD / 2, CH = HD / 8, KS = HD / 16, PITCH = L::PITCH;
   extern __shared__ __align__(128) uint8_t sm[];
   pdl_enter();
   const int hk = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;  // fragment row (query head) and column pair
   const int64_t chunk = (A.len + A.splits - 1) / A.splits;
   const int64_t t0 = min(A.len, (int64_t)sp * chunk), t1 = min(A.len, t0 + chunk);
   const int64_t pos = A.len - 1;
   const bool has_new = ROPE && pos >= t0 && pos < t1;
-  const int64_t copy_end = has_new ? pos : t1;  // the bulk copies stop before the appended row
   const int ntiles = (int)((t1 - t0 + AT_TILE - 1) / AT_TILE);
   const float* row = A.q + (int64_t)b * A.q_ld;
   const int64_t base = ((int64_t)b * A.hkv + hk) * A.max_seq * HD;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + L::BAR);
   float* q_s = reinterpret_cast<float*>(sm + L::Q);
   float* s_s = reinterpret_cast<float*>(sm + L::S);
   float* m_s = reinterpret_cast<float*>(sm + L::ML);
   float* l_s = m_s + G;
   float* c_s = l_s + G;
+  float* x_s = c_s + G;  // 2^e of each head's q scaling
   __half* new_s = reinterpret_cast<__half*>(sm + L::NEW);
 
-  auto issue = [&](int j) {  // tile j into stage j % 2 (one thread)
+  // tile j into stage j % 2 (every thread issues its share, then one group);
+  // rows past the split and the appended row are zero-filled (the latter is
+  // patched in from new_s)
+  auto issue = [&](int j) {
     const int64_t r0 = t0 + (int64_t)j * AT_TILE;
-    const int64_t r1 = min(copy_end, r0 + AT_TILE);
-    const uint32_t bytes = r1 > r0 ? (uint32_t)((r1 - r0) * HD * 2) : 0u;
-    sm100::mbar_expect_tx(&bar[j & 1], 2 * bytes);
-    if (bytes) {
-      uint8_t* st = sm + (j & 1) * L::STAGE;
-      sm100::bulk_load(st, A.kc + base + r0 * HD, bytes, &bar[j & 1]);
-      sm100::bulk_load(st + L::TILE_B, A.vc + base + r0 * HD, bytes, &bar[j & 1]);
+    uint8_t* st = sm + (j & 1) * L::STAGE;
+    for (int e = tid; e < 2 * AT_TILE * CH; e += AT_THREADS) {
+      const int kv = e / (AT_TILE * CH), rem = e - kv * (AT_TILE * CH);
+      const int r = rem / CH, ch = rem - r * CH;
+      const int64_t t = r0 + r;
+      const bool live = t < t1 && !(has_new && t == pos);
+      const __half* src = (kv ? A.vc : A.kc) + base + (live ? t : t0) * HD + ch * 8;
+      at_cp16(st + kv * L::TILE_B + r * PITCH + ch * 16, src, live ? 16u : 0u);
     }
+    at_commit();
   };
-  if (tid == 0) {
-    sm100::mbar_init(&bar[0], 1);
-    sm100::mbar_init(&bar[1], 1);
-    sm100::mbar_fence_init();
-    if (ntiles > 0) issue(0);
-    if (ntiles > 1) issue(1);
-  }
+  if (ntiles > 0) issue(0); else at_commit();
+  if (ntiles > 1) issue(1); else at_commit();
+
   for (int e = tid; e < G * HALF; e += AT_THREADS) {
-    const int g = e / HALF, i = e - g * HALF;
-    const float* p = row + (int64_t)(hk * G + g) * HD;
+    const int gg = e / HALF, i = e - gg * HALF;
+    const float* p = row + (int64_t)(hk * G + gg) * HD;
     if constexpr (ROPE) {
-      float c, s;
-      rope_cs(pos, i, HALF, A.theta, c, s);
+      float cs, sn;
+      rope_cs(pos, i, HALF, A.theta, cs, sn);
       const float a = p[i], bb = p[i + HALF];
-      q_s[g * HD + i] = (a * c - bb * s) * A.scale;
-      q_s[g * HD + i + HALF] = (a * s + bb * c) * A.scale;
+      q_s[gg * HD + i] = (a * cs - bb * sn) * A.scale;
+      q_s[gg * HD + i + HALF] = (a * sn + bb * cs) * A.scale;
     } else {
-      q_s[g * HD + i] = p[i] * A.scale;
-      q_s[g * HD + i + HALF] = p[i + HALF] * A.scale;
+      q_s[gg * HD + i] = p[i] * A.scale;
+      q_s[gg * HD + i + HALF] = p[i + HALF] * A.scale;
     }
   }
   if (has_new) {
@@ -216,10 +258,10 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
     const float* vp = row + (int64_t)(A.hq + A.hkv + hk) * HD;
     const int64_t o = base + pos * HD;
     for (int i = tid; i < HALF; i += AT_THREADS) {
-      float c, s;
-      rope_cs(pos, i, HALF, A.theta, c, s);
+      float cs, sn;
+      rope_cs(pos, i, HALF, A.theta, cs, sn);
       const float a = kp[i], bb = kp[i + HALF];
-      const __half k0 = __float2half_rn(a * c - bb * s), k1 = __float2half_rn(a * s + bb * c);
+      const __half k0 = __float2half_rn(a * cs - bb * sn), k1 = __float2half_rn(a * sn + bb * cs);
       const __half v0 = __float2half_rn(vp[i]), v1 = __float2half_rn(vp[i + HALF]);
       A.kc[o + i] = k0;
       A.kc[o + i + HALF] = k1;
@@ -235,116 +277,132 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
     m_s[tid] = -INFINITY;
     l_s[tid] = 0.f;
   }
-  float2 acc[NPAIR];
-#pragma unroll
-  for (int k = 0; k < NPAIR; ++k) acc[k] = make_float2(0.f, 0.f);
   __syncthreads();
+  // each head's power-of-two q scale: largest |q| 2^-e in [2^14, 2^15)
+  if (warp < G) {
+    float mx = 0.f;
+    for (int i = lane; i < HD; i += 32) mx = fmaxf(mx, fabsf(q_s[warp * HD + i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) {
+      int e = 0;
+      if (mx > 0.f && mx <= 3.4e38f) e = (int)((__float_as_uint(mx) >> 23) & 0xff) - 127 - 14;
+      e = max(-126, min(126, e));
+      x_s[warp] = __uint_as_float((uint32_t)(127 + e) << 23);
+    }
+  }
+  __syncthreads();
+  // q as A fragments (rows = query heads): hi and lo f16 parts, 2 registers per k16 step
+  uint32_t qh[KS][2], ql[KS][2];
+  {
+    const float inv = g < G ? 1.f / x_s[g] : 0.f;  // a power of two: exact
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int d = 16 * kk + 8 * h + 2 * c;
+        const float v0 = g < G ? q_s[g * HD + d] * inv : 0.f, v1 = g < G ? q_s[g * HD + d + 1] * inv : 0.f;
+        at_split(v0, v1, qh[kk][h], ql[kk][h]);
+      }
+  }
+  float o[2][4];  // P.V accumulators: head g, dims 16 warp + 8 t + 2c, +1
+#pragma unroll
+  for (int t = 0; t < 2; ++t) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
 
   for (int j = 0; j < ntiles; ++j) {
     const int64_t r0 = t0 + (int64_t)j * AT_TILE;
     const int rows = (int)(t1 - r0 < AT_TILE ? t1 - r0 : AT_TILE);
-    __half* Ks = reinterpret_cast<__half*>(sm + (j & 1) * L::STAGE);
-    __half* Vs = Ks + AT_TILE * HD;
-    const bool ok = sm100::mbar_wait(&bar[j & 1], (j >> 1) & 1, A.err, ERR_ATT_WAIT);
-    if (!__syncthreads_and(ok)) {
-      // give up: let the copies already issued land before the CTA exits
-      if (tid == 0 && j + 1 < ntiles) sm100::mbar_wait(&bar[(j + 1) & 1], ((j + 1) >> 1) & 1, A.err, ERR_ATT_WAIT);
-      return;
-    }
+    uint8_t* Ks = sm + (j & 1) * L::STAGE;
+    uint8_t* Vs = Ks + L::TILE_B;
+    at_wait_prev();  // this thread's copies of tile j have landed (tile j + 1 may be in flight)
+    __syncthreads();
     if (has_new && pos >= r0 && pos < r0 + rows) {
       const int r = (int)(pos - r0);
       for (int i = tid; i < HD; i += AT_THREADS) {
-        Ks[r * HD + i] = new_s[i];
-        Vs[r * HD + i] = new_s[HD + i];
+        reinterpret_cast<__half*>(Ks + r * PITCH)[i] = new_s[i];
+        reinterpret_cast<__half*>(Vs + r * PITCH)[i] = new_s[HD + i];
       }
       __syncthreads();
     }
-    // scores of (query head g, position t)
-    for (int e = tid; e < G * AT_TILE; e += AT_THREADS) {
-      const int g = e / AT_TILE, t = e - g * AT_TILE;
-      if (t < rows) {
-        const uint4* kr = reinterpret_cast<const uint4*>(Ks + t * HD);
-        const float4* qg = reinterpret_cast<const float4*>(q_s + g * HD);
-        float d = 0.f;
+    // scores of (query head g, positions 8 warp + 2c, +1)
+    {
+      const uint8_t* kt = Ks + (8 * warp + g) * PITCH + 4 * c;
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int c = 0; c < C8; ++c) {
-          const int cc = (c + t) & (C8 - 1);
-          const uint4 kw = kr[cc];
-          const float4 qa = qg[2 * cc], qb = qg[2 * cc + 1];
-          const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kw.x));
-          const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kw.y));
-          const float2 k2 = __half22float2(*reinterpret_cast<const __half2*>(&kw.z));
-          const float2 k3 = __half22float2(*reinterpret_cast<const __half2*>(&kw.w));
-          d = fmaf(qa.x, k0.x, d);
-          d = fmaf(qa.y, k0.y, d);
-          d = fmaf(qa.z, k1.x, d);
-          d = fmaf(qa.w, k1.y, d);
-          d = fmaf(qb.x, k2.x, d);
-          d = fmaf(qb.y, k2.y, d);
-          d = fmaf(qb.z, k3.x, d);
-          d = fmaf(qb.w, k3.y, d);
-        }
-        s_s[g * AT_TILE + t] = d;
+      for (int kk = 0; kk < KS; ++kk) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kt + 32 * kk);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kt + 32 * kk + 16);
+        at_mma(sc, qh[kk][0], qh[kk][1], b0, b1);
+        at_mma(sc, ql[kk][0], ql[kk][1], b0, b1);
+      }
+      if (g < G) {
+        const float xs = x_s[g];
+        *reinterpret_cast<float2*>(s_s + g * AT_TILE + 8 * warp + 2 * c) = make_float2(sc[0] * xs, sc[1] * xs);
       }
     }
     __syncthreads();
-    // online softmax: warp g updates query head g
-    for (int g = warp; g < G; g += AT_THREADS / 32) {
-      const float v0 = lane < rows ? s_s[g * AT_TILE + lane] : -INFINITY;
-      const float v1 = lane + 32 < rows ? s_s[g * AT_TILE + lane + 32] : -INFINITY;
+    // online softmax: warp gg updates query head gg
+    for (int gg = warp; gg < G; gg += AT_THREADS / 32) {
+      const float v0 = lane < rows ? s_s[gg * AT_TILE + lane] : -INFINITY;
+      const float v1 = lane + 32 < rows ? s_s[gg * AT_TILE + lane + 32] : -INFINITY;
       float mx = fmaxf(v0, v1);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const float mold = m_s[g], mnew = fmaxf(mold, mx);
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mold = m_s[gg], mnew = fmaxf(mold, mx);
       const float p0 = lane < rows ? __expf(v0 - mnew) : 0.f;
       const float p1 = lane + 32 < rows ? __expf(v1 - mnew) : 0.f;
-      s_s[g * AT_TILE + lane] = p0;
-      s_s[g * AT_TILE + lane + 32] = p1;
+      s_s[gg * AT_TILE + lane] = p0;
+      s_s[gg * AT_TILE + lane + 32] = p1;
       float ps = p0 + p1;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
       if (lane == 0) {
         const float corr = __expf(mold - mnew);  // 0 while mold is -inf
-        c_s[g] = corr;
-        l_s[g] = l_s[g] * corr + ps;
-        m_s[g] = mnew;
+        c_s[gg] = corr;
+        l_s[gg] = l_s[gg] * corr + ps;
+        m_s[gg] = mnew;
       }
     }
     __syncthreads();
-    // P.V: thread = (query head g, dims 2 d2, 2 d2 + 1)
+    // P.V: warp w owns head dims 16w .. 16w+15 (two n8 tiles)
+    if (warp < HD / 16) {
+      const float corr = g < G ? c_s[g] : 0.f;
 #pragma unroll
-    for (int k = 0; k < NPAIR; ++k) {
-      const int e = tid + k * AT_THREADS;
-      if (e < G * HALF) {
-        const int g = e / HALF, d2 = e - g * HALF;
-        const __half2* vcol = reinterpret_cast<const __half2*>(Vs) + d2;
-        const float* pg = s_s + g * AT_TILE;
-        const float corr = c_s[g];
-        float2 a = make_float2(acc[k].x * corr, acc[k].y * corr);
-#pragma unroll 8
-        for (int t = 0; t < rows; ++t) {
-          const float2 v = __half22float2(vcol[t * HALF]);
-          const float p = pg[t];
-          a.x = fmaf(p, v.x, a.x);
-          a.y = fmaf(p, v.y, a.y);
-        }
-        acc[k] = a;
+      for (int t = 0; t < 2; ++t) {
+        o[t][0] *= corr;
+        o[t][1] *= corr;
+      }
+      const int mat = lane >> 3, rr = lane & 7;
+      const uint8_t* va = Vs + ((mat & 1) * 8 + rr) * PITCH + (16 * warp + (mat >> 1) * 8) * 2;
+#pragma unroll
+      for (int kk = 0; kk < AT_TILE / 16; ++kk) {
+        const float2 pa = g < G ? *reinterpret_cast<const float2*>(s_s + g * AT_TILE + 16 * kk + 2 * c)
+                                : make_float2(0.f, 0.f);
+        const float2 pb = g < G ? *reinterpret_cast<const float2*>(s_s + g * AT_TILE + 16 * kk + 8 + 2 * c)
+                                : make_float2(0.f, 0.f);
+        uint32_t ph0, pl0, ph2, pl2;
+        at_split(pa.x, pa.y, ph0, pl0);
+        at_split(pb.x, pb.y, ph2, pl2);
+        uint32_t v0, v1, v2, v3;
+        at_ldm_x4_trans(va + 16 * kk * PITCH, v0, v1, v2, v3);
+        at_mma(o[0], ph0, ph2, v0, v1);
+        at_mma(o[0], pl0, pl2, v0, v1);
+        at_mma(o[1], ph0, ph2, v2, v3);
+        at_mma(o[1], pl0, pl2, v2, v3);
       }
     }
     __syncthreads();  // the stage and the scores are free again
-    if (tid == 0 && j + 2 < ntiles) issue(j + 2);
+    if (j + 2 < ntiles) issue(j + 2); else at_commit();
   }
 
   // this split's partial per query head
   constexpr int PS = HD + 4;  // partial row: max, sum, 2 pad, acc[HD] (16-byte aligned)
   float* pb = A.part + ((int64_t)b * A.hq + hk * G) * A.splits * PS;
+  if (warp < HD / 16 && g < G) {
 #pragma unroll
-  for (int k = 0; k < NPAIR; ++k) {
-    const int e = tid + k * AT_THREADS;
-    if (e < G * HALF) {
-      const int g = e / HALF, d2 = e - g * HALF;
-      *reinterpret_cast<float2*>(pb + ((int64_t)g * A.splits + sp) * PS + 4 + 2 * d2) = acc[k];
-    }
+    for (int t = 0; t < 2; ++t)
+      *reinterpret_cast<float2*>(pb + ((int64_t)g * A.splits + sp) * PS + 4 + 16 * warp + 8 * t + 2 * c) =
+          make_float2(o[t][0], o[t][1]);
   }
   if (tid < G) *reinterpret_cast<float2*>(pb + ((int64_t)tid * A.splits + sp) * PS) = make_float2(m_s[tid], l_s[tid]);
   // the last CTA of (token, kv head) merges the splits
