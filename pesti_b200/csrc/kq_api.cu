@@ -168,9 +168,8 @@ int check_device_error(kq_ctx* ctx) {
   cudaDeviceSynchronize();
   cudaGetLastError();
   return fail(ctx, KQ_ERR_CUDA,
-              "a device-side wait gave up (code %d: 1-5 tcgen05 pipeline, 21-23 decode weight ring, 24 "
-              "attention KV ring, 27-28 batched Q4_K ring, 31-32 tensor-parallel peer flag); the call's output "
-              "is invalid",
+              "a device-side wait gave up (code %d: 1-5 tcgen05 pipeline, 21-23 decode weight ring, "
+              "27-28 batched integer-MMA ring, 31-32 tensor-parallel peer flag); the call's output is invalid",
               code);
 }
 
