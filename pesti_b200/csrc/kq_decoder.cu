@@ -150,8 +150,9 @@ struct AttnSmem {
   static constexpr int TILE_B = AT_TILE * PITCH;   // one K or V tile
   static constexpr int STAGE = 2 * TILE_B;
   static constexpr int Q = 2 * STAGE;                       // q [G][HD] f32
-  static constexpr int S = Q + G * HD * 4;                  // scores / probabilities [G][AT_TILE]
-  static constexpr int ML = S + G * AT_TILE * 4;            // running max, sum, tile correction, q scale [4][G]
+  static constexpr int SP = AT_TILE + 8;                    // score row pitch (floats): rows 8 banks apart
+  static constexpr int S = Q + G * HD * 4;                  // scores / probabilities [G][SP]
+  static constexpr int ML = S + G * SP * 4;                 // running max, sum, tile correction, q scale [4][G]
   static constexpr int NEW = ML + ((4 * G * 4 + 15) / 16) * 16;  // appended k | v row, f16
   static constexpr int END = NEW + 2 * HD * 2;
   // after the last tile the ring is reused by the split merge
@@ -337,22 +338,22 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
       }
       if (g < G) {
         const float xs = x_s[g];
-        *reinterpret_cast<float2*>(s_s + g * AT_TILE + 8 * warp + 2 * c) = make_float2(sc[0] * xs, sc[1] * xs);
+        *reinterpret_cast<float2*>(s_s + g * L::SP + 8 * warp + 2 * c) = make_float2(sc[0] * xs, sc[1] * xs);
       }
     }
     __syncthreads();
     // online softmax: warp gg updates query head gg
     for (int gg = warp; gg < G; gg += AT_THREADS / 32) {
-      const float v0 = lane < rows ? s_s[gg * AT_TILE + lane] : -INFINITY;
-      const float v1 = lane + 32 < rows ? s_s[gg * AT_TILE + lane + 32] : -INFINITY;
+      const float v0 = lane < rows ? s_s[gg * L::SP + lane] : -INFINITY;
+      const float v1 = lane + 32 < rows ? s_s[gg * L::SP + lane + 32] : -INFINITY;
       float mx = fmaxf(v0, v1);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
       const float mold = m_s[gg], mnew = fmaxf(mold, mx);
       const float p0 = lane < rows ? __expf(v0 - mnew) : 0.f;
       const float p1 = lane + 32 < rows ? __expf(v1 - mnew) : 0.f;
-      s_s[gg * AT_TILE + lane] = p0;
-      s_s[gg * AT_TILE + lane + 32] = p1;
+      s_s[gg * L::SP + lane] = p0;
+      s_s[gg * L::SP + lane + 32] = p1;
       float ps = p0 + p1;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
@@ -376,9 +377,9 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
       const uint8_t* va = Vs + ((mat & 1) * 8 + rr) * PITCH + (16 * warp + (mat >> 1) * 8) * 2;
 #pragma unroll
       for (int kk = 0; kk < AT_TILE / 16; ++kk) {
-        const float2 pa = g < G ? *reinterpret_cast<const float2*>(s_s + g * AT_TILE + 16 * kk + 2 * c)
+        const float2 pa = g < G ? *reinterpret_cast<const float2*>(s_s + g * L::SP + 16 * kk + 2 * c)
                                 : make_float2(0.f, 0.f);
-        const float2 pb = g < G ? *reinterpret_cast<const float2*>(s_s + g * AT_TILE + 16 * kk + 8 + 2 * c)
+        const float2 pb = g < G ? *reinterpret_cast<const float2*>(s_s + g * L::SP + 16 * kk + 8 + 2 * c)
                                 : make_float2(0.f, 0.f);
         uint32_t ph0, pl0, ph2, pl2;
         at_split(pa.x, pa.y, ph0, pl0);
