@@ -40,6 +40,7 @@ extern "C" {
 #define KQ_ERR_NCCL 5         /* a collective failed                    */
 #define KQ_ERR_STATE 6        /* call out of order (e.g. no TP group)   */
 #define KQ_ERR_NOMEM 7        /* device allocation failed               */
+#define KQ_ERR_FORMAT 8       /* file unreadable or not well-formed GGUF */
 
 /* weight encodings (values follow GGML's type ids for the GGUF layouts) */
 enum kq_type {
@@ -179,6 +180,47 @@ int kq_tp_linear_f32(kq_tp *tp, const kq_weight *shard, int64_t row0, int64_t n_
 int kq_tp_allgather_f32(kq_tp *tp, const float *y_local, int64_t m, int64_t row0, int64_t rows,
                         int64_t n_total, float *y, int64_t y_ld, int flags);
 int kq_tp_destroy(kq_tp *tp);
+
+/* ---- GGUF files ----------------------------------------------------------- */
+/* A GGUF (version 2 or 3) file's metadata and tensor directory, read once on
+ * open; tensor bytes are read on demand.  Stands in for the external
+ * pesti-gguf reader the reference calls to get raw tensor bytes
+ * (extract_tensor_bytes_from_path, pesti-runner/src/gguf_weight_loader.rs:
+ * 79-81; GgufDtype / stored_size, :20-21).  Host code: no context or GPU is
+ * needed except for kq_gguf_upload.  A malformed file gives KQ_ERR_FORMAT and
+ * a message in err (err_len bytes, may be 0). */
+typedef struct kq_gguf kq_gguf;
+int kq_gguf_open(const char *path, kq_gguf **out, char *err, size_t err_len);
+void kq_gguf_close(kq_gguf *f);
+/* Tensors: index 0 .. count-1 in file order; -1 when not found. */
+int64_t kq_gguf_tensor_count(const kq_gguf *f);
+int64_t kq_gguf_find_tensor(const kq_gguf *f, const char *name);
+/* ggml_type: the file's type code (12 Q4_K, 14 Q6_K, 0 F32, ...); dims[4]:
+ * ne[0] (innermost, the row length) first, unused dims 1; file_offset:
+ * absolute; nbytes: 0 for a type the reader does not size.  name stays valid
+ * until kq_gguf_close. */
+int kq_gguf_tensor_info(const kq_gguf *f, int64_t i, const char **name, int *ggml_type, int *n_dims,
+                        int64_t *dims, uint64_t *file_offset, uint64_t *nbytes);
+/* The tensor's bytes as stored into dst (dst_bytes >= nbytes). */
+int kq_gguf_read_tensor(const kq_gguf *f, int64_t i, void *dst, uint64_t dst_bytes);
+/* A 2-D Q4_K / Q6_K tensor [ne1 rows][ne0] as a device-resident weight
+ * (out_features = ne[1], in_features = ne[0]), through kq_weight_upload. */
+int kq_gguf_upload(kq_ctx *ctx, const kq_gguf *f, int64_t i, kq_weight **out);
+/* Metadata: value_type / elem_type are GGUF's codes (0 u8 .. 12 f64, 8
+ * string, 9 array; elem_type -1 unless an array); count: 1 for a scalar or a
+ * string, the element count of an array.  Nested arrays are listed with their
+ * count only.  kq_gguf_meta_int takes any integer or bool scalar,
+ * kq_gguf_meta_float any number; kq_gguf_meta_string a string (j = 0) or
+ * element j of a string array; kq_gguf_meta_array the packed little-endian
+ * elements of a numeric array.  Pointers stay valid until kq_gguf_close. */
+int64_t kq_gguf_meta_count(const kq_gguf *f);
+int64_t kq_gguf_find_meta(const kq_gguf *f, const char *key);
+int kq_gguf_meta_info(const kq_gguf *f, int64_t i, const char **key, int *value_type, int *elem_type,
+                      uint64_t *count);
+int kq_gguf_meta_int(const kq_gguf *f, int64_t i, int64_t *v);
+int kq_gguf_meta_float(const kq_gguf *f, int64_t i, double *v);
+int kq_gguf_meta_string(const kq_gguf *f, int64_t i, uint64_t j, const char **s, uint64_t *len);
+int kq_gguf_meta_array(const kq_gguf *f, int64_t i, const void **data, uint64_t *elem_bytes);
 
 #ifdef __cplusplus
 }

@@ -228,6 +228,11 @@ int prepare_f32(kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
 
 }  // namespace
 
+namespace kq {
+// kq_last_error text for entry points defined in other files (the GGUF reader)
+int api_fail(kq_ctx* ctx, int status, const char* msg) { return fail(ctx, status, "%s", msg); }
+}  // namespace kq
+
 extern "C" {
 
 int kq_abi_version(void) { return KQ_ABI_VERSION; }
@@ -242,6 +247,7 @@ const char* kq_status_string(int status) {
     case KQ_ERR_NCCL: return "collective error";
     case KQ_ERR_STATE: return "invalid state";
     case KQ_ERR_NOMEM: return "out of device memory";
+    case KQ_ERR_FORMAT: return "malformed or unreadable file";
     default: return "unknown status";
   }
 }

@@ -35,6 +35,7 @@ KQ_ERR_SHORT_BUFFER = 4
 KQ_ERR_NCCL = 5
 KQ_ERR_STATE = 6
 KQ_ERR_NOMEM = 7
+KQ_ERR_FORMAT = 8
 
 KQ_GGUF_Q4_K = 12
 KQ_GGUF_Q6_K = 14
@@ -63,6 +64,9 @@ EXPORTED_SYMBOLS = (
     "kq_tp_destroy", "kq_dec_rmsnorm", "kq_dec_rope_append", "kq_dec_attention_scratch", "kq_dec_attention",
     "kq_dec_swiglu", "kq_dec_add", "kq_dec_embed", "kq_dec_norm_linear", "kq_dec_swiglu_linear",
     "kq_dec_residual_linear", "kq_dec_rope_attention", "kq_dec_tp_partial_linear", "kq_dec_tp_reduce_linear",
+    "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_find_tensor", "kq_gguf_tensor_info",
+    "kq_gguf_read_tensor", "kq_gguf_upload", "kq_gguf_meta_count", "kq_gguf_find_meta", "kq_gguf_meta_info",
+    "kq_gguf_meta_int", "kq_gguf_meta_float", "kq_gguf_meta_string", "kq_gguf_meta_array",
 )
 
 
@@ -124,6 +128,24 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
             "kq_tp_linear_f32": ([P, P, I64, I64, P, I64, P, P, I], I),
             "kq_tp_allgather_f32": ([P, P, I64, I64, I64, I64, P, I64, I], I),
             "kq_tp_destroy": ([P], I),
+            "kq_gguf_open": ([ctypes.c_char_p, PP, ctypes.c_char_p, Z], I),
+            "kq_gguf_close": ([P], None),
+            "kq_gguf_tensor_count": ([P], I64),
+            "kq_gguf_find_tensor": ([P, ctypes.c_char_p], I64),
+            "kq_gguf_tensor_info": ([P, I64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(I), ctypes.POINTER(I),
+                                     ctypes.POINTER(I64), ctypes.POINTER(ctypes.c_uint64),
+                                     ctypes.POINTER(ctypes.c_uint64)], I),
+            "kq_gguf_read_tensor": ([P, I64, P, ctypes.c_uint64], I),
+            "kq_gguf_upload": ([P, P, I64, PP], I),
+            "kq_gguf_meta_count": ([P], I64),
+            "kq_gguf_find_meta": ([P, ctypes.c_char_p], I64),
+            "kq_gguf_meta_info": ([P, I64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(I), ctypes.POINTER(I),
+                                   ctypes.POINTER(ctypes.c_uint64)], I),
+            "kq_gguf_meta_int": ([P, I64, ctypes.POINTER(I64)], I),
+            "kq_gguf_meta_float": ([P, I64, ctypes.POINTER(ctypes.c_double)], I),
+            "kq_gguf_meta_string": ([P, I64, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p),
+                                     ctypes.POINTER(ctypes.c_uint64)], I),
+            "kq_gguf_meta_array": ([P, I64, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_uint64)], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(lib, name)
@@ -259,6 +281,17 @@ class Weight:
         dev_bytes = ctypes.c_int64()
         ctx.lib.kq_weight_info(h, None, None, None, ctypes.byref(dev_bytes))
         self.device_bytes = dev_bytes.value
+
+    @classmethod
+    def _adopt(cls, ctx: Context, handle: ctypes.c_void_p) -> "Weight":
+        """Wrap a kq_weight the library created (e.g. kq_gguf_upload)."""
+        w = cls.__new__(cls)
+        w.ctx = ctx
+        w.handle = handle
+        kt, n, k, dev_bytes = ctypes.c_int(), ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        ctx.lib.kq_weight_info(handle, ctypes.byref(kt), ctypes.byref(n), ctypes.byref(k), ctypes.byref(dev_bytes))
+        w.kq_type, w.out_features, w.in_features, w.device_bytes = kt.value, n.value, k.value, dev_bytes.value
+        return w
 
     def linear(self, x, m: int, y, bias=None, device_ptrs: bool = False, sync: bool = False) -> None:
         flags = (KQ_DEVICE_PTRS if device_ptrs else KQ_HOST_PTRS) | (KQ_SYNC if sync else 0)
@@ -461,3 +494,120 @@ class QuantizedLinear:
         self.ctx.set_stream(torch.cuda.current_stream(x.device).cuda_stream)
         self.weight.linear(x, m, out, bias, device_ptrs=True)
         return out
+
+
+# ---- GGUF files ---------------------------------------------------------------
+
+#: GGUF metadata value types
+GGUF_STRING, GGUF_ARRAY = 8, 9
+_GGUF_NUMPY = {0: np.uint8, 1: np.int8, 2: np.uint16, 3: np.int16, 4: np.uint32, 5: np.int32, 6: np.float32,
+               7: np.uint8, 10: np.uint64, 11: np.int64, 12: np.float64}
+
+
+class GgufTensor:
+    """One entry of a GGUF tensor directory.  ``shape`` is in row-major order
+    (the file's ne reversed: [..., rows, row length])."""
+
+    def __init__(self, index, name, ggml_type, dims, offset, nbytes):
+        self.index, self.name, self.ggml_type = index, name, ggml_type
+        self.dims, self.offset, self.nbytes = tuple(dims), offset, nbytes
+        self.shape = tuple(reversed(self.dims))
+
+    def __repr__(self):
+        return f"GgufTensor({self.name!r}, type={self.ggml_type}, shape={self.shape})"
+
+
+class GgufFile:
+    """A GGUF file opened through the library's reader (kq_gguf_*): the
+    tensor directory and metadata, the raw bytes of any tensor, and Q4_K /
+    Q6_K tensors uploaded as device-resident weights -- the path the
+    reference takes through pesti-gguf's extract_tensor_bytes_from_path
+    (gguf_weight_loader.rs:79-81) without its f32 copies."""
+
+    def __init__(self, path: str):
+        self.lib = load_library()
+        h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        rc = self.lib.kq_gguf_open(os.fsencode(path), ctypes.byref(h), err, len(err))
+        if rc != KQ_OK:
+            raise KqError(rc, f"kq_gguf_open: {err.value.decode(errors='replace')}")
+        self.handle = h
+        self.path = path
+        self.tensors = {}
+        for i in range(self.lib.kq_gguf_tensor_count(h)):
+            name, t, nd = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int()
+            dims, off, nb = (ctypes.c_int64 * 4)(), ctypes.c_uint64(), ctypes.c_uint64()
+            self._check(self.lib.kq_gguf_tensor_info(h, i, ctypes.byref(name), ctypes.byref(t), ctypes.byref(nd), dims,
+                                                     ctypes.byref(off), ctypes.byref(nb)), "kq_gguf_tensor_info")
+            nm = name.value.decode()
+            self.tensors[nm] = GgufTensor(i, nm, t.value, list(dims)[:nd.value], off.value, nb.value)
+        self.metadata = {}
+        for i in range(self.lib.kq_gguf_meta_count(h)):
+            key, vt, et, cnt = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int(), ctypes.c_uint64()
+            self._check(self.lib.kq_gguf_meta_info(h, i, ctypes.byref(key), ctypes.byref(vt), ctypes.byref(et),
+                                                   ctypes.byref(cnt)), "kq_gguf_meta_info")
+            self.metadata[key.value.decode()] = self._value(i, vt.value, et.value, cnt.value)
+
+    def _check(self, rc, what):
+        if rc != KQ_OK:
+            raise KqError(rc, f"{what} failed on {self.path}")
+
+    def _string(self, i, j):
+        p, n = ctypes.c_void_p(), ctypes.c_uint64()
+        self._check(self.lib.kq_gguf_meta_string(self.handle, i, j, ctypes.byref(p), ctypes.byref(n)),
+                    "kq_gguf_meta_string")
+        return ctypes.string_at(p, n.value).decode(errors="replace")
+
+    def _value(self, i, vt, et, count):
+        if vt == GGUF_STRING:
+            return self._string(i, 0)
+        if vt == GGUF_ARRAY:
+            if et == GGUF_STRING:
+                return [self._string(i, j) for j in range(count)]
+            if et == GGUF_ARRAY:
+                return None  # nested arrays are listed, not kept
+            p, eb = ctypes.c_void_p(), ctypes.c_uint64()
+            self._check(self.lib.kq_gguf_meta_array(self.handle, i, ctypes.byref(p), ctypes.byref(eb)),
+                        "kq_gguf_meta_array")
+            raw = ctypes.string_at(p, count * eb.value) if count else b""
+            arr = np.frombuffer(raw, dtype=_GGUF_NUMPY[et]).copy()
+            return arr.astype(bool) if et == 7 else arr
+        if vt in (6, 12):
+            v = ctypes.c_double()
+            self._check(self.lib.kq_gguf_meta_float(self.handle, i, ctypes.byref(v)), "kq_gguf_meta_float")
+            return v.value
+        v = ctypes.c_int64()
+        self._check(self.lib.kq_gguf_meta_int(self.handle, i, ctypes.byref(v)), "kq_gguf_meta_int")
+        return bool(v.value) if vt == 7 else v.value
+
+    def read(self, name: str) -> np.ndarray:
+        """The tensor's stored bytes (uint8)."""
+        t = self.tensors[name]
+        out = np.empty(t.nbytes, np.uint8)
+        self._check(self.lib.kq_gguf_read_tensor(self.handle, t.index, out.ctypes.data if t.nbytes else None,
+                                                 t.nbytes), "kq_gguf_read_tensor")
+        return out
+
+    def upload(self, ctx: Context, name: str) -> Weight:
+        """A 2-D Q4_K / Q6_K tensor as a device-resident Weight."""
+        t = self.tensors[name]
+        h = ctypes.c_void_p()
+        ctx.check(self.lib.kq_gguf_upload(ctx.handle, self.handle, t.index, ctypes.byref(h)), "kq_gguf_upload")
+        return Weight._adopt(ctx, h)
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.kq_gguf_close(self.handle)
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
