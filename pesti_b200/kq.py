@@ -455,6 +455,17 @@ class QuantizedLinear:
             raise KqError(KQ_ERR_UNSUPPORTED, f"Unsupported quantization type for QuantizedLinear: {gguf_dtype}")
         return cls(data, dtype, in_features, out_features, bias, **kw)
 
+    @classmethod
+    def from_gguf(cls, gguf_file, name: str, bias=None, **kw):
+        """The layer of a 2-D Q4_K / Q6_K tensor of a GGUF file (a path or a
+        GgufFile): its stored bytes, in_features = the row length."""
+        f = gguf_file if isinstance(gguf_file, GgufFile) else GgufFile(gguf_file)
+        t = f.tensors[name]
+        dtype = {KQ_GGUF_Q4_K: "Q4_K", KQ_GGUF_Q6_K: "Q6_K"}.get(t.ggml_type)
+        if dtype is None or len(t.dims) != 2:
+            raise KqError(KQ_ERR_UNSUPPORTED, f"{name}: not a 2-D Q4_K or Q6_K tensor (type {t.ggml_type})")
+        return cls(f.read(name), dtype, t.dims[0], t.dims[1], bias, **kw)
+
     # quantized_linear.rs:70-83
     def memory_bytes(self) -> int:
         return int(self.data.size + (0 if self.bias is None else self.bias.size * 4))

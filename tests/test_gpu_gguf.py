@@ -42,3 +42,10 @@ def test_upload_from_gguf_matches_direct_upload(gpu_ctx, tmp_path):
         with pytest.raises(kq.KqError) as e:
             f.upload(gpu_ctx, "norm.weight")
         assert e.value.status == kq.KQ_ERR_UNSUPPORTED
+        # the drop-in layer built from the same file
+        ql = kq.QuantizedLinear.from_gguf(f, "b.weight", ctx=gpu_ctx)
+        assert (ql.dtype, ql.in_features, ql.out_features) == ("Q6_K", 2048, 200)
+        x = synthetic.activations(2, 2048, seed=9)
+        y = ql.forward(x, 2).reshape(2, 200)
+        ref = oracle.gguf_linear(oracle.GGUF_Q6_K, q6, 200, 2048, x)
+        assert float(np.max(np.abs(y - ref)) / np.max(np.abs(ref))) <= TOL
