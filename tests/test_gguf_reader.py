@@ -113,3 +113,10 @@ def test_read_rejects_a_short_buffer(model_file):
         assert f.lib.kq_gguf_read_tensor(f.handle, 99, buf.ctypes.data, buf.size) == kq.KQ_ERR_INVALID_ARG
         assert f.lib.kq_gguf_find_tensor(f.handle, b"nope") == -1
         assert f.lib.kq_gguf_find_meta(f.handle, b"general.name") >= 0
+
+
+def test_layer_from_a_tensor_that_is_not_a_k_quant_is_refused(model_file):
+    path, _ = model_file
+    with pytest.raises(kq.KqError) as e:
+        kq.QuantizedLinear.from_gguf(str(path), "norm.weight")
+    assert e.value.status == kq.KQ_ERR_UNSUPPORTED
