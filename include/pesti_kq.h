@@ -143,8 +143,9 @@ int kq_linear_bf16(kq_ctx *ctx, const kq_weight *w, const void *x_bf16, int64_t 
  * GGUF weights, 1 <= m <= 4, device pointers only (flags must hold
  * KQ_DEVICE_PTRS).  Scratch comes from one fixed 256 KiB device array per
  * device (enough for in_features <= 16384); larger shapes are rejected with
- * KQ_ERR_UNSUPPORTED.  The array's address is looked up on the first call on
- * each device, so make that first call before any stream capture.  Calls on
+ * KQ_ERR_UNSUPPORTED.  The array's address is looked up (host side) on every
+ * call; the first lookup on a device may load the library's device code, so
+ * make the first call on each device before any stream capture.  Calls on
  * one device that are not ordered with each other race on the shared scratch. */
 int kq_linear_f32_static(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t m,
                          const float *bias, float *y, int flags);

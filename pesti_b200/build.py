@@ -8,6 +8,7 @@ torch extension.  The CUDA runtime is linked statically.
 """
 from __future__ import annotations
 
+import concurrent.futures
 import glob
 import hashlib
 import os
@@ -50,6 +51,24 @@ def _digest(files) -> str:
     return h.hexdigest()
 
 
+def _compile(nvcc, src, obj, deps_digest, verbose):
+    """Compile one source unless its object was built from the same source,
+    headers and flags (a digest beside the object)."""
+    stamp = obj + ".stamp"
+    want = _digest([src]) + deps_digest
+    if os.path.exists(obj) and os.path.exists(stamp):
+        with open(stamp) as fh:
+            if fh.read().strip() == want:
+                return obj
+    cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    with open(stamp, "w") as fh:
+        fh.write(want)
+    return obj
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     srcs, hdrs = _sources()
     digest = _digest(srcs + hdrs)
@@ -60,14 +79,15 @@ def build(force: bool = False, verbose: bool = False) -> str:
     nvcc = _nvcc()
     objdir = os.path.join(HERE, "_build")
     os.makedirs(objdir, exist_ok=True)
-    objs = []
-    for src in srcs:
-        obj = os.path.join(objdir, os.path.basename(src) + ".o")
-        cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
-        objs.append(obj)
+    if force:
+        for f in glob.glob(os.path.join(objdir, "*.stamp")):
+            os.remove(f)
+    deps = _digest(hdrs)
+    objs = [os.path.join(objdir, os.path.basename(src) + ".o") for src in srcs]
+    # one nvcc per translation unit, in parallel (each is single-threaded)
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(srcs), os.cpu_count() or 1))) as ex:
+        for f in [ex.submit(_compile, nvcc, s, o, deps, verbose) for s, o in zip(srcs, objs)]:
+            f.result()
     tmp = LIB + ".tmp"
     cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-lpthread", "-ldl", "-lrt"]
     if verbose:

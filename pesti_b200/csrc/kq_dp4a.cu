@@ -35,7 +35,6 @@
 
 #include <algorithm>
 #include <map>
-#include <mutex>
 #include <utility>
 
 namespace kq {
@@ -1275,24 +1274,18 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
 // ordering between them) race on its contents.
 static __device__ __align__(256) uint8_t g_dp4a_static_scratch[DP4A_STATIC_SCRATCH];
 
+// The array's device address, looked up with the device current.  The lookup
+// is repeated on every call (a host-side table read once the module is
+// loaded): a cached address would dangle after cudaDeviceReset or a torn-down
+// primary context, and the next kernel would write through it.  The first
+// lookup on a device may load this file's module, which is why the first
+// call on a device should come before any stream capture.
 cudaError_t dp4a_static_scratch(void** ptr) {
-  constexpr int MAX_DEVICES = 64;
-  static std::mutex mu;
-  static void* cached[MAX_DEVICES] = {};
   *ptr = nullptr;
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_dp4a_static_scratch);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= MAX_DEVICES) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lk(mu);
-  if (!cached[dev]) {
-    // once per device, with that device current
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_dp4a_static_scratch);
-    if (e != cudaSuccess) return e;
-    cached[dev] = p;
-  }
-  *ptr = cached[dev];
+  *ptr = p;
   return cudaSuccess;
 }
 

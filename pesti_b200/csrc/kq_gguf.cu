@@ -24,6 +24,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -261,6 +262,17 @@ int kq_gguf_open(const char* path, kq_gguf** out, char* err, size_t err_len) {
         set_err(err, err_len, "truncated or malformed tensor entry", t.name);
         break;
       }
+    }
+    if (!ok) break;
+    {
+      // a tensor name identifies one tensor: a directory that repeats a name is malformed
+      std::set<std::string> seen;
+      for (const auto& t : g->tensors)
+        if (!seen.insert(t.name).second) {
+          ok = false;
+          set_err(err, err_len, "tensor name appears twice in the directory", t.name);
+          break;
+        }
     }
     if (!ok) break;
     g->data_start = (r.pos() + g->alignment - 1) / g->alignment * g->alignment;

@@ -459,7 +459,10 @@ class QuantizedLinear:
     def from_gguf(cls, gguf_file, name: str, bias=None, **kw):
         """The layer of a 2-D Q4_K / Q6_K tensor of a GGUF file (a path or a
         GgufFile): its stored bytes, in_features = the row length."""
-        f = gguf_file if isinstance(gguf_file, GgufFile) else GgufFile(gguf_file)
+        if not isinstance(gguf_file, GgufFile):
+            with GgufFile(gguf_file) as f:  # opened here, so closed here
+                return cls.from_gguf(f, name, bias, **kw)
+        f = gguf_file
         t = f.tensors[name]
         dtype = {KQ_GGUF_Q4_K: "Q4_K", KQ_GGUF_Q6_K: "Q6_K"}.get(t.ggml_type)
         if dtype is None or len(t.dims) != 2:
@@ -550,14 +553,22 @@ class GgufFile:
             dims, off, nb = (ctypes.c_int64 * 4)(), ctypes.c_uint64(), ctypes.c_uint64()
             self._check(self.lib.kq_gguf_tensor_info(h, i, ctypes.byref(name), ctypes.byref(t), ctypes.byref(nd), dims,
                                                      ctypes.byref(off), ctypes.byref(nb)), "kq_gguf_tensor_info")
-            nm = name.value.decode()
+            nm = self._name(name.value, "tensor name")
             self.tensors[nm] = GgufTensor(i, nm, t.value, list(dims)[:nd.value], off.value, nb.value)
         self.metadata = {}
         for i in range(self.lib.kq_gguf_meta_count(h)):
             key, vt, et, cnt = ctypes.c_char_p(), ctypes.c_int(), ctypes.c_int(), ctypes.c_uint64()
             self._check(self.lib.kq_gguf_meta_info(h, i, ctypes.byref(key), ctypes.byref(vt), ctypes.byref(et),
                                                    ctypes.byref(cnt)), "kq_gguf_meta_info")
-            self.metadata[key.value.decode()] = self._value(i, vt.value, et.value, cnt.value)
+            self.metadata[self._name(key.value, "metadata key")] = self._value(i, vt.value, et.value, cnt.value)
+
+    def _name(self, raw: bytes, what: str) -> str:
+        # GGUF names are UTF-8; anything else is a malformed file, not a Python decode error
+        try:
+            return raw.decode("utf-8", errors="strict")
+        except UnicodeDecodeError as e:
+            self.close()
+            raise KqError(KQ_ERR_FORMAT, f"{self.path}: {what} is not UTF-8 ({e})") from None
 
     def _check(self, rc, what):
         if rc != KQ_OK:

@@ -120,3 +120,40 @@ def test_layer_from_a_tensor_that_is_not_a_k_quant_is_refused(model_file):
     with pytest.raises(kq.KqError) as e:
         kq.QuantizedLinear.from_gguf(str(path), "norm.weight")
     assert e.value.status == kq.KQ_ERR_UNSUPPORTED
+
+
+def test_repeated_or_non_utf8_tensor_names_are_format_errors(tmp_path):
+    # two tensors whose names differ in one byte; patching that byte makes the
+    # directory repeat a name, or hold a name that is not UTF-8
+    a = np.ones(4, np.float32)
+    path = tmp_path / "n.gguf"
+    _write(path, [("w.aa", a, None), ("w.ab", 2 * a, None)])
+    data = path.read_bytes()
+    at = data.index(b"w.ab")
+    bad = tmp_path / "dup.gguf"
+    bad.write_bytes(data[:at + 3] + b"a" + data[at + 4:])
+    with pytest.raises(kq.KqError) as e:
+        kq.GgufFile(str(bad))
+    assert e.value.status == kq.KQ_ERR_FORMAT and "twice" in str(e.value)
+    bad.write_bytes(data[:at + 3] + b"\xff" + data[at + 4:])
+    with pytest.raises(kq.KqError) as e:
+        kq.GgufFile(str(bad))
+    assert e.value.status == kq.KQ_ERR_FORMAT and "UTF-8" in str(e.value)
+    with kq.GgufFile(str(path)) as f:  # the unpatched file reads
+        assert list(f.tensors) == ["w.aa", "w.ab"]
+
+
+def test_layer_from_a_path_closes_the_file_it_opened(model_file, monkeypatch):
+    path, _ = model_file
+    closed = []
+    orig = kq.GgufFile.close
+
+    def spy(self):
+        if self.handle:
+            closed.append(self.path)
+        orig(self)
+
+    monkeypatch.setattr(kq.GgufFile, "close", spy)
+    with pytest.raises(kq.KqError):
+        kq.QuantizedLinear.from_gguf(str(path), "norm.weight")
+    assert closed == [str(path)]

@@ -66,3 +66,38 @@ def test_static_scratch_rejects_shapes_beyond_its_size(ctx):
     with pytest.raises(kq.KqError):
         w.linear_static(x, 5, y)  # more rows than the batched kernels serve
     w.free()
+
+
+def test_static_entry_allocates_nothing_on_a_fresh_context():
+    """A context that has only ever run kq_linear_f32_static grows no scratch:
+    the device's free memory is the same before and after its calls, and the
+    result matches the oracle.  The kernels run once first on a throwaway
+    context, so the driver's one-time loading of their code is not counted."""
+    import torch
+
+    import oracle
+    qtype, n, k, m = kq.KQ_GGUF_Q6_K, 257, 14336, 3
+    raw = synthetic.gguf_weight(qtype, n, k, seed=5)
+    x = torch.from_numpy(synthetic.activations(m, k, seed=6)).cuda()
+    warm = kq.Context(0)
+    ww = kq.Weight(warm, qtype, raw, n, k)
+    yw = torch.empty((m, n), device="cuda")
+    ww.linear_static(x, m, yw, sync=True)
+    ww.free()
+    warm.close()
+
+    c = kq.Context(0)
+    w = kq.Weight(c, qtype, raw, n, k)
+    ys = [torch.full((m, n), float("nan"), device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for y in ys:
+        w.linear_static(x, m, y, sync=True)
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    ref = oracle.gguf_linear(oracle.GGUF_Q6_K, raw, n, k, x.cpu().numpy())
+    for y in ys:
+        assert rel_err(y.cpu().numpy(), ref) <= TOL
+    assert torch.equal(ys[0], ys[1])
+    w.free()
+    c.close()
