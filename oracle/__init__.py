@@ -26,10 +26,16 @@ import threading
 
 import numpy as np
 
+GGUF_Q2_K = 10
+GGUF_Q3_K = 11
 GGUF_Q4_K = 12
+GGUF_Q5_K = 13
 GGUF_Q6_K = 14
 PESTI_Q4_K_LEGACY = 112
+PESTI_Q5_K_LEGACY = 113
 PESTI_Q6_K_LEGACY = 114
+#: bytes of one 256-weight GGUF superblock
+GGUF_BLOCK_BYTES = {GGUF_Q2_K: 84, GGUF_Q3_K: 110, GGUF_Q4_K: 144, GGUF_Q5_K: 176, GGUF_Q6_K: 210}
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 _LIB_PATH = os.path.join(_HERE, "liboracle.so")
@@ -60,8 +66,12 @@ def _load():
             lib.kqo_f16_to_f32.restype = ctypes.c_float
             lib.kqo_gguf_row_bytes.argtypes = [I, I64]
             lib.kqo_gguf_row_bytes.restype = I64
-            lib.kqo_dequant_q4_k.argtypes = [P, I64, P]
-            lib.kqo_dequant_q6_k.argtypes = [P, I64, P]
+            for name in ("kqo_dequant_q2_k", "kqo_dequant_q3_k", "kqo_dequant_q4_k", "kqo_dequant_q5_k",
+                         "kqo_dequant_q6_k"):
+                getattr(lib, name).argtypes = [P, I64, P]
+                getattr(lib, name).restype = I
+            lib.kqo_dequant_blocks.argtypes = [I, P, I64, P]
+            lib.kqo_dequant_blocks.restype = I
             lib.kqo_gguf_dequant_rows.argtypes = [I, P, I64, I64, I64, I64, P]
             lib.kqo_gguf_linear.argtypes = [I, P, I64, I64, P, I64, P, P, I]
             lib.kqo_legacy_row_bytes.argtypes = [I, I64]
@@ -111,13 +121,14 @@ def legacy_row_bytes(qtype: int, k: int) -> int:
 def dequant_blocks(qtype: int, raw) -> np.ndarray:
     """Decode whole GGUF superblocks (raw bytes, any shape) to f32 [nblocks*256]."""
     raw = _u8(raw)
-    bs = 144 if qtype == GGUF_Q4_K else 210
+    bs = GGUF_BLOCK_BYTES.get(qtype)
+    if bs is None:
+        raise OracleError(f"type {qtype} is not a GGUF K-quant")
     if raw.size % bs:
         raise OracleError("byte count is not a whole number of superblocks")
     nb = raw.size // bs
     out = np.empty(nb * 256, np.float32)
-    fn = _load().kqo_dequant_q4_k if qtype == GGUF_Q4_K else _load().kqo_dequant_q6_k
-    _check(fn(_ptr(raw), nb, _ptr(out)), "dequant")
+    _check(_load().kqo_dequant_blocks(qtype, _ptr(raw), nb, _ptr(out)), "dequant")
     return out
 
 
@@ -144,7 +155,7 @@ def gguf_linear(qtype: int, w, n: int, k: int, x, bias=None, nthreads: int | Non
 def legacy_dequant_tile(qtype: int, data, tile_size: int) -> np.ndarray:
     data = _u8(data)
     out = np.empty(tile_size, np.float32)
-    fn = (_load().kqo_legacy_dequant_q4_k_tile if qtype == PESTI_Q4_K_LEGACY
+    fn = (_load().kqo_legacy_dequant_q4_k_tile if qtype in (PESTI_Q4_K_LEGACY, PESTI_Q5_K_LEGACY)
           else _load().kqo_legacy_dequant_q6_k_tile)
     _check(fn(_ptr(data), data.size, tile_size, _ptr(out)), "legacy_dequant_tile")
     return out

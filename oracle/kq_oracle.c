@@ -46,10 +46,20 @@ static inline uint16_t rd16(const uint8_t *p) {
 /* ------------------------------------------------------------------------ */
 
 int64_t kqo_gguf_row_bytes(int type, int64_t k) {
-  if (k <= 0 || (k % 256) != 0) return -1;
-  if (type == KQO_GGUF_Q4_K) return (k / 256) * 144;
-  if (type == KQO_GGUF_Q6_K) return (k / 256) * 210;
-  return -1;
+  int64_t bs = kqo_gguf_block_bytes(type);
+  if (k <= 0 || (k % 256) != 0 || bs < 0) return -1;
+  return (k / 256) * bs;
+}
+
+int64_t kqo_gguf_block_bytes(int type) {
+  switch (type) {
+    case KQO_GGUF_Q2_K: return 84;
+    case KQO_GGUF_Q3_K: return 110;
+    case KQO_GGUF_Q4_K: return 144;
+    case KQO_GGUF_Q5_K: return 176;
+    case KQO_GGUF_Q6_K: return 210;
+    default: return -1;
+  }
 }
 
 /* Q4_K superblock: d f16 | dmin f16 | 12 bytes of packed 6-bit (scale,min)
@@ -121,6 +131,102 @@ int kqo_dequant_q6_k(const uint8_t *blocks, int64_t nblocks, float *out) {
   return KQO_OK;
 }
 
+/* Q5_K superblock: d f16 | dmin f16 | the 12 scale/min bytes of Q4_K | qh[32]
+ * | qs[128].  Element e: chunk c = e/64 of qs (low nibbles for e%64 < 32,
+ * high nibbles above), plus bit e/32 of qh[e%32] as bit 4; sub-block e/32
+ * takes (sc, m) as in Q4_K.  value = (d*sc)*q - (dmin*m), q in [0, 31]. */
+int kqo_dequant_q5_k(const uint8_t *blocks, int64_t nblocks, float *out) {
+  if (nblocks < 0 || (!blocks && nblocks) || (!out && nblocks)) return KQO_ERR_ARG;
+  for (int64_t b = 0; b < nblocks; ++b) {
+    const uint8_t *blk = blocks + b * 176;
+    float d = kqo_f16_to_f32(rd16(blk));
+    float dmin = kqo_f16_to_f32(rd16(blk + 2));
+    const uint8_t *sc = blk + 4;
+    const uint8_t *qh = blk + 16;
+    const uint8_t *qs = blk + 48;
+    float *o = out + b * 256;
+    for (int e = 0; e < 256; ++e) {
+      int j = e / 32, l = e % 32;
+      int s, m;
+      q4k_scale_min(sc, j, &s, &m);
+      uint8_t byte = qs[32 * (e / 64) + l];
+      int lo = (j & 1) ? (byte >> 4) : (byte & 0x0f);
+      int q = lo | (((qh[l] >> j) & 1) << 4);
+      float ds = d * (float)s, dm = dmin * (float)m;
+      o[e] = ds * (float)q - dm;
+    }
+  }
+  return KQO_OK;
+}
+
+/* Q2_K superblock: scales[16] (low nibble: scale, high nibble: min of each
+ * 16-weight sub-block) | qs[64] | d f16 | dmin f16.  Element e: bits
+ * 2*((e%128)/32) .. +1 of qs[32*(e/128) + e%32]; sub-block e/16.
+ * value = (d*sc)*q - (dmin*m), q in [0, 3]. */
+int kqo_dequant_q2_k(const uint8_t *blocks, int64_t nblocks, float *out) {
+  if (nblocks < 0 || (!blocks && nblocks) || (!out && nblocks)) return KQO_ERR_ARG;
+  for (int64_t b = 0; b < nblocks; ++b) {
+    const uint8_t *blk = blocks + b * 84;
+    const uint8_t *sc = blk;
+    const uint8_t *qs = blk + 16;
+    float d = kqo_f16_to_f32(rd16(blk + 80));
+    float dmin = kqo_f16_to_f32(rd16(blk + 82));
+    float *o = out + b * 256;
+    for (int e = 0; e < 256; ++e) {
+      int s = e / 16;
+      int q = (qs[32 * (e / 128) + e % 32] >> (2 * ((e % 128) / 32))) & 3;
+      float dl = d * (float)(sc[s] & 0x0f);
+      float ml = dmin * (float)(sc[s] >> 4);
+      o[e] = dl * (float)q - ml;
+    }
+  }
+  return KQO_OK;
+}
+
+/* Q3_K sub-block scale s (0..15): a 6-bit value whose low 4 bits are the low
+ * (s < 8) or high (s >= 8) nibble of byte s%8, whose high 2 bits are bits
+ * 2*(s/4) .. +1 of byte 8 + s%4; the signed scale is that value - 32. */
+static int q3k_scale(const uint8_t *sc, int s) {
+  int lo = s < 8 ? (sc[s] & 0x0f) : (sc[s - 8] >> 4);
+  int hi = (sc[8 + s % 4] >> (2 * (s / 4))) & 3;
+  return (lo | (hi << 4)) - 32;
+}
+
+/* Q3_K superblock: hmask[32] | qs[64] | scales[12] | d f16.  Element e: two
+ * low bits as in Q2_K (qs[32*(e/128) + e%32] at bit 2*((e%128)/32)); the
+ * third bit is bit e/32 of hmask[e%32], and a clear bit subtracts 4.
+ * value = (d*scale[e/16]) * q, q in [-4, 3]. */
+int kqo_dequant_q3_k(const uint8_t *blocks, int64_t nblocks, float *out) {
+  if (nblocks < 0 || (!blocks && nblocks) || (!out && nblocks)) return KQO_ERR_ARG;
+  for (int64_t b = 0; b < nblocks; ++b) {
+    const uint8_t *blk = blocks + b * 110;
+    const uint8_t *hm = blk;
+    const uint8_t *qs = blk + 32;
+    const uint8_t *sc = blk + 96;
+    float d = kqo_f16_to_f32(rd16(blk + 108));
+    float *o = out + b * 256;
+    for (int e = 0; e < 256; ++e) {
+      int lo = (qs[32 * (e / 128) + e % 32] >> (2 * ((e % 128) / 32))) & 3;
+      int hb = (hm[e % 32] >> (e / 32)) & 1;
+      int q = lo - (hb ? 0 : 4);
+      float ds = d * (float)q3k_scale(sc, e / 16);
+      o[e] = ds * (float)q;
+    }
+  }
+  return KQO_OK;
+}
+
+int kqo_dequant_blocks(int type, const uint8_t *blocks, int64_t nblocks, float *out) {
+  switch (type) {
+    case KQO_GGUF_Q2_K: return kqo_dequant_q2_k(blocks, nblocks, out);
+    case KQO_GGUF_Q3_K: return kqo_dequant_q3_k(blocks, nblocks, out);
+    case KQO_GGUF_Q4_K: return kqo_dequant_q4_k(blocks, nblocks, out);
+    case KQO_GGUF_Q5_K: return kqo_dequant_q5_k(blocks, nblocks, out);
+    case KQO_GGUF_Q6_K: return kqo_dequant_q6_k(blocks, nblocks, out);
+    default: return KQO_ERR_UNSUPPORTED;
+  }
+}
+
 int kqo_gguf_dequant_rows(int type, const uint8_t *w, int64_t n, int64_t k,
                           int64_t row0, int64_t nrows, float *out) {
   int64_t rb = kqo_gguf_row_bytes(type, k);
@@ -129,10 +235,7 @@ int kqo_gguf_dequant_rows(int type, const uint8_t *w, int64_t n, int64_t k,
   for (int64_t r = 0; r < nrows; ++r) {
     const uint8_t *row = w + (row0 + r) * rb;
     float *o = out + r * k;
-    if (type == KQO_GGUF_Q4_K)
-      kqo_dequant_q4_k(row, k / 256, o);
-    else
-      kqo_dequant_q6_k(row, k / 256, o);
+    kqo_dequant_blocks(type, row, k / 256, o);
   }
   return KQO_OK;
 }
@@ -203,6 +306,7 @@ int kqo_gguf_linear(int type, const uint8_t *w, int64_t n, int64_t k,
 int64_t kqo_legacy_row_bytes(int type, int64_t in_features) {
   if (in_features < 0) return -1;
   if (type == KQO_PESTI_Q4_K_LEGACY) return ((in_features + 15) / 16) * 28;
+  if (type == KQO_PESTI_Q5_K_LEGACY) return ((in_features + 15) / 16) * 36;
   if (type == KQO_PESTI_Q6_K_LEGACY) return ((in_features + 15) / 16) * 42;
   return -1;
 }
@@ -278,9 +382,13 @@ int kqo_legacy_dequant_q6_k_tile(const uint8_t *data, int64_t len,
   return KQO_OK;
 }
 
+/* QuantizedLinear's Q5_K rows are 36 bytes per 16 weights
+ * (quantized_linear.rs:91) but are decoded by the Q4_K tile routine
+ * (quantized_linear.rs:170-173): the 28-byte Q4_K blocks are read from the
+ * start of each 36-byte-per-16 row. */
 static int legacy_tile(int type, const uint8_t *p, int64_t len, int64_t k,
                        float *out) {
-  if (type == KQO_PESTI_Q4_K_LEGACY)
+  if (type == KQO_PESTI_Q4_K_LEGACY || type == KQO_PESTI_Q5_K_LEGACY)
     return kqo_legacy_dequant_q4_k_tile(p, len, k, out);
   return kqo_legacy_dequant_q6_k_tile(p, len, k, out);
 }

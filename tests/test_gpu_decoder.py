@@ -2,6 +2,7 @@
 (oracle/decoder_oracle.py) on small models: same weights, same KV-cache
 prefix, logits within tolerance; CUDA-graph replay; tensor parallelism on 2
 GPUs giving the same logits as one GPU."""
+import dataclasses
 import os
 import socket
 
@@ -87,6 +88,37 @@ def test_decode_step_replays_from_a_cuda_graph(gpu_ctx, batch):
     finally:
         gpu_ctx.set_stream(None)
     model.close()
+
+
+# The benchmark's model shapes: Qwen2.5-0.5B-shaped in full (24 layers, 896
+# activations on 1024-wide K-quant rows, vocab 151936, context 512) and
+# Llama-3-8B-shaped at full width and vocabulary with 2 of its 32 layers
+# (context 2048; the per-layer shapes are those of the 32-layer model).
+LLAMA3_8B_2L = dataclasses.replace(dec.LLAMA3_8B, name="llama-3-8b-shaped-2-layers", layers=2)
+
+
+@pytest.mark.parametrize("cfg,ctx_len,batch", [(dec.QWEN25_05B, 512, 1), (LLAMA3_8B_2L, 2048, 1),
+                                               (LLAMA3_8B_2L, 2048, 8)],
+                         ids=["qwen05b-full-b1", "llama8b-2layers-b1", "llama8b-2layers-b8"])
+def test_full_shape_decode_step_matches_the_restated_reference(gpu_ctx, cfg, ctx_len, batch):
+    import torch
+    from oracle import decoder_oracle
+    model = dec.Decoder(cfg, gpu_ctx, batch, ctx_len, max_new=2, seed=9, keep_raw=True)
+    ks, vs = _oracle_caches(model, cfg)
+    toks = [(1000 + 7919 * i) % cfg.vocab for i in range(batch)]
+    model.tokens.copy_(torch.tensor(toks, dtype=torch.int32))
+    model.step(ctx_len)
+    gpu_ctx.synchronize()
+    got = model.logits.cpu().numpy()
+    model.close()
+    ref = decoder_oracle.decode_step(cfg, model.raw, toks, ctx_len, ks, vs)
+    assert got.shape == (batch, cfg.vocab)
+    assert np.isfinite(got).all()
+    err = rel_err(got, ref)
+    assert err <= TOL, err
+    # every sequence of the batch, not only the one with the largest logit
+    for b in range(batch):
+        assert rel_err(got[b], ref[b]) <= TOL, (b, rel_err(got[b], ref[b]))
 
 
 def test_decoder_rejects_heads_that_do_not_split(gpu_ctx):

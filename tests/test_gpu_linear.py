@@ -201,6 +201,28 @@ def test_prefill_bf16_matches_f32_product(gpu_ctx, dt, n, k, m):
     assert rel_err(y, ref) <= PREFILL_TOL
 
 
+@pytest.mark.parametrize("n", [4096, 14336])
+def test_prefill_at_the_benchmark_shapes(gpu_ctx, n):
+    """The prefill GEMM at every (N, K, M) the benchmark quotes: Q4_K weights
+    of 4096x4096 and 14336x4096 against bf16 N(0, 1) activations at M = 512,
+    2048 and 4096 tokens, each against the f64 product of the oracle's
+    dequantized weight and the bf16-rounded activations (<= 2e-2 of max|y|)."""
+    kt, ot = GGUF["Q4_K"]
+    k = 4096
+    raw = synthetic.gguf_weight(kt, n, k, seed=n + 7)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    wf = oracle.gguf_dequant_rows(ot, raw, n, k).astype(np.float64)
+    for m in (512, 2048, 4096):
+        bits, xr = to_bf16_bits(synthetic.activations(m, k, seed=m + n))
+        y = np.empty((m, n), np.float32)
+        w.linear_bf16(bits, m, y)
+        ref = xr.astype(np.float64) @ wf.T
+        err = rel_err(y, ref)
+        assert err <= PREFILL_TOL, (n, m, err)
+        assert np.isfinite(y).all()
+    w.free()
+
+
 @pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
 @pytest.mark.parametrize("n,k,m", [(37, 300, 1), (37, 300, 5), (16, 16, 2), (5, 20, 1)])
 def test_legacy_linear_matches_reference_forward(gpu_ctx, dt, n, k, m):
