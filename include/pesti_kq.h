@@ -44,9 +44,15 @@ extern "C" {
 
 /* weight encodings (values follow GGML's type ids for the GGUF layouts) */
 enum kq_type {
+  KQ_GGUF_Q2_K = 10,          /* 84 B per 256 weights (CUDA-core kernels) */
+  KQ_GGUF_Q3_K = 11,          /* 110 B per 256 weights (CUDA-core)        */
   KQ_GGUF_Q4_K = 12,          /* 144 B per 256 weights                    */
+  KQ_GGUF_Q5_K = 13,          /* 176 B per 256 weights (CUDA-core)        */
   KQ_GGUF_Q6_K = 14,          /* 210 B per 256 weights                    */
   KQ_PESTI_Q4_K_LEGACY = 112, /* tile_dequant.rs 28 B per 16 weights      */
+  KQ_PESTI_Q5_K_LEGACY = 113, /* QuantizedLinear Q5_K rows: 36 B per 16   */
+                              /* weights read as 28 B Q4_K tiles          */
+                              /* (quantized_linear.rs:91,170-173)         */
   KQ_PESTI_Q6_K_LEGACY = 114, /* tile_dequant.rs 42 B per 16 weights      */
 };
 
@@ -129,7 +135,9 @@ int kq_weight_info(const kq_weight *w, int *kq_type, int64_t *out_features,
 /* ---- compute ------------------------------------------------------------ */
 /* y[m][out] = x[m][in] . W[out][in] (+ bias[out]), f32 in and out.
  * QuantizedLinear::forward (quantized_linear.rs:101-143) / Linear::forward
- * (transformer/linear.rs:108-150).  bias may be NULL. */
+ * (transformer/linear.rs:108-150).  bias may be NULL.  Every kq_type is
+ * served; GGUF Q2_K / Q3_K / Q5_K run on one CUDA-core kernel family whatever
+ * kq_ctx_set_path selects. */
 int kq_linear_f32(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t m,
                   const float *bias, float *y, int flags);
 /* Prefill form: x is bf16 [m][in] (raw 16-bit values), y f32 [m][out].  The
@@ -204,8 +212,9 @@ int kq_gguf_tensor_info(const kq_gguf *f, int64_t i, const char **name, int *ggm
                         int64_t *dims, uint64_t *file_offset, uint64_t *nbytes);
 /* The tensor's bytes as stored into dst (dst_bytes >= nbytes). */
 int kq_gguf_read_tensor(const kq_gguf *f, int64_t i, void *dst, uint64_t dst_bytes);
-/* A 2-D Q4_K / Q6_K tensor [ne1 rows][ne0] as a device-resident weight
- * (out_features = ne[1], in_features = ne[0]), through kq_weight_upload. */
+/* A 2-D Q2_K / Q3_K / Q4_K / Q5_K / Q6_K tensor [ne1 rows][ne0] as a
+ * device-resident weight (out_features = ne[1], in_features = ne[0]),
+ * through kq_weight_upload. */
 int kq_gguf_upload(kq_ctx *ctx, const kq_gguf *f, int64_t i, kq_weight **out);
 /* Metadata: value_type / elem_type are GGUF's codes (0 u8 .. 12 f64, 8
  * string, 9 array; elem_type -1 unless an array); count: 1 for a scalar or a

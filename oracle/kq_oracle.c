@@ -419,6 +419,22 @@ typedef struct {
   int64_t o0, o1; /* output rows */
 } fwd_job;
 
+typedef struct {
+  int type;
+  const uint8_t *data;
+  int64_t len, k, o0, o1;
+  float *w;
+  int rc;
+} deq_job;
+
+static void *legacy_deq_worker(void *arg) {
+  deq_job *j = (deq_job *)arg;
+  j->rc = j->o1 > j->o0 ? kqo_legacy_dequant_rows(j->type, j->data, j->len, j->k, j->o0, j->o1 - j->o0,
+                                                  j->w + j->o0 * j->k)
+                        : KQO_OK;
+  return NULL;
+}
+
 static void *legacy_fwd_worker(void *arg) {
   fwd_job *j = (fwd_job *)arg;
   for (int64_t b = j->b0; b < j->b1; ++b) {
@@ -444,14 +460,33 @@ int kqo_legacy_forward(int type, const uint8_t *data, int64_t len,
   /* dequantize the full weight first, as quantized_linear.rs:108 does */
   float *w = (float *)malloc(sizeof(float) * (size_t)(n * k > 0 ? n * k : 1));
   if (!w) return KQO_ERR_ARG;
-  int rc = kqo_legacy_dequant_rows(type, data, len, k, 0, n, w);
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > 256) nthreads = 256;
+  pthread_t th[256];
+  int rc;
+  if (threads_over_batch) {
+    rc = kqo_legacy_dequant_rows(type, data, len, k, 0, n, w);
+  } else {
+    /* the all-cores variant also spreads the dequantization over the threads,
+     * each taking the block of output rows it later multiplies */
+    int nd = n < nthreads ? (int)(n > 0 ? n : 1) : nthreads;
+    deq_job dj[256];
+    for (int t = 0; t < nd; ++t) {
+      deq_job j = {type, data, len, k, n * t / nd, n * (t + 1) / nd, w, 0};
+      dj[t] = j;
+    }
+    for (int t = 1; t < nd; ++t) pthread_create(&th[t], NULL, legacy_deq_worker, &dj[t]);
+    legacy_deq_worker(&dj[0]);
+    rc = dj[0].rc;
+    for (int t = 1; t < nd; ++t) {
+      pthread_join(th[t], NULL);
+      if (dj[t].rc && !rc) rc = dj[t].rc;
+    }
+  }
   if (rc) {
     free(w);
     return rc; /* the reference prints and returns the zeroed output */
   }
-  if (nthreads < 1) nthreads = 1;
-  if (nthreads > 256) nthreads = 256;
-  pthread_t th[256];
   fwd_job jobs[256];
   int nt;
   if (threads_over_batch) {

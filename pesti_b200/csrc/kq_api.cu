@@ -142,16 +142,21 @@ int ensure(kq_ctx* ctx, void** buf, size_t* have, size_t need, const char* what,
   return KQ_OK;
 }
 
+// GGUF Q4_K / Q6_K: the types every kernel family serves
 bool is_gguf(int t) { return t == kq::GGUF_Q4_K || t == kq::GGUF_Q6_K; }
-bool is_legacy(int t) { return t == kq::LEGACY_Q4_K || t == kq::LEGACY_Q6_K; }
+// GGUF Q2_K / Q3_K / Q5_K: the CUDA-core kernels of kq_kx.cu
+bool is_kx(int t) { return kq::kx_type(t); }
+bool is_legacy(int t) { return t == kq::LEGACY_Q4_K || t == kq::LEGACY_Q5_K || t == kq::LEGACY_Q6_K; }
 
 int64_t legacy_row_bytes(int t, int64_t k) {
-  return t == kq::LEGACY_Q4_K ? ((k + 15) / 16) * 28 : ((k + 15) / 16) * 42;
+  if (t == kq::LEGACY_Q4_K) return ((k + 15) / 16) * 28;
+  if (t == kq::LEGACY_Q5_K) return ((k + 15) / 16) * 36;  // quantized_linear.rs:91
+  return ((k + 15) / 16) * 42;
 }
 
 // Bytes the legacy tile decoder reads from the last row (tile_dequant.rs:224-227, 334-335).
 int64_t legacy_tile_bytes(int t, int64_t k) {
-  if (t == kq::LEGACY_Q4_K) return (k / 16) * 28 + ((k % 16) ? 4 : 0);
+  if (t == kq::LEGACY_Q4_K || t == kq::LEGACY_Q5_K) return (k / 16) * 28 + ((k % 16) ? 4 : 0);
   return ((k + 15) / 16) * 42;
 }
 
@@ -271,6 +276,7 @@ int kq_ctx_create(int device, kq_ctx** out) {
   if (e == cudaSuccess) e = kq::dp4a_init_device();
   if (e == cudaSuccess) e = kq::imma_init_device();
   if (e == cudaSuccess) e = kq::dec_init_device();
+  if (e == cudaSuccess) e = kq::kx_init_device();
   if (e != cudaSuccess) {
     cudaGetLastError();
     return KQ_ERR_CUDA;
@@ -364,7 +370,7 @@ int kq_ctx_synchronize(kq_ctx* ctx) {
 int kq_ctx_reserve(kq_ctx* ctx, const kq_weight* w, int64_t m) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!w || m < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "bad reserve arguments");
-  if (!is_gguf(w->dw.type) || m == 0 || w->dw.k == 0) return KQ_OK;
+  if (!is_gguf(w->dw.type) || m == 0 || w->dw.k == 0) return KQ_OK;  // the other types need no scratch
   DeviceGuard g(ctx->device);
   // every call with 1..m rows may pick a different kernel family: cover them all
   size_t ws = kq::tc_workspace_bytes_bf16(m, w->dw.k), ctr = 0;
@@ -435,6 +441,11 @@ int kq_row_bytes(int type, int64_t in_features, int64_t* out) {
     *out = (in_features / kq::QK) * (type == kq::GGUF_Q4_K ? kq::Q4K_BYTES : kq::Q6K_BYTES);
     return KQ_OK;
   }
+  if (is_kx(type)) {
+    if (in_features % kq::QK) return KQ_ERR_UNSUPPORTED;
+    *out = (in_features / kq::QK) * kq::kx_block_bytes(type);
+    return KQ_OK;
+  }
   if (is_legacy(type)) {
     *out = legacy_row_bytes(type, in_features);
     return KQ_OK;
@@ -448,8 +459,9 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
   if (!out) return fail(ctx, KQ_ERR_INVALID_ARG, "out is null");
   *out = nullptr;
   if (n < 0 || k < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative shape %lld x %lld", (long long)n, (long long)k);
-  if (!is_gguf(type) && !is_legacy(type)) return fail(ctx, KQ_ERR_UNSUPPORTED, "unsupported kq_type %d", type);
-  if (is_gguf(type) && k % kq::QK)
+  if (!is_gguf(type) && !is_kx(type) && !is_legacy(type))
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "unsupported kq_type %d", type);
+  if ((is_gguf(type) || is_kx(type)) && k % kq::QK)
     return fail(ctx, KQ_ERR_UNSUPPORTED, "GGUF K-quant rows hold whole 256-weight superblocks; in_features=%lld",
                 (long long)k);
   if (n > (int64_t)1 << 31 || k > (int64_t)1 << 28)
@@ -457,6 +469,8 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
   int64_t need;
   if (is_gguf(type)) {
     need = n * (k / kq::QK) * (type == kq::GGUF_Q4_K ? kq::Q4K_BYTES : kq::Q6K_BYTES);
+  } else if (is_kx(type)) {
+    need = n * (k / kq::QK) * kq::kx_block_bytes(type);
   } else {
     need = (n == 0 || k == 0) ? 0 : (n - 1) * legacy_row_bytes(type, k) + legacy_tile_bytes(type, k);
   }
@@ -472,7 +486,7 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
   w->dw.type = type;
   w->dw.n = n;
   w->dw.k = k;
-  w->dw.sb = is_gguf(type) ? k / kq::QK : 0;
+  w->dw.sb = (is_gguf(type) || is_kx(type)) ? k / kq::QK : 0;
   w->dw.row_bytes = is_legacy(type) ? legacy_row_bytes(type, k) : 0;
   cudaError_t e = cudaSuccess;
   const size_t pad = 64;  // vector loads never read past the allocation
@@ -496,6 +510,19 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
     }
     if (raw) cudaFree(raw);
     w->device_bytes = nsb * (kq::Q6K_BODY + 2);
+    w->dw.len = w->device_bytes;
+  } else if (is_kx(type)) {
+    // rows at a 16-byte stride (the row's bytes rounded up), one 2-D copy
+    const int64_t src_rb = w->dw.sb * kq::kx_block_bytes(type);
+    const int64_t dst_rb = (src_rb + 15) & ~int64_t(15);
+    w->dw.row_bytes = dst_rb;
+    e = cudaMalloc(&w->q_alloc, (size_t)(n * dst_rb) + pad);
+    if (e == cudaSuccess) e = cudaMemsetAsync(w->q_alloc, 0, (size_t)(n * dst_rb) + pad, ctx->stream);
+    if (e == cudaSuccess && need)
+      e = cudaMemcpy2DAsync(w->q_alloc, (size_t)dst_rb, bytes, (size_t)src_rb, (size_t)src_rb, (size_t)n,
+                            cudaMemcpyDefault, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    w->device_bytes = n * dst_rb;
     w->dw.len = w->device_bytes;
   } else {
     e = cudaMalloc(&w->q_alloc, (size_t)need + pad);
@@ -555,7 +582,7 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
   if (m < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative m");
   if (m > (int64_t)1 << 24) return fail(ctx, KQ_ERR_UNSUPPORTED, "m = %lld is too large", (long long)m);
   if (bf16 && !is_gguf(w->dw.type))
-    return fail(ctx, KQ_ERR_UNSUPPORTED, "bf16 activations need a GGUF Q4_K / Q6_K weight");
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "bf16 activations need a GGUF Q4_K / Q6_K weight (type %d)", w->dw.type);
   const int64_t n = w->dw.n, k = w->dw.k;
   if (m == 0 || n == 0) return KQ_OK;
   if (!y || (k > 0 && !x)) return fail(ctx, KQ_ERR_INVALID_ARG, "x or y is null");
@@ -604,6 +631,8 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
   } else if (bf16) {
     if ((rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes_bf16(m, k), "workspace"))) return rc;
     e = kq::launch_tc_bf16(w->dw, xd, m, bd, yd, ctx->ws, ctx->dev_err, s, &launches, ctx->next_bracket());
+  } else if (is_kx(w->dw.type)) {
+    e = kq::launch_gemv_kx(w->dw, static_cast<const float*>(xd), m, bd, yd, s, &launches, ctx->next_bracket());
   } else if (is_gguf(w->dw.type)) {
     if ((rc = prepare_f32(ctx, w->dw, m))) return rc;
     const int fam = f32_family(ctx, w->dw, m);
@@ -1083,7 +1112,8 @@ int kq_dequant_f32(kq_ctx* ctx, const kq_weight* w, int64_t row0, int64_t nrows,
     if ((rc = ensure(ctx, &ctx->ybuf, &ctx->ybuf_bytes, (size_t)count * 4, "output staging"))) return rc;
     od = static_cast<float*>(ctx->ybuf);
   }
-  cudaError_t e = kq::launch_dequant_f32(w->dw, row0, nrows, od, ctx->stream);
+  cudaError_t e = is_kx(w->dw.type) ? kq::launch_dequant_kx(w->dw, row0, nrows, od, ctx->stream)
+                                    : kq::launch_dequant_f32(w->dw, row0, nrows, od, ctx->stream);
   if (e != cudaSuccess) return cuda_fail(ctx, e, "dequant launch");
   ++ctx->launches;
   if (!dev) {

@@ -95,6 +95,7 @@ __global__ void dequant_kernel(DevWeight w, int64_t row0, int64_t nrows, float* 
         break;
       }
       case LEGACY_Q4_K:
+      case LEGACY_Q5_K:  // quantized_linear.rs:170-173: Q5_K rows go through the Q4_K tile decoder
         v = legacy_q4k_value(w.q + r * w.row_bytes, w.k, i);
         break;
       default:
@@ -142,7 +143,7 @@ __global__ void __launch_bounds__(256) legacy_gemv_kernel(DevWeight w, const flo
 #pragma unroll
     for (int e = 0; e < 16; ++e) {
       const int64_t i = b * 16 + e;
-      v[e] = (i < w.k) ? (w.type == LEGACY_Q4_K ? legacy_q4k_value(rp, w.k, i) : legacy_q6k_value(rp, i))
+      v[e] = (i < w.k) ? (w.type == LEGACY_Q6_K ? legacy_q6k_value(rp, i) : legacy_q4k_value(rp, w.k, i))
                        : 0.f;
     }
 #pragma unroll

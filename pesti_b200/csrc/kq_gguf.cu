@@ -354,9 +354,11 @@ int kq_gguf_upload(kq_ctx* ctx, const kq_gguf* f, int64_t i, kq_weight** out) {
     return kq::api_fail(ctx, KQ_ERR_INVALID_ARG, "kq_gguf_upload: null argument or tensor index out of range");
   *out = nullptr;
   const Tensor& t = f->tensors[(size_t)i];
-  if ((t.type != KQ_GGUF_Q4_K && t.type != KQ_GGUF_Q6_K) || t.n_dims != 2)
+  if ((t.type != KQ_GGUF_Q2_K && t.type != KQ_GGUF_Q3_K && t.type != KQ_GGUF_Q4_K && t.type != KQ_GGUF_Q5_K &&
+       t.type != KQ_GGUF_Q6_K) ||
+      t.n_dims != 2)
     return kq::api_fail(ctx, KQ_ERR_UNSUPPORTED,
-                        ("kq_gguf_upload: " + t.name + " is not a 2-D Q4_K or Q6_K tensor").c_str());
+                        ("kq_gguf_upload: " + t.name + " is not a 2-D Q2_K / Q3_K / Q4_K / Q5_K / Q6_K tensor").c_str());
   void* host = malloc(t.nbytes ? (size_t)t.nbytes : 1);
   if (!host) return kq::api_fail(ctx, KQ_ERR_NOMEM, "kq_gguf_upload: no host memory for the tensor bytes");
   int rc = kq_gguf_read_tensor(f, i, host, t.nbytes);

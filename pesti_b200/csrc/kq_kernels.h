@@ -14,9 +14,13 @@ constexpr int Q6K_BYTES = 210;  // GGUF Q6_K superblock
 constexpr int Q6K_BODY = 208;   // device Q6_K body: ql(128) | qh(64) | scales(16)
 
 enum QType : int {
+  GGUF_Q2_K = 10,
+  GGUF_Q3_K = 11,
   GGUF_Q4_K = 12,
+  GGUF_Q5_K = 13,
   GGUF_Q6_K = 14,
   LEGACY_Q4_K = 112,
+  LEGACY_Q5_K = 113,  // QuantizedLinear's Q5_K: 36 B per 16 weights, decoded as Q4_K tiles
   LEGACY_Q6_K = 114,
 };
 
@@ -26,6 +30,8 @@ enum QType : int {
 //  GGUF_Q6_K: q = bodies [n][sb][208] (ql|qh|scales), d = f16 [n][d_ld]
 //             (row-major, d_ld = sb rounded up to 8 so every row's d is a
 //             whole number of 16-byte units and a block of rows is one run).
+//  GGUF_Q2_K / Q3_K / Q5_K: q = raw superblocks, rows row_bytes apart (the
+//             row's bytes rounded up to a multiple of 16).
 //  LEGACY_*:  q = raw bytes as uploaded (row stride = legacy row bytes), len.
 // wmap / dmap: TMA descriptors of q (128 rows x one superblock per box) and d.
 struct DevWeight {
@@ -35,7 +41,7 @@ struct DevWeight {
   const uint16_t* d;
   int64_t d_ld;
   int64_t len;        // uploaded byte count (legacy) / device bytes
-  int64_t row_bytes;  // legacy row stride
+  int64_t row_bytes;  // row stride: legacy types and GGUF Q2_K / Q3_K / Q5_K
   CUtensorMap wmap, dmap;
 };
 
@@ -99,6 +105,16 @@ cudaError_t launch_dequant_f32(const DevWeight& w, int64_t row0, int64_t nrows, 
 // d [n][d_ld] (padding entries are left as they are).
 cudaError_t launch_q6k_relayout(const uint8_t* raw, int64_t n, int64_t sb, uint8_t* body, uint16_t* d,
                                 cudaStream_t s);
+
+// ---- GGUF Q2_K / Q3_K / Q5_K: kq_kx.cu ----
+bool kx_type(int type);
+int64_t kx_block_bytes(int type);  // bytes of one 256-weight superblock (0: not one of these types)
+cudaError_t kx_init_device();
+// y = x . W^T (+bias), f32 x and y, any m (tiles of up to 8 tokens per launch).
+cudaError_t launch_gemv_kx(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y, cudaStream_t s,
+                           int* launches, Bracket br = Bracket());
+// Bit-exact dequantization of rows [row0, row0 + nrows) to f32 [nrows][k].
+cudaError_t launch_dequant_kx(const DevWeight& w, int64_t row0, int64_t nrows, float* out, cudaStream_t s);
 
 // ---- integer tensor-core batched decode, GGUF Q4_K: kq_imma.cu ----
 cudaError_t imma_init_device();

@@ -37,9 +37,13 @@ KQ_ERR_STATE = 6
 KQ_ERR_NOMEM = 7
 KQ_ERR_FORMAT = 8
 
+KQ_GGUF_Q2_K = 10
+KQ_GGUF_Q3_K = 11
 KQ_GGUF_Q4_K = 12
+KQ_GGUF_Q5_K = 13
 KQ_GGUF_Q6_K = 14
 KQ_PESTI_Q4_K_LEGACY = 112
+KQ_PESTI_Q5_K_LEGACY = 113
 KQ_PESTI_Q6_K_LEGACY = 114
 
 KQ_HOST_PTRS = 0
@@ -393,20 +397,34 @@ class TensorParallel:
 
 
 class QuantDtype:
-    """pesti-runner/src/tile_dequant.rs:394-402 (the K-quant members)."""
+    """pesti-runner/src/tile_dequant.rs:394-402 (the K-quant members: Q4_K,
+    Q5_K, Q6_K), plus the GGUF Q2_K and Q3_K superblock types, which the
+    reference's loader decodes (gguf_weight_loader.rs:334-477) but its
+    QuantizedLinear does not hold."""
+    Q2_K = "Q2_K"
+    Q3_K = "Q3_K"
     Q4_K = "Q4_K"
+    Q5_K = "Q5_K"
     Q6_K = "Q6_K"
 
 
+# quantized_linear.rs:51-57 (the K-quant names), plus the Q2_K / Q3_K names
 _DTYPE_NAMES = {
     "Q4_K": QuantDtype.Q4_K, "Q4_K_M": QuantDtype.Q4_K, "Q4_K_S": QuantDtype.Q4_K,
+    "Q5_K": QuantDtype.Q5_K, "Q5_K_M": QuantDtype.Q5_K, "Q5_K_S": QuantDtype.Q5_K,
     "Q6_K": QuantDtype.Q6_K, "Q6_K_S": QuantDtype.Q6_K,
+    "Q2_K": QuantDtype.Q2_K, "Q2_K_S": QuantDtype.Q2_K,
+    "Q3_K": QuantDtype.Q3_K, "Q3_K_S": QuantDtype.Q3_K, "Q3_K_M": QuantDtype.Q3_K, "Q3_K_L": QuantDtype.Q3_K,
 }
 
 _LAYOUTS = {
+    ("gguf", QuantDtype.Q2_K): KQ_GGUF_Q2_K,
+    ("gguf", QuantDtype.Q3_K): KQ_GGUF_Q3_K,
     ("gguf", QuantDtype.Q4_K): KQ_GGUF_Q4_K,
+    ("gguf", QuantDtype.Q5_K): KQ_GGUF_Q5_K,
     ("gguf", QuantDtype.Q6_K): KQ_GGUF_Q6_K,
     ("pesti-legacy", QuantDtype.Q4_K): KQ_PESTI_Q4_K_LEGACY,
+    ("pesti-legacy", QuantDtype.Q5_K): KQ_PESTI_Q5_K_LEGACY,
     ("pesti-legacy", QuantDtype.Q6_K): KQ_PESTI_Q6_K_LEGACY,
 }
 
@@ -464,9 +482,10 @@ class QuantizedLinear:
                 return cls.from_gguf(f, name, bias, **kw)
         f = gguf_file
         t = f.tensors[name]
-        dtype = {KQ_GGUF_Q4_K: "Q4_K", KQ_GGUF_Q6_K: "Q6_K"}.get(t.ggml_type)
+        dtype = {KQ_GGUF_Q2_K: "Q2_K", KQ_GGUF_Q3_K: "Q3_K", KQ_GGUF_Q4_K: "Q4_K", KQ_GGUF_Q5_K: "Q5_K",
+                 KQ_GGUF_Q6_K: "Q6_K"}.get(t.ggml_type)
         if dtype is None or len(t.dims) != 2:
-            raise KqError(KQ_ERR_UNSUPPORTED, f"{name}: not a 2-D Q4_K or Q6_K tensor (type {t.ggml_type})")
+            raise KqError(KQ_ERR_UNSUPPORTED, f"{name}: not a 2-D K-quant tensor (type {t.ggml_type})")
         return cls(f.read(name), dtype, t.dims[0], t.dims[1], bias, **kw)
 
     # quantized_linear.rs:70-83

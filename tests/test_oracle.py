@@ -17,6 +17,8 @@ import oracle
 from pesti_b200 import synthetic
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "gguf_kquant_golden.npz")
+GOLDEN_MORE = os.path.join(os.path.dirname(__file__), "golden", "gguf_kquant_more_golden.npz")
+MORE = [("q2k", oracle.GGUF_Q2_K), ("q3k", oracle.GGUF_Q3_K), ("q5k", oracle.GGUF_Q5_K)]
 
 
 def same_bits(a, b):
@@ -33,6 +35,11 @@ def f16(v):
 @pytest.fixture(scope="module")
 def golden():
     return np.load(GOLDEN)
+
+
+@pytest.fixture(scope="module")
+def golden_more():
+    return np.load(GOLDEN_MORE)
 
 
 # ---- O1: GGUF superblocks ------------------------------------------------
@@ -72,6 +79,41 @@ def test_gguf_linear_matches_f64_fixture(golden, tag, qtype):
     assert err < 1e-5
 
 
+@pytest.mark.parametrize("tag,qtype", MORE)
+def test_other_k_quants_match_golden(golden_more, tag, qtype):
+    raw = golden_more[f"{tag}_raw"]
+    want = golden_more[f"{tag}_bits"].view(np.float32).reshape(-1)
+    assert same_bits(oracle.dequant_blocks(qtype, raw), want)
+    vals = want
+    assert np.isnan(vals).any() and np.isinf(vals).any() and (vals == 0).any()
+    w, x, y64 = golden_more[f"lin_{tag}_w"], golden_more[f"lin_{tag}_x"], golden_more[f"lin_{tag}_y64"]
+    y = oracle.gguf_linear(qtype, w, y64.shape[1], x.shape[1], x)
+    assert np.max(np.abs(y - y64)) / np.max(np.abs(y64)) < 1e-5
+
+
+@pytest.mark.parametrize("tag,qtype", MORE)
+def test_other_k_quants_match_gguf_py(tag, qtype):
+    gguf = pytest.importorskip("gguf")
+    qt = {oracle.GGUF_Q2_K: gguf.GGMLQuantizationType.Q2_K, oracle.GGUF_Q3_K: gguf.GGMLQuantizationType.Q3_K,
+          oracle.GGUF_Q5_K: gguf.GGMLQuantizationType.Q5_K}[qtype]
+    rng = np.random.default_rng(98)
+    raw = rng.integers(0, 256, (20000, oracle.GGUF_BLOCK_BYTES[qtype]), dtype=np.uint8)
+    with np.errstate(all="ignore"):
+        want = gguf.quants.dequantize(raw, qt).reshape(-1).astype(np.float32)
+    assert same_bits(oracle.dequant_blocks(qtype, raw), want)
+
+
+def test_legacy_q5k_rows_decode_as_q4k_tiles():
+    # quantized_linear.rs:91,170-173: 36 bytes per 16 weights per row, read by the Q4_K tile routine
+    n, k = 5, 300
+    data = synthetic.legacy_weight(oracle.PESTI_Q5_K_LEGACY, n, k, seed=3)
+    assert data.shape == (n, ((k + 15) // 16) * 36) == (n, oracle.legacy_row_bytes(oracle.PESTI_Q5_K_LEGACY, k))
+    for r in range(n):
+        want = oracle.legacy_dequant_tile(oracle.PESTI_Q4_K_LEGACY, data[r], k)
+        got = oracle.legacy_dequant_rows(oracle.PESTI_Q5_K_LEGACY, data, k, r, 1)[0]
+        assert same_bits(got, want)
+
+
 def test_gguf_linear_threading_is_bitwise_stable():
     w = synthetic.q4_k_weight(37, 512, seed=3)
     x = synthetic.activations(2, 512, seed=4)
@@ -85,6 +127,9 @@ def test_gguf_row_bytes():
     assert oracle.gguf_row_bytes(oracle.GGUF_Q4_K, 4096) == 16 * 144
     assert oracle.gguf_row_bytes(oracle.GGUF_Q6_K, 14336) == 56 * 210
     assert oracle.gguf_row_bytes(oracle.GGUF_Q4_K, 300) == -1
+    assert oracle.gguf_row_bytes(oracle.GGUF_Q2_K, 512) == 2 * 84
+    assert oracle.gguf_row_bytes(oracle.GGUF_Q3_K, 512) == 2 * 110
+    assert oracle.gguf_row_bytes(oracle.GGUF_Q5_K, 512) == 2 * 176
 
 
 def test_f16_conversion_exhaustive():
