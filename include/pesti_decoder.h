@@ -94,6 +94,53 @@ int kq_dec_residual_linear(kq_ctx *ctx, const kq_weight *w, const float *x, floa
 int kq_dec_tp_partial_linear(kq_tp *tp, const kq_weight *w, const float *x, int act, int flags);
 int kq_dec_tp_reduce_linear(kq_tp *tp, const kq_weight *w, const float *h_in, float *h_out, const float *norm_w,
                             int64_t dim, float eps, int act, float *y, int flags);
+/* ---- the batch-1 decode step as one persistent kernel ----------------------
+ * A step program lists the step's linears and attention in order; one
+ * cooperative launch of one CTA per SM runs them all (kq_step_run), a
+ * producer warp per SM streaming every stage's weight rows and KV tile ahead
+ * of the compute warps, grid barriers where a stage reads a vector other CTAs
+ * wrote, and exchange words for the residual updates.  It replaces the
+ * layer's separate kernels (the forward pass of transformer/layer.rs:344-372
+ * per layer, model.rs:1025-1061 over the layers) with one launch per token.
+ * Weights: GGUF Q4_K / Q6_K (in_features <= 30720).  Pointers are device
+ * pointers; vectors are batch 1.
+ *   in_mode:  PLAIN     x[0:in_features] as is;
+ *             NORM      rmsnorm(x[0:dim]; norm_w, eps), zero past dim;
+ *             RESIDUAL  x = the residual h (in x) + the partial outputs every
+ *                       rank sent in the preceding PARTIAL stage (summed in
+ *                       rank order), also written to h_out (distinct from x);
+ *                       dim = the partials' length;
+ *             RESIDUAL_NORM  the same, then RMSNorm.
+ *   out_mode: STORE     y[0:out_features];
+ *             SWIGLU    W's rows are (gate, up) pairs, y[j] = swiglu(row 2j,
+ *                       row 2j + 1; act) (act as kq_dec_swiglu's mode);
+ *             PARTIAL   this rank's part of a residual update of
+ *                       out_features values (a column-split weight, or the
+ *                       whole weight on one GPU), consumed by the next
+ *                       RESIDUAL stage; y unused.
+ * kq_step_attention adds RoPE + KV append + attention of the new token
+ * (heads / kv_heads heads of head_dim 64 or 128, group <= 8) over this rank's
+ * caches [kv_heads][max_seq][head_dim] f16; qkv = q | k | v of this rank's
+ * heads.  With a tensor-parallel group every rank builds the same sequence of
+ * stages over its own shards.  kq_step_run(pos) queues one launch on the
+ * context's stream; its first call sizes and allocates the step's scratch
+ * (make it before any stream capture). */
+typedef struct kq_step kq_step;
+#define KQ_STEP_IN_PLAIN 0
+#define KQ_STEP_IN_NORM 1
+#define KQ_STEP_IN_RESIDUAL 2
+#define KQ_STEP_IN_RESIDUAL_NORM 3
+#define KQ_STEP_OUT_STORE 0
+#define KQ_STEP_OUT_SWIGLU 1
+#define KQ_STEP_OUT_PARTIAL 2
+int kq_step_create(kq_ctx *ctx, kq_tp *tp, kq_step **out);
+int kq_step_linear(kq_step *step, const kq_weight *w, int in_mode, const float *x, const float *norm_w, int64_t dim,
+                   float eps, float *h_out, int out_mode, float *y, int act);
+int kq_step_attention(kq_step *step, const float *qkv, void *k_cache, void *v_cache, float *out, int heads,
+                      int kv_heads, int head_dim, int64_t max_seq, float theta);
+int kq_step_run(kq_step *step, int64_t pos, int flags);
+int kq_step_destroy(kq_step *step);
+
 /* out[b] = table[tokens[b]] (Model::embed, model.rs:966-984); table f32 [vocab][dim]. */
 int kq_dec_embed(kq_ctx *ctx, const float *table, const int32_t *tokens, float *out, int64_t out_ld,
                  int64_t batch, int64_t dim);

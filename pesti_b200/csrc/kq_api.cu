@@ -81,6 +81,23 @@ struct kq_weight {
   int64_t device_bytes = 0;
 };
 
+// A decode-step program (kq_step_*): its stages on the host, and once built,
+// their device copy and the scratch the persistent kernel needs.
+struct kq_step {
+  kq_ctx* ctx = nullptr;
+  kq_tp* tp = nullptr;  // NULL: one GPU, with a local exchange buffer
+  std::vector<kq::StepStage> stages;
+  int nexch = 0;             // PARTIAL stages so far
+  int64_t pending_len = -1;  // length of the exchange a RESIDUAL stage may consume (-1: none)
+  bool built = false;
+  kq::StepArgs args{};
+  void* d_stages = nullptr;
+  void* sync = nullptr;      // sync words, zero between launches
+  void* attn_part = nullptr;
+  void* exch = nullptr;      // one GPU: two slots of exchange words
+  void* epoch = nullptr;     // one GPU: the exchange epoch
+};
+
 namespace {
 
 const char* kNoCtx = "no context";
@@ -174,7 +191,8 @@ int check_device_error(kq_ctx* ctx) {
   cudaGetLastError();
   return fail(ctx, KQ_ERR_CUDA,
               "a device-side wait gave up (code %d: 1-5 tcgen05 pipeline, 21-23 decode weight ring, "
-              "27-28 batched integer-MMA ring, 31-32 tensor-parallel peer flag); the call's output is invalid",
+              "27-28 batched integer-MMA ring, 31-32 tensor-parallel peer flag, 41-45 decode-step ring, "
+              "barrier or exchange); the call's output is invalid",
               code);
 }
 
@@ -277,6 +295,7 @@ int kq_ctx_create(int device, kq_ctx** out) {
   if (e == cudaSuccess) e = kq::imma_init_device();
   if (e == cudaSuccess) e = kq::dec_init_device();
   if (e == cudaSuccess) e = kq::kx_init_device();
+  if (e == cudaSuccess) e = kq::step_init_device();
   if (e != cudaSuccess) {
     cudaGetLastError();
     return KQ_ERR_CUDA;
@@ -1090,6 +1109,277 @@ int kq_dec_embed(kq_ctx* ctx, const float* table, const int32_t* tokens, float* 
   DeviceGuard g(ctx->device);
   ctx->launches += 1;
   return dec_status(ctx, kq::dec_embed(table, tokens, out, out_ld, batch, dim, ctx->stream), "embed");
+}
+
+// ---- persistent decode step ------------------------------------------------------
+
+int kq_step_create(kq_ctx* ctx, kq_tp* tp, kq_step** out) {
+  if (check_ctx(ctx) || !out) return KQ_ERR_INVALID_ARG;
+  *out = nullptr;
+  if (tp && (tp->ctx != ctx || !tp->opened))
+    return fail(ctx, KQ_ERR_STATE, "kq_step_create: the tensor-parallel group must be open and on this context");
+  kq_step* st = new kq_step;
+  st->ctx = ctx;
+  st->tp = tp;
+  *out = st;
+  return KQ_OK;
+}
+
+static void step_release(kq_step* st) {
+  for (void* p : {st->d_stages, st->sync, st->attn_part, st->exch, st->epoch})
+    if (p) cudaFree(p);
+  st->d_stages = st->sync = st->attn_part = st->exch = st->epoch = nullptr;
+  st->built = false;
+}
+
+int kq_step_destroy(kq_step* st) {
+  if (!st) return KQ_ERR_INVALID_ARG;
+  {
+    DeviceGuard g(st->ctx->device);
+    cudaStreamSynchronize(st->ctx->stream);
+    step_release(st);
+    cudaGetLastError();
+  }
+  delete st;
+  return KQ_OK;
+}
+
+int kq_step_linear(kq_step* st, const kq_weight* w, int in_mode, const float* x, const float* norm_w, int64_t dim,
+                   float eps, float* h_out, int out_mode, float* y, int act) {
+  if (!st) return KQ_ERR_INVALID_ARG;
+  kq_ctx* ctx = st->ctx;
+  if (!w || w->device != ctx->device) return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: no weight on this device");
+  if (!is_gguf(w->dw.type))
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_linear: the step kernel serves GGUF Q4_K / Q6_K weights");
+  const int nk = (int)((w->dw.sb + 7) / 8);
+  if (w->dw.n < 1 || nk < 1 || nk > kq::STEP_COMPUTE_WARPS || w->dw.n > (int64_t)1 << 30)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_linear: %lld x %lld is outside the step kernel's shapes",
+                (long long)w->dw.n, (long long)w->dw.k);
+  if (in_mode < KQ_STEP_IN_PLAIN || in_mode > KQ_STEP_IN_RESIDUAL_NORM || out_mode < KQ_STEP_OUT_STORE ||
+      out_mode > KQ_STEP_OUT_PARTIAL || act < 0 || act > 1)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: bad mode (in %d, out %d, act %d)", in_mode, out_mode, act);
+  const bool residual = in_mode == KQ_STEP_IN_RESIDUAL || in_mode == KQ_STEP_IN_RESIDUAL_NORM;
+  const bool norm = in_mode == KQ_STEP_IN_NORM || in_mode == KQ_STEP_IN_RESIDUAL_NORM;
+  if (!x || (norm && !norm_w) || (residual && (!h_out || h_out == x)) || (out_mode != KQ_STEP_OUT_PARTIAL && !y))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: missing x, norm weights, h_out (distinct from x) or y");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(h_out) | reinterpret_cast<uintptr_t>(norm_w)) & 15)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: x, h_out and norm weights must be 16-byte aligned");
+  if ((norm || residual) && (dim < 4 || (dim & 3) || dim > w->dw.k))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: dim %lld must be a positive multiple of 4 <= in_features",
+                (long long)dim);
+  if (residual && st->pending_len != dim)
+    return fail(ctx, KQ_ERR_STATE, "kq_step_linear: a residual input needs a preceding partial output of length %lld",
+                (long long)dim);
+  if (out_mode == KQ_STEP_OUT_PARTIAL) {
+    if (st->pending_len >= 0 && !residual)
+      return fail(ctx, KQ_ERR_STATE, "kq_step_linear: the previous partial output has not been consumed");
+    if (w->dw.n & 3) return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_linear: a partial output needs rows % 4 == 0");
+    if (st->tp && w->dw.n * st->tp->world > st->tp->max_elems)
+      return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_linear: %d partials of %lld exceed the exchange slot",
+                  st->tp->world, (long long)w->dw.n);
+  }
+  if (out_mode == KQ_STEP_OUT_SWIGLU && (w->dw.n & 1))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: SwiGLU rows come in (gate, up) pairs");
+  kq::StepStage S;
+  S.kind = kq::STEP_GEMV;
+  S.barrier = !residual && !st->stages.empty();
+  S.qt = w->dw.type;
+  S.n = (int)w->dw.n;
+  S.sb = (int)w->dw.sb;
+  S.nk = nk;
+  S.G = kq::STEP_COMPUTE_WARPS / nk;
+  S.row_bytes = w->dw.sb * (w->dw.type == kq::GGUF_Q4_K ? kq::Q4K_BYTES : kq::Q6K_BODY);
+  S.d_row_bytes = w->dw.type == kq::GGUF_Q6_K ? (int)(w->dw.d_ld * 2) : 0;
+  S.q = w->dw.q;
+  S.d = w->dw.d;
+  S.xmode = in_mode == KQ_STEP_IN_PLAIN ? kq::SX_PLAIN
+            : in_mode == KQ_STEP_IN_NORM ? kq::SX_NORM
+            : in_mode == KQ_STEP_IN_RESIDUAL ? kq::SX_REDUCE : kq::SX_REDUCE_NORM;
+  S.ymode = out_mode == KQ_STEP_OUT_STORE ? kq::SY_STORE : out_mode == KQ_STEP_OUT_SWIGLU ? kq::SY_SWIGLU
+                                                                                          : kq::SY_PARTIAL;
+  S.x = x;
+  S.nw = norm_w;
+  S.dim = (int)((norm || residual) ? dim : 0);
+  S.eps = eps;
+  S.act = act;
+  S.y = y;
+  S.h_in = residual ? x : nullptr;
+  S.h_out = residual ? h_out : nullptr;
+  if (residual) {
+    S.exch = st->nexch - 1;
+    st->pending_len = -1;
+  }
+  if (out_mode == KQ_STEP_OUT_PARTIAL) {
+    S.exch = st->nexch++;
+    st->pending_len = w->dw.n;
+  }
+  st->stages.push_back(S);
+  st->built = false;
+  return KQ_OK;
+}
+
+int kq_step_attention(kq_step* st, const float* qkv, void* k_cache, void* v_cache, float* out, int heads,
+                      int kv_heads, int head_dim, int64_t max_seq, float theta) {
+  if (!st) return KQ_ERR_INVALID_ARG;
+  kq_ctx* ctx = st->ctx;
+  if (!qkv || !k_cache || !v_cache || !out)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_attention: null qkv, cache or output");
+  if ((head_dim != 64 && head_dim != 128) || kv_heads < 1 || heads < kv_heads || heads % kv_heads ||
+      heads / kv_heads > kq::STEP_ATTN_MAX_GROUP || (heads / kv_heads) * head_dim / 2 > 32 * kq::STEP_COMPUTE_WARPS ||
+      max_seq < 1)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_attention: %d / %d heads of %d (head_dim 64 or 128, group <= %d)",
+                heads, kv_heads, head_dim, kq::STEP_ATTN_MAX_GROUP);
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_attention: the caches must be 16-byte aligned");
+  kq::StepStage S;
+  S.kind = kq::STEP_ATTN;
+  S.barrier = !st->stages.empty();
+  S.qkv = qkv;
+  S.kc = k_cache;
+  S.vc = v_cache;
+  S.out = out;
+  S.hq = heads;
+  S.hkv = kv_heads;
+  S.hd = head_dim;
+  S.max_seq = max_seq;
+  S.theta = theta;
+  S.splits = std::max(1, ctx->num_sms / kv_heads);
+  st->stages.push_back(S);
+  st->built = false;
+  return KQ_OK;
+}
+
+// Size the kernel's shared memory and scratch for the stages, and copy them
+// to the device (synchronous: call outside any stream capture).
+static int step_build(kq_step* st) {
+  kq_ctx* ctx = st->ctx;
+  if (st->stages.empty()) return fail(ctx, KQ_ERR_STATE, "kq_step_run: the program has no stages");
+  if (st->pending_len >= 0 && !st->tp)
+    return fail(ctx, KQ_ERR_STATE, "kq_step_run: the last partial output is never consumed");
+  step_release(st);
+  const int C = ctx->num_sms;
+  kq::StepArgs& a = st->args;
+  a = kq::StepArgs();
+  int64_t slot = 0, xr = 0, partial = 0;
+  int nk_max = 1, rows_max = 1, max_hkv = 0;
+  for (auto& S : st->stages) {
+    if (S.kind != kq::STEP_GEMV) continue;
+    slot = std::max<int64_t>(slot, 2 * S.G * (S.row_bytes + S.d_row_bytes));
+    nk_max = std::max(nk_max, S.nk);
+    for (int b = 0; b < C; ++b) {  // the kernel's row split (sp_rows)
+      int64_t r0, r1;
+      if (S.ymode == kq::SY_SWIGLU) {
+        r0 = 2 * ((int64_t)(S.n / 2) * b / C);
+        r1 = 2 * ((int64_t)(S.n / 2) * (b + 1) / C);
+      } else if (S.ymode == kq::SY_PARTIAL) {
+        r0 = 4 * ((int64_t)(S.n / 4) * b / C);
+        r1 = b == C - 1 ? S.n : 4 * ((int64_t)(S.n / 4) * (b + 1) / C);
+        partial = std::max<int64_t>(partial, S.n);
+      } else {
+        r0 = (int64_t)S.n * b / C;
+        r1 = (int64_t)S.n * (b + 1) / C;
+      }
+      rows_max = std::max(rows_max, (int)(r1 - r0));
+    }
+    if (S.xmode == kq::SX_REDUCE || S.xmode == kq::SX_REDUCE_NORM) xr = std::max<int64_t>(xr, S.dim);
+  }
+  int attn_bytes = 0;
+  int64_t part_floats = 0;
+  for (auto& S : st->stages) {
+    if (S.kind != kq::STEP_ATTN) continue;
+    slot = std::max<int64_t>(slot, (int64_t)S.hd * 2 * 64);  // at least 64 positions per KV tile
+  }
+  slot = (slot + 127) & ~int64_t(127);
+  for (auto& S : st->stages) {
+    if (S.kind != kq::STEP_ATTN) continue;
+    S.tile = (int)std::min<int64_t>(slot / (S.hd * 2), 1024);
+    const int G = S.hq / S.hkv;
+    attn_bytes = std::max(attn_bytes, G * S.hd * 4 + G * (S.tile + 4) * 4 + 3 * kq::STEP_ATTN_MAX_GROUP * 4 +
+                                          2 * S.hd * 2 + 16);
+    part_floats = std::max<int64_t>(part_floats, (int64_t)S.hkv * S.splits * G * (S.hd + 4));
+    max_hkv = std::max(max_hkv, S.hkv);
+  }
+  const size_t fixed = kq::StepSmem(0, (int)slot, nk_max, rows_max, (int)((xr + 3) & ~3), attn_bytes).end;
+  if (slot > (1 << 20) || fixed + 2 * (size_t)slot > (size_t)kq::STEP_MAX_SMEM)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_run: a stage needs %lld-byte ring slots; two do not fit",
+                (long long)slot);
+  const int fit = (int)((kq::STEP_MAX_SMEM - fixed - 64) / (size_t)slot);
+  a.S = std::max(2, std::min(fit, std::max(2, (int)((176 * 1024) / slot))));
+  a.slot_bytes = (int)slot;
+  a.nk_max = nk_max;
+  a.rows_max = rows_max;
+  a.xr_floats = (int)((xr + 3) & ~3);
+  a.attn_bytes = attn_bytes;
+  a.nexch = st->nexch;
+  DeviceGuard g(ctx->device);
+  const size_t sync_bytes = (size_t)(kq::STEP_SYNC_ATTN + max_hkv + 2) * sizeof(unsigned);
+  cudaError_t e = cudaMalloc(&st->sync, sync_bytes);
+  if (e == cudaSuccess) e = cudaMemset(st->sync, 0, sync_bytes);
+  if (e == cudaSuccess && part_floats) e = cudaMalloc(&st->attn_part, (size_t)part_floats * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&st->d_stages, st->stages.size() * sizeof(kq::StepStage));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(st->d_stages, st->stages.data(), st->stages.size() * sizeof(kq::StepStage), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess && st->tp) {
+    for (int p = 0; p < st->tp->world; ++p) a.exch[p] = static_cast<unsigned long long*>(st->tp->peer_base[p]);
+    a.slot_elems = st->tp->max_elems;
+    a.world = st->tp->world;
+    a.rank = st->tp->rank;
+    a.epoch = st->tp->ctr + 1;
+  } else if (e == cudaSuccess) {
+    const int64_t elems = std::max<int64_t>(partial, 4);
+    e = cudaMalloc(&st->exch, (size_t)2 * elems * 8);
+    if (e == cudaSuccess) e = cudaMemset(st->exch, 0, (size_t)2 * elems * 8);
+    if (e == cudaSuccess) e = cudaMalloc(&st->epoch, 16);
+    if (e == cudaSuccess) e = cudaMemset(st->epoch, 0, 16);
+    a.exch[0] = static_cast<unsigned long long*>(st->exch);
+    a.slot_elems = elems;
+    a.world = 1;
+    a.rank = 0;
+    a.epoch = static_cast<unsigned*>(st->epoch);
+  }
+  if (e != cudaSuccess) {
+    step_release(st);
+    return cuda_fail(ctx, e, "kq_step_run: allocate the step's scratch");
+  }
+  a.stages = static_cast<const kq::StepStage*>(st->d_stages);
+  a.nstages = (int)st->stages.size();
+  a.sync = static_cast<unsigned*>(st->sync);
+  a.attn_part = static_cast<float*>(st->attn_part);
+  a.err = ctx->dev_err;
+  st->built = true;
+  return KQ_OK;
+}
+
+int kq_step_run(kq_step* st, int64_t pos, int flags) {
+  if (!st) return KQ_ERR_INVALID_ARG;
+  kq_ctx* ctx = st->ctx;
+  if (flags & ~KQ_SYNC) return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_run: bad flags 0x%x", flags);
+  for (const auto& S : st->stages)
+    if (S.kind == kq::STEP_ATTN && (pos < 0 || pos >= S.max_seq))
+      return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_run: position %lld outside the cache (%lld)", (long long)pos,
+                  (long long)S.max_seq);
+  DeviceGuard g(ctx->device);
+  if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
+  if (!st->built) {
+    const int rc = step_build(st);
+    if (rc) return rc;
+  }
+  kq::StepArgs a = st->args;
+  a.pos = pos;
+  kq::Bracket br = ctx->next_bracket();
+  kq::bracket_record(br.start, ctx->stream);
+  cudaError_t e = kq::launch_step(a, ctx->num_sms, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "kq_step_run: launch");
+  kq::bracket_record(br.stop, ctx->stream);
+  ctx->launches += 1;
+  if (flags & KQ_SYNC) {
+    const int rc = finish_sync(ctx, "kq_step_run");
+    if (rc != KQ_OK && st->sync) {  // a wait gave up: counters may be left mid-count
+      st->built = false;  // the next run rebuilds (and re-zeroes) every scratch word
+    }
+    return rc;
+  }
+  return KQ_OK;
 }
 
 int kq_dequant_f32(kq_ctx* ctx, const kq_weight* w, int64_t row0, int64_t nrows, float* out, int flags) {

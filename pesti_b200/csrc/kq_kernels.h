@@ -197,6 +197,87 @@ struct XsInput {
 cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* bias, float* y, int num_sms, int* err,
                            const Prefetch* pf, cudaStream_t s, int* launches, Bracket br = Bracket());
 
+// ---- persistent batch-1 decode step: kq_step.cu ----
+constexpr int STEP_COMPUTE_WARPS = 15;
+constexpr int STEP_THREADS = 32 * (STEP_COMPUTE_WARPS + 1);
+constexpr int STEP_MAX_SMEM = 227 * 1024 - 1024;  // dynamic shared memory (static use stays below 1 KB)
+constexpr int STEP_ATTN_MAX_GROUP = 8;            // query heads per KV head
+// sync words (zero between launches): barrier arrivals, exits, then one
+// arrival counter per KV head of the attention stages
+enum : int { STEP_SYNC_BAR = 0, STEP_SYNC_EXIT = 1, STEP_SYNC_ATTN = 2 };
+enum : int { STEP_GEMV = 0, STEP_ATTN = 1 };
+// GEMV input: x as is; RMSNorm of x[0:dim]; x = h_in + the pending exchange's
+// partials (written to h_out), optionally RMS-normalised
+enum : int { SX_PLAIN = 0, SX_NORM = 1, SX_REDUCE = 2, SX_REDUCE_NORM = 3 };
+// GEMV output: y; SwiGLU of (gate, up) row pairs into y; this rank's partial
+// of a residual update, sent to every rank as exchange words
+enum : int { SY_STORE = 0, SY_SWIGLU = 1, SY_PARTIAL = 2 };
+struct StepStage {
+  int kind = STEP_GEMV;
+  int barrier = 0;  // grid barrier before the stage (its input was produced by other CTAs)
+  // GEMV (GGUF Q4_K / Q6_K)
+  int qt = 0, n = 0, sb = 0, nk = 0, G = 0;
+  int64_t row_bytes = 0;
+  int d_row_bytes = 0;
+  const uint8_t* q = nullptr;
+  const uint16_t* d = nullptr;
+  int xmode = SX_PLAIN, ymode = SY_STORE;
+  const float* x = nullptr;   // PLAIN / NORM input
+  const float* nw = nullptr;  // NORM weights
+  int dim = 0;                // NORM / REDUCE: vector length
+  float eps = 0.f;
+  int act = 0;                // SWIGLU gate activation
+  float* y = nullptr;
+  int exch = 0;               // REDUCE: exchange read; PARTIAL: exchange written (index within the step)
+  const float* h_in = nullptr;
+  float* h_out = nullptr;
+  // ATTN (batch 1): qkv row = q (hq heads) | k (hkv) | v (hkv), caches [hkv][max_seq][hd] f16
+  const float* qkv = nullptr;
+  void* kc = nullptr;
+  void* vc = nullptr;
+  float* out = nullptr;       // [hq][hd]
+  int hq = 0, hkv = 0, hd = 0, splits = 0, tile = 0;
+  int64_t max_seq = 0;
+  float theta = 0.f;
+};
+struct StepArgs {
+  const StepStage* stages = nullptr;
+  int nstages = 0;
+  int64_t pos = 0;                 // the new token's position
+  unsigned* sync = nullptr;        // STEP_SYNC_* words
+  float* attn_part = nullptr;      // [hkv][splits][G][hd + 4] partials of the attention splits
+  int* err = nullptr;
+  unsigned long long* exch[TP_MAX_WORLD] = {};  // every rank's exchange buffer (two slots)
+  int64_t slot_elems = 0;
+  int world = 1, rank = 0;
+  unsigned* epoch = nullptr;       // last published exchange epoch of this rank
+  int nexch = 0;                   // exchanges per step
+  int S = 0, slot_bytes = 0, nk_max = 0, rows_max = 0, xr_floats = 0, attn_bytes = 0;
+};
+// Dynamic shared memory of the step kernel: ring | staged x | sums | 2^e per
+// superblock | row partials | reduction | reduced x (REDUCE) | barriers; the
+// attention scratch reuses the staging area.
+struct StepSmem {
+  size_t ring, xw, sums, xsf, part, red, xr, attn, bar, end;
+  __host__ __device__ StepSmem(int S, int slot_bytes, int nk_max, int rows_max, int xr_floats, int attn_bytes) {
+    const size_t units = (size_t)8 * nk_max * 4;
+    ring = 0;
+    xw = (size_t)S * (size_t)slot_bytes;
+    sums = xw + units * 128;
+    xsf = sums + units * 64;
+    part = xsf + units;
+    red = (part + (size_t)rows_max * nk_max * 4 + 15) & ~size_t(15);
+    xr = red + 32 * 4;
+    attn = xw;
+    const size_t gemv_end = xr + (size_t)xr_floats * 4, attn_end = attn + (size_t)attn_bytes;
+    bar = ((gemv_end > attn_end ? gemv_end : attn_end) + 15) & ~size_t(15);
+    end = bar + (size_t)2 * S * 8;
+  }
+};
+cudaError_t step_init_device();
+// One cooperative launch of `grid` CTAs (the SM count: one per SM).
+cudaError_t launch_step(const StepArgs& a, int grid, cudaStream_t s);
+
 // ---- tensor parallel: all-gather of row-sharded outputs over peer memory (kq_tp.cu) ----
 struct TpArgs {
   const float* y_local;                  // [m][r1 - r0] this rank's block

@@ -80,13 +80,24 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "kq_dec_rope_attention": [P, P, I64, P, P, P, I64, I64, I, I, I, I64, I64, F, P, Z],
         "kq_dec_tp_partial_linear": [P, P, P, I, I],
         "kq_dec_tp_reduce_linear": [P, P, P, P, P, I64, F, I, P, I],
+        "kq_step_linear": [P, P, I, P, P, I64, F, P, I, P, I],
+        "kq_step_attention": [P, P, P, P, P, I, I, I, I64, F],
+        "kq_step_run": [P, I64, I],
+        "kq_step_destroy": [P],
     }
     for name, args in sig.items():
         getattr(lib, name).argtypes = args
         getattr(lib, name).restype = I
     lib.kq_dec_attention_scratch.argtypes = [P, I64, I, I, I, I64]
     lib.kq_dec_attention_scratch.restype = Z
+    lib.kq_step_create.argtypes = [P, P, ctypes.POINTER(P)]
+    lib.kq_step_create.restype = I
     return lib
+
+
+# kq_step_linear modes (include/pesti_decoder.h)
+STEP_IN_PLAIN, STEP_IN_NORM, STEP_IN_RESIDUAL, STEP_IN_RESIDUAL_NORM = 0, 1, 2, 3
+STEP_OUT_STORE, STEP_OUT_SWIGLU, STEP_OUT_PARTIAL = 0, 1, 2
 
 
 def gguf_weight_device(qtype: int, n: int, k: int, seed: int, device):
@@ -135,7 +146,7 @@ class Decoder:
     def __init__(self, cfg: DecoderConfig, ctx: "kq.Context", batch: int, context_len: int, max_new: int = 8,
                  world: int = 1, rank: int = 0, tp: Optional["kq.TensorParallel"] = None, seed: int = 0,
                  swiglu_mode: int = SWIGLU_REFERENCE, kv_scale: float = 1.0, keep_raw: bool = False,
-                 fused: bool = True, prefetch: bool = False):
+                 fused: bool = True, prefetch: bool = False, step_kernel: bool = True):
         import torch
         if cfg.heads % world or cfg.kv_heads % world:
             raise ValueError(f"{cfg.name}: {cfg.heads} query / {cfg.kv_heads} KV heads do not split over {world}")
@@ -157,6 +168,10 @@ class Decoder:
         # paths that run it (one GPU or the column split at batch 1); otherwise
         # [gate block | up block] for the separate SwiGLU kernel
         self.pairs = self.fused and (world == 1 or self.col_split)
+        # batch 1: the whole step as one persistent kernel (kq_step_*), on one
+        # GPU or with the column split; otherwise one kernel per operation
+        self.step_kernel = step_kernel and self.fused and (world == 1 or self.col_split)
+        self._step = None
         self.lib = _bind(ctx.lib)
         dev = torch.device("cuda", ctx.device)
         self.device = dev
@@ -317,6 +332,9 @@ class Decoder:
         ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
         if not 0 <= pos < self.max_seq:
             raise ValueError(f"position {pos} outside the cache ({self.max_seq})")
+        if self.step_kernel:
+            self._step_persistent(pos)
+            return
         if self.col_split:
             self._step_col_split(pos)
             return
@@ -423,6 +441,66 @@ class Decoder:
             self.head.linear(cur, 1, self.logits_r, device_ptrs=True)
         self._gather(self.logits_r, cfg.vocab, v0, v1 - v0, self.logits, cfg.vocab, False)
 
+    def _build_step(self) -> None:
+        """The step program of the persistent kernel (kq_step_*): per layer
+        RMSNorm + q|k|v, attention, the output projection as a partial residual
+        update, residual + RMSNorm + gate/up + SwiGLU, the down projection as a
+        partial; then the residual, the final norm and the head.  On one GPU the
+        output and down projections are whole weights whose 'partial' is the full
+        update; with the column split each rank holds W[:, its heads / FFN block]."""
+        import torch
+        cfg, lib = self.cfg, self.lib
+        D, hd = cfg.dim, cfg.head_dim
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None  # noqa: E731
+        h = ctypes.c_void_p()
+        self.ctx.check(lib.kq_step_create(self.ctx.handle, self.tp.handle if self.tp is not None else None,
+                                          ctypes.byref(h)), "kq_step_create")
+        self._step = h
+        if self.h2 is None:
+            self.h2 = torch.zeros_like(self.h)
+        cur, nxt = self.h, self.h2
+        pending = False
+        c = lambda rc, what: self.ctx.check(rc, what)  # noqa: E731
+        for L in self.layers:
+            if pending:
+                c(lib.kq_step_linear(h, L["qkv"].handle, STEP_IN_RESIDUAL_NORM, ptr(cur), ptr(L["attn_norm"]), D,
+                                     cfg.eps, ptr(nxt), STEP_OUT_STORE, ptr(self.qkv), 0), "step qkv")
+                cur, nxt = nxt, cur
+            else:
+                c(lib.kq_step_linear(h, L["qkv"].handle, STEP_IN_NORM, ptr(cur), ptr(L["attn_norm"]), D, cfg.eps,
+                                     None, STEP_OUT_STORE, ptr(self.qkv), 0), "step qkv")
+            out = self.attn_r if self.col_split else self.attn
+            c(lib.kq_step_attention(h, ptr(self.qkv), ptr(L["k"]), ptr(L["v"]), ptr(out), self.hq, self.hkv, hd,
+                                    self.max_seq, cfg.theta), "step attention")
+            c(lib.kq_step_linear(h, L["o"].handle, STEP_IN_PLAIN, ptr(out), None, 0, 0.0, None, STEP_OUT_PARTIAL,
+                                 None, 0), "step o")
+            c(lib.kq_step_linear(h, L["gu"].handle, STEP_IN_RESIDUAL_NORM, ptr(cur), ptr(L["ffn_norm"]), D, cfg.eps,
+                                 ptr(nxt), STEP_OUT_SWIGLU, ptr(self.s_r if self.col_split else self.s),
+                                 self.swiglu_mode), "step gate/up")
+            cur, nxt = nxt, cur
+            c(lib.kq_step_linear(h, L["down"].handle, STEP_IN_PLAIN, ptr(self.s_r if self.col_split else self.s),
+                                 None, 0, 0.0, None, STEP_OUT_PARTIAL, None, 0), "step down")
+            pending = True
+        logits = self.logits_r if self.world > 1 else self.logits
+        mode = STEP_IN_RESIDUAL_NORM if self.final_norm is not None else STEP_IN_RESIDUAL
+        c(lib.kq_step_linear(h, self.head.handle, mode, ptr(cur), ptr(self.final_norm), D, cfg.eps, ptr(nxt),
+                             STEP_OUT_STORE, ptr(logits), 0), "step head")
+        self._step_in = self.h  # the embedding goes here; the residual ends in `nxt`
+
+    def _step_persistent(self, pos: int) -> None:
+        """Batch-1 step: embedding lookup, the persistent step kernel, and (tensor
+        parallel) the all-gather of the logits slices."""
+        cfg, lib, c = self.cfg, self.lib, self.ctx.handle
+        ptr = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        if self._step is None:
+            self._build_step()
+        self._check(lib.kq_dec_embed(c, ptr(self.embed), ptr(self.tokens), ptr(self._step_in), self.Dp, 1, cfg.dim),
+                    "embed")
+        self._check(lib.kq_step_run(self._step, pos, 0), "kq_step_run")
+        if self.world > 1:
+            v0, v1 = self.v_rows
+            self._gather(self.logits_r, cfg.vocab, v0, v1 - v0, self.logits, cfg.vocab, False)
+
     def weight_bytes(self) -> int:
         """HBM bytes of this rank's quantized weights."""
         total = self.head.device_bytes
@@ -435,6 +513,9 @@ class Decoder:
         return self.cfg.layers * 2 * self.batch * self.hkv * (pos + 1) * self.cfg.head_dim * 2
 
     def close(self) -> None:
+        if self._step is not None:
+            self.lib.kq_step_destroy(self._step)
+            self._step = None
         for L in self.layers:
             for key in ("qkv", "o", "gu", "down"):
                 L[key].free()

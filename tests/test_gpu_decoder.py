@@ -38,17 +38,21 @@ def _oracle_caches(model, cfg):
     return ks, vs
 
 
-# batch 1 runs the fused single-token linears (RMSNorm / SwiGLU / residual
-# inside the GEMV), batch 2 the separate kernels; "unfused" forces the latter at batch 1
+# batch 1 runs the whole step as one persistent kernel ("b1"), or the fused
+# single-token linears (RMSNorm / SwiGLU / residual inside the GEMV) one
+# kernel per operation ("b1-kernels"); batch 2 the separate kernels;
+# "unfused" forces the latter at batch 1
 @pytest.mark.parametrize("cfg", [QWEN_TINY, LLAMA_TINY], ids=lambda c: c.name)
 @pytest.mark.parametrize("mode", [dec.SWIGLU_REFERENCE, dec.SWIGLU_SILU])
-@pytest.mark.parametrize("batch,fused", [(1, True), (1, False), (2, True)], ids=["b1", "b1-unfused", "b2"])
-def test_decode_steps_match_the_restated_reference(gpu_ctx, cfg, mode, batch, fused):
+@pytest.mark.parametrize("batch,fused,step", [(1, True, True), (1, True, False), (1, False, False), (2, True, False)],
+                         ids=["b1", "b1-kernels", "b1-unfused", "b2"])
+def test_decode_steps_match_the_restated_reference(gpu_ctx, cfg, mode, batch, fused, step):
     import torch
     from oracle import decoder_oracle
     ctx_len = 20
     model = dec.Decoder(cfg, gpu_ctx, batch, ctx_len, max_new=4, seed=5, swiglu_mode=mode, keep_raw=True,
-                        fused=fused)
+                        fused=fused, step_kernel=step)
+    assert model.step_kernel == step
     ks, vs = _oracle_caches(model, cfg)
     for step, toks in enumerate(([3, 250][:batch], [17, 9][:batch])):
         pos = ctx_len + step
@@ -97,13 +101,15 @@ def test_decode_step_replays_from_a_cuda_graph(gpu_ctx, batch):
 LLAMA3_8B_2L = dataclasses.replace(dec.LLAMA3_8B, name="llama-3-8b-shaped-2-layers", layers=2)
 
 
-@pytest.mark.parametrize("cfg,ctx_len,batch", [(dec.QWEN25_05B, 512, 1), (LLAMA3_8B_2L, 2048, 1),
-                                               (LLAMA3_8B_2L, 2048, 8)],
-                         ids=["qwen05b-full-b1", "llama8b-2layers-b1", "llama8b-2layers-b8"])
-def test_full_shape_decode_step_matches_the_restated_reference(gpu_ctx, cfg, ctx_len, batch):
+@pytest.mark.parametrize("cfg,ctx_len,batch,step", [(dec.QWEN25_05B, 512, 1, True), (dec.QWEN25_05B, 512, 1, False),
+                                                    (LLAMA3_8B_2L, 2048, 1, True), (LLAMA3_8B_2L, 2048, 1, False),
+                                                    (LLAMA3_8B_2L, 2048, 8, False)],
+                         ids=["qwen05b-full-b1", "qwen05b-full-b1-kernels", "llama8b-2layers-b1",
+                              "llama8b-2layers-b1-kernels", "llama8b-2layers-b8"])
+def test_full_shape_decode_step_matches_the_restated_reference(gpu_ctx, cfg, ctx_len, batch, step):
     import torch
     from oracle import decoder_oracle
-    model = dec.Decoder(cfg, gpu_ctx, batch, ctx_len, max_new=2, seed=9, keep_raw=True)
+    model = dec.Decoder(cfg, gpu_ctx, batch, ctx_len, max_new=2, seed=9, keep_raw=True, step_kernel=step)
     ks, vs = _oracle_caches(model, cfg)
     toks = [(1000 + 7919 * i) % cfg.vocab for i in range(batch)]
     model.tokens.copy_(torch.tensor(toks, dtype=torch.int32))
@@ -154,10 +160,10 @@ def _tp_worker(rank, world, port, out_dir, cfg_names=("LLAMA_TINY", "LLAMA_TINY_
         ctx = kq.Context(rank)
         for cfg in (globals()[c] for c in cfg_names):
             tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, 2))
-            for batch in (1, 2):
+            for batch, step in ((1, True), (1, False), (2, False)):
                 model = dec.Decoder(cfg, ctx, batch, 20, max_new=3, world=world, rank=rank, tp=tp, seed=7,
-                                    keep_raw=True)
-                single = dec.Decoder(cfg, ctx, batch, 20, max_new=3, seed=7)
+                                    keep_raw=True, step_kernel=step)
+                single = dec.Decoder(cfg, ctx, batch, 20, max_new=3, seed=7, step_kernel=step)
                 expect_split = cfg is not LLAMA_TINY and batch == 1
                 if status == "ok" and model.col_split != expect_split:
                     status = f"{cfg.name} batch {batch}: column split {model.col_split}"
@@ -176,7 +182,7 @@ def _tp_worker(rank, world, port, out_dir, cfg_names=("LLAMA_TINY", "LLAMA_TINY_
                     # oracle's tolerance and half of it against one GPU.
                     tol = TOL / 2 if model.col_split else 1e-5
                     if status == "ok" and (not np.isfinite(a).all() or rel_err(a, b) > tol or rel_err(a, ref) > TOL):
-                        status = (f"{cfg.name} batch {batch} pos {pos}: logits differ: {rel_err(a, b):.2e} "
+                        status = (f"{cfg.name} batch {batch} step {step} pos {pos}: logits differ: {rel_err(a, b):.2e} "
                                   f"from one GPU, {rel_err(a, ref):.2e} from the oracle")
                 model.close()
                 single.close()
