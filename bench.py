@@ -107,8 +107,8 @@ def parse():
                    help="each GEMV prefetches the next one's weight into L2 (kq_ctx_prefetch_next)")
     p.add_argument("--no-fuse", action="store_true",
                    help="decoders: separate RMSNorm / SwiGLU / add kernels at batch 1")
-    p.add_argument("--no-step", action="store_true",
-                   help="decoders at batch 1: one kernel per operation instead of the persistent step kernel")
+    p.add_argument("--step", action="store_true",
+                   help="decoders at batch 1: the persistent step kernel instead of one kernel per operation")
     p.add_argument("--len", type=int, default=2049, help="attention: positions attended (the new one included)")
     p.add_argument("--rows", type=int, default=28672, help="norm-swiglu: weight rows ((gate, up) pairs)")
     p.add_argument("--k", type=int, default=4096, help="norm-swiglu: in_features")
@@ -759,7 +759,7 @@ def measure_decoder(args, workload, batch, rank, world, local_rank, steps, warmu
     ctx.set_path(kernel_path(args.path))
     tp = kq.TensorParallel(ctx, world, rank, max_out_elems=dec.exchange_elems(cfg, B)) if world > 1 else None
     model = dec.Decoder(cfg, ctx, B, ctx_len, max_new=2, world=world, rank=rank, tp=tp, seed=11,
-                        fused=not args.no_fuse, prefetch=args.prefetch, step_kernel=not args.no_step)
+                        fused=not args.no_fuse, prefetch=args.prefetch, step_kernel=args.step)
     gen = torch.Generator(device=dev)
     gen.manual_seed(3)
     model.tokens.copy_(torch.randint(0, cfg.vocab, (B,), generator=gen, device=dev, dtype=torch.int32))

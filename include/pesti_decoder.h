@@ -105,19 +105,20 @@ int kq_dec_tp_reduce_linear(kq_tp *tp, const kq_weight *w, const float *h_in, fl
  * Weights: GGUF Q4_K / Q6_K (in_features <= 30720).  Pointers are device
  * pointers; vectors are batch 1.
  *   in_mode:  PLAIN     x[0:in_features] as is;
- *             NORM      rmsnorm(x[0:dim]; norm_w, eps), zero past dim;
- *             RESIDUAL  x = the residual h (in x) + the partial outputs every
- *                       rank sent in the preceding PARTIAL stage (summed in
- *                       rank order), also written to h_out (distinct from x);
- *                       dim = the partials' length;
+ *             NORM      rmsnorm(x[0:dim]; norm_w, eps), zero past dim (dim a
+ *                       multiple of 8);
+ *             RESIDUAL  the new residual h' = h + u of the preceding PARTIAL
+ *                       stage's update (the sum, in rank order, of the parts
+ *                       every rank sent), also written to h; x is not read;
+ *                       dim = the update's length;
  *             RESIDUAL_NORM  the same, then RMSNorm.
  *   out_mode: STORE     y[0:out_features];
  *             SWIGLU    W's rows are (gate, up) pairs, y[j] = swiglu(row 2j,
  *                       row 2j + 1; act) (act as kq_dec_swiglu's mode);
- *             PARTIAL   this rank's part of a residual update of
- *                       out_features values (a column-split weight, or the
- *                       whole weight on one GPU), consumed by the next
- *                       RESIDUAL stage; y unused.
+ *             PARTIAL   this rank's part of the update u of out_features
+ *                       values (a column-split weight, or the whole weight on
+ *                       one GPU) to the residual h (h NULL: a bare sum of the
+ *                       parts); consumed by the next RESIDUAL stage; y unused.
  * kq_step_attention adds RoPE + KV append + attention of the new token
  * (heads / kv_heads heads of head_dim 64 or 128, group <= 8) over this rank's
  * caches [kv_heads][max_seq][head_dim] f16; qkv = q | k | v of this rank's
@@ -135,10 +136,17 @@ typedef struct kq_step kq_step;
 #define KQ_STEP_OUT_PARTIAL 2
 int kq_step_create(kq_ctx *ctx, kq_tp *tp, kq_step **out);
 int kq_step_linear(kq_step *step, const kq_weight *w, int in_mode, const float *x, const float *norm_w, int64_t dim,
-                   float eps, float *h_out, int out_mode, float *y, int act);
+                   float eps, float *h, int out_mode, float *y, int act);
 int kq_step_attention(kq_step *step, const float *qkv, void *k_cache, void *v_cache, float *out, int heads,
                       int kv_heads, int head_dim, int64_t max_seq, float theta);
 int kq_step_run(kq_step *step, int64_t pos, int flags);
+/* Profiling hook: while `trace` (device memory, words >= SMs x stages x 6) is
+ * set, every run stores, per CTA and stage, six global-timer stamps (ns):
+ * before the stage's grid barrier, after it, after the input staging (GEMV) or
+ * the query rotation (attention), after the weight loop (attention: once the
+ * first KV tile has landed), after the outputs (attention: after the KV loop),
+ * and at the stage's end.  NULL stops it.  No reference counterpart. */
+int kq_step_trace(kq_step *step, uint64_t *trace, size_t words);
 int kq_step_destroy(kq_step *step);
 
 /* out[b] = table[tokens[b]] (Model::embed, model.rs:966-984); table f32 [vocab][dim]. */

@@ -96,6 +96,7 @@ struct kq_step {
   void* attn_part = nullptr;
   void* exch = nullptr;      // one GPU: two slots of exchange words
   void* epoch = nullptr;     // one GPU: the exchange epoch
+  unsigned long long* trace = nullptr;  // kq_step_trace buffer (caller's), or NULL
 };
 
 namespace {
@@ -1145,7 +1146,7 @@ int kq_step_destroy(kq_step* st) {
 }
 
 int kq_step_linear(kq_step* st, const kq_weight* w, int in_mode, const float* x, const float* norm_w, int64_t dim,
-                   float eps, float* h_out, int out_mode, float* y, int act) {
+                   float eps, float* h, int out_mode, float* y, int act) {
   if (!st) return KQ_ERR_INVALID_ARG;
   kq_ctx* ctx = st->ctx;
   if (!w || w->device != ctx->device) return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: no weight on this device");
@@ -1160,20 +1161,22 @@ int kq_step_linear(kq_step* st, const kq_weight* w, int in_mode, const float* x,
     return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: bad mode (in %d, out %d, act %d)", in_mode, out_mode, act);
   const bool residual = in_mode == KQ_STEP_IN_RESIDUAL || in_mode == KQ_STEP_IN_RESIDUAL_NORM;
   const bool norm = in_mode == KQ_STEP_IN_NORM || in_mode == KQ_STEP_IN_RESIDUAL_NORM;
-  if (!x || (norm && !norm_w) || (residual && (!h_out || h_out == x)) || (out_mode != KQ_STEP_OUT_PARTIAL && !y))
-    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: missing x, norm weights, h_out (distinct from x) or y");
-  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(h_out) | reinterpret_cast<uintptr_t>(norm_w)) & 15)
-    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: x, h_out and norm weights must be 16-byte aligned");
-  if ((norm || residual) && (dim < 4 || (dim & 3) || dim > w->dw.k))
-    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: dim %lld must be a positive multiple of 4 <= in_features",
+  if ((!residual && !x) || (norm && !norm_w) || (residual && !h) || (out_mode != KQ_STEP_OUT_PARTIAL && !y))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: missing x, norm weights, h or y");
+  if (residual && out_mode == KQ_STEP_OUT_PARTIAL)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_linear: a residual input cannot feed a partial output");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(h) | reinterpret_cast<uintptr_t>(norm_w)) & 15)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: x, h and norm weights must be 16-byte aligned");
+  if ((norm || residual) && (dim < 8 || (dim & 7) || dim > w->dw.k))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "kq_step_linear: dim %lld must be a positive multiple of 8 <= in_features",
                 (long long)dim);
   if (residual && st->pending_len != dim)
     return fail(ctx, KQ_ERR_STATE, "kq_step_linear: a residual input needs a preceding partial output of length %lld",
                 (long long)dim);
   if (out_mode == KQ_STEP_OUT_PARTIAL) {
-    if (st->pending_len >= 0 && !residual)
+    if (st->pending_len >= 0)
       return fail(ctx, KQ_ERR_STATE, "kq_step_linear: the previous partial output has not been consumed");
-    if (w->dw.n & 3) return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_linear: a partial output needs rows % 4 == 0");
+    if (w->dw.n & 7) return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_linear: a partial output needs rows % 8 == 0");
     if (st->tp && w->dw.n * st->tp->world > st->tp->max_elems)
       return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_linear: %d partials of %lld exceed the exchange slot",
                   st->tp->world, (long long)w->dw.n);
@@ -1197,14 +1200,14 @@ int kq_step_linear(kq_step* st, const kq_weight* w, int in_mode, const float* x,
             : in_mode == KQ_STEP_IN_RESIDUAL ? kq::SX_REDUCE : kq::SX_REDUCE_NORM;
   S.ymode = out_mode == KQ_STEP_OUT_STORE ? kq::SY_STORE : out_mode == KQ_STEP_OUT_SWIGLU ? kq::SY_SWIGLU
                                                                                           : kq::SY_PARTIAL;
-  S.x = x;
+  S.x = residual ? nullptr : x;
   S.nw = norm_w;
   S.dim = (int)((norm || residual) ? dim : 0);
   S.eps = eps;
   S.act = act;
   S.y = y;
-  S.h_in = residual ? x : nullptr;
-  S.h_out = residual ? h_out : nullptr;
+  S.h_in = out_mode == KQ_STEP_OUT_PARTIAL ? h : nullptr;
+  S.h_out = residual ? h : nullptr;
   if (residual) {
     S.exch = st->nexch - 1;
     st->pending_len = -1;
@@ -1260,7 +1263,7 @@ static int step_build(kq_step* st) {
   const int C = ctx->num_sms;
   kq::StepArgs& a = st->args;
   a = kq::StepArgs();
-  int64_t slot = 0, xr = 0, partial = 0;
+  int64_t slot = 0, xr = 0, nwf = 0, partial = 0;
   int nk_max = 1, rows_max = 1, max_hkv = 0;
   for (auto& S : st->stages) {
     if (S.kind != kq::STEP_GEMV) continue;
@@ -1282,6 +1285,7 @@ static int step_build(kq_step* st) {
       rows_max = std::max(rows_max, (int)(r1 - r0));
     }
     if (S.xmode == kq::SX_REDUCE || S.xmode == kq::SX_REDUCE_NORM) xr = std::max<int64_t>(xr, S.dim);
+    if (S.xmode == kq::SX_NORM || S.xmode == kq::SX_REDUCE_NORM) nwf = std::max<int64_t>(nwf, S.dim);
   }
   int attn_bytes = 0;
   int64_t part_floats = 0;
@@ -1295,11 +1299,12 @@ static int step_build(kq_step* st) {
     S.tile = (int)std::min<int64_t>(slot / (S.hd * 2), 1024);
     const int G = S.hq / S.hkv;
     attn_bytes = std::max(attn_bytes, G * S.hd * 4 + G * (S.tile + 4) * 4 + 3 * kq::STEP_ATTN_MAX_GROUP * 4 +
-                                          2 * S.hd * 2 + 16);
+                                          G * S.splits * 4 + 2 * S.hd * 2 + 16);
     part_floats = std::max<int64_t>(part_floats, (int64_t)S.hkv * S.splits * G * (S.hd + 4));
     max_hkv = std::max(max_hkv, S.hkv);
   }
-  const size_t fixed = kq::StepSmem(0, (int)slot, nk_max, rows_max, (int)((xr + 3) & ~3), attn_bytes).end;
+  const size_t fixed =
+      kq::StepSmem(0, (int)slot, nk_max, rows_max, (int)((xr + 3) & ~3), (int)((nwf + 3) & ~3), attn_bytes).end;
   if (slot > (1 << 20) || fixed + 2 * (size_t)slot > (size_t)kq::STEP_MAX_SMEM)
     return fail(ctx, KQ_ERR_UNSUPPORTED, "kq_step_run: a stage needs %lld-byte ring slots; two do not fit",
                 (long long)slot);
@@ -1309,6 +1314,7 @@ static int step_build(kq_step* st) {
   a.nk_max = nk_max;
   a.rows_max = rows_max;
   a.xr_floats = (int)((xr + 3) & ~3);
+  a.nw_floats = (int)((nwf + 3) & ~3);
   a.attn_bytes = attn_bytes;
   a.nexch = st->nexch;
   DeviceGuard g(ctx->device);
@@ -1350,6 +1356,15 @@ static int step_build(kq_step* st) {
   return KQ_OK;
 }
 
+int kq_step_trace(kq_step* st, uint64_t* trace, size_t words) {
+  if (!st) return KQ_ERR_INVALID_ARG;
+  const size_t need = (size_t)st->ctx->num_sms * st->stages.size() * kq::STEP_TRACE_POINTS;
+  if (trace && words < need)
+    return fail(st->ctx, KQ_ERR_SHORT_BUFFER, "kq_step_trace: %zu words; the program needs %zu", words, need);
+  st->trace = reinterpret_cast<unsigned long long*>(trace);
+  return KQ_OK;
+}
+
 int kq_step_run(kq_step* st, int64_t pos, int flags) {
   if (!st) return KQ_ERR_INVALID_ARG;
   kq_ctx* ctx = st->ctx;
@@ -1366,6 +1381,7 @@ int kq_step_run(kq_step* st, int64_t pos, int flags) {
   }
   kq::StepArgs a = st->args;
   a.pos = pos;
+  a.trace = st->trace;
   kq::Bracket br = ctx->next_bracket();
   kq::bracket_record(br.start, ctx->stream);
   cudaError_t e = kq::launch_step(a, ctx->num_sms, ctx->stream);

@@ -202,15 +202,17 @@ constexpr int STEP_COMPUTE_WARPS = 15;
 constexpr int STEP_THREADS = 32 * (STEP_COMPUTE_WARPS + 1);
 constexpr int STEP_MAX_SMEM = 227 * 1024 - 1024;  // dynamic shared memory (static use stays below 1 KB)
 constexpr int STEP_ATTN_MAX_GROUP = 8;            // query heads per KV head
+constexpr int STEP_TRACE_POINTS = 6;              // global-timer stamps per CTA and stage
 // sync words (zero between launches): barrier arrivals, exits, then one
 // arrival counter per KV head of the attention stages
 enum : int { STEP_SYNC_BAR = 0, STEP_SYNC_EXIT = 1, STEP_SYNC_ATTN = 2 };
 enum : int { STEP_GEMV = 0, STEP_ATTN = 1 };
-// GEMV input: x as is; RMSNorm of x[0:dim]; x = h_in + the pending exchange's
-// partials (written to h_out), optionally RMS-normalised
+// GEMV input: x as is; RMSNorm of x[0:dim]; x = the sum of the pending
+// exchange's parts (the new residual, written to h_out), optionally RMS-normalised
 enum : int { SX_PLAIN = 0, SX_NORM = 1, SX_REDUCE = 2, SX_REDUCE_NORM = 3 };
-// GEMV output: y; SwiGLU of (gate, up) row pairs into y; this rank's partial
-// of a residual update, sent to every rank as exchange words
+// GEMV output: y; SwiGLU of (gate, up) row pairs into y; this rank's part of
+// a residual update, sent to every rank as exchange words (rank 0 adds h_in,
+// the residual being updated)
 enum : int { SY_STORE = 0, SY_SWIGLU = 1, SY_PARTIAL = 2 };
 struct StepStage {
   int kind = STEP_GEMV;
@@ -229,8 +231,8 @@ struct StepStage {
   int act = 0;                // SWIGLU gate activation
   float* y = nullptr;
   int exch = 0;               // REDUCE: exchange read; PARTIAL: exchange written (index within the step)
-  const float* h_in = nullptr;
-  float* h_out = nullptr;
+  const float* h_in = nullptr;  // PARTIAL: the residual the update applies to (rank 0 adds it), or NULL
+  float* h_out = nullptr;       // REDUCE: receives the new residual
   // ATTN (batch 1): qkv row = q (hq heads) | k (hkv) | v (hkv), caches [hkv][max_seq][hd] f16
   const float* qkv = nullptr;
   void* kc = nullptr;
@@ -252,14 +254,16 @@ struct StepArgs {
   int world = 1, rank = 0;
   unsigned* epoch = nullptr;       // last published exchange epoch of this rank
   int nexch = 0;                   // exchanges per step
-  int S = 0, slot_bytes = 0, nk_max = 0, rows_max = 0, xr_floats = 0, attn_bytes = 0;
+  int S = 0, slot_bytes = 0, nk_max = 0, rows_max = 0, xr_floats = 0, nw_floats = 0, attn_bytes = 0;
+  unsigned long long* trace = nullptr;  // optional [CTAs][stages][STEP_TRACE_POINTS] global-timer stamps
 };
 // Dynamic shared memory of the step kernel: ring | staged x | sums | 2^e per
 // superblock | row partials | reduction | reduced x (REDUCE) | barriers; the
 // attention scratch reuses the staging area.
 struct StepSmem {
-  size_t ring, xw, sums, xsf, part, red, xr, attn, bar, end;
-  __host__ __device__ StepSmem(int S, int slot_bytes, int nk_max, int rows_max, int xr_floats, int attn_bytes) {
+  size_t ring, xw, sums, xsf, part, red, xr, nw, attn, bar, end;
+  __host__ __device__ StepSmem(int S, int slot_bytes, int nk_max, int rows_max, int xr_floats, int nw_floats,
+                               int attn_bytes) {
     const size_t units = (size_t)8 * nk_max * 4;
     ring = 0;
     xw = (size_t)S * (size_t)slot_bytes;
@@ -268,8 +272,9 @@ struct StepSmem {
     part = xsf + units;
     red = (part + (size_t)rows_max * nk_max * 4 + 15) & ~size_t(15);
     xr = red + 32 * 4;
+    nw = xr + (size_t)xr_floats * 4;
     attn = xw;
-    const size_t gemv_end = xr + (size_t)xr_floats * 4, attn_end = attn + (size_t)attn_bytes;
+    const size_t gemv_end = nw + (size_t)nw_floats * 4, attn_end = attn + (size_t)attn_bytes;
     bar = ((gemv_end > attn_end ? gemv_end : attn_end) + 15) & ~size_t(15);
     end = bar + (size_t)2 * S * 8;
   }

@@ -5,11 +5,12 @@
 //   GEMV  y = act(x) . W^T for a GGUF Q4_K / Q6_K weight, with the work split
 //         and integer arithmetic of the single-token kernel (kq_dp4a.cu).
 //         x is staged PLAIN, NORM (RMSNorm folded into a per-row output
-//         scale) or REDUCE(_NORM): x = h_in + the partial vectors every rank
-//         sent in the pending exchange, summed in rank order and written to
-//         h_out.  y is written STORE, SWIGLU ((gate, up) row pairs) or
-//         PARTIAL: this rank's partial of the next residual update, stored as
-//         exchange words into every rank's buffer.
+//         scale) or REDUCE(_NORM): x = the sum, in rank order, of the parts
+//         every rank sent in the pending exchange (the new residual), also
+//         written to h_out.  y is written STORE, SWIGLU ((gate, up) row pairs)
+//         or PARTIAL: this rank's part of a residual update, stored as
+//         exchange words into every rank's buffer; rank 0's part carries the
+//         residual being updated, so the parts sum to the new residual.
 //   ATTN  RoPE of the new token's q and k, the KV append, and split-sequence
 //         GQA attention over the f16 cache, merged per KV head by the last
 //         CTA to finish it.
@@ -24,11 +25,11 @@
 //     attention, attention -> output projection, SwiGLU -> down projection)
 //     starts after a grid barrier (arrival counter, bounded acquire spin);
 //   * a REDUCE stage waits only on the exchange words it reads: each word
-//     carries its exchange's epoch.  A CTA writes its slice of h_out while
-//     staging and later, in the PARTIAL stage, the exchange words of the
-//     same elements (the row split of both is the same 4-aligned partition),
-//     with a fence between; a reader that has seen those words fences and
-//     then reads h_in, so it sees the slice.
+//     carries its exchange's epoch.  The residual itself travels in rank 0's
+//     words: the CTA that adds residual element i into its part is the one
+//     that wrote element i to h_out in the REDUCE before (both stages split
+//     the vector by the same 4-aligned partition), so no CTA reads another
+//     CTA's residual slice.
 // Ring slots hold 2G rows of a GEMV stage (as the single-token kernel) or one
 // KV tile, and are released with a proxy fence before the producer's next
 // bulk copy overwrites them.  Every wait is bounded and reports through the
@@ -53,6 +54,19 @@ enum : int { SP_ERR_FULL = 41, SP_ERR_EMPTY = 42, SP_ERR_DRAIN = 43, SP_ERR_BAR 
 
 __device__ __forceinline__ void sp_sync() { xs_named_sync(1, SP_CT); }
 
+// Optional trace (a profiling hook): global timer stamps per CTA and stage,
+// STEP_TRACE_POINTS of them: before the barrier, after it, after the input
+// staging (attention: the query rotation), after the weight loop
+// (attention: once the first KV tile has landed), after the outputs
+// (attention: after the KV loop), at the stage's end.
+__device__ __forceinline__ void sp_stamp(const StepArgs& A, int si, int k) {
+  if (A.trace && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    A.trace[((size_t)blockIdx.x * A.nstages + si) * STEP_TRACE_POINTS + k] = t;
+  }
+}
+
 __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -68,13 +82,12 @@ __device__ void sp_grid_sync(unsigned* ctr, unsigned target, int* err) {
   if (threadIdx.x == 0) {
     __threadfence();
     atomicAdd(ctr, 1u);
-    for (uint32_t i = 0;; ++i) {
+    for (uint32_t i = 0;; ++i) {  // one poller per CTA: no back-off
       if (ld_acquire(ctr) >= target) break;
       if (i >= SP_SPIN || ((i & 255u) == 255u && err_set(err))) {
         atomicCAS(err, 0, SP_ERR_BAR);
         break;
       }
-      __nanosleep(32);
     }
     __threadfence();
   }
@@ -97,13 +110,21 @@ __device__ __forceinline__ void sp_rows(const StepStage& S, int b, int C, int64_
   }
 }
 
+// Splits of each KV head's positions: at least SP_ATT_MIN positions each (a
+// split is one CTA's work; fewer, longer splits keep the merge short), at most
+// the stage's bound (the CTAs per KV head).
+constexpr int SP_ATT_MIN = 64;
+__device__ __forceinline__ int sp_attn_splits(const StepStage& S, int64_t len) {
+  return (int)max((int64_t)1, min((int64_t)S.splits, (len + SP_ATT_MIN - 1) / SP_ATT_MIN));
+}
 // Attention item of CTA b: (kv head, split) and its positions [t0, t1).
 __device__ __forceinline__ bool sp_attn_item(const StepStage& S, int b, int64_t len, int& hk, int64_t& t0,
                                              int64_t& t1) {
-  if (b >= S.hkv * S.splits) return false;
-  hk = b / S.splits;
-  const int sp = b - hk * S.splits;
-  const int64_t chunk = (len + S.splits - 1) / S.splits;
+  const int splits = sp_attn_splits(S, len);
+  if (b >= S.hkv * splits) return false;
+  hk = b / splits;
+  const int sp = b - hk * splits;
+  const int64_t chunk = (len + splits - 1) / splits;
   t0 = min(len, (int64_t)sp * chunk);
   t1 = min(len, t0 + chunk);
   return true;
@@ -112,6 +133,37 @@ __device__ __forceinline__ bool sp_attn_item(const StepStage& S, int b, int64_t 
 // ---------------------------------------------------------------------------
 // producer: every stage's bytes for this CTA, in program order
 // ---------------------------------------------------------------------------
+constexpr int64_t SP_PF_CHUNK = 64 * 1024;     // bytes per L2 prefetch instruction
+constexpr int64_t SP_PF_MAX = 384 * 1024;      // at most this much of a stage per CTA
+
+__device__ __forceinline__ void sp_prefetch_range(const uint8_t* p, int64_t bytes) {
+  bytes &= ~int64_t(15);  // whole 16-byte units only: nothing past the range is touched
+  for (int64_t o = 0; o < bytes; o += SP_PF_CHUNK) {
+    const uint32_t n = (uint32_t)min(SP_PF_CHUNK, bytes - o);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + o), "r"(n) : "memory");
+  }
+}
+
+// L2 prefetch of the bytes CTA b will copy for stage S (its rows, or its KV
+// tile), up to SP_PF_MAX bytes.
+__device__ void sp_prefetch_l2(const StepStage& S, const StepArgs& A, int b, int C) {
+  if (S.kind == STEP_GEMV) {
+    int64_t r0, r1;
+    sp_rows(S, b, C, r0, r1);
+    const int64_t rows = r1 - r0;
+    sp_prefetch_range(S.q + r0 * S.row_bytes, min(rows * S.row_bytes, SP_PF_MAX));
+    if (S.d_row_bytes)
+      sp_prefetch_range(reinterpret_cast<const uint8_t*>(S.d) + r0 * S.d_row_bytes, rows * S.d_row_bytes);
+  } else {
+    int hk;
+    int64_t t0, t1;
+    if (!sp_attn_item(S, b, A.pos + 1, hk, t0, t1)) return;
+    const int64_t rowb = (int64_t)S.hd * 2, off = ((int64_t)hk * S.max_seq + t0) * rowb;
+    const int64_t bytes = min((t1 - t0) * rowb, SP_PF_MAX / 2);
+    sp_prefetch_range(static_cast<const uint8_t*>(S.kc) + off, bytes);
+    sp_prefetch_range(static_cast<const uint8_t*>(S.vc) + off, bytes);
+  }
+}
 __device__ void sp_produce(const StepArgs& A, const StepSmem& L, uint8_t* sm) {
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bar);
   uint64_t* empty = full + A.S;
@@ -131,6 +183,9 @@ __device__ void sp_produce(const StepArgs& A, const StepSmem& L, uint8_t* sm) {
   };
   for (int si = 0; si < A.nstages && ok; ++si) {
     const StepStage& S = A.stages[si];
+    // the next stage's bytes of this CTA into L2 now, so HBM keeps streaming
+    // while the compute warps wait on this stage's dependencies
+    if (si + 1 < A.nstages) sp_prefetch_l2(A.stages[si + 1], A, b, C);
     if (S.kind == STEP_GEMV) {
       int64_t r0, r1;
       sp_rows(S, b, C, r0, r1);
@@ -190,8 +245,9 @@ __device__ __forceinline__ void sp_release(const StepArgs& A, uint64_t* empty, u
 // Stage x of a GEMV stage into shared memory as the single-token kernel does
 // (15-bit hi / lo bytes per superblock, swizzled in the order lanes read
 // them; Q4_K exact f32 sub-block sums, Q6_K -32 * byte sums).  REDUCE first
-// forms h_in + the exchange's partials (rank order) in xr and writes this
-// CTA's slice to h_out.  Returns nothing; NORM leaves per-warp sum(x^2) in red.
+// sums the exchange's parts (rank order) into xr and writes this CTA's slice
+// to h_out.  NORM copies the norm weights to shared memory first and leaves
+// per-warp sum(x^2) in red.
 template <int QT>
 __device__ void sp_stage_x(const StepStage& S, const StepArgs& A, const StepSmem& L, uint8_t* sm, unsigned ep0) {
   uint4* xw = reinterpret_cast<uint4*>(sm + L.xw);
@@ -200,48 +256,60 @@ __device__ void sp_stage_x(const StepStage& S, const StepArgs& A, const StepSmem
   const int lane = threadIdx.x & 31;
   const bool reduce = S.xmode == SX_REDUCE || S.xmode == SX_REDUCE_NORM;
   const bool norm = S.xmode == SX_NORM || S.xmode == SX_REDUCE_NORM;
+  float* nws = reinterpret_cast<float*>(sm + L.nw);
+  if (norm && !reduce)  // the norm weights are read-only: their copy does not wait on anything
+    for (int i = 4 * threadIdx.x; i < S.dim; i += 4 * SP_CT)
+      *reinterpret_cast<float4*>(nws + i) = __ldg(reinterpret_cast<const float4*>(S.nw + i));
   if (reduce) {
     const unsigned epoch = ep0 + 1u + (unsigned)S.exch;
     const unsigned long long* img = A.exch[A.rank] + (size_t)(epoch & 1u) * (size_t)A.slot_elems;
     const int q4 = S.dim / 4, C = gridDim.x, b = blockIdx.x;
     const int lo = 4 * (int)((int64_t)q4 * b / C), hi = b == C - 1 ? S.dim : 4 * (int)((int64_t)q4 * (b + 1) / C);
     bool ok = !err_set(A.err);
-    for (int i = 4 * threadIdx.x; i < S.dim; i += 4 * SP_CT) {
-      // rank by rank (rank order: every rank sums the same way); a rank's four
-      // words are re-read only while one still carries an older epoch
-      float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+    // every rank's parts of this thread's 8-element groups (one per thread for
+    // vectors up to 3840 elements), summed in rank order (every rank sums the
+    // same way); a rank's eight words are re-read only while one still
+    // carries an older epoch
+    for (int i = 8 * threadIdx.x; i < S.dim; i += 8 * SP_CT) {
+      // the norm weights of these elements are loaded while the words are polled
+      float4 nw0 = make_float4(0.f, 0.f, 0.f, 0.f), nw1 = nw0;
+      if (norm) {
+        nw0 = __ldg(reinterpret_cast<const float4*>(S.nw + i));
+        nw1 = __ldg(reinterpret_cast<const float4*>(S.nw + i + 4));
+      }
+      float p[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int r = 0; r < A.world; ++r) {
         const unsigned long long* wp = img + (size_t)r * S.dim + i;
-        unsigned long long w0, w1, w2, w3;
+        unsigned long long w[8];
         for (uint32_t it = 0;; ++it) {
-          ld_words2(wp, w0, w1);
-          ld_words2(wp + 2, w2, w3);
-          const bool ready = (unsigned)(w0 >> 32) == epoch && (unsigned)(w1 >> 32) == epoch &&
-                             (unsigned)(w2 >> 32) == epoch && (unsigned)(w3 >> 32) == epoch;
+#pragma unroll
+          for (int c = 0; c < 8; c += 2) ld_words2(wp + c, w[c], w[c + 1]);
+          bool ready = true;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) ready = ready && (unsigned)(w[c] >> 32) == epoch;
           if (ready || !ok) break;
           if (it >= SP_SPIN || ((it & 255u) == 255u && err_set(A.err))) {
             atomicCAS(A.err, 0, SP_ERR_TP);  // the output is invalid; the kernel still runs to its end
             ok = false;
             break;
           }
-          __nanosleep(32);
+          if (it >= 64) __nanosleep(64);
         }
-        p.x += __uint_as_float((unsigned)w0);
-        p.y += __uint_as_float((unsigned)w1);
-        p.z += __uint_as_float((unsigned)w2);
-        p.w += __uint_as_float((unsigned)w3);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) p[c] += __uint_as_float((unsigned)w[c]);
       }
-      __threadfence();  // the words were seen: h_in's slice written before them is visible now
-      float4 v = __ldcg(reinterpret_cast<const float4*>(S.h_in + i));
-      v.x += p.x;
-      v.y += p.y;
-      v.z += p.z;
-      v.w += p.w;
-      *reinterpret_cast<float4*>(xr + i) = v;
-      if (i >= lo && i < hi) *reinterpret_cast<float4*>(S.h_out + i) = v;
+      const float4 a = make_float4(p[0], p[1], p[2], p[3]), b4 = make_float4(p[4], p[5], p[6], p[7]);
+      *reinterpret_cast<float4*>(xr + i) = a;
+      *reinterpret_cast<float4*>(xr + i + 4) = b4;
+      if (norm) {
+        *reinterpret_cast<float4*>(nws + i) = nw0;
+        *reinterpret_cast<float4*>(nws + i + 4) = nw1;
+      }
+      if (i >= lo && i < hi) *reinterpret_cast<float4*>(S.h_out + i) = a;
+      if (i + 4 >= lo && i + 4 < hi) *reinterpret_cast<float4*>(S.h_out + i + 4) = b4;
     }
-    sp_sync();
   }
+  if (reduce || norm) sp_sync();
   float ss = 0.f;
   const int total = SP_SPW * S.nk * 8;  // half-units (32 weights each), a multiple of 64
   for (int base = (threadIdx.x & ~31); base < total; base += SP_CT) {
@@ -259,7 +327,7 @@ __device__ void sp_stage_x(const StepStage& S, const StepArgs& A, const StepSmem
       if (live && (!norm && !reduce || gi < S.dim)) {
         f = reduce ? *reinterpret_cast<const float4*>(xr + gi) : __ldcg(reinterpret_cast<const float4*>(S.x + gi));
         if (norm) {
-          const float4 wv = __ldg(reinterpret_cast<const float4*>(S.nw + gi));
+          const float4 wv = *reinterpret_cast<const float4*>(nws + gi);
           ss = fmaf(f.x, f.x, fmaf(f.y, f.y, fmaf(f.z, f.z, fmaf(f.w, f.w, ss))));
           f.x *= wv.x;
           f.y *= wv.y;
@@ -422,7 +490,7 @@ __device__ __forceinline__ float sp_row_partial(const uint8_t* rowp, const uint8
 
 template <int QT>
 __device__ void sp_gemv(const StepStage& S, const StepArgs& A, const StepSmem& L, uint8_t* sm, uint32_t& seq,
-                        unsigned ep0) {
+                        unsigned ep0, int si) {
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bar);
   uint64_t* empty = full + A.S;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -433,6 +501,7 @@ __device__ void sp_gemv(const StepStage& S, const StepArgs& A, const StepSmem& L
 
   sp_stage_x<QT>(S, A, L, sm, ep0);
   sp_sync();
+  sp_stamp(A, si, 2);
   float yscale = 1.f;  // RMSNorm: 1 / sqrt(mean(x^2) + eps), applied to every output row
   if (norm) {
     const float* red = reinterpret_cast<const float*>(sm + L.red);
@@ -501,6 +570,7 @@ __device__ void sp_gemv(const StepStage& S, const StepArgs& A, const StepSmem& L
   }
   seq += (uint32_t)T;
   sp_sync();
+  sp_stamp(A, si, 3);
   const int tid = threadIdx.x;
   if (S.ymode == SY_SWIGLU) {
     for (int j = tid; 2 * j < rows; j += SP_CT) {
@@ -522,14 +592,19 @@ __device__ void sp_gemv(const StepStage& S, const StepArgs& A, const StepSmem& L
     const unsigned epoch = ep0 + 1u + (unsigned)S.exch;
     const unsigned long long tag = (unsigned long long)epoch << 32;
     const size_t at = (size_t)(epoch & 1u) * (size_t)A.slot_elems + (size_t)A.rank * S.n + r0;
-    __threadfence();  // this CTA's h_out slice (written while staging) before the words that announce it
+    // rank 0 adds the residual being updated; its rows [r0, r1) are the slice
+    // this CTA itself wrote (or the launch's input)
+    const float* res = A.rank == 0 ? S.h_in : nullptr;
     for (int q = tid; q < rows; q += SP_CT) {
       float acc = 0.f;
       for (int t = 0; t < S.nk; ++t) acc += part[q * S.nk + t];
-      const unsigned long long wv = tag | __float_as_uint(acc * yscale);
+      float v = acc * yscale;
+      if (res) v = __ldcg(res + r0 + q) + v;
+      const unsigned long long wv = tag | __float_as_uint(v);
       for (int p = 0; p < A.world; ++p) st_word(A.exch[p] + at + q, wv);
     }
   }
+  sp_stamp(A, si, 4);
 }
 
 // ---------------------------------------------------------------------------
@@ -544,11 +619,69 @@ __device__ __forceinline__ void sp_rope_cs(int64_t pos, int i, int half, float t
   s = sinf(angle);
 }
 
+// Scores q_g . k_p of one KV tile into s_s[g][p] (G <= GP query heads, GP a
+// power of two <= 8).  A warp pass takes 32 / GP positions: lane l holds its
+// HD / 32 dims of every head's q in registers and accumulates its part of all
+// 32 (head, position) products; one transpose-reduction (31 shuffles) then
+// leaves the total of pair l in lane l.  K rows are read with the lanes
+// across the row (conflict-free).
+template <int HD, int GP>
+__device__ __forceinline__ void sp_scores(const uint8_t* Ks, const float* q_s, float* s_s, int G, int np, int TP) {
+  constexpr int DPL = HD / 32, NP = 32 / GP;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float qr[GP][DPL];
+#pragma unroll
+  for (int g = 0; g < GP; ++g)
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) qr[g][j] = g < G ? q_s[g * HD + DPL * lane + j] : 0.f;
+  for (int p0 = warp * NP; p0 < np; p0 += SP_NC * NP) {
+    float v[32];  // index g * NP + pi
+#pragma unroll
+    for (int pi = 0; pi < NP; ++pi) {
+      float kf[DPL];
+      const int p = p0 + pi;
+      if (p < np) {
+        const __half2* kr = reinterpret_cast<const __half2*>(Ks + (size_t)p * HD * 2) + (DPL / 2) * lane;
+#pragma unroll
+        for (int j = 0; j < DPL / 2; ++j) {
+          const float2 f = __half22float2(kr[j]);
+          kf[2 * j] = f.x;
+          kf[2 * j + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) kf[j] = 0.f;
+      }
+#pragma unroll
+      for (int g = 0; g < GP; ++g) {
+        float d = 0.f;
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) d = fmaf(qr[g][j], kf[j], d);
+        v[g * NP + pi] = d;
+      }
+    }
+#pragma unroll
+    for (int st = 0; st < 5; ++st) {  // halves of 16, 8, 4, 2, 1 values
+      const int off = 16 >> st;
+      const bool up = lane & off;
+#pragma unroll
+      for (int i = 0; i < (16 >> st); ++i) {
+        const float send = up ? v[i] : v[i + (16 >> st)];
+        const float keep = up ? v[i + (16 >> st)] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    const int g = lane / NP, p = p0 + lane % NP;
+    if (g < G && p < np) s_s[g * (TP + 4) + p] = v[0];
+  }
+}
+
 template <int HD>
-__device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSmem& L, uint8_t* sm, uint32_t& seq) {
+__device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSmem& L, uint8_t* sm, uint32_t& seq,
+                             int si) {
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bar);
   uint64_t* empty = full + A.S;
-  constexpr int HALF = HD / 2, DPL = HD / 32;  // dims per lane in the score products
+  constexpr int HALF = HD / 2;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = S.hq / S.hkv;
   const int64_t pos = A.pos;
@@ -556,10 +689,12 @@ __device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSm
   int64_t t0, t1;
   if (!sp_attn_item(S, blockIdx.x, pos + 1, hk, t0, t1)) return;
   const int TP = S.tile;
+  const int splits = sp_attn_splits(S, pos + 1);
   float* q_s = reinterpret_cast<float*>(sm + L.attn);             // [G][HD], scaled by 1/sqrt(HD)
   float* s_s = q_s + G * HD;                                      // [G][TP + 4] scores / probabilities
   float* st_s = s_s + G * (TP + 4);                               // [3][G]: running max, sum, tile correction
-  __half* new_s = reinterpret_cast<__half*>(st_s + 3 * STEP_ATTN_MAX_GROUP);  // the new k | v row
+  float* w_s = st_s + 3 * STEP_ATTN_MAX_GROUP;                    // [G][splits] merge weights
+  __half* new_s = reinterpret_cast<__half*>(w_s + G * S.splits);  // the new k | v row
   const bool has_new = pos >= t0 && pos < t1;
   const float* row = S.qkv;
   const float scale = rsqrtf((float)HD);
@@ -599,6 +734,7 @@ __device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSm
     st_s[STEP_ATTN_MAX_GROUP + tid] = 0.f;
   }
   sp_sync();
+  sp_stamp(A, si, 2);
   // P.V accumulators: thread (g, pair) for g < G, pair < HALF
   const int pg = tid / HALF, pd = tid - pg * HALF;
   const bool pv = pg < G;
@@ -607,6 +743,7 @@ __device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSm
     const int np = (int)min((int64_t)TP, t1 - p0);
     bool ok = sp_wait_full(A, full, seq);
     ok = sp_wait_full(A, full, seq + 1) && ok;
+    if (p0 == t0) sp_stamp(A, si, 3);
     uint8_t* Ks = sm + L.ring + (size_t)(seq % A.S) * A.slot_bytes;
     uint8_t* Vs = sm + L.ring + (size_t)((seq + 1) % A.S) * A.slot_bytes;
     if (has_new && pos >= p0 && pos < p0 + np) {  // the copied row is the stale cache entry: use the new one
@@ -618,22 +755,10 @@ __device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSm
     }
     sp_sync();
     if (ok) {
-      // scores: warp per position, lanes over head dims
-      for (int p = warp; p < np; p += SP_NC) {
-        float kf[DPL];
-        const __half* kr = reinterpret_cast<const __half*>(Ks) + p * HD + DPL * lane;
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) kf[j] = __half2float(kr[j]);
-        for (int g = 0; g < G; ++g) {
-          const float* qg = q_s + g * HD + DPL * lane;
-          float d = 0.f;
-#pragma unroll
-          for (int j = 0; j < DPL; ++j) d = fmaf(qg[j], kf[j], d);
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-          if (lane == 0) s_s[g * (TP + 4) + p] = d;
-        }
-      }
+      if (G == 1) sp_scores<HD, 1>(Ks, q_s, s_s, G, np, TP);
+      else if (G == 2) sp_scores<HD, 2>(Ks, q_s, s_s, G, np, TP);
+      else if (G <= 4) sp_scores<HD, 4>(Ks, q_s, s_s, G, np, TP);
+      else sp_scores<HD, 8>(Ks, q_s, s_s, G, np, TP);
     }
     sp_sync();
     // online softmax per head: warp g
@@ -667,6 +792,7 @@ __device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSm
       acc1 *= corr;
       const float* pr = s_s + pg * (TP + 4);
       const __half2* vr = reinterpret_cast<const __half2*>(Vs) + pd;
+#pragma unroll 4
       for (int p = 0; p < np; ++p) {
         const float2 v = __half22float2(vr[p * HALF]);
         acc0 = fmaf(pr[p], v.x, acc0);
@@ -678,10 +804,11 @@ __device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSm
     sp_release(A, empty, seq + 1);
     seq += 2;
   }
+  sp_stamp(A, si, 4);
   // this split's partial (max, sum, acc[HD]) per query head
-  const int sp = blockIdx.x - hk * S.splits;
+  const int sp = blockIdx.x - hk * splits;
   const int64_t pstride = HD + 4;
-  float* part = A.attn_part + ((int64_t)hk * S.splits + sp) * G * pstride;
+  float* part = A.attn_part + ((int64_t)hk * splits + sp) * G * pstride;
   if (pv) {
     part[pg * pstride + 4 + 2 * pd] = acc0;
     part[pg * pstride + 4 + 2 * pd + 1] = acc1;
@@ -695,7 +822,7 @@ __device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSm
   __shared__ int last;
   if (tid == 0) {
     unsigned* ctr = A.sync + STEP_SYNC_ATTN + hk;
-    last = atomicAdd(ctr, 1u) == (unsigned)S.splits - 1;
+    last = atomicAdd(ctr, 1u) == (unsigned)splits - 1;
     if (last) {
       *ctr = 0u;  // ready for the next attention stage
       __threadfence();
@@ -703,26 +830,42 @@ __device__ void sp_attention(const StepStage& S, const StepArgs& A, const StepSm
   }
   sp_sync();
   if (!last) return;
-  // the last split of this KV head merges every split's partial into the output
-  const float* base = A.attn_part + (int64_t)hk * S.splits * G * pstride;
+  // the last split of this KV head merges every split's partial into the
+  // output: per head (warp g) the weights e^(m_j - M) / L of the splits, then
+  // per output element the weighted sum of the splits' accumulators
+  const float* base = A.attn_part + (int64_t)hk * splits * G * pstride;
+  if (warp < G) {
+    float M = -INFINITY;
+    for (int j = lane; j < splits; j += 32) M = fmaxf(M, __ldcg(base + ((int64_t)j * G + warp) * pstride));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float lsum = 0.f;
+    for (int j = lane; j < splits; j += 32) {
+      const float* pj = base + ((int64_t)j * G + warp) * pstride;
+      const float w = __expf(__ldcg(pj) - M);  // empty splits: exp(-inf) = 0
+      w_s[warp * S.splits + j] = w;
+      lsum = fmaf(__ldcg(pj + 1), w, lsum);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    const float inv = 1.f / lsum;
+    for (int j = lane; j < splits; j += 32) w_s[warp * S.splits + j] *= inv;
+  }
+  sp_sync();
   for (int e = tid; e < G * HD; e += SP_CT) {
     const int g = e / HD, d = e - g * HD;
-    float M = -INFINITY;
-    for (int j = 0; j < S.splits; ++j) M = fmaxf(M, __ldcg(base + ((int64_t)j * G + g) * pstride));
-    float lsum = 0.f, o = 0.f;
-    for (int j = 0; j < S.splits; ++j) {
-      const float* pj = base + ((int64_t)j * G + g) * pstride;
-      const float w = __expf(__ldcg(pj) - M);  // empty splits: exp(-inf) = 0
-      lsum = fmaf(__ldcg(pj + 1), w, lsum);
-      o = fmaf(__ldcg(pj + 4 + d), w, o);
-    }
-    S.out[(int64_t)(hk * G + g) * HD + d] = o / lsum;
+    const float* wg = w_s + g * S.splits;
+    const float* pd0 = base + (int64_t)g * pstride + 4 + d;
+    float o = 0.f;
+#pragma unroll 8
+    for (int j = 0; j < splits; ++j) o = fmaf(wg[j], __ldcg(pd0 + (int64_t)j * G * pstride), o);
+    S.out[(int64_t)(hk * G + g) * HD + d] = o;
   }
 }
 
 __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const StepArgs A) {
   extern __shared__ __align__(128) uint8_t sm[];
-  const StepSmem L(A.S, A.slot_bytes, A.nk_max, A.rows_max, A.xr_floats, A.attn_bytes);
+  const StepSmem L(A.S, A.slot_bytes, A.nk_max, A.rows_max, A.xr_floats, A.nw_floats, A.attn_bytes);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + L.bar);
   uint64_t* empty = full + A.S;
   if (threadIdx.x == 0) {
@@ -744,15 +887,18 @@ __global__ void __launch_bounds__(STEP_THREADS, 1) step_kernel(const StepArgs A)
   const unsigned C = gridDim.x;
   for (int si = 0; si < A.nstages; ++si) {
     const StepStage& S = A.stages[si];
+    sp_stamp(A, si, 0);
     if (S.barrier) sp_grid_sync(A.sync + STEP_SYNC_BAR, ++nbar * C, A.err);
+    sp_stamp(A, si, 1);
     if (S.kind == STEP_GEMV) {
-      if (S.qt == GGUF_Q4_K) sp_gemv<GGUF_Q4_K>(S, A, L, sm, seq, ep0);
-      else sp_gemv<GGUF_Q6_K>(S, A, L, sm, seq, ep0);
+      if (S.qt == GGUF_Q4_K) sp_gemv<GGUF_Q4_K>(S, A, L, sm, seq, ep0, si);
+      else sp_gemv<GGUF_Q6_K>(S, A, L, sm, seq, ep0, si);
     } else {
-      if (S.hd == 128) sp_attention<128>(S, A, L, sm, seq);
-      else sp_attention<64>(S, A, L, sm, seq);
+      if (S.hd == 128) sp_attention<128>(S, A, L, sm, seq, si);
+      else sp_attention<64>(S, A, L, sm, seq, si);
     }
     sp_sync();
+    sp_stamp(A, si, 5);
   }
   // the last CTA out resets the barrier counters and publishes the epoch
   if (threadIdx.x == 0) {
@@ -773,7 +919,7 @@ cudaError_t step_init_device() {
 }
 
 cudaError_t launch_step(const StepArgs& a, int grid, cudaStream_t s) {
-  const StepSmem L(a.S, a.slot_bytes, a.nk_max, a.rows_max, a.xr_floats, a.attn_bytes);
+  const StepSmem L(a.S, a.slot_bytes, a.nk_max, a.rows_max, a.xr_floats, a.nw_floats, a.attn_bytes);
   if (L.end > (size_t)STEP_MAX_SMEM) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid);

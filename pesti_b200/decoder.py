@@ -83,6 +83,7 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "kq_step_linear": [P, P, I, P, P, I64, F, P, I, P, I],
         "kq_step_attention": [P, P, P, P, P, I, I, I, I64, F],
         "kq_step_run": [P, I64, I],
+        "kq_step_trace": [P, P, Z],
         "kq_step_destroy": [P],
     }
     for name, args in sig.items():
@@ -146,7 +147,7 @@ class Decoder:
     def __init__(self, cfg: DecoderConfig, ctx: "kq.Context", batch: int, context_len: int, max_new: int = 8,
                  world: int = 1, rank: int = 0, tp: Optional["kq.TensorParallel"] = None, seed: int = 0,
                  swiglu_mode: int = SWIGLU_REFERENCE, kv_scale: float = 1.0, keep_raw: bool = False,
-                 fused: bool = True, prefetch: bool = False, step_kernel: bool = True):
+                 fused: bool = True, prefetch: bool = False, step_kernel: bool = False):
         import torch
         if cfg.heads % world or cfg.kv_heads % world:
             raise ValueError(f"{cfg.name}: {cfg.heads} query / {cfg.kv_heads} KV heads do not split over {world}")
@@ -168,8 +169,10 @@ class Decoder:
         # paths that run it (one GPU or the column split at batch 1); otherwise
         # [gate block | up block] for the separate SwiGLU kernel
         self.pairs = self.fused and (world == 1 or self.col_split)
-        # batch 1: the whole step as one persistent kernel (kq_step_*), on one
-        # GPU or with the column split; otherwise one kernel per operation
+        # batch 1, opt-in: the whole step as one persistent kernel (kq_step_*),
+        # on one GPU or with the column split; otherwise one kernel per
+        # operation (measured faster: the per-operation kernels overlap each
+        # launch's start-up with the previous kernel's tail)
         self.step_kernel = step_kernel and self.fused and (world == 1 or self.col_split)
         self._step = None
         self.lib = _bind(ctx.lib)
@@ -458,12 +461,14 @@ class Decoder:
         self._step = h
         if self.h2 is None:
             self.h2 = torch.zeros_like(self.h)
+        # the residual alternates between two buffers: a RESIDUAL stage writes the
+        # new residual to the other one, the next PARTIAL stage updates it
         cur, nxt = self.h, self.h2
         pending = False
         c = lambda rc, what: self.ctx.check(rc, what)  # noqa: E731
         for L in self.layers:
             if pending:
-                c(lib.kq_step_linear(h, L["qkv"].handle, STEP_IN_RESIDUAL_NORM, ptr(cur), ptr(L["attn_norm"]), D,
+                c(lib.kq_step_linear(h, L["qkv"].handle, STEP_IN_RESIDUAL_NORM, None, ptr(L["attn_norm"]), D,
                                      cfg.eps, ptr(nxt), STEP_OUT_STORE, ptr(self.qkv), 0), "step qkv")
                 cur, nxt = nxt, cur
             else:
@@ -472,18 +477,18 @@ class Decoder:
             out = self.attn_r if self.col_split else self.attn
             c(lib.kq_step_attention(h, ptr(self.qkv), ptr(L["k"]), ptr(L["v"]), ptr(out), self.hq, self.hkv, hd,
                                     self.max_seq, cfg.theta), "step attention")
-            c(lib.kq_step_linear(h, L["o"].handle, STEP_IN_PLAIN, ptr(out), None, 0, 0.0, None, STEP_OUT_PARTIAL,
+            c(lib.kq_step_linear(h, L["o"].handle, STEP_IN_PLAIN, ptr(out), None, 0, 0.0, ptr(cur), STEP_OUT_PARTIAL,
                                  None, 0), "step o")
-            c(lib.kq_step_linear(h, L["gu"].handle, STEP_IN_RESIDUAL_NORM, ptr(cur), ptr(L["ffn_norm"]), D, cfg.eps,
+            c(lib.kq_step_linear(h, L["gu"].handle, STEP_IN_RESIDUAL_NORM, None, ptr(L["ffn_norm"]), D, cfg.eps,
                                  ptr(nxt), STEP_OUT_SWIGLU, ptr(self.s_r if self.col_split else self.s),
                                  self.swiglu_mode), "step gate/up")
             cur, nxt = nxt, cur
             c(lib.kq_step_linear(h, L["down"].handle, STEP_IN_PLAIN, ptr(self.s_r if self.col_split else self.s),
-                                 None, 0, 0.0, None, STEP_OUT_PARTIAL, None, 0), "step down")
+                                 None, 0, 0.0, ptr(cur), STEP_OUT_PARTIAL, None, 0), "step down")
             pending = True
         logits = self.logits_r if self.world > 1 else self.logits
         mode = STEP_IN_RESIDUAL_NORM if self.final_norm is not None else STEP_IN_RESIDUAL
-        c(lib.kq_step_linear(h, self.head.handle, mode, ptr(cur), ptr(self.final_norm), D, cfg.eps, ptr(nxt),
+        c(lib.kq_step_linear(h, self.head.handle, mode, None, ptr(self.final_norm), D, cfg.eps, ptr(nxt),
                              STEP_OUT_STORE, ptr(logits), 0), "step head")
         self._step_in = self.h  # the embedding goes here; the residual ends in `nxt`
 

@@ -68,9 +68,9 @@ def test_a_program_of_linears_matches_the_oracle(gpu_ctx, step_env):
                            ptr(y1), 0), "norm -> store")
     chk(lib.kq_step_linear(h, ws[1].handle, dec.STEP_IN_PLAIN, ptr(y1), None, 0, 0.0, None, dec.STEP_OUT_STORE,
                            ptr(y2), 0), "plain -> store")
-    chk(lib.kq_step_linear(h, ws[2].handle, dec.STEP_IN_PLAIN, ptr(y2), None, 0, 0.0, None, dec.STEP_OUT_PARTIAL,
-                           None, 0), "plain -> partial")
-    chk(lib.kq_step_linear(h, ws[3].handle, dec.STEP_IN_RESIDUAL_NORM, ptr(hd), ptr(n4), D, eps, ptr(h2),
+    chk(lib.kq_step_linear(h, ws[2].handle, dec.STEP_IN_PLAIN, ptr(y2), None, 0, 0.0, ptr(hd), dec.STEP_OUT_PARTIAL,
+                           None, 0), "plain -> partial update of h")
+    chk(lib.kq_step_linear(h, ws[3].handle, dec.STEP_IN_RESIDUAL_NORM, None, ptr(n4), D, eps, ptr(h2),
                            dec.STEP_OUT_STORE, ptr(y4), 0), "residual + norm -> store")
     for _ in range(3):  # repeated runs: the sync words and the exchange epoch carry over
         y4.zero_()
@@ -99,7 +99,7 @@ def test_the_builder_rejects_bad_programs(gpu_ctx, step_env):
     # nothing to run yet
     assert lib.kq_step_run(h, 0, 0) == kq.KQ_ERR_STATE
     # a residual input with no partial output before it
-    assert lib.kq_step_linear(h, w.handle, dec.STEP_IN_RESIDUAL, ptr(x), None, 64, 0.0, ptr(h2),
+    assert lib.kq_step_linear(h, w.handle, dec.STEP_IN_RESIDUAL, None, None, 64, 0.0, ptr(h2),
                               dec.STEP_OUT_STORE, ptr(y), 0) == kq.KQ_ERR_STATE
     # weights outside the step kernel's types, bad modes, misaligned input
     assert lib.kq_step_linear(h, wl.handle, dec.STEP_IN_PLAIN, ptr(x), None, 0, 0.0, None, dec.STEP_OUT_STORE,
