@@ -66,11 +66,11 @@ def test_decode_steps_match_the_restated_reference(gpu_ctx, cfg, mode, batch, fu
     model.close()
 
 
-@pytest.mark.parametrize("batch", [1, 2])
-def test_decode_step_replays_from_a_cuda_graph(gpu_ctx, batch):
+@pytest.mark.parametrize("batch,step", [(1, False), (1, True), (2, False)], ids=["b1", "b1-step-kernel", "b2"])
+def test_decode_step_replays_from_a_cuda_graph(gpu_ctx, batch, step):
     import torch
     cfg = LLAMA_TINY
-    model = dec.Decoder(cfg, gpu_ctx, batch, 20, max_new=2, seed=6)
+    model = dec.Decoder(cfg, gpu_ctx, batch, 20, max_new=2, seed=6, step_kernel=step)
     model.tokens.copy_(torch.tensor([1, 2][:batch], dtype=torch.int32))
     s = torch.cuda.Stream()
     gpu_ctx.set_stream(s.cuda_stream)
