@@ -491,9 +491,12 @@ def measure_gemv(args, workload, m, rank, world, local_rank, steps, warmup):
         xn, yn = xh.numpy(), [y.numpy() for y in yh]
 
         def step_host():
+            # every call queues H2D x, its kernels and D2H y (KQ_ASYNC); one wait per step
             for w, y in zip(weights, yn):
-                w.linear(xn, m, y)  # synchronous: H2D x, kernels, D2H y
-        api = "kq_linear_f32 with host pointers (pinned), synchronous per call"
+                w.linear(xn, m, y, queue=True)
+            ctx.synchronize()
+        api = ("kq_linear_f32 with host pointers (pinned): each call queues its H2D copy of x, kernels and D2H "
+               "copy of y (KQ_ASYNC), one kq_ctx_synchronize per step")
     else:
         xd = torch.empty_like(x)
 

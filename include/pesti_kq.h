@@ -17,7 +17,9 @@
  *  - Pointer arguments of the compute entries are host pointers unless
  *    KQ_DEVICE_PTRS is set, in which case they are device pointers on the
  *    context's device and the call is stream-ordered (asynchronous unless
- *    KQ_SYNC is also set).  Host-pointer calls are synchronous.
+ *    KQ_SYNC is also set).  Host-pointer calls are synchronous, unless
+ *    KQ_ASYNC queues them (the copies through the context's staging buffers
+ *    are ordered on its stream, so queued calls may follow one another).
  */
 #ifndef PESTI_KQ_H
 #define PESTI_KQ_H
@@ -61,6 +63,10 @@ enum kq_type {
 #define KQ_DEVICE_PTRS 1 /* x / bias / y are device pointers (async)      */
 #define KQ_SYNC 2        /* synchronise the context stream before return  */
 #define KQ_ACCUMULATE 4  /* kq_tp_allgather_f32: add into y instead of overwrite */
+#define KQ_ASYNC 8       /* kq_linear_f32 / kq_linear_bf16 with host pointers:  */
+                         /* queue the copies and kernels without waiting; the   */
+                         /* caller keeps x, bias and y alive (pinned memory     */
+                         /* lets the copies overlap) until kq_ctx_synchronize   */
 
 /* kernel families for GGUF weights with f32 activations (kq_ctx_set_path) */
 #define KQ_PATH_AUTO 0    /* default: DP4A m = 1; Q4_K IMMA m <= 64; Q6_K    */

@@ -596,7 +596,9 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
                        float* y, int flags, bool bf16) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!w) return fail(ctx, KQ_ERR_INVALID_ARG, "weight is null");
-  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
+  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC | KQ_ASYNC)) return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
+  if ((flags & KQ_ASYNC) && (flags & (KQ_DEVICE_PTRS | KQ_SYNC)))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "KQ_ASYNC applies to host pointers without KQ_SYNC (flags 0x%x)", flags);
   if (w->device != ctx->device)
     return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device, ctx->device);
   if (m < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "negative m");
@@ -680,7 +682,7 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
     e = cudaMemcpyAsync(y, ctx->ybuf, (size_t)(m * n * 4), cudaMemcpyDeviceToHost, s);
     if (e != cudaSuccess) return cuda_fail(ctx, e, "copy y to host");
   }
-  if (!dev || (flags & KQ_SYNC)) return finish_sync(ctx, "linear");
+  if ((!dev && !(flags & KQ_ASYNC)) || (flags & KQ_SYNC)) return finish_sync(ctx, "linear");
   return KQ_OK;
 }
 

@@ -50,6 +50,7 @@ KQ_HOST_PTRS = 0
 KQ_DEVICE_PTRS = 1
 KQ_SYNC = 2
 KQ_ACCUMULATE = 4
+KQ_ASYNC = 8
 
 KQ_PATH_AUTO = 0
 KQ_PATH_TCGEN05 = 1
@@ -298,8 +299,12 @@ class Weight:
         w.kq_type, w.out_features, w.in_features, w.device_bytes = kt.value, n.value, k.value, dev_bytes.value
         return w
 
-    def linear(self, x, m: int, y, bias=None, device_ptrs: bool = False, sync: bool = False) -> None:
-        flags = (KQ_DEVICE_PTRS if device_ptrs else KQ_HOST_PTRS) | (KQ_SYNC if sync else 0)
+    def linear(self, x, m: int, y, bias=None, device_ptrs: bool = False, sync: bool = False,
+               queue: bool = False) -> None:
+        """y = x . W^T (+bias).  Host arrays are copied in and out synchronously,
+        unless queue=True (KQ_ASYNC): then the call only queues its copies and
+        kernels, and x, bias and y must stay alive until Context.synchronize()."""
+        flags = (KQ_DEVICE_PTRS if device_ptrs else KQ_HOST_PTRS) | (KQ_SYNC if sync else 0) | (KQ_ASYNC if queue else 0)
         rc = self.ctx.lib.kq_linear_f32(self.ctx.handle, self.handle, _ptr(x), m, _ptr(bias), _ptr(y), flags)
         self.ctx.check(rc, "kq_linear_f32")
 

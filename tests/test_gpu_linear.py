@@ -328,3 +328,28 @@ def test_invalid_arguments_report_status(gpu_ctx):
     assert rc == kq.KQ_ERR_INVALID_ARG
     rc = gpu_ctx.lib.kq_linear_f32(gpu_ctx.handle, w.handle, None, 1, None, None, 0x40)
     assert rc == kq.KQ_ERR_INVALID_ARG
+
+
+def test_queued_host_pointer_calls_match_synchronous_ones(gpu_ctx):
+    """KQ_ASYNC: host-pointer calls queued back to back through the same
+    staging buffers, one synchronize at the end, give the synchronous results
+    (stream order keeps each call's staging copies apart)."""
+    import torch
+    n, k, m = 1024, 4096, 3
+    raws = [synthetic.gguf_weight(kt, n, k, seed=40 + i) for i, kt in enumerate((kq.KQ_GGUF_Q4_K, kq.KQ_GGUF_Q6_K,
+                                                                                   kq.KQ_GGUF_Q4_K))]
+    ws = [kq.Weight(gpu_ctx, kt, r, n, k) for kt, r in zip((kq.KQ_GGUF_Q4_K, kq.KQ_GGUF_Q6_K, kq.KQ_GGUF_Q4_K), raws)]
+    xs = [torch.from_numpy(synthetic.activations(m, k, seed=50 + i)).pin_memory() for i in range(3)]
+    ys = [torch.full((m, n), float("nan")).pin_memory() for _ in range(3)]
+    for w, x, y in zip(ws, xs, ys):
+        w.linear(x.numpy(), m, y.numpy(), queue=True)
+    gpu_ctx.synchronize()
+    for w, x, y in zip(ws, xs, ys):
+        ref = np.empty((m, n), np.float32)
+        w.linear(x.numpy(), m, ref)
+        assert np.array_equal(y.numpy(), ref)
+    rc = gpu_ctx.lib.kq_linear_f32(gpu_ctx.handle, ws[0].handle, None, 1, None, None,
+                                   kq.KQ_DEVICE_PTRS | kq.KQ_ASYNC)
+    assert rc == kq.KQ_ERR_INVALID_ARG
+    for w in ws:
+        w.free()
