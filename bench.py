@@ -102,6 +102,8 @@ def parse():
     p.add_argument("--path", choices=["auto", "tcgen05", "mma", "dp4a", "imma"], default="auto",
                    help="kernel family for the GEMV (auto: dp4a m=1, integer MMA / mma.sync m<=64, tcgen05 above)")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--layout", choices=["gguf", "legacy"], default="gguf",
+                   help="GEMV workloads: GGUF superblocks, or the reference's own 28 / 42-byte 16-weight blocks")
     p.add_argument("--no-extras", action="store_true", help="default line only, without its sub-records")
     p.add_argument("--prefetch", action="store_true",
                    help="each GEMV prefetches the next one's weight into L2 (kq_ctx_prefetch_next)")
@@ -122,7 +124,10 @@ def kernel_path(name):
 
 
 def algorithmic_bytes(qtype, n, k, m):
-    wbytes = n * (k // 256) * (144 if qtype == 12 else 210)
+    if qtype in (112, 114):  # the reference's blocks: 28 / 42 bytes per 16 weights
+        wbytes = n * ((k + 15) // 16) * (28 if qtype == 112 else 42)
+    else:
+        wbytes = n * (k // 256) * (144 if qtype == 12 else 210)
     return wbytes, wbytes + m * k * 4 + m * n * 4
 
 
@@ -279,30 +284,31 @@ class CpuReference:
         self.data = synthetic.legacy_weight(self.legacy, self.n, self.k, seed=seed)
         self.x = synthetic.activations(m, self.k, seed=seed + 1)
 
-    def run(self, row0, rows, all_cores=False):
+    def run(self, row0, rows, all_cores=False, legacy_bytes=False):
         """Forward over rows [row0, row0+rows); returns (seconds, algorithmic
-        bytes).  all_cores: the same algorithm threaded over output rows."""
+        bytes: of the GGUF workload, or of the legacy blocks themselves).
+        all_cores: the same algorithm threaded over output rows."""
         sub = self.data[row0:row0 + rows]
         t0 = time.perf_counter()
         self.oracle.legacy_forward(self.legacy, sub, self.k, rows, self.x, self.m,
                                    nthreads=os.cpu_count() or 1, threads_over_batch=not all_cores)
         dt = time.perf_counter() - t0
-        return dt, algorithmic_bytes(self.qtype, rows, self.k, self.m)[1]
+        return dt, algorithmic_bytes(self.legacy if legacy_bytes else self.qtype, rows, self.k, self.m)[1]
 
 
-def cpu_baseline(workload, m, budget_s=12.0):
+def cpu_baseline(workload, m, budget_s=12.0, legacy=False):
     ref = CpuReference(workload, m)
     n, k = ref.n, ref.k
     total_t, total_b, passes = 0.0, 0, 0
     while total_t < budget_s and passes < 64:
-        dt, alg = ref.run(0, n)
+        dt, alg = ref.run(0, n, legacy_bytes=legacy)
         total_t += dt
         total_b += alg
         passes += 1
     # the same algorithm with its output rows spread over every core
     at, ab, ap = 0.0, 0, 0
     while at < budget_s / 4 and ap < 256:
-        dt, alg = ref.run(0, n, all_cores=True)
+        dt, alg = ref.run(0, n, all_cores=True, legacy_bytes=legacy)
         at += dt
         ab += alg
         ap += 1
@@ -310,7 +316,7 @@ def cpu_baseline(workload, m, budget_s=12.0):
     return {"value": round(total_b / total_t / 1e9, 4), "unit": "GB/s", "cores": cores, "kind": "port",
             "sample": f"{passes} full passes of QuantizedLinear::forward (full f32 dequant + sequential "
                       f"dot, threads over batch rows) over a {n}x{k} pesti-legacy weight at M={m}; "
-                      f"bytes counted as the GGUF workload's",
+                      f"bytes counted as the {'legacy blocks' if legacy else 'GGUF workload'}'s",
             "host_cpus": os.cpu_count(),
             "all_cores": {"value": round(ab / at / 1e9, 4), "unit": "GB/s", "cores": os.cpu_count() or 1,
                           "sample": f"{ap} passes of the same algorithm threaded over output rows"}}
@@ -420,7 +426,11 @@ def measure_gemv(args, workload, m, rank, world, local_rank, steps, warmup):
     from pesti_b200 import decoder as dec, kq, synthetic
 
     dev = torch.device("cuda", local_rank)
-    qtype, _, n, k, desc = WORKLOADS[workload]
+    qtype, legacy_type, n, k, desc = WORKLOADS[workload]
+    legacy = getattr(args, "layout", "gguf") == "legacy"
+    if legacy:
+        qtype = legacy_type
+        desc = desc.replace("Q6_K", "Q6_K (reference 42-byte blocks)").replace("Q4_K", "Q4_K (reference 28-byte blocks)")
     wbytes, alg = algorithmic_bytes(qtype, n, k, m)
     nw = num_weights(wbytes, world)
     r0, r1 = kq.shard_rows(n, world, rank)
@@ -428,7 +438,10 @@ def measure_gemv(args, workload, m, rank, world, local_rank, steps, warmup):
     tp = kq.TensorParallel(ctx, world, rank, max_out_elems=m * n) if world > 1 else None
     weights = []
     for i in range(nw):  # the same seeded weights on every rank; each keeps its rows
-        full = dec.gguf_weight_device(qtype, n, k, seed=1000 + i, device=dev)
+        if legacy:
+            full = torch.from_numpy(synthetic.legacy_weight(qtype, n, k, seed=1000 + i)).to(dev)
+        else:
+            full = dec.gguf_weight_device(qtype, n, k, seed=1000 + i, device=dev)
         weights.append(kq.Weight(ctx, qtype, full[r0:r1].contiguous(), r1 - r0, k))
         del full
     x = torch.from_numpy(synthetic.activations(m, k, seed=7)).to(dev)
@@ -529,7 +542,7 @@ def measure_gemv(args, workload, m, rank, world, local_rank, steps, warmup):
         "one_kernel": launches_per_step == nw,
         "e2e": nw * alg * e2e_steps / e2e_s / 1e9, "e2e_api": api,
         "h2d": m * k * 4 if tp is not None else nw * m * k * 4, "d2h": nw * m * n * 4, "clocks": clocks,
-        "rows_per_rank": r1 - r0,
+        "rows_per_rank": r1 - r0, "legacy": legacy,
     }
     del plain, bracketed
     for w in weights:
@@ -556,13 +569,13 @@ def gemv_roofline(res, world):
             "kernel_us": round(kernel_us, 3), "kernel_us_isolated": round(res["kernel_us_isolated"], 3),
             "frac_isolated": round(rank_alg / (res["kernel_us_isolated"] * 1e-6) / 1e9 / peak, 4),
             "algorithmic_bytes_per_launch": int(rank_alg),
-            "traffic": profiled_traffic(res["workload"], res["m"]) if world == 1 else None}
+            "traffic": profiled_traffic(res["workload"], res["m"]) if world == 1 and not res["legacy"] else None}
 
 
 def run_gemv(args, rank, world, local_rank):
     res = measure_gemv(args, args.workload, args.m, rank, world, local_rank, args.steps, args.warmup)
     extras = {}
-    if args.workload == "q6k-gemv" and args.m == 1 and not args.no_extras:
+    if args.workload == "q6k-gemv" and args.m == 1 and args.layout == "gguf" and not args.no_extras:
         extras = measure_extras(args, rank, world, local_rank)
     if rank != 0:
         return 0
@@ -579,6 +592,7 @@ def run_gemv(args, rank, world, local_rank):
         "higher_is_better": True, "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded random GGUF superblocks, x ~ N(0,1))",
         "config": {"workload": f"{args.workload}: {res['desc']}, M={m}, {nw} distinct weights per step",
+                   "layout": args.layout,
                    "rows": res["n"], "k": res["k"], "m": m, "weights_per_step": nw,
                    "weight_bytes_per_gemv": res["wbytes"], "algorithmic_bytes_per_gemv": res["alg"],
                    "l2": f"inputs larger than L2 ({nw * res['wbytes'] / world / 1e6:.0f} MB of weights per rank "
@@ -595,7 +609,7 @@ def run_gemv(args, rank, world, local_rank):
     }
     line.update(extras)
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.workload, m)
+        line["cpu_baseline"] = cpu_baseline(args.workload, m, legacy=args.layout == "legacy")
     print(json.dumps(line), flush=True)
     return 0
 
