@@ -123,9 +123,43 @@ __global__ void q6k_relayout_kernel(const uint8_t* __restrict__ raw, int64_t n, 
   }
 }
 
-// Legacy linear: one warp per output row, lanes stride over 16-weight blocks.
-// Not a tuned path: it exists so the reference's own block layout can be run
-// on the device and compared with its CPU forward.
+// Legacy linear: one warp per output row; lane l takes 16-weight blocks l,
+// l + 32, ... and loads each block's fields once (Q4_K: d, delta, the two
+// nibble words and h0 / h1 as four 32-bit words; Q6_K: d, the four scales,
+// the low-bit and flag words as 16-bit pieces -- its blocks start on 2-byte
+// boundaries), decodes its 16 values in registers with the CPU association,
+// and multiplies them with the activations (f32 accumulate).  A warp's 32
+// blocks are one contiguous run of the row, so the loads are coalesced.
+__device__ __forceinline__ void legacy_q4k_block(const uint8_t* p, float (&v)[16]) {
+  const uint32_t w0 = *reinterpret_cast<const uint32_t*>(p);       // d | delta
+  const uint32_t lo = *reinterpret_cast<const uint32_t*>(p + 4);   // elements 0..7
+  const uint32_t hi = *reinterpret_cast<const uint32_t*>(p + 8);   // elements 8..15
+  const uint32_t hh = *reinterpret_cast<const uint32_t*>(p + 12);  // h0 | h1
+  const float d = f16_bits_to_f32((uint16_t)(w0 & 0xffff)), delta = f16_bits_to_f32((uint16_t)(w0 >> 16));
+  const float t0 = __fmul_rn(delta, f16_bits_to_f32((uint16_t)(hh & 0xffff)));
+  const float t1 = __fmul_rn(delta, f16_bits_to_f32((uint16_t)(hh >> 16)));
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    v[e] = __fadd_rn(__fmul_rn(t0, __fsub_rn((float)((lo >> (4 * e)) & 15u), 4.0f)), d);
+    v[8 + e] = __fadd_rn(__fmul_rn(t1, __fsub_rn((float)((hi >> (4 * e)) & 15u), 4.0f)), d);
+  }
+}
+__device__ __forceinline__ void legacy_q6k_block(const uint8_t* p, float (&v)[16]) {
+  const uint16_t* h = reinterpret_cast<const uint16_t*>(p);
+  const float d = f16_bits_to_f32(h[0]);
+  float sc[4];
+#pragma unroll
+  for (int s = 0; s < 4; ++s) sc[s] = f16_bits_to_f32(h[1 + s]);
+  const uint32_t ql = (uint32_t)h[5] | ((uint32_t)h[6] << 16);  // bytes 10..13: 2 low bits per element
+  const uint32_t fl = (uint32_t)h[9] | ((uint32_t)h[10] << 16); // bytes 18..21: 2 flag bits per element
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int qlow = (ql >> (2 * e)) & 3, flag = (fl >> (2 * e)) & 3;
+    const int q = qlow + 4 * (flag == 0 ? 0 : flag - 1);
+    v[e] = __fmul_rn(__fmul_rn(d, __fsub_rn((float)q, 32.0f)), sc[e >> 2]);
+  }
+}
+
 template <int M>
 __global__ void __launch_bounds__(256) legacy_gemv_kernel(DevWeight w, const float* __restrict__ x,
                                                           const float* __restrict__ bias,
@@ -134,24 +168,40 @@ __global__ void __launch_bounds__(256) legacy_gemv_kernel(DevWeight w, const flo
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= w.n) return;
   const uint8_t* rp = w.q + row * w.row_bytes;
+  const bool q6 = w.type == LEGACY_Q6_K;
+  const int bs = q6 ? 42 : 28;
   float acc[M];
 #pragma unroll
   for (int mi = 0; mi < M; ++mi) acc[mi] = 0.f;
-  const int64_t nblk = (w.k + 15) / 16;
-  for (int64_t b = lane; b < nblk; b += 32) {
+  const int64_t nfull = w.k / 16;
+  const bool x4 = (w.k & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  for (int64_t b = lane; b < nfull; b += 32) {
     float v[16];
-#pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      const int64_t i = b * 16 + e;
-      v[e] = (i < w.k) ? (w.type == LEGACY_Q6_K ? legacy_q6k_value(rp, i) : legacy_q4k_value(rp, w.k, i))
-                       : 0.f;
-    }
+    if (q6) legacy_q6k_block(rp + b * bs, v);
+    else legacy_q4k_block(rp + b * bs, v);
 #pragma unroll
     for (int mi = 0; mi < M; ++mi) {
       const float* xr = x + mi * w.k + b * 16;
+      if (x4) {  // rows of x start on 16-byte boundaries
 #pragma unroll
-      for (int e = 0; e < 16; ++e)
-        if (b * 16 + e < w.k) acc[mi] = fmaf(v[e], __ldg(xr + e), acc[mi]);
+        for (int j = 0; j < 4; ++j) {
+          const float4 xv = __ldg(reinterpret_cast<const float4*>(xr) + j);
+          acc[mi] = fmaf(v[4 * j], xv.x, acc[mi]);
+          acc[mi] = fmaf(v[4 * j + 1], xv.y, acc[mi]);
+          acc[mi] = fmaf(v[4 * j + 2], xv.z, acc[mi]);
+          acc[mi] = fmaf(v[4 * j + 3], xv.w, acc[mi]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) acc[mi] = fmaf(v[e], __ldg(xr + e), acc[mi]);
+      }
+    }
+  }
+  if (lane == 0 && nfull * 16 < w.k) {  // trailing partial block (element-wise decode)
+    for (int64_t i = nfull * 16; i < w.k; ++i) {
+      const float v = q6 ? legacy_q6k_value(rp, i) : legacy_q4k_value(rp, w.k, i);
+#pragma unroll
+      for (int mi = 0; mi < M; ++mi) acc[mi] = fmaf(v, x[mi * w.k + i], acc[mi]);
     }
   }
 #pragma unroll
