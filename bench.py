@@ -63,7 +63,15 @@ WORKLOADS = {
     # name: (gguf type, legacy type, N rows, K, description)
     "q6k-gemv": (14, 114, 4096, 14336, "Q6_K dequant+GEMV 4096x14336 (down-proj shape)"),
     "q4k-gemv": (12, 112, 4096, 4096, "Q4_K dequant+GEMV 4096x4096"),
+    # the other K-quant types on the same 4096x4096 shape (their CPU legs run the
+    # reference's Q5_K rows; Q2_K / Q3_K have no QuantizedLinear form there)
+    "q5k-gemv": (13, 113, 4096, 4096, "Q5_K dequant+GEMV 4096x4096"),
+    "q3k-gemv": (11, 113, 4096, 4096, "Q3_K dequant+GEMV 4096x4096"),
+    "q2k-gemv": (10, 113, 4096, 4096, "Q2_K dequant+GEMV 4096x4096"),
 }
+# bytes per 256 weights (GGUF) or per 16 weights (the reference's legacy blocks)
+BLOCK_BYTES = {10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210),
+               112: (16, 28), 113: (16, 36), 114: (16, 42)}
 PREFILL_METRIC = "Q4_K prefill dequant-GEMM TFLOP/s (% dense bf16 peak)"
 PREFILL = {
     # name: (gguf type, legacy type, N rows, K, description); bf16 activations, M tokens
@@ -124,10 +132,8 @@ def kernel_path(name):
 
 
 def algorithmic_bytes(qtype, n, k, m):
-    if qtype in (112, 114):  # the reference's blocks: 28 / 42 bytes per 16 weights
-        wbytes = n * ((k + 15) // 16) * (28 if qtype == 112 else 42)
-    else:
-        wbytes = n * (k // 256) * (144 if qtype == 12 else 210)
+    per, bs = BLOCK_BYTES[qtype]
+    wbytes = n * ((k + per - 1) // per) * bs
     return wbytes, wbytes + m * k * 4 + m * n * 4
 
 
@@ -429,6 +435,8 @@ def measure_gemv(args, workload, m, rank, world, local_rank, steps, warmup):
     qtype, legacy_type, n, k, desc = WORKLOADS[workload]
     legacy = getattr(args, "layout", "gguf") == "legacy"
     if legacy:
+        if qtype not in (12, 14):
+            raise SystemExit(f"{workload}: the reference's legacy blocks exist for Q4_K and Q6_K only")
         qtype = legacy_type
         desc = desc.replace("Q6_K", "Q6_K (reference 42-byte blocks)").replace("Q4_K", "Q4_K (reference 28-byte blocks)")
     wbytes, alg = algorithmic_bytes(qtype, n, k, m)
@@ -440,8 +448,10 @@ def measure_gemv(args, workload, m, rank, world, local_rank, steps, warmup):
     for i in range(nw):  # the same seeded weights on every rank; each keeps its rows
         if legacy:
             full = torch.from_numpy(synthetic.legacy_weight(qtype, n, k, seed=1000 + i)).to(dev)
-        else:
+        elif qtype in (12, 14):
             full = dec.gguf_weight_device(qtype, n, k, seed=1000 + i, device=dev)
+        else:
+            full = torch.from_numpy(synthetic.gguf_weight(qtype, n, k, seed=1000 + i)).to(dev)
         weights.append(kq.Weight(ctx, qtype, full[r0:r1].contiguous(), r1 - r0, k))
         del full
     x = torch.from_numpy(synthetic.activations(m, k, seed=7)).to(dev)
