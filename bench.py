@@ -34,7 +34,7 @@ Sub-records of the default line (skipped with --no-extras):
 * prefill  -- (one GPU) the Q4_K 14336x4096 bf16 prefill dequant-GEMM at M =
               4096 tokens, TFLOP/s against the sustained bf16 peak;
 * decode   -- the Llama-3-8B-shaped Q4_K_M decode step (context 2048) at
-              batch 1 and 8, tokens/s over the N GPUs (tensor parallel).
+              batch 1, 8 and 32, tokens/s over the N GPUs (tensor parallel).
 
 Other workloads (--workload): q4k-gemv, prefill-4096 / prefill-14336 (--m
 tokens), decode-llama8b / decode-qwen05b (--batch), and the single-op
@@ -647,7 +647,7 @@ def measure_extras(args, rank, world, local_rank):
                           "peak_source": f"{sus_kind} (cuBLAS bf16, sustained: the kernel runs inside a long "
                                          f"timed region)", "clocks": p["clocks"]}
     decode = {}
-    for batch in (1, 8):
+    for batch in (1, 8, 32):
         d = measure_decoder(args, "decode-llama8b", batch, rank, world, local_rank, min(steps, 50), args.warmup)
         peak, _ = peaks()
         decode[f"batch{batch}"] = {"value": round(d["value"], 2), "unit": "tok/s", "ms_per_step": round(

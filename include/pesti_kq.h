@@ -77,6 +77,8 @@ enum kq_type {
                           /* larger m falls back to the AUTO choice          */
 #define KQ_PATH_IMMA 4    /* integer mma.sync on the raw 4/6-bit codes        */
                           /* (TMA-fed 128-row tiles, split-K)                */
+/* Q2_K / Q3_K / Q5_K: m = 1 under AUTO and DP4A runs the single-token dp4a  */
+/* kernel (in_features <= 30720); every other case the CUDA-core f32 kernel. */
 
 typedef struct kq_ctx kq_ctx;
 typedef struct kq_weight kq_weight;

@@ -532,15 +532,22 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
     w->device_bytes = nsb * (kq::Q6K_BODY + 2);
     w->dw.len = w->device_bytes;
   } else if (is_kx(type)) {
-    // rows at a 16-byte stride (the row's bytes rounded up), one 2-D copy
-    const int64_t src_rb = w->dw.sb * kq::kx_block_bytes(type);
-    const int64_t dst_rb = (src_rb + 15) & ~int64_t(15);
+    // rows at a 16-byte stride (the row's bytes rounded up), one 2-D copy;
+    // Q3_K: superblocks at their device stride (each padded to 112 bytes)
+    const int64_t bs = kq::kx_block_bytes(type), ds = kq::kx_dev_stride(type);
+    const int64_t src_rb = w->dw.sb * bs;
+    const int64_t dst_rb = (w->dw.sb * ds + 15) & ~int64_t(15);
     w->dw.row_bytes = dst_rb;
     e = cudaMalloc(&w->q_alloc, (size_t)(n * dst_rb) + pad);
     if (e == cudaSuccess) e = cudaMemsetAsync(w->q_alloc, 0, (size_t)(n * dst_rb) + pad, ctx->stream);
-    if (e == cudaSuccess && need)
-      e = cudaMemcpy2DAsync(w->q_alloc, (size_t)dst_rb, bytes, (size_t)src_rb, (size_t)src_rb, (size_t)n,
-                            cudaMemcpyDefault, ctx->stream);
+    if (e == cudaSuccess && need) {
+      if (ds == bs)
+        e = cudaMemcpy2DAsync(w->q_alloc, (size_t)dst_rb, bytes, (size_t)src_rb, (size_t)src_rb, (size_t)n,
+                              cudaMemcpyDefault, ctx->stream);
+      else  // dst_rb == sb * ds: the superblocks of all rows are one run of n * sb
+        e = cudaMemcpy2DAsync(w->q_alloc, (size_t)ds, bytes, (size_t)bs, (size_t)bs, (size_t)(n * w->dw.sb),
+                              cudaMemcpyDefault, ctx->stream);
+    }
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     w->device_bytes = n * dst_rb;
     w->dw.len = w->device_bytes;
@@ -654,7 +661,17 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
     if ((rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes_bf16(m, k), "workspace"))) return rc;
     e = kq::launch_tc_bf16(w->dw, xd, m, bd, yd, ctx->ws, ctx->dev_err, s, &launches, ctx->next_bracket());
   } else if (is_kx(w->dw.type)) {
-    e = kq::launch_gemv_kx(w->dw, static_cast<const float*>(xd), m, bd, yd, s, &launches, ctx->next_bracket());
+    // one token: the single-token dp4a kernel (AUTO / DP4A; widths it cannot
+    // stage fall through); otherwise the CUDA-core f32 kernel
+    const kq::Bracket br = ctx->next_bracket();
+    e = cudaErrorNotSupported;
+    if (m == 1 && (ctx->path == KQ_PATH_AUTO || ctx->path == KQ_PATH_DP4A)) {
+      kq::XsInput in;
+      in.x = static_cast<const float*>(xd);
+      e = kq::launch_gemv_xs(w->dw, in, bd, yd, ctx->num_sms, ctx->dev_err, pf, s, &launches, br);
+    }
+    if (e == cudaErrorNotSupported)
+      e = kq::launch_gemv_kx(w->dw, static_cast<const float*>(xd), m, bd, yd, s, &launches, br);
   } else if (is_gguf(w->dw.type)) {
     if ((rc = prepare_f32(ctx, w->dw, m))) return rc;
     const int fam = f32_family(ctx, w->dw, m);

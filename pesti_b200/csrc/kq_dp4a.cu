@@ -539,6 +539,24 @@ constexpr int64_t XS_INFLIGHT = 144 * 1024;  // ring bytes in flight per CTA
 enum : int { XS_ERR_FULL = 21, XS_ERR_EMPTY = 22, XS_ERR_DRAIN = 23, XS_ERR_TP = 32 };
 constexpr int64_t XS_PF_CHUNK = 64 * 1024;  // bytes per L2 prefetch instruction
 
+// Device bytes of one superblock within a row (Q6_K: the body; its d values
+// are a separate array), and a row's stride: its superblocks rounded up to a
+// whole number of 16-byte units (the same stride the upload gives each type).
+__host__ __device__ constexpr int xs_stride(int qt) {
+  return qt == GGUF_Q4_K   ? Q4K_BYTES
+         : qt == GGUF_Q6_K ? Q6K_BODY
+         : qt == GGUF_Q5_K ? Q5K_BYTES
+         : qt == GGUF_Q3_K ? Q3K_DEV
+                           : Q2K_BYTES;
+}
+__host__ __device__ constexpr int64_t xs_row_bytes(int qt, int64_t sb) { return (sb * xs_stride(qt) + 15) & ~int64_t(15); }
+// Types whose sub-blocks hold 16 weights (Q2_K, Q3_K) instead of 32 (Q4_K, Q5_K).
+__host__ __device__ constexpr bool xs_g16(int qt) { return qt == GGUF_Q2_K || qt == GGUF_Q3_K; }
+// Activation sums kept per 64-weight unit: Q4_K / Q5_K float2 (the unit's two
+// 32-weight sub-blocks), Q2_K / Q3_K float4 (four 16-weight sub-blocks),
+// Q6_K int4[4] (the -32 corrections of its 8-weight groups).
+__host__ __device__ constexpr int xs_sum_bytes(int qt) { return qt == GGUF_Q6_K ? 64 : xs_g16(qt) ? 16 : 8; }
+
 struct XsParams {
   const uint8_t* q;     // [n][row_bytes]
   // (tensor-parallel fields last)
@@ -581,7 +599,7 @@ struct XsSmem {
     ring = 0;
     xw = ring + (size_t)S * (size_t)stage_bytes;
     sums = xw + units * 128;
-    xsf = sums + units * (qt == GGUF_Q4_K ? 8 : 64);
+    xsf = sums + units * xs_sum_bytes(qt);
     part = xsf + units;  // one float per superblock = units / 4 floats
     red = (part + (size_t)rows_max * nk * 4 + 15) & ~size_t(15);
     xr = red + 32 * 4;
@@ -690,7 +708,7 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       int off;
-      if constexpr (QT == GGUF_Q4_K) off = 64 * u + 16 * hf + (i < 4 ? 4 * i : 32 + 4 * (i - 4));
+      if constexpr (QT != GGUF_Q6_K) off = 64 * u + 16 * hf + (i < 4 ? 4 * i : 32 + 4 * (i - 4));
       else off = 128 * hf + 32 * (i >> 1) + 8 * u + 4 * (i & 1);
       float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
       if constexpr (XM == XS_X_PLAIN) {
@@ -736,8 +754,9 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
     const XScale sc = xs_scale(amax);
     uint4* unit = xw + (size_t)(kb * 4 + u) * 8;
     const int sw = xs_swz(kb, u);
-    if constexpr (QT == GGUF_Q4_K) {
+    if constexpr (QT != GGUF_Q6_K) {
       // word 4 hf + j: {hi, lo} of A elements 4j.., then of B elements 4j..
+      // (A: unit elements 0-31, B: 32-63; this half-unit holds 16 hf .. 16 hf + 15 of each)
       float sa = 0.f, sbb = 0.f;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -751,9 +770,16 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
         xs_pack4(v[16 + 4 * j], v[17 + 4 * j], v[18 + 4 * j], v[19 + 4 * j], sc.inv, o.z, o.w);
         unit[(4 * hf + j) ^ sw] = o;
       }
-      sa += __shfl_xor_sync(0xffffffffu, sa, 1);  // the unit's other half
-      sbb += __shfl_xor_sync(0xffffffffu, sbb, 1);
-      if (hf == 0) reinterpret_cast<float2*>(smem + L.sums)[kb * 4 + u] = make_float2(sa, sbb);
+      if constexpr (xs_g16(QT)) {
+        // a half-unit's A and B runs are whole 16-weight sub-blocks: 4u + hf and 4u + 2 + hf
+        float* s4 = reinterpret_cast<float*>(smem + L.sums) + (size_t)(kb * 4 + u) * 4;
+        s4[hf] = sa;
+        s4[2 + hf] = sbb;
+      } else {
+        sa += __shfl_xor_sync(0xffffffffu, sa, 1);  // the unit's other half
+        sbb += __shfl_xor_sync(0xffffffffu, sbb, 1);
+        if (hf == 0) reinterpret_cast<float2*>(smem + L.sums)[kb * 4 + u] = make_float2(sa, sbb);
+      }
     } else {
       // h = hf; word 4h + 2w + gp holds {hi, lo} of group (h, 2gp, w), then of (h, 2gp + 1, w)
       int shs[4], sls[4];
@@ -876,13 +902,16 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
     for (int j = 0; j < 8; ++j) X[j] = unit[j ^ sw];
   }
   const float xf = reinterpret_cast<const float*>(xs_smem + L.xsf)[kb];
-  float sa = 0.f, sbb = 0.f;   // Q4_K: exact sums of the sub-block 2u / 2u+1 activations
+  float sa = 0.f, sbb = 0.f;   // Q4_K / Q5_K: exact sums of the sub-block 2u / 2u+1 activations
+  float4 s16 = make_float4(0.f, 0.f, 0.f, 0.f);  // Q2_K / Q3_K: exact sums of sub-blocks 4u .. 4u+3
   int Sh[2][4], Sl[2][4];      // Q6_K: -32 * (sum of hi / lo bytes) of group (h, g)
   uint32_t sel_lo = 0, sel_hi = 0;  // Q6_K: PRMT selectors of this lane's scale bytes
-  if constexpr (QT == GGUF_Q4_K) {
+  if constexpr (QT == GGUF_Q4_K || QT == GGUF_Q5_K) {
     const float2 t = reinterpret_cast<const float2*>(xs_smem + L.sums)[kb * 4 + u];
     sa = t.x;
     sbb = t.y;
+  } else if constexpr (xs_g16(QT)) {
+    s16 = reinterpret_cast<const float4*>(xs_smem + L.sums)[kb * 4 + u];
   } else {
     const int4* si = reinterpret_cast<const int4*>(xs_smem + L.sums) + (size_t)(kb * 4 + u) * 4;
 #pragma unroll
@@ -898,8 +927,13 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
     sel_hi = b2 | ((b2 | 8) << 4) | ((b2 | 8) << 8) | ((b2 | 8) << 12);
   }
   float* part = reinterpret_cast<float*>(xs_smem + L.part);
-  const bool hi4 = u >= 2;  // Q4_K: sub-blocks 2u, 2u+1 take the packed high scale/min bits
+  const bool hi4 = u >= 2;  // Q4_K / Q5_K: sub-blocks 2u, 2u+1 take the packed high scale/min bits
   const int sh = 16 * (u & 1);
+  // Q5_K: left rotations moving bit 2u / 2u+1 of every qh byte to bit 4;
+  // Q3_K: moving bit 2u / 2u+1 of every hmask byte to bit 2
+  const int r5a = (4 - 2 * u) & 31, r5b = (3 - 2 * u) & 31;
+  const int r3a = (2 - 2 * u) & 31, r3b = (1 - 2 * u) & 31;
+  const int sh2 = 4 * (u & 1);  // Q2_K / Q3_K: bit offset of the unit's 2-bit codes in its qs bytes
 
   // one row of this warp's slice: returns the lane's partial (0 for lanes past the row's end)
   auto row_partial = [&](const uint8_t* rowp, const uint8_t* drow) -> float {
@@ -936,6 +970,115 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
         const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xffff));
         const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
         const float msum = fmaf((float)(mp & 0xffu), sa, (float)(mp >> 8) * sbb);
+        v = fmaf(d * xf, (float)iv, -dmin * msum);
+      } else if constexpr (QT == GGUF_Q5_K) {
+        // d | dmin | 12 scale bytes (as Q4_K) | qh[32] | qs[128]; this lane's
+        // qs bytes 32u .. 32u+31 hold sub-blocks 2u (low nibbles) and 2u+1
+        // (high nibbles), whose fifth bits are bits 2u and 2u+1 of qh[0..31]
+        const uint8_t* blk = rowp + kb * Q5K_BYTES;
+        const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+        const uint4 h0 = *reinterpret_cast<const uint4*>(blk + 16);
+        const uint4 h1 = *reinterpret_cast<const uint4*>(blk + 32);
+        const uint4 qa = *reinterpret_cast<const uint4*>(blk + 48 + 32 * u);
+        const uint4 qb = *reinterpret_cast<const uint4*>(blk + 64 + 32 * u);
+        const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        const uint32_t H[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+        int ahi = 0, alo = 0, bhi = 0, blo = 0;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const uint32_t qA = (W[w] & 0x0F0F0F0Fu) | (__funnelshift_l(H[w], H[w], r5a) & 0x10101010u);
+          const uint32_t qB = ((W[w] >> 4) & 0x0F0F0F0Fu) | (__funnelshift_l(H[w], H[w], r5b) & 0x10101010u);
+          ahi = dp4a_s(qA, X[w].x, ahi);
+          alo = dp4a_u(qA, X[w].y, alo);
+          bhi = dp4a_s(qB, X[w].z, bhi);
+          blo = dp4a_u(qB, X[w].w, blo);
+        }
+        const uint32_t s0 = hdr.y, s1 = hdr.z, s2 = hdr.w;
+        uint32_t scp, mp;
+        if (!hi4) {
+          scp = (s0 >> sh) & 0x3F3Fu;
+          mp = (s1 >> sh) & 0x3F3Fu;
+        } else {
+          scp = ((s2 >> sh) & 0x0F0Fu) | ((s0 >> (sh + 2)) & 0x3030u);
+          mp = ((s2 >> (sh + 4)) & 0x0F0Fu) | ((s1 >> (sh + 2)) & 0x3030u);
+        }
+        // |da|, |db| <= 32 * 31 * 2^14 < 2^24; |iv| <= 2 * 63 * 32 * 31 * 2^14 < 2^31
+        const int da = ahi * 256 + alo, db = bhi * 256 + blo;
+        const int iv = (int)(scp & 0xffu) * da + (int)(scp >> 8) * db;
+        const float d = f16_bits_to_f32((uint16_t)(hdr.x & 0xffff));
+        const float dmin = f16_bits_to_f32((uint16_t)(hdr.x >> 16));
+        const float msum = fmaf((float)(mp & 0xffu), sa, (float)(mp >> 8) * sbb);
+        v = fmaf(d * xf, (float)iv, -dmin * msum);
+      } else if constexpr (QT == GGUF_Q3_K) {
+        // device superblock (112 bytes): hmask[32] | qs[64] | scales[12] | d | 2 zero bytes.
+        // This lane's elements: 2-bit codes at bits sh2 (A) / sh2 + 2 (B) of
+        // qs bytes 32(u/2) .. + 31, third bits 2u / 2u+1 of hmask[0..31]; the
+        // code q + 4 = lo | h << 2 is in [0, 7] and the -4 goes through the sums
+        const uint8_t* blk = rowp + kb * Q3K_DEV;
+        const uint4 m0 = *reinterpret_cast<const uint4*>(blk);
+        const uint4 m1 = *reinterpret_cast<const uint4*>(blk + 16);
+        const uint4 qa = *reinterpret_cast<const uint4*>(blk + 32 + 32 * (u >> 1));
+        const uint4 qb = *reinterpret_cast<const uint4*>(blk + 48 + 32 * (u >> 1));
+        const uint4 sd = *reinterpret_cast<const uint4*>(blk + 96);  // scales 0-11 | d
+        const uint32_t W[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+        const uint32_t H[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
+        int gh[4] = {0, 0, 0, 0}, gl[4] = {0, 0, 0, 0};  // sub-blocks 4u .. 4u+3
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const uint32_t t = W[w] >> sh2;
+          const uint32_t qA = (t & 0x03030303u) | (__funnelshift_l(H[w], H[w], r3a) & 0x04040404u);
+          const uint32_t qB = ((t >> 2) & 0x03030303u) | (__funnelshift_l(H[w], H[w], r3b) & 0x04040404u);
+          const int a = w >> 2, bb = 2 + (w >> 2);
+          gh[a] = dp4a_s(qA, X[w].x, gh[a]);
+          gl[a] = dp4a_u(qA, X[w].y, gl[a]);
+          gh[bb] = dp4a_s(qB, X[w].z, gh[bb]);
+          gl[bb] = dp4a_u(qB, X[w].w, gl[bb]);
+        }
+        // six-bit scale of sub-block 4u + i (byte i): low nibble of scale
+        // byte 4u + i (u < 2) or high nibble of byte 4(u-2) + i, and bits 2u
+        // of byte 8 + i on top; minus 32
+        const uint32_t sc4 = (((u & 1) ? sd.y : sd.x) >> (4 * (u >> 1)) & 0x0F0F0F0Fu) |
+                             (((sd.z >> (2 * u)) & 0x03030303u) << 4);
+        const float S[4] = {s16.x, s16.y, s16.z, s16.w};
+        int iv = 0;  // |.| <= 4 * 32 * 16 * 7 * 2^14 < 2^28
+        float fs = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int sc = (int)((sc4 >> (8 * i)) & 63u) - 32;
+          iv += sc * (gh[i] * 256 + gl[i]);
+          fs = fmaf((float)sc, S[i], fs);
+        }
+        v = f16_bits_to_f32((uint16_t)(sd.w & 0xffff)) * fmaf(xf, (float)iv, -4.f * fs);
+      } else if constexpr (QT == GGUF_Q2_K) {
+        // scales[16] | qs[64] | d | dmin at an 84-byte stride: 4-byte aligned,
+        // so 32-bit loads.  Codes at bits sh2 (A) / sh2 + 2 (B) of qs bytes
+        // 32(u/2) .. + 31; the B codes are used in place (4x) and their sums
+        // divided by 4, exactly
+        const uint32_t* blk = reinterpret_cast<const uint32_t*>(rowp + kb * Q2K_BYTES);
+        const uint32_t scw = blk[u];  // scale / min nibbles of sub-blocks 4u .. 4u+3
+        const uint32_t dd = blk[20];  // d | dmin
+        const uint32_t* qs = blk + 4 + 8 * (u >> 1);
+        int gh[4] = {0, 0, 0, 0}, gl[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          const uint32_t t = qs[w] >> sh2;
+          const uint32_t qA = t & 0x03030303u, qB4 = t & 0x0C0C0C0Cu;
+          const int a = w >> 2, bb = 2 + (w >> 2);
+          gh[a] = dp4a_s(qA, X[w].x, gh[a]);
+          gl[a] = dp4a_u(qA, X[w].y, gl[a]);
+          gh[bb] = dp4a_s(qB4, X[w].z, gh[bb]);
+          gl[bb] = dp4a_u(qB4, X[w].w, gl[bb]);
+        }
+        const float S[4] = {s16.x, s16.y, s16.z, s16.w};
+        int iv = 0;  // |.| <= 4 * 15 * 16 * 3 * 2^14 < 2^26
+        float msum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int D = (gh[i] * 256 + gl[i]) >> (i >= 2 ? 2 : 0);
+          iv += (int)((scw >> (8 * i)) & 15u) * D;
+          msum = fmaf((float)((scw >> (8 * i + 4)) & 15u), S[i], msum);
+        }
+        const float d = f16_bits_to_f32((uint16_t)(dd & 0xffff)), dmin = f16_bits_to_f32((uint16_t)(dd >> 16));
         v = fmaf(d * xf, (float)iv, -dmin * msum);
       } else {
         const uint8_t* blk = rowp + kb * Q6K_BODY;
@@ -1074,7 +1217,7 @@ XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms, int64_t xr_floats 
   r.threads = 32 * (nk * r.G + 1);
   r.grid = (int)std::min<int64_t>(n, num_sms);
   r.rows_max = (int)((n + r.grid - 1) / r.grid);
-  const int64_t row_bytes = sb * (qt == GGUF_Q4_K ? Q4K_BYTES : Q6K_BODY);
+  const int64_t row_bytes = xs_row_bytes(qt, sb);
   const int64_t d_row_bytes = qt == GGUF_Q6_K ? q6k_d_ld(sb) * 2 : 0;
   r.stage_bytes = 2 * r.G * (row_bytes + d_row_bytes);  // 2G rows per stage
   const int T = (r.rows_max + 2 * r.G - 1) / (2 * r.G);
@@ -1096,7 +1239,7 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
   XsParams P;
   P.q = w.q;
   P.d = w.d;
-  P.row_bytes = w.sb * (QT == GGUF_Q4_K ? Q4K_BYTES : Q6K_BODY);
+  P.row_bytes = xs_row_bytes(QT, w.sb);
   P.d_row_bytes = QT == GGUF_Q6_K ? (int)(w.d_ld * 2) : 0;
   P.n = (int)w.n;
   P.sb = (int)w.sb;
@@ -1131,6 +1274,10 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if constexpr (QT != GGUF_Q4_K && QT != GGUF_Q6_K) {  // Q2_K / Q3_K / Q5_K: plain linears only
+    if (in.mode != XS_X_PLAIN || in.ymode != XS_Y_LOCAL) return cudaErrorNotSupported;
+    return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_LOCAL>, P);
+  }
   if (in.ymode == XS_Y_SWIGLU) {
     switch (in.mode) {
       case XS_X_PLAIN: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_SWIGLU>, P);
@@ -1217,13 +1364,23 @@ static cudaError_t xs_attrs() {
 cudaError_t dp4a_init_device() {
   cudaError_t e = xs_attrs<GGUF_Q4_K>();
   if (e == cudaSuccess) e = xs_attrs<GGUF_Q6_K>();
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<GGUF_Q2_K, XS_X_PLAIN, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<GGUF_Q3_K, XS_X_PLAIN, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<GGUF_Q5_K, XS_X_PLAIN, XS_Y_LOCAL>);
   return e;
 }
 
 cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* bias, float* y, int num_sms, int* err,
                            const Prefetch* pf, cudaStream_t s, int* launches, Bracket br) {
-  if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
+  if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K && w.type != GGUF_Q2_K && w.type != GGUF_Q3_K &&
+      w.type != GGUF_Q5_K)
+    return cudaErrorNotSupported;
   if (in.mode < XS_X_PLAIN || in.mode > XS_X_REDUCE_NORM) return cudaErrorInvalidValue;
+  // Q2_K / Q3_K / Q5_K: plain linears, rows laid out at the stride the kernel streams
+  if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K) {
+    if (in.mode != XS_X_PLAIN || in.ymode != XS_Y_LOCAL) return cudaErrorNotSupported;
+    if (w.row_bytes != xs_row_bytes(w.type, w.sb)) return cudaErrorInvalidValue;
+  }
   const bool reduce = in.mode == XS_X_REDUCE || in.mode == XS_X_REDUCE_NORM;
   const bool norm = in.mode == XS_X_NORM || in.mode == XS_X_REDUCE_NORM;
   if (in.ymode == XS_Y_SWIGLU && (w.n & 1)) return cudaErrorInvalidValue;
@@ -1231,8 +1388,14 @@ cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* b
   const XsLaunch sh = xs_shape(w.type, w.n, w.sb, num_sms, reduce ? vec : 0, norm ? vec : 0);
   if (!sh.ok) return cudaErrorNotSupported;
   bracket_record(br.start, s);
-  cudaError_t e = w.type == GGUF_Q4_K ? launch_xs<GGUF_Q4_K>(w, in, bias, y, err, pf, s, sh)
-                                      : launch_xs<GGUF_Q6_K>(w, in, bias, y, err, pf, s, sh);
+  cudaError_t e;
+  switch (w.type) {
+    case GGUF_Q4_K: e = launch_xs<GGUF_Q4_K>(w, in, bias, y, err, pf, s, sh); break;
+    case GGUF_Q6_K: e = launch_xs<GGUF_Q6_K>(w, in, bias, y, err, pf, s, sh); break;
+    case GGUF_Q5_K: e = launch_xs<GGUF_Q5_K>(w, in, bias, y, err, pf, s, sh); break;
+    case GGUF_Q3_K: e = launch_xs<GGUF_Q3_K>(w, in, bias, y, err, pf, s, sh); break;
+    default: e = launch_xs<GGUF_Q2_K>(w, in, bias, y, err, pf, s, sh); break;
+  }
   if (e != cudaSuccess) return e;
   if (launches) ++*launches;
   bracket_record(br.stop, s);

@@ -20,8 +20,10 @@
 // Every product is rounded on its own (__fmul_rn / __fsub_rn), in this
 // association, so the decode matches the CPU definition bit for bit.
 //
-// Device layout: rows as uploaded, the row stride rounded up to 16 bytes
-// (row_bytes) so every row starts on a 16-byte boundary for cp.async.
+// Device layout: Q2_K and Q5_K rows as uploaded, the row stride rounded up to
+// 16 bytes (row_bytes) so every row starts on a 16-byte boundary for
+// cp.async; Q3_K superblocks at a 112-byte stride (two zero bytes after each),
+// so that every one starts on a 16-byte boundary for vector loads.
 //
 // GEMV: a CTA owns KX_RB rows (two per warp) and walks K in chunks of CH
 // superblocks.  Each chunk's activations (up to MT tokens) and the CTA's
@@ -48,20 +50,19 @@ constexpr int KX_RB = 16;        // rows per CTA: two per warp
 
 template <int QT>
 struct KxFmt;
+// BS: bytes of a superblock in the file; DS: device stride between the
+// superblocks of a row; CH: superblocks per chunk (CH * DS is a multiple of 16)
 template <>
 struct KxFmt<GGUF_Q2_K> {
-  static constexpr int BS = 84;
-  static constexpr int CH = 4;  // superblocks per chunk (CH * BS is a multiple of 16)
+  static constexpr int BS = Q2K_BYTES, DS = Q2K_BYTES, CH = 4;
 };
 template <>
 struct KxFmt<GGUF_Q3_K> {
-  static constexpr int BS = 110;
-  static constexpr int CH = 8;
+  static constexpr int BS = Q3K_BYTES, DS = Q3K_DEV, CH = 4;
 };
 template <>
 struct KxFmt<GGUF_Q5_K> {
-  static constexpr int BS = 176;
-  static constexpr int CH = 4;
+  static constexpr int BS = Q5K_BYTES, DS = Q5K_BYTES, CH = 4;
 };
 
 __device__ __forceinline__ uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
@@ -147,9 +148,9 @@ __device__ __forceinline__ void cp_async_wait() {
 
 template <int QT, int MT>
 struct KxSmem {
-  static constexpr int BS = KxFmt<QT>::BS, CH = KxFmt<QT>::CH;
+  static constexpr int DS = KxFmt<QT>::DS, CH = KxFmt<QT>::CH;
   static constexpr int XB = MT * CH * 256 * 4;  // activations of one chunk, [MT][CH * 256] f32
-  static constexpr int WP = CH * BS;            // one row's bytes of one chunk (a multiple of 16)
+  static constexpr int WP = CH * DS;            // one row's bytes of one chunk (a multiple of 16)
   static constexpr int STAGE = XB + KX_RB * WP;
   static constexpr int TOTAL = 2 * STAGE;
   static_assert(WP % 16 == 0, "chunk rows must be whole 16-byte units");
@@ -179,11 +180,11 @@ __global__ void __launch_bounds__(KX_THREADS) kx_gemv_kernel(const uint8_t* __re
     }
     // whole 16-byte units: a partial chunk reads up to 15 bytes past its
     // last superblock, inside the row's padded stride or the allocation's pad
-    const int wu = (chv * L::BS + 15) >> 4;
+    const int wu = (chv * L::DS + 15) >> 4;
     for (int i = threadIdx.x; i < rows * wu; i += KX_THREADS) {
       const int r = i / wu, u = i - r * wu;
       cp_async16(st + L::XB + r * L::WP + u * 16,
-                 q + (int64_t)(row0 + r) * row_bytes + (int64_t)c * CH * L::BS + u * 16);
+                 q + (int64_t)(row0 + r) * row_bytes + (int64_t)c * CH * L::DS + u * 16);
     }
     cp_async_commit();
   };
@@ -218,7 +219,7 @@ __global__ void __launch_bounds__(KX_THREADS) kx_gemv_kernel(const uint8_t* __re
         const int r = 2 * warp + rr;
         if (r < rows) {
           float w[8];
-          kx_decode8<QT>(ws + r * L::WP + j * L::BS, lane, w);
+          kx_decode8<QT>(ws + r * L::WP + j * L::DS, lane, w);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -248,7 +249,7 @@ __global__ void kx_dequant_kernel(const uint8_t* __restrict__ q, int64_t row_byt
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = idx / k, i = idx - r * k;
-    out[idx] = kx_value<QT>(q + (row0 + r) * row_bytes + (i >> 8) * KxFmt<QT>::BS, (int)(i & 255));
+    out[idx] = kx_value<QT>(q + (row0 + r) * row_bytes + (i >> 8) * KxFmt<QT>::DS, (int)(i & 255));
   }
 }
 
@@ -302,6 +303,15 @@ int64_t kx_block_bytes(int type) {
     case GGUF_Q2_K: return KxFmt<GGUF_Q2_K>::BS;
     case GGUF_Q3_K: return KxFmt<GGUF_Q3_K>::BS;
     case GGUF_Q5_K: return KxFmt<GGUF_Q5_K>::BS;
+    default: return 0;
+  }
+}
+
+int64_t kx_dev_stride(int type) {
+  switch (type) {
+    case GGUF_Q2_K: return KxFmt<GGUF_Q2_K>::DS;
+    case GGUF_Q3_K: return KxFmt<GGUF_Q3_K>::DS;
+    case GGUF_Q5_K: return KxFmt<GGUF_Q5_K>::DS;
     default: return 0;
   }
 }

@@ -1,8 +1,9 @@
-"""GGUF Q2_K, Q3_K and Q5_K on the device (kq_kx.cu) and the reference's
-legacy Q5_K rows: dequantization bit-exact with the oracle (on the gguf-py
-fixture superblocks and on random weights), linears within 1e-3 of max|y|
-of the oracle's sequential f32 product at 1 to 13 tokens, upload from a GGUF
-file, and the drop-in constructors' dtype names."""
+"""GGUF Q2_K, Q3_K and Q5_K on the device (kq_kx.cu, and the single-token
+dp4a kernel of kq_dp4a.cu) and the reference's legacy Q5_K rows:
+dequantization bit-exact with the oracle (on the gguf-py fixture superblocks
+and on random weights), linears within 1e-3 of max|y| of the oracle's
+sequential f32 product at 1 to 13 tokens, upload from a GGUF file, and the
+drop-in constructors' dtype names."""
 import os
 
 import numpy as np
@@ -64,6 +65,51 @@ def test_linear_matches_the_oracle(gpu_ctx, name, kt, ot, tag, n, k, m):
     assert rel_err(y, ref) <= TOL
     for t in range(m):  # every token, not only the one with the largest output
         assert rel_err(y[t], ref[t]) <= TOL
+    w.free()
+
+
+@pytest.mark.parametrize("name,kt,ot,tag", TYPES, ids=[t[0] for t in TYPES])
+@pytest.mark.parametrize("n,k", [(4096, 4096), (37, 1280), (1024, 14336), (16, 32768)])
+def test_one_token_on_both_kernels(gpu_ctx, name, kt, ot, tag, n, k):
+    """m = 1 runs the single-token dp4a kernel under AUTO (in_features up to
+    30720; wider rows fall through to the f32 kernel) and the f32 kernel
+    under another path; both against the oracle, and against each other."""
+    raw = synthetic.gguf_weight(kt, n, k, seed=5 * n + k)
+    x = synthetic.activations(1, k, seed=17)
+    bias = np.linspace(-1, 1, n).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    ref = oracle.gguf_linear(ot, raw, n, k, x, bias)
+    y_auto = np.empty((1, n), np.float32)
+    y_f32 = np.empty((1, n), np.float32)
+    try:
+        w.linear(x, 1, y_auto, bias)
+        gpu_ctx.set_path(kq.KQ_PATH_MMA)
+        w.linear(x, 1, y_f32, bias)
+    finally:
+        gpu_ctx.set_path(kq.KQ_PATH_AUTO)
+    assert rel_err(y_auto, ref) <= TOL
+    assert rel_err(y_f32, ref) <= TOL
+    assert rel_err(y_auto, y_f32) <= TOL
+    w.free()
+
+
+@pytest.mark.parametrize("name,kt,ot,tag", TYPES, ids=[t[0] for t in TYPES])
+def test_one_token_with_non_finite_and_zero_activations(gpu_ctx, name, kt, ot, tag):
+    """The single-token kernel's per-superblock activation scale: an all-zero
+    superblock of x gives exact zeros from it, and an inf in x makes NaN
+    (or inf) the rows the f32 product makes non-finite, as the oracle does."""
+    n, k = 64, 1024
+    raw = synthetic.gguf_weight(kt, n, k, seed=9)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    x = synthetic.activations(1, k, seed=3)
+    x[0, 256:512] = 0.0
+    y = np.empty((1, n), np.float32)
+    w.linear(x, 1, y)
+    assert rel_err(y, oracle.gguf_linear(ot, raw, n, k, x)) <= TOL
+    x[0, 700] = np.inf
+    w.linear(x, 1, y)
+    ref = oracle.gguf_linear(ot, raw, n, k, x)
+    assert np.array_equal(np.isfinite(y), np.isfinite(ref))
     w.free()
 
 
