@@ -209,11 +209,24 @@ int finish_sync(kq_ctx* ctx, const char* what) {
   return check_device_error(ctx);
 }
 
+// The CUDA-core f32 kernel of Q2_K / Q3_K / Q5_K (kq_kx.cu): internal
+// family code, never a KQ_PATH_* value.
+constexpr int FAM_KX = -1;
+
 // Kernel family for a GGUF f32 call of m tokens.  AUTO follows the measured
 // decode throughput of each family: integer dot products for one token (and
 // two Q6_K tokens), integer tensor-core tiles for Q4_K up to 64 tokens and
 // Q6_K up to 8, mma.sync bf16 tiles for Q6_K up to 64, tcgen05 above.
+// Q2_K / Q3_K / Q5_K: the single-token kernel at one token (AUTO, DP4A),
+// Q5_K on integer tensor-core tiles up to 64 tokens (AUTO, IMMA), otherwise
+// the CUDA-core f32 kernel.
 int f32_family(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
+  if (is_kx(w.type)) {
+    const bool auto_ = ctx->path == KQ_PATH_AUTO;
+    if (m == 1 && (auto_ || ctx->path == KQ_PATH_DP4A)) return KQ_PATH_DP4A;
+    if (w.type == kq::GGUF_Q5_K && m <= 64 && (auto_ || ctx->path == KQ_PATH_IMMA)) return KQ_PATH_IMMA;
+    return FAM_KX;
+  }
   const bool q4 = w.type == kq::GGUF_Q4_K;
   if (ctx->path == KQ_PATH_IMMA || ctx->path == KQ_PATH_MMA || ctx->path == KQ_PATH_TCGEN05) return ctx->path;
   if (m == 1 || (ctx->path == KQ_PATH_DP4A && m <= kq::DP4A_MAX_M)) return KQ_PATH_DP4A;
@@ -223,7 +236,8 @@ int f32_family(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
   return m <= 64 ? KQ_PATH_MMA : KQ_PATH_TCGEN05;
 }
 
-// Scratch bytes and zeroed counter bytes a GGUF f32 call of m tokens needs.
+// Scratch bytes and zeroed counter bytes a GGUF f32 call of m tokens needs
+// (the single-token kernel and the Q2_K / Q3_K / Q5_K f32 kernel need none).
 void f32_needs(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m, size_t* ws, size_t* ctr) {
   *ws = 0;
   *ctr = 0;
@@ -237,7 +251,7 @@ void f32_needs(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m, size_t* ws,
     *ws = kq::tc_workspace_bytes(m, w.n, w.k, ctx->num_sms);
     size_t off = 0;
     kq::tc_counter_span(m, w.n, w.k, ctx->num_sms, &off, ctr);
-  } else {
+  } else if (fam != FAM_KX) {
     *ws = kq::gemv_gguf_workspace_bytes(m, w.k);
   }
 }
@@ -390,10 +404,11 @@ int kq_ctx_synchronize(kq_ctx* ctx) {
 int kq_ctx_reserve(kq_ctx* ctx, const kq_weight* w, int64_t m) {
   if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
   if (!w || m < 0) return fail(ctx, KQ_ERR_INVALID_ARG, "bad reserve arguments");
-  if (!is_gguf(w->dw.type) || m == 0 || w->dw.k == 0) return KQ_OK;  // the other types need no scratch
+  if ((!is_gguf(w->dw.type) && !is_kx(w->dw.type)) || m == 0 || w->dw.k == 0)
+    return KQ_OK;  // the other types need no scratch
   DeviceGuard g(ctx->device);
   // every call with 1..m rows may pick a different kernel family: cover them all
-  size_t ws = kq::tc_workspace_bytes_bf16(m, w->dw.k), ctr = 0;
+  size_t ws = is_gguf(w->dw.type) ? kq::tc_workspace_bytes_bf16(m, w->dw.k) : 0, ctr = 0;
   for (int64_t i = 1; i <= m; ++i) {
     size_t a = 0, b = 0;
     f32_needs(ctx, w->dw, i, &a, &b);
@@ -569,7 +584,8 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
   }
   w->dw.q = static_cast<const uint8_t*>(w->q_alloc);
   w->dw.d = static_cast<const uint16_t*>(w->d_alloc);
-  if (is_gguf(type) && n > 0 && k > 0 && !kq::tc_make_weight_maps(w->dw)) {
+  // TMA descriptors: Q4_K / Q6_K (every tensor-core path), Q5_K (integer MMA)
+  if ((is_gguf(type) || type == kq::GGUF_Q5_K) && n > 0 && k > 0 && !kq::tc_make_weight_maps(w->dw)) {
     cudaFree(w->q_alloc);
     if (w->d_alloc) cudaFree(w->d_alloc);
     delete w;
@@ -660,19 +676,19 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
   } else if (bf16) {
     if ((rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes_bf16(m, k), "workspace"))) return rc;
     e = kq::launch_tc_bf16(w->dw, xd, m, bd, yd, ctx->ws, ctx->dev_err, s, &launches, ctx->next_bracket());
-  } else if (is_kx(w->dw.type)) {
+  } else if (is_kx(w->dw.type) && f32_family(ctx, w->dw, m) != KQ_PATH_IMMA) {
     // one token: the single-token dp4a kernel (AUTO / DP4A; widths it cannot
     // stage fall through); otherwise the CUDA-core f32 kernel
     const kq::Bracket br = ctx->next_bracket();
     e = cudaErrorNotSupported;
-    if (m == 1 && (ctx->path == KQ_PATH_AUTO || ctx->path == KQ_PATH_DP4A)) {
+    if (f32_family(ctx, w->dw, m) == KQ_PATH_DP4A) {
       kq::XsInput in;
       in.x = static_cast<const float*>(xd);
       e = kq::launch_gemv_xs(w->dw, in, bd, yd, ctx->num_sms, ctx->dev_err, pf, s, &launches, br);
     }
     if (e == cudaErrorNotSupported)
       e = kq::launch_gemv_kx(w->dw, static_cast<const float*>(xd), m, bd, yd, s, &launches, br);
-  } else if (is_gguf(w->dw.type)) {
+  } else if (is_gguf(w->dw.type) || is_kx(w->dw.type)) {
     if ((rc = prepare_f32(ctx, w->dw, m))) return rc;
     const int fam = f32_family(ctx, w->dw, m);
     if (fam == KQ_PATH_IMMA) {

@@ -1,5 +1,5 @@
-// kq_imma.cu -- batched decode linear (2..32 tokens per chunk) for GGUF Q4_K
-// and Q6_K on the integer tensor-core path: y[m][n] = x[m][k] . W[n][k] (+ bias).
+// kq_imma.cu -- batched decode linear (2..32 tokens per chunk) for GGUF Q4_K,
+// Q5_K and Q6_K on the integer tensor-core path: y[m][n] = x[m][k] . W[n][k] (+ bias).
 //
 // A Q4_K sub-block is 32 weights with one 6-bit scale and one 6-bit min, so it
 // is exactly one k32 step of mma.sync.m16n8k32 with 8-bit operands:
@@ -13,6 +13,8 @@
 //  * per sub-block the int32 result is scaled by sc (f32 accumulate) and the
 //    min term dmin m_j sum(x) uses exact int32 sums of the quantized
 //    activations; d, dmin and 2^e are applied once per superblock.
+// Q5_K is Q4_K with a fifth bit per weight: its codes (nibble | qh bit << 4,
+// at most 31) are the A fragment of the same k32 steps, the rest as Q4_K.
 // Q6_K's scale groups are 16 weights (elements 16s .. 16s+15 of a
 // superblock), so a group is one k16 step of mma.sync.m16n8k16 with 8-bit
 // operands: in the device body layout a lane's four codes of a group are one
@@ -81,7 +83,7 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
   if (wid >= (int64_t)slots * sb) return;
   const int t = (int)(wid / sb), kb = (int)(wid - (int64_t)t * sb);
   const int j = lane >> 2, c = lane & 3;
-  constexpr bool Q4 = QT == GGUF_Q4_K;
+  constexpr bool Q4 = QT == GGUF_Q4_K;  // Q5_K calls the Q4_K form (the same 32-weight sub-blocks)
   // Q4_K: sub-block j, elements 32j + 4c.. and 32j + 16 + 4c..; Q6_K: groups j and j + 8,
   // elements 16j + 4c.. and 16(j + 8) + 4c..
   const int64_t ea = Q4 ? 32 * j + 4 * c : 16 * j + 4 * c;
@@ -141,10 +143,13 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
   if (lane == 0) scl[(int64_t)kb * 32 + t] = factor;
 }
 
+// Device bytes of one superblock in the weight's tensor map box.
+constexpr int im_block_bytes(int qt) { return qt == GGUF_Q4_K ? Q4K_BYTES : qt == GGUF_Q5_K ? Q5K_BYTES : Q6K_BODY; }
+
 template <int QT, int NT>
 struct ImStage {
-  static constexpr bool Q4 = QT == GGUF_Q4_K;
-  static constexpr int W = IM_ROWS * (Q4 ? Q4K_BYTES : Q6K_BODY);  // 18432 / 26624
+  static constexpr bool Q4 = QT != GGUF_Q6_K;                     // Q4_K / Q5_K: 32-weight sub-blocks
+  static constexpr int W = IM_ROWS * im_block_bytes(QT);           // 18432 / 22528 / 26624
   static constexpr int D = Q4 ? 0 : IM_ROWS * 16;                  // Q6_K: d of 8 superblocks per row
   static constexpr int B = NT * 4096;                              // activation fragments, 8 tokens per tile
   static constexpr int S = 32 * (Q4 ? 8 : 16) * 4;                 // activation sums of the 32 token slots
@@ -208,8 +213,10 @@ template <int QT, int NT>
 __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
     imma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap dmap, const ImParams P) {
   using St = ImStage<QT, NT>;
-  constexpr bool Q4 = QT == GGUF_Q4_K;
-  constexpr int BPS = Q4 ? Q4K_BYTES : Q6K_BODY;
+  constexpr bool Q4 = QT != GGUF_Q6_K;  // Q4_K and Q5_K
+  constexpr bool Q5 = QT == GGUF_Q5_K;
+  constexpr int BPS = im_block_bytes(QT);
+  constexpr int QS = Q5 ? 48 : 16;  // offset of the qs bytes in the superblock
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_trigger();
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)P.S * St::BYTES);
@@ -278,8 +285,8 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
     if (!sm100::mbar_wait_warp(&full[st], (t / P.S) & 1, P.err, IM_ERR_FULL)) break;
     const uint8_t* stage = smem + (size_t)st * St::BYTES;
     if constexpr (Q4) {
-      const uint8_t* pa = stage + ra * Q4K_BYTES;
-      const uint8_t* pb = stage + rb * Q4K_BYTES;
+      const uint8_t* pa = stage + ra * BPS;
+      const uint8_t* pb = stage + rb * BPS;
       const uint4 ha = *reinterpret_cast<const uint4*>(pa), hb = *reinterpret_cast<const uint4*>(pb);
       // the eight 6-bit scales / mins of each row as bytes: [0..3] and [4..7]
       const uint32_t sca_lo = ha.y & 0x3F3F3F3Fu, ma_lo = ha.z & 0x3F3F3F3Fu;
@@ -299,18 +306,33 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
           fa[i][e] = 0.f;
           ma[i][e] = 0;
         }
+      // Q5_K: the qh bytes of this lane's k (bit j of byte l is the fifth bit
+      // of element l of sub-block j), the same for every pair
+      uint32_t ha0 = 0, ha1 = 0, hb0 = 0, hb1 = 0;
+      if constexpr (Q5) {
+        ha0 = *reinterpret_cast<const uint32_t*>(pa + 16 + 4 * c);
+        ha1 = *reinterpret_cast<const uint32_t*>(pa + 32 + 4 * c);
+        hb0 = *reinterpret_cast<const uint32_t*>(pb + 16 + 4 * c);
+        hb1 = *reinterpret_cast<const uint32_t*>(pb + 32 + 4 * c);
+      }
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
-        // qs of pair p: bytes 16 + 32p ..; this lane's k = 4c..4c+3 and 16+4c..
-        const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(pa + 16 + 32 * p + 4 * c);
-        const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(pa + 32 + 32 * p + 4 * c);
-        const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(pb + 16 + 32 * p + 4 * c);
-        const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(pb + 32 + 32 * p + 4 * c);
+        // qs of pair p: bytes QS + 32p ..; this lane's k = 4c..4c+3 and 16+4c..
+        const uint32_t wa0 = *reinterpret_cast<const uint32_t*>(pa + QS + 32 * p + 4 * c);
+        const uint32_t wa1 = *reinterpret_cast<const uint32_t*>(pa + QS + 16 + 32 * p + 4 * c);
+        const uint32_t wb0 = *reinterpret_cast<const uint32_t*>(pb + QS + 32 * p + 4 * c);
+        const uint32_t wb1 = *reinterpret_cast<const uint32_t*>(pb + QS + 16 + 32 * p + 4 * c);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           const int j = 2 * p + h;
-          const uint32_t a0 = (h ? wa0 >> 4 : wa0) & 0x0F0F0F0Fu, a1 = (h ? wb0 >> 4 : wb0) & 0x0F0F0F0Fu;
-          const uint32_t a2 = (h ? wa1 >> 4 : wa1) & 0x0F0F0F0Fu, a3 = (h ? wb1 >> 4 : wb1) & 0x0F0F0F0Fu;
+          uint32_t a0 = (h ? wa0 >> 4 : wa0) & 0x0F0F0F0Fu, a1 = (h ? wb0 >> 4 : wb0) & 0x0F0F0F0Fu;
+          uint32_t a2 = (h ? wa1 >> 4 : wa1) & 0x0F0F0F0Fu, a3 = (h ? wb1 >> 4 : wb1) & 0x0F0F0F0Fu;
+          if constexpr (Q5) {  // bit j of every qh byte to bit 4: a left rotation by 4 - j
+            a0 |= __funnelshift_l(ha0, ha0, (4 - j) & 31) & 0x10101010u;
+            a1 |= __funnelshift_l(hb0, hb0, (4 - j) & 31) & 0x10101010u;
+            a2 |= __funnelshift_l(ha1, ha1, (4 - j) & 31) & 0x10101010u;
+            a3 |= __funnelshift_l(hb1, hb1, (4 - j) & 31) & 0x10101010u;
+          }
           const int sh = 8 * (j & 3);
           const float sca = (float)(((j < 4 ? sca_lo : sca_hi) >> sh) & 0xffu);
           const float scb = (float)(((j < 4 ? scb_lo : scb_hi) >> sh) & 0xffu);
@@ -524,7 +546,7 @@ ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms) {
     }
     if (tiles * sp >= 2 * slots) break;
   }
-  const int stage = qt == GGUF_Q4_K ? IM_ROWS * Q4K_BYTES + nt * 4096 + 32 * 8 * 4 + 128
+  const int stage = qt != GGUF_Q6_K ? IM_ROWS * im_block_bytes(qt) + nt * 4096 + 32 * 8 * 4 + 128
                                     : IM_ROWS * Q6K_BODY + IM_ROWS * 16 + nt * 4096 + 32 * 16 * 4 + 128;
   const int fit = ((per_sm == 2 ? IM_HALF_SMEM : IM_MAX_SMEM) - 2 * 8 * 8) / (stage + 16);
   r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
@@ -608,6 +630,7 @@ static cudaError_t im_attrs() {
 
 cudaError_t imma_init_device() {
   cudaError_t e = im_attrs<GGUF_Q4_K>();
+  if (e == cudaSuccess) e = im_attrs<GGUF_Q5_K>();
   if (e == cudaSuccess) e = im_attrs<GGUF_Q6_K>();
   return e;
 }
@@ -617,8 +640,8 @@ size_t imma_counter_bytes(int64_t n) { return (size_t)((n + IM_ROWS - 1) / IM_RO
 
 cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, const float* bias, float* y, void* ws,
                              unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br) {
-  if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
-  const bool q4 = w.type == GGUF_Q4_K;
+  if (w.type != GGUF_Q4_K && w.type != GGUF_Q5_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
+  const bool q4 = w.type != GGUF_Q6_K;  // Q4_K and Q5_K share the activation preparation
   const ImWs L = im_ws(m64, w.n, w.k, num_sms);
   const int sb = (int)w.sb;
   for (int64_t m0 = 0; m0 < m64; m0 += 32) {
@@ -638,12 +661,19 @@ cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, co
     if (launches) ++*launches;
     bracket_record(br.start, s);
     float* yc = y + m0 * w.n;
-    if (q4) {
+    if (w.type == GGUF_Q4_K) {
       switch (nt) {
         case 1: e = launch_im<GGUF_Q4_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
         case 2: e = launch_im<GGUF_Q4_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
         case 3: e = launch_im<GGUF_Q4_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
         default: e = launch_im<GGUF_Q4_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+      }
+    } else if (w.type == GGUF_Q5_K) {
+      switch (nt) {
+        case 1: e = launch_im<GGUF_Q5_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 2: e = launch_im<GGUF_Q5_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 3: e = launch_im<GGUF_Q5_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        default: e = launch_im<GGUF_Q5_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
       }
     } else {
       switch (nt) {

@@ -643,14 +643,17 @@ void tc_counter_span(int64_t m, int64_t n, int64_t k, int num_sms, size_t* offse
 }
 
 bool tc_make_weight_maps(DevWeight& w) {
-  if (w.type == GGUF_Q4_K) {
-    const uint64_t rb = (uint64_t)w.sb * Q4K_BYTES;
-    if (!make_map_2d(&w.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q, rb, (uint64_t)w.n, rb, Q4K_BYTES, TM,
+  if (w.type == GGUF_Q4_K || w.type == GGUF_Q5_K) {
+    // one box = one superblock of 128 rows (Q5_K rows: sb x 176 bytes, the integer-MMA kernel's map)
+    const uint32_t bs = w.type == GGUF_Q4_K ? Q4K_BYTES : Q5K_BYTES;
+    const uint64_t rb = (uint64_t)w.sb * bs;
+    if (!make_map_2d(&w.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q, rb, (uint64_t)w.n, rb, bs, TM,
                      CU_TENSOR_MAP_SWIZZLE_NONE))
       return false;
     w.dmap = w.wmap;
     return true;
   }
+  if (w.type != GGUF_Q6_K) return false;
   const uint64_t rb = (uint64_t)w.sb * Q6K_BODY;
   if (!make_map_2d(&w.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q, rb, (uint64_t)w.n, rb, Q6K_BODY, TM,
                    CU_TENSOR_MAP_SWIZZLE_NONE))

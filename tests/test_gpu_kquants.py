@@ -1,5 +1,6 @@
-"""GGUF Q2_K, Q3_K and Q5_K on the device (kq_kx.cu, and the single-token
-dp4a kernel of kq_dp4a.cu) and the reference's legacy Q5_K rows:
+"""GGUF Q2_K, Q3_K and Q5_K on the device (kq_kx.cu, the single-token dp4a
+kernel of kq_dp4a.cu, Q5_K on the integer-MMA kernel of kq_imma.cu) and the
+reference's legacy Q5_K rows:
 dequantization bit-exact with the oracle (on the gguf-py fixture superblocks
 and on random weights), linears within 1e-3 of max|y| of the oracle's
 sequential f32 product at 1 to 13 tokens, upload from a GGUF file, and the
@@ -90,6 +91,29 @@ def test_one_token_on_both_kernels(gpu_ctx, name, kt, ot, tag, n, k):
     assert rel_err(y_auto, ref) <= TOL
     assert rel_err(y_f32, ref) <= TOL
     assert rel_err(y_auto, y_f32) <= TOL
+    w.free()
+
+
+@pytest.mark.parametrize("n,k,m", [(4096, 4096, 8), (300, 2816, 5), (1024, 14336, 32), (130, 1280, 40)])
+def test_q5k_batches_on_integer_mma_and_the_f32_kernel(gpu_ctx, n, k, m):
+    """Q5_K at 2..64 tokens runs the integer tensor-core kernel under AUTO
+    (32-token chunks above 32) and the f32 kernel under another path."""
+    raw = synthetic.gguf_weight(kq.KQ_GGUF_Q5_K, n, k, seed=n + 7 * k + m)
+    x = synthetic.activations(m, k, seed=m)
+    bias = np.linspace(-1, 1, n).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q5_K, raw, n, k)
+    ref = oracle.gguf_linear(oracle.GGUF_Q5_K, raw, n, k, x, bias)
+    y_mma = np.empty((m, n), np.float32)
+    y_f32 = np.empty((m, n), np.float32)
+    try:
+        w.linear(x, m, y_mma, bias)
+        gpu_ctx.set_path(kq.KQ_PATH_MMA)
+        w.linear(x, m, y_f32, bias)
+    finally:
+        gpu_ctx.set_path(kq.KQ_PATH_AUTO)
+    for t in range(m):
+        assert rel_err(y_mma[t], ref[t]) <= TOL
+        assert rel_err(y_f32[t], ref[t]) <= TOL
     w.free()
 
 
