@@ -75,6 +75,22 @@ int kq_dec_swiglu_linear(kq_ctx *ctx, const kq_weight *w, const float *gate_up, 
                          int flags);
 /* h[0:out_features] += x . W^T (the residual connection fused into the linear). */
 int kq_dec_residual_linear(kq_ctx *ctx, const kq_weight *w, const float *x, float *h, int flags);
+/* Batched forms (m tokens; GGUF Q4_K / Q5_K / Q6_K where the AUTO choice for
+ * this weight and m is the integer tensor-core kernel: Q4_K / Q5_K 2 <= m <=
+ * 64, Q6_K 3 <= m <= 8; KQ_ERR_UNSUPPORTED otherwise, with nothing queued,
+ * and the caller queues kq_dec_rmsnorm / kq_linear_f32 / kq_dec_add).
+ * No reference counterpart: the reference runs these steps one after the
+ * other on the host (layer.rs:169-244).
+ *   norm_linear_batch:     y[m][out_features] = rmsnorm(x[t][0:dim]; norm_w,
+ *                          eps) . W^T, the normalised rows zero past dim
+ *                          (dim a multiple of 4 <= in_features; x rows x_ld
+ *                          floats apart, x_ld >= in_features and a multiple
+ *                          of 4; x and norm_w 16-byte aligned);
+ *   residual_linear_batch: h[m][out_features] += x[m][in_features] . W^T.
+ * flags: KQ_SYNC or 0 (pointers are device pointers). */
+int kq_dec_norm_linear_batch(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t x_ld, int64_t m,
+                             const float *norm_w, int64_t dim, float eps, float *y, int flags);
+int kq_dec_residual_linear_batch(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t m, float *h, int flags);
 /* Tensor-parallel single-token linears (batch 1) for the column-split
  * layout: a projection whose input is split across the ranks (the output
  * projection over this rank's heads, the down projection over its FFN block)

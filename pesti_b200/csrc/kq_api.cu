@@ -1031,6 +1031,58 @@ static int fused_linear(kq_ctx* ctx, const kq_weight* w, const kq::XsInput& in, 
   return KQ_OK;
 }
 
+// Shared checks of the batched decoder forms (m tokens on the integer
+// tensor-core kernel; KQ_ERR_UNSUPPORTED, with nothing queued, where AUTO
+// would pick another kernel family for this weight and m).
+static int batched_linear(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, float* y,
+                          const kq::ImOpts& op, int flags, const char* what) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!w || !x || !y || m < 1) return fail(ctx, KQ_ERR_INVALID_ARG, "%s: null weight, input or output, or m < 1", what);
+  if (flags & ~(KQ_SYNC | KQ_DEVICE_PTRS)) return fail(ctx, KQ_ERR_INVALID_ARG, "%s: bad flags 0x%x", what, flags);
+  if (w->device != ctx->device)
+    return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device, ctx->device);
+  if (w->dw.k == 0 || w->dw.n == 0) return fail(ctx, KQ_ERR_UNSUPPORTED, "%s: empty weight", what);
+  if ((!is_gguf(w->dw.type) && w->dw.type != kq::GGUF_Q5_K) || f32_family(ctx, w->dw, m) != KQ_PATH_IMMA)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "%s: the integer tensor-core kernel does not serve type %d at m = %lld",
+                what, w->dw.type, (long long)m);
+  if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(op.nw)) & 15) ||
+      (reinterpret_cast<uintptr_t>(y) & 3))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "%s: x and the norm weights must be 16-byte aligned, y 4-byte", what);
+  DeviceGuard g(ctx->device);
+  if (g.status != cudaSuccess) return cuda_fail(ctx, g.status, "cudaSetDevice");
+  if (int rc = prepare_f32(ctx, w->dw, m)) return rc;
+  int launches = 0;
+  const cudaError_t e =
+      kq::launch_gemv_imma(w->dw, x, m, nullptr, y, ctx->ws, static_cast<unsigned*>(ctx->ctr), ctx->num_sms,
+                           ctx->dev_err, ctx->stream, &launches, ctx->next_bracket(), op);
+  ctx->launches += launches;
+  if (e != cudaSuccess) return cuda_fail(ctx, e, what);
+  if (flags & KQ_SYNC) return finish_sync(ctx, what);
+  return KQ_OK;
+}
+
+int kq_dec_norm_linear_batch(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t x_ld, int64_t m,
+                             const float* norm_w, int64_t dim, float eps, float* y, int flags) {
+  if (check_ctx(ctx)) return KQ_ERR_INVALID_ARG;
+  if (!norm_w) return fail(ctx, KQ_ERR_INVALID_ARG, "norm_linear_batch: null norm weights");
+  if (!w || dim < 4 || (dim & 3) || dim > w->dw.k || x_ld < w->dw.k || (x_ld & 3))
+    return fail(ctx, KQ_ERR_INVALID_ARG,
+                "norm_linear_batch: dim %lld must be a positive multiple of 4 <= in_features, x_ld %lld a "
+                "multiple of 4 >= in_features", (long long)dim, (long long)x_ld);
+  kq::ImOpts op;
+  op.x_ld = x_ld;
+  op.nw = norm_w;
+  op.dim = (int)dim;
+  op.eps = eps;
+  return batched_linear(ctx, w, x, m, y, op, flags, "norm_linear_batch");
+}
+
+int kq_dec_residual_linear_batch(kq_ctx* ctx, const kq_weight* w, const float* x, int64_t m, float* h, int flags) {
+  kq::ImOpts op;
+  op.accumulate = true;
+  return batched_linear(ctx, w, x, m, h, op, flags, "residual_linear_batch");
+}
+
 // act -1: plain rows; 0 / 1: (gate, up) row pairs through the SwiGLU gate.
 static int set_pairs(kq_ctx* ctx, const kq_weight* w, int act, kq::XsInput& in, const char* what) {
   if (act < -1 || act > 1) return fail(ctx, KQ_ERR_INVALID_ARG, "%s: activation %d", what, act);

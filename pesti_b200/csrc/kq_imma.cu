@@ -71,11 +71,18 @@ __device__ __forceinline__ void split4(int v0, int v1, int v2, int v3, uint32_t&
 //   scl[kb * 32 + t] = 2^e (NaN when the superblock holds a non-finite value)
 // Q6_K: lane = (group s0 = lane/4, c = lane%4) handles groups s0 and s0 + 8:
 //   bq[((tile * sb + kb) * 16 + s) * 32 + 4 * (t % 8) + c] = uint2 {hi(k 4c..4c+3), lo(..)} of group s
-//   ssum[(kb * 32 + t) * 16 + s] = 32 x the sum of the 16 quantized values of group s
+//   ssum as int2 [(kb * 16 + s) * 32 + t] = {-32 x the sum of the 16 high bytes of group s,
+//                                            -32 x the sum of its 16 low bytes}
+//   (the code offset of sum (q - 32) x, applied to each limb's product)
+// With a norm (nw != nullptr) the quantized activations are RMSNorm(x) =
+// x / sqrt(mean(x[0:dim]^2) + eps) * nw, zero past dim: each warp first
+// reduces its token's sum of squares over the whole row (the row is small and
+// L2-resident, so the redundant reads across a token's superblocks are cheap).
 template <int QT>
-__global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict__ x, int m, int slots, int64_t k,
-                                                        int sb, uint4* __restrict__ bq, int* __restrict__ ssum,
-                                                        float* __restrict__ scl) {
+__global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict__ x, int64_t x_ld, int m, int slots,
+                                                        int64_t k, int sb, uint4* __restrict__ bq,
+                                                        int* __restrict__ ssum, float* __restrict__ scl,
+                                                        const float* __restrict__ nw, int dim, float eps) {
   pdl_trigger();
   pdl_wait();  // x may be the previous kernel's output
   const int lane = threadIdx.x & 31;
@@ -100,8 +107,24 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
     }
     return;
   }
-  const float* xs = x + (int64_t)t * k + (int64_t)kb * 256;
-  const float4 a = ldg_f4(xs + ea), b = ldg_f4(xs + eb);
+  const float* xs = x + (int64_t)t * x_ld + (int64_t)kb * 256;
+  float4 a = ldg_f4(xs + ea), b = ldg_f4(xs + eb);
+  if (nw) {
+    const float* xr = x + (int64_t)t * x_ld;
+    float ss = 0.f;
+    for (int i = 4 * lane; i < dim; i += 128) {
+      const float4 v = ldg_f4(xr + i);
+      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rinv = 1.f / sqrtf(ss / (float)dim + eps);
+    const int64_t ga = (int64_t)kb * 256 + ea, gb = (int64_t)kb * 256 + eb;  // dim % 4 == 0: whole float4s
+    const float4 wa = ga < dim ? ldg_f4(nw + ga) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 wb = gb < dim ? ldg_f4(nw + gb) : make_float4(0.f, 0.f, 0.f, 0.f);
+    a = ga < dim ? make_float4(a.x * rinv * wa.x, a.y * rinv * wa.y, a.z * rinv * wa.z, a.w * rinv * wa.w) : wa;
+    b = gb < dim ? make_float4(b.x * rinv * wb.x, b.y * rinv * wb.y, b.z * rinv * wb.z, b.w * rinv * wb.w) : wb;
+  }
   float amax = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
   amax = fmaxf(amax, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
 #pragma unroll
@@ -130,14 +153,20 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
   } else {
     *dst2a = make_uint2(o.x, o.z);
     *dst2b = make_uint2(o.y, o.w);
-    int sa = v0 + v1 + v2 + v3, sbv = v4 + v5 + v6 + v7;
-    sa += __shfl_xor_sync(0xffffffffu, sa, 1);
-    sa += __shfl_xor_sync(0xffffffffu, sa, 2);
-    sbv += __shfl_xor_sync(0xffffffffu, sbv, 1);
-    sbv += __shfl_xor_sync(0xffffffffu, sbv, 2);
-    if (c == 0) {  // times the code offset 32
-      ssum[((int64_t)kb * 32 + t) * 16 + j] = 32 * sa;
-      ssum[((int64_t)kb * 32 + t) * 16 + j + 8] = 32 * sbv;
+    // limb sums of groups j (v0..v3) and j + 8 (v4..v7): high bytes v >> 8, low bytes v & 255
+    int ha = (v0 >> 8) + (v1 >> 8) + (v2 >> 8) + (v3 >> 8), la = (v0 & 255) + (v1 & 255) + (v2 & 255) + (v3 & 255);
+    int hb = (v4 >> 8) + (v5 >> 8) + (v6 >> 8) + (v7 >> 8), lb = (v4 & 255) + (v5 & 255) + (v6 & 255) + (v7 & 255);
+#pragma unroll
+    for (int o2 = 1; o2 <= 2; o2 <<= 1) {
+      ha += __shfl_xor_sync(0xffffffffu, ha, o2);
+      la += __shfl_xor_sync(0xffffffffu, la, o2);
+      hb += __shfl_xor_sync(0xffffffffu, hb, o2);
+      lb += __shfl_xor_sync(0xffffffffu, lb, o2);
+    }
+    if (c == 0) {  // times the code offset 32, negated: the MMAs' start values
+      int2* s2 = reinterpret_cast<int2*>(ssum);
+      s2[((int64_t)kb * 16 + j) * 32 + t] = make_int2(-32 * ha, -32 * la);
+      s2[((int64_t)kb * 16 + j + 8) * 32 + t] = make_int2(-32 * hb, -32 * lb);
     }
   }
   if (lane == 0) scl[(int64_t)kb * 32 + t] = factor;
@@ -146,15 +175,25 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
 // Device bytes of one superblock in the weight's tensor map box.
 constexpr int im_block_bytes(int qt) { return qt == GGUF_Q4_K ? Q4K_BYTES : qt == GGUF_Q5_K ? Q5K_BYTES : Q6K_BODY; }
 
+// Bytes of one ring stage for type qt and nt 8-token tiles: the weight box,
+// Q6_K's d box, the activation fragments, the activation sums of the 32 token
+// slots (Q4_K / Q5_K: one int per sub-block; Q6_K: two limb sums per group)
+// and the 32 slots' 2^e.  The kernel's stage layout (ImStage) and the launch's
+// shared-memory size (im_shape) both come from here.
+constexpr int im_stage_w(int qt) { return IM_ROWS * im_block_bytes(qt); }
+constexpr int im_stage_d(int qt) { return qt == GGUF_Q6_K ? IM_ROWS * 16 : 0; }
+constexpr int im_stage_s(int qt) { return qt == GGUF_Q6_K ? 32 * 16 * 8 : 32 * 8 * 4; }
+constexpr int im_stage_bytes(int qt, int nt) { return im_stage_w(qt) + im_stage_d(qt) + nt * 4096 + im_stage_s(qt) + 32 * 4; }
+
 template <int QT, int NT>
 struct ImStage {
-  static constexpr bool Q4 = QT != GGUF_Q6_K;                     // Q4_K / Q5_K: 32-weight sub-blocks
-  static constexpr int W = IM_ROWS * im_block_bytes(QT);           // 18432 / 22528 / 26624
-  static constexpr int D = Q4 ? 0 : IM_ROWS * 16;                  // Q6_K: d of 8 superblocks per row
-  static constexpr int B = NT * 4096;                              // activation fragments, 8 tokens per tile
-  static constexpr int S = 32 * (Q4 ? 8 : 16) * 4;                 // activation sums of the 32 token slots
-  static constexpr int F = 32 * 4;                                 // 2^e of the 32 token slots
-  static constexpr int BYTES = W + D + B + S + F;                  // a multiple of 128
+  static constexpr int W = im_stage_w(QT);     // 18432 / 22528 / 26624
+  static constexpr int D = im_stage_d(QT);     // Q6_K: d of 8 superblocks per row
+  static constexpr int B = NT * 4096;          // activation fragments, 8 tokens per tile
+  static constexpr int S = im_stage_s(QT);     // activation sums of the 32 token slots
+  static constexpr int F = 32 * 4;             // 2^e of the 32 token slots
+  static constexpr int BYTES = W + D + B + S + F;
+  static_assert(BYTES == im_stage_bytes(QT, NT) && BYTES % 128 == 0, "stage layout");
 };
 
 struct ImParams {
@@ -167,6 +206,7 @@ struct ImParams {
   unsigned* ctr;
   int64_t n;
   int sb, m, splits, kb_per, S;
+  int accumulate;  // y += the product instead of y = (the residual update)
   int* err;
 };
 
@@ -297,13 +337,15 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       const uint32_t mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
       const uint4* bs = reinterpret_cast<const uint4*>(stage + St::W);
       const int* ss = reinterpret_cast<const int*>(stage + St::W + St::B);
-      float fa[NT][4];
-      int ma[NT][4];
+      // sum over sub-blocks of scale x limb product, exact in int32: a
+      // sub-block's high-limb sum is < 2^16 in size, its low-limb one < 2^18
+      // (codes up to 31), so 8 six-bit scales keep them below 2^25 / 2^27
+      int aH[NT][4], aL[NT][4], ma[NT][4];
 #pragma unroll
       for (int i = 0; i < NT; ++i)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          fa[i][e] = 0.f;
+          aH[i][e] = aL[i][e] = 0;
           ma[i][e] = 0;
         }
       // Q5_K: the qh bytes of this lane's k (bit j of byte l is the fifth bit
@@ -334,8 +376,8 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
             a3 |= __funnelshift_l(hb1, hb1, (4 - j) & 31) & 0x10101010u;
           }
           const int sh = 8 * (j & 3);
-          const float sca = (float)(((j < 4 ? sca_lo : sca_hi) >> sh) & 0xffu);
-          const float scb = (float)(((j < 4 ? scb_lo : scb_hi) >> sh) & 0xffu);
+          const int sca = (int)(((j < 4 ? sca_lo : sca_hi) >> sh) & 0xffu);
+          const int scb = (int)(((j < 4 ? scb_lo : scb_hi) >> sh) & 0xffu);
           const int mina = (int)(((j < 4 ? ma_lo : ma_hi) >> sh) & 0xffu);
           const int minb = (int)(((j < 4 ? mb_lo : mb_hi) >> sh) & 0xffu);
 #pragma unroll
@@ -345,10 +387,14 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
             mma_u8s8(ch, a0, a1, a2, a3, bv.x, bv.y);
             mma_u8u8(cl, a0, a1, a2, a3, bv.z, bv.w);
             // C: [0], [1] row g, tokens 8i + 2c, +1; [2], [3] row g + 8
-            fa[i][0] = fmaf((float)(ch[0] * 256 + cl[0]), sca, fa[i][0]);
-            fa[i][1] = fmaf((float)(ch[1] * 256 + cl[1]), sca, fa[i][1]);
-            fa[i][2] = fmaf((float)(ch[2] * 256 + cl[2]), scb, fa[i][2]);
-            fa[i][3] = fmaf((float)(ch[3] * 256 + cl[3]), scb, fa[i][3]);
+            aH[i][0] += sca * ch[0];
+            aH[i][1] += sca * ch[1];
+            aH[i][2] += scb * ch[2];
+            aH[i][3] += scb * ch[3];
+            aL[i][0] += sca * cl[0];
+            aL[i][1] += sca * cl[1];
+            aL[i][2] += scb * cl[2];
+            aL[i][3] += scb * cl[3];
             const int s0 = ss[(8 * i + 2 * c) * 8 + j], s1 = ss[(8 * i + 2 * c + 1) * 8 + j];
             ma[i][0] += mina * s0;
             ma[i][1] += mina * s1;
@@ -370,8 +416,10 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       for (int i = 0; i < NT; ++i) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          tot[i][e] = fmaf(f[i][e], fmaf(da, fa[i][e], -dma * (float)ma[i][e]), tot[i][e]);
-          tot[i][2 + e] = fmaf(f[i][e], fmaf(db, fa[i][2 + e], -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
+          const float va = fmaf(256.f, (float)aH[i][e], (float)aL[i][e]);
+          const float vb = fmaf(256.f, (float)aH[i][2 + e], (float)aL[i][2 + e]);
+          tot[i][e] = fmaf(f[i][e], fmaf(da, va, -dma * (float)ma[i][e]), tot[i][e]);
+          tot[i][2 + e] = fmaf(f[i][e], fmaf(db, vb, -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
         }
       }
     } else {
@@ -380,10 +428,16 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       const uint16_t* dtile = reinterpret_cast<const uint16_t*>(stage + St::W);
       const uint4 sca4 = *reinterpret_cast<const uint4*>(pa + 192), scb4 = *reinterpret_cast<const uint4*>(pb + 192);
       const uint2* bs = reinterpret_cast<const uint2*>(stage + St::W + St::D);
-      const int* ss = reinterpret_cast<const int*>(stage + St::W + St::D + St::B);
-      float fa[NT][4];
+      // {-32 sum hi, -32 sum lo} of tokens 8i + 2c and 8i + 2c + 1 for group sg: int4 [sg][4i + c]
+      const int4* ss4 = reinterpret_cast<const int4*>(stage + St::W + St::D + St::B);
+      // sum over groups of scale x limb product, exact in int32: a group's
+      // high-limb sum (q - 32) hi is < 2^15 in size, its low-limb one < 2^17,
+      // so 16 groups of int8 scales stay below 2^26 / 2^28
+      int aH[NT][4], aL[NT][4];
 #pragma unroll
-      for (int i = 0; i < NT; ++i) fa[i][0] = fa[i][1] = fa[i][2] = fa[i][3] = 0.f;
+      for (int i = 0; i < NT; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) aH[i][e] = aL[i][e] = 0;
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -404,21 +458,24 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
               const uint32_t a1 = ((nib ? qlb >> 4 : qlb) & 0x0F0F0F0Fu) | (((qhb >> (2 * G)) & 0x03030303u) << 4);
               const uint32_t wsa = sg < 4 ? sca4.x : sg < 8 ? sca4.y : sg < 12 ? sca4.z : sca4.w;
               const uint32_t wsb = sg < 4 ? scb4.x : sg < 8 ? scb4.y : sg < 12 ? scb4.z : scb4.w;
-              const float sca = (float)(int)(int8_t)(wsa >> (8 * (sg & 3)));
-              const float scb = (float)(int)(int8_t)(wsb >> (8 * (sg & 3)));
+              const int sca = (int)(int8_t)(wsa >> (8 * (sg & 3)));
+              const int scb = (int)(int8_t)(wsb >> (8 * (sg & 3)));
 #pragma unroll
               for (int i = 0; i < NT; ++i) {
                 const uint2 bv = bs[(i * 16 + sg) * 32 + lane];
-                // sum (q - 32) x = sum q x - 32 sum x: the low-byte product starts
-                // from -32 sum x; |.| < 2^24, exact in int32 and as a float
-                const int s0 = ss[(8 * i + 2 * c) * 16 + sg], s1 = ss[(8 * i + 2 * c + 1) * 16 + sg];
-                int ch[4] = {0, 0, 0, 0}, cl[4] = {-s0, -s1, -s0, -s1};
+                // sum (q - 32) x per limb: each product starts from -32 x its limb sum
+                const int4 sv = ss4[sg * 16 + 4 * i + c];
+                int ch[4] = {sv.x, sv.z, sv.x, sv.z}, cl[4] = {sv.y, sv.w, sv.y, sv.w};
                 mma16_u8s8(ch, a0, a1, bv.x);
                 mma16_u8u8(cl, a0, a1, bv.y);
-                fa[i][0] = fmaf((float)(ch[0] * 256 + cl[0]), sca, fa[i][0]);
-                fa[i][1] = fmaf((float)(ch[1] * 256 + cl[1]), sca, fa[i][1]);
-                fa[i][2] = fmaf((float)(ch[2] * 256 + cl[2]), scb, fa[i][2]);
-                fa[i][3] = fmaf((float)(ch[3] * 256 + cl[3]), scb, fa[i][3]);
+                aH[i][0] += sca * ch[0];
+                aH[i][1] += sca * ch[1];
+                aH[i][2] += scb * ch[2];
+                aH[i][3] += scb * ch[3];
+                aL[i][0] += sca * cl[0];
+                aL[i][1] += sca * cl[1];
+                aL[i][2] += scb * cl[2];
+                aL[i][3] += scb * cl[3];
               }
             }
           }
@@ -436,8 +493,10 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       for (int i = 0; i < NT; ++i) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          tot[i][e] = fmaf(f[i][e] * da, fa[i][e], tot[i][e]);
-          tot[i][2 + e] = fmaf(f[i][e] * db, fa[i][2 + e], tot[i][2 + e]);
+          const float va = fmaf(256.f, (float)aH[i][e], (float)aL[i][e]);
+          const float vb = fmaf(256.f, (float)aH[i][2 + e], (float)aL[i][2 + e]);
+          tot[i][e] = fmaf(f[i][e] * da, va, tot[i][e]);
+          tot[i][2 + e] = fmaf(f[i][e] * db, vb, tot[i][2 + e]);
         }
       }
     }
@@ -453,8 +512,17 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
     for (int e = 0; e < 2; ++e) {
       const int tk = 8 * i + 2 * c + e;
       if (tk < P.m) {
-        if (rowa < P.n) dst[(int64_t)tk * P.n + rowa] = tot[i][e] + (add_bias ? P.bias[rowa] : 0.f);
-        if (rowb < P.n) dst[(int64_t)tk * P.n + rowb] = tot[i][2 + e] + (add_bias ? P.bias[rowb] : 0.f);
+        // one writer per output; the residual form adds to what y holds (only the last write, splits == 1)
+        if (rowa < P.n) {
+          float* d = dst + (int64_t)tk * P.n + rowa;
+          const float v = tot[i][e] + (add_bias ? P.bias[rowa] : 0.f);
+          *d = P.splits == 1 && P.accumulate ? *d + v : v;
+        }
+        if (rowb < P.n) {
+          float* d = dst + (int64_t)tk * P.n + rowb;
+          const float v = tot[i][2 + e] + (add_bias ? P.bias[rowb] : 0.f);
+          *d = P.splits == 1 && P.accumulate ? *d + v : v;
+        }
       }
     }
   if (P.splits == 1) return;
@@ -502,10 +570,17 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       const int e = threadIdx.x + u * 32 * IM_WARPS;
       if (e < total4) {
         float* yo = P.y + (int64_t)(e / (IM_ROWS / 4)) * P.n + row0 + 4 * (e & (IM_ROWS / 4 - 1));
-        yo[0] = v[u].x;
-        yo[1] = v[u].y;
-        yo[2] = v[u].z;
-        yo[3] = v[u].w;
+        if (P.accumulate) {
+          yo[0] += v[u].x;
+          yo[1] += v[u].y;
+          yo[2] += v[u].z;
+          yo[3] += v[u].w;
+        } else {
+          yo[0] = v[u].x;
+          yo[1] = v[u].y;
+          yo[2] = v[u].z;
+          yo[3] = v[u].w;
+        }
       }
     }
   } else {
@@ -514,7 +589,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       const int64_t idx = (int64_t)tk * P.n + row0 + r;
       float v = P.bias ? P.bias[row0 + r] : 0.f;
       for (int q = 0; q < P.splits; ++q) v += __ldcg(P.part + (size_t)q * P.m * P.n + idx);
-      P.y[idx] = v;
+      P.y[idx] = P.accumulate ? P.y[idx] + v : v;
     }
   }
   if (threadIdx.x == 0) P.ctr[blockIdx.x] = 0u;  // ready for the next call (stream-ordered)
@@ -546,8 +621,7 @@ ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms) {
     }
     if (tiles * sp >= 2 * slots) break;
   }
-  const int stage = qt != GGUF_Q6_K ? IM_ROWS * im_block_bytes(qt) + nt * 4096 + 32 * 8 * 4 + 128
-                                    : IM_ROWS * Q6K_BODY + IM_ROWS * 16 + nt * 4096 + 32 * 16 * 4 + 128;
+  const int stage = im_stage_bytes(qt, nt);
   const int fit = ((per_sm == 2 ? IM_HALF_SMEM : IM_MAX_SMEM) - 2 * 8 * 8) / (stage + 16);
   r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
   r.smem = (size_t)r.S * stage + (size_t)2 * r.S * 8;
@@ -564,7 +638,7 @@ ImWs im_ws(int64_t m, int64_t n, int64_t k, int num_sms) {
   ImWs L;
   L.bq = 0;
   L.ssum = (size_t)nt * sb * 4096;
-  L.scl = L.ssum + (size_t)sb * 32 * 16 * 4;  // room for Q6_K's 16 group sums
+  L.scl = L.ssum + (size_t)sb * 32 * 16 * 8;  // room for Q6_K's 16 groups x two limb sums
   L.part = (L.scl + (size_t)sb * 32 * 4 + 255) & ~size_t(255);
   // partials of the largest chunk: a full 32-token chunk and the tail chunk
   // can split K differently (one or two CTAs per SM); the split count does
@@ -581,7 +655,7 @@ ImWs im_ws(int64_t m, int64_t n, int64_t k, int num_sms) {
 
 template <int QT, int NT>
 cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const float* bias, float* y, unsigned* ctr,
-                      int num_sms, int* err, cudaStream_t s) {
+                      int num_sms, int* err, cudaStream_t s, bool accumulate) {
   const ImShape sh = im_shape(QT, NT, w.n, (int)w.sb, num_sms);
   char* base = static_cast<char*>(ws);
   ImParams P;
@@ -598,6 +672,7 @@ cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const 
   P.splits = sh.splits;
   P.kb_per = sh.kb_per;
   P.S = sh.S;
+  P.accumulate = accumulate ? 1 : 0;
   P.err = err;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((w.n + IM_ROWS - 1) / IM_ROWS), (unsigned)sh.splits);
@@ -639,8 +714,10 @@ size_t imma_workspace_bytes(int64_t m, int64_t n, int64_t k, int num_sms) { retu
 size_t imma_counter_bytes(int64_t n) { return (size_t)((n + IM_ROWS - 1) / IM_ROWS) * 4 + 256; }
 
 cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, const float* bias, float* y, void* ws,
-                             unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br) {
+                             unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br,
+                             const ImOpts& op) {
   if (w.type != GGUF_Q4_K && w.type != GGUF_Q5_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
+  const int64_t x_ld = op.x_ld ? op.x_ld : w.k;
   const bool q4 = w.type != GGUF_Q6_K;  // Q4_K and Q5_K share the activation preparation
   const ImWs L = im_ws(m64, w.n, w.k, num_sms);
   const int sb = (int)w.sb;
@@ -653,34 +730,35 @@ cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, co
     uint4* bq = reinterpret_cast<uint4*>(base + L.bq);
     int* ssum = reinterpret_cast<int*>(base + L.ssum);
     float* scl = reinterpret_cast<float*>(base + L.scl);
-    cudaError_t e = q4 ? launch_pdl(imma_prep_kernel<GGUF_Q4_K>, pg, dim3(256), 0, s, x + m0 * w.k, m, nt * 8, w.k,
-                                    sb, bq, ssum, scl)
-                       : launch_pdl(imma_prep_kernel<GGUF_Q6_K>, pg, dim3(256), 0, s, x + m0 * w.k, m, nt * 8, w.k,
-                                    sb, bq, ssum, scl);
+    const float* xc = x + m0 * x_ld;
+    cudaError_t e = q4 ? launch_pdl(imma_prep_kernel<GGUF_Q4_K>, pg, dim3(256), 0, s, xc, x_ld, m, nt * 8, w.k, sb,
+                                    bq, ssum, scl, op.nw, op.dim, op.eps)
+                       : launch_pdl(imma_prep_kernel<GGUF_Q6_K>, pg, dim3(256), 0, s, xc, x_ld, m, nt * 8, w.k, sb,
+                                    bq, ssum, scl, op.nw, op.dim, op.eps);
     if (e != cudaSuccess) return e;
     if (launches) ++*launches;
     bracket_record(br.start, s);
     float* yc = y + m0 * w.n;
     if (w.type == GGUF_Q4_K) {
       switch (nt) {
-        case 1: e = launch_im<GGUF_Q4_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        case 2: e = launch_im<GGUF_Q4_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        case 3: e = launch_im<GGUF_Q4_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        default: e = launch_im<GGUF_Q4_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 1: e = launch_im<GGUF_Q4_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        case 2: e = launch_im<GGUF_Q4_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        case 3: e = launch_im<GGUF_Q4_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        default: e = launch_im<GGUF_Q4_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
       }
     } else if (w.type == GGUF_Q5_K) {
       switch (nt) {
-        case 1: e = launch_im<GGUF_Q5_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        case 2: e = launch_im<GGUF_Q5_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        case 3: e = launch_im<GGUF_Q5_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        default: e = launch_im<GGUF_Q5_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 1: e = launch_im<GGUF_Q5_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        case 2: e = launch_im<GGUF_Q5_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        case 3: e = launch_im<GGUF_Q5_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        default: e = launch_im<GGUF_Q5_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
       }
     } else {
       switch (nt) {
-        case 1: e = launch_im<GGUF_Q6_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        case 2: e = launch_im<GGUF_Q6_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        case 3: e = launch_im<GGUF_Q6_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
-        default: e = launch_im<GGUF_Q6_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s); break;
+        case 1: e = launch_im<GGUF_Q6_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        case 2: e = launch_im<GGUF_Q6_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        case 3: e = launch_im<GGUF_Q6_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
+        default: e = launch_im<GGUF_Q6_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
       }
     }
     bracket_record(br.stop, s);

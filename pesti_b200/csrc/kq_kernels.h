@@ -124,16 +124,27 @@ cudaError_t launch_gemv_kx(const DevWeight& w, const float* x, int64_t m, const 
 // Bit-exact dequantization of rows [row0, row0 + nrows) to f32 [nrows][k].
 cudaError_t launch_dequant_kx(const DevWeight& w, int64_t row0, int64_t nrows, float* out, cudaStream_t s);
 
-// ---- integer tensor-core batched decode, GGUF Q4_K: kq_imma.cu ----
+// ---- integer tensor-core batched decode, GGUF Q4_K / Q5_K / Q6_K: kq_imma.cu ----
 cudaError_t imma_init_device();
 // Scratch (bytes) for m tokens of an n x k weight, and the zeroed counters.
 size_t imma_workspace_bytes(int64_t m, int64_t n, int64_t k, int num_sms);
 size_t imma_counter_bytes(int64_t n);
-// y = x . W^T (+bias) for GGUF Q4_K (cudaErrorNotSupported otherwise); any m,
-// in chunks of 32 tokens; *err receives 27 / 28 if a pipeline wait gave up.
+// Options of the batched decoder forms: x rows x_ld floats apart (0: k);
+// nw != nullptr: the activations are RMSNorm(x[0:dim]; nw, eps), zero past dim
+// (dim a multiple of 4, x rows 16-byte aligned); accumulate: y += the product.
+struct ImOpts {
+  int64_t x_ld = 0;
+  const float* nw = nullptr;
+  int dim = 0;
+  float eps = 0.f;
+  bool accumulate = false;
+};
+// y = x . W^T (+bias) for GGUF Q4_K / Q5_K / Q6_K (cudaErrorNotSupported
+// otherwise); any m, in chunks of 32 tokens; *err receives 27 / 28 if a
+// pipeline wait gave up.
 cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y, void* ws,
                              unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches,
-                             Bracket br = Bracket());
+                             Bracket br = Bracket(), const ImOpts& op = ImOpts());
 
 // ---- CUDA-core integer decode path: kq_dp4a.cu ----
 constexpr int DP4A_MAX_M = 4;

@@ -77,6 +77,8 @@ def _bind(lib: ctypes.CDLL) -> ctypes.CDLL:
         "kq_dec_norm_linear": [P, P, P, P, I64, F, I, P, P, I],
         "kq_dec_swiglu_linear": [P, P, P, I, P, P, I],
         "kq_dec_residual_linear": [P, P, P, P, I],
+        "kq_dec_norm_linear_batch": [P, P, P, I64, I64, P, I64, F, P, I],
+        "kq_dec_residual_linear_batch": [P, P, P, I64, P, I],
         "kq_dec_rope_attention": [P, P, I64, P, P, P, I64, I64, I, I, I, I64, I64, F, P, Z],
         "kq_dec_tp_partial_linear": [P, P, P, I, I],
         "kq_dec_tp_reduce_linear": [P, P, P, P, P, I64, F, I, P, I],
@@ -159,6 +161,11 @@ class Decoder:
         # RMSNorm, SwiGLU and the residual adds inside the single-token GEMVs;
         # prefetch: each linear pulls the next one's weight into L2
         self.fused_attention, self.fused, self.prefetch = fused, fused and batch == 1, prefetch
+        # batch > 1: RMSNorm inside the integer-MMA linears' activation
+        # preparation and the residual adds in their epilogue, where that
+        # kernel serves the weight at this batch (the calls report
+        # unsupported otherwise and the separate kernels run)
+        self.fuse_batch = fused and batch > 1
         # column split (batch 1, tensor parallel): the output and down
         # projections hold W[:, this rank's heads / FFN block] and exchange
         # partial residual vectors (2 exchanges per layer) instead of
@@ -322,9 +329,27 @@ class Decoder:
             self._check(self.lib.kq_dec_norm_linear(c, w.handle, ptr(self.h), ptr(norm), cfg.dim, cfg.eps, act, None,
                                                     ptr(y), 0), "norm_linear")
             return
+        if self.fuse_batch:
+            rc = self.lib.kq_dec_norm_linear_batch(c, w.handle, ptr(self.h), self.Dp, self.batch, ptr(norm), cfg.dim,
+                                                   cfg.eps, ptr(y), 0)
+            if rc != kq.KQ_ERR_UNSUPPORTED:
+                self._check(rc, "norm_linear_batch")
+                return
         self._check(self.lib.kq_dec_rmsnorm(c, ptr(self.h), self.Dp, ptr(norm), ptr(self.a), self.Dp, self.batch,
                                             cfg.dim, cfg.eps), "rmsnorm")
         w.linear(self.a, self.batch, y, device_ptrs=True)
+
+    def _residual_batch(self, w, x) -> bool:
+        """h += x . W^T in the linear's epilogue (batch > 1, one GPU, residual
+        rows not padded); False when the caller must queue linear + add."""
+        if not self.fuse_batch or self.world > 1 or self.Dp != self.cfg.dim:
+            return False
+        rc = self.lib.kq_dec_residual_linear_batch(self.ctx.handle, w.handle, ctypes.c_void_p(x.data_ptr()),
+                                                   self.batch, ctypes.c_void_p(self.h.data_ptr()), 0)
+        if rc == kq.KQ_ERR_UNSUPPORTED:
+            return False
+        self._check(rc, "residual_linear_batch")
+        return True
 
     def step(self, pos: int) -> None:
         """Queue one decode step for the tokens in ``self.tokens`` at position
@@ -368,7 +393,7 @@ class Decoder:
                 self._gather(self.o, D, r0, r1 - r0, self.h, self.Dp, True)
             elif self.fused:
                 self._check(lib.kq_dec_residual_linear(c, L["o"].handle, ptr(self.attn), ptr(self.h), 0), "o")
-            else:
+            elif not self._residual_batch(L["o"], self.attn):
                 L["o"].linear(self.attn, B, self.o, device_ptrs=True)
                 self._check(lib.kq_dec_add(c, ptr(self.h), self.Dp, ptr(self.o), D, B, D), "add")
             if self.fused and not tp:
@@ -383,10 +408,11 @@ class Decoder:
                                           self.swiglu_mode), "swiglu")
             if tp:
                 self._gather(self.s_r, F, f0, f1 - f0, self.s, F, False)
-            L["down"].linear(self.s, B, self.dn, device_ptrs=True)
             if tp:
+                L["down"].linear(self.s, B, self.dn, device_ptrs=True)
                 self._gather(self.dn, D, r0, r1 - r0, self.h, self.Dp, True)
-            else:
+            elif not self._residual_batch(L["down"], self.s):
+                L["down"].linear(self.s, B, self.dn, device_ptrs=True)
                 self._check(lib.kq_dec_add(c, ptr(self.h), self.Dp, ptr(self.dn), D, B, D), "add")
         v0, v1 = self.v_rows
         logits = self.logits_r if tp else self.logits

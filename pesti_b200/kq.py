@@ -68,7 +68,8 @@ EXPORTED_SYMBOLS = (
     "kq_tp_create", "kq_tp_handle", "kq_tp_open", "kq_tp_linear_f32", "kq_tp_allgather_f32",
     "kq_tp_destroy", "kq_dec_rmsnorm", "kq_dec_rope_append", "kq_dec_attention_scratch", "kq_dec_attention",
     "kq_dec_swiglu", "kq_dec_add", "kq_dec_embed", "kq_dec_norm_linear", "kq_dec_swiglu_linear",
-    "kq_dec_residual_linear", "kq_dec_rope_attention", "kq_dec_tp_partial_linear", "kq_dec_tp_reduce_linear",
+    "kq_dec_residual_linear", "kq_dec_norm_linear_batch", "kq_dec_residual_linear_batch", "kq_dec_rope_attention",
+    "kq_dec_tp_partial_linear", "kq_dec_tp_reduce_linear",
     "kq_step_create", "kq_step_linear", "kq_step_attention", "kq_step_run", "kq_step_trace", "kq_step_destroy",
     "kq_gguf_open", "kq_gguf_close", "kq_gguf_tensor_count", "kq_gguf_find_tensor", "kq_gguf_tensor_info",
     "kq_gguf_read_tensor", "kq_gguf_upload", "kq_gguf_meta_count", "kq_gguf_find_meta", "kq_gguf_meta_info",

@@ -168,3 +168,85 @@ def test_prefetch_hint_leaves_results_unchanged(gpu_ctx):
             gpu_ctx.synchronize()
             assert torch.equal(y, plain[i])
     gpu_ctx.prefetch_next(None)
+
+
+BATCH_TYPES = {"Q4_K": (kq.KQ_GGUF_Q4_K, oracle.GGUF_Q4_K), "Q5_K": (kq.KQ_GGUF_Q5_K, oracle.GGUF_Q5_K),
+               "Q6_K": (kq.KQ_GGUF_Q6_K, oracle.GGUF_Q6_K)}
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q5_K", "Q6_K"])
+@pytest.mark.parametrize("n,k,dim,m", [(256, 1024, 896, 8), (300, 4096, 4096, 5), (1024, 14336, 14336, 3),
+                                       (600, 4096, 4000, 40)])
+def test_batched_norm_linear_matches_rmsnorm_then_linear(gpu_ctx, dt, n, k, dim, m):
+    """kq_dec_norm_linear_batch: every token's RMSNorm inside the integer-MMA
+    kernel's activation preparation; rows of x x_ld = k + 8 floats apart."""
+    kt, ot = BATCH_TYPES[dt]
+    if dt == "Q6_K" and m > 8:
+        m = 8  # Q6_K runs integer MMA up to 8 tokens
+    rng = np.random.default_rng(n + k + m)
+    raw = synthetic.gguf_weight(kt, n, k, seed=k + 1)
+    ld = k + 8
+    h = np.zeros((m, ld), np.float32)
+    h[:, :dim] = 3.0 * rng.standard_normal((m, dim))
+    h[:, dim:] = 7.0  # past dim (and past k): must not enter
+    nw = (1.0 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    hd, nwd, yd = _dev(h), _dev(nw), _dev(np.full((m, n), np.nan, np.float32))
+    rc = _lib(gpu_ctx).kq_dec_norm_linear_batch(gpu_ctx.handle, w.handle, _p(hd), ld, m, _p(nwd), dim, 1e-5, _p(yd),
+                                                kq.KQ_SYNC)
+    gpu_ctx.check(rc, "norm_linear_batch")
+    a = np.zeros((m, k), np.float32)
+    a[:, :dim] = decoder_oracle.rmsnorm(h[:, :dim], nw, 1e-5)
+    ref = a.astype(np.float64) @ _w64(ot, raw, n, k).T
+    y = yd.cpu().numpy()
+    for t in range(m):
+        assert rel_err(y[t], ref[t]) <= TOL
+    w.free()
+
+
+@pytest.mark.parametrize("dt", ["Q4_K", "Q5_K", "Q6_K"])
+@pytest.mark.parametrize("n,k,m", [(4096, 4096, 8), (4096, 14336, 4), (130, 1024, 33)])
+def test_batched_residual_linear_adds_into_h(gpu_ctx, dt, n, k, m):
+    """kq_dec_residual_linear_batch: h += x . W^T from the kernel's epilogue,
+    with and without split-K (the 4096-row cases split K across CTAs)."""
+    kt, ot = BATCH_TYPES[dt]
+    if dt == "Q6_K" and m > 8:
+        m = 8
+    raw = synthetic.gguf_weight(kt, n, k, seed=n + 3)
+    x = synthetic.activations(m, k, seed=m + 5)
+    h0 = np.random.default_rng(9).standard_normal((m, n)).astype(np.float32)
+    w = kq.Weight(gpu_ctx, kt, raw, n, k)
+    xd, hd = _dev(x), _dev(h0)
+    lib = _lib(gpu_ctx)
+    for rep in range(2):  # twice: the second call adds onto the first's result
+        gpu_ctx.check(lib.kq_dec_residual_linear_batch(gpu_ctx.handle, w.handle, _p(xd), m, _p(hd), kq.KQ_SYNC),
+                      "residual_linear_batch")
+        ref = h0.astype(np.float64) + (rep + 1) * (x.astype(np.float64) @ _w64(ot, raw, n, k).T)
+        got = hd.cpu().numpy()
+        for t in range(m):
+            assert rel_err(got[t] - h0[t], ref[t] - h0[t]) <= TOL
+    w.free()
+
+
+def test_batched_forms_report_unsupported_cases(gpu_ctx):
+    """Where AUTO picks another kernel family (one token; Q6_K above 8
+    tokens; Q2_K) the batched forms queue nothing and say so."""
+    lib = _lib(gpu_ctx)
+    x = _dev(np.zeros((16, 1024), np.float32))
+    nwd = _dev(np.ones(1024, np.float32))
+    y = _dev(np.zeros((16, 256), np.float32))
+    for kt, m in [(kq.KQ_GGUF_Q4_K, 1), (kq.KQ_GGUF_Q6_K, 9), (kq.KQ_GGUF_Q2_K, 4)]:
+        w = kq.Weight(gpu_ctx, kt, synthetic.gguf_weight(kt, 256, 1024, seed=1), 256, 1024)
+        launches = gpu_ctx.launch_count
+        assert lib.kq_dec_residual_linear_batch(gpu_ctx.handle, w.handle, _p(x), m, _p(y), 0) == kq.KQ_ERR_UNSUPPORTED
+        assert lib.kq_dec_norm_linear_batch(gpu_ctx.handle, w.handle, _p(x), 1024, m, _p(nwd), 1024, 1e-5, _p(y),
+                                            0) == kq.KQ_ERR_UNSUPPORTED
+        assert gpu_ctx.launch_count == launches
+        w.free()
+    w = kq.Weight(gpu_ctx, kq.KQ_GGUF_Q4_K, synthetic.gguf_weight(kq.KQ_GGUF_Q4_K, 256, 1024, seed=1), 256, 1024)
+    # bad norm sizes and strides
+    assert lib.kq_dec_norm_linear_batch(gpu_ctx.handle, w.handle, _p(x), 1024, 4, _p(nwd), 1026, 1e-5, _p(y),
+                                        0) == kq.KQ_ERR_INVALID_ARG
+    assert lib.kq_dec_norm_linear_batch(gpu_ctx.handle, w.handle, _p(x), 1000, 4, _p(nwd), 1000, 1e-5, _p(y),
+                                        0) == kq.KQ_ERR_INVALID_ARG
+    w.free()
