@@ -829,6 +829,10 @@ def measure_decoder(args, workload, batch, rank, world, local_rank, steps, warmu
     step_bytes = float(wb[0] + wb[1])
     if world == 1:
         par = "single GPU"
+    elif model.col_batch:
+        par = (f"tensor parallel x{world}: heads, KV cache and FFN blocks split; output and down projections "
+               f"column-split, each partial residual block all-reduced over NVLink peer memory (2 exchanges per "
+               f"layer)")
     elif model.col_split:
         par = (f"tensor parallel x{world}: heads, KV cache and FFN blocks split; output and down projections "
                f"column-split, their partial residual vectors exchanged over NVLink peer memory from inside the "

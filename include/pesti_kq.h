@@ -62,7 +62,7 @@ enum kq_type {
 #define KQ_HOST_PTRS 0   /* x / bias / y are host pointers (synchronous)  */
 #define KQ_DEVICE_PTRS 1 /* x / bias / y are device pointers (async)      */
 #define KQ_SYNC 2        /* synchronise the context stream before return  */
-#define KQ_ACCUMULATE 4  /* kq_tp_allgather_f32: add into y instead of overwrite */
+#define KQ_ACCUMULATE 4  /* kq_tp_allgather_f32 / _allreduce_f32: add into y  */
 #define KQ_ASYNC 8       /* kq_linear_f32 / kq_linear_bf16 with host pointers:  */
                          /* queue the copies and kernels without waiting; the   */
                          /* caller keeps x, bias and y alive (pinned memory     */
@@ -196,6 +196,13 @@ int kq_tp_linear_f32(kq_tp *tp, const kq_weight *shard, int64_t row0, int64_t n_
  * KQ_ACCUMULATE in flags the gathered values are added to y (a residual). */
 int kq_tp_allgather_f32(kq_tp *tp, const float *y_local, int64_t m, int64_t row0, int64_t rows,
                         int64_t n_total, float *y, int64_t y_ld, int flags);
+/* All-reduce of per-rank partials (no reference counterpart: the reference
+ * runs on one device): partial[m][n] is this rank's contribution; y[m][n]
+ * (rows y_ld floats apart) receives the sum over the ranks, taken in rank
+ * order so every rank holds the same bits, or with KQ_ACCUMULATE has it
+ * added.  Needs world x m x n <= the group's max_out_elems.  Device pointers
+ * only; every rank makes the same sequence of calls. */
+int kq_tp_allreduce_f32(kq_tp *tp, const float *partial, int64_t m, int64_t n, float *y, int64_t y_ld, int flags);
 int kq_tp_destroy(kq_tp *tp);
 
 /* ---- GGUF files ----------------------------------------------------------- */

@@ -879,6 +879,44 @@ int kq_tp_allgather_f32(kq_tp* tp, const float* y_local, int64_t m, int64_t row0
   return KQ_OK;
 }
 
+int kq_tp_allreduce_f32(kq_tp* tp, const float* partial, int64_t m, int64_t n, float* y, int64_t y_ld, int flags) {
+  if (!tp) return KQ_ERR_INVALID_ARG;
+  kq_ctx* ctx = tp->ctx;
+  if (!tp->opened) return fail(ctx, KQ_ERR_STATE, "kq_tp_open has not been called");
+  if (!(flags & KQ_DEVICE_PTRS)) return fail(ctx, KQ_ERR_INVALID_ARG, "tensor-parallel calls take device pointers");
+  if (flags & ~(KQ_DEVICE_PTRS | KQ_SYNC | KQ_ACCUMULATE))
+    return fail(ctx, KQ_ERR_INVALID_ARG, "bad flags 0x%x", flags);
+  if (m < 1 || n < 1 || !partial || !y || y_ld < n) return fail(ctx, KQ_ERR_INVALID_ARG, "bad all-reduce shape");
+  if ((int64_t)tp->world * m * n > tp->max_elems)
+    return fail(ctx, KQ_ERR_UNSUPPORTED, "world x m x n = %lld exceeds the exchange buffer (%lld words)",
+                (long long)(tp->world * m * n), (long long)tp->max_elems);
+  DeviceGuard g(ctx->device);
+  kq::TpArgs a{};
+  a.y_local = partial;
+  a.y_out = y;
+  a.y_ld = y_ld;
+  a.accumulate = (flags & KQ_ACCUMULATE) ? 1 : 0;
+  a.m = m;
+  a.n = n;
+  a.r0 = 0;
+  a.r1 = n;
+  a.world = tp->world;
+  a.rank = tp->rank;
+  for (int p = 0; p < tp->world; ++p) a.exch[p] = static_cast<unsigned long long*>(tp->peer_base[p]);
+  a.max_elems = tp->max_elems;
+  a.ctr = tp->ctr;
+  a.epoch = tp->ctr + 1;
+  a.err = ctx->dev_err;
+  // about 4 summed elements per thread, at most one CTA per SM
+  const int64_t work = m * n;
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ctx->num_sms, (work + 2047) / 2048));
+  cudaError_t e = kq::launch_tp_allreduce(a, blocks, ctx->stream);
+  if (e != cudaSuccess) return cuda_fail(ctx, e, "all-reduce launch");
+  ctx->launches += 1;
+  if (flags & KQ_SYNC) return finish_sync(ctx, "all-reduce");
+  return KQ_OK;
+}
+
 int kq_tp_linear_f32(kq_tp* tp, const kq_weight* shard, int64_t row0, int64_t n_total, const float* x, int64_t m,
                      const float* bias, float* y, int flags) {
   if (!tp || !shard) return KQ_ERR_INVALID_ARG;

@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(float* __restrict__ qk
 // ordered by cp.async groups and block barriers.
 constexpr int AT_THREADS = 256;
 constexpr int AT_TILE = 64;  // positions per ring stage
+constexpr int AT_STAGES = 2;  // ring stages: one tile in flight while one is multiplied
 constexpr int ATT_MAX_GROUP = 8;  // query heads per kv head
 constexpr int ATT_MAX_SPLITS = 64;
 
@@ -149,7 +150,7 @@ struct AttnSmem {
   static constexpr int PITCH = HD * 2 + 16;        // bytes per K / V row in shared memory
   static constexpr int TILE_B = AT_TILE * PITCH;   // one K or V tile
   static constexpr int STAGE = 2 * TILE_B;
-  static constexpr int Q = 2 * STAGE;                       // q [G][HD] f32
+  static constexpr int Q = AT_STAGES * STAGE;               // q [G][HD] f32
   static constexpr int SP = AT_TILE + 8;                    // score row pitch (floats): rows 8 banks apart
   static constexpr int S = Q + G * HD * 4;                  // scores / probabilities [G][SP]
   static constexpr int ML = S + G * SP * 4;                 // running max, sum, tile correction, q scale [4][G]
@@ -160,7 +161,7 @@ struct AttnSmem {
   static constexpr int CL = CF + G * ATT_MAX_SPLITS * 4;    // sums [G][ATT_MAX_SPLITS]
   static constexpr int CI = CL + G * ATT_MAX_SPLITS * 4;    // 1 / total sum [G]
   static constexpr int CR = CI + ((G * 4 + 15) / 16) * 16;  // per-warp sums [AT_THREADS / 32][G * HD]
-  static_assert(CR + (AT_THREADS / 32) * G * HD * 4 <= 2 * STAGE, "merge scratch exceeds the ring");
+  static_assert(CR + (AT_THREADS / 32) * G * HD * 4 <= AT_STAGES * STAGE, "merge scratch exceeds the ring");
   static_assert(HD / 16 <= AT_THREADS / 32 && AT_TILE == 8 * (AT_THREADS / 32), "warp roles");
 };
 
@@ -170,7 +171,10 @@ __device__ __forceinline__ void at_cp16(void* dst, const void* src, uint32_t src
                : "memory");
 }
 __device__ __forceinline__ void at_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void at_wait_prev() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+// this thread's copies of the oldest pending tile have landed (the AT_STAGES - 1 newer groups may be in flight)
+__device__ __forceinline__ void at_wait_tile() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(AT_STAGES - 1) : "memory");
+}
 
 // f16 pair {hi(a), hi(b)} and the pair of remainders {a - hi(a), b - hi(b)}, low half = a
 __device__ __forceinline__ void at_split(float a, float b, uint32_t& hi, uint32_t& lo) {
@@ -221,12 +225,12 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
   float* x_s = c_s + G;  // 2^e of each head's q scaling
   __half* new_s = reinterpret_cast<__half*>(sm + L::NEW);
 
-  // tile j into stage j % 2 (every thread issues its share, then one group);
+  // tile j into stage j % AT_STAGES (every thread issues its share, then one group);
   // rows past the split and the appended row are zero-filled (the latter is
   // patched in from new_s)
   auto issue = [&](int j) {
     const int64_t r0 = t0 + (int64_t)j * AT_TILE;
-    uint8_t* st = sm + (j & 1) * L::STAGE;
+    uint8_t* st = sm + (j % AT_STAGES) * L::STAGE;
     for (int e = tid; e < 2 * AT_TILE * CH; e += AT_THREADS) {
       const int kv = e / (AT_TILE * CH), rem = e - kv * (AT_TILE * CH);
       const int r = rem / CH, ch = rem - r * CH;
@@ -237,8 +241,10 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
     }
     at_commit();
   };
-  if (ntiles > 0) issue(0); else at_commit();
-  if (ntiles > 1) issue(1); else at_commit();
+#pragma unroll
+  for (int j = 0; j < AT_STAGES; ++j) {
+    if (j < ntiles) issue(j); else at_commit();  // one group per stage, empty past the split
+  }
 
   for (int e = tid; e < G * HALF; e += AT_THREADS) {
     const int gg = e / HALF, i = e - gg * HALF;
@@ -313,9 +319,9 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
   for (int j = 0; j < ntiles; ++j) {
     const int64_t r0 = t0 + (int64_t)j * AT_TILE;
     const int rows = (int)(t1 - r0 < AT_TILE ? t1 - r0 : AT_TILE);
-    uint8_t* Ks = sm + (j & 1) * L::STAGE;
+    uint8_t* Ks = sm + (j % AT_STAGES) * L::STAGE;
     uint8_t* Vs = Ks + L::TILE_B;
-    at_wait_prev();  // this thread's copies of tile j have landed (tile j + 1 may be in flight)
+    at_wait_tile();  // this thread's copies of tile j have landed (later tiles may be in flight)
     __syncthreads();
     if (has_new && pos >= r0 && pos < r0 + rows) {
       const int r = (int)(pos - r0);
@@ -393,7 +399,7 @@ __global__ void __launch_bounds__(AT_THREADS, 2) attn_decode_kernel(const AttnAr
       }
     }
     __syncthreads();  // the stage and the scores are free again
-    if (j + 2 < ntiles) issue(j + 2); else at_commit();
+    if (j + AT_STAGES < ntiles) issue(j + AT_STAGES); else at_commit();
   }
 
   // this split's partial per query head

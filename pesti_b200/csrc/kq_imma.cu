@@ -538,7 +538,38 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   // all of them at once (one memory round trip per split); summation order as
   // in the scalar form (bias, then the splits in order)
   const int rows = (int)(P.n - row0 < IM_ROWS ? P.n - row0 : IM_ROWS);
-  if (rows == IM_ROWS && (P.n & 3) == 0) {
+  if (rows == IM_ROWS && (P.n & 3) == 0 && P.m * (IM_ROWS / 4) <= 32 * IM_WARPS) {
+    // up to 8 tokens: one 4-row group per thread, eight splits' loads in
+    // flight per round trip (the same summation order as below)
+    const int e = threadIdx.x;
+    if (e < P.m * (IM_ROWS / 4)) {
+      const int r = 4 * (e & (IM_ROWS / 4 - 1));
+      const int64_t off = (int64_t)(e / (IM_ROWS / 4)) * P.n + row0 + r;
+      float4 v = P.bias ? make_float4(P.bias[row0 + r], P.bias[row0 + r + 1], P.bias[row0 + r + 2],
+                                      P.bias[row0 + r + 3])
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+      for (int q = 0; q < P.splits; ++q) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(P.part + (size_t)q * P.m * P.n + off));
+        v.x += t.x;
+        v.y += t.y;
+        v.z += t.z;
+        v.w += t.w;
+      }
+      float* yo = P.y + off;
+      if (P.accumulate) {
+        yo[0] += v.x;
+        yo[1] += v.y;
+        yo[2] += v.z;
+        yo[3] += v.w;
+      } else {
+        yo[0] = v.x;
+        yo[1] = v.y;
+        yo[2] = v.z;
+        yo[3] = v.w;
+      }
+    }
+  } else if (rows == IM_ROWS && (P.n & 3) == 0) {
     constexpr int U = 32 * (IM_ROWS / 4) / (32 * IM_WARPS);
     const int total4 = P.m * (IM_ROWS / 4);
     float4 v[U];
@@ -606,14 +637,15 @@ ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms) {
   const int per_sm = im_ctas_per_sm(nt);
   const int64_t slots = (int64_t)per_sm * num_sms;
   // split-K count: the fewest waves of CTAs x (superblocks per CTA + one for
-  // a CTA's fixed start-up and merge), fewer splits on a tie
+  // a CTA's fixed start-up) plus the merge (one round trip per 8 splits), fewer
+  // splits on a tie
   r.splits = 1;
   r.kb_per = sb;
   int64_t best = INT64_MAX;
   for (int s = 1; s <= sb; ++s) {
     const int per = (sb + s - 1) / s, sp = (sb + per - 1) / per;
     if (sp != s) continue;  // the same split as a smaller count
-    const int64_t cost = (tiles * sp + slots - 1) / slots * (per + 1);
+    const int64_t cost = (tiles * sp + slots - 1) / slots * (per + 1) + (sp + 7) / 8;
     if (cost < best) {
       best = cost;
       r.splits = sp;

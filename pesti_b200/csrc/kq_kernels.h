@@ -318,6 +318,10 @@ struct TpArgs {
 };
 // One launch per call; `blocks` must fit the GPU at once (<= SM count).
 cudaError_t launch_tp_allgather(const TpArgs& a, int blocks, cudaStream_t s);
+// All-reduce: y_local [m][n] is this rank's partial (r0 / r1 unused); y_out
+// receives (or, accumulate, adds) the rank-ordered sum; needs world * m * n
+// <= max_elems.
+cudaError_t launch_tp_allreduce(const TpArgs& a, int blocks, cudaStream_t s);
 
 // ---- decoder step kernels: kq_decoder.cu ----
 cudaError_t dec_rmsnorm(const float* x, int64_t x_ld, const float* w, float* out, int64_t out_ld, int64_t rows,

@@ -11,12 +11,17 @@ runs through ``kq_linear_f32``; the small ops are the kernels of
 
 Tensor parallelism (``world > 1``, one process per GPU): heads are split across
 ranks -- rank r owns query heads and KV heads [r*h/world, (r+1)*h/world), its
-slice of the fused Q|K|V rows, its KV cache, a contiguous block of the output,
-down-projection and head rows and of the gate|up rows.  Four all-gathers per
-layer move activations over NVLink peer memory (``kq_tp_allgather_f32``): the
-attention output, the output projection (added into the residual), the SwiGLU
-output and the down projection (added into the residual); one more gathers the
-logits.
+slice of the fused Q|K|V rows, its KV cache, a contiguous block of the head
+rows and of the gate|up rows.  Up to 16 tokens (heads and FFN blocks on
+superblock edges) the output and down projections are column-split -- rank r
+holds the columns of its heads / FFN block -- and each one's partial residual
+block is summed over the ranks into the residual (at one token inside the
+GEMVs through exchange words, above it by ``kq_tp_allreduce_f32``): two
+exchanges per layer.  Otherwise those projections are row-split and four
+all-gathers per layer move activations over NVLink peer memory
+(``kq_tp_allgather_f32``): the attention output, the output projection (added
+into the residual), the SwiGLU output and the down projection (added into the
+residual).  One more gathers the logits.
 
 Weights are synthetic (no checkpoints): random GGUF superblocks generated on
 the GPU from a seed per tensor, the same bytes on every rank, so a model
@@ -127,10 +132,10 @@ def gguf_weight_device(qtype: int, n: int, k: int, seed: int, device):
 
 
 def exchange_elems(cfg: DecoderConfig, batch: int, world: int = 8) -> int:
-    """Floats one slot of the tensor-parallel exchange buffer needs for this
+    """Words one slot of the tensor-parallel exchange buffer needs for this
     model: the widest all-gathered activation (logits, SwiGLU output, residual
-    stream) or, at batch 1, one partial residual vector per rank."""
-    return max(batch * max(cfg.vocab, cfg.ffn, cfg.dim, cfg.heads * cfg.head_dim), world * cfg.dim)
+    stream) or one partial residual block per rank (the column split)."""
+    return max(batch * max(cfg.vocab, cfg.ffn, cfg.dim, cfg.heads * cfg.head_dim), world * batch * cfg.dim)
 
 
 def column_block(raw, k: int, c0: int, c1: int):
@@ -170,8 +175,13 @@ class Decoder:
         # projections hold W[:, this rank's heads / FFN block] and exchange
         # partial residual vectors (2 exchanges per layer) instead of
         # all-gathering row blocks (4); needs both blocks on superblock edges
-        self.col_split = (world > 1 and self.fused and (cfg.heads // world * cfg.head_dim) % 256 == 0
-                          and cfg.ffn % (256 * world) == 0)
+        aligned = (cfg.heads // world * cfg.head_dim) % 256 == 0 and cfg.ffn % (256 * world) == 0
+        self.col_split = world > 1 and self.fused and aligned
+        # the same column split at 2..16 tokens: each projection's partial
+        # residual block [batch][dim] is all-reduced into the residual
+        # (kq_tp_allreduce_f32), 2 exchanges per layer instead of 4 all-gathers
+        # (above 16 tokens the all-gathers move fewer bytes)
+        self.col_batch = world > 1 and self.fuse_batch and aligned and batch <= 16
         # gate/up as (gate, up) row pairs with the SwiGLU in the GEMV epilogue: the
         # paths that run it (one GPU or the column split at batch 1); otherwise
         # [gate block | up block] for the separate SwiGLU kernel
@@ -226,7 +236,7 @@ class Decoder:
             wo = gguf_weight_device(cfg.linear_type, D, self.Ap, slot(li, "o"), dev)
             keep((li, "o"), wo)
             r0, r1 = self.o_rows
-            if self.col_split:
+            if self.col_split or self.col_batch:
                 a0, a1 = hq0 * hd, (hq0 + self.hq) * hd
                 L["o"] = upload(column_block(wo, self.Ap, a0, a1), cfg.linear_type, D, a1 - a0)
             else:
@@ -244,7 +254,7 @@ class Decoder:
             del wg, wu, gu
             wd = gguf_weight_device(cfg.down_type, D, F, slot(li, "down"), dev)
             keep((li, "down"), wd)
-            if self.col_split:
+            if self.col_split or self.col_batch:
                 L["down"] = upload(column_block(wd, F, f0, f1), cfg.down_type, D, f1 - f0)
             else:
                 L["down"] = upload(wd[r0:r1].contiguous(), cfg.down_type, r1 - r0, F)
@@ -294,6 +304,7 @@ class Decoder:
         self.dn = z(B, r1 - r0)
         self.logits_r = z(B, v1 - v0)
         self.logits = z(B, cfg.vocab)
+        self.part = z(B, D) if self.col_batch else None  # this rank's partial residual block
         self.tokens = torch.zeros(B, dtype=torch.int32, device=dev)
         sbytes = self.lib.kq_dec_attention_scratch(ctx.handle, B, self.hq, self.hkv, hd, self.max_seq)
         self.att_scratch = torch.zeros(max(sbytes // 4, 1), device=dev)  # counters start at zero
@@ -384,11 +395,14 @@ class Decoder:
                 self._check(lib.kq_dec_attention(c, ptr(self.qkv), self.qkv_ld, ptr(L["k"]), ptr(L["v"]), ptr(out),
                                                  out_ld, B, self.hq, self.hkv, hd, pos + 1, self.max_seq,
                                                  ptr(self.att_scratch), self.att_scratch_bytes), "attention")
-            if tp:
+            if tp and not self.col_batch:
                 self._gather(self.attn_r, cfg.heads * hd, self.rank * self.hq * hd, self.hq * hd, self.attn, self.Ap,
                              False)
             self._hint(L["o"])
-            if tp:
+            if self.col_batch:  # W_o[:, this rank's heads] . attn_r, summed over the ranks into h
+                L["o"].linear(self.attn_r, B, self.part, device_ptrs=True)
+                self.tp.allreduce(self.part, B, D, self.h, y_ld=self.Dp, accumulate=True)
+            elif tp:
                 L["o"].linear(self.attn, B, self.o, device_ptrs=True)
                 self._gather(self.o, D, r0, r1 - r0, self.h, self.Dp, True)
             elif self.fused:
@@ -406,9 +420,11 @@ class Decoder:
             self._hint(L["down"])
             self._check(lib.kq_dec_swiglu(c, ptr(self.gu), ptr(self.s_r if tp else self.s), B, f1 - f0,
                                           self.swiglu_mode), "swiglu")
-            if tp:
+            if self.col_batch:  # W_down[:, this rank's FFN block] . s_r, summed over the ranks into h
+                L["down"].linear(self.s_r, B, self.part, device_ptrs=True)
+                self.tp.allreduce(self.part, B, D, self.h, y_ld=self.Dp, accumulate=True)
+            elif tp:
                 self._gather(self.s_r, F, f0, f1 - f0, self.s, F, False)
-            if tp:
                 L["down"].linear(self.s, B, self.dn, device_ptrs=True)
                 self._gather(self.dn, D, r0, r1 - r0, self.h, self.Dp, True)
             elif not self._residual_batch(L["down"], self.s):

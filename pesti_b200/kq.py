@@ -66,6 +66,7 @@ EXPORTED_SYMBOLS = (
     "kq_ctx_profile_end", "kq_ctx_profile_read", "kq_row_bytes", "kq_weight_upload", "kq_weight_free", "kq_weight_info",
     "kq_linear_f32", "kq_linear_bf16", "kq_linear_f32_static", "kq_dequant_f32",
     "kq_tp_create", "kq_tp_handle", "kq_tp_open", "kq_tp_linear_f32", "kq_tp_allgather_f32",
+    "kq_tp_allreduce_f32",
     "kq_tp_destroy", "kq_dec_rmsnorm", "kq_dec_rope_append", "kq_dec_attention_scratch", "kq_dec_attention",
     "kq_dec_swiglu", "kq_dec_add", "kq_dec_embed", "kq_dec_norm_linear", "kq_dec_swiglu_linear",
     "kq_dec_residual_linear", "kq_dec_norm_linear_batch", "kq_dec_residual_linear_batch", "kq_dec_rope_attention",
@@ -134,6 +135,7 @@ def load_library(build_if_missing: bool = True) -> ctypes.CDLL:
             "kq_tp_open": ([P, P, Z], I),
             "kq_tp_linear_f32": ([P, P, I64, I64, P, I64, P, P, I], I),
             "kq_tp_allgather_f32": ([P, P, I64, I64, I64, I64, P, I64, I], I),
+            "kq_tp_allreduce_f32": ([P, P, I64, I64, P, I64, I], I),
             "kq_tp_destroy": ([P], I),
             "kq_gguf_open": ([ctypes.c_char_p, PP, ctypes.c_char_p, Z], I),
             "kq_gguf_close": ([P], None),
@@ -390,6 +392,14 @@ class TensorParallel:
         rc = self.ctx.lib.kq_tp_allgather_f32(self.handle, _ptr(y_local), m, row0, rows, n_total, _ptr(y),
                                               n_total if y_ld is None else y_ld, flags)
         self.ctx.check(rc, "kq_tp_allgather_f32")
+
+    def allreduce(self, partial, m: int, n: int, y, y_ld: Optional[int] = None, accumulate: bool = False,
+                  sync: bool = False):
+        """y (+)= the sum over the ranks of each rank's partial[m][n], in rank order."""
+        flags = KQ_DEVICE_PTRS | (KQ_SYNC if sync else 0) | (KQ_ACCUMULATE if accumulate else 0)
+        rc = self.ctx.lib.kq_tp_allreduce_f32(self.handle, _ptr(partial), m, n, _ptr(y), n if y_ld is None else y_ld,
+                                              flags)
+        self.ctx.check(rc, "kq_tp_allreduce_f32")
 
     def close(self) -> None:
         if getattr(self, "handle", None):

@@ -19,7 +19,8 @@ from pesti_b200 import kq  # noqa: E402
 QWEN_TINY = dec.DecoderConfig("qwen-like-tiny", 2, 448, 7, 1, 64, 512, 300, 1e-6, 1e6, True)
 LLAMA_TINY = dec.DecoderConfig("llama-like-tiny", 2, 512, 4, 2, 128, 768, 300, 1e-5, 5e5, False)
 # FFN 1024: both column blocks fall on superblock edges at 2 ranks, so batch 1
-# takes the column-split exchange of partials (batch 2 the row all-gathers)
+# takes the column-split exchange of partials and batch 2 the column split with
+# all-reduced partials (LLAMA_TINY, whose blocks do not, the row all-gathers)
 LLAMA_TINY_TP = dec.DecoderConfig("llama-like-tiny-tp", 2, 512, 4, 2, 128, 1024, 300, 1e-5, 5e5, False)
 # 16 query / 8 KV heads of 128 and FFN 4096: the column blocks stay on superblock
 # edges up to 8 ranks (2 heads = 256 columns, FFN block 512)
@@ -167,6 +168,8 @@ def _tp_worker(rank, world, port, out_dir, cfg_names=("LLAMA_TINY", "LLAMA_TINY_
                 expect_split = cfg is not LLAMA_TINY and batch == 1
                 if status == "ok" and model.col_split != expect_split:
                     status = f"{cfg.name} batch {batch}: column split {model.col_split}"
+                if status == "ok" and model.col_batch != (cfg is not LLAMA_TINY and batch > 1):
+                    status = f"{cfg.name} batch {batch}: batched column split {model.col_batch}"
                 ks, vs = _oracle_caches(model, cfg)
                 for pos in (20, 21):  # two steps: the exchange slots alternate
                     toks = [4 + pos, 5][:batch]
@@ -180,7 +183,7 @@ def _tp_worker(rank, world, port, out_dir, cfg_names=("LLAMA_TINY", "LLAMA_TINY_
                     # projection in per-rank parts: f32 rounding differs, and the activations'
                     # 15-bit quantization can round a value one step apart, so it is held to the
                     # oracle's tolerance and half of it against one GPU.
-                    tol = TOL / 2 if model.col_split else 1e-5
+                    tol = TOL / 2 if model.col_split or model.col_batch else 1e-5
                     if status == "ok" and (not np.isfinite(a).all() or rel_err(a, b) > tol or rel_err(a, ref) > TOL):
                         status = (f"{cfg.name} batch {batch} step {step} pos {pos}: logits differ: {rel_err(a, b):.2e} "
                                   f"from one GPU, {rel_err(a, ref):.2e} from the oracle")
@@ -207,7 +210,8 @@ def test_tensor_parallel_decode_matches_one_gpu(tmp_path):
 @pytest.mark.skipif(_gpus() < 4, reason="needs 4 GPUs")
 def test_tensor_parallel_decode_on_every_gpu(tmp_path):
     """4 or 8 ranks (all GPUs of the box, up to 8): column-split exchange at
-    batch 1, row all-gathers at batch 2, against one GPU and the oracle."""
+    batch 1, column split with all-reduced partials at batch 2, against one
+    GPU and the oracle."""
     import torch.multiprocessing as mp
     world = 8 if _gpus() >= 8 else 4
     mp.start_processes(_tp_worker, args=(world, _free_port(), str(tmp_path), ("LLAMA_TINY_TP8",)), nprocs=world,

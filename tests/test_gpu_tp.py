@@ -1,5 +1,6 @@
 """Tensor-parallel linear on 2+ GPUs of one node (one process per GPU): row
-shards all-gathered over NVLink peer memory.  Skipped with fewer than 2 GPUs.
+shards all-gathered over NVLink peer memory, and the all-reduce of per-rank
+partials.  Skipped with fewer than 2 GPUs.
 Each rank compares the gathered output with the unsharded product on its own
 GPU (bit-identical for the row-local single-token kernel) and with the oracle."""
 import os
@@ -75,6 +76,25 @@ def _worker(rank, world, port, out_dir, mode):
                         status = f"{n}x{k} m={m} call {call}: error {rel_err(yh, ref):.2e}"
                 shard.free()
                 full.free()
+        elif mode == "allreduce":
+            # every rank's partial summed in rank order: the same f32 additions
+            # as a sequential sum, so bit-identical to numpy's and across ranks
+            m, n, ld = 5, 2800, 2816
+            for call in range(3):  # consecutive calls cycle both exchange slots
+                parts = [np.random.default_rng(100 * call + r).standard_normal((m, n)).astype(np.float32)
+                         for r in range(world)]
+                want = np.zeros((m, n), np.float32)
+                for p in parts:
+                    want = want + p
+                pd = torch.from_numpy(parts[rank]).cuda()
+                y = torch.full((m, ld), 3.0, device="cuda")
+                tp.allreduce(pd, m, n, y, y_ld=ld, sync=True)
+                got = y.cpu().numpy()
+                if not np.array_equal(got[:, :n], want) or not (got[:, n:] == 3.0).all():
+                    status = f"all-reduce call {call}: not the rank-ordered sum"
+                tp.allreduce(pd, m, n, y, y_ld=ld, accumulate=True, sync=True)
+                if not np.array_equal(y.cpu().numpy()[:, :n], want + want):
+                    status = f"accumulating all-reduce call {call}: wrong"
         elif mode == "missing_peer":
             # the last rank never joins the call: every other rank's bounded
             # wait for its flag must give up and report an error
@@ -119,6 +139,16 @@ def test_tp_linear_matches_unsharded_product_2gpu(tmp_path):
 @pytest.mark.skipif(_gpus() < 4, reason="needs 4 GPUs")
 def test_tp_linear_matches_unsharded_product_4gpu(tmp_path):
     _run(4, "linear", tmp_path)
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_tp_allreduce_is_the_rank_ordered_sum_2gpu(tmp_path):
+    _run(2, "allreduce", tmp_path)
+
+
+@pytest.mark.skipif(_gpus() < 4, reason="needs 4 GPUs")
+def test_tp_allreduce_is_the_rank_ordered_sum_4gpu(tmp_path):
+    _run(4, "allreduce", tmp_path)
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
