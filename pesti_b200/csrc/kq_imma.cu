@@ -74,57 +74,58 @@ __device__ __forceinline__ void split4(int v0, int v1, int v2, int v3, uint32_t&
 //   ssum as int2 [(kb * 16 + s) * 32 + t] = {-32 x the sum of the 16 high bytes of group s,
 //                                            -32 x the sum of its 16 low bytes}
 //   (the code offset of sum (q - 32) x, applied to each limb's product)
-// With a norm (nw != nullptr) the quantized activations are RMSNorm(x) =
-// x / sqrt(mean(x[0:dim]^2) + eps) * nw, zero past dim: each warp first
-// reduces its token's sum of squares over the whole row (the row is small and
-// L2-resident, so the redundant reads across a token's superblocks are cheap).
+// Where one (token slot t, superblock) job of the preparation writes: the
+// activation fragments of its 8-token tile, its sums and its 2^e.  The
+// preparation kernel points these into the scratch workspace, the fused
+// kernel into its shared-memory copy of its K range (the same per-superblock
+// layout the ring stages receive).
+struct ImPrepDst {
+  uint4* frag;  // Q4_K / Q5_K: [8 j][32] uint4 of this tile; Q6_K: [16 s][32] uint2 (as uint4*: reinterpreted)
+  int* sum;     // Q4_K / Q5_K: [32 t][8 j] int; Q6_K: [16 s][32 t] int2 (as int*: reinterpreted)
+  float* scale; // [32 t]
+};
+
+// This lane's two runs of four activations of job (t, superblock): Q4_K:
+// sub-block j = lane / 4, elements 32j + 4c.. and 32j + 16 + 4c..; Q6_K: groups
+// j and j + 8, elements 16j + 4c.. and 16(j + 8) + 4c.. (c = lane % 4).
 template <int QT>
-__global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict__ x, int64_t x_ld, int m, int slots,
-                                                        int64_t k, int sb, uint4* __restrict__ bq,
-                                                        int* __restrict__ ssum, float* __restrict__ scl,
-                                                        const float* __restrict__ nw, int dim, float eps) {
-  pdl_trigger();
-  pdl_wait();  // x may be the previous kernel's output
-  const int lane = threadIdx.x & 31;
-  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (wid >= (int64_t)slots * sb) return;
-  const int t = (int)(wid / sb), kb = (int)(wid - (int64_t)t * sb);
+__device__ __forceinline__ void im_prep_offsets(int lane, int& ea, int& eb) {
   const int j = lane >> 2, c = lane & 3;
-  constexpr bool Q4 = QT == GGUF_Q4_K;  // Q5_K calls the Q4_K form (the same 32-weight sub-blocks)
-  // Q4_K: sub-block j, elements 32j + 4c.. and 32j + 16 + 4c..; Q6_K: groups j and j + 8,
-  // elements 16j + 4c.. and 16(j + 8) + 4c..
-  const int64_t ea = Q4 ? 32 * j + 4 * c : 16 * j + 4 * c;
-  const int64_t eb = Q4 ? ea + 16 : ea + 128;
-  uint4* dst4 = bq + ((int64_t)((t >> 3) * sb + kb) * 8 + j) * 32 + 4 * (t & 7) + c;
-  uint2* dst2a = reinterpret_cast<uint2*>(bq) + ((int64_t)((t >> 3) * sb + kb) * 16 + j) * 32 + 4 * (t & 7) + c;
-  uint2* dst2b = dst2a + 8 * 32;
-  if (t >= m) {
-    if constexpr (Q4) {
-      *dst4 = make_uint4(0u, 0u, 0u, 0u);
-    } else {
-      *dst2a = make_uint2(0u, 0u);
-      *dst2b = make_uint2(0u, 0u);
-    }
-    return;
+  constexpr bool Q4 = QT == GGUF_Q4_K;
+  ea = Q4 ? 32 * j + 4 * c : 16 * j + 4 * c;
+  eb = Q4 ? ea + 16 : ea + 128;
+}
+
+// RMSNorm scaling of the two runs (global element offsets ga, gb; dim % 4 ==
+// 0 so each float4 is wholly inside or past dim, where the result is zero).
+__device__ __forceinline__ void im_prep_norm(float4& a, float4& b, int64_t ga, int64_t gb, const float* nw, int dim,
+                                             float rinv) {
+  const float4 wa = ga < dim ? ldg_f4(nw + ga) : make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 wb = gb < dim ? ldg_f4(nw + gb) : make_float4(0.f, 0.f, 0.f, 0.f);
+  a = ga < dim ? make_float4(a.x * rinv * wa.x, a.y * rinv * wa.y, a.z * rinv * wa.z, a.w * rinv * wa.w) : wa;
+  b = gb < dim ? make_float4(b.x * rinv * wb.x, b.y * rinv * wb.y, b.z * rinv * wb.z, b.w * rinv * wb.w) : wb;
+}
+
+// 1 / sqrt(mean(row[0:dim]^2) + eps), reduced over the warp.
+__device__ __forceinline__ float im_row_rinv(const float* row, int dim, float eps, int lane) {
+  float ss = 0.f;
+#pragma unroll 4
+  for (int i = 4 * lane; i < dim; i += 128) {
+    const float4 v = ldg_f4(row + i);
+    ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
   }
-  const float* xs = x + (int64_t)t * x_ld + (int64_t)kb * 256;
-  float4 a = ldg_f4(xs + ea), b = ldg_f4(xs + eb);
-  if (nw) {
-    const float* xr = x + (int64_t)t * x_ld;
-    float ss = 0.f;
-    for (int i = 4 * lane; i < dim; i += 128) {
-      const float4 v = ldg_f4(xr + i);
-      ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rinv = 1.f / sqrtf(ss / (float)dim + eps);
-    const int64_t ga = (int64_t)kb * 256 + ea, gb = (int64_t)kb * 256 + eb;  // dim % 4 == 0: whole float4s
-    const float4 wa = ga < dim ? ldg_f4(nw + ga) : make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4 wb = gb < dim ? ldg_f4(nw + gb) : make_float4(0.f, 0.f, 0.f, 0.f);
-    a = ga < dim ? make_float4(a.x * rinv * wa.x, a.y * rinv * wa.y, a.z * rinv * wa.z, a.w * rinv * wa.w) : wa;
-    b = gb < dim ? make_float4(b.x * rinv * wb.x, b.y * rinv * wb.y, b.z * rinv * wb.z, b.w * rinv * wb.w) : wb;
-  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  return 1.f / sqrtf(ss / (float)dim + eps);
+}
+
+// Quantize one job's activations (this lane's runs a, b; the whole warp
+// takes part) and write its fragments (token slot position tt = t % 8 in the
+// tile), sums (slot t) and scale.
+template <int QT>
+__device__ __forceinline__ void im_prep_store(float4 a, float4 b, int lane, int t, const ImPrepDst& d) {
+  constexpr bool Q4 = QT == GGUF_Q4_K;
+  const int j = lane >> 2, c = lane & 3, tt = t & 7;
   float amax = fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w)));
   amax = fmaxf(amax, fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
 #pragma unroll
@@ -145,14 +146,15 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
   split4(v0, v1, v2, v3, o.x, o.z);
   split4(v4, v5, v6, v7, o.y, o.w);
   if constexpr (Q4) {
-    *dst4 = o;
+    d.frag[j * 32 + 4 * tt + c] = o;
     int s = v0 + v1 + v2 + v3 + v4 + v5 + v6 + v7;
     s += __shfl_xor_sync(0xffffffffu, s, 1);
     s += __shfl_xor_sync(0xffffffffu, s, 2);
-    if (c == 0) ssum[((int64_t)kb * 32 + t) * 8 + j] = s;
+    if (c == 0) d.sum[t * 8 + j] = s;
   } else {
-    *dst2a = make_uint2(o.x, o.z);
-    *dst2b = make_uint2(o.y, o.w);
+    uint2* f2 = reinterpret_cast<uint2*>(d.frag);
+    f2[j * 32 + 4 * tt + c] = make_uint2(o.x, o.z);
+    f2[(j + 8) * 32 + 4 * tt + c] = make_uint2(o.y, o.w);
     // limb sums of groups j (v0..v3) and j + 8 (v4..v7): high bytes v >> 8, low bytes v & 255
     int ha = (v0 >> 8) + (v1 >> 8) + (v2 >> 8) + (v3 >> 8), la = (v0 & 255) + (v1 & 255) + (v2 & 255) + (v3 & 255);
     int hb = (v4 >> 8) + (v5 >> 8) + (v6 >> 8) + (v7 >> 8), lb = (v4 & 255) + (v5 & 255) + (v6 & 255) + (v7 & 255);
@@ -164,12 +166,76 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
       lb += __shfl_xor_sync(0xffffffffu, lb, o2);
     }
     if (c == 0) {  // times the code offset 32, negated: the MMAs' start values
-      int2* s2 = reinterpret_cast<int2*>(ssum);
-      s2[((int64_t)kb * 16 + j) * 32 + t] = make_int2(-32 * ha, -32 * la);
-      s2[((int64_t)kb * 16 + j + 8) * 32 + t] = make_int2(-32 * hb, -32 * lb);
+      int2* s2 = reinterpret_cast<int2*>(d.sum);
+      s2[j * 32 + t] = make_int2(-32 * ha, -32 * la);
+      s2[(j + 8) * 32 + t] = make_int2(-32 * hb, -32 * lb);
     }
   }
-  if (lane == 0) scl[(int64_t)kb * 32 + t] = factor;
+  if (lane == 0) d.scale[t] = factor;
+}
+
+// Zero fragments for a token slot past m (the rest of the last 8-token tile);
+// its sums and scale are written as zero too.
+template <int QT>
+__device__ __forceinline__ void im_prep_zero(int lane, int t, const ImPrepDst& d) {
+  const int j = lane >> 2, c = lane & 3, tt = t & 7;
+  if constexpr (QT == GGUF_Q4_K) {
+    d.frag[j * 32 + 4 * tt + c] = make_uint4(0u, 0u, 0u, 0u);
+    if (c == 0) d.sum[t * 8 + j] = 0;
+  } else {
+    uint2* f2 = reinterpret_cast<uint2*>(d.frag);
+    f2[j * 32 + 4 * tt + c] = make_uint2(0u, 0u);
+    f2[(j + 8) * 32 + 4 * tt + c] = make_uint2(0u, 0u);
+    if (c == 0) {
+      int2* s2 = reinterpret_cast<int2*>(d.sum);
+      s2[j * 32 + t] = make_int2(0, 0);
+      s2[(j + 8) * 32 + t] = make_int2(0, 0);
+    }
+  }
+  if (lane == 0) d.scale[t] = 0.f;
+}
+
+// Workspace layout per superblock kb: fragments [tile][kb] 4096 bytes each,
+// sums [kb] (Q4_K 1024 / Q6_K 4096 bytes), scales [kb] 128 bytes.
+template <int QT>
+__device__ __forceinline__ ImPrepDst im_ws_dst(uint4* bq, int* ssum, float* scl, int sb, int kb, int t) {
+  ImPrepDst d;
+  d.frag = bq + (size_t)((t >> 3) * sb + kb) * 256;
+  d.sum = ssum + (size_t)kb * (QT == GGUF_Q4_K ? 256 : 1024);
+  d.scale = scl + (size_t)kb * 32;
+  return d;
+}
+
+// With a norm (nw != nullptr) the quantized activations are RMSNorm(x) =
+// x / sqrt(mean(x[0:dim]^2) + eps) * nw, zero past dim: each warp first
+// reduces its token's sum of squares over the whole row (the row is small and
+// L2-resident, so the redundant reads across a token's superblocks are cheap).
+// Q5_K uses the Q4_K form (the same 32-weight sub-blocks).
+template <int QT>
+__global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict__ x, int64_t x_ld, int m, int slots,
+                                                        int64_t k, int sb, uint4* __restrict__ bq,
+                                                        int* __restrict__ ssum, float* __restrict__ scl,
+                                                        const float* __restrict__ nw, int dim, float eps) {
+  pdl_trigger();
+  pdl_wait();  // x may be the previous kernel's output
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (wid >= (int64_t)slots * sb) return;
+  const int t = (int)(wid / sb), kb = (int)(wid - (int64_t)t * sb);
+  const ImPrepDst d = im_ws_dst<QT>(bq, ssum, scl, sb, kb, t);
+  if (t >= m) {
+    im_prep_zero<QT>(lane, t, d);
+    return;
+  }
+  int ea, eb;
+  im_prep_offsets<QT>(lane, ea, eb);
+  const float* xs = x + (int64_t)t * x_ld + (int64_t)kb * 256;
+  float4 a = ldg_f4(xs + ea), b = ldg_f4(xs + eb);
+  if (nw) {
+    const float rinv = im_row_rinv(x + (int64_t)t * x_ld, dim, eps, lane);
+    im_prep_norm(a, b, (int64_t)kb * 256 + ea, (int64_t)kb * 256 + eb, nw, dim, rinv);
+  }
+  im_prep_store<QT>(a, b, lane, t, d);
 }
 
 // Device bytes of one superblock in the weight's tensor map box.
@@ -208,6 +274,15 @@ struct ImParams {
   int sb, m, splits, kb_per, S;
   int accumulate;  // y += the product instead of y = (the residual update)
   int* err;
+  // shared-memory plan: ring stages stage_bytes apart, the fused form's
+  // prepared K range at xp_off (xp_stride bytes per superblock), barriers at bar_off
+  int stage_bytes, xp_off, xp_stride, bar_off;
+  // fused form: the activations (rows x_ld floats apart), optional RMSNorm
+  const float* x;
+  int64_t x_ld;
+  const float* nw;
+  int dim;
+  float eps;
 };
 
 // Hand a ring stage back to the producer.  The warp's shared-memory reads of
@@ -249,7 +324,12 @@ __device__ __forceinline__ void mma16_u8u8(int (&c)[4], uint32_t a0, uint32_t a1
                : "r"(a0), "r"(a1), "r"(b0));
 }
 
-template <int QT, int NT>
+// FUSED: the CTA prepares the activation fragments, sums and scales of its
+// own K range itself (its MMA warps, into shared memory, while the producer's
+// first weight copies are in flight) instead of a preparation kernel writing
+// them to the workspace for the producer to copy per stage; chosen where that
+// range fits beside the ring.
+template <int QT, int NT, bool FUSED>
 __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
     imma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap dmap, const ImParams P) {
   using St = ImStage<QT, NT>;
@@ -259,7 +339,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   constexpr int QS = Q5 ? 48 : 16;  // offset of the qs bytes in the superblock
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_trigger();
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)P.S * St::BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + P.bar_off);
   uint64_t* empty = full + P.S;
   __shared__ int last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -283,14 +363,16 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       if constexpr (!Q4) sm100::tma_prefetch(&dmap);
       auto weights = [&](int t) {
         const int st = t % P.S, kb = kb0 + t;
-        uint8_t* dst = smem + (size_t)st * St::BYTES;
-        mbar_expect_only(&full[st], St::W + St::D);
+        uint8_t* dst = smem + (size_t)st * P.stage_bytes;
+        // fused: the weights are the whole stage, so this is the stage's arrival
+        if constexpr (FUSED) sm100::mbar_expect_tx(&full[st], St::W + St::D);
+        else mbar_expect_only(&full[st], St::W + St::D);
         sm100::tma_load_2d(dst, &wmap, kb * BPS, (int)row0, &full[st]);
         if constexpr (!Q4) sm100::tma_load_2d(dst + St::W, &dmap, kb & ~7, (int)row0, &full[st]);
       };
       const int pre = min(T, P.S);
       for (int t = 0; t < pre; ++t) weights(t);
-      pdl_wait();  // activation fragments and sums come from the prep kernel
+      if constexpr (!FUSED) pdl_wait();  // activation fragments and sums come from the prep kernel
       int t = 0;
       for (; t < T; ++t) {
         const int st = t % P.S, kb = kb0 + t;
@@ -298,7 +380,8 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
           if (!sm100::mbar_wait(&empty[st], ((t / P.S) - 1) & 1, P.err, IM_ERR_EMPTY)) break;
           weights(t);
         }
-        uint8_t* dst = smem + (size_t)st * St::BYTES + St::W + St::D;
+        if constexpr (FUSED) continue;
+        uint8_t* dst = smem + (size_t)st * P.stage_bytes + St::W + St::D;
         sm100::mbar_expect_tx(&full[st], St::B + St::S + St::F);  // the stage's arrival
 #pragma unroll
         for (int i = 0; i < NT; ++i)
@@ -313,7 +396,57 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   }
 
   // ---- MMA warps: warp w owns tile rows 16w + g (C rows 0-7) and 16w + g + 8
-  pdl_wait();  // the per-(superblock, token) scales come from the prep kernel
+  pdl_wait();  // x, or the per-(superblock, token) fragments and scales the prep kernel wrote
+  if constexpr (FUSED) {
+    // this CTA's K range [kb0, kb0 + T) for every token slot: job (t, i) =
+    // slot t, local superblock i, one warp each, JB jobs' loads in flight per warp
+    constexpr int PQT = QT == GGUF_Q6_K ? GGUF_Q6_K : GGUF_Q4_K;  // Q5_K: the Q4_K preparation
+    constexpr int JB = 4;
+    __shared__ float rinv_s[32];
+    if (P.nw) {
+      for (int t = warp; t < P.m; t += IM_WARPS) {
+        const float r = im_row_rinv(P.x + (int64_t)t * P.x_ld, P.dim, P.eps, lane);
+        if (lane == 0) rinv_s[t] = r;
+      }
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
+    }
+    int ea, eb;
+    im_prep_offsets<PQT>(lane, ea, eb);
+    const int jobs = NT * 8 * T;
+    for (int j0 = warp; j0 < jobs; j0 += IM_WARPS * JB) {
+      float4 a[JB], b[JB];
+#pragma unroll
+      for (int u = 0; u < JB; ++u) {
+        const int job = j0 + u * IM_WARPS, t = job / max(T, 1), i = job - t * max(T, 1);
+        a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (job < jobs && t < P.m) {
+          const float* xs = P.x + (int64_t)t * P.x_ld + (int64_t)(kb0 + i) * 256;
+          a[u] = ldg_f4(xs + ea);
+          b[u] = ldg_f4(xs + eb);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < JB; ++u) {
+        const int job = j0 + u * IM_WARPS, t = job / max(T, 1), i = job - t * max(T, 1);
+        if (job >= jobs) continue;  // uniform across the warp
+        uint8_t* blk = smem + P.xp_off + (size_t)i * P.xp_stride;
+        ImPrepDst d;
+        d.frag = reinterpret_cast<uint4*>(blk) + (t >> 3) * 256;
+        d.sum = reinterpret_cast<int*>(blk + St::B);
+        d.scale = reinterpret_cast<float*>(blk + St::B + St::S);
+        if (t >= P.m) {
+          im_prep_zero<PQT>(lane, t, d);
+        } else {
+          if (P.nw) {
+            const int64_t base = (int64_t)(kb0 + i) * 256;
+            im_prep_norm(a[u], b[u], base + ea, base + eb, P.nw, P.dim, rinv_s[t]);
+          }
+          im_prep_store<PQT>(a[u], b[u], lane, t, d);
+        }
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
+  }
   const int g = lane >> 2, c = lane & 3;
   const int ra = 16 * warp + g, rb = ra + 8;
   float tot[NT][4];
@@ -323,7 +456,9 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   for (int t = 0; t < T; ++t) {
     const int st = t % P.S, kb = kb0 + t;
     if (!sm100::mbar_wait_warp(&full[st], (t / P.S) & 1, P.err, IM_ERR_FULL)) break;
-    const uint8_t* stage = smem + (size_t)st * St::BYTES;
+    const uint8_t* stage = smem + (size_t)st * P.stage_bytes;
+    // fragments | sums | scales of this superblock: the stage's copies, or the fused preparation's
+    const uint8_t* bsf = FUSED ? smem + P.xp_off + (size_t)t * P.xp_stride : stage + St::W + St::D;
     if constexpr (Q4) {
       const uint8_t* pa = stage + ra * BPS;
       const uint8_t* pb = stage + rb * BPS;
@@ -335,8 +470,8 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       const uint32_t scb_lo = hb.y & 0x3F3F3F3Fu, mb_lo = hb.z & 0x3F3F3F3Fu;
       const uint32_t scb_hi = (hb.w & 0x0F0F0F0Fu) | ((hb.y >> 2) & 0x30303030u);
       const uint32_t mb_hi = ((hb.w >> 4) & 0x0F0F0F0Fu) | ((hb.z >> 2) & 0x30303030u);
-      const uint4* bs = reinterpret_cast<const uint4*>(stage + St::W);
-      const int* ss = reinterpret_cast<const int*>(stage + St::W + St::B);
+      const uint4* bs = reinterpret_cast<const uint4*>(bsf);
+      const int* ss = reinterpret_cast<const int*>(bsf + St::B);
       // sum over sub-blocks of scale x limb product, exact in int32: a
       // sub-block's high-limb sum is < 2^16 in size, its low-limb one < 2^18
       // (codes up to 31), so 8 six-bit scales keep them below 2^25 / 2^27
@@ -403,7 +538,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
           }
         }
       }
-      const float* fsc = reinterpret_cast<const float*>(stage + St::W + St::B + St::S);
+      const float* fsc = reinterpret_cast<const float*>(bsf + St::B + St::S);
       float f[NT][2];
 #pragma unroll
       for (int i = 0; i < NT; ++i)
@@ -427,9 +562,9 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       const uint8_t* pb = stage + rb * Q6K_BODY;
       const uint16_t* dtile = reinterpret_cast<const uint16_t*>(stage + St::W);
       const uint4 sca4 = *reinterpret_cast<const uint4*>(pa + 192), scb4 = *reinterpret_cast<const uint4*>(pb + 192);
-      const uint2* bs = reinterpret_cast<const uint2*>(stage + St::W + St::D);
+      const uint2* bs = reinterpret_cast<const uint2*>(bsf);
       // {-32 sum hi, -32 sum lo} of tokens 8i + 2c and 8i + 2c + 1 for group sg: int4 [sg][4i + c]
-      const int4* ss4 = reinterpret_cast<const int4*>(stage + St::W + St::D + St::B);
+      const int4* ss4 = reinterpret_cast<const int4*>(bsf + St::B);
       // sum over groups of scale x limb product, exact in int32: a group's
       // high-limb sum (q - 32) hi is < 2^15 in size, its low-limb one < 2^17,
       // so 16 groups of int8 scales stay below 2^26 / 2^28
@@ -482,7 +617,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
         }
       // the superblock scales leave the stage before it is released
       const float da = f16_bits_to_f32(dtile[ra * 8 + (kb & 7)]), db = f16_bits_to_f32(dtile[rb * 8 + (kb & 7)]);
-      const float* fsc = reinterpret_cast<const float*>(stage + St::W + St::D + St::B + St::S);
+      const float* fsc = reinterpret_cast<const float*>(bsf + St::B + St::S);
       float f[NT][2];
 #pragma unroll
       for (int i = 0; i < NT; ++i)
@@ -629,9 +764,11 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
 // Ring stages and K-splits: about one CTA per SM, at least 2 superblocks per CTA.
 struct ImShape {
   int S, splits, kb_per;
+  int stage_bytes, xp_off, xp_stride, bar_off;
+  bool ok = true;  // fused: the CTA's prepared K range fits beside a ring of at least two stages
   size_t smem;
 };
-ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms) {
+ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms, bool fused = false) {
   ImShape r;
   const int64_t tiles = (n + IM_ROWS - 1) / IM_ROWS;
   const int per_sm = im_ctas_per_sm(nt);
@@ -653,10 +790,29 @@ ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms) {
     }
     if (tiles * sp >= 2 * slots) break;
   }
-  const int stage = im_stage_bytes(qt, nt);
-  const int fit = ((per_sm == 2 ? IM_HALF_SMEM : IM_MAX_SMEM) - 2 * 8 * 8) / (stage + 16);
-  r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
-  r.smem = (size_t)r.S * stage + (size_t)2 * r.S * 8;
+  const int budget = (per_sm == 2 ? IM_HALF_SMEM : IM_MAX_SMEM) - 2 * 8 * 8;
+  if (!fused) {
+    const int stage = im_stage_bytes(qt, nt);
+    const int fit = budget / (stage + 16);
+    r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
+    r.stage_bytes = stage;
+    r.xp_off = r.xp_stride = 0;
+    r.bar_off = r.S * stage;
+  } else {
+    // ring stages hold the weights (and Q6_K's d box) only; the prepared
+    // fragments | sums | scales of the CTA's kb_per superblocks sit after them
+    const int stage = im_stage_w(qt) + im_stage_d(qt);
+    r.xp_stride = nt * 4096 + im_stage_s(qt) + 32 * 4;
+    const int xp = r.kb_per * r.xp_stride;
+    const int fit = xp < budget ? (budget - xp) / (stage + 16) : 0;
+    // and the preparation stays short: at most 8 jobs (token slot x superblock) per MMA warp
+    r.ok = fit >= 2 && nt * r.kb_per <= 8;
+    r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
+    r.stage_bytes = stage;
+    r.xp_off = r.S * stage;
+    r.bar_off = r.xp_off + xp;
+  }
+  r.smem = (size_t)r.bar_off + (size_t)2 * r.S * 8;
   return r;
 }
 
@@ -685,10 +841,10 @@ ImWs im_ws(int64_t m, int64_t n, int64_t k, int num_sms) {
   return L;
 }
 
-template <int QT, int NT>
+template <int QT, int NT, bool FUSED>
 cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const float* bias, float* y, unsigned* ctr,
-                      int num_sms, int* err, cudaStream_t s, bool accumulate) {
-  const ImShape sh = im_shape(QT, NT, w.n, (int)w.sb, num_sms);
+                      int num_sms, int* err, cudaStream_t s, const float* x, const ImOpts& op) {
+  const ImShape sh = im_shape(QT, NT, w.n, (int)w.sb, num_sms, FUSED);
   char* base = static_cast<char*>(ws);
   ImParams P;
   P.bq = reinterpret_cast<const uint4*>(base + L.bq);
@@ -704,8 +860,17 @@ cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const 
   P.splits = sh.splits;
   P.kb_per = sh.kb_per;
   P.S = sh.S;
-  P.accumulate = accumulate ? 1 : 0;
+  P.accumulate = op.accumulate ? 1 : 0;
   P.err = err;
+  P.stage_bytes = sh.stage_bytes;
+  P.xp_off = sh.xp_off;
+  P.xp_stride = sh.xp_stride;
+  P.bar_off = sh.bar_off;
+  P.x = x;
+  P.x_ld = op.x_ld ? op.x_ld : w.k;
+  P.nw = op.nw;
+  P.dim = op.dim;
+  P.eps = op.eps;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((w.n + IM_ROWS - 1) / IM_ROWS), (unsigned)sh.splits);
   cfg.blockDim = dim3(32 * (IM_WARPS + 1));
@@ -716,22 +881,58 @@ cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, imma_kernel<QT, NT>, w.wmap, w.dmap, P);
+  return cudaLaunchKernelEx(&cfg, imma_kernel<QT, NT, FUSED>, w.wmap, w.dmap, P);
+}
+
+// One chunk of up to 32 tokens: the fused kernel where its shared-memory plan
+// fits, else the preparation kernel and the plain one.
+template <int QT, int NT>
+cudaError_t launch_chunk(const DevWeight& w, int m, const ImWs& L, void* ws, const float* bias, float* y,
+                         unsigned* ctr, int num_sms, int* err, cudaStream_t s, const float* x, const ImOpts& op,
+                         int* launches, Bracket br) {
+  if (im_shape(QT, NT, w.n, (int)w.sb, num_sms, true).ok) {
+    bracket_record(br.start, s);
+    const cudaError_t e = launch_im<QT, NT, true>(w, m, L, ws, bias, y, ctr, num_sms, err, s, x, op);
+    if (e == cudaSuccess && launches) ++*launches;
+    bracket_record(br.stop, s);
+    return e;
+  }
+  constexpr int PQT = QT == GGUF_Q6_K ? GGUF_Q6_K : GGUF_Q4_K;  // Q5_K: the Q4_K preparation
+  const int sb = (int)w.sb, nt = NT;
+  const int64_t warps = (int64_t)nt * 8 * sb;
+  const int64_t x_ld = op.x_ld ? op.x_ld : w.k;
+  char* base = static_cast<char*>(ws);
+  cudaError_t e = launch_pdl(imma_prep_kernel<PQT>, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, s, x, x_ld, m,
+                             nt * 8, w.k, sb, reinterpret_cast<uint4*>(base + L.bq),
+                             reinterpret_cast<int*>(base + L.ssum), reinterpret_cast<float*>(base + L.scl), op.nw,
+                             op.dim, op.eps);
+  if (e != cudaSuccess) return e;
+  if (launches) ++*launches;
+  bracket_record(br.start, s);
+  e = launch_im<QT, NT, false>(w, m, L, ws, bias, y, ctr, num_sms, err, s, x, op);
+  if (e == cudaSuccess && launches) ++*launches;
+  bracket_record(br.stop, s);
+  return e;
 }
 
 }  // namespace
 
+template <typename K>
+static cudaError_t im_attr(K kernel) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM);
+}
+
 template <int QT>
 static cudaError_t im_attrs() {
   cudaError_t e = cudaSuccess, r;
-  if ((r = cudaFuncSetAttribute(imma_kernel<QT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
-    e = r;
-  if ((r = cudaFuncSetAttribute(imma_kernel<QT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
-    e = r;
-  if ((r = cudaFuncSetAttribute(imma_kernel<QT, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
-    e = r;
-  if ((r = cudaFuncSetAttribute(imma_kernel<QT, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, IM_MAX_SMEM)))
-    e = r;
+  if ((r = im_attr(imma_kernel<QT, 1, false>))) e = r;
+  if ((r = im_attr(imma_kernel<QT, 2, false>))) e = r;
+  if ((r = im_attr(imma_kernel<QT, 3, false>))) e = r;
+  if ((r = im_attr(imma_kernel<QT, 4, false>))) e = r;
+  if ((r = im_attr(imma_kernel<QT, 1, true>))) e = r;
+  if ((r = im_attr(imma_kernel<QT, 2, true>))) e = r;
+  if ((r = im_attr(imma_kernel<QT, 3, true>))) e = r;
+  if ((r = im_attr(imma_kernel<QT, 4, true>))) e = r;
   return e;
 }
 
@@ -750,53 +951,30 @@ cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, co
                              const ImOpts& op) {
   if (w.type != GGUF_Q4_K && w.type != GGUF_Q5_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
   const int64_t x_ld = op.x_ld ? op.x_ld : w.k;
-  const bool q4 = w.type != GGUF_Q6_K;  // Q4_K and Q5_K share the activation preparation
   const ImWs L = im_ws(m64, w.n, w.k, num_sms);
-  const int sb = (int)w.sb;
   for (int64_t m0 = 0; m0 < m64; m0 += 32) {
     const int m = (int)((m64 - m0) < 32 ? (m64 - m0) : 32);
     const int nt = (m + 7) / 8;
-    char* base = static_cast<char*>(ws);
-    const int64_t warps = (int64_t)nt * 8 * sb;
-    const dim3 pg((unsigned)((warps + 7) / 8));
-    uint4* bq = reinterpret_cast<uint4*>(base + L.bq);
-    int* ssum = reinterpret_cast<int*>(base + L.ssum);
-    float* scl = reinterpret_cast<float*>(base + L.scl);
     const float* xc = x + m0 * x_ld;
-    cudaError_t e = q4 ? launch_pdl(imma_prep_kernel<GGUF_Q4_K>, pg, dim3(256), 0, s, xc, x_ld, m, nt * 8, w.k, sb,
-                                    bq, ssum, scl, op.nw, op.dim, op.eps)
-                       : launch_pdl(imma_prep_kernel<GGUF_Q6_K>, pg, dim3(256), 0, s, xc, x_ld, m, nt * 8, w.k, sb,
-                                    bq, ssum, scl, op.nw, op.dim, op.eps);
-    if (e != cudaSuccess) return e;
-    if (launches) ++*launches;
-    bracket_record(br.start, s);
     float* yc = y + m0 * w.n;
+    cudaError_t e;
+#define KQ_IM_CHUNK(QT)                                                                                          \
+  switch (nt) {                                                                                                  \
+    case 1: e = launch_chunk<QT, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, xc, op, launches, br); break;  \
+    case 2: e = launch_chunk<QT, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, xc, op, launches, br); break;  \
+    case 3: e = launch_chunk<QT, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, xc, op, launches, br); break;  \
+    default: e = launch_chunk<QT, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, xc, op, launches, br); break; \
+  }
     if (w.type == GGUF_Q4_K) {
-      switch (nt) {
-        case 1: e = launch_im<GGUF_Q4_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        case 2: e = launch_im<GGUF_Q4_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        case 3: e = launch_im<GGUF_Q4_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        default: e = launch_im<GGUF_Q4_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-      }
+      KQ_IM_CHUNK(GGUF_Q4_K)
     } else if (w.type == GGUF_Q5_K) {
-      switch (nt) {
-        case 1: e = launch_im<GGUF_Q5_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        case 2: e = launch_im<GGUF_Q5_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        case 3: e = launch_im<GGUF_Q5_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        default: e = launch_im<GGUF_Q5_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-      }
+      KQ_IM_CHUNK(GGUF_Q5_K)
     } else {
-      switch (nt) {
-        case 1: e = launch_im<GGUF_Q6_K, 1>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        case 2: e = launch_im<GGUF_Q6_K, 2>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        case 3: e = launch_im<GGUF_Q6_K, 3>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-        default: e = launch_im<GGUF_Q6_K, 4>(w, m, L, ws, bias, yc, ctr, num_sms, err, s, op.accumulate); break;
-      }
+      KQ_IM_CHUNK(GGUF_Q6_K)
     }
-    bracket_record(br.stop, s);
+#undef KQ_IM_CHUNK
     br = Bracket();  // only the first chunk is bracketed
     if (e != cudaSuccess) return e;
-    if (launches) ++*launches;
   }
   return cudaSuccess;
 }
