@@ -805,8 +805,10 @@ ImShape im_shape(int qt, int nt, int64_t n, int sb, int num_sms, bool fused = fa
     r.xp_stride = nt * 4096 + im_stage_s(qt) + 32 * 4;
     const int xp = r.kb_per * r.xp_stride;
     const int fit = xp < budget ? (budget - xp) / (stage + 16) : 0;
-    // and the preparation stays short: at most 8 jobs (token slot x superblock) per MMA warp
-    r.ok = fit >= 2 && nt * r.kb_per <= 8;
+    // and the preparation stays short: one token tile (a 32-token chunk's RMSNorm pass
+    // alone reads 32 rows per CTA; measured slower at 8 GPUs, batch 32), at most 8 jobs
+    // (token slot x superblock) per MMA warp
+    r.ok = fit >= 2 && nt == 1 && r.kb_per <= 8;
     r.S = std::max(2, std::min(std::min(fit, 6), r.kb_per));
     r.stage_bytes = stage;
     r.xp_off = r.S * stage;
