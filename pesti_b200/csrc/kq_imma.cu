@@ -51,6 +51,11 @@ constexpr int IM_MAX_SMEM = 226 * 1024;   // dynamic; room for the static bytes
 constexpr int IM_HALF_SMEM = 112 * 1024;  // two CTAs per SM
 // CTAs per SM: one or two token tiles leave registers and shared memory for two
 constexpr int im_ctas_per_sm(int nt) { return nt <= 2 ? 2 : 1; }
+// MMA warps per CTA and token tiles per MMA warp: up to two tiles, 8 warps
+// (one per 16-row group); three or four, 16 warps (two per 16-row group, two
+// tiles each), so one CTA per SM still has 16 warps issuing
+constexpr int im_mma_warps(int nt) { return nt > 2 ? 16 : 8; }
+constexpr int im_tiles_per_warp(int nt) { return nt > 2 ? 2 : nt; }
 constexpr int IM_ERR_FULL = 27, IM_ERR_EMPTY = 28;
 
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -330,9 +335,12 @@ __device__ __forceinline__ void mma16_u8u8(int (&c)[4], uint32_t a0, uint32_t a1
 // them to the workspace for the producer to copy per stage; chosen where that
 // range fits beside the ring.
 template <int QT, int NT, bool FUSED>
-__global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
+__global__ void __launch_bounds__(32 * (im_mma_warps(NT) + 1), im_ctas_per_sm(NT))
     imma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap dmap, const ImParams P) {
   using St = ImStage<QT, NT>;
+  // MMA warps: 16 for three or four token tiles (warps w and w + 8 share a
+  // 16-row group and take two tiles each), 8 otherwise
+  constexpr int MW = im_mma_warps(NT), NTW = im_tiles_per_warp(NT);
   constexpr bool Q4 = QT != GGUF_Q6_K;  // Q4_K and Q5_K
   constexpr bool Q5 = QT == GGUF_Q5_K;
   constexpr int BPS = im_block_bytes(QT);
@@ -350,13 +358,13 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   if (threadIdx.x == 0) {
     for (int i = 0; i < P.S; ++i) {
       sm100::mbar_init(&full[i], 1);
-      sm100::mbar_init(&empty[i], IM_WARPS);
+      sm100::mbar_init(&empty[i], MW);
     }
     sm100::mbar_fence_init();
   }
   __syncthreads();
 
-  if (warp == IM_WARPS) {
+  if (warp == MW) {
     // ---- producer: the weights first (they do not depend on the previous kernel)
     if (lane == 0) {
       sm100::tma_prefetch(&wmap);
@@ -404,20 +412,20 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
     constexpr int JB = 4;
     __shared__ float rinv_s[32];
     if (P.nw) {
-      for (int t = warp; t < P.m; t += IM_WARPS) {
+      for (int t = warp; t < P.m; t += MW) {
         const float r = im_row_rinv(P.x + (int64_t)t * P.x_ld, P.dim, P.eps, lane);
         if (lane == 0) rinv_s[t] = r;
       }
-      asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * MW) : "memory");
     }
     int ea, eb;
     im_prep_offsets<PQT>(lane, ea, eb);
     const int jobs = NT * 8 * T;
-    for (int j0 = warp; j0 < jobs; j0 += IM_WARPS * JB) {
+    for (int j0 = warp; j0 < jobs; j0 += MW * JB) {
       float4 a[JB], b[JB];
 #pragma unroll
       for (int u = 0; u < JB; ++u) {
-        const int job = j0 + u * IM_WARPS, t = job / max(T, 1), i = job - t * max(T, 1);
+        const int job = j0 + u * MW, t = job / max(T, 1), i = job - t * max(T, 1);
         a[u] = b[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (job < jobs && t < P.m) {
           const float* xs = P.x + (int64_t)t * P.x_ld + (int64_t)(kb0 + i) * 256;
@@ -427,7 +435,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       }
 #pragma unroll
       for (int u = 0; u < JB; ++u) {
-        const int job = j0 + u * IM_WARPS, t = job / max(T, 1), i = job - t * max(T, 1);
+        const int job = j0 + u * MW, t = job / max(T, 1), i = job - t * max(T, 1);
         if (job >= jobs) continue;  // uniform across the warp
         uint8_t* blk = smem + P.xp_off + (size_t)i * P.xp_stride;
         ImPrepDst d;
@@ -445,13 +453,14 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
         }
       }
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"r"(32 * MW) : "memory");
   }
   const int g = lane >> 2, c = lane & 3;
-  const int ra = 16 * warp + g, rb = ra + 8;
-  float tot[NT][4];
+  const int i0 = (warp / 8) * NTW;  // this warp's first token tile
+  const int ra = 16 * (warp % 8) + g, rb = ra + 8;
+  float tot[NTW][4];
 #pragma unroll
-  for (int i = 0; i < NT; ++i) tot[i][0] = tot[i][1] = tot[i][2] = tot[i][3] = 0.f;
+  for (int i = 0; i < NTW; ++i) tot[i][0] = tot[i][1] = tot[i][2] = tot[i][3] = 0.f;
 
   for (int t = 0; t < T; ++t) {
     const int st = t % P.S, kb = kb0 + t;
@@ -475,9 +484,9 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       // sum over sub-blocks of scale x limb product, exact in int32: a
       // sub-block's high-limb sum is < 2^16 in size, its low-limb one < 2^18
       // (codes up to 31), so 8 six-bit scales keep them below 2^25 / 2^27
-      int aH[NT][4], aL[NT][4], ma[NT][4];
+      int aH[NTW][4], aL[NTW][4], ma[NTW][4];
 #pragma unroll
-      for (int i = 0; i < NT; ++i)
+      for (int i = 0; i < NTW; ++i)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           aH[i][e] = aL[i][e] = 0;
@@ -516,8 +525,10 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
           const int mina = (int)(((j < 4 ? ma_lo : ma_hi) >> sh) & 0xffu);
           const int minb = (int)(((j < 4 ? mb_lo : mb_hi) >> sh) & 0xffu);
 #pragma unroll
-          for (int i = 0; i < NT; ++i) {
-            const uint4 bv = bs[(i * 8 + j) * 32 + lane];
+          for (int i = 0; i < NTW; ++i) {
+            const int ti = i0 + i;  // token tile
+            if (ti >= NT) break;    // uniform across the warp
+            const uint4 bv = bs[(ti * 8 + j) * 32 + lane];
             int ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
             mma_u8s8(ch, a0, a1, a2, a3, bv.x, bv.y);
             mma_u8u8(cl, a0, a1, a2, a3, bv.z, bv.w);
@@ -530,7 +541,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
             aL[i][1] += sca * cl[1];
             aL[i][2] += scb * cl[2];
             aL[i][3] += scb * cl[3];
-            const int s0 = ss[(8 * i + 2 * c) * 8 + j], s1 = ss[(8 * i + 2 * c + 1) * 8 + j];
+            const int s0 = ss[(8 * ti + 2 * c) * 8 + j], s1 = ss[(8 * ti + 2 * c + 1) * 8 + j];
             ma[i][0] += mina * s0;
             ma[i][1] += mina * s1;
             ma[i][2] += minb * s0;
@@ -539,16 +550,19 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
         }
       }
       const float* fsc = reinterpret_cast<const float*>(bsf + St::B + St::S);
-      float f[NT][2];
+      float f[NTW][2];
 #pragma unroll
-      for (int i = 0; i < NT; ++i)
+      for (int i = 0; i < NTW; ++i)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) f[i][e] = 8 * i + 2 * c + e < P.m ? fsc[8 * i + 2 * c + e] : 0.f;
+        for (int e = 0; e < 2; ++e) {
+          const int tk = 8 * (i0 + i) + 2 * c + e;
+          f[i][e] = tk < P.m ? fsc[tk] : 0.f;
+        }
       stage_release(&empty[st], lane);
       const float da = f16_bits_to_f32((uint16_t)(ha.x & 0xffff)), dma = f16_bits_to_f32((uint16_t)(ha.x >> 16));
       const float db = f16_bits_to_f32((uint16_t)(hb.x & 0xffff)), dmb = f16_bits_to_f32((uint16_t)(hb.x >> 16));
 #pragma unroll
-      for (int i = 0; i < NT; ++i) {
+      for (int i = 0; i < NTW; ++i) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float va = fmaf(256.f, (float)aH[i][e], (float)aL[i][e]);
@@ -568,9 +582,9 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       // sum over groups of scale x limb product, exact in int32: a group's
       // high-limb sum (q - 32) hi is < 2^15 in size, its low-limb one < 2^17,
       // so 16 groups of int8 scales stay below 2^26 / 2^28
-      int aH[NT][4], aL[NT][4];
+      int aH[NTW][4], aL[NTW][4];
 #pragma unroll
-      for (int i = 0; i < NT; ++i)
+      for (int i = 0; i < NTW; ++i)
 #pragma unroll
         for (int e = 0; e < 4; ++e) aH[i][e] = aL[i][e] = 0;
 #pragma unroll
@@ -596,10 +610,12 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
               const int sca = (int)(int8_t)(wsa >> (8 * (sg & 3)));
               const int scb = (int)(int8_t)(wsb >> (8 * (sg & 3)));
 #pragma unroll
-              for (int i = 0; i < NT; ++i) {
-                const uint2 bv = bs[(i * 16 + sg) * 32 + lane];
+              for (int i = 0; i < NTW; ++i) {
+                const int ti = i0 + i;  // token tile
+                if (ti >= NT) break;    // uniform across the warp
+                const uint2 bv = bs[(ti * 16 + sg) * 32 + lane];
                 // sum (q - 32) x per limb: each product starts from -32 x its limb sum
-                const int4 sv = ss4[sg * 16 + 4 * i + c];
+                const int4 sv = ss4[sg * 16 + 4 * ti + c];
                 int ch[4] = {sv.x, sv.z, sv.x, sv.z}, cl[4] = {sv.y, sv.w, sv.y, sv.w};
                 mma16_u8s8(ch, a0, a1, bv.x);
                 mma16_u8u8(cl, a0, a1, bv.y);
@@ -618,14 +634,17 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       // the superblock scales leave the stage before it is released
       const float da = f16_bits_to_f32(dtile[ra * 8 + (kb & 7)]), db = f16_bits_to_f32(dtile[rb * 8 + (kb & 7)]);
       const float* fsc = reinterpret_cast<const float*>(bsf + St::B + St::S);
-      float f[NT][2];
+      float f[NTW][2];
 #pragma unroll
-      for (int i = 0; i < NT; ++i)
+      for (int i = 0; i < NTW; ++i)
 #pragma unroll
-        for (int e = 0; e < 2; ++e) f[i][e] = 8 * i + 2 * c + e < P.m ? fsc[8 * i + 2 * c + e] : 0.f;
+        for (int e = 0; e < 2; ++e) {
+          const int tk = 8 * (i0 + i) + 2 * c + e;
+          f[i][e] = tk < P.m ? fsc[tk] : 0.f;
+        }
       stage_release(&empty[st], lane);
 #pragma unroll
-      for (int i = 0; i < NT; ++i) {
+      for (int i = 0; i < NTW; ++i) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float va = fmaf(256.f, (float)aH[i][e], (float)aL[i][e]);
@@ -642,10 +661,10 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   float* dst = P.splits == 1 ? P.y : P.part + (size_t)sp * P.m * P.n;
   const bool add_bias = P.splits == 1 && P.bias;
 #pragma unroll
-  for (int i = 0; i < NT; ++i)
+  for (int i = 0; i < NTW; ++i)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      const int tk = 8 * i + 2 * c + e;
+      const int tk = 8 * (i0 + i) + 2 * c + e;
       if (tk < P.m) {
         // one writer per output; the residual form adds to what y holds (only the last write, splits == 1)
         if (rowa < P.n) {
@@ -663,9 +682,9 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   if (P.splits == 1) return;
   // split-K: the last CTA of this row tile adds the splits in order
   __threadfence();
-  asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"r"(32 * MW) : "memory");
   if (threadIdx.x == 0) last = atomicAdd(P.ctr + blockIdx.x, 1u) == (unsigned)P.splits - 1;
-  asm volatile("bar.sync 1, %0;" ::"r"(32 * IM_WARPS) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"r"(32 * MW) : "memory");
   if (!last) return;
   __threadfence();
   // a full tile (128 rows, n a multiple of 4): each thread owns up to four
@@ -673,7 +692,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
   // all of them at once (one memory round trip per split); summation order as
   // in the scalar form (bias, then the splits in order)
   const int rows = (int)(P.n - row0 < IM_ROWS ? P.n - row0 : IM_ROWS);
-  if (rows == IM_ROWS && (P.n & 3) == 0 && P.m * (IM_ROWS / 4) <= 32 * IM_WARPS) {
+  if (rows == IM_ROWS && (P.n & 3) == 0 && P.m * (IM_ROWS / 4) <= 32 * MW) {
     // up to 8 tokens: one 4-row group per thread, eight splits' loads in
     // flight per round trip (the same summation order as below)
     const int e = threadIdx.x;
@@ -705,12 +724,12 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       }
     }
   } else if (rows == IM_ROWS && (P.n & 3) == 0) {
-    constexpr int U = 32 * (IM_ROWS / 4) / (32 * IM_WARPS);
+    constexpr int U = 32 * (IM_ROWS / 4) / (32 * MW);
     const int total4 = P.m * (IM_ROWS / 4);
     float4 v[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int e = threadIdx.x + u * 32 * IM_WARPS, r = 4 * (e & (IM_ROWS / 4 - 1));
+      const int e = threadIdx.x + u * 32 * MW, r = 4 * (e & (IM_ROWS / 4 - 1));
       v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       if (e < total4 && P.bias)
         v[u] = make_float4(P.bias[row0 + r], P.bias[row0 + r + 1], P.bias[row0 + r + 2], P.bias[row0 + r + 3]);
@@ -720,7 +739,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       const float* pq = P.part + (size_t)q * P.m * P.n + row0;
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const int e = threadIdx.x + u * 32 * IM_WARPS;
+        const int e = threadIdx.x + u * 32 * MW;
         if (e < total4) {
           const float4 t = __ldcg(reinterpret_cast<const float4*>(pq + (int64_t)(e / (IM_ROWS / 4)) * P.n +
                                                                   4 * (e & (IM_ROWS / 4 - 1))));
@@ -733,7 +752,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int e = threadIdx.x + u * 32 * IM_WARPS;
+      const int e = threadIdx.x + u * 32 * MW;
       if (e < total4) {
         float* yo = P.y + (int64_t)(e / (IM_ROWS / 4)) * P.n + row0 + 4 * (e & (IM_ROWS / 4 - 1));
         if (P.accumulate) {
@@ -750,7 +769,7 @@ __global__ void __launch_bounds__(32 * (IM_WARPS + 1), im_ctas_per_sm(NT))
       }
     }
   } else {
-    for (int e = threadIdx.x; e < P.m * rows; e += 32 * IM_WARPS) {
+    for (int e = threadIdx.x; e < P.m * rows; e += 32 * MW) {
       const int tk = e / rows, r = e - tk * rows;
       const int64_t idx = (int64_t)tk * P.n + row0 + r;
       float v = P.bias ? P.bias[row0 + r] : 0.f;
@@ -875,7 +894,7 @@ cudaError_t launch_im(const DevWeight& w, int m, const ImWs& L, void* ws, const 
   P.eps = op.eps;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((w.n + IM_ROWS - 1) / IM_ROWS), (unsigned)sh.splits);
-  cfg.blockDim = dim3(32 * (IM_WARPS + 1));
+  cfg.blockDim = dim3(32 * (im_mma_warps(NT) + 1));
   cfg.dynamicSmemBytes = sh.smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
