@@ -707,7 +707,20 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
                                ctx->next_bracket());
     }
   } else {
-    e = kq::launch_gemv_legacy(w->dw, static_cast<const float*>(xd), m, bd, yd, s, &launches, ctx->next_bracket());
+    // the reference's blocks: one token over whole 256-weight spans (Q4_K / Q6_K
+    // tiles) on the single-token kernel under AUTO / DP4A, otherwise the block kernel
+    const kq::Bracket br = ctx->next_bracket();
+    e = cudaErrorNotSupported;
+    if (m == 1 && (ctx->path == KQ_PATH_AUTO || ctx->path == KQ_PATH_DP4A) && k % kq::QK == 0 &&
+        (w->dw.type == kq::LEGACY_Q4_K || w->dw.type == kq::LEGACY_Q6_K)) {
+      kq::DevWeight lw = w->dw;
+      lw.sb = k / kq::QK;
+      kq::XsInput in;
+      in.x = static_cast<const float*>(xd);
+      e = kq::launch_gemv_xs(lw, in, bd, yd, ctx->num_sms, ctx->dev_err, pf, s, &launches, br);
+    }
+    if (e == cudaErrorNotSupported)
+      e = kq::launch_gemv_legacy(w->dw, static_cast<const float*>(xd), m, bd, yd, s, &launches, br);
   }
   ctx->launches += launches;
   if (e != cudaSuccess) return cuda_fail(ctx, e, "kernel launch");

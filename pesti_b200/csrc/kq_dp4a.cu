@@ -543,19 +543,27 @@ constexpr int64_t XS_PF_CHUNK = 64 * 1024;  // bytes per L2 prefetch instruction
 // are a separate array), and a row's stride: its superblocks rounded up to a
 // whole number of 16-byte units (the same stride the upload gives each type).
 __host__ __device__ constexpr int xs_stride(int qt) {
-  return qt == GGUF_Q4_K   ? Q4K_BYTES
-         : qt == GGUF_Q6_K ? Q6K_BODY
-         : qt == GGUF_Q5_K ? Q5K_BYTES
-         : qt == GGUF_Q3_K ? Q3K_DEV
-                           : Q2K_BYTES;
+  return qt == GGUF_Q4_K     ? Q4K_BYTES
+         : qt == GGUF_Q6_K   ? Q6K_BODY
+         : qt == GGUF_Q5_K   ? Q5K_BYTES
+         : qt == GGUF_Q3_K   ? Q3K_DEV
+         : qt == LEGACY_Q4_K ? 16 * 28  // the reference's blocks: 16 per 256 weights
+         : qt == LEGACY_Q6_K ? 16 * 42
+                             : Q2K_BYTES;
 }
+// The reference's own 16-weight blocks (rows of k % 256 == 0 weights, so a
+// row is whole 256-weight spans of 448 / 672 bytes).
+__host__ __device__ constexpr bool xs_legacy(int qt) { return qt == LEGACY_Q4_K || qt == LEGACY_Q6_K; }
 __host__ __device__ constexpr int64_t xs_row_bytes(int qt, int64_t sb) { return (sb * xs_stride(qt) + 15) & ~int64_t(15); }
 // Types whose sub-blocks hold 16 weights (Q2_K, Q3_K) instead of 32 (Q4_K, Q5_K).
 __host__ __device__ constexpr bool xs_g16(int qt) { return qt == GGUF_Q2_K || qt == GGUF_Q3_K; }
 // Activation sums kept per 64-weight unit: Q4_K / Q5_K float2 (the unit's two
 // 32-weight sub-blocks), Q2_K / Q3_K float4 (four 16-weight sub-blocks),
 // Q6_K int4[4] (the -32 corrections of its 8-weight groups).
-__host__ __device__ constexpr int xs_sum_bytes(int qt) { return qt == GGUF_Q6_K ? 64 : xs_g16(qt) ? 16 : 8; }
+// Legacy Q4_K: eight floats per unit (the sums of each block half); legacy Q6_K none (16 kept for alignment).
+__host__ __device__ constexpr int xs_sum_bytes(int qt) {
+  return qt == GGUF_Q6_K ? 64 : qt == LEGACY_Q4_K ? 32 : (xs_g16(qt) || qt == LEGACY_Q6_K) ? 16 : 8;
+}
 
 struct XsParams {
   const uint8_t* q;     // [n][row_bytes]
@@ -708,7 +716,8 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       int off;
-      if constexpr (QT != GGUF_Q6_K) off = 64 * u + 16 * hf + (i < 4 ? 4 * i : 32 + 4 * (i - 4));
+      if constexpr (xs_legacy(QT)) off = 64 * u + 32 * hf + 4 * i;  // contiguous: blocks 4u + 2hf, +1
+      else if constexpr (QT != GGUF_Q6_K) off = 64 * u + 16 * hf + (i < 4 ? 4 * i : 32 + 4 * (i - 4));
       else off = 128 * hf + 32 * (i >> 1) + 8 * u + 4 * (i & 1);
       float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
       if constexpr (XM == XS_X_PLAIN) {
@@ -754,7 +763,29 @@ __device__ __forceinline__ void xs_stage_x(const XsParams& P, const XsSmem& L, u
     const XScale sc = xs_scale(amax);
     uint4* unit = xw + (size_t)(kb * 4 + u) * 8;
     const int sw = xs_swz(kb, u);
-    if constexpr (QT != GGUF_Q6_K) {
+    if constexpr (xs_legacy(QT)) {
+      // word 4 hf + j covers elements 8j .. 8j + 7 of this half-unit (block 4u + 2hf + j/2,
+      // its half j % 2).  Legacy Q6_K: {hi, lo} of the scale group 8j..8j+3, then of 8j+4..;
+      // legacy Q4_K: {hi, lo} of the even elements 8j, +2, +4, +6, then of the odd ones
+      // (the low and high nibbles of the block's code bytes), and the half's exact sum.
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 o;
+        const float* q = v + 8 * j;
+        if constexpr (QT == LEGACY_Q6_K) {
+          xs_pack4(q[0], q[1], q[2], q[3], sc.inv, o.x, o.y);
+          xs_pack4(q[4], q[5], q[6], q[7], sc.inv, o.z, o.w);
+        } else {
+          xs_pack4(q[0], q[2], q[4], q[6], sc.inv, o.x, o.y);
+          xs_pack4(q[1], q[3], q[5], q[7], sc.inv, o.z, o.w);
+          float hs = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) hs += q[e];
+          reinterpret_cast<float*>(smem + L.sums)[(size_t)(kb * 4 + u) * 8 + 4 * hf + j] = hs;
+        }
+        unit[(4 * hf + j) ^ sw] = o;
+      }
+    } else if constexpr (QT != GGUF_Q6_K) {
       // word 4 hf + j: {hi, lo} of A elements 4j.., then of B elements 4j..
       // (A: unit elements 0-31, B: 32-63; this half-unit holds 16 hf .. 16 hf + 15 of each)
       float sa = 0.f, sbb = 0.f;
@@ -906,12 +937,20 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
   float4 s16 = make_float4(0.f, 0.f, 0.f, 0.f);  // Q2_K / Q3_K: exact sums of sub-blocks 4u .. 4u+3
   int Sh[2][4], Sl[2][4];      // Q6_K: -32 * (sum of hi / lo bytes) of group (h, g)
   uint32_t sel_lo = 0, sel_hi = 0;  // Q6_K: PRMT selectors of this lane's scale bytes
+  float lsum[8];               // legacy Q4_K: exact sums of the unit's eight block halves
   if constexpr (QT == GGUF_Q4_K || QT == GGUF_Q5_K) {
     const float2 t = reinterpret_cast<const float2*>(xs_smem + L.sums)[kb * 4 + u];
     sa = t.x;
     sbb = t.y;
   } else if constexpr (xs_g16(QT)) {
     s16 = reinterpret_cast<const float4*>(xs_smem + L.sums)[kb * 4 + u];
+  } else if constexpr (xs_legacy(QT)) {
+    if constexpr (QT == LEGACY_Q4_K) {
+      const float4* t = reinterpret_cast<const float4*>(xs_smem + L.sums) + (size_t)(kb * 4 + u) * 2;
+      const float4 a = t[0], b = t[1];
+      lsum[0] = a.x; lsum[1] = a.y; lsum[2] = a.z; lsum[3] = a.w;
+      lsum[4] = b.x; lsum[5] = b.y; lsum[6] = b.z; lsum[7] = b.w;
+    }
   } else {
     const int4* si = reinterpret_cast<const int4*>(xs_smem + L.sums) + (size_t)(kb * 4 + u) * 4;
 #pragma unroll
@@ -1049,6 +1088,64 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
           fs = fmaf((float)sc, S[i], fs);
         }
         v = f16_bits_to_f32((uint16_t)(sd.w & 0xffff)) * fmaf(xf, (float)iv, -4.f * fs);
+      } else if constexpr (QT == LEGACY_Q4_K) {
+        // four 28-byte blocks (pesti-runner/src/tile_dequant.rs:238-290): d | delta,
+        // the code nibbles of elements 0-7 and 8-15, h0 | h1; value = delta * h * (q - 4) + d.
+        // Per block half: sum q x from the even / odd nibbles (exact int32), then
+        // delta * h * (x-scale * that - 4 * sum x) + d * sum x
+        const uint8_t* unitp = rowp + kb * (16 * 28) + u * 112;
+#pragma unroll
+        for (int bl = 0; bl < 4; ++bl) {
+          const uint32_t* bw = reinterpret_cast<const uint32_t*>(unitp + 28 * bl);  // 4-byte aligned
+          const uint32_t w0 = bw[0], hh = bw[3];
+          const float d = f16_bits_to_f32((uint16_t)(w0 & 0xffff)), delta = f16_bits_to_f32((uint16_t)(w0 >> 16));
+#pragma unroll
+          for (int hb = 0; hb < 2; ++hb) {
+            const uint32_t word = bw[1 + hb];
+            const uint32_t ev = word & 0x0F0F0F0Fu, od = (word >> 4) & 0x0F0F0F0Fu;
+            const uint4 xw = X[2 * bl + hb];
+            const int hi = dp4a_us(od, xw.z, dp4a_us(ev, xw.x, 0));
+            const int lo = dp4a_u(od, xw.w, dp4a_u(ev, xw.y, 0));
+            const float hs = lsum[2 * bl + hb];
+            const float t = delta * f16_bits_to_f32((uint16_t)(hb ? hh >> 16 : hh & 0xffff));
+            v = fmaf(t, fmaf(xf, (float)(hi * 256 + lo), -4.f * hs), fmaf(d, hs, v));  // |hi*256+lo| < 2^21
+          }
+        }
+      } else if constexpr (QT == LEGACY_Q6_K) {
+        // four 42-byte blocks (tile_dequant.rs:347-374, 2-byte aligned): d, four f16 group
+        // scales, 2-bit low codes (bytes 10-13), 2-bit flags (bytes 18-21); q = low + 4 *
+        // (flag ? flag - 1 : 0) and value = d * (q - 32) * scale of its group of four.
+        // Byte-parallel: word C_j holds position j of the four groups; a 4x4 byte
+        // transpose gives each group's four codes, OR 0xE0 makes q - 32 a signed byte
+        const uint16_t* unitp = reinterpret_cast<const uint16_t*>(rowp + kb * (16 * 42) + u * 168);
+#pragma unroll
+        for (int bl = 0; bl < 4; ++bl) {
+          const uint16_t* h = unitp + 21 * bl;
+          const float d = f16_bits_to_f32(h[0]);
+          const uint32_t ql = (uint32_t)h[5] | ((uint32_t)h[6] << 16);
+          const uint32_t fl = (uint32_t)h[9] | ((uint32_t)h[10] << 16);
+          uint32_t C[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t lq = (ql >> (2 * j)) & 0x03030303u, f = (fl >> (2 * j)) & 0x03030303u;
+            const uint32_t qh = f - ((f | (f >> 1)) & 0x01010101u);  // per byte: flag ? flag - 1 : 0
+            C[j] = lq + (qh << 2);                                     // per byte <= 11: no carries
+          }
+          const uint32_t T0 = prmt(C[0], C[1], 0x5140u), T1 = prmt(C[0], C[1], 0x7362u);
+          const uint32_t T2 = prmt(C[2], C[3], 0x5140u), T3 = prmt(C[2], C[3], 0x7362u);
+          const uint32_t G[4] = {prmt(T0, T2, 0x5410u), prmt(T0, T2, 0x7632u), prmt(T1, T3, 0x5410u),
+                                 prmt(T1, T3, 0x7632u)};
+          float acc = 0.f;
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const uint32_t sq = G[g] | 0xE0E0E0E0u;  // q - 32 as signed bytes
+            const uint4 xw = X[2 * bl + (g >> 1)];
+            const uint32_t xh = (g & 1) ? xw.z : xw.x, xl = (g & 1) ? xw.w : xw.y;
+            const int D = dp4a_s(sq, xh, 0) * 256 + dp4a_su(sq, xl, 0);  // |.| < 2^21
+            acc = fmaf(f16_bits_to_f32(h[1 + g]), (float)D, acc);
+          }
+          v = fmaf(d * xf, acc, v);
+        }
       } else if constexpr (QT == GGUF_Q2_K) {
         // scales[16] | qs[64] | d | dmin at an 84-byte stride: 4-byte aligned,
         // so 32-bit loads.  Codes at bits sh2 (A) / sh2 + 2 (B) of qs bytes
@@ -1213,23 +1310,29 @@ XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms, int64_t xr_floats 
   r.nw_floats = nw_floats;
   const int nk = (int)((sb + XS_SPW - 1) / XS_SPW);
   if (n < 1 || nk < 1 || nk > XS_MAX_COMPUTE) return r;
-  r.G = XS_MAX_COMPUTE / nk;
-  r.threads = 32 * (nk * r.G + 1);
-  r.grid = (int)std::min<int64_t>(n, num_sms);
-  r.rows_max = (int)((n + r.grid - 1) / r.grid);
-  const int64_t row_bytes = xs_row_bytes(qt, sb);
-  const int64_t d_row_bytes = qt == GGUF_Q6_K ? q6k_d_ld(sb) * 2 : 0;
-  r.stage_bytes = 2 * r.G * (row_bytes + d_row_bytes);  // 2G rows per stage
-  const int T = (r.rows_max + 2 * r.G - 1) / (2 * r.G);
-  const size_t fixed = XsSmem(qt, nk, r.stage_bytes, 0, r.rows_max, xr_floats, nw_floats).end + 64;
-  if (fixed >= (size_t)XS_MAX_SMEM) return r;
-  const int64_t fit = (int64_t)((XS_MAX_SMEM - fixed) / (size_t)(r.stage_bytes + 16));
-  const int64_t want = std::max<int64_t>(2, (XS_INFLIGHT + r.stage_bytes / 2) / r.stage_bytes);
-  const int S = (int)std::min<int64_t>(std::min<int64_t>(T, fit), want);
-  if (S < std::min(T, 2)) return r;
-  r.S = S;
-  r.smem = XsSmem(qt, nk, r.stage_bytes, S, r.rows_max, xr_floats, nw_floats).end;
-  r.ok = r.smem <= (size_t)XS_MAX_SMEM;
+  // the most row groups whose two-row-per-group stages still give a ring of
+  // two (only rows of tens of KB, the reference's blocks, need fewer groups)
+  for (int G = XS_MAX_COMPUTE / nk; G >= 1; --G) {
+    r.G = G;
+    r.threads = 32 * (nk * r.G + 1);
+    r.grid = (int)std::min<int64_t>(n, num_sms);
+    r.rows_max = (int)((n + r.grid - 1) / r.grid);
+    const int64_t row_bytes = xs_row_bytes(qt, sb);
+    const int64_t d_row_bytes = qt == GGUF_Q6_K ? q6k_d_ld(sb) * 2 : 0;
+    r.stage_bytes = 2 * r.G * (row_bytes + d_row_bytes);  // 2G rows per stage
+    const int T = (r.rows_max + 2 * r.G - 1) / (2 * r.G);
+    const size_t fixed = XsSmem(qt, nk, r.stage_bytes, 0, r.rows_max, xr_floats, nw_floats).end + 64;
+    if (fixed >= (size_t)XS_MAX_SMEM) continue;
+    const int64_t fit = (int64_t)((XS_MAX_SMEM - fixed) / (size_t)(r.stage_bytes + 16));
+    const int64_t want = std::max<int64_t>(2, (XS_INFLIGHT + r.stage_bytes / 2) / r.stage_bytes);
+    const int S = (int)std::min<int64_t>(std::min<int64_t>(T, fit), want);
+    if (S < std::min(T, 2)) continue;
+    r.S = S;
+    r.smem = XsSmem(qt, nk, r.stage_bytes, S, r.rows_max, xr_floats, nw_floats).end;
+    r.ok = r.smem <= (size_t)XS_MAX_SMEM;
+    if (r.ok) return r;
+  }
+  r.ok = false;
   return r;
 }
 
@@ -1274,10 +1377,10 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if constexpr (QT != GGUF_Q4_K && QT != GGUF_Q6_K) {  // Q2_K / Q3_K / Q5_K: plain linears only
+  if constexpr (QT != GGUF_Q4_K && QT != GGUF_Q6_K) {  // the other types: plain linears only
     if (in.mode != XS_X_PLAIN || in.ymode != XS_Y_LOCAL) return cudaErrorNotSupported;
     return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_LOCAL>, P);
-  }
+  } else {
   if (in.ymode == XS_Y_SWIGLU) {
     switch (in.mode) {
       case XS_X_PLAIN: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_PLAIN, XS_Y_SWIGLU>, P);
@@ -1301,6 +1404,7 @@ cudaError_t launch_xs(const DevWeight& w, const XsInput& in, const float* bias, 
     case XS_X_REDUCE_NORM: return cudaLaunchKernelEx(&cfg, xs_gemv_kernel<QT, XS_X_REDUCE_NORM, XS_Y_LOCAL>, P);
   }
   return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
@@ -1367,18 +1471,22 @@ cudaError_t dp4a_init_device() {
   if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<GGUF_Q2_K, XS_X_PLAIN, XS_Y_LOCAL>);
   if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<GGUF_Q3_K, XS_X_PLAIN, XS_Y_LOCAL>);
   if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<GGUF_Q5_K, XS_X_PLAIN, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<LEGACY_Q4_K, XS_X_PLAIN, XS_Y_LOCAL>);
+  if (e == cudaSuccess) e = xs_attr(xs_gemv_kernel<LEGACY_Q6_K, XS_X_PLAIN, XS_Y_LOCAL>);
   return e;
 }
 
 cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* bias, float* y, int num_sms, int* err,
                            const Prefetch* pf, cudaStream_t s, int* launches, Bracket br) {
   if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K && w.type != GGUF_Q2_K && w.type != GGUF_Q3_K &&
-      w.type != GGUF_Q5_K)
+      w.type != GGUF_Q5_K && !xs_legacy(w.type))
     return cudaErrorNotSupported;
   if (in.mode < XS_X_PLAIN || in.mode > XS_X_REDUCE_NORM) return cudaErrorInvalidValue;
-  // Q2_K / Q3_K / Q5_K: plain linears, rows laid out at the stride the kernel streams
+  // Q2_K / Q3_K / Q5_K and the legacy blocks: plain linears, rows laid out at
+  // the stride the kernel streams (legacy: whole 256-weight spans, sb = k / 256)
   if (w.type != GGUF_Q4_K && w.type != GGUF_Q6_K) {
     if (in.mode != XS_X_PLAIN || in.ymode != XS_Y_LOCAL) return cudaErrorNotSupported;
+    if (xs_legacy(w.type) && (w.sb < 1 || w.sb * 256 != w.k)) return cudaErrorNotSupported;
     if (w.row_bytes != xs_row_bytes(w.type, w.sb)) return cudaErrorInvalidValue;
   }
   const bool reduce = in.mode == XS_X_REDUCE || in.mode == XS_X_REDUCE_NORM;
@@ -1394,6 +1502,8 @@ cudaError_t launch_gemv_xs(const DevWeight& w, const XsInput& in, const float* b
     case GGUF_Q6_K: e = launch_xs<GGUF_Q6_K>(w, in, bias, y, err, pf, s, sh); break;
     case GGUF_Q5_K: e = launch_xs<GGUF_Q5_K>(w, in, bias, y, err, pf, s, sh); break;
     case GGUF_Q3_K: e = launch_xs<GGUF_Q3_K>(w, in, bias, y, err, pf, s, sh); break;
+    case LEGACY_Q4_K: e = launch_xs<LEGACY_Q4_K>(w, in, bias, y, err, pf, s, sh); break;
+    case LEGACY_Q6_K: e = launch_xs<LEGACY_Q6_K>(w, in, bias, y, err, pf, s, sh); break;
     default: e = launch_xs<GGUF_Q2_K>(w, in, bias, y, err, pf, s, sh); break;
   }
   if (e != cudaSuccess) return e;
