@@ -535,6 +535,7 @@ constexpr int XS_SPW = 8;          // superblocks per warp slice
 constexpr int XS_MAX_COMPUTE = 15;  // compute warps (+ 1 producer = 512 threads)
 constexpr int XS_MAX_SMEM = 227 * 1024;
 constexpr int64_t XS_INFLIGHT = 144 * 1024;  // ring bytes in flight per CTA
+constexpr int64_t XS_STAGE_MAX = 64 * 1024;  // bytes of one ring stage (unless one row group exceeds it)
 
 enum : int { XS_ERR_FULL = 21, XS_ERR_EMPTY = 22, XS_ERR_DRAIN = 23, XS_ERR_TP = 32 };
 constexpr int64_t XS_PF_CHUNK = 64 * 1024;  // bytes per L2 prefetch instruction
@@ -1310,9 +1311,11 @@ XsLaunch xs_shape(int qt, int64_t n, int64_t sb, int num_sms, int64_t xr_floats 
   r.nw_floats = nw_floats;
   const int nk = (int)((sb + XS_SPW - 1) / XS_SPW);
   if (n < 1 || nk < 1 || nk > XS_MAX_COMPUTE) return r;
-  // the most row groups whose two-row-per-group stages still give a ring of
-  // two (only rows of tens of KB, the reference's blocks, need fewer groups)
+  // the most row groups whose two-row-per-group stages stay within
+  // XS_STAGE_MAX and still give a ring of two (only rows of KBs, the
+  // reference's blocks, need fewer groups: bulk copies stream best at tens of KB)
   for (int G = XS_MAX_COMPUTE / nk; G >= 1; --G) {
+    if (G > 1 && 2 * G * xs_row_bytes(qt, sb) > XS_STAGE_MAX) continue;
     r.G = G;
     r.threads = 32 * (nk * r.G + 1);
     r.grid = (int)std::min<int64_t>(n, num_sms);
