@@ -31,6 +31,8 @@ into the full y on every rank), all inside the timed region.
 Sub-records of the default line (skipped with --no-extras):
 * q4k_gemv -- the Q4_K 4096x4096 decode GEMV (M = 1), per call in a stream of
               distinct weights and timed alone;
+* legacy_gemv -- (one GPU) the default line's GEMV over the reference's own
+              42-byte Q6_K blocks;
 * prefill  -- (one GPU) the Q4_K 14336x4096 bf16 prefill dequant-GEMM at M =
               4096 tokens, TFLOP/s against the sustained bf16 peak;
 * decode   -- the Llama-3-8B-shaped Q4_K_M decode step (context 2048) at
@@ -637,6 +639,17 @@ def measure_extras(args, rank, world, local_rank):
                        "us_per_call": round(q4["ms_per_step"] * 1e3 / q4["weights"], 3),
                        "roofline": rl, "e2e": round(q4["e2e"], 2), "clocks": q4["clocks"]}
     if world == 1:
+        # the same GEMV over the reference's own 42-byte blocks (the layout its
+        # QuantizedLinear holds today), bytes counted as those blocks
+        import copy
+        la = copy.copy(args)
+        la.layout = "legacy"
+        lg = measure_gemv(la, "q6k-gemv", 1, rank, world, local_rank, steps, args.warmup)
+        rl = gemv_roofline(lg, world)
+        out["legacy_gemv"] = {"workload": "Q6_K dequant+GEMV 4096x14336, M=1, the reference's 42-byte blocks",
+                              "weights_per_step": lg["weights"], "value": round(lg["value"], 2), "unit": "GB/s",
+                              "us_per_call": round(lg["ms_per_step"] * 1e3 / lg["weights"], 3), "roofline": rl,
+                              "e2e": round(lg["e2e"], 2), "clocks": lg["clocks"]}
         p = measure_prefill(args, "prefill-14336", 4096, rank, world, local_rank, min(steps, 20), args.warmup)
         sus, sus_kind = peaks("bf16_tflops_sustained", FALLBACK_BF16_SUSTAINED)
         out["prefill"] = {"workload": "Q4_K dequant-GEMM 14336x4096, bf16 x, M=4096 tokens, f32 accumulate",

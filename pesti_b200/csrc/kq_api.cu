@@ -707,17 +707,23 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
                                ctx->next_bracket());
     }
   } else {
-    // the reference's blocks: one token over whole 256-weight spans (Q4_K / Q6_K
-    // tiles) on the single-token kernel under AUTO / DP4A, otherwise the block kernel
+    // the reference's blocks over whole 256-weight spans (Q4_K / Q6_K tiles), up
+    // to 4 tokens, under AUTO / DP4A: one pass of the single-token kernel per
+    // token (each pass streams the weight again, and still beats the block
+    // kernel's 4-token pass, measured); otherwise the block kernel
     const kq::Bracket br = ctx->next_bracket();
     e = cudaErrorNotSupported;
-    if (m == 1 && (ctx->path == KQ_PATH_AUTO || ctx->path == KQ_PATH_DP4A) && k % kq::QK == 0 &&
+    if (m <= kq::DP4A_MAX_M && (ctx->path == KQ_PATH_AUTO || ctx->path == KQ_PATH_DP4A) && k % kq::QK == 0 &&
         (w->dw.type == kq::LEGACY_Q4_K || w->dw.type == kq::LEGACY_Q6_K)) {
       kq::DevWeight lw = w->dw;
       lw.sb = k / kq::QK;
-      kq::XsInput in;
-      in.x = static_cast<const float*>(xd);
-      e = kq::launch_gemv_xs(lw, in, bd, yd, ctx->num_sms, ctx->dev_err, pf, s, &launches, br);
+      for (int64_t t = 0; t < m; ++t) {
+        kq::XsInput in;
+        in.x = static_cast<const float*>(xd) + t * k;
+        e = kq::launch_gemv_xs(lw, in, bd, yd + t * n, ctx->num_sms, ctx->dev_err, t == 0 ? pf : nullptr, s,
+                               &launches, t == 0 ? br : kq::Bracket());
+        if (e != cudaSuccess) break;  // not supported: the first pass, before anything ran
+      }
     }
     if (e == cudaErrorNotSupported)
       e = kq::launch_gemv_legacy(w->dw, static_cast<const float*>(xd), m, bd, yd, s, &launches, br);

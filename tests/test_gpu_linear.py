@@ -239,28 +239,31 @@ def test_legacy_linear_matches_reference_forward(gpu_ctx, dt, n, k, m):
 
 @pytest.mark.parametrize("dt", ["Q4_K", "Q6_K"])
 @pytest.mark.parametrize("n,k", [(4096, 4096), (4096, 14336), (37, 256), (300, 2816), (64, 4000), (16, 32768)])
-def test_legacy_one_token_on_both_kernels(gpu_ctx, dt, n, k):
-    """One token over the reference's blocks: the single-token integer kernel
-    under AUTO where rows are whole 256-weight spans up to 30720 weights (the
-    others fall through), the block kernel under another path; both against
-    the reference's forward and against each other."""
+@pytest.mark.parametrize("m", [1, 3])
+def test_legacy_small_batches_on_both_kernels(gpu_ctx, dt, n, k, m):
+    """Up to 4 tokens over the reference's blocks: the single-token integer
+    kernel (one pass per token) under AUTO where rows are whole 256-weight
+    spans up to 30720 weights (the others fall through), the block kernel
+    under another path; both against the reference's forward, every token,
+    and against each other."""
     kt, ot = LEGACY[dt]
     raw = synthetic.legacy_weight(kt, n, k, seed=n + k)
-    x = synthetic.activations(1, k, seed=k)
+    x = synthetic.activations(m, k, seed=k)
     bias = np.linspace(-1, 1, n).astype(np.float32)
     w = kq.Weight(gpu_ctx, kt, raw, n, k)
-    ref = oracle.legacy_forward(ot, raw, k, n, x, 1, bias=bias).reshape(1, n)
-    y_auto = np.empty((1, n), np.float32)
-    y_blk = np.empty((1, n), np.float32)
+    ref = oracle.legacy_forward(ot, raw, k, n, x, m, bias=bias).reshape(m, n)
+    y_auto = np.empty((m, n), np.float32)
+    y_blk = np.empty((m, n), np.float32)
     try:
-        w.linear(x, 1, y_auto, bias)
+        w.linear(x, m, y_auto, bias)
         gpu_ctx.set_path(kq.KQ_PATH_MMA)
-        w.linear(x, 1, y_blk, bias)
+        w.linear(x, m, y_blk, bias)
     finally:
         gpu_ctx.set_path(kq.KQ_PATH_AUTO)
-    assert rel_err(y_auto, ref) <= TOL
-    assert rel_err(y_blk, ref) <= TOL
-    assert rel_err(y_auto, y_blk) <= TOL
+    for t in range(m):
+        assert rel_err(y_auto[t], ref[t]) <= TOL
+        assert rel_err(y_blk[t], ref[t]) <= TOL
+        assert rel_err(y_auto[t], y_blk[t]) <= TOL
     w.free()
 
 
