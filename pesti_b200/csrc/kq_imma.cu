@@ -244,7 +244,12 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
 }
 
 // Device bytes of one superblock in the weight's tensor map box.
-constexpr int im_block_bytes(int qt) { return qt == GGUF_Q4_K ? Q4K_BYTES : qt == GGUF_Q5_K ? Q5K_BYTES : Q6K_BODY; }
+constexpr int im_block_bytes(int qt) {
+  return qt == GGUF_Q4_K ? Q4K_BYTES : qt == GGUF_Q5_K ? Q5K_BYTES : qt == GGUF_Q3_K ? Q3K_DEV : Q6K_BODY;
+}
+// Types whose scale groups are 16 weights (one k16 step each): Q6_K and Q3_K;
+// they share the Q6_K activation preparation (groups j and j + 8 per lane).
+constexpr bool im_k16(int qt) { return qt == GGUF_Q6_K || qt == GGUF_Q3_K; }
 
 // Bytes of one ring stage for type qt and nt 8-token tiles: the weight box,
 // Q6_K's d box, the activation fragments, the activation sums of the 32 token
@@ -253,7 +258,7 @@ constexpr int im_block_bytes(int qt) { return qt == GGUF_Q4_K ? Q4K_BYTES : qt =
 // shared-memory size (im_shape) both come from here.
 constexpr int im_stage_w(int qt) { return IM_ROWS * im_block_bytes(qt); }
 constexpr int im_stage_d(int qt) { return qt == GGUF_Q6_K ? IM_ROWS * 16 : 0; }
-constexpr int im_stage_s(int qt) { return qt == GGUF_Q6_K ? 32 * 16 * 8 : 32 * 8 * 4; }
+constexpr int im_stage_s(int qt) { return im_k16(qt) ? 32 * 16 * 8 : 32 * 8 * 4; }
 constexpr int im_stage_bytes(int qt, int nt) { return im_stage_w(qt) + im_stage_d(qt) + nt * 4096 + im_stage_s(qt) + 32 * 4; }
 
 template <int QT, int NT>
@@ -341,8 +346,9 @@ __global__ void __launch_bounds__(32 * (im_mma_warps(NT) + 1), im_ctas_per_sm(NT
   // MMA warps: 16 for three or four token tiles (warps w and w + 8 share a
   // 16-row group and take two tiles each), 8 otherwise
   constexpr int MW = im_mma_warps(NT), NTW = im_tiles_per_warp(NT);
-  constexpr bool Q4 = QT != GGUF_Q6_K;  // Q4_K and Q5_K
+  constexpr bool Q4 = !im_k16(QT);  // Q4_K and Q5_K: 32-weight sub-blocks
   constexpr bool Q5 = QT == GGUF_Q5_K;
+  constexpr bool Q6 = QT == GGUF_Q6_K;  // the only type with a separate d box
   constexpr int BPS = im_block_bytes(QT);
   constexpr int QS = Q5 ? 48 : 16;  // offset of the qs bytes in the superblock
   extern __shared__ __align__(128) uint8_t smem[];
@@ -368,7 +374,7 @@ __global__ void __launch_bounds__(32 * (im_mma_warps(NT) + 1), im_ctas_per_sm(NT
     // ---- producer: the weights first (they do not depend on the previous kernel)
     if (lane == 0) {
       sm100::tma_prefetch(&wmap);
-      if constexpr (!Q4) sm100::tma_prefetch(&dmap);
+      if constexpr (Q6) sm100::tma_prefetch(&dmap);
       auto weights = [&](int t) {
         const int st = t % P.S, kb = kb0 + t;
         uint8_t* dst = smem + (size_t)st * P.stage_bytes;
@@ -376,7 +382,7 @@ __global__ void __launch_bounds__(32 * (im_mma_warps(NT) + 1), im_ctas_per_sm(NT
         if constexpr (FUSED) sm100::mbar_expect_tx(&full[st], St::W + St::D);
         else mbar_expect_only(&full[st], St::W + St::D);
         sm100::tma_load_2d(dst, &wmap, kb * BPS, (int)row0, &full[st]);
-        if constexpr (!Q4) sm100::tma_load_2d(dst + St::W, &dmap, kb & ~7, (int)row0, &full[st]);
+        if constexpr (Q6) sm100::tma_load_2d(dst + St::W, &dmap, kb & ~7, (int)row0, &full[st]);
       };
       const int pre = min(T, P.S);
       for (int t = 0; t < pre; ++t) weights(t);
@@ -408,7 +414,7 @@ __global__ void __launch_bounds__(32 * (im_mma_warps(NT) + 1), im_ctas_per_sm(NT
   if constexpr (FUSED) {
     // this CTA's K range [kb0, kb0 + T) for every token slot: job (t, i) =
     // slot t, local superblock i, one warp each, JB jobs' loads in flight per warp
-    constexpr int PQT = QT == GGUF_Q6_K ? GGUF_Q6_K : GGUF_Q4_K;  // Q5_K: the Q4_K preparation
+    constexpr int PQT = im_k16(QT) ? GGUF_Q6_K : GGUF_Q4_K;  // Q5_K: the Q4_K preparation, Q3_K the Q6_K one
     constexpr int JB = 4;
     __shared__ float rinv_s[32];
     if (P.nw) {
@@ -569,6 +575,84 @@ __global__ void __launch_bounds__(32 * (im_mma_warps(NT) + 1), im_ctas_per_sm(NT
           const float vb = fmaf(256.f, (float)aH[i][2 + e], (float)aL[i][2 + e]);
           tot[i][e] = fmaf(f[i][e], fmaf(da, va, -dma * (float)ma[i][e]), tot[i][e]);
           tot[i][2 + e] = fmaf(f[i][e], fmaf(db, vb, -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
+        }
+      }
+    } else if constexpr (QT == GGUF_Q3_K) {
+      // device superblock (112 bytes): hmask[32] | qs[64] | scales[12] | d.  Group
+      // s = 8h + 2G + b (elements 16s..16s+15): this lane's four codes are bits 2G of
+      // qs word (h, b) (bytes 32h + 16b + 4c..) and bit 4h + G of hmask word b (bytes
+      // 16b + 4c..) as bit 2: q + 4 in [0, 7], the -4 through the limb sums (the
+      // preparation's -32 sums divided by 8, exactly)
+      const uint8_t* pa = stage + ra * Q3K_DEV;
+      const uint8_t* pb = stage + rb * Q3K_DEV;
+      const uint4 sda = *reinterpret_cast<const uint4*>(pa + 96), sdb = *reinterpret_cast<const uint4*>(pb + 96);
+      const uint2* bs = reinterpret_cast<const uint2*>(bsf);
+      const int4* ss4 = reinterpret_cast<const int4*>(bsf + St::B);
+      int aH[NTW][4], aL[NTW][4];
+#pragma unroll
+      for (int i = 0; i < NTW; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) aH[i][e] = aL[i][e] = 0;
+#pragma unroll
+      for (int b2 = 0; b2 < 2; ++b2) {
+        const uint32_t hma = *reinterpret_cast<const uint32_t*>(pa + 16 * b2 + 4 * c);
+        const uint32_t hmb = *reinterpret_cast<const uint32_t*>(pb + 16 * b2 + 4 * c);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t qsa = *reinterpret_cast<const uint32_t*>(pa + 32 + 32 * h + 16 * b2 + 4 * c);
+          const uint32_t qsb = *reinterpret_cast<const uint32_t*>(pb + 32 + 32 * h + 16 * b2 + 4 * c);
+#pragma unroll
+          for (int G = 0; G < 4; ++G) {
+            const int sg = 8 * h + 2 * G + b2;
+            const uint32_t a0 = ((qsa >> (2 * G)) & 0x03030303u) | (((hma >> (4 * h + G)) & 0x01010101u) << 2);
+            const uint32_t a1 = ((qsb >> (2 * G)) & 0x03030303u) | (((hmb >> (4 * h + G)) & 0x01010101u) << 2);
+            // six-bit scale of group sg, minus 32: low nibble of scale byte sg (sg < 8)
+            // or high nibble of byte sg - 8, bits 2(sg/4) of byte 8 + sg%4 on top
+            const uint32_t wlo_a = (sg & 4) ? sda.y : sda.x, wlo_b = (sg & 4) ? sdb.y : sdb.x;
+            const int sh = 8 * (sg & 3), hs = 2 * (sg >> 2);
+            const int sca = (int)(((wlo_a >> (sh + ((sg & 8) ? 4 : 0))) & 15u) | (((sda.z >> (sh + hs)) & 3u) << 4)) - 32;
+            const int scb = (int)(((wlo_b >> (sh + ((sg & 8) ? 4 : 0))) & 15u) | (((sdb.z >> (sh + hs)) & 3u) << 4)) - 32;
+#pragma unroll
+            for (int i = 0; i < NTW; ++i) {
+              const int ti = i0 + i;  // token tile
+              if (ti >= NT) break;    // uniform across the warp
+              const uint2 bv = bs[(ti * 16 + sg) * 32 + lane];
+              const int4 sv = ss4[sg * 16 + 4 * ti + c];
+              int ch[4] = {sv.x >> 3, sv.z >> 3, sv.x >> 3, sv.z >> 3};
+              int cl[4] = {sv.y >> 3, sv.w >> 3, sv.y >> 3, sv.w >> 3};
+              mma16_u8s8(ch, a0, a1, bv.x);
+              mma16_u8u8(cl, a0, a1, bv.y);
+              aH[i][0] += sca * ch[0];
+              aH[i][1] += sca * ch[1];
+              aH[i][2] += scb * ch[2];
+              aH[i][3] += scb * ch[3];
+              aL[i][0] += sca * cl[0];
+              aL[i][1] += sca * cl[1];
+              aL[i][2] += scb * cl[2];
+              aL[i][3] += scb * cl[3];
+            }
+          }
+        }
+      }
+      const float da = f16_bits_to_f32((uint16_t)(sda.w & 0xffff)), db = f16_bits_to_f32((uint16_t)(sdb.w & 0xffff));
+      const float* fsc = reinterpret_cast<const float*>(bsf + St::B + St::S);
+      float f[NTW][2];
+#pragma unroll
+      for (int i = 0; i < NTW; ++i)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tk = 8 * (i0 + i) + 2 * c + e;
+          f[i][e] = tk < P.m ? fsc[tk] : 0.f;
+        }
+      stage_release(&empty[st], lane);
+#pragma unroll
+      for (int i = 0; i < NTW; ++i) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float va = fmaf(256.f, (float)aH[i][e], (float)aL[i][e]);
+          const float vb = fmaf(256.f, (float)aH[i][2 + e], (float)aL[i][2 + e]);
+          tot[i][e] = fmaf(f[i][e] * da, va, tot[i][e]);
+          tot[i][2 + e] = fmaf(f[i][e] * db, vb, tot[i][2 + e]);
         }
       }
     } else {
@@ -918,7 +1002,7 @@ cudaError_t launch_chunk(const DevWeight& w, int m, const ImWs& L, void* ws, con
     bracket_record(br.stop, s);
     return e;
   }
-  constexpr int PQT = QT == GGUF_Q6_K ? GGUF_Q6_K : GGUF_Q4_K;  // Q5_K: the Q4_K preparation
+  constexpr int PQT = im_k16(QT) ? GGUF_Q6_K : GGUF_Q4_K;  // Q5_K: the Q4_K preparation, Q3_K the Q6_K one
   const int sb = (int)w.sb, nt = NT;
   const int64_t warps = (int64_t)nt * 8 * sb;
   const int64_t x_ld = op.x_ld ? op.x_ld : w.k;
@@ -960,6 +1044,7 @@ static cudaError_t im_attrs() {
 cudaError_t imma_init_device() {
   cudaError_t e = im_attrs<GGUF_Q4_K>();
   if (e == cudaSuccess) e = im_attrs<GGUF_Q5_K>();
+  if (e == cudaSuccess) e = im_attrs<GGUF_Q3_K>();
   if (e == cudaSuccess) e = im_attrs<GGUF_Q6_K>();
   return e;
 }
@@ -970,7 +1055,8 @@ size_t imma_counter_bytes(int64_t n) { return (size_t)((n + IM_ROWS - 1) / IM_RO
 cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, const float* bias, float* y, void* ws,
                              unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br,
                              const ImOpts& op) {
-  if (w.type != GGUF_Q4_K && w.type != GGUF_Q5_K && w.type != GGUF_Q6_K) return cudaErrorNotSupported;
+  if (w.type != GGUF_Q4_K && w.type != GGUF_Q5_K && w.type != GGUF_Q6_K && w.type != GGUF_Q3_K)
+    return cudaErrorNotSupported;
   const int64_t x_ld = op.x_ld ? op.x_ld : w.k;
   const ImWs L = im_ws(m64, w.n, w.k, num_sms);
   for (int64_t m0 = 0; m0 < m64; m0 += 32) {
@@ -990,6 +1076,8 @@ cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, co
       KQ_IM_CHUNK(GGUF_Q4_K)
     } else if (w.type == GGUF_Q5_K) {
       KQ_IM_CHUNK(GGUF_Q5_K)
+    } else if (w.type == GGUF_Q3_K) {
+      KQ_IM_CHUNK(GGUF_Q3_K)
     } else {
       KQ_IM_CHUNK(GGUF_Q6_K)
     }
