@@ -78,8 +78,8 @@ enum kq_type {
 #define KQ_PATH_IMMA 4    /* integer mma.sync on the raw 4/6-bit codes        */
                           /* (TMA-fed 128-row tiles, split-K)                */
 /* Q2_K / Q3_K / Q5_K: m = 1 under AUTO and DP4A runs the single-token dp4a  */
-/* kernel (in_features <= 30720), Q3_K / Q5_K 2 <= m <= 64 under AUTO and    */
-/* IMMA the integer MMA kernel; every other case the CUDA-core f32 kernel.   */
+/* kernel (in_features <= 30720), 2 <= m <= 64 under AUTO and IMMA the      */
+/* integer MMA kernel; every other case the CUDA-core f32 kernel.            */
 /* KQ_PESTI_Q4_K_LEGACY / _Q6_K_LEGACY: m <= 4 with in_features a multiple  */
 /* of 256 (<= 30720) under AUTO and DP4A runs the single-token dp4a kernel   */
 /* once per token; every other case the block kernel.                        */

@@ -218,14 +218,13 @@ constexpr int FAM_KX = -1;
 // two Q6_K tokens), integer tensor-core tiles for Q4_K up to 64 tokens and
 // Q6_K up to 8, mma.sync bf16 tiles for Q6_K up to 64, tcgen05 above.
 // Q2_K / Q3_K / Q5_K: the single-token kernel at one token (AUTO, DP4A),
-// Q5_K and Q3_K on integer tensor-core tiles up to 64 tokens (AUTO, IMMA), otherwise
+// on integer tensor-core tiles up to 64 tokens (AUTO, IMMA), otherwise
 // the CUDA-core f32 kernel.
 int f32_family(const kq_ctx* ctx, const kq::DevWeight& w, int64_t m) {
   if (is_kx(w.type)) {
     const bool auto_ = ctx->path == KQ_PATH_AUTO;
     if (m == 1 && (auto_ || ctx->path == KQ_PATH_DP4A)) return KQ_PATH_DP4A;
-    if ((w.type == kq::GGUF_Q5_K || w.type == kq::GGUF_Q3_K) && m <= 64 && (auto_ || ctx->path == KQ_PATH_IMMA))
-      return KQ_PATH_IMMA;
+    if (m <= 64 && (auto_ || ctx->path == KQ_PATH_IMMA)) return KQ_PATH_IMMA;
     return FAM_KX;
   }
   const bool q4 = w.type == kq::GGUF_Q4_K;
@@ -585,8 +584,8 @@ int kq_weight_upload(kq_ctx* ctx, int type, const void* bytes, size_t nbytes, in
   }
   w->dw.q = static_cast<const uint8_t*>(w->q_alloc);
   w->dw.d = static_cast<const uint16_t*>(w->d_alloc);
-  // TMA descriptors: Q4_K / Q6_K (every tensor-core path), Q5_K and Q3_K (integer MMA)
-  if ((is_gguf(type) || type == kq::GGUF_Q5_K || type == kq::GGUF_Q3_K) && n > 0 && k > 0 &&
+  // TMA descriptors: Q4_K / Q6_K (every tensor-core path), the other K-quants (integer MMA)
+  if ((is_gguf(type) || is_kx(type)) && n > 0 && k > 0 &&
       !kq::tc_make_weight_maps(w->dw)) {
     cudaFree(w->q_alloc);
     if (w->d_alloc) cudaFree(w->d_alloc);
@@ -1101,8 +1100,7 @@ static int batched_linear(kq_ctx* ctx, const kq_weight* w, const float* x, int64
   if (w->device != ctx->device)
     return fail(ctx, KQ_ERR_INVALID_ARG, "weight lives on device %d, context on %d", w->device, ctx->device);
   if (w->dw.k == 0 || w->dw.n == 0) return fail(ctx, KQ_ERR_UNSUPPORTED, "%s: empty weight", what);
-  if ((!is_gguf(w->dw.type) && w->dw.type != kq::GGUF_Q5_K && w->dw.type != kq::GGUF_Q3_K) ||
-      f32_family(ctx, w->dw, m) != KQ_PATH_IMMA)
+  if ((!is_gguf(w->dw.type) && !is_kx(w->dw.type)) || f32_family(ctx, w->dw, m) != KQ_PATH_IMMA)
     return fail(ctx, KQ_ERR_UNSUPPORTED, "%s: the integer tensor-core kernel does not serve type %d at m = %lld",
                 what, w->dw.type, (long long)m);
   if (((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(op.nw)) & 15) ||

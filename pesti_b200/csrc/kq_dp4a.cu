@@ -550,7 +550,7 @@ __host__ __device__ constexpr int xs_stride(int qt) {
          : qt == GGUF_Q3_K   ? Q3K_DEV
          : qt == LEGACY_Q4_K ? 16 * 28  // the reference's blocks: 16 per 256 weights
          : qt == LEGACY_Q6_K ? 16 * 42
-                             : Q2K_BYTES;
+                             : Q2K_DEV;
 }
 // The reference's own 16-weight blocks (rows of k % 256 == 0 weights, so a
 // row is whole 256-weight spans of 448 / 672 bytes).
@@ -1148,11 +1148,11 @@ __global__ void __launch_bounds__(32 * (XS_MAX_COMPUTE + 1), 1) xs_gemv_kernel(c
           v = fmaf(d * xf, acc, v);
         }
       } else if constexpr (QT == GGUF_Q2_K) {
-        // scales[16] | qs[64] | d | dmin at an 84-byte stride: 4-byte aligned,
-        // so 32-bit loads.  Codes at bits sh2 (A) / sh2 + 2 (B) of qs bytes
+        // scales[16] | qs[64] | d | dmin at the 96-byte device stride (32-bit
+        // loads).  Codes at bits sh2 (A) / sh2 + 2 (B) of qs bytes
         // 32(u/2) .. + 31; the B codes are used in place (4x) and their sums
         // divided by 4, exactly
-        const uint32_t* blk = reinterpret_cast<const uint32_t*>(rowp + kb * Q2K_BYTES);
+        const uint32_t* blk = reinterpret_cast<const uint32_t*>(rowp + kb * Q2K_DEV);
         const uint32_t scw = blk[u];  // scale / min nibbles of sub-blocks 4u .. 4u+3
         const uint32_t dd = blk[20];  // d | dmin
         const uint32_t* qs = blk + 4 + 8 * (u >> 1);

@@ -245,11 +245,15 @@ __global__ void __launch_bounds__(256) imma_prep_kernel(const float* __restrict_
 
 // Device bytes of one superblock in the weight's tensor map box.
 constexpr int im_block_bytes(int qt) {
-  return qt == GGUF_Q4_K ? Q4K_BYTES : qt == GGUF_Q5_K ? Q5K_BYTES : qt == GGUF_Q3_K ? Q3K_DEV : Q6K_BODY;
+  return qt == GGUF_Q4_K   ? Q4K_BYTES
+         : qt == GGUF_Q5_K ? Q5K_BYTES
+         : qt == GGUF_Q3_K ? Q3K_DEV
+         : qt == GGUF_Q2_K ? Q2K_DEV
+                           : Q6K_BODY;
 }
-// Types whose scale groups are 16 weights (one k16 step each): Q6_K and Q3_K;
-// they share the Q6_K activation preparation (groups j and j + 8 per lane).
-constexpr bool im_k16(int qt) { return qt == GGUF_Q6_K || qt == GGUF_Q3_K; }
+// Types whose scale groups are 16 weights (one k16 step each): Q6_K, Q3_K and
+// Q2_K; they share the Q6_K activation preparation (groups j and j + 8 per lane).
+constexpr bool im_k16(int qt) { return qt == GGUF_Q6_K || qt == GGUF_Q3_K || qt == GGUF_Q2_K; }
 
 // Bytes of one ring stage for type qt and nt 8-token tiles: the weight box,
 // Q6_K's d box, the activation fragments, the activation sums of the 32 token
@@ -567,6 +571,86 @@ __global__ void __launch_bounds__(32 * (im_mma_warps(NT) + 1), im_ctas_per_sm(NT
       stage_release(&empty[st], lane);
       const float da = f16_bits_to_f32((uint16_t)(ha.x & 0xffff)), dma = f16_bits_to_f32((uint16_t)(ha.x >> 16));
       const float db = f16_bits_to_f32((uint16_t)(hb.x & 0xffff)), dmb = f16_bits_to_f32((uint16_t)(hb.x >> 16));
+#pragma unroll
+      for (int i = 0; i < NTW; ++i) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float va = fmaf(256.f, (float)aH[i][e], (float)aL[i][e]);
+          const float vb = fmaf(256.f, (float)aH[i][2 + e], (float)aL[i][2 + e]);
+          tot[i][e] = fmaf(f[i][e], fmaf(da, va, -dma * (float)ma[i][e]), tot[i][e]);
+          tot[i][2 + e] = fmaf(f[i][e], fmaf(db, vb, -dmb * (float)ma[i][2 + e]), tot[i][2 + e]);
+        }
+      }
+    } else if constexpr (QT == GGUF_Q2_K) {
+      // device superblock (96 bytes): scales[16] | qs[64] | d | dmin | 12 zero bytes.
+      // Group s = 8h + 2G + b (elements 16s..16s+15): this lane's four 2-bit codes are
+      // bits 2G of qs word (h, b) (bytes 16 + 32h + 16b + 4c..); scale byte s holds the
+      // group's scale (low nibble) and min (high nibble); value = d sc q - dmin m.  The
+      // min term takes the group's activation sum from the Q6_K preparation's limb sums:
+      // sum x = -(256 S_hi + S_lo) / 32, exactly
+      const uint8_t* pa = stage + ra * Q2K_DEV;
+      const uint8_t* pb = stage + rb * Q2K_DEV;
+      const uint4 sca4 = *reinterpret_cast<const uint4*>(pa), scb4 = *reinterpret_cast<const uint4*>(pb);
+      const uint32_t dda = *reinterpret_cast<const uint32_t*>(pa + 80);
+      const uint32_t ddb = *reinterpret_cast<const uint32_t*>(pb + 80);
+      const uint2* bs = reinterpret_cast<const uint2*>(bsf);
+      const int4* ss4 = reinterpret_cast<const int4*>(bsf + St::B);
+      int aH[NTW][4], aL[NTW][4], ma[NTW][4];
+#pragma unroll
+      for (int i = 0; i < NTW; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) aH[i][e] = aL[i][e] = ma[i][e] = 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int b2 = 0; b2 < 2; ++b2) {
+          const uint32_t qsa = *reinterpret_cast<const uint32_t*>(pa + 16 + 32 * h + 16 * b2 + 4 * c);
+          const uint32_t qsb = *reinterpret_cast<const uint32_t*>(pb + 16 + 32 * h + 16 * b2 + 4 * c);
+#pragma unroll
+          for (int G = 0; G < 4; ++G) {
+            const int sg = 8 * h + 2 * G + b2;
+            const uint32_t a0 = (qsa >> (2 * G)) & 0x03030303u, a1 = (qsb >> (2 * G)) & 0x03030303u;
+            const uint32_t wa = (sg < 4 ? sca4.x : sg < 8 ? sca4.y : sg < 12 ? sca4.z : sca4.w) >> (8 * (sg & 3));
+            const uint32_t wb = (sg < 4 ? scb4.x : sg < 8 ? scb4.y : sg < 12 ? scb4.z : scb4.w) >> (8 * (sg & 3));
+            const int sca = (int)(wa & 15u), mina = (int)((wa >> 4) & 15u);
+            const int scb = (int)(wb & 15u), minb = (int)((wb >> 4) & 15u);
+#pragma unroll
+            for (int i = 0; i < NTW; ++i) {
+              const int ti = i0 + i;  // token tile
+              if (ti >= NT) break;    // uniform across the warp
+              const uint2 bv = bs[(ti * 16 + sg) * 32 + lane];
+              const int4 sv = ss4[sg * 16 + 4 * ti + c];
+              int ch[4] = {0, 0, 0, 0}, cl[4] = {0, 0, 0, 0};
+              mma16_u8s8(ch, a0, a1, bv.x);
+              mma16_u8u8(cl, a0, a1, bv.y);
+              aH[i][0] += sca * ch[0];
+              aH[i][1] += sca * ch[1];
+              aH[i][2] += scb * ch[2];
+              aH[i][3] += scb * ch[3];
+              aL[i][0] += sca * cl[0];
+              aL[i][1] += sca * cl[1];
+              aL[i][2] += scb * cl[2];
+              aL[i][3] += scb * cl[3];
+              const int s0 = -((sv.x * 256 + sv.y) >> 5), s1 = -((sv.z * 256 + sv.w) >> 5);  // tokens 2c, 2c+1
+              ma[i][0] += mina * s0;
+              ma[i][1] += mina * s1;
+              ma[i][2] += minb * s0;
+              ma[i][3] += minb * s1;
+            }
+          }
+        }
+      const float da = f16_bits_to_f32((uint16_t)(dda & 0xffff)), dma = f16_bits_to_f32((uint16_t)(dda >> 16));
+      const float db = f16_bits_to_f32((uint16_t)(ddb & 0xffff)), dmb = f16_bits_to_f32((uint16_t)(ddb >> 16));
+      const float* fsc = reinterpret_cast<const float*>(bsf + St::B + St::S);
+      float f[NTW][2];
+#pragma unroll
+      for (int i = 0; i < NTW; ++i)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tk = 8 * (i0 + i) + 2 * c + e;
+          f[i][e] = tk < P.m ? fsc[tk] : 0.f;
+        }
+      stage_release(&empty[st], lane);
 #pragma unroll
       for (int i = 0; i < NTW; ++i) {
 #pragma unroll
@@ -1045,6 +1129,7 @@ cudaError_t imma_init_device() {
   cudaError_t e = im_attrs<GGUF_Q4_K>();
   if (e == cudaSuccess) e = im_attrs<GGUF_Q5_K>();
   if (e == cudaSuccess) e = im_attrs<GGUF_Q3_K>();
+  if (e == cudaSuccess) e = im_attrs<GGUF_Q2_K>();
   if (e == cudaSuccess) e = im_attrs<GGUF_Q6_K>();
   return e;
 }
@@ -1055,7 +1140,8 @@ size_t imma_counter_bytes(int64_t n) { return (size_t)((n + IM_ROWS - 1) / IM_RO
 cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, const float* bias, float* y, void* ws,
                              unsigned* ctr, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br,
                              const ImOpts& op) {
-  if (w.type != GGUF_Q4_K && w.type != GGUF_Q5_K && w.type != GGUF_Q6_K && w.type != GGUF_Q3_K)
+  if (w.type != GGUF_Q4_K && w.type != GGUF_Q5_K && w.type != GGUF_Q6_K && w.type != GGUF_Q3_K &&
+      w.type != GGUF_Q2_K)
     return cudaErrorNotSupported;
   const int64_t x_ld = op.x_ld ? op.x_ld : w.k;
   const ImWs L = im_ws(m64, w.n, w.k, num_sms);
@@ -1078,6 +1164,8 @@ cudaError_t launch_gemv_imma(const DevWeight& w, const float* x, int64_t m64, co
       KQ_IM_CHUNK(GGUF_Q5_K)
     } else if (w.type == GGUF_Q3_K) {
       KQ_IM_CHUNK(GGUF_Q3_K)
+    } else if (w.type == GGUF_Q2_K) {
+      KQ_IM_CHUNK(GGUF_Q2_K)
     } else {
       KQ_IM_CHUNK(GGUF_Q6_K)
     }

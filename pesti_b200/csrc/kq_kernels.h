@@ -12,7 +12,8 @@ constexpr int QK = 256;         // weights per K-quant superblock
 constexpr int Q4K_BYTES = 144;  // GGUF Q4_K superblock
 constexpr int Q6K_BYTES = 210;  // GGUF Q6_K superblock
 constexpr int Q6K_BODY = 208;   // device Q6_K body: ql(128) | qh(64) | scales(16)
-constexpr int Q2K_BYTES = 84;   // GGUF Q2_K superblock (stored as is: 4-byte aligned at any index)
+constexpr int Q2K_BYTES = 84;   // GGUF Q2_K superblock
+constexpr int Q2K_DEV = 96;     // device Q2_K superblock: the 84 bytes + 12 zero bytes (16-byte aligned)
 constexpr int Q3K_BYTES = 110;  // GGUF Q3_K superblock
 constexpr int Q3K_DEV = 112;    // device Q3_K superblock: the 110 bytes + 2 zero bytes (16-byte aligned)
 constexpr int Q5K_BYTES = 176;  // GGUF Q5_K superblock (stored as is)
@@ -34,11 +35,11 @@ enum QType : int {
 //  GGUF_Q6_K: q = bodies [n][sb][208] (ql|qh|scales), d = f16 [n][d_ld]
 //             (row-major, d_ld = sb rounded up to 8 so every row's d is a
 //             whole number of 16-byte units and a block of rows is one run).
-//  GGUF_Q2_K / Q5_K: q = raw superblocks, rows row_bytes apart (the row's
-//             bytes rounded up to a multiple of 16).
-//  GGUF_Q3_K: q = superblocks at a 112-byte stride (each padded with two
-//             zero bytes, so every superblock starts on a 16-byte boundary),
-//             rows row_bytes = 112 sb apart.
+//  GGUF_Q5_K: q = raw superblocks, rows row_bytes = 176 sb apart.
+//  GGUF_Q3_K / Q2_K: q = superblocks at a 112 / 96-byte stride (each padded
+//             with zero bytes, so every superblock starts on a 16-byte
+//             boundary and is one TMA box column), rows row_bytes = 112 / 96 sb
+//             apart.
 //  LEGACY_*:  q = raw bytes as uploaded (row stride = legacy row bytes), len.
 // wmap / dmap: TMA descriptors of q (128 rows x one superblock per box) and d.
 struct DevWeight {

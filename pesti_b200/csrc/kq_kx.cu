@@ -20,10 +20,10 @@
 // Every product is rounded on its own (__fmul_rn / __fsub_rn), in this
 // association, so the decode matches the CPU definition bit for bit.
 //
-// Device layout: Q2_K and Q5_K rows as uploaded, the row stride rounded up to
-// 16 bytes (row_bytes) so every row starts on a 16-byte boundary for
-// cp.async; Q3_K superblocks at a 112-byte stride (two zero bytes after each),
-// so that every one starts on a 16-byte boundary for vector loads.
+// Device layout: Q5_K rows as uploaded (176-byte superblocks, 16-byte
+// multiples); Q3_K and Q2_K superblocks at a 112 / 96-byte stride (zero bytes
+// after each), so that every one starts on a 16-byte boundary for vector loads
+// and tensor-map boxes.
 //
 // GEMV: a CTA owns KX_RB rows (two per warp) and walks K in chunks of CH
 // superblocks.  Each chunk's activations (up to MT tokens) and the CTA's
@@ -54,7 +54,7 @@ struct KxFmt;
 // superblocks of a row; CH: superblocks per chunk (CH * DS is a multiple of 16)
 template <>
 struct KxFmt<GGUF_Q2_K> {
-  static constexpr int BS = Q2K_BYTES, DS = Q2K_BYTES, CH = 4;
+  static constexpr int BS = Q2K_BYTES, DS = Q2K_DEV, CH = 4;
 };
 template <>
 struct KxFmt<GGUF_Q3_K> {

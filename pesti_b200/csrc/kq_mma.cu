@@ -643,10 +643,13 @@ void tc_counter_span(int64_t m, int64_t n, int64_t k, int num_sms, size_t* offse
 }
 
 bool tc_make_weight_maps(DevWeight& w) {
-  if (w.type == GGUF_Q4_K || w.type == GGUF_Q5_K || w.type == GGUF_Q3_K) {
-    // one box = one superblock of 128 rows (Q5_K / Q3_K rows: sb x 176 / 112 bytes, the
-    // integer-MMA kernel's maps)
-    const uint32_t bs = w.type == GGUF_Q4_K ? Q4K_BYTES : w.type == GGUF_Q5_K ? Q5K_BYTES : Q3K_DEV;
+  if (w.type == GGUF_Q4_K || w.type == GGUF_Q5_K || w.type == GGUF_Q3_K || w.type == GGUF_Q2_K) {
+    // one box = one superblock of 128 rows (Q5_K / Q3_K / Q2_K rows: sb x 176 / 112 / 96
+    // bytes, the integer-MMA kernel's maps)
+    const uint32_t bs = w.type == GGUF_Q4_K   ? Q4K_BYTES
+                        : w.type == GGUF_Q5_K ? Q5K_BYTES
+                        : w.type == GGUF_Q3_K ? Q3K_DEV
+                                              : Q2K_DEV;
     const uint64_t rb = (uint64_t)w.sb * bs;
     if (!make_map_2d(&w.wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w.q, rb, (uint64_t)w.n, rb, bs, TM,
                      CU_TENSOR_MAP_SWIZZLE_NONE))

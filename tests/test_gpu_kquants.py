@@ -1,5 +1,5 @@
 """GGUF Q2_K, Q3_K and Q5_K on the device (kq_kx.cu, the single-token dp4a
-kernel of kq_dp4a.cu, Q5_K and Q3_K on the integer-MMA kernel of kq_imma.cu) and the
+kernel of kq_dp4a.cu, batches on the integer-MMA kernel of kq_imma.cu) and the
 reference's legacy Q5_K rows:
 dequantization bit-exact with the oracle (on the gguf-py fixture superblocks
 and on random weights), linears within 1e-3 of max|y| of the oracle's
@@ -95,11 +95,12 @@ def test_one_token_on_both_kernels(gpu_ctx, name, kt, ot, tag, n, k):
 
 
 @pytest.mark.parametrize("name,kt,ot", [("Q5_K", kq.KQ_GGUF_Q5_K, oracle.GGUF_Q5_K),
-                                        ("Q3_K", kq.KQ_GGUF_Q3_K, oracle.GGUF_Q3_K)], ids=["Q5_K", "Q3_K"])
+                                        ("Q3_K", kq.KQ_GGUF_Q3_K, oracle.GGUF_Q3_K),
+                                        ("Q2_K", kq.KQ_GGUF_Q2_K, oracle.GGUF_Q2_K)], ids=["Q5_K", "Q3_K", "Q2_K"])
 @pytest.mark.parametrize("n,k,m", [(4096, 4096, 8), (300, 2816, 5), (1024, 14336, 32), (130, 1280, 40)])
 def test_batches_on_integer_mma_and_the_f32_kernel(gpu_ctx, name, kt, ot, n, k, m):
-    """Q5_K and Q3_K at 2..64 tokens run the integer tensor-core kernel under
-    AUTO (32-token chunks above 32) and the f32 kernel under another path."""
+    """Q5_K, Q3_K and Q2_K at 2..64 tokens run the integer tensor-core kernel
+    under AUTO (32-token chunks above 32) and the f32 kernel under another path."""
     raw = synthetic.gguf_weight(kt, n, k, seed=n + 7 * k + m)
     x = synthetic.activations(m, k, seed=m)
     bias = np.linspace(-1, 1, n).astype(np.float32)
