@@ -230,13 +230,16 @@ def test_batched_residual_linear_adds_into_h(gpu_ctx, dt, n, k, m):
 
 def test_batched_forms_report_unsupported_cases(gpu_ctx):
     """Where AUTO picks another kernel family (one token; Q6_K above 8
-    tokens; Q2_K) the batched forms queue nothing and say so."""
+    tokens; the reference's legacy blocks) the batched forms queue nothing
+    and say so."""
     lib = _lib(gpu_ctx)
     x = _dev(np.zeros((16, 1024), np.float32))
     nwd = _dev(np.ones(1024, np.float32))
     y = _dev(np.zeros((16, 256), np.float32))
-    for kt, m in [(kq.KQ_GGUF_Q4_K, 1), (kq.KQ_GGUF_Q6_K, 9), (kq.KQ_GGUF_Q2_K, 4)]:
-        w = kq.Weight(gpu_ctx, kt, synthetic.gguf_weight(kt, 256, 1024, seed=1), 256, 1024)
+    for kt, m in [(kq.KQ_GGUF_Q4_K, 1), (kq.KQ_GGUF_Q6_K, 9), (kq.KQ_PESTI_Q4_K_LEGACY, 4)]:
+        raw = (synthetic.legacy_weight(kt, 256, 1024, seed=1) if kt == kq.KQ_PESTI_Q4_K_LEGACY
+               else synthetic.gguf_weight(kt, 256, 1024, seed=1))
+        w = kq.Weight(gpu_ctx, kt, raw, 256, 1024)
         launches = gpu_ctx.launch_count
         assert lib.kq_dec_residual_linear_batch(gpu_ctx.handle, w.handle, _p(x), m, _p(y), 0) == kq.KQ_ERR_UNSUPPORTED
         assert lib.kq_dec_norm_linear_batch(gpu_ctx.handle, w.handle, _p(x), 1024, m, _p(nwd), 1024, 1e-5, _p(y),
