@@ -155,7 +155,7 @@ int kq_linear_f32(kq_ctx *ctx, const kq_weight *w, const float *x, int64_t m,
 /* Prefill form: x is bf16 [m][in] (raw 16-bit values), y f32 [m][out].  The
  * weights are dequantized to bf16 tiles on the tensor cores (tcgen05); GGUF
  * weights only.  No reference counterpart: the reference has no prefill
- * kernel (the north-star prefill dequant-GEMM). */
+ * dequant-GEMM. */
 int kq_linear_bf16(kq_ctx *ctx, const kq_weight *w, const void *x_bf16, int64_t m,
                    const float *bias, float *y, int flags);
 /* Same product for callers that must not allocate device memory during the
