@@ -676,7 +676,7 @@ static int linear_impl(kq_ctx* ctx, const kq_weight* w, const void* x, size_t xe
     }
   } else if (bf16) {
     if ((rc = ensure(ctx, &ctx->ws, &ctx->ws_bytes, kq::tc_workspace_bytes_bf16(m, k), "workspace"))) return rc;
-    e = kq::launch_tc_bf16(w->dw, xd, m, bd, yd, ctx->ws, ctx->dev_err, s, &launches, ctx->next_bracket());
+    e = kq::launch_tc_bf16(w->dw, xd, m, bd, yd, ctx->ws, ctx->num_sms, ctx->dev_err, s, &launches, ctx->next_bracket());
   } else if (is_kx(w->dw.type) && f32_family(ctx, w->dw, m) != KQ_PATH_IMMA) {
     // one token: the single-token dp4a kernel (AUTO / DP4A; widths it cannot
     // stage fall through); otherwise the CUDA-core f32 kernel

@@ -365,8 +365,10 @@ void tc_counter_span(int64_t m, int64_t n, int64_t k, int num_sms, size_t* offse
 cudaError_t launch_tc_f32(const DevWeight& w, const float* x, int64_t m, const float* bias, float* y,
                           void* ws, int num_sms, int* err, cudaStream_t s, int* launches, Bracket br,
                           unsigned* counters);
-// Same with bf16 x (prefill); A is dequantized to bf16.
+// Same with bf16 x (prefill); A is dequantized to bf16.  Tiles of 256 tokens,
+// or 128 where 256-token tiles would leave SMs idle (num_sms).
 cudaError_t launch_tc_bf16(const DevWeight& w, const void* x, int64_t m, const float* bias, float* y,
-                           void* ws, int* err, cudaStream_t s, int* launches, Bracket br = Bracket());
+                           void* ws, int num_sms, int* err, cudaStream_t s, int* launches,
+                           Bracket br = Bracket());
 
 }  // namespace kq

@@ -2,16 +2,24 @@
 //
 // y[t][row] = sum_k x[t][k] * W[row][k] for a 128-row weight tile per CTA:
 //
-//   warps 0-3  dequantize: thread r owns weight row r of the tile.  It reads
-//              its row's raw superblock from shared memory (TMA-loaded),
-//              rebuilds 64 weights at a time as f16 / bf16 pairs and writes
-//              them straight into tensor memory (tcgen05.st), where they are
-//              the A operand of the MMA.  They also run the epilogue.
-//   warp 4     TMA producer: raw weight tiles (128 rows x one superblock) and
-//              activation tiles (BN columns x 64 k, 128-byte swizzle).
-//   warp 5     MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from shared
+//   warps 0-7  dequantize: thread r of warp w owns weight row r = 32*(w%4) +
+//              lane of the tile and quarters 2*(w/4), 2*(w/4)+1 of every
+//              superblock.  It reads its row's raw superblock from shared
+//              memory (TMA-loaded), rebuilds 64 weights at a time as f16 /
+//              bf16 pairs and writes them straight into tensor memory
+//              (tcgen05.st), where they are the A operand of the MMA.  Warps
+//              0-3 also run the epilogue.
+//   warp 8     TMA producer of the raw weight tiles (128 rows x one superblock).
+//   warp 9     TMA producer of the activation tiles (BN columns x 64 k,
+//              128-byte swizzle), in pairs.
+//   warp 10    MMA issuer: tcgen05.mma kind::f16, A from TMEM, B from shared
 //              memory, accumulator (128 x BN f32) in TMEM; tcgen05.commit
-//              frees A slots and activation slots and signals the epilogue.
+//              frees activation pairs and A superblock slots and signals the
+//              epilogue.  Its barrier waits and commits cost about as much
+//              issue time as the MMAs, so there is one wait / commit per
+//              activation pair and per superblock of A, not per quarter
+//              (measured: 838 -> 1066 TFLOP/s on a 14336 x 4096 Q4_K weight
+//              at 4096 tokens).
 //
 // The weights' K order inside a superblock is the order in which a thread
 // unpacks them cheaply (per 64-weight quarter c and step s: weights e, e+2,
@@ -42,10 +50,18 @@ using namespace sm100;
 
 constexpr int TM = 128;    // weight rows per CTA = UMMA M
 constexpr int KSTEP = 64;  // k per A slot / activation tile (one quarter superblock)
-constexpr int DEQ_WARPS = 8;             // two per TMEM lane quadrant, each doing 2 quarters
-constexpr int PRODUCER_WARP = DEQ_WARPS;
-constexpr int MMA_WARP = DEQ_WARPS + 1;
-constexpr int THREADS = 32 * (DEQ_WARPS + 2);
+// Warp roles: eight dequant warps (two per TMEM lane quadrant, each doing two
+// of the four 64-k quarters of every superblock), one TMA producer for the raw
+// weight tiles, one for the activation tiles, one MMA issuer.  The two
+// producers run independently, so a raw tile is requested as soon as its ring
+// slot is free rather than behind the activation tiles' waits on the MMAs.
+struct W {
+  static constexpr int DEQ = 8;       // dequant warps
+  static constexpr int RAW = DEQ;      // raw-tile producer
+  static constexpr int ACT = DEQ + 1;  // activation-tile producer
+  static constexpr int MMA = DEQ + 2;
+  static constexpr int THREADS = 32 * (DEQ + 3);
+};
 
 enum : int { ERR_WAIT_RAW = 1, ERR_WAIT_A = 2, ERR_WAIT_B = 3, ERR_WAIT_ACC = 4, ERR_WAIT_MMA = 5 };
 
@@ -66,9 +82,16 @@ struct RawTile<GGUF_Q6_K> {
 
 template <int QT, int BN>
 struct Cfg {
-  static constexpr int RS = BN <= 64 ? 3 : 2;             // raw weight stages
-  static constexpr int BS = BN <= 64 ? 8 : 4;             // activation stages
-  static constexpr int AS = 4;                            // A slots in TMEM (32 columns each)
+  // The MMA warp's waits and commits cost about as much as its MMAs, so they
+  // are made per group: activation tiles come in groups of BG quarters (one
+  // full / empty barrier pair per group), the A operand in TMEM per
+  // superblock (four 32-column quarters per slot).
+  static constexpr int RS = BN <= 64 ? 3 : (QT == GGUF_Q6_K ? 2 : 3);  // raw weight stages
+  static constexpr int BG = 2;                            // quarters per activation group
+  static constexpr int BGS = BN <= 128 ? 4 : 2;           // activation group slots
+  static constexpr int BS = BG * BGS;                     // activation tile slots
+  static constexpr int ASB = BN >= 128 ? 2 : 1;           // A superblock slots in TMEM
+  static constexpr int AS = 4 * ASB;                      // A quarter slots (32 columns each)
   static constexpr int BTILE = BN * 128;                  // activation tile bytes (64 k x BN x 2 B)
   // Small-N MMAs into one accumulator serialise on their latency, so decode
   // tiles rotate their k16 steps over independent accumulator sets that the
@@ -82,8 +105,9 @@ struct Cfg {
   static constexpr int OFF_B = 0;                         // 1024-aligned (swizzled tiles)
   static constexpr int OFF_RAW = OFF_B + BS * BTILE;
   static constexpr int OFF_BAR = OFF_RAW + RS * RawTile<QT>::BYTES;
-  static constexpr int NBAR = 2 * RS + 2 * BS + 2 * AS + 1;
+  static constexpr int NBAR = 2 * RS + 2 * BGS + 2 * ASB + 1;
   static constexpr int SMEM = OFF_BAR + NBAR * 8 + 16 + 1024;  // + tmem holder + alignment slack
+  static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
 
 // ---- per-row superblock unpacking (thread = row) ---------------------------
@@ -213,7 +237,7 @@ __device__ __forceinline__ void raw_release(uint64_t* empty) {
 }
 
 template <int QT, int BN, bool BF16>
-__global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
+__global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
     kq_mma_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap dmap,
                   const __grid_constant__ CUtensorMap xmap, Params P) {
   using C = Cfg<QT, BN>;
@@ -225,11 +249,11 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* raw_full = bar;
   uint64_t* raw_empty = raw_full + C::RS;
-  uint64_t* b_full = raw_empty + C::RS;
-  uint64_t* b_empty = b_full + C::BS;
-  uint64_t* a_full = b_empty + C::BS;
-  uint64_t* a_empty = a_full + C::AS;
-  uint64_t* acc_full = a_empty + C::AS;
+  uint64_t* b_full = raw_empty + C::RS;  // per activation group slot
+  uint64_t* b_empty = b_full + C::BGS;
+  uint64_t* a_full = b_empty + C::BGS;   // per A superblock slot
+  uint64_t* a_empty = a_full + C::ASB;
+  uint64_t* acc_full = a_empty + C::ASB;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acc_full + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -243,14 +267,14 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::RS; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 32 * DEQ_WARPS);
+      mbar_init(&raw_empty[i], 32 * W::DEQ);
     }
-    for (int i = 0; i < C::BS; ++i) {
+    for (int i = 0; i < C::BGS; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
     }
-    for (int i = 0; i < C::AS; ++i) {
-      mbar_init(&a_full[i], 128);
+    for (int i = 0; i < C::ASB; ++i) {
+      mbar_init(&a_full[i], 32 * W::DEQ);  // every dequant thread, once per superblock
       mbar_init(&a_empty[i], 1);
     }
     mbar_init(acc_full, 1);
@@ -262,15 +286,12 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
 
-  if (warp == PRODUCER_WARP) {
-    // ---------------- TMA producer ----------------
+  if (warp == W::RAW) {
+    // ---------------- TMA producer: raw weight tiles, RS superblocks ahead ----------------
     if (lane == 0) {
       tma_prefetch(&wmap);
-      tma_prefetch(&xmap);
       if (QT == GGUF_Q6_K) tma_prefetch(&dmap);
-      int bq = 0;  // next activation quarter to load
-      bool ok = true;
-      for (int i = 0; i < nsb && ok; ++i) {
+      for (int i = 0; i < nsb; ++i) {
         const int rs = i % C::RS;
         if (i >= C::RS && !mbar_wait(&raw_empty[rs], ((i / C::RS) - 1) & 1, P.err, ERR_WAIT_RAW)) break;
         uint8_t* dst = smem + C::OFF_RAW + rs * R::BYTES;
@@ -278,44 +299,62 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
         const int kb = sb_lo + i;
         tma_load_2d(dst, &wmap, kb * R::ROW, row0, &raw_full[rs]);
         if constexpr (QT == GGUF_Q6_K) tma_load_2d(dst + R::BODY, &dmap, kb & ~7, row0, &raw_full[rs]);
-        for (; bq < nq && bq < 4 * (i + 1); ++bq) {
-          const int bs = bq % C::BS;
-          if (bq >= C::BS && !mbar_wait(&b_empty[bs], ((bq / C::BS) - 1) & 1, P.err, ERR_WAIT_B)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(&b_full[bs], C::BTILE);
-          tma_load_2d(smem + C::OFF_B + bs * C::BTILE, &xmap, (sb_lo * 4 + bq) * KSTEP, blockIdx.y * BN,
-                      &b_full[bs]);
-        }
       }
     }
-  } else if (warp == MMA_WARP) {
+  } else if (warp == W::ACT) {
+    // ---------------- TMA producer: activation tiles, BGS groups of BG quarters ahead ----------------
+    if (lane == 0) {
+      tma_prefetch(&xmap);
+      for (int g = 0; g < nq / C::BG; ++g) {
+        const int gs = g % C::BGS;
+        if (g >= C::BGS && !mbar_wait(&b_empty[gs], ((g / C::BGS) - 1) & 1, P.err, ERR_WAIT_B)) break;
+        mbar_expect_tx(&b_full[gs], C::BG * C::BTILE);
+#pragma unroll
+        for (int j = 0; j < C::BG; ++j)
+          tma_load_2d(smem + C::OFF_B + (gs * C::BG + j) * C::BTILE, &xmap, (sb_lo * 4 + g * C::BG + j) * KSTEP,
+                      blockIdx.y * BN, &b_full[gs]);
+      }
+    }
+  } else if (warp == W::MMA) {
     // ---------------- MMA issuer ----------------
     constexpr uint32_t IDESC = idesc_f16(BF16, TM, BN);
-    int q = 0;
-    for (; q < nq; ++q) {
-      const int as = q % C::AS, bs = q % C::BS;
-      if (!mbar_wait_warp(&a_full[as], (q / C::AS) & 1, P.err, ERR_WAIT_A)) break;
-      if (!mbar_wait_warp(&b_full[bs], (q / C::BS) & 1, P.err, ERR_WAIT_B)) break;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t a_addr = tmem + C::A_COL0 + as * 32;
-        const uint32_t b_addr = smem_u32(smem + C::OFF_B + bs * C::BTILE);
+    constexpr int GPS = 4 / C::BG;  // activation groups per superblock
+    bool ok = true, issued = false;
+    for (int i = 0; i < nsb && ok; ++i) {
+      const int as = i % C::ASB;
+      ok = mbar_wait_warp(&a_full[as], (i / C::ASB) & 1, P.err, ERR_WAIT_A);
+      for (int h = 0; h < GPS && ok; ++h) {
+        const int g = GPS * i + h, gs = g % C::BGS;
+        ok = mbar_wait_warp(&b_full[gs], (g / C::BGS) & 1, P.err, ERR_WAIT_B);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) {
 #pragma unroll
-        for (int k16 = 0; k16 < 4; ++k16) {
-          const int step = 4 * q + k16;
-          const uint32_t d_addr = tmem + (uint32_t)((step % C::ACC_SETS) * BN);
-          mma_ts(d_addr, a_addr + 8 * k16, desc_kmajor_sw128(b_addr + 32 * k16), IDESC,
-                 step >= C::ACC_SETS ? 1u : 0u);
+          for (int j = 0; j < C::BG; ++j) {
+            const int qq = C::BG * h + j, q = 4 * i + qq;  // quarter within the superblock / overall
+            const uint32_t a_addr = tmem + C::A_COL0 + as * 128 + qq * 32;
+            const uint32_t b_addr = smem_u32(smem + C::OFF_B + (gs * C::BG + j) * C::BTILE);
+#pragma unroll
+            for (int k16 = 0; k16 < 4; ++k16) {
+              const int step = 4 * q + k16;
+              const uint32_t d_addr = tmem + (uint32_t)((step % C::ACC_SETS) * BN);
+              mma_ts(d_addr, a_addr + 8 * k16, desc_kmajor_sw128(b_addr + 32 * k16), IDESC,
+                     step >= C::ACC_SETS ? 1u : 0u);
+            }
+          }
+          tc_commit(&b_empty[gs]);
         }
+        issued = true;
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (lane == 0) {
         tc_commit(&a_empty[as]);
-        tc_commit(&b_empty[bs]);
-        if (q == nq - 1) tc_commit(acc_full);
+        if (i == nsb - 1) tc_commit(acc_full);
       }
       __syncwarp();
     }
-    if (q > 0 && q < nq) {
+    if (!ok && issued) {
       // stopped early: let the MMAs already issued finish before TMEM is freed
       if (lane == 0) tc_commit(acc_full);
       mbar_wait_warp(acc_full, 0, P.err, ERR_WAIT_MMA);
@@ -324,16 +363,17 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
     // ---------------- dequant (warps 0-7) ----------------
     // Warp w serves TMEM lanes 32*(w%4).. (rows of the tile) and quarters
     // 2*(w/4), 2*(w/4)+1 of every superblock.  The second quarter is unpacked
-    // while the first one's TMEM store completes.
+    // while the first one's TMEM store completes; each thread arrives on the
+    // superblock's A slot once both are stored.
     const int r = (warp & 3) * 32 + lane;  // tile row = TMEM lane
     const int c0 = 2 * (warp >> 2);
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    bool ok = true;
-    for (int i = 0; i < nsb && ok; ++i) {
-      const int rs = i % C::RS;
+    for (int i = 0; i < nsb; ++i) {
+      const int rs = i % C::RS, as = i % C::ASB;
       if (!mbar_wait_warp(&raw_full[rs], (i / C::RS) & 1, P.err, ERR_WAIT_RAW)) break;
       const uint8_t* raw = smem + C::OFF_RAW + rs * R::BYTES;
       const uint4* rp = reinterpret_cast<const uint4*>(raw + r * R::ROW);
+      const uint32_t a_col = tmem + lane_base + C::A_COL0 + as * 128 + c0 * 32;
       uint32_t a0[32], a1[32];
       if constexpr (QT == GGUF_Q4_K) {
         const uint4 hdr = rp[0];
@@ -342,9 +382,8 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
         for (int j = 0; j < 4; ++j) qs[2 * c0 + j] = rp[1 + 2 * c0 + j];
         raw_release(&raw_empty[rs]);
         unpack_q4<BF16>(qs, hdr, c0, a0);
-        const int q0 = 4 * i + c0, s0 = q0 % C::AS;
-        if (q0 >= C::AS && !mbar_wait_warp(&a_empty[s0], ((q0 / C::AS) - 1) & 1, P.err, ERR_WAIT_MMA)) break;
-        tmem_st32(tmem + lane_base + C::A_COL0 + s0 * 32, a0);
+        if (i >= C::ASB && !mbar_wait_warp(&a_empty[as], ((i / C::ASB) - 1) & 1, P.err, ERR_WAIT_MMA)) break;
+        tmem_st32(a_col, a0);
         unpack_q4<BF16>(qs, hdr, c0 + 1, a1);
       } else {
         const uint4 p0 = rp[3 * c0], p1 = rp[3 * c0 + 1], p2 = rp[3 * c0 + 2];
@@ -353,23 +392,14 @@ __global__ void __launch_bounds__(THREADS, BN <= 64 ? 2 : 1)
         const float d = f16_bits_to_f32(reinterpret_cast<const uint16_t*>(raw + R::BODY)[r * 8 + ((sb_lo + i) & 7)]);
         raw_release(&raw_empty[rs]);
         unpack_q6<BF16>(p0, p1, p2, sc, d, c0, a0);
-        const int q0 = 4 * i + c0, s0 = q0 % C::AS;
-        if (q0 >= C::AS && !mbar_wait_warp(&a_empty[s0], ((q0 / C::AS) - 1) & 1, P.err, ERR_WAIT_MMA)) break;
-        tmem_st32(tmem + lane_base + C::A_COL0 + s0 * 32, a0);
+        if (i >= C::ASB && !mbar_wait_warp(&a_empty[as], ((i / C::ASB) - 1) & 1, P.err, ERR_WAIT_MMA)) break;
+        tmem_st32(a_col, a0);
         unpack_q6<BF16>(p3, p4, p5, sc, d, c0 + 1, a1);
       }
-      {
-        const int q0 = 4 * i + c0, q1 = q0 + 1;
-        const int s0 = q0 % C::AS, s1 = q1 % C::AS;
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&a_full[s0]);
-        if (q1 >= C::AS && !mbar_wait_warp(&a_empty[s1], ((q1 / C::AS) - 1) & 1, P.err, ERR_WAIT_MMA)) break;
-        tmem_st32(tmem + lane_base + C::A_COL0 + s1 * 32, a1);
-        tmem_wait_st();
-        tc_fence_before();
-        mbar_arrive(&a_full[s1]);
-      }
+      tmem_st32(a_col + 32, a1);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&a_full[as]);
     }
   }
   if (warp < 4) {
@@ -562,7 +592,7 @@ template <int QT, int BN, bool BF16>
 cudaError_t launch_kernel(const CUtensorMap& wm, const CUtensorMap& dm, const CUtensorMap& xm, const Params& P,
                           dim3 grid, cudaStream_t s) {
   using C = Cfg<QT, BN>;
-  kq_mma_kernel<QT, BN, BF16><<<grid, THREADS, C::SMEM, s>>>(wm, dm, xm, P);
+  kq_mma_kernel<QT, BN, BF16><<<grid, W::THREADS, C::SMEM, s>>>(wm, dm, xm, P);
   return cudaGetLastError();
 }
 
@@ -580,6 +610,7 @@ cudaError_t set_attrs_q() {
   if ((r = set_attr<QT, 64, false>()) != cudaSuccess) e = r;
   if ((r = set_attr<QT, 128, false>()) != cudaSuccess) e = r;
   if ((r = set_attr<QT, 256, false>()) != cudaSuccess) e = r;
+  if ((r = set_attr<QT, 128, true>()) != cudaSuccess) e = r;
   if ((r = set_attr<QT, 256, true>()) != cudaSuccess) e = r;
   return e;
 }
@@ -598,6 +629,15 @@ cudaError_t launch_bn(int bn, const CUtensorMap& wm, const CUtensorMap& dm, cons
 
 int pick_bn_f32(int64_t m) {  // two columns (hi, lo) per token
   return m <= 8 ? 16 : m <= 16 ? 32 : m <= 32 ? 64 : m <= 64 ? 128 : 256;
+}
+
+// bf16 (prefill) tile width in tokens: 256, or 128 where 256-token tiles would
+// leave SMs without a CTA (a 4096-row weight at 512 tokens: 64 CTAs of 256
+// tokens, 128 of 128).  A 128-token Q4_K CTA takes ~104 KB of shared memory,
+// so two of them share an SM.
+int pick_bn_bf16(int64_t m, int64_t n, int num_sms) {
+  const int64_t rt = (n + TM - 1) / TM;
+  return rt * ((m + 255) / 256) < num_sms ? 128 : 256;
 }
 
 int64_t splits_for(int64_t m, int64_t n, int64_t k, int num_sms) {
@@ -708,8 +748,8 @@ cudaError_t launch_tc_f32(const DevWeight& w, const float* x, int64_t m, const f
 }
 
 cudaError_t launch_tc_bf16(const DevWeight& w, const void* x, int64_t m, const float* bias, float* y, void* ws,
-                           int* err, cudaStream_t s, int* launches, Bracket br) {
-  constexpr int BN = 256;
+                           int num_sms, int* err, cudaStream_t s, int* launches, Bracket br) {
+  const int bn = pick_bn_bf16(m, w.n, num_sms);
   __nv_bfloat16* xq = static_cast<__nv_bfloat16*>(ws);
   const int64_t quads = m * (w.k / 4);
   const unsigned pg = (unsigned)std::min<int64_t>((quads + 255) / 256, 148 * 32);
@@ -720,14 +760,19 @@ cudaError_t launch_tc_bf16(const DevWeight& w, const void* x, int64_t m, const f
   if (launches) ++*launches;
   CUtensorMap xm;
   if (!make_map_2d(&xm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xq, (uint64_t)w.k, (uint64_t)m, (uint64_t)w.k * 2,
-                   KSTEP, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+                   KSTEP, bn, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  const int64_t rt = (w.n + TM - 1) / TM, tiles = (m + BN - 1) / BN;
+  const int64_t rt = (w.n + TM - 1) / TM, tiles = (m + bn - 1) / bn;
   Params P{(int)w.n, (int)w.sb, (int)m, 1, nullptr, bias, y, nullptr, nullptr, err};
   dim3 grid((unsigned)rt, (unsigned)tiles, 1);
   bracket_record(br.start, s);
-  cudaError_t e = w.type == GGUF_Q4_K ? launch_kernel<GGUF_Q4_K, BN, true>(w.wmap, w.dmap, xm, P, grid, s)
-                                      : launch_kernel<GGUF_Q6_K, BN, true>(w.wmap, w.dmap, xm, P, grid, s);
+  cudaError_t e;
+  if (bn == 128)
+    e = w.type == GGUF_Q4_K ? launch_kernel<GGUF_Q4_K, 128, true>(w.wmap, w.dmap, xm, P, grid, s)
+                            : launch_kernel<GGUF_Q6_K, 128, true>(w.wmap, w.dmap, xm, P, grid, s);
+  else
+    e = w.type == GGUF_Q4_K ? launch_kernel<GGUF_Q4_K, 256, true>(w.wmap, w.dmap, xm, P, grid, s)
+                            : launch_kernel<GGUF_Q6_K, 256, true>(w.wmap, w.dmap, xm, P, grid, s);
   bracket_record(br.stop, s);
   if (launches) ++*launches;
   return e;

@@ -178,6 +178,7 @@ PREFILL_CASES = [
     ("Q6_K", 1024, 4096, 300),   # m not a multiple of the 256-token tile
     ("Q4_K", 100, 1024, 37),     # partial row tile, few tokens
     ("Q6_K", 256, 4864, 257),
+    ("Q6_K", 4864, 1024, 1000),  # 38 row tiles x 4 token tiles: 256-token tiles on 148 SMs
 ]
 
 
