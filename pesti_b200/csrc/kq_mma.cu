@@ -17,9 +17,9 @@
 //              frees activation pairs and A superblock slots and signals the
 //              epilogue.  Its barrier waits and commits cost about as much
 //              issue time as the MMAs, so there is one wait / commit per
-//              activation pair and per superblock of A, not per quarter
-//              (measured: 838 -> 1066 TFLOP/s on a 14336 x 4096 Q4_K weight
-//              at 4096 tokens).
+//              activation pair and per superblock of A, not per quarter, all
+//              from one thread (measured: 838 -> 1111 TFLOP/s on a 14336 x
+//              4096 Q4_K weight at 4096 tokens).
 //
 // The weights' K order inside a superblock is the order in which a thread
 // unpacks them cheaply (per 64-weight quarter c and step s: weights e, e+2,
@@ -319,16 +319,17 @@ __global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
     // ---------------- MMA issuer ----------------
     constexpr uint32_t IDESC = idesc_f16(BF16, TM, BN);
     constexpr int GPS = 4 / C::BG;  // activation groups per superblock
-    bool ok = true, issued = false;
-    for (int i = 0; i < nsb && ok; ++i) {
-      const int as = i % C::ASB;
-      ok = mbar_wait_warp(&a_full[as], (i / C::ASB) & 1, P.err, ERR_WAIT_A);
-      for (int h = 0; h < GPS && ok; ++h) {
-        const int g = GPS * i + h, gs = g % C::BGS;
-        ok = mbar_wait_warp(&b_full[gs], (g / C::BGS) & 1, P.err, ERR_WAIT_B);
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) {
+    // one thread waits, issues and commits (no warp votes between the steps)
+    if (lane == 0) {
+      bool ok = true, issued = false;
+      for (int i = 0; i < nsb && ok; ++i) {
+        const int as = i % C::ASB;
+        ok = mbar_wait(&a_full[as], (i / C::ASB) & 1, P.err, ERR_WAIT_A);
+        for (int h = 0; h < GPS && ok; ++h) {
+          const int g = GPS * i + h, gs = g % C::BGS;
+          ok = mbar_wait(&b_full[gs], (g / C::BGS) & 1, P.err, ERR_WAIT_B);
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
           for (int j = 0; j < C::BG; ++j) {
             const int qq = C::BG * h + j, q = 4 * i + qq;  // quarter within the superblock / overall
@@ -343,22 +344,19 @@ __global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
             }
           }
           tc_commit(&b_empty[gs]);
+          issued = true;
         }
-        issued = true;
-        __syncwarp();
-      }
-      if (!ok) break;
-      if (lane == 0) {
+        if (!ok) break;
         tc_commit(&a_empty[as]);
         if (i == nsb - 1) tc_commit(acc_full);
       }
-      __syncwarp();
+      if (!ok && issued) {
+        // stopped early: let the MMAs already issued finish before TMEM is freed
+        tc_commit(acc_full);
+        mbar_wait(acc_full, 0, P.err, ERR_WAIT_MMA);
+      }
     }
-    if (!ok && issued) {
-      // stopped early: let the MMAs already issued finish before TMEM is freed
-      if (lane == 0) tc_commit(acc_full);
-      mbar_wait_warp(acc_full, 0, P.err, ERR_WAIT_MMA);
-    }
+    __syncwarp();
   } else {
     // ---------------- dequant (warps 0-7) ----------------
     // Warp w serves TMEM lanes 32*(w%4).. (rows of the tile) and quarters
@@ -402,10 +400,15 @@ __global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
       mbar_arrive(&a_full[as]);
     }
   }
-  if (warp < 4) {
-    // ---------------- epilogue (warps 0-3, one tile row per thread) ----------------
-    const int r = warp * 32 + lane;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  // epilogue warps: 0-3 for decode tiles, 0-7 for 128/256-token tiles (warps
+  // w and w+4 share a TMEM lane quadrant and take one half of the tokens each)
+  constexpr int EW = BN >= 128 ? 8 : 4;
+  if (warp < EW) {
+    // ---------------- epilogue (one tile row per thread) ----------------
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    constexpr int TPW = TPT / (EW / 4);  // tokens per epilogue warp
+    const int tb = (warp >> 2) * TPW;    // this warp's first token
     const bool acc_ok = nq > 0 && mbar_wait_warp(acc_full, 0, P.err, ERR_WAIT_ACC);
     tc_fence_after();
     const int row = row0 + r;
@@ -421,7 +424,7 @@ __global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
     }
     const float bias = (P.splits == 1 && P.bias && row < P.n) ? P.bias[row] : 0.f;
 #pragma unroll 1
-    for (int t0 = 0; t0 < TPT; t0 += 8) {
+    for (int t0 = tb; t0 < tb + TPW; t0 += 8) {
       float hi[8], lo[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) hi[j] = lo[j] = 0.f;
@@ -454,22 +457,22 @@ __global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
     if (P.splits > 1) {
       // the last CTA of this (row tile, token tile) adds the partials in split order
       __threadfence();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * EW) : "memory");
       unsigned* ctr = P.counters + (blockIdx.y * gridDim.x + blockIdx.x);
-      if (r == 0) last_cta = atomicAdd(ctr, 1u) == (unsigned)(P.splits - 1);
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 0) last_cta = atomicAdd(ctr, 1u) == (unsigned)(P.splits - 1);
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * EW) : "memory");
       if (last_cta) {
         __threadfence();
         if (row < P.n) {
           const float b = P.bias ? P.bias[row] : 0.f;
-          for (int t = 0; t < mt; ++t) {
+          for (int t = tb; t < min(tb + TPW, mt); ++t) {
             float s = 0.f;
             for (int zz = 0; zz < P.splits; ++zz)
               s += __ldcg(&P.ws[((int64_t)zz * P.m + tok0 + t) * P.n + row]);
             P.y[(int64_t)(tok0 + t) * P.n + row] = s + b;
           }
         }
-        if (r == 0) *ctr = 0u;
+        if (threadIdx.x == 0) *ctr = 0u;
       }
     }
   }
