@@ -423,32 +423,37 @@ __global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
       ldd = P.n;
     }
     const float bias = (P.splits == 1 && P.bias && row < P.n) ? P.bias[row] : 0.f;
+    constexpr int E = BF16 ? 16 : 8;  // tokens per TMEM round trip
 #pragma unroll 1
-    for (int t0 = tb; t0 < tb + TPW; t0 += 8) {
-      float hi[8], lo[8];
+    for (int t0 = tb; t0 < tb + TPW; t0 += E) {
+      float hi[E], lo[E];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) hi[j] = lo[j] = 0.f;
+      for (int j = 0; j < E; ++j) hi[j] = lo[j] = 0.f;
       if (acc_ok) {
 #pragma unroll
         for (int set = 0; set < C::ACC_SETS; ++set) {
-          uint32_t h[8], l[8];
-          tmem_ld8(tmem + lane_base + set * BN + t0, h);
-          if (!BF16) tmem_ld8(tmem + lane_base + set * BN + TPT + t0, l);
+          uint32_t h[E], l[E];
+          if constexpr (BF16) {
+            tmem_ld16(tmem + lane_base + set * BN + t0, h);
+          } else {
+            tmem_ld8(tmem + lane_base + set * BN + t0, h);
+            tmem_ld8(tmem + lane_base + set * BN + TPT + t0, l);
+          }
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
+          for (int j = 0; j < E; ++j) {
             hi[j] += __uint_as_float(h[j]);
-            if (!BF16) lo[j] += __uint_as_float(l[j]);
+            if constexpr (!BF16) lo[j] += __uint_as_float(l[j]);
           }
         }
       }
       if (row < P.n) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < E; ++j) {
           const int t = t0 + j;
           if (t < mt) {
             float v = hi[j];
-            if (!BF16) v = (v + lo[j]) * P.tok_scale[tok0 + t];
+            if constexpr (!BF16) v = (v + lo[j]) * P.tok_scale[tok0 + t];
             dst[(int64_t)t * ldd + row] = v + bias;
           }
         }
