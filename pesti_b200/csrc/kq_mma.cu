@@ -641,8 +641,7 @@ int pick_bn_f32(int64_t m) {  // two columns (hi, lo) per token
 
 // bf16 (prefill) tile width in tokens: 256, or 128 where 256-token tiles would
 // leave SMs without a CTA (a 4096-row weight at 512 tokens: 64 CTAs of 256
-// tokens, 128 of 128).  A 128-token Q4_K CTA takes ~104 KB of shared memory,
-// so two of them share an SM.
+// tokens, 128 of 128; each runs alone on its SM).
 int pick_bn_bf16(int64_t m, int64_t n, int num_sms) {
   const int64_t rt = (n + TM - 1) / TM;
   return rt * ((m + 255) / 256) < num_sms ? 128 : 256;
