@@ -47,6 +47,18 @@
 namespace kq {
 namespace {
 using namespace sm100;
+// The MMA thread's waits: a completed phase answers a non-blocking test
+// (cheaper than the blocking try-wait loop, measured 2-6% on the prefill);
+// otherwise the bounded wait.
+__device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, int* err, int code) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done ? true : mbar_wait(bar, parity, err, code);
+}
 
 constexpr int TM = 128;    // weight rows per CTA = UMMA M
 constexpr int KSTEP = 64;  // k per A slot / activation tile (one quarter superblock)
@@ -324,10 +336,10 @@ __global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
       bool ok = true, issued = false;
       for (int i = 0; i < nsb && ok; ++i) {
         const int as = i % C::ASB;
-        ok = mbar_wait(&a_full[as], (i / C::ASB) & 1, P.err, ERR_WAIT_A);
+        ok = mbar_wait_fast(&a_full[as], (i / C::ASB) & 1, P.err, ERR_WAIT_A);
         for (int h = 0; h < GPS && ok; ++h) {
           const int g = GPS * i + h, gs = g % C::BGS;
-          ok = mbar_wait(&b_full[gs], (g / C::BGS) & 1, P.err, ERR_WAIT_B);
+          ok = mbar_wait_fast(&b_full[gs], (g / C::BGS) & 1, P.err, ERR_WAIT_B);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
