@@ -346,13 +346,14 @@ __global__ void __launch_bounds__(W::THREADS, BN <= 64 ? 2 : 1)
           for (int j = 0; j < C::BG; ++j) {
             const int qq = C::BG * h + j, q = 4 * i + qq;  // quarter within the superblock / overall
             const uint32_t a_addr = tmem + C::A_COL0 + as * 128 + qq * 32;
-            const uint32_t b_addr = smem_u32(smem + C::OFF_B + (gs * C::BG + j) * C::BTILE);
+            // descriptor of the tile's first k16 step; the next steps start 32 bytes
+            // further (2 in the address field, which holds addresses / 16 < 2^14)
+            const uint64_t b_desc = desc_kmajor_sw128(smem_u32(smem + C::OFF_B + (gs * C::BG + j) * C::BTILE));
 #pragma unroll
             for (int k16 = 0; k16 < 4; ++k16) {
               const int step = 4 * q + k16;
               const uint32_t d_addr = tmem + (uint32_t)((step % C::ACC_SETS) * BN);
-              mma_ts(d_addr, a_addr + 8 * k16, desc_kmajor_sw128(b_addr + 32 * k16), IDESC,
-                     step >= C::ACC_SETS ? 1u : 0u);
+              mma_ts(d_addr, a_addr + 8 * k16, b_desc + (uint64_t)(2 * k16), IDESC, step >= C::ACC_SETS ? 1u : 0u);
             }
           }
           tc_commit(&b_empty[gs]);
